@@ -1,0 +1,360 @@
+"""MoE-layer benchmark (BASELINE metric: MoE-layer tokens/s on B200).
+
+Workload (N=1 headline): BASELINE config 2, the Qwen3.5-35B-A3B-shaped decode
+MoE layer (d=2048, 256 experts, top-8, expert width 512, shared expert, Q8_0),
+T=64 tokens per step and per GPU. One step = one MoE-layer forward
+(router -> top-k -> dispatch -> expert SwiGLU -> combine) over T tokens. The
+steps cycle through L distinct layers (default 8 x 0.86 GB of weights, far
+larger than the 126 MB L2), so no step reads weights another step left in L2.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 (torchrun, one process per GPU) every rank runs its own replica on
+its own T tokens (tokens are data-parallel, no collective on the path):
+weak scaling; time = max over ranks of the device-timed region.
+
+--impl reference times the reference's CPU path on the host: the C++
+restatement in oracle/ (the Rust reference cannot be built in this image),
+with the reference's own threading (2 expert threads + the shared expert on
+the calling thread), on a bounded token sample per step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer tokens/s"
+UNIT = "tokens/s"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--tokens", type=int, default=64, help="tokens per step per GPU")
+    p.add_argument("--layers", type=int, default=8, help="distinct layers cycled through")
+    p.add_argument("--no-sweep", action="store_true")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# algorithmic bytes (per realised routing)
+# ---------------------------------------------------------------------------
+def q8_bytes(n):
+    return n // 32 * 34
+
+
+def layer_bytes(cfg, U, T):
+    """Algorithmic HBM bytes of one C2 layer pass: every routed expert's and the
+    shared expert's weights once, the router and shared-gate vector, tokens in/out."""
+    per_mat = q8_bytes(cfg.d * cfg.f)
+    gu = (U + (1 if cfg.shared else 0)) * 2 * per_mat
+    dn = (U + (1 if cfg.shared else 0)) * per_mat
+    router = cfg.E * cfg.d * 4 + (cfg.d * 4 if cfg.shared else 0)
+    return dict(gateup=gu + T * q8_bytes(cfg.d), down=dn, total=gu + dn + router + T * cfg.d * 4 * 2)
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device, self.proc, self.lines = device, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "100", "-i", str(self.device)], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx.append(float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[4:8]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle's restatement of the reference
+# ---------------------------------------------------------------------------
+def cpu_layer_tensors(cfg, seed=0, layer=0):
+    """Host copies of one layer's tensors (generated on the GPU when one is present)."""
+    import torch
+
+    from powerinfer_x64_b200 import synth
+
+    if torch.cuda.is_available():
+        t = synth.moe_tensors(cfg, seed, layer)
+        h = lambda a: None if a is None else a.cpu().numpy()
+        out = dict(router=h(t["router"]), gate_exps=h(t["gate_exps"]), up_exps=h(t["up_exps"]),
+                   down_exps=h(t["down_exps"]), shared=tuple(h(a) for a in t["shared"]) if cfg.shared else None)
+        del t
+        torch.cuda.empty_cache()
+        return out
+    raise RuntimeError("the CPU baseline uses GPU-generated inputs")
+
+
+def run_cpu(cfg, tensors, x, reps):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import pi_oracle as orc
+
+    orc.set_threads(0)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        orc.moe_layer(x, cfg.d, cfg.f, cfg.E, cfg.k, cfg.qtype, tensors["router"], tensors["gate_exps"],
+                      tensors["up_exps"], tensors["down_exps"], shared=tensors["shared"], threads=0)
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def reference_arm(args):
+    import numpy as np
+    import torch
+
+    from powerinfer_x64_b200 import dist, synth
+
+    rank, local, world = dist.env_rank()
+    if rank != 0:
+        return 0
+    if torch.cuda.is_available():
+        torch.cuda.set_device(local)
+    cfg = synth.C2
+    tensors = cpu_layer_tensors(cfg)
+    sample = 8  # tokens per step: the reference handles tokens one by one, so this is a bounded sample
+    x = synth.normal_host(synth.stream_seed(0, "x"), sample * cfg.d, 1.0).reshape(sample, cfg.d)
+    run_cpu(cfg, tensors, x, args.warmup)
+    times = run_cpu(cfg, tensors, x, args.steps)
+    tps = sample * len(times) / sum(times)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": f"{cfg.name} (BASELINE config 2) T={args.tokens}; step = {sample}-token sample",
+                   "tokens_per_step": sample},
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 3, "kind": "port",
+                         "sample": f"{sample} tokens of one C2 layer per step",
+                         "host_threads_available": os.cpu_count(),
+                         "note": "C++ restatement of the reference CPU path (oracle/); reference threading: "
+                                 "2 expert threads + shared expert on the caller"},
+        "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import numpy as np
+    import torch
+
+    from powerinfer_x64_b200 import Context, dist, synth
+
+    rank, local, world = dist.init()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = synth.C2
+    T = args.tokens
+    ctx = Context.default(local)
+
+    # layers + fixed per-layer tokens (each rank its own seed stream)
+    layers, xs, routing = [], [], []
+    for li in range(args.layers):
+        L = synth.moe_layer(cfg, seed=rank, layer=li)
+        x = synth.tokens_dev(cfg.d, T, seed=rank, layer=li)
+        r = L.route(x)
+        U = int((r["counts"] > 0).sum().item())
+        layers.append(L)
+        xs.append(x)
+        routing.append(U)
+    torch.cuda.synchronize()
+    out = torch.empty((T, cfg.d), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def step(i):
+        layers[i % args.layers].forward(xs[i % args.layers], out=out)
+
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+
+    # ---- timed region (device time, kernel timing live via CUDA events) ----
+    ctx.profile(True)
+    dist.barrier(local)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        e0.record(stream)
+        for i in range(args.steps):
+            step(i)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dist.barrier(local)
+    ms = e0.elapsed_time(e1)
+    kern = ctx.profile_read()
+    ctx.profile(False)
+    ms_max = dist.max_over_ranks(ms, device=dev)
+    value = world * T * args.steps / (ms_max / 1e3)
+
+    # per-kernel averages, roofline of the dominant kernel (gate/up GEMV)
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        pass
+    peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    Us = [routing[i % args.layers] for i in range(args.steps)]
+    b_gu = sum(layer_bytes(cfg, U, T)["gateup"] for U in Us)
+    b_tot = sum(layer_bytes(cfg, U, T)["total"] for U in Us)
+    gu_ms, gu_n = kern.get("k_gateup", (float("nan"), 0))
+    achieved = b_gu / (gu_ms / 1e3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "ncu_traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get("k_gateup_c2_T64_bytes_per_launch")
+        except Exception:
+            traffic = None
+    launches = sum(n for (_, n) in kern.values())
+
+    # ---- end to end: host tokens in (pinned), host output back, per step ----
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = torch.empty((T, cfg.d), dtype=torch.float32).pin_memory()
+    xd = torch.empty((T, cfg.d), dtype=torch.float32, device=dev)
+
+    def e2e_step(i):
+        xd.copy_(xh[i % args.layers], non_blocking=True)
+        layers[i % args.layers].forward(xd, out=out)
+        oh.copy_(out, non_blocking=True)
+
+    for i in range(args.warmup):
+        e2e_step(i)
+    dist.barrier(local)
+    torch.cuda.synchronize()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i)
+    f1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = dist.max_over_ranks(f0.elapsed_time(f1), device=dev)
+    e2e_val = world * T * args.steps / (e2e_ms / 1e3)
+
+    # ---- decode batch sweep (T in 1, 4, 16, 64) ----
+    sweep = []
+    if not args.no_sweep:
+        for Ts in (1, 4, 16, 64):
+            xs_s = [synth.tokens_dev(cfg.d, Ts, seed=rank + 100, layer=li) for li in range(args.layers)]
+            Us_s = [int((layers[li].route(xs_s[li])["counts"] > 0).sum().item()) for li in range(args.layers)]
+            os_ = torch.empty((Ts, cfg.d), dtype=torch.float32, device=dev)
+            for i in range(args.warmup):
+                layers[i % args.layers].forward(xs_s[i % args.layers], out=os_)
+            torch.cuda.synchronize()
+            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            g0.record(stream)
+            for i in range(args.steps):
+                layers[i % args.layers].forward(xs_s[i % args.layers], out=os_)
+            g1.record(stream)
+            torch.cuda.synchronize()
+            sm = g0.elapsed_time(g1)
+            byt = sum(layer_bytes(cfg, Us_s[i % args.layers], Ts)["total"] for i in range(args.steps))
+            sweep.append({"T": Ts, "tokens_per_s": Ts * args.steps / (sm / 1e3), "us_per_layer": 1e3 * sm / args.steps,
+                          "layer_hbm_gbs": byt / (sm / 1e3) / 1e9,
+                          "layer_frac_of_peak": byt / (sm / 1e3) / 1e9 / peak})
+
+    # ---- CPU baseline (rank 0, N=1): the oracle, reference threading ----
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        tensors = cpu_layer_tensors(cfg, seed=0, layer=0)
+        sample = 16
+        xsmp = xs[0][:sample].cpu().numpy()
+        run_cpu(cfg, tensors, xsmp, 1)
+        times = run_cpu(cfg, tensors, xsmp, 5)
+        med = statistics.median(times)
+        cpu = {"value": sample / med, "unit": UNIT, "cores": 3, "kind": "port",
+               "sample": f"{sample} tokens of one C2 layer, median of 5 runs after 1 warm-up",
+               "host_threads_available": os.cpu_count()}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> Q8_0)",
+            "config": {"workload": f"{cfg.name} (BASELINE config 2): d=2048 E=256 k=8 f=512 +shared, Q8_0",
+                       "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": f"dp{world} (replicas)",
+                       "layers_cycled": args.layers, "l2": "inputs larger than L2: steps cycle through "
+                       f"{args.layers} layers x {layer_bytes(cfg, 256, T)['total'] / 1e9:.2f} GB"},
+            "roofline": {"bound": "hbm", "kernel": "k_gateup", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                         "algorithmic_bytes_per_launch": b_gu / args.steps,
+                         "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1)},
+            "layer_roofline": {"achieved_gbs": b_tot / (ms_max / 1e3) / 1e9,
+                               "frac": b_tot / (ms_max / 1e3) / 1e9 / peak},
+            "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in kern.items()},
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": T * cfg.d * 4,
+                    "d2h_bytes_per_step": T * cfg.d * 4},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "sweep": sweep,
+        }
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

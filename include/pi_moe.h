@@ -1,0 +1,208 @@
+/*
+ * pi_moe.h — C ABI of the B200 (sm_100a) MoE feed-forward and hot-neuron
+ * sparse-FFN path for PowerInfer_x64.
+ *
+ * The entry points replace, one for one, the reference's Rust operator
+ * functions on this path (citations: file:line in the reference project).
+ * The Rust side keeps its `quant`, `moe` and `predictor` signatures and calls
+ * these through a thin `extern "C"` block.
+ *
+ * Conventions
+ *   - Every function returns an int status: PI_OK (0) or one of PI_ERR_*.
+ *     pi_last_error(ctx) gives a human-readable message for the last failure.
+ *   - Pointers to activations, outputs and index lists are DEVICE pointers
+ *     (caller-owned) unless a parameter says otherwise. Weight sources passed
+ *     to the *_create functions may be host or device memory (src_on_host).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream). Calls are
+ *     asynchronous on it; results are valid after the stream synchronises.
+ *   - Device-side index validation (an out-of-range index in a device list)
+ *     is reported through pi_ctx_check(), which synchronises the stream.
+ *   - There is no CPU fallback: every call runs CUDA kernels for sm_100a.
+ *   - A context may be used from several host threads; concurrent calls on
+ *     DIFFERENT streams each get their own scratch arena.
+ */
+#ifndef PI_MOE_H
+#define PI_MOE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* status codes */
+#define PI_OK 0
+#define PI_ERR_ARG 1     /* bad argument: null pointer, bad size, unsupported type */
+#define PI_ERR_INDEX 2   /* an index is out of range (reference: anyhow Err)        */
+#define PI_ERR_SHORT 3   /* raw buffer shorter than the shape needs                 */
+#define PI_ERR_OOM 4     /* device allocation failed                                */
+#define PI_ERR_CUDA 5    /* a CUDA runtime call or kernel launch failed             */
+#define PI_ERR_TIMEOUT 6 /* a bounded device-side wait gave up                      */
+
+/* GGML tensor type ids (numbering of ggml_type; reference quant/mod.rs:12-40) */
+#define PI_QT_F32 0
+#define PI_QT_F16 1
+#define PI_QT_Q4_0 2
+#define PI_QT_Q8_0 8
+
+/* pi_moe_forward flags */
+#define PI_FWD_RMSNORM 1  /* apply RMSNorm (unit weight) before routing: model/mod.rs:1239 */
+#define PI_FWD_RESIDUAL 2 /* out = x + ffn(x): model/mod.rs:1627-1633                     */
+
+typedef struct pi_ctx pi_ctx;
+typedef struct pi_moe_layer pi_moe_layer;
+typedef struct pi_sparse_ffn pi_sparse_ffn;
+
+/* ---- context ----------------------------------------------------------
+ * Replaces GpuDevice::new / GpuResources::init (src/cuda/mod.rs:193-218,
+ * :387-460): binds one CUDA device; owns per-stream scratch. */
+int pi_ctx_create(int device, pi_ctx** out);
+void pi_ctx_destroy(pi_ctx* ctx);
+const char* pi_last_error(const pi_ctx* ctx);
+/* Synchronises `stream`, then reports (and clears) device-side errors. */
+int pi_ctx_check(pi_ctx* ctx, void* stream);
+/* Pre-sizes the scratch arena of `stream` for `bytes` (0 = no-op), so later
+ * calls on that stream allocate nothing (e.g. before CUDA-graph capture). */
+int pi_ctx_reserve(pi_ctx* ctx, void* stream, uint64_t bytes);
+
+/* Kernel timing (no reference counterpart; the reference has no GPU
+ * profiler hook). enable != 0 starts recording a CUDA event pair around each
+ * kernel launch of the layer path on its stream; pi_ctx_profile(ctx, 0) stops
+ * and clears. pi_ctx_profile_read synchronises the device and writes up to
+ * max_entries kernel names (32 chars each), accumulated milliseconds and
+ * launch counts; it returns the number of distinct kernels timed. */
+int pi_ctx_profile(pi_ctx* ctx, int enable);
+int pi_ctx_profile_read(pi_ctx* ctx, int max_entries, char* names, double* total_ms, int64_t* launches);
+
+/* ---- quant drop-ins (raw GGUF bytes in device memory) ------------------ */
+
+/* quant::dequantize (src/quant/mod.rs:110-143): raw -> f32 [rows*cols].
+ * Types F32, F16, Q4_0 (reference nibble order, :180-204), Q8_0 (:320-339).
+ * raw_len < needed -> PI_ERR_SHORT (the reference's Err at :122-128). */
+int pi_dequantize(pi_ctx* ctx, const void* raw, uint64_t raw_len, int qtype, int64_t rows, int64_t cols,
+                  float* out, void* stream);
+
+/* The reference's Q8_0 quantiser quantize_f32_to_q8_0 (src/quant/mod.rs:698-736)
+ * emitted as GGUF Q8_0 blocks (34 B: f16 d, 32 x int8). n % 32 == 0. */
+int pi_quantize_q8_0(pi_ctx* ctx, const float* x, int64_t n, void* out_raw, void* stream);
+
+/* GGUF Q4_0 blocks (18 B) with the ggml-style quantiser (d = max/-8,
+ * q = min(15, trunc(x/d + 8.5))), nibbles packed in the order the reference's
+ * decoder reads them (src/quant/mod.rs:193-199). No reference counterpart
+ * (the reference only reads Q4_0); used to build synthetic weights. */
+int pi_quantize_q4_0(pi_ctx* ctx, const float* x, int64_t n, void* out_raw, void* stream);
+
+/* quant::matvec_col_major (src/quant/mod.rs:939-970): y[j] = x . W[:,j],
+ * W = [ne0=n_in, ne1=n_out]. Q8_0 quantises x (:698-736) and uses the
+ * integer block dot (:652-689); F32 / Q4_0 use f32 x. */
+int pi_matvec_col_major(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in,
+                        int64_t n_out, void* stream);
+
+/* quant::matvec_col_major_select (src/quant/mod.rs:974-1068): y[s] = x . W[:, idx[s]].
+ * idx: int64 device array. Out-of-range -> device error (pi_ctx_check -> PI_ERR_INDEX). */
+int pi_matvec_col_major_select(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in,
+                               int64_t n_out, const int64_t* idx, int64_t n_idx, void* stream);
+
+/* quant::matvec_col_major_sparse_input (src/quant/mod.rs:1073-1169):
+ * y = W @ x_sparse, x[s] is the value at input row idx[s]. n_idx == 0 -> y = 0. */
+int pi_matvec_col_major_sparse_input(pi_ctx* ctx, float* y, const float* x, const int64_t* idx, int64_t n_idx,
+                                     const void* raw, int qtype, int64_t n_in, int64_t n_out, void* stream);
+
+/* quant::ffn_swiglu_q (src/quant/mod.rs:1179-1204). */
+int pi_ffn_swiglu_q(pi_ctx* ctx, float* out, const float* x, const void* gate_raw, const void* up_raw,
+                    const void* down_raw, int qtype, int64_t n_embd, int64_t n_ff, void* stream);
+
+/* quant::ffn_swiglu_q_selected (src/quant/mod.rs:1208-1249): empty idx -> zeros,
+ * n_idx >= n_ff -> dense pi_ffn_swiglu_q. */
+int pi_ffn_swiglu_q_selected(pi_ctx* ctx, float* out, const float* x, const void* gate_raw, const void* up_raw,
+                             const void* down_raw, int qtype, int64_t n_embd, int64_t n_ff, const int64_t* idx,
+                             int64_t n_idx, void* stream);
+
+/* ---- MoE layer (weights repacked once into an HBM-resident layout) ----- */
+
+typedef struct pi_moe_layer_desc {
+    int64_t n_embd;         /* d                                                   */
+    int64_t n_ff_exp;       /* expert SwiGLU width f (expert_intermediate_size)    */
+    int64_t n_ff_shexp;     /* shared-expert width; the reference uses n_ff_exp    */
+    int32_t n_expert;       /* E                                                   */
+    int32_t n_expert_used;  /* k                                                   */
+    int32_t qtype;          /* PI_QT_Q8_0 or PI_QT_Q4_0 (experts and shared expert) */
+    int32_t src_on_host;    /* 1: the pointers below are host memory               */
+    const float* router;         /* ffn_gate_inp   f32 [ne0=d, ne1=E]                 */
+    const float* router_bias;    /* optional f32 [E], added to the logits (not in the reference) */
+    const void* gate_exps;       /* ffn_gate_exps  GGUF bytes [ne0=d, ne1=f, ne2=E]   */
+    const void* up_exps;         /* ffn_up_exps    GGUF bytes [ne0=d, ne1=f, ne2=E]   */
+    const void* down_exps;       /* ffn_down_exps  GGUF bytes [ne0=f, ne1=d, ne2=E]   */
+    const void* gate_shexp;      /* optional ffn_gate_shexp [ne0=d, ne1=f_sh]         */
+    const void* up_shexp;        /* optional ffn_up_shexp                             */
+    const void* down_shexp;      /* optional ffn_down_shexp [ne0=f_sh, ne1=d]         */
+    const float* gate_inp_shexp; /* optional ffn_gate_inp_shexp f32 [d]               */
+} pi_moe_layer_desc;
+
+/* Builds the device layer: repacks each expert slice (weights.rs:78-113
+ * expert_raw_slice) from GGUF array-of-blocks to structure-of-arrays. */
+int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* desc, pi_moe_layer** out);
+void pi_moe_layer_destroy(pi_moe_layer* layer);
+
+/* Routing only: model/mod.rs:1254-1312 for T tokens x [T][d] (f32, device).
+ * idx/gates [T][k] (ascending expert per token; renormalised gates),
+ * counts/offsets [E], perm [T*k] (perm[offsets[e]+r] = r-th token routed to e,
+ * tokens ascending). Any output pointer may be NULL. */
+int pi_moe_route(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, int32_t* idx, float* gates,
+                 int32_t* counts, int32_t* offsets, int32_t* perm, void* stream);
+
+/* Full MoE FFN for T tokens: router -> top-k -> dispatch -> expert SwiGLU ->
+ * gate-weighted combine + sigmoid-gated shared expert
+ * (model/mod.rs:1245-1571). out [T][d] f32. flags: PI_FWD_*. */
+int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, float* out, int32_t flags,
+                   void* stream);
+
+/* MoeRouter::route of the standalone operator API (src/moe/mod.rs:69-108)
+ * for T tokens: router f32 expert-major [E][d] (row e = column e of the
+ * reference's row-major [d, E] gate), logits summed sequentially, top-k by
+ * logit (ties to the lowest index) in descending-logit order, softmax over
+ * the selected k (ops::softmax, src/ops.rs:160-180). idx/weights [T][k]. */
+int pi_router_topk_softmax(pi_ctx* ctx, const float* x, int64_t T, const float* router, int64_t d, int32_t E,
+                           int32_t k, int32_t* idx, float* weights, void* stream);
+
+/* ---- hot-neuron sparse dense FFN --------------------------------------- */
+
+/* Dense SwiGLU FFN weights for the sparse path (model/mod.rs:1573-1612):
+ * gate/up GGUF [ne0=n_embd, ne1=n_ff], down [ne0=n_ff, ne1=n_embd]. The down
+ * projection is repacked neuron-major so active neurons are contiguous. */
+int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const void* up_raw, const void* down_raw, int32_t qtype,
+                         int64_t n_embd, int64_t n_ff, int32_t src_on_host, pi_sparse_ffn** out);
+void pi_sparse_ffn_destroy(pi_sparse_ffn* ffn);
+
+/* ffn_swiglu_q_selected per token (quant/mod.rs:1208-1249, called per token at
+ * model/mod.rs:1601-1612) for T tokens, token t using the ascending neuron
+ * list idx[ptr[t] .. ptr[t+1]) (CSR, int64 device arrays, ptr has T+1 entries).
+ * out [T][n_embd]. An empty list gives zeros; a list of n_ff or more neurons
+ * gives the dense FFN. */
+int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* ffn, const float* x, int64_t T, const int64_t* ptr,
+                          const int64_t* idx, float* out, void* stream);
+
+/* Predictor::predict (src/predictor/mod.rs:63-84): probs = sigmoid(W2 relu(W1 a + b1) + b2)
+ * for T inputs a [T][n_in]; W1 [n_hidden][n_in], W2 [n_out][n_hidden] row-major f32. */
+int pi_predictor_forward(pi_ctx* ctx, const float* a, int64_t T, const float* W1, const float* b1, const float* W2,
+                         const float* b2, int64_t n_in, int64_t n_hidden, int64_t n_out, float* probs, void* stream);
+
+/* ---- synthetic inputs (benchmarks and tests; no reference counterpart) --
+ * out[i] = std * N(0,1) from SplitMix64 (model/mod.rs:2041-2061) + Box-Muller,
+ * element i of stream `seed` (i = 2m, 2m+1 take the cos / sin halves of pair m). */
+int pi_synth_normal(pi_ctx* ctx, uint64_t seed, uint64_t offset, int64_t n, float std, float* out, void* stream);
+/* The same values computed on the host (x86 libm), for fixtures. */
+int pi_synth_normal_host(uint64_t seed, uint64_t offset, int64_t n, float std, float* out);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PI_MOE_H */

@@ -1,0 +1,120 @@
+// Internal (non-ABI) declarations shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+#include <deque>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+#include "../../include/pi_moe.h"
+
+// One quantised matrix family stored structure-of-arrays in HBM:
+//   Q8_0: q = int8  [n][rows][cols]        d = f16 [n][rows][cols/32]
+//   Q4_0: q = uint8 [n][rows][cols/2]      d = f16 [n][rows][cols/32]
+//         (the 16 nibble bytes of each GGUF block kept in their original
+//          order: byte i low nibble = element 2i, high nibble = 2i+1)
+//   F32 : q = float [n][rows][cols]        d = null
+// Rows are 16-byte aligned whenever cols % 32 == 0 (Q8_0) or % 64 == 0 (Q4_0),
+// which the layer constructor requires, so kernels use 16-byte vector loads.
+struct PiMats {
+    int qtype = PI_QT_F32;
+    int64_t n = 0, rows = 0, cols = 0;
+    void* q = nullptr;
+    __half* d = nullptr;
+    int64_t q_row_bytes() const {
+        return qtype == PI_QT_Q8_0 ? cols : (qtype == PI_QT_Q4_0 ? cols / 2 : cols * 4);
+    }
+    int64_t q_mat_bytes() const { return q_row_bytes() * rows; }
+    int64_t d_mat_elems() const { return rows * (cols / 32); }
+};
+
+struct pi_moe_layer {
+    pi_ctx* ctx = nullptr;
+    int64_t d = 0, f = 0, f_sh = 0;
+    int E = 0, k = 0, qtype = 0;
+    bool has_shared = false, has_shared_gate = false, has_bias = false;
+    float* router = nullptr;   // f32 [E + 1][d]; row E = shared-expert gate vector (zeros if absent)
+    float* bias = nullptr;     // f32 [E] or null
+    PiMats gate, up, down;     // routed experts: gate/up [E][f][d], down [E][d][f]
+    PiMats gate_sh, up_sh, down_sh;  // shared expert (n = 1)
+    std::vector<void*> allocs;
+};
+
+struct pi_sparse_ffn {
+    pi_ctx* ctx = nullptr;
+    int64_t n_embd = 0, n_ff = 0;
+    int qtype = 0;
+    PiMats gate, up;           // [1][n_ff][n_embd]
+    // down projection repacked neuron-major: for neuron s, the n_embd weights
+    // W_down[c][s] (c = 0..n_embd-1) are contiguous.
+    //   Q4_0: nib [n_ff][n_embd/2] (element c of neuron s in byte c/2, low
+    //         nibble for even c); scale [n_ff/32][n_embd] f16 (the GGUF block
+    //         scale of W_down row c, block s/32 — shared by 32 neurons)
+    //   Q8_0: q [n_ff][n_embd] int8, same scale layout
+    void* down_q = nullptr;
+    __half* down_d = nullptr;
+    std::vector<void*> allocs;
+};
+
+// Per-stream scratch arena (grown on demand, never shrunk).
+struct PiArena {
+    char* base = nullptr;
+    size_t cap = 0;
+};
+
+// Optional per-kernel timing (CUDA events recorded around each launch of
+// the layer path on its stream; totals read back by pi_ctx_profile_read).
+struct PiProfEntry {
+    std::string name;
+    std::vector<cudaEvent_t> beg, end;  // one pair per launch since the last read
+    double total_ms = 0;
+    long launches = 0;
+};
+
+struct pi_ctx {
+    int device = 0;
+    bool profiling = false;
+    std::deque<PiProfEntry> prof;  // deque: entries never move while a scope holds one
+    int sm_count = 0;
+    std::mutex mu;
+    std::string last_error;
+    std::unordered_map<cudaStream_t, PiArena> arenas;
+    uint32_t* dev_err = nullptr;  // device error word
+};
+
+// Bump allocator over an arena; every sub-buffer is 256-byte aligned.
+struct PiBump {
+    char* base;
+    size_t off = 0;
+    template <typename T>
+    T* take(size_t count) {
+        off = (off + 255) & ~size_t(255);
+        T* p = reinterpret_cast<T*>(base + off);
+        off += count * sizeof(T);
+        return p;
+    }
+};
+
+int pi_set_error(pi_ctx* ctx, int code, const std::string& msg);
+// Kernel timing scope: records an event pair on `st` when profiling is on.
+struct PiProfScope {
+    pi_ctx* ctx;
+    cudaStream_t st;
+    PiProfEntry* e = nullptr;
+    PiProfScope(pi_ctx* c, cudaStream_t s, const char* name);
+    ~PiProfScope();
+};
+int pi_cuda_check(pi_ctx* ctx, cudaError_t e, const char* what);
+// Returns scratch of at least `bytes` for `stream` (allocating if needed).
+int pi_scratch(pi_ctx* ctx, cudaStream_t stream, size_t bytes, char** out);
+
+// Layer forward pieces (pi_moe.cu)
+size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T);
+int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
+               float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
+               cudaStream_t st);
+int pi_repack_mats(pi_ctx* ctx, PiMats* m, const void* raw, int qtype, int64_t n, int64_t rows, int64_t cols,
+                   int src_on_host, std::vector<void*>* allocs);

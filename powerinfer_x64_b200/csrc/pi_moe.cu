@@ -1,0 +1,937 @@
+// MoE feed-forward layer on B200: routing, dispatch, expert SwiGLU, combine.
+//
+// Reference path being replaced: model/mod.rs:1245-1571 (one token at a
+// time, two CPU threads of quant::ffn_swiglu_q calls). Here one call runs a
+// whole batch of T tokens through six kernels on one stream:
+//
+//   k_prep        RMSNorm (optional, ops.rs:13-27 lane order) + Q8_0
+//                 activation quantiser (quant/mod.rs:698-736), per token.
+//   k_router      exact router logits: the reference's sequential f32 sum
+//                 (quant/mod.rs:921-935) per (token, expert), plus the
+//                 shared-expert gate dot (model/mod.rs:1500-1509) as row E.
+//   k_topk        softmax -> top-k (ties to the lowest index) -> ascending
+//                 sort -> renormalised gates (model/mod.rs:1278-1312).
+//   k_dispatch    per-expert counts, offsets, stable token permutation and
+//                 the work-item list for the expert kernels (no reference
+//                 counterpart: the reference loops token by token).
+//   k_gateup_*    gate+up GEMV over the tokens of each work item, SwiGLU,
+//                 and (Q8_0) re-quantisation of h (quant/mod.rs:1179-1204).
+//   k_down_*      down-projection GEMV per routed (token, expert) slot.
+//   k_combine     ascending-expert gate-weighted sum + sigmoid-gated shared
+//                 expert + optional residual (model/mod.rs:1525-1534,
+//                 :1627-1633), in the reference's exact f32 order.
+//
+// The expert kernels stream each weight row from HBM exactly once per work
+// item with 16-byte coalesced loads and keep it in registers while looping
+// over the item's tokens (decode-sized T: HBM-bound).
+#include "pi_common.cuh"
+#include "pi_internal.h"
+
+#include <algorithm>
+
+namespace {
+
+constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one warp per token)
+
+// ---------------------------------------------------------------------------
+// k_prep: optional RMSNorm, then Q8_0 quantisation of the (normed) tokens.
+// grid T, block 256.
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
+                                              float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
+                                              float* __restrict__ xs) {
+    const int t = blockIdx.x;
+    const float* xr = x + (size_t)t * d;
+    __shared__ float s_inv;
+    const float* src = xr;
+    if (do_norm) {
+        // sum_squares_sse (simd.rs:116-137): 4 lane accumulators over
+        // elements i = 4m + lane, then (l0 + l1) + (l2 + l3), then a scalar tail.
+        if (threadIdx.x < 32) {
+            const int lane = threadIdx.x;
+            float acc = 0.0f;
+            const int n4 = d & ~3;
+            if (lane < 4)
+                for (int i = lane; i < n4; i += 4) acc = fadd(acc, fmul(xr[i], xr[i]));
+            float a1 = __shfl_sync(0xffffffffu, acc, 1);
+            float a2 = __shfl_sync(0xffffffffu, acc, 2);
+            float a3 = __shfl_sync(0xffffffffu, acc, 3);
+            if (lane == 0) {
+                float ss = fadd(fadd(acc, a1), fadd(a2, a3));
+                for (int i = n4; i < d; ++i) ss = fadd(ss, fmul(xr[i], xr[i]));
+                float rms = __fsqrt_rn(fadd(fdiv(ss, (float)d), eps));
+                s_inv = fdiv(1.0f, rms);
+            }
+        }
+        __syncthreads();
+        const float inv = s_inv;
+        float* nr = normed + (size_t)t * d;
+        for (int i = threadIdx.x; i < d; i += blockDim.x) nr[i] = fmul(xr[i], inv);  // * weight (1.0) is exact
+        __syncthreads();
+        src = nr;
+    }
+    if (!do_quant) return;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nb = d / 32;
+    for (int b = warp; b < nb; b += blockDim.x / 32) {
+        float sc;
+        int8_t q = warp_quant_q8(src[b * 32 + lane], &sc);
+        xq[(size_t)t * d + b * 32 + lane] = q;
+        if (lane == 0) xs[(size_t)t * nb + b] = sc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_router: exact logits. Thread = expert row (E routed rows + row E for the
+// shared-expert gate), TT tokens per CTA, each chain a sequential f32 sum in
+// the reference's order: sum = sum + w[i] * x[i], i ascending, no FMA.
+// grid (ceil((E+1)/128), ceil(T/TT)), block 128.
+// ---------------------------------------------------------------------------
+constexpr int RT_TT = 8, RT_CH = 256;
+__global__ __launch_bounds__(128) void k_router(const float* __restrict__ xin, const float* __restrict__ W,
+                                                const float* __restrict__ bias, int T, int d, int E, int nrows,
+                                                float* __restrict__ logits) {
+    __shared__ __align__(16) float xs[RT_TT][RT_CH];
+    const int Ep1 = E + 1;
+    const int e = blockIdx.x * 128 + threadIdx.x;
+    const int t0 = blockIdx.y * RT_TT;
+    const int nt = min(RT_TT, T - t0);
+    const float* wr = W + (size_t)min(e, nrows - 1) * d;
+    float acc[RT_TT];
+#pragma unroll
+    for (int t = 0; t < RT_TT; ++t) acc[t] = 0.0f;
+    for (int c0 = 0; c0 < d; c0 += RT_CH) {
+        __syncthreads();
+        for (int q = threadIdx.x; q < RT_TT * RT_CH; q += 128) {
+            int t = q / RT_CH, i = q % RT_CH;
+            xs[t][i] = (t < nt && c0 + i < d) ? xin[(size_t)(t0 + t) * d + c0 + i] : 0.0f;
+        }
+        __syncthreads();
+        const int lim = min(RT_CH, d - c0);
+        for (int i = 0; i < lim; i += 4) {
+            float4 w = __ldg(reinterpret_cast<const float4*>(wr + c0 + i));
+#pragma unroll
+            for (int t = 0; t < RT_TT; ++t) {
+                float4 xv = *reinterpret_cast<const float4*>(&xs[t][i]);
+                float a = acc[t];
+                a = fadd(a, fmul(w.x, xv.x));
+                a = fadd(a, fmul(w.y, xv.y));
+                a = fadd(a, fmul(w.z, xv.z));
+                a = fadd(a, fmul(w.w, xv.w));
+                acc[t] = a;
+            }
+        }
+    }
+    if (e >= nrows) return;
+#pragma unroll
+    for (int t = 0; t < RT_TT; ++t) {
+        if (t < nt) {
+            float v = acc[t];
+            if (bias && e < E) v = fadd(v, bias[e]);
+            logits[(size_t)(t0 + t) * Ep1 + e] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_topk: one warp per token. E <= 32 * TK_PER_LANE.
+// ---------------------------------------------------------------------------
+constexpr int TK_PER_LANE = 16, TK_WARPS = 4;
+__global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits, int T, int E, int k,
+                                                        int has_shgate, int32_t* __restrict__ idx,
+                                                        float* __restrict__ gates, float* __restrict__ shscale,
+                                                        int32_t* __restrict__ counts) {
+    __shared__ float s_p[TK_WARPS][32 * TK_PER_LANE];
+    __shared__ int s_sel[TK_WARPS][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * TK_WARPS + warp;
+    if (t >= T) return;
+    const float* lr = logits + (size_t)t * (E + 1);
+    float l[TK_PER_LANE];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        int e = lane + 32 * j;
+        l[j] = (e < E) ? lr[e] : -INFINITY;
+        if (e < E) m = fmaxf(m, l[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float* p = s_p[warp];
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        int e = lane + 32 * j;
+        if (e < E) p[e] = exp_cr(fsub(l[j], m));
+    }
+    __syncwarp();
+    // exp_sum: sequential sum in expert order (model/mod.rs:1282)
+    float es = 0.0f;
+    if (lane == 0)
+        for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
+    es = __shfl_sync(0xffffffffu, es, 0);
+    float pr[TK_PER_LANE];
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        int e = lane + 32 * j;
+        pr[j] = (e < E) ? fdiv(p[e], es) : -INFINITY;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        int e = lane + 32 * j;
+        if (e < E) p[e] = pr[j];
+    }
+    // top-k by probability, ties broken to the lowest expert index
+    uint32_t taken = 0;
+    for (int r = 0; r < k; ++r) {
+        float bp = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < TK_PER_LANE; ++j) {
+            int e = lane + 32 * j;
+            if (e < E && !((taken >> j) & 1u) && (pr[j] > bp || (pr[j] == bp && e < bi))) { bp = pr[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == 0) s_sel[warp][r] = bi;
+    }
+    __syncwarp();
+    // ascending sort of the k selected indices (model/mod.rs:1303)
+    int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
+    int rank = 0;
+    for (int r = 0; r < k; ++r) rank += (s_sel[warp][r] < mine);
+    __syncwarp();
+    if (lane < k) s_sel[warp][rank] = mine;
+    __syncwarp();
+    float ssum = 0.0f;
+    if (lane == 0)
+        for (int r = 0; r < k; ++r) ssum = fadd(ssum, p[s_sel[warp][r]]);
+    ssum = __shfl_sync(0xffffffffu, ssum, 0);
+    if (lane < k) {
+        int e = s_sel[warp][lane];
+        float pe = p[e];
+        idx[(size_t)t * k + lane] = e;
+        gates[(size_t)t * k + lane] = (ssum > 0.0f) ? fdiv(pe, ssum) : pe;
+        atomicAdd(&counts[e], 1);
+    }
+    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
+}
+
+// ---------------------------------------------------------------------------
+// k_topk_api: MoeRouter::route of the standalone operator API
+// (moe/mod.rs:69-108): top-k by logit (ties to the lowest index), ordered by
+// descending logit, then ops::softmax over the k selected (ops.rs:160-180:
+// max, v = exp(v - max), sequential sum, v *= 1/sum).
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(TK_WARPS * 32) void k_topk_api(const float* __restrict__ logits, int T, int E, int k,
+                                                            int32_t* __restrict__ idx, float* __restrict__ wts) {
+    __shared__ int s_sel[TK_WARPS][32];
+    __shared__ float s_v[TK_WARPS][32];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * TK_WARPS + warp;
+    if (t >= T) return;
+    const float* lr = logits + (size_t)t * (E + 1);
+    float l[TK_PER_LANE];
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        int e = lane + 32 * j;
+        l[j] = (e < E) ? lr[e] : -INFINITY;
+    }
+    uint32_t taken = 0;
+    for (int r = 0; r < k; ++r) {
+        float bp = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < TK_PER_LANE; ++j) {
+            int e = lane + 32 * j;
+            if (e < E && !((taken >> j) & 1u) && (l[j] > bp || (l[j] == bp && e < bi))) { bp = l[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            float op = __shfl_xor_sync(0xffffffffu, bp, o);
+            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == 0) { s_sel[warp][r] = bi; s_v[warp][r] = bp; }
+    }
+    __syncwarp();
+    if (lane == 0) {
+        float mx = -INFINITY;
+        for (int r = 0; r < k; ++r) mx = fmaxf(mx, s_v[warp][r]);
+        float sum = 0.0f;
+        for (int r = 0; r < k; ++r) {
+            const float v = exp_cr(fsub(s_v[warp][r], mx));
+            s_v[warp][r] = v;
+            sum = fadd(sum, v);
+        }
+        const float inv = fdiv(1.0f, sum);
+        for (int r = 0; r < k; ++r) {
+            idx[(size_t)t * k + r] = s_sel[warp][r];
+            wts[(size_t)t * k + r] = fmul(s_v[warp][r], inv);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_dispatch: one CTA per expert (+ CTA E for the shared expert's items).
+// offsets[e] = sum counts[<e]; perm lists the tokens routed to e ascending;
+// slot_of[t*k+j] = slot of (token t, its j-th expert); work items of <= TG
+// tokens: item = {expert, first slot, n tokens}. Shared-expert slots follow
+// the T*k routed slots (slot T*k + t for token t).
+// ---------------------------------------------------------------------------
+__device__ int block_sum_int(int v, int* red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    int s = 0;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) s += red[w];
+    return s;
+}
+
+__global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ idx, const int32_t* __restrict__ counts,
+                                                  int T, int k, int E, int has_shared, int32_t* __restrict__ offsets,
+                                                  int32_t* __restrict__ perm, int32_t* __restrict__ slot_of,
+                                                  int4* __restrict__ items, int32_t* __restrict__ n_items) {
+    __shared__ int red[8];
+    __shared__ int s_wsum[8];
+    const int e = blockIdx.x;
+    int s_off = 0, s_items = 0;
+    for (int i = threadIdx.x; i < e; i += blockDim.x) {
+        int c = counts[i];
+        s_off += c;
+        s_items += (c + TG - 1) / TG;
+    }
+    const int off = block_sum_int(s_off, red);
+    const int ibase = block_sum_int(s_items, red);
+    if (e == E) {  // shared-expert items + total item count
+        int n_routed_items = ibase;
+        int nsh = has_shared ? (T + TG - 1) / TG : 0;
+        for (int q = threadIdx.x; q < nsh; q += blockDim.x)
+            items[n_routed_items + q] = make_int4(E, T * k + q * TG, min(TG, T - q * TG), 0);
+        if (threadIdx.x == 0) *n_items = n_routed_items + nsh;
+        return;
+    }
+    const int cnt = counts[e];
+    if (threadIdx.x == 0 && offsets) offsets[e] = off;
+    const int nI = (cnt + TG - 1) / TG;
+    for (int q = threadIdx.x; q < nI; q += blockDim.x)
+        items[ibase + q] = make_int4(e, off + q * TG, min(TG, cnt - q * TG), 0);
+    if (cnt == 0) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int base = 0;
+    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
+        const int t = t0 + threadIdx.x;
+        int jsel = -1;
+        if (t < T)
+            for (int j = 0; j < k; ++j)
+                if (idx[(size_t)t * k + j] == e) jsel = j;
+        const unsigned bal = __ballot_sync(0xffffffffu, jsel >= 0);
+        const int wrank = __popc(bal & ((1u << lane) - 1u));
+        __syncthreads();
+        if (lane == 0) s_wsum[warp] = __popc(bal);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+            if (w < warp) before += s_wsum[w];
+            total += s_wsum[w];
+        }
+        if (jsel >= 0) {
+            const int slot = off + base + before + wrank;
+            perm[slot] = t;
+            slot_of[(size_t)t * k + jsel] = slot;
+        }
+        base += total;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Expert GEMV kernels.
+// ---------------------------------------------------------------------------
+struct ExpertArgs {
+    // routed experts
+    const void* g;
+    const void* u;
+    const void* dn;
+    const __half* gd;
+    const __half* ud;
+    const __half* dd;
+    // shared expert (n = 1)
+    const void* gs;
+    const void* us;
+    const void* dns;
+    const __half* gsd;
+    const __half* usd;
+    const __half* dsd;
+    int E, d, f;  // f = routed and shared width (equal)
+    const int4* items;
+    const int32_t* n_items;
+    const int32_t* perm;
+    int n_routed;  // T*k
+    // activations
+    const int8_t* xq;  // Q8_0 path: quantised tokens [T][d]
+    const float* xs;   // Q8_0 path: scales [T][d/32]
+    const float* xf;   // Q4_0 path: f32 tokens [T][d]
+    // hidden
+    int8_t* hq;  // Q8_0: [slots][f]
+    float* hs;   // Q8_0: [slots][f/32]
+    float* hf;   // Q4_0: [slots][f]
+    float* y;    // [slots][d]
+};
+
+PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
+
+// Q8_0 gate+up: CTA = 32 rows of one expert (16 warps x 2 rows, gate and up),
+// CPL = d/512 16-byte chunks per lane per row (lane l holds chunks l + 32c;
+// chunk pairs (2m, 2m+1) form 32-element block m).
+template <int CPL>
+__global__ __launch_bounds__(512) void k_gateup_q8(ExpertArgs a) {
+    __shared__ float hbuf[TG][33];
+    const int it = blockIdx.y;
+    if (it >= *a.n_items) return;
+    const int4 item = a.items[it];
+    const bool sh = (item.x == a.E);
+    const int d = a.d, f = a.f, nb = d / 32;
+    const int row0 = blockIdx.x * 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int rA = row0 + 2 * warp;
+    const size_t mat = sh ? 0 : (size_t)item.x * f;
+    const int8_t* G = (const int8_t*)(sh ? a.gs : a.g) + (mat + rA) * d;
+    const int8_t* U = (const int8_t*)(sh ? a.us : a.u) + (mat + rA) * d;
+    const __half* GD = (sh ? a.gsd : a.gd) + (mat + rA) * nb;
+    const __half* UD = (sh ? a.usd : a.ud) + (mat + rA) * nb;
+    int4 w[4][CPL];
+    float sw[4][CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        const int ch = lane + 32 * c;
+        w[0][c] = ld_stream(G + ch * 16);
+        w[1][c] = ld_stream(U + ch * 16);
+        w[2][c] = ld_stream(G + d + ch * 16);
+        w[3][c] = ld_stream(U + d + ch * 16);
+        sw[0][c] = __half2float(GD[ch >> 1]);
+        sw[1][c] = __half2float(UD[ch >> 1]);
+        sw[2][c] = __half2float(GD[nb + (ch >> 1)]);
+        sw[3][c] = __half2float(UD[nb + (ch >> 1)]);
+    }
+    const bool even = (lane & 1) == 0;
+    for (int tk = 0; tk < item.z; ++tk) {
+        const int slot = item.y + tk;
+        const int tok = slot_token(a, sh, slot);
+        const int8_t* xr = a.xq + (size_t)tok * d;
+        const float* sr = a.xs + (size_t)tok * nb;
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int ch = lane + 32 * c;
+            const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
+            const float sx = even ? sr[ch >> 1] : 0.0f;
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+                int s = dp4a(w[r][c].x, xv.x, 0);
+                s = dp4a(w[r][c].y, xv.y, s);
+                s = dp4a(w[r][c].z, xv.z, s);
+                s = dp4a(w[r][c].w, xv.w, s);
+                s += __shfl_xor_sync(0xffffffffu, s, 1);
+                acc[r] += (float)s * (sw[r][c] * sx);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < 4; ++r) acc[r] = warp_sum(acc[r]);
+        if (lane == 0) {
+            hbuf[tk][2 * warp] = swiglu_ref(acc[0], acc[1]);
+            hbuf[tk][2 * warp + 1] = swiglu_ref(acc[2], acc[3]);
+        }
+    }
+    __syncthreads();
+    if (warp < item.z) {
+        const int slot = item.y + warp;
+        float sc;
+        const int8_t q = warp_quant_q8(hbuf[warp][lane], &sc);
+        a.hq[(size_t)slot * f + row0 + lane] = q;
+        if (lane == 0) a.hs[(size_t)slot * (f / 32) + row0 / 32] = sc;
+    }
+}
+
+// Q8_0 down: CTA = 128 output rows (8 warps x 16 rows), 4 lanes per row,
+// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass.
+template <int CPQ>
+__global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
+    const int it = blockIdx.y;
+    if (it >= *a.n_items) return;
+    const int4 item = a.items[it];
+    const bool sh = (item.x == a.E);
+    const int d = a.d, f = a.f, fb = f / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = lane & 3;
+    const int rbase = blockIdx.x * 128 + warp * 16 + (lane >> 2);
+    const size_t mat = sh ? 0 : (size_t)item.x * d;
+    const int8_t* D = (const int8_t*)(sh ? a.dns : a.dn) + mat * f;
+    const __half* DD = (sh ? a.dsd : a.dd) + mat * fb;
+    constexpr int BPQ = CPQ / 2;  // blocks per lane
+    int4 w[2][CPQ];
+    float sw[2][BPQ];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+        const int row = rbase + 8 * p;
+#pragma unroll
+        for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)row * f + (q * CPQ + c) * 16);
+#pragma unroll
+        for (int b = 0; b < BPQ; ++b) sw[p][b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
+    }
+    for (int tk = 0; tk < item.z; ++tk) {
+        const int slot = item.y + tk;
+        const int8_t* hr = a.hq + (size_t)slot * f + q * CPQ * 16;
+        const float* hsr = a.hs + (size_t)slot * fb + q * BPQ;
+        int4 hv[CPQ];
+        float hsv[BPQ];
+#pragma unroll
+        for (int c = 0; c < CPQ; ++c) hv[c] = *reinterpret_cast<const int4*>(hr + c * 16);
+#pragma unroll
+        for (int b = 0; b < BPQ; ++b) hsv[b] = hsr[b];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+            float acc = 0.f;
+#pragma unroll
+            for (int b = 0; b < BPQ; ++b) {
+                int s = 0;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int4 wv = w[p][2 * b + h], xv = hv[2 * b + h];
+                    s = dp4a(wv.x, xv.x, s);
+                    s = dp4a(wv.y, xv.y, s);
+                    s = dp4a(wv.z, xv.z, s);
+                    s = dp4a(wv.w, xv.w, s);
+                }
+                acc += (float)s * (sw[p][b] * hsv[b]);
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (q == 0) a.y[(size_t)slot * d + rbase + 8 * p] = acc;
+        }
+    }
+}
+
+// Q4_0 helpers: the 16 nibble bytes of a block hold elements 2i (low) and
+// 2i+1 (high) of byte i; value = (nibble - 8) * d.
+PI_DEV float nib_f(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616.0f; }  // v - 8, exact
+
+// dot of one Q4_0 block (16 nibble bytes) with 32 f32 values held in registers
+PI_DEV float q4_dot_regs(const int4 wv, const float (&xv)[32]) {
+    const uint32_t wd[4] = {(uint32_t)wv.x, (uint32_t)wv.y, (uint32_t)wv.z, (uint32_t)wv.w};
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s = fmaf(nib_f((wd[i] >> (4 * j)) & 15u), xv[8 * i + j], s);
+    }
+    return s;
+}
+
+PI_DEV void load32(const float* __restrict__ x, float (&xv)[32]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 v = *reinterpret_cast<const float4*>(x + 4 * i);
+        xv[4 * i] = v.x;
+        xv[4 * i + 1] = v.y;
+        xv[4 * i + 2] = v.z;
+        xv[4 * i + 3] = v.w;
+    }
+}
+
+// Q4_0 gate+up with f32 activations (the reference dequantises Q4_0 and
+// runs an f32 dot, quant/mod.rs:958-969). CPL = d/1024 blocks per lane per row.
+template <int CPL>
+__global__ __launch_bounds__(512) void k_gateup_q4(ExpertArgs a) {
+    const int it = blockIdx.y;
+    if (it >= *a.n_items) return;
+    const int4 item = a.items[it];
+    const bool sh = (item.x == a.E);
+    const int d = a.d, f = a.f, nb = d / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t mat = sh ? 0 : (size_t)item.x * f;
+    // one row (gate and up) at a time keeps the weights of 2 x CPL blocks in registers
+#pragma unroll 1
+    for (int rr = 0; rr < 2; ++rr) {
+        const int row = blockIdx.x * 32 + 2 * warp + rr;
+        const uint8_t* G = (const uint8_t*)(sh ? a.gs : a.g) + (mat + row) * (d / 2);
+        const uint8_t* U = (const uint8_t*)(sh ? a.us : a.u) + (mat + row) * (d / 2);
+        const __half* GD = (sh ? a.gsd : a.gd) + (mat + row) * nb;
+        const __half* UD = (sh ? a.usd : a.ud) + (mat + row) * nb;
+        int4 wg[CPL], wu[CPL];
+        float sg[CPL], su[CPL];
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int b = lane + 32 * c;
+            wg[c] = ld_stream(G + b * 16);
+            wu[c] = ld_stream(U + b * 16);
+            sg[c] = __half2float(GD[b]);
+            su[c] = __half2float(UD[b]);
+        }
+#pragma unroll 1
+        for (int tk = 0; tk < item.z; ++tk) {
+            const int slot = item.y + tk;
+            const int tok = slot_token(a, sh, slot);
+            const float* xr = a.xf + (size_t)tok * d;
+            float ag = 0.f, au = 0.f;
+#pragma unroll
+            for (int c = 0; c < CPL; ++c) {
+                float xv[32];
+                load32(xr + (lane + 32 * c) * 32, xv);
+                ag += sg[c] * q4_dot_regs(wg[c], xv);
+                au += su[c] * q4_dot_regs(wu[c], xv);
+            }
+            ag = warp_sum(ag);
+            au = warp_sum(au);
+            if (lane == 0) a.hf[(size_t)slot * f + row] = swiglu_ref(ag, au);
+        }
+    }
+}
+
+// Q4_0 down with f32 hidden: 4 lanes per row, BPQ = f/128 blocks per lane.
+template <int BPQ>
+__global__ __launch_bounds__(256) void k_down_q4(ExpertArgs a) {
+    const int it = blockIdx.y;
+    if (it >= *a.n_items) return;
+    const int4 item = a.items[it];
+    const bool sh = (item.x == a.E);
+    const int d = a.d, f = a.f, fb = f / 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int q = lane & 3;
+    const size_t mat = sh ? 0 : (size_t)item.x * d;
+    const uint8_t* D = (const uint8_t*)(sh ? a.dns : a.dn) + mat * (f / 2);
+    const __half* DD = (sh ? a.dsd : a.dd) + mat * fb;
+#pragma unroll 1
+    for (int p = 0; p < 2; ++p) {
+        const int row = blockIdx.x * 128 + warp * 16 + (lane >> 2) + 8 * p;
+        int4 w[BPQ];
+        float sw[BPQ];
+#pragma unroll
+        for (int b = 0; b < BPQ; ++b) {
+            w[b] = ld_stream(D + (size_t)row * (f / 2) + (q * BPQ + b) * 16);
+            sw[b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
+        }
+#pragma unroll 1
+        for (int tk = 0; tk < item.z; ++tk) {
+            const int slot = item.y + tk;
+            const float* hr = a.hf + (size_t)slot * f + q * BPQ * 32;
+            float acc = 0.f;
+#pragma unroll
+            for (int b = 0; b < BPQ; ++b) {
+                float xv[32];
+                load32(hr + b * 32, xv);
+                acc += sw[b] * q4_dot_regs(w[b], xv);
+            }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            if (q == 0) a.y[(size_t)slot * d + row] = acc;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_combine: out[t] = (x[t] +) sum_j gates[t][j] * y[slot(t,j)] + s_t * y_sh[t],
+// experts ascending, each step o = o + g * y (no FMA), as model/mod.rs:1525-1534.
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, const float* __restrict__ y,
+                                                 const float* __restrict__ gates, const int32_t* __restrict__ slot_of,
+                                                 const float* __restrict__ shscale, int T, int k, int d,
+                                                 int has_shared, int residual, float* __restrict__ out) {
+    const int t = blockIdx.x;
+    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+        float acc = 0.0f;
+        for (int j = 0; j < k; ++j) {
+            const int slot = slot_of[(size_t)t * k + j];
+            acc = fadd(acc, fmul(gates[(size_t)t * k + j], y[(size_t)slot * d + c]));
+        }
+        if (has_shared) acc = fadd(acc, fmul(shscale[t], y[((size_t)T * k + t) * d + c]));
+        out[(size_t)t * d + c] = residual ? fadd(x[(size_t)t * d + c], acc) : acc;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Repack: GGUF array-of-blocks -> structure-of-arrays (one thread per block).
+// ---------------------------------------------------------------------------
+__global__ void k_repack_q8(const uint8_t* __restrict__ src, int64_t nblk, int8_t* __restrict__ q,
+                            __half* __restrict__ dd) {
+    int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const uint8_t* p = src + b * 34;
+    dd[b] = __ushort_as_half((uint16_t)(p[0] | (p[1] << 8)));
+    uint32_t wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+        wv[i] = (uint32_t)p[2 + 4 * i] | ((uint32_t)p[3 + 4 * i] << 8) | ((uint32_t)p[4 + 4 * i] << 16) |
+                ((uint32_t)p[5 + 4 * i] << 24);
+    int4* o = reinterpret_cast<int4*>(q + b * 32);
+    o[0] = make_int4(wv[0], wv[1], wv[2], wv[3]);
+    o[1] = make_int4(wv[4], wv[5], wv[6], wv[7]);
+}
+
+__global__ void k_repack_q4(const uint8_t* __restrict__ src, int64_t nblk, uint8_t* __restrict__ q,
+                            __half* __restrict__ dd) {
+    int64_t b = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (b >= nblk) return;
+    const uint8_t* p = src + b * 18;
+    dd[b] = __ushort_as_half((uint16_t)(p[0] | (p[1] << 8)));
+    uint32_t wv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+        wv[i] = (uint32_t)p[2 + 4 * i] | ((uint32_t)p[3 + 4 * i] << 8) | ((uint32_t)p[4 + 4 * i] << 16) |
+                ((uint32_t)p[5 + 4 * i] << 24);
+    *reinterpret_cast<int4*>(q + b * 16) = make_int4(wv[0], wv[1], wv[2], wv[3]);
+}
+
+}  // namespace
+
+// ===========================================================================
+// Host side
+// ===========================================================================
+
+static int64_t gguf_bytes(int qtype, int64_t n) {
+    if (qtype == PI_QT_Q8_0) return n / 32 * 34;
+    if (qtype == PI_QT_Q4_0) return n / 32 * 18;
+    if (qtype == PI_QT_F32) return n * 4;
+    return -1;
+}
+
+int pi_repack_mats(pi_ctx* ctx, PiMats* m, const void* raw, int qtype, int64_t n, int64_t rows, int64_t cols,
+                   int src_on_host, std::vector<void*>* allocs) {
+    m->qtype = qtype;
+    m->n = n;
+    m->rows = rows;
+    m->cols = cols;
+    const int64_t per_mat = gguf_bytes(qtype, rows * cols);
+    const int64_t qb = m->q_mat_bytes() * n;
+    const int64_t nd = m->d_mat_elems() * n;
+    if (pi_cuda_check(ctx, cudaMalloc(&m->q, (size_t)qb), "cudaMalloc(weights)")) return PI_ERR_OOM;
+    allocs->push_back(m->q);
+    if (pi_cuda_check(ctx, cudaMalloc(&m->d, (size_t)nd * 2), "cudaMalloc(scales)")) return PI_ERR_OOM;
+    allocs->push_back(m->d);
+    // Stage host sources one matrix at a time.
+    void* stage = nullptr;
+    if (src_on_host) {
+        if (pi_cuda_check(ctx, cudaMalloc(&stage, (size_t)per_mat), "cudaMalloc(stage)")) return PI_ERR_OOM;
+    }
+    const int64_t nblk = rows * cols / 32;
+    int rc = PI_OK;
+    for (int64_t i = 0; i < n && rc == PI_OK; ++i) {
+        const uint8_t* src = (const uint8_t*)raw + i * per_mat;
+        if (src_on_host) {
+            if (pi_cuda_check(ctx, cudaMemcpy(stage, src, (size_t)per_mat, cudaMemcpyHostToDevice), "upload")) {
+                rc = PI_ERR_CUDA;
+                break;
+            }
+            src = (const uint8_t*)stage;
+        }
+        const int thr = 256;
+        const int64_t grid = (nblk + thr - 1) / thr;
+        if (qtype == PI_QT_Q8_0)
+            k_repack_q8<<<(unsigned)grid, thr>>>(src, nblk, (int8_t*)m->q + i * m->q_mat_bytes(),
+                                                  m->d + i * m->d_mat_elems());
+        else
+            k_repack_q4<<<(unsigned)grid, thr>>>(src, nblk, (uint8_t*)m->q + i * m->q_mat_bytes(),
+                                                  m->d + i * m->d_mat_elems());
+        if (pi_cuda_check(ctx, cudaGetLastError(), "repack")) rc = PI_ERR_CUDA;
+        if (src_on_host && rc == PI_OK && pi_cuda_check(ctx, cudaDeviceSynchronize(), "repack sync"))
+            rc = PI_ERR_CUDA;
+    }
+    if (stage) cudaFree(stage);
+    if (rc == PI_OK && pi_cuda_check(ctx, cudaDeviceSynchronize(), "repack")) rc = PI_ERR_CUDA;
+    return rc;
+}
+
+namespace {
+struct FwdBufs {
+    float* normed;
+    int8_t* xq;
+    float* xs;
+    float* logits;
+    int32_t* idx;
+    float* gates;
+    float* shscale;
+    int32_t* counts;
+    int32_t* offsets;
+    int32_t* perm;
+    int32_t* slot_of;
+    int4* items;
+    int32_t* n_items;
+    int8_t* hq;
+    float* hs;
+    float* hf;
+    float* y;
+    size_t bytes;
+};
+
+int64_t max_items(const pi_moe_layer* L, int64_t T) {
+    const int64_t Tk = T * L->k;
+    return std::min<int64_t>(L->E, Tk) + (Tk + TG - 1) / TG + (L->has_shared ? (T + TG - 1) / TG : 0) + 1;
+}
+
+FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
+    PiBump b{base};
+    FwdBufs f;
+    const int64_t d = L->d, F = L->f, E = L->E, k = L->k;
+    const int64_t slots = T * k + (L->has_shared ? T : 0);
+    f.normed = b.take<float>(T * d);
+    f.xq = b.take<int8_t>(T * d);
+    f.xs = b.take<float>(T * (d / 32));
+    f.logits = b.take<float>(T * (E + 1));
+    f.idx = b.take<int32_t>(T * k);
+    f.gates = b.take<float>(T * k);
+    f.shscale = b.take<float>(T);
+    f.counts = b.take<int32_t>(E);
+    f.offsets = b.take<int32_t>(E);
+    f.perm = b.take<int32_t>(T * k);
+    f.slot_of = b.take<int32_t>(T * k);
+    f.items = b.take<int4>(max_items(L, T));
+    f.n_items = b.take<int32_t>(1);
+    if (L->qtype == PI_QT_Q8_0) {
+        f.hq = b.take<int8_t>(slots * F);
+        f.hs = b.take<float>(slots * (F / 32));
+        f.hf = nullptr;
+    } else {
+        f.hq = nullptr;
+        f.hs = nullptr;
+        f.hf = b.take<float>(slots * F);
+    }
+    f.y = b.take<float>(slots * d);
+    f.bytes = b.off + 256;
+    return f;
+}
+}  // namespace
+
+size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T) { return carve(L, T, nullptr).bytes; }
+
+int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
+               float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
+               cudaStream_t st) {
+    FwdBufs B = carve(L, T, scratch);
+    const int d = (int)L->d, E = L->E, k = L->k;
+    const bool q8 = L->qtype == PI_QT_Q8_0;
+    const bool route_only = (out == nullptr);
+    const int do_norm = (flags & PI_FWD_RMSNORM) ? 1 : 0;
+    const float* xin = do_norm ? B.normed : x;
+    int32_t* idx = idx_out ? idx_out : B.idx;
+    float* gates = gates_out ? gates_out : B.gates;
+    int32_t* counts = counts_out ? counts_out : B.counts;
+    int32_t* offsets = offsets_out ? offsets_out : B.offsets;
+    int32_t* perm = perm_out ? perm_out : B.perm;
+
+    if (do_norm || (q8 && !route_only)) {
+        PiProfScope ps(ctx, st, "k_prep");
+        k_prep<<<(unsigned)T, 256, 0, st>>>(x, d, do_norm, 1e-6f, B.normed, (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
+    }
+    dim3 rg((unsigned)((E + 1 + 127) / 128), (unsigned)((T + RT_TT - 1) / RT_TT));
+    {
+        PiProfScope ps(ctx, st, "k_router");
+        k_router<<<rg, 128, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, E + 1, B.logits);
+    }
+    if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
+    {
+        PiProfScope ps(ctx, st, "k_topk");
+        k_topk<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(
+            B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts);
+    }
+    {
+        PiProfScope ps(ctx, st, "k_dispatch");
+        k_dispatch<<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
+                                                      perm, B.slot_of, B.items, B.n_items);
+    }
+    if (route_only) return pi_cuda_check(ctx, cudaGetLastError(), "route") ? PI_ERR_CUDA : PI_OK;
+
+    ExpertArgs a;
+    a.g = L->gate.q;
+    a.u = L->up.q;
+    a.dn = L->down.q;
+    a.gd = L->gate.d;
+    a.ud = L->up.d;
+    a.dd = L->down.d;
+    a.gs = L->gate_sh.q;
+    a.us = L->up_sh.q;
+    a.dns = L->down_sh.q;
+    a.gsd = L->gate_sh.d;
+    a.usd = L->up_sh.d;
+    a.dsd = L->down_sh.d;
+    a.E = E;
+    a.d = d;
+    a.f = (int)L->f;
+    a.items = B.items;
+    a.n_items = B.n_items;
+    a.perm = perm;
+    a.n_routed = (int)(T * k);
+    a.xq = B.xq;
+    a.xs = B.xs;
+    a.xf = xin;
+    a.hq = B.hq;
+    a.hs = B.hs;
+    a.hf = B.hf;
+    a.y = B.y;
+    const unsigned ni = (unsigned)max_items(L, T);
+    const dim3 gu((unsigned)(L->f / 32), ni), dn((unsigned)(L->d / 128), ni);
+    if (q8) {
+        {
+        PiProfScope ps(ctx, st, "k_gateup");
+        switch (d / 512) {
+            case 1: k_gateup_q8<1><<<gu, 512, 0, st>>>(a); break;
+            case 2: k_gateup_q8<2><<<gu, 512, 0, st>>>(a); break;
+            case 4: k_gateup_q8<4><<<gu, 512, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 512, 1024 or 2048");
+        }
+        }
+        PiProfScope ps(ctx, st, "k_down");
+        switch (L->f / 64) {
+            case 2: k_down_q8<2><<<dn, 256, 0, st>>>(a); break;
+            case 4: k_down_q8<4><<<dn, 256, 0, st>>>(a); break;
+            case 8: k_down_q8<8><<<dn, 256, 0, st>>>(a); break;
+            case 16: k_down_q8<16><<<dn, 256, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128..1024 (x2)");
+        }
+    } else {
+        {
+        PiProfScope ps(ctx, st, "k_gateup");
+        switch (d / 1024) {
+            case 1: k_gateup_q4<1><<<gu, 512, 0, st>>>(a); break;
+            case 2: k_gateup_q4<2><<<gu, 512, 0, st>>>(a); break;
+            case 4: k_gateup_q4<4><<<gu, 512, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: n_embd must be 1024, 2048 or 4096");
+        }
+        }
+        PiProfScope ps(ctx, st, "k_down");
+        switch (L->f / 128) {
+            case 1: k_down_q4<1><<<dn, 256, 0, st>>>(a); break;
+            case 2: k_down_q4<2><<<dn, 256, 0, st>>>(a); break;
+            case 4: k_down_q4<4><<<dn, 256, 0, st>>>(a); break;
+            case 8: k_down_q4<8><<<dn, 256, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: expert width must be 128..1024 (x2)");
+        }
+    }
+    PiProfScope ps(ctx, st, "k_combine");
+    k_combine<<<(unsigned)T, 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0,
+                                            (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
+    return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
+}
+
+extern "C" int pi_router_topk_softmax(pi_ctx* ctx, const float* x, int64_t T, const float* router, int64_t d,
+                                      int32_t E, int32_t k, int32_t* idx, float* weights, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (T < 0 || E < 1 || E > 512 || k < 1 || k > E || k > 32 || d < 4 || d % 4)
+        return pi_set_error(ctx, PI_ERR_ARG, "router: need 1 <= k <= min(E, 32), E <= 512, d % 4 == 0");
+    if (T == 0) return PI_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* scr;
+    if (int rc = pi_scratch(ctx, st, (size_t)T * (E + 1) * 4 + 256, &scr)) return rc;
+    float* logits = reinterpret_cast<float*>(scr);
+    dim3 rg((unsigned)((E + 127) / 128), (unsigned)((T + RT_TT - 1) / RT_TT));
+    k_router<<<rg, 128, 0, st>>>(x, router, nullptr, (int)T, (int)d, E, E, logits);
+    k_topk_api<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(logits, (int)T, E, k, idx, weights);
+    return pi_cuda_check(ctx, cudaGetLastError(), "router") ? PI_ERR_CUDA : PI_OK;
+}

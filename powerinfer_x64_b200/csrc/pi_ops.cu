@@ -1,0 +1,836 @@
+// Per-function drop-ins for the reference's quant:: operators on raw GGUF
+// bytes, the hot-neuron sparse FFN, the predictor MLP, weight quantisers and
+// the synthetic-input generator.
+//
+// The per-function drop-ins (pi_matvec_col_major & co.) read the GGUF
+// array-of-blocks bytes in place and keep the reference's summation order
+// exactly (one sequential f32 chain per output, mul then add, no FMA), so
+// they are bit-identical to the reference whenever its exp rounding agrees.
+// The sparse-FFN object instead repacks its weights and parallelises the
+// sums (results within the stated tolerance).
+#include "pi_common.cuh"
+#include "pi_internal.h"
+
+#include <cmath>
+
+namespace {
+
+// --------------------------------------------------------------------------
+// GGUF block readers (blocks are 2-byte aligned: 18 B / 34 B).
+// --------------------------------------------------------------------------
+PI_DEV float gguf_scale(const uint8_t* blk) {
+    return half_bits_to_float(*reinterpret_cast<const uint16_t*>(blk));
+}
+// int8 value i of a Q8_0 block
+PI_DEV float q8_val(const uint8_t* blk, int i) { return (float)(int8_t)blk[2 + i]; }
+// dequantised Q4_0 element i of a block (reference nibble order)
+PI_DEV float q4_val(const uint8_t* blk, int i) {
+    const uint8_t byte = blk[2 + (i >> 1)];
+    const int nib = (i & 1) ? (byte >> 4) : (byte & 15);
+    return (float)(nib - 8);
+}
+
+// element i of an F32 / Q4_0 / Q8_0 row, dequantised exactly as the reference
+// (value * scale, f32 multiply).
+PI_DEV float row_elem(const uint8_t* row, int qtype, int64_t i) {
+    if (qtype == PI_QT_F32) return reinterpret_cast<const float*>(row)[i];
+    if (qtype == PI_QT_Q4_0) {
+        const uint8_t* blk = row + (i >> 5) * 18;
+        return fmul(q4_val(blk, (int)(i & 31)), gguf_scale(blk));
+    }
+    const uint8_t* blk = row + (i >> 5) * 34;
+    return fmul(q8_val(blk, (int)(i & 31)), gguf_scale(blk));
+}
+
+PI_DEV int64_t row_bytes(int qtype, int64_t n) {
+    return qtype == PI_QT_F32 ? n * 4 : (qtype == PI_QT_Q4_0 ? n / 32 * 18 : n / 32 * 34);
+}
+
+// --------------------------------------------------------------------------
+// Q8_0 activation quantiser over a vector (warp per 32-block).
+// --------------------------------------------------------------------------
+__global__ void k_quant_act(const float* __restrict__ x, int64_t n, int8_t* __restrict__ xq, float* __restrict__ xs) {
+    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b * 32 >= n) return;
+    const int64_t i = b * 32 + lane;
+    float sc;
+    const int8_t q = warp_quant_q8(i < n ? x[i] : 0.0f, &sc);
+    xq[i] = q;
+    if (lane == 0) xs[b] = sc;
+}
+
+// --------------------------------------------------------------------------
+// Q8_0 int-dot rows (matvec_col_major_q8_0, quant/mod.rs:652-689): warp per
+// output row; lanes compute per-block integer dots; lane 0 then adds the
+// block terms (float)sumi * (d_w * d_x) sequentially, blocks ascending.
+// rows: idx == null -> row j; else row idx[j] (range-checked).
+// --------------------------------------------------------------------------
+__global__ __launch_bounds__(256) void k_rows_q8(float* __restrict__ y, const int8_t* __restrict__ xq,
+                                                 const float* __restrict__ xs, const uint8_t* __restrict__ raw,
+                                                 int64_t n_in, int64_t n_out, const int64_t* __restrict__ idx,
+                                                 int64_t n_rows, uint32_t* err) {
+    extern __shared__ float terms[];  // [8 warps][nb]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t j = blockIdx.x * 8LL + warp;
+    if (j >= n_rows) return;
+    int64_t r = j;
+    if (idx) {
+        r = idx[j];
+        if (r < 0 || r >= n_out) {
+            if (lane == 0) atomicOr(err, PI_DEVERR_INDEX);
+            return;
+        }
+    }
+    const int64_t nb = n_in / 32;
+    float* tw = terms + warp * nb;
+    const uint8_t* row = raw + r * nb * 34;
+    for (int64_t b = lane; b < nb; b += 32) {
+        const uint8_t* blk = row + b * 34;
+        const uint16_t* q16 = reinterpret_cast<const uint16_t*>(blk + 2);
+        const int* xi = reinterpret_cast<const int*>(xq + b * 32);
+        int s = 0;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const uint32_t lo = q16[2 * m], hi = q16[2 * m + 1];
+            s = dp4a((int)(lo | (hi << 16)), xi[m], s);
+        }
+        tw[b] = fmul((float)s, fmul(gguf_scale(blk), xs[b]));
+    }
+    __syncwarp();
+    if (lane == 0) {
+        float sum = 0.0f;
+        for (int64_t b = 0; b < nb; ++b) sum = fadd(sum, tw[b]);
+        y[j] = sum;
+    }
+}
+
+// --------------------------------------------------------------------------
+// f32-activation rows (F32 weights, or any type through the reference's
+// dequantise-then-dot fallback, quant/mod.rs:958-969): thread per output row,
+// sum = sum + x[i] * w[i], i ascending.
+// --------------------------------------------------------------------------
+__global__ __launch_bounds__(128) void k_rows_f32(float* __restrict__ y, const float* __restrict__ x,
+                                                  const uint8_t* __restrict__ raw, int qtype, int64_t n_in,
+                                                  int64_t n_out, const int64_t* __restrict__ idx, int64_t n_rows,
+                                                  uint32_t* err) {
+    __shared__ float xs[1024];
+    const int64_t j = blockIdx.x * 128LL + threadIdx.x;
+    int64_t r = j;
+    bool ok = j < n_rows;
+    if (ok && idx) {
+        r = idx[j];
+        if (r < 0 || r >= n_out) {
+            atomicOr(err, PI_DEVERR_INDEX);
+            ok = false;
+        }
+    }
+    const uint8_t* row = raw + (ok ? r : 0) * row_bytes(qtype, n_in);
+    float sum = 0.0f;
+    for (int64_t c0 = 0; c0 < n_in; c0 += 1024) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 1024; i += 128) xs[i] = (c0 + i < n_in) ? x[c0 + i] : 0.0f;
+        __syncthreads();
+        if (!ok) continue;
+        const int64_t lim = min((int64_t)1024, n_in - c0);
+        for (int64_t i = 0; i < lim; ++i) sum = fadd(sum, fmul(xs[i], row_elem(row, qtype, c0 + i)));
+    }
+    if (ok) y[j] = sum;
+}
+
+// --------------------------------------------------------------------------
+// sparse-input matvec (quant/mod.rs:1073-1169): thread per output c,
+// sum = sum + x[s] * w[c][idx[s]] over s ascending (x NOT quantised).
+// --------------------------------------------------------------------------
+__global__ __launch_bounds__(128) void k_sparse_input(float* __restrict__ y, const float* __restrict__ x,
+                                                      const int64_t* __restrict__ idx, int64_t n_idx,
+                                                      const uint8_t* __restrict__ raw, int qtype, int64_t n_in,
+                                                      int64_t n_out, uint32_t* err) {
+    __shared__ float xs[512];
+    __shared__ int64_t is[512];
+    const int64_t c = blockIdx.x * 128LL + threadIdx.x;
+    const uint8_t* row = raw + (c < n_out ? c : 0) * row_bytes(qtype, n_in);
+    float sum = 0.0f;
+    bool bad = false;
+    for (int64_t s0 = 0; s0 < n_idx; s0 += 512) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < 512; i += 128) {
+            xs[i] = (s0 + i < n_idx) ? x[s0 + i] : 0.0f;
+            is[i] = (s0 + i < n_idx) ? idx[s0 + i] : 0;
+        }
+        __syncthreads();
+        const int64_t lim = min((int64_t)512, n_idx - s0);
+        for (int64_t s = 0; s < lim; ++s) {
+            const int64_t r = is[s];
+            if (r < 0 || r >= n_in) { bad = true; continue; }
+            sum = fadd(sum, fmul(xs[s], row_elem(row, qtype, r)));
+        }
+    }
+    if (bad && threadIdx.x == 0) atomicOr(err, PI_DEVERR_INDEX);
+    if (c < n_out) y[c] = sum;
+}
+
+__global__ void k_swiglu_vec(float* __restrict__ g, const float* __restrict__ u, int64_t n) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i < n) g[i] = swiglu_ref(g[i], u[i]);
+}
+
+__global__ void k_dequant(const uint8_t* __restrict__ raw, int qtype, int64_t n, float* __restrict__ out) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (qtype == PI_QT_F16) out[i] = half_bits_to_float(reinterpret_cast<const uint16_t*>(raw)[i]);
+    else out[i] = row_elem(raw, qtype, i);
+}
+
+// --------------------------------------------------------------------------
+// Weight quantisers -> GGUF blocks. Warp per block.
+// --------------------------------------------------------------------------
+__global__ void k_quant_q8_blocks(const float* __restrict__ x, int64_t nblk, uint8_t* __restrict__ out) {
+    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= nblk) return;
+    float sc;
+    const int8_t q = warp_quant_q8(x[b * 32 + lane], &sc);
+    uint8_t* o = out + b * 34;
+    o[2 + lane] = (uint8_t)q;
+    if (lane == 0) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(sc));
+        o[0] = (uint8_t)(h & 0xff);
+        o[1] = (uint8_t)(h >> 8);
+    }
+}
+
+// ggml-style Q4_0: m = first element with the largest |x|; d = m / -8;
+// id = 1/d; q = min(15, (int8)(x*id + 8.5)); packed byte i = q[2i] | q[2i+1] << 4.
+__global__ void k_quant_q4_blocks(const float* __restrict__ x, int64_t nblk, uint8_t* __restrict__ out) {
+    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= nblk) return;
+    const float v = x[b * 32 + lane];
+    float ba = fabsf(v);
+    if (ba != ba) ba = -1.0f;
+    int bi = lane;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float oa = __shfl_xor_sync(0xffffffffu, ba, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (oa > ba || (oa == ba && oi < bi)) { ba = oa; bi = oi; }
+    }
+    const float m = __shfl_sync(0xffffffffu, v, bi);
+    const float dd = fdiv(m, -8.0f);
+    const float id = (dd != 0.0f) ? fdiv(1.0f, dd) : 0.0f;
+    const float t = truncf(fadd(fmul(v, id), 8.5f));
+    int q = (int)fminf(15.0f, fmaxf(0.0f, t));
+    const int other = __shfl_xor_sync(0xffffffffu, q, 1);
+    uint8_t* o = out + b * 18;
+    if ((lane & 1) == 0) o[2 + (lane >> 1)] = (uint8_t)(q | (other << 4));
+    if (lane == 0) {
+        const uint16_t h = __half_as_ushort(__float2half_rn(dd));
+        o[0] = (uint8_t)(h & 0xff);
+        o[1] = (uint8_t)(h >> 8);
+    }
+}
+
+// --------------------------------------------------------------------------
+// Synthetic normals: SplitMix64 (model/mod.rs:2041-2061) + Box-Muller.
+// --------------------------------------------------------------------------
+__host__ __device__ inline uint64_t splitmix_at(uint64_t seed, uint64_t j) {
+    uint64_t z = seed + (j + 1) * 0x9E3779B97F4A7C15ull;  // state after j+1 steps
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__global__ void k_synth(uint64_t seed, uint64_t offset, int64_t n, float stdv, float* __restrict__ out) {
+    const int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    const uint64_t i = offset + (uint64_t)k;
+    const uint64_t m = i >> 1;
+    const double u1 = 1.0 - (double)(splitmix_at(seed, 2 * m) >> 11) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(splitmix_at(seed, 2 * m + 1) >> 11) * (1.0 / 9007199254740992.0);
+    const double r = sqrt(-2.0 * log(u1));
+    const double th = 6.283185307179586 * u2;
+    const double v = (i & 1) ? r * sin(th) : r * cos(th);
+    out[k] = (float)(v * (double)stdv);
+}
+
+// --------------------------------------------------------------------------
+// Predictor MLP (predictor/mod.rs:63-84): thread per output unit.
+// --------------------------------------------------------------------------
+__global__ void k_pred_layer(const float* __restrict__ in, int64_t T, int64_t n_in, const float* __restrict__ W,
+                             const float* __restrict__ b, int64_t n_out, int act, float* __restrict__ out) {
+    const int64_t j = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t t = blockIdx.y;
+    if (j >= n_out || t >= T) return;
+    const float* a = in + t * n_in;
+    const float* w = W + j * n_in;
+    float s = 0.0f;
+    for (int64_t i = 0; i < n_in; ++i) s = fadd(s, fmul(w[i], a[i]));
+    s = fadd(s, b[j]);
+    out[t * n_out + j] = act == 0 ? fmaxf(s, 0.0f) : sigmoid_ref(s);
+}
+
+// --------------------------------------------------------------------------
+// Hot-neuron sparse FFN (C-ABI pi_sparse_ffn_*).
+// --------------------------------------------------------------------------
+constexpr int SF_TMAX = 8;  // tokens per mask pass
+
+// mask[s] bit t (t < SF_TMAX within the pass) = neuron s active for token t0+t.
+__global__ void k_sf_mask(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx, int t0, int nt,
+                          int64_t n_ff, uint32_t* __restrict__ mask, uint32_t* err) {
+    const int t = blockIdx.y;
+    if (t >= nt) return;
+    const int64_t beg = ptr[t0 + t], end = ptr[t0 + t + 1];
+    const int64_t cnt = end - beg;
+    if (cnt >= n_ff) {  // dense path (quant/mod.rs:1221-1223)
+        for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n_ff; s += gridDim.x * (int64_t)blockDim.x)
+            atomicOr(&mask[s], 1u << t);
+        return;
+    }
+    for (int64_t q = beg + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < end; q += gridDim.x * (int64_t)blockDim.x) {
+        const int64_t s = idx[q];
+        if (s < 0 || s >= n_ff) { atomicOr(err, PI_DEVERR_INDEX); continue; }
+        atomicOr(&mask[s], 1u << t);
+    }
+}
+
+// gate/up for masked neurons: warp per neuron, BPL blocks per lane
+// (n_embd = 32 * 32 * BPL). Q4_0 (f32 x) and Q8_0 (quantised x) variants.
+PI_DEV float nibf(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616.0f; }
+PI_DEV float q4dot16(const int4 wv, const float* __restrict__ x) {
+    const uint32_t wd[4] = {(uint32_t)wv.x, (uint32_t)wv.y, (uint32_t)wv.z, (uint32_t)wv.w};
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 xa = *reinterpret_cast<const float4*>(x + 8 * i);
+        const float4 xb = *reinterpret_cast<const float4*>(x + 8 * i + 4);
+        const uint32_t v = wd[i];
+        s += nibf(v & 15u) * xa.x;
+        s += nibf((v >> 4) & 15u) * xa.y;
+        s += nibf((v >> 8) & 15u) * xa.z;
+        s += nibf((v >> 12) & 15u) * xa.w;
+        s += nibf((v >> 16) & 15u) * xb.x;
+        s += nibf((v >> 20) & 15u) * xb.y;
+        s += nibf((v >> 24) & 15u) * xb.z;
+        s += nibf(v >> 28) * xb.w;
+    }
+    return s;
+}
+
+template <int BPL>
+__global__ __launch_bounds__(256) void k_sf_gateup_q4(const uint8_t* __restrict__ G, const uint8_t* __restrict__ U,
+                                                      const __half* __restrict__ GD, const __half* __restrict__ UD,
+                                                      const uint32_t* __restrict__ mask, const float* __restrict__ x,
+                                                      int t0, int64_t n_embd, int64_t n_ff, float* __restrict__ h) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t s = blockIdx.x * 8LL + warp;
+    if (s >= n_ff) return;
+    uint32_t m = mask[s];
+    if (!m) return;
+    const int64_t nb = n_embd / 32;
+    int4 wg[BPL], wu[BPL];
+    float sg[BPL], su[BPL];
+#pragma unroll
+    for (int c = 0; c < BPL; ++c) {
+        const int64_t b = lane + 32 * c;
+        wg[c] = ld_stream(G + s * (n_embd / 2) + b * 16);
+        wu[c] = ld_stream(U + s * (n_embd / 2) + b * 16);
+        sg[c] = __half2float(GD[s * nb + b]);
+        su[c] = __half2float(UD[s * nb + b]);
+    }
+    while (m) {
+        const int t = __ffs(m) - 1;
+        m &= m - 1;
+        const float* xr = x + (int64_t)(t0 + t) * n_embd;
+        float ag = 0.f, au = 0.f;
+#pragma unroll
+        for (int c = 0; c < BPL; ++c) {
+            const float* xb = xr + (lane + 32 * c) * 32;
+            ag += sg[c] * q4dot16(wg[c], xb);
+            au += su[c] * q4dot16(wu[c], xb);
+        }
+        ag = warp_sum(ag);
+        au = warp_sum(au);
+        if (lane == 0) h[(int64_t)t * n_ff + s] = swiglu_ref(ag, au);
+    }
+}
+
+template <int CPL>
+__global__ __launch_bounds__(256) void k_sf_gateup_q8(const int8_t* __restrict__ G, const int8_t* __restrict__ U,
+                                                      const __half* __restrict__ GD, const __half* __restrict__ UD,
+                                                      const uint32_t* __restrict__ mask,
+                                                      const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                                                      int t0, int64_t n_embd, int64_t n_ff, float* __restrict__ h) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t s = blockIdx.x * 8LL + warp;
+    if (s >= n_ff) return;
+    uint32_t m = mask[s];
+    if (!m) return;
+    const int64_t nb = n_embd / 32;
+    int4 wg[CPL], wu[CPL];
+    float sg[CPL], su[CPL];
+#pragma unroll
+    for (int c = 0; c < CPL; ++c) {
+        const int64_t ch = lane + 32 * c;
+        wg[c] = ld_stream(G + s * n_embd + ch * 16);
+        wu[c] = ld_stream(U + s * n_embd + ch * 16);
+        sg[c] = __half2float(GD[s * nb + (ch >> 1)]);
+        su[c] = __half2float(UD[s * nb + (ch >> 1)]);
+    }
+    const bool even = (lane & 1) == 0;
+    while (m) {
+        const int t = __ffs(m) - 1;
+        m &= m - 1;
+        const int8_t* xr = xq + (int64_t)(t0 + t) * n_embd;
+        const float* sr = xs + (int64_t)(t0 + t) * nb;
+        float ag = 0.f, au = 0.f;
+#pragma unroll
+        for (int c = 0; c < CPL; ++c) {
+            const int64_t ch = lane + 32 * c;
+            const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
+            const float sx = even ? sr[ch >> 1] : 0.f;
+            int a = dp4a(wg[c].x, xv.x, 0);
+            a = dp4a(wg[c].y, xv.y, a);
+            a = dp4a(wg[c].z, xv.z, a);
+            a = dp4a(wg[c].w, xv.w, a);
+            int b = dp4a(wu[c].x, xv.x, 0);
+            b = dp4a(wu[c].y, xv.y, b);
+            b = dp4a(wu[c].z, xv.z, b);
+            b = dp4a(wu[c].w, xv.w, b);
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            b += __shfl_xor_sync(0xffffffffu, b, 1);
+            ag += (float)a * (sg[c] * sx);
+            au += (float)b * (su[c] * sx);
+        }
+        ag = warp_sum(ag);
+        au = warp_sum(au);
+        if (lane == 0) h[(int64_t)t * n_ff + s] = swiglu_ref(ag, au);
+    }
+}
+
+// down, neuron-major: CTA = (column tile of 1024 outputs, neuron split);
+// thread owns 4 consecutive columns; y accumulated with atomicAdd over splits.
+template <int QT>
+__global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
+                                                 const uint32_t* __restrict__ mask, const float* __restrict__ h,
+                                                 int t0, int nt, int64_t n_embd, int64_t n_ff, int64_t per_split,
+                                                 float* __restrict__ y) {
+    const int64_t c = blockIdx.x * 1024LL + threadIdx.x * 4;
+    if (c >= n_embd) return;
+    const int64_t s_beg = blockIdx.y * per_split, s_end = min(n_ff, s_beg + per_split);
+    float acc[SF_TMAX][4];
+#pragma unroll
+    for (int t = 0; t < SF_TMAX; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) acc[t][q] = 0.f;
+    int64_t cur_g = -1;
+    float sc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t s = s_beg; s < s_end; ++s) {
+        uint32_t m = mask[s];
+        if (!m) continue;
+        const int64_t g = s >> 5;
+        if (g != cur_g) {
+            const uint2 sv = *reinterpret_cast<const uint2*>(DS + g * n_embd + c);
+            sc[0] = __half2float(__ushort_as_half((uint16_t)(sv.x & 0xffff)));
+            sc[1] = __half2float(__ushort_as_half((uint16_t)(sv.x >> 16)));
+            sc[2] = __half2float(__ushort_as_half((uint16_t)(sv.y & 0xffff)));
+            sc[3] = __half2float(__ushort_as_half((uint16_t)(sv.y >> 16)));
+            cur_g = g;
+        }
+        float w[4];
+        if (QT == PI_QT_Q4_0) {
+            const uint16_t v = *reinterpret_cast<const uint16_t*>(DQ + s * (n_embd / 2) + c / 2);
+            w[0] = nibf(v & 15u) * sc[0];
+            w[1] = nibf((v >> 4) & 15u) * sc[1];
+            w[2] = nibf((v >> 8) & 15u) * sc[2];
+            w[3] = nibf((v >> 12) & 15u) * sc[3];
+        } else {
+            const uint32_t v = *reinterpret_cast<const uint32_t*>(DQ + s * n_embd + c);
+            w[0] = (float)(int8_t)(v & 0xff) * sc[0];
+            w[1] = (float)(int8_t)((v >> 8) & 0xff) * sc[1];
+            w[2] = (float)(int8_t)((v >> 16) & 0xff) * sc[2];
+            w[3] = (float)(int8_t)(v >> 24) * sc[3];
+        }
+#pragma unroll
+        for (int t = 0; t < SF_TMAX; ++t) {
+            if ((m >> t) & 1u) {
+                const float hv = h[(int64_t)t * n_ff + s];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[t][q] += hv * w[q];
+            }
+        }
+    }
+    for (int t = 0; t < nt; ++t)
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+            if (acc[t][q] != 0.f) atomicAdd(&y[(int64_t)(t0 + t) * n_embd + c + q], acc[t][q]);
+}
+
+// Repack GGUF down [ne0=n_ff, ne1=n_embd] to neuron-major. Thread per
+// (output pair c, c+1; block b of 32 neurons).
+__global__ void k_repack_down_nm(const uint8_t* __restrict__ raw, int qtype, int64_t n_embd, int64_t n_ff,
+                                 uint8_t* __restrict__ q, __half* __restrict__ sc) {
+    const int64_t nb = n_ff / 32;
+    const int64_t tid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int64_t b = tid % nb, cp = tid / nb;
+    const int64_t c = cp * 2;
+    if (c >= n_embd) return;
+    const int bsz = qtype == PI_QT_Q4_0 ? 18 : 34;
+    const uint8_t* b0 = raw + (c * nb + b) * bsz;
+    const uint8_t* b1 = raw + ((c + 1) * nb + b) * bsz;
+    sc[b * n_embd + c] = __ushort_as_half(*reinterpret_cast<const uint16_t*>(b0));
+    sc[b * n_embd + c + 1] = __ushort_as_half(*reinterpret_cast<const uint16_t*>(b1));
+    for (int i = 0; i < 32; ++i) {
+        const int64_t s = b * 32 + i;
+        if (qtype == PI_QT_Q4_0) {
+            const uint8_t v0 = b0[2 + (i >> 1)], v1 = b1[2 + (i >> 1)];
+            const uint8_t n0 = (i & 1) ? (v0 >> 4) : (v0 & 15), n1 = (i & 1) ? (v1 >> 4) : (v1 & 15);
+            q[s * (n_embd / 2) + c / 2] = (uint8_t)(n0 | (n1 << 4));
+        } else {
+            q[s * n_embd + c] = b0[2 + i];
+            q[s * n_embd + c + 1] = b1[2 + i];
+        }
+    }
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+static int64_t gguf_size(int qtype, int64_t n) {
+    switch (qtype) {
+        case PI_QT_F32: return n * 4;
+        case PI_QT_F16: return n * 2;
+        case PI_QT_Q4_0: return n / 32 * 18;
+        case PI_QT_Q8_0: return n / 32 * 34;
+    }
+    return -1;
+}
+
+static bool qtype_ok(int qt) { return qt == PI_QT_F32 || qt == PI_QT_Q4_0 || qt == PI_QT_Q8_0; }
+
+#define ST(s) ((cudaStream_t)(s))
+#define LAUNCH_CHECK(what) \
+    if (pi_cuda_check(ctx, cudaGetLastError(), what)) return PI_ERR_CUDA
+
+static unsigned nblocks(int64_t n, int thr) { return (unsigned)((n + thr - 1) / thr); }
+
+extern "C" int pi_dequantize(pi_ctx* ctx, const void* raw, uint64_t raw_len, int qtype, int64_t rows, int64_t cols,
+                             float* out, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (!raw || !out || rows < 0 || cols < 0) return pi_set_error(ctx, PI_ERR_ARG, "dequantize: bad argument");
+    if (!(qtype_ok(qtype) || qtype == PI_QT_F16)) return pi_set_error(ctx, PI_ERR_ARG, "dequantize: unsupported type");
+    int64_t n = rows * cols;
+    if (qtype == PI_QT_Q4_0 || qtype == PI_QT_Q8_0) n = rows * (cols / 32) * 32;
+    if ((int64_t)raw_len < gguf_size(qtype, n))
+        return pi_set_error(ctx, PI_ERR_SHORT, "Insufficient data for dequantization");
+    if (n == 0) return PI_OK;
+    k_dequant<<<nblocks(n, 256), 256, 0, ST(stream)>>>((const uint8_t*)raw, qtype, n, out);
+    LAUNCH_CHECK("dequantize");
+    return PI_OK;
+}
+
+extern "C" int pi_quantize_q8_0(pi_ctx* ctx, const float* x, int64_t n, void* out_raw, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (!x || !out_raw || n < 0 || n % 32) return pi_set_error(ctx, PI_ERR_ARG, "quantize_q8_0: n % 32 != 0");
+    if (n == 0) return PI_OK;
+    k_quant_q8_blocks<<<nblocks(n, 256), 256, 0, ST(stream)>>>(x, n / 32, (uint8_t*)out_raw);
+    LAUNCH_CHECK("quantize_q8_0");
+    return PI_OK;
+}
+
+extern "C" int pi_quantize_q4_0(pi_ctx* ctx, const float* x, int64_t n, void* out_raw, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (!x || !out_raw || n < 0 || n % 32) return pi_set_error(ctx, PI_ERR_ARG, "quantize_q4_0: n % 32 != 0");
+    if (n == 0) return PI_OK;
+    k_quant_q4_blocks<<<nblocks(n, 256), 256, 0, ST(stream)>>>(x, n / 32, (uint8_t*)out_raw);
+    LAUNCH_CHECK("quantize_q4_0");
+    return PI_OK;
+}
+
+// rows of a col-major matvec, selected (idx) or all (idx == null, n_rows = n_out)
+static int run_rows(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in, int64_t n_out,
+                    const int64_t* idx, int64_t n_rows, cudaStream_t st) {
+    if (n_rows == 0) return PI_OK;
+    if (qtype == PI_QT_Q8_0 && n_in % 32 == 0) {
+        char* scr;
+        int rc = pi_scratch(ctx, st, (size_t)n_in + (size_t)(n_in / 32) * 4 + 512, &scr);
+        if (rc) return rc;
+        PiBump b{scr};
+        int8_t* xq = b.take<int8_t>(n_in);
+        float* xs = b.take<float>(n_in / 32);
+        k_quant_act<<<nblocks(n_in, 256), 256, 0, st>>>(x, n_in, xq, xs);
+        const size_t smem = (size_t)8 * (n_in / 32) * 4;
+        if (smem > 200 * 1024) return pi_set_error(ctx, PI_ERR_ARG, "matvec: n_in too large");
+        if (smem > 48 * 1024)
+            cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k_rows_q8<<<nblocks(n_rows, 8), 256, smem, st>>>(y, xq, xs, (const uint8_t*)raw, n_in, n_out, idx, n_rows,
+                                                         ctx->dev_err);
+    } else {
+        k_rows_f32<<<nblocks(n_rows, 128), 128, 0, st>>>(y, x, (const uint8_t*)raw, qtype, n_in, n_out, idx, n_rows,
+                                                          ctx->dev_err);
+    }
+    LAUNCH_CHECK("matvec");
+    return PI_OK;
+}
+
+static int check_mv(pi_ctx* ctx, int qtype, int64_t n_in, int64_t n_out) {
+    if (!qtype_ok(qtype)) return pi_set_error(ctx, PI_ERR_ARG, "unsupported quantisation type");
+    if (n_in < 0 || n_out < 0) return pi_set_error(ctx, PI_ERR_ARG, "negative size");
+    if (qtype != PI_QT_F32 && n_in % 32) return pi_set_error(ctx, PI_ERR_ARG, "n_in must be a multiple of 32");
+    return PI_OK;
+}
+
+extern "C" int pi_matvec_col_major(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in,
+                                   int64_t n_out, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (int rc = check_mv(ctx, qtype, n_in, n_out)) return rc;
+    return run_rows(ctx, y, x, raw, qtype, n_in, n_out, nullptr, n_out, ST(stream));
+}
+
+extern "C" int pi_matvec_col_major_select(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype,
+                                          int64_t n_in, int64_t n_out, const int64_t* idx, int64_t n_idx,
+                                          void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (int rc = check_mv(ctx, qtype, n_in, n_out)) return rc;
+    if (n_idx > 0 && !idx) return pi_set_error(ctx, PI_ERR_ARG, "null index list");
+    return run_rows(ctx, y, x, raw, qtype, n_in, n_out, idx, n_idx, ST(stream));
+}
+
+extern "C" int pi_matvec_col_major_sparse_input(pi_ctx* ctx, float* y, const float* x, const int64_t* idx,
+                                                int64_t n_idx, const void* raw, int qtype, int64_t n_in,
+                                                int64_t n_out, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (int rc = check_mv(ctx, qtype, n_in, n_out)) return rc;
+    if (n_out == 0) return PI_OK;
+    if (n_idx == 0) {
+        if (pi_cuda_check(ctx, cudaMemsetAsync(y, 0, sizeof(float) * n_out, ST(stream)), "memset")) return PI_ERR_CUDA;
+        return PI_OK;
+    }
+    k_sparse_input<<<nblocks(n_out, 128), 128, 0, ST(stream)>>>(y, x, idx, n_idx, (const uint8_t*)raw, qtype, n_in,
+                                                                 n_out, ctx->dev_err);
+    LAUNCH_CHECK("sparse_input");
+    return PI_OK;
+}
+
+static int ffn_core(pi_ctx* ctx, float* out, const float* x, const void* g, const void* u, const void* dn, int qtype,
+                    int64_t n_embd, int64_t n_ff, const int64_t* idx, int64_t n_sel, cudaStream_t st) {
+    // scratch: gate/up [n_sel] f32, plus the Q8_0 quantised hidden for dense down
+    char* scr;
+    const size_t need = (size_t)n_sel * 8 + 1024 + (size_t)n_ff + (size_t)n_ff / 8 + (size_t)n_embd + n_embd / 8 + 2048;
+    int rc = pi_scratch(ctx, st, need, &scr);
+    if (rc) return rc;
+    PiBump b{scr};
+    float* gv = b.take<float>(n_sel);
+    float* uv = b.take<float>(n_sel);
+    // the row kernels use the arena tail for the quantised x; give them their own offset
+    (void)b;
+    // run gate/up with row kernels that quantise x into a separate region
+    if (qtype == PI_QT_Q8_0) {
+        int8_t* xq = b.take<int8_t>(n_embd);
+        float* xs = b.take<float>(n_embd / 32);
+        k_quant_act<<<nblocks(n_embd, 256), 256, 0, st>>>(x, n_embd, xq, xs);
+        const size_t smem = (size_t)8 * (n_embd / 32) * 4;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k_rows_q8<<<nblocks(n_sel, 8), 256, smem, st>>>(gv, xq, xs, (const uint8_t*)g, n_embd, n_ff, idx, n_sel,
+                                                        ctx->dev_err);
+        k_rows_q8<<<nblocks(n_sel, 8), 256, smem, st>>>(uv, xq, xs, (const uint8_t*)u, n_embd, n_ff, idx, n_sel,
+                                                        ctx->dev_err);
+    } else {
+        k_rows_f32<<<nblocks(n_sel, 128), 128, 0, st>>>(gv, x, (const uint8_t*)g, qtype, n_embd, n_ff, idx, n_sel,
+                                                         ctx->dev_err);
+        k_rows_f32<<<nblocks(n_sel, 128), 128, 0, st>>>(uv, x, (const uint8_t*)u, qtype, n_embd, n_ff, idx, n_sel,
+                                                         ctx->dev_err);
+    }
+    k_swiglu_vec<<<nblocks(n_sel, 256), 256, 0, st>>>(gv, uv, n_sel);
+    if (idx) {
+        // selected: down over the sparse input (x = h at rows idx), f32 h
+        k_sparse_input<<<nblocks(n_embd, 128), 128, 0, st>>>(out, gv, idx, n_sel, (const uint8_t*)dn, qtype, n_ff,
+                                                              n_embd, ctx->dev_err);
+    } else if (qtype == PI_QT_Q8_0) {
+        int8_t* hq = b.take<int8_t>(n_ff);
+        float* hs = b.take<float>(n_ff / 32);
+        k_quant_act<<<nblocks(n_ff, 256), 256, 0, st>>>(gv, n_ff, hq, hs);
+        const size_t smem = (size_t)8 * (n_ff / 32) * 4;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        k_rows_q8<<<nblocks(n_embd, 8), 256, smem, st>>>(out, hq, hs, (const uint8_t*)dn, n_ff, n_embd, nullptr,
+                                                         n_embd, ctx->dev_err);
+    } else {
+        k_rows_f32<<<nblocks(n_embd, 128), 128, 0, st>>>(out, gv, (const uint8_t*)dn, qtype, n_ff, n_embd, nullptr,
+                                                          n_embd, ctx->dev_err);
+    }
+    LAUNCH_CHECK("ffn_swiglu_q");
+    return PI_OK;
+}
+
+extern "C" int pi_ffn_swiglu_q(pi_ctx* ctx, float* out, const float* x, const void* gate_raw, const void* up_raw,
+                               const void* down_raw, int qtype, int64_t n_embd, int64_t n_ff, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (int rc = check_mv(ctx, qtype, n_embd, n_ff)) return rc;
+    if (qtype != PI_QT_F32 && n_ff % 32) return pi_set_error(ctx, PI_ERR_ARG, "n_ff must be a multiple of 32");
+    return ffn_core(ctx, out, x, gate_raw, up_raw, down_raw, qtype, n_embd, n_ff, nullptr, n_ff, ST(stream));
+}
+
+extern "C" int pi_ffn_swiglu_q_selected(pi_ctx* ctx, float* out, const float* x, const void* gate_raw,
+                                        const void* up_raw, const void* down_raw, int qtype, int64_t n_embd,
+                                        int64_t n_ff, const int64_t* idx, int64_t n_idx, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (int rc = check_mv(ctx, qtype, n_embd, n_ff)) return rc;
+    if (n_idx == 0) {
+        if (pi_cuda_check(ctx, cudaMemsetAsync(out, 0, sizeof(float) * n_embd, ST(stream)), "memset"))
+            return PI_ERR_CUDA;
+        return PI_OK;
+    }
+    if (n_idx >= n_ff) return pi_ffn_swiglu_q(ctx, out, x, gate_raw, up_raw, down_raw, qtype, n_embd, n_ff, stream);
+    if (!idx) return pi_set_error(ctx, PI_ERR_ARG, "null index list");
+    return ffn_core(ctx, out, x, gate_raw, up_raw, down_raw, qtype, n_embd, n_ff, idx, n_idx, ST(stream));
+}
+
+extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const void* up_raw, const void* down_raw,
+                                    int32_t qtype, int64_t n_embd, int64_t n_ff, int32_t src_on_host,
+                                    pi_sparse_ffn** out) {
+    if (!ctx || !out) return PI_ERR_ARG;
+    *out = nullptr;
+    if (qtype != PI_QT_Q4_0 && qtype != PI_QT_Q8_0)
+        return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: weights must be Q4_0 or Q8_0");
+    const int64_t unit = qtype == PI_QT_Q4_0 ? 1024 : 512;
+    if (n_embd % unit || n_embd / unit > 4 || n_embd / unit < 1 || n_ff % 32 || n_embd % 1024)
+        return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: n_embd must be 1024/2048/4096, n_ff % 32 == 0");
+    cudaSetDevice(ctx->device);
+    pi_sparse_ffn* F = new pi_sparse_ffn();
+    F->ctx = ctx;
+    F->n_embd = n_embd;
+    F->n_ff = n_ff;
+    F->qtype = qtype;
+    int rc = pi_repack_mats(ctx, &F->gate, gate_raw, qtype, 1, n_ff, n_embd, src_on_host, &F->allocs);
+    if (!rc) rc = pi_repack_mats(ctx, &F->up, up_raw, qtype, 1, n_ff, n_embd, src_on_host, &F->allocs);
+    const int64_t dbytes = gguf_size(qtype, n_embd * n_ff);
+    const void* dsrc = down_raw;
+    void* stage = nullptr;
+    if (!rc && src_on_host) {
+        if (pi_cuda_check(ctx, cudaMalloc(&stage, dbytes), "cudaMalloc")) rc = PI_ERR_OOM;
+        else if (pi_cuda_check(ctx, cudaMemcpy(stage, down_raw, dbytes, cudaMemcpyHostToDevice), "upload"))
+            rc = PI_ERR_CUDA;
+        dsrc = stage;
+    }
+    if (!rc) {
+        const int64_t qb = qtype == PI_QT_Q4_0 ? n_ff * n_embd / 2 : n_ff * n_embd;
+        if (pi_cuda_check(ctx, cudaMalloc(&F->down_q, qb), "cudaMalloc")) rc = PI_ERR_OOM;
+        else F->allocs.push_back(F->down_q);
+        if (!rc && pi_cuda_check(ctx, cudaMalloc(&F->down_d, (n_ff / 32) * n_embd * 2), "cudaMalloc")) rc = PI_ERR_OOM;
+        else if (!rc) F->allocs.push_back(F->down_d);
+    }
+    if (!rc) {
+        const int64_t nthr = (n_embd / 2) * (n_ff / 32);
+        k_repack_down_nm<<<nblocks(nthr, 256), 256>>>((const uint8_t*)dsrc, qtype, n_embd, n_ff,
+                                                      (uint8_t*)F->down_q, F->down_d);
+        if (pi_cuda_check(ctx, cudaDeviceSynchronize(), "repack down")) rc = PI_ERR_CUDA;
+    }
+    if (stage) cudaFree(stage);
+    if (rc) {
+        pi_sparse_ffn_destroy(F);
+        return rc;
+    }
+    *out = F;
+    return PI_OK;
+}
+
+extern "C" void pi_sparse_ffn_destroy(pi_sparse_ffn* F) {
+    if (!F) return;
+    for (void* p : F->allocs) cudaFree(p);
+    delete F;
+}
+
+extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float* x, int64_t T, const int64_t* ptr,
+                                     const int64_t* idx, float* out, void* stream) {
+    if (!ctx || !F) return PI_ERR_ARG;
+    if (T < 0 || (T > 0 && (!x || !ptr || !out))) return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: bad argument");
+    if (T == 0) return PI_OK;
+    cudaStream_t st = ST(stream);
+    const int64_t d = F->n_embd, n_ff = F->n_ff;
+    char* scr;
+    const size_t need = (size_t)n_ff * 4 + (size_t)SF_TMAX * n_ff * 4 + (size_t)T * d + (size_t)T * (d / 32) * 4 + 4096;
+    if (int rc = pi_scratch(ctx, st, need, &scr)) return rc;
+    PiBump b{scr};
+    uint32_t* mask = b.take<uint32_t>(n_ff);
+    float* h = b.take<float>((size_t)SF_TMAX * n_ff);
+    int8_t* xq = nullptr;
+    float* xs = nullptr;
+    if (F->qtype == PI_QT_Q8_0) {
+        xq = b.take<int8_t>(T * d);
+        xs = b.take<float>(T * (d / 32));
+        k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
+    }
+    if (pi_cuda_check(ctx, cudaMemsetAsync(out, 0, sizeof(float) * T * d, st), "memset")) return PI_ERR_CUDA;
+    const int64_t splits = std::max<int64_t>(1, std::min<int64_t>(n_ff / 32, (ctx->sm_count * 2 + 3) / 4));
+    const int64_t per_split = ((n_ff + splits - 1) / splits + 31) / 32 * 32;
+    const int64_t nsplit = (n_ff + per_split - 1) / per_split;
+    for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
+        const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
+        if (pi_cuda_check(ctx, cudaMemsetAsync(mask, 0, sizeof(uint32_t) * n_ff, st), "memset")) return PI_ERR_CUDA;
+        k_sf_mask<<<dim3(32, nt), 256, 0, st>>>(ptr, idx, (int)t0, nt, n_ff, mask, ctx->dev_err);
+        const unsigned gblocks = nblocks(n_ff, 8);
+        if (F->qtype == PI_QT_Q4_0) {
+            const uint8_t* G = (const uint8_t*)F->gate.q;
+            const uint8_t* U = (const uint8_t*)F->up.q;
+            switch (d / 1024) {
+                case 1: k_sf_gateup_q4<1><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
+                case 2: k_sf_gateup_q4<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
+                case 4: k_sf_gateup_q4<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
+            }
+            k_sf_down<PI_QT_Q4_0><<<dim3((unsigned)(d / 1024), (unsigned)nsplit), 256, 0, st>>>(
+                (const uint8_t*)F->down_q, F->down_d, mask, h, (int)t0, nt, d, n_ff, per_split, out);
+        } else {
+            const int8_t* G = (const int8_t*)F->gate.q;
+            const int8_t* U = (const int8_t*)F->up.q;
+            switch (d / 512) {
+                case 2: k_sf_gateup_q8<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
+                case 4: k_sf_gateup_q8<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
+                case 8: k_sf_gateup_q8<8><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
+            }
+            k_sf_down<PI_QT_Q8_0><<<dim3((unsigned)(d / 1024), (unsigned)nsplit), 256, 0, st>>>(
+                (const uint8_t*)F->down_q, F->down_d, mask, h, (int)t0, nt, d, n_ff, per_split, out);
+        }
+        LAUNCH_CHECK("sparse ffn");
+    }
+    return PI_OK;
+}
+
+extern "C" int pi_predictor_forward(pi_ctx* ctx, const float* a, int64_t T, const float* W1, const float* b1,
+                                    const float* W2, const float* b2, int64_t n_in, int64_t n_hidden, int64_t n_out,
+                                    float* probs, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (T <= 0) return PI_OK;
+    if (!a || !W1 || !b1 || !W2 || !b2 || !probs) return pi_set_error(ctx, PI_ERR_ARG, "predictor: null pointer");
+    char* scr;
+    if (int rc = pi_scratch(ctx, ST(stream), (size_t)T * n_hidden * 4 + 256, &scr)) return rc;
+    float* h = reinterpret_cast<float*>(scr);
+    k_pred_layer<<<dim3(nblocks(n_hidden, 128), (unsigned)T), 128, 0, ST(stream)>>>(a, T, n_in, W1, b1, n_hidden, 0, h);
+    k_pred_layer<<<dim3(nblocks(n_out, 128), (unsigned)T), 128, 0, ST(stream)>>>(h, T, n_hidden, W2, b2, n_out, 1,
+                                                                                 probs);
+    LAUNCH_CHECK("predictor");
+    return PI_OK;
+}
+
+extern "C" int pi_synth_normal(pi_ctx* ctx, uint64_t seed, uint64_t offset, int64_t n, float stdv, float* out,
+                               void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (n <= 0) return PI_OK;
+    k_synth<<<nblocks(n, 256), 256, 0, ST(stream)>>>(seed, offset, n, stdv, out);
+    LAUNCH_CHECK("synth");
+    return PI_OK;
+}
+
+extern "C" int pi_synth_normal_host(uint64_t seed, uint64_t offset, int64_t n, float stdv, float* out) {
+    for (int64_t k = 0; k < n; ++k) {
+        const uint64_t i = offset + (uint64_t)k, m = i >> 1;
+        const double u1 = 1.0 - (double)(splitmix_at(seed, 2 * m) >> 11) * (1.0 / 9007199254740992.0);
+        const double u2 = (double)(splitmix_at(seed, 2 * m + 1) >> 11) * (1.0 / 9007199254740992.0);
+        const double r = std::sqrt(-2.0 * std::log(u1));
+        const double th = 6.283185307179586 * u2;
+        const double v = (i & 1) ? r * std::sin(th) : r * std::cos(th);
+        out[k] = (float)(v * (double)stdv);
+    }
+    return PI_OK;
+}
