@@ -246,6 +246,6 @@ extern "C" int pi_moe_route(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_
 
 extern "C" int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int32_t flags,
                               void* stream) {
-    if (!out) return pi_set_error(ctx, PI_ERR_ARG, "moe: null output");
+    if (!out && T > 0) return pi_set_error(ctx, PI_ERR_ARG, "moe: null output");
     return moe_common(ctx, L, x, T, out, flags, nullptr, nullptr, nullptr, nullptr, nullptr, stream);
 }

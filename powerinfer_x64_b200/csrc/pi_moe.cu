@@ -389,12 +389,26 @@ struct ExpertArgs {
 
 PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
 
-// Q8_0 gate+up: CTA = 32 rows of one expert (16 warps x 2 rows, gate and up),
-// CPL = d/512 16-byte chunks per lane per row (lane l holds chunks l + 32c;
-// chunk pairs (2m, 2m+1) form 32-element block m).
+// Q8_0 gate+up: CTA = 32 rows of one expert (16 warps x 2 rows, gate and
+// up = 4 row-vectors per warp), CPL = d/512 16-byte chunks per lane per row
+// (lane l holds chunks l + 32c; chunks 2m, 2m+1 form 32-element block m).
+//
+// The sums keep the reference's order exactly (matvec_q8_0_sse_range,
+// quant/mod.rs:835-871): per block an exact int32 dot, the term
+// (float)sumi * (d_w * d_x), and the terms added sequentially in block order.
+// Terms are staged in shared memory; lane (rv, token) of each warp then runs
+// the sequential chain for one (row-vector, token) pair. h is therefore the
+// reference's h bit for bit (up to its expf rounding), so the Q8_0
+// re-quantisation of h below makes the same integer choices.
+constexpr int GU_TB = 8;  // tokens per batch: 4 row-vectors x 8 tokens = 32 chains per warp
 template <int CPL>
 __global__ __launch_bounds__(512) void k_gateup_q8(ExpertArgs a) {
-    __shared__ float hbuf[TG][33];
+    constexpr int NB = 16 * CPL;   // blocks per row
+    constexpr int STRIDE = NB + 4; // padded chain stride (floats): conflict-free 16-byte reads
+    extern __shared__ __align__(16) float smem[];
+    float* terms = smem + (threadIdx.x >> 5) * (4 * GU_TB * STRIDE);
+    __shared__ float hbuf[GU_TB][33];
+    __shared__ float res[16][4][GU_TB];
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -423,42 +437,64 @@ __global__ __launch_bounds__(512) void k_gateup_q8(ExpertArgs a) {
         sw[3][c] = __half2float(UD[nb + (ch >> 1)]);
     }
     const bool even = (lane & 1) == 0;
-    for (int tk = 0; tk < item.z; ++tk) {
-        const int slot = item.y + tk;
-        const int tok = slot_token(a, sh, slot);
-        const int8_t* xr = a.xq + (size_t)tok * d;
-        const float* sr = a.xs + (size_t)tok * nb;
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    const int crv = lane >> 3, ctk = lane & 7;  // this lane's chain
+    for (int t0 = 0; t0 < item.z; t0 += GU_TB) {
+        const int nt = min(GU_TB, item.z - t0);
+        for (int tk = 0; tk < nt; ++tk) {
+            const int slot = item.y + t0 + tk;
+            const int tok = slot_token(a, sh, slot);
+            const int8_t* xr = a.xq + (size_t)tok * d;
+            const float* sr = a.xs + (size_t)tok * nb;
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-            const int ch = lane + 32 * c;
-            const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
-            const float sx = even ? sr[ch >> 1] : 0.0f;
+            for (int c = 0; c < CPL; ++c) {
+                const int ch = lane + 32 * c;
+                const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
+                const float sx = sr[ch >> 1];
 #pragma unroll
-            for (int r = 0; r < 4; ++r) {
-                int s = dp4a(w[r][c].x, xv.x, 0);
-                s = dp4a(w[r][c].y, xv.y, s);
-                s = dp4a(w[r][c].z, xv.z, s);
-                s = dp4a(w[r][c].w, xv.w, s);
-                s += __shfl_xor_sync(0xffffffffu, s, 1);
-                acc[r] += (float)s * (sw[r][c] * sx);
+                for (int r = 0; r < 4; ++r) {
+                    int s = dp4a(w[r][c].x, xv.x, 0);
+                    s = dp4a(w[r][c].y, xv.y, s);
+                    s = dp4a(w[r][c].z, xv.z, s);
+                    s = dp4a(w[r][c].w, xv.w, s);
+                    s += __shfl_xor_sync(0xffffffffu, s, 1);
+                    if (even) terms[(r * GU_TB + tk) * STRIDE + (ch >> 1)] = fmul((float)s, fmul(sw[r][c], sx));
+                }
             }
         }
+        __syncwarp();
+        if (ctk < nt) {
+            const float4* tp = reinterpret_cast<const float4*>(terms + (crv * GU_TB + ctk) * STRIDE);
+            float acc = 0.0f;
 #pragma unroll
-        for (int r = 0; r < 4; ++r) acc[r] = warp_sum(acc[r]);
-        if (lane == 0) {
-            hbuf[tk][2 * warp] = swiglu_ref(acc[0], acc[1]);
-            hbuf[tk][2 * warp + 1] = swiglu_ref(acc[2], acc[3]);
+            for (int q = 0; q < NB / 4; ++q) {
+                const float4 v = tp[q];
+                acc = fadd(acc, v.x);
+                acc = fadd(acc, v.y);
+                acc = fadd(acc, v.z);
+                acc = fadd(acc, v.w);
+            }
+            res[warp][crv][ctk] = acc;
         }
+        __syncwarp();
+        if (lane < 2 * GU_TB) {
+            const int r = lane / GU_TB, tk = lane % GU_TB;  // row rA + r
+            if (tk < nt) hbuf[tk][2 * warp + r] = swiglu_ref(res[warp][2 * r][tk], res[warp][2 * r + 1][tk]);
+        }
+        __syncthreads();
+        if (warp < nt) {
+            const int slot = item.y + t0 + warp;
+            float sc;
+            const int8_t q = warp_quant_q8(hbuf[warp][lane], &sc);
+            a.hq[(size_t)slot * f + row0 + lane] = q;
+            if (lane == 0) a.hs[(size_t)slot * (f / 32) + row0 / 32] = sc;
+        }
+        __syncthreads();
     }
-    __syncthreads();
-    if (warp < item.z) {
-        const int slot = item.y + warp;
-        float sc;
-        const int8_t q = warp_quant_q8(hbuf[warp][lane], &sc);
-        a.hq[(size_t)slot * f + row0 + lane] = q;
-        if (lane == 0) a.hs[(size_t)slot * (f / 32) + row0 / 32] = sc;
-    }
+}
+
+template <int CPL>
+constexpr size_t gateup_q8_smem() {
+    return (size_t)16 * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
 }
 
 // Q8_0 down: CTA = 128 output rows (8 warps x 16 rows), 4 lanes per row,
@@ -881,9 +917,21 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         {
         PiProfScope ps(ctx, st, "k_gateup");
         switch (d / 512) {
-            case 1: k_gateup_q8<1><<<gu, 512, 0, st>>>(a); break;
-            case 2: k_gateup_q8<2><<<gu, 512, 0, st>>>(a); break;
-            case 4: k_gateup_q8<4><<<gu, 512, 0, st>>>(a); break;
+#define GU_Q8(C)                                                                                              \
+    case C: {                                                                                                 \
+        static bool attr = false;                                                                             \
+        if (!attr) {                                                                                          \
+            cudaFuncSetAttribute(k_gateup_q8<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                                 (int)gateup_q8_smem<C>());                                                   \
+            attr = true;                                                                                      \
+        }                                                                                                     \
+        k_gateup_q8<C><<<gu, 512, gateup_q8_smem<C>(), st>>>(a);                                             \
+        break;                                                                                                \
+    }
+            GU_Q8(1)
+            GU_Q8(2)
+            GU_Q8(4)
+#undef GU_Q8
             default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 512, 1024 or 2048");
         }
         }

@@ -191,13 +191,14 @@ __global__ void k_quant_q8_blocks(const float* __restrict__ x, int64_t nblk, uin
     if (b >= nblk) return;
     float sc;
     const int8_t q = warp_quant_q8(x[b * 32 + lane], &sc);
-    uint8_t* o = out + b * 34;
-    o[2 + lane] = (uint8_t)q;
-    if (lane == 0) {
-        const uint16_t h = __half_as_ushort(__float2half_rn(sc));
-        o[0] = (uint8_t)(h & 0xff);
-        o[1] = (uint8_t)(h >> 8);
-    }
+    // the 34-byte block as 17 little-endian u16 words: word 0 = f16 scale,
+    // word j >= 1 = (q[2j-2], q[2j-1]); block starts are 2-byte aligned.
+    const uint32_t qb = (uint8_t)q;
+    const uint32_t lo = __shfl_sync(0xffffffffu, qb, (2 * lane - 2) & 31);
+    const uint32_t hi = __shfl_sync(0xffffffffu, qb, (2 * lane - 1) & 31);
+    uint16_t* o = reinterpret_cast<uint16_t*>(out + b * 34);
+    if (lane == 0) o[0] = __half_as_ushort(__float2half_rn(sc));
+    else if (lane < 17) o[lane] = (uint16_t)(lo | (hi << 8));
 }
 
 // ggml-style Q4_0: m = first element with the largest |x|; d = m / -8;
@@ -221,14 +222,15 @@ __global__ void k_quant_q4_blocks(const float* __restrict__ x, int64_t nblk, uin
     const float id = (dd != 0.0f) ? fdiv(1.0f, dd) : 0.0f;
     const float t = truncf(fadd(fmul(v, id), 8.5f));
     int q = (int)fminf(15.0f, fmaxf(0.0f, t));
-    const int other = __shfl_xor_sync(0xffffffffu, q, 1);
-    uint8_t* o = out + b * 18;
-    if ((lane & 1) == 0) o[2 + (lane >> 1)] = (uint8_t)(q | (other << 4));
-    if (lane == 0) {
-        const uint16_t h = __half_as_ushort(__float2half_rn(dd));
-        o[0] = (uint8_t)(h & 0xff);
-        o[1] = (uint8_t)(h >> 8);
-    }
+    // packed byte i = q[2i] | q[2i+1] << 4; the 18-byte block as 9 u16 words:
+    // word 0 = f16 scale, word j >= 1 = (byte 2j-2, byte 2j-1) = q[4j-4 .. 4j-1]
+    const int q0 = __shfl_sync(0xffffffffu, q, (4 * lane - 4) & 31);
+    const int q1 = __shfl_sync(0xffffffffu, q, (4 * lane - 3) & 31);
+    const int q2 = __shfl_sync(0xffffffffu, q, (4 * lane - 2) & 31);
+    const int q3 = __shfl_sync(0xffffffffu, q, (4 * lane - 1) & 31);
+    uint16_t* o = reinterpret_cast<uint16_t*>(out + b * 18);
+    if (lane == 0) o[0] = __half_as_ushort(__float2half_rn(dd));
+    else if (lane < 9) o[lane] = (uint16_t)((q0 | (q1 << 4)) | ((q2 | (q3 << 4)) << 8));
 }
 
 // --------------------------------------------------------------------------
@@ -464,6 +466,23 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
 #pragma unroll
         for (int q = 0; q < 4; ++q)
             if (acc[t][q] != 0.f) atomicAdd(&y[(int64_t)(t0 + t) * n_embd + c + q], acc[t][q]);
+}
+
+// Q8_0 weights, token with a full index list: the reference then takes the
+// dense ffn_swiglu_q (quant/mod.rs:1221-1223), whose down projection
+// re-quantises h to Q8_0 blocks (quant/mod.rs:1203). Replace such a token's h
+// by its Q8_0 value q * d so the f32 down kernel sums the same quantities.
+__global__ void k_sf_requant_dense(const int64_t* __restrict__ ptr, int t0, int nt, int64_t n_ff,
+                                   float* __restrict__ h) {
+    const int t = blockIdx.y;
+    if (t >= nt || ptr[t0 + t + 1] - ptr[t0 + t] < n_ff) return;
+    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b * 32 >= n_ff) return;
+    float* hr = h + (int64_t)t * n_ff + b * 32;
+    float sc;
+    const int8_t q = warp_quant_q8(hr[lane], &sc);
+    hr[lane] = fmul((float)q, sc);
 }
 
 // Repack GGUF down [ne0=n_ff, ne1=n_embd] to neuron-major. Thread per
@@ -789,6 +808,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
                 case 4: k_sf_gateup_q8<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
                 case 8: k_sf_gateup_q8<8><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
             }
+            k_sf_requant_dense<<<dim3(nblocks(n_ff, 256), nt), 256, 0, st>>>(ptr, (int)t0, nt, n_ff, h);
             k_sf_down<PI_QT_Q8_0><<<dim3((unsigned)(d / 1024), (unsigned)nsplit), 256, 0, st>>>(
                 (const uint8_t*)F->down_q, F->down_d, mask, h, (int)t0, nt, d, n_ff, per_split, out);
         }

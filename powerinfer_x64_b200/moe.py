@@ -100,6 +100,8 @@ class MoeLayer:
         T = xd.numel() // self.n_embd
         if out is None:
             out = torch.empty((T, self.n_embd), dtype=torch.float32, device="cuda")
+        if T == 0:
+            return out
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
         self.ctx.check(lib().pi_moe_forward(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, stream_ptr(stream)))
         return out

@@ -146,8 +146,8 @@ def matvec_col_major(y, x, raw, qtype, n_in: int, n_out: int) -> None:
     """quant::matvec_col_major (quant/mod.rs:939-970): y[j] = x . W[:, j]."""
     call = _Call()
     yd = call.out(y, n_out)
-    rc = lib().pi_matvec_col_major(call.ctx.h, ptr(yd), ptr(_f32(x)), ptr(_u8(raw)), int(qtype), n_in, n_out,
-                                   stream_ptr())
+    xd, rd = _f32(x), _u8(raw)  # keep the device copies alive until the launch is queued
+    rc = lib().pi_matvec_col_major(call.ctx.h, ptr(yd), ptr(xd), ptr(rd), int(qtype), n_in, n_out, stream_ptr())
     call.finish(rc)
 
 
@@ -159,7 +159,8 @@ def matvec_col_major_select(y, x, raw, qtype, n_in: int, n_out: int, indices) ->
     call = _Call()
     idx = _i64(indices)
     yd = call.out(y, idx.numel())
-    rc = lib().pi_matvec_col_major_select(call.ctx.h, ptr(yd), ptr(_f32(x)), ptr(_u8(raw)), int(qtype), n_in, n_out,
+    xd, rd = _f32(x), _u8(raw)
+    rc = lib().pi_matvec_col_major_select(call.ctx.h, ptr(yd), ptr(xd), ptr(rd), int(qtype), n_in, n_out,
                                           ptr(idx), idx.numel(), stream_ptr())
     call.finish(rc, sync=not _is_dev(y))
 
@@ -172,7 +173,8 @@ def matvec_col_major_sparse_input(y, x, indices, raw, qtype, n_in: int, n_out: i
     idx = _i64(indices) if len(indices) else None
     n_idx = 0 if idx is None else idx.numel()
     xd = _f32(x) if n_idx else None
-    rc = lib().pi_matvec_col_major_sparse_input(call.ctx.h, ptr(yd), ptr(xd), ptr(idx), n_idx, ptr(_u8(raw)),
+    rd = _u8(raw)
+    rc = lib().pi_matvec_col_major_sparse_input(call.ctx.h, ptr(yd), ptr(xd), ptr(idx), n_idx, ptr(rd),
                                                 int(qtype), n_in, n_out, stream_ptr())
     call.finish(rc, sync=not _is_dev(y))
 
@@ -181,8 +183,9 @@ def ffn_swiglu_q(out, x, gate_raw, up_raw, down_raw, qtype, n_embd: int, n_ff: i
     """quant::ffn_swiglu_q (quant/mod.rs:1179-1204)."""
     call = _Call()
     od = call.out(out, n_embd)
-    rc = lib().pi_ffn_swiglu_q(call.ctx.h, ptr(od), ptr(_f32(x)), ptr(_u8(gate_raw)), ptr(_u8(up_raw)),
-                               ptr(_u8(down_raw)), int(qtype), n_embd, n_ff, stream_ptr())
+    xd, g, u, d = _f32(x), _u8(gate_raw), _u8(up_raw), _u8(down_raw)
+    rc = lib().pi_ffn_swiglu_q(call.ctx.h, ptr(od), ptr(xd), ptr(g), ptr(u), ptr(d), int(qtype), n_embd, n_ff,
+                               stream_ptr())
     call.finish(rc)
 
 
@@ -195,6 +198,7 @@ def ffn_swiglu_q_selected(out, x, gate_raw, up_raw, down_raw, qtype, n_embd: int
     od = call.out(out, n_embd)
     idx = _i64(selected_indices) if len(selected_indices) else None
     n_idx = 0 if idx is None else idx.numel()
-    rc = lib().pi_ffn_swiglu_q_selected(call.ctx.h, ptr(od), ptr(_f32(x)), ptr(_u8(gate_raw)), ptr(_u8(up_raw)),
-                                        ptr(_u8(down_raw)), int(qtype), n_embd, n_ff, ptr(idx), n_idx, stream_ptr())
+    xd, g, u, d = _f32(x), _u8(gate_raw), _u8(up_raw), _u8(down_raw)
+    rc = lib().pi_ffn_swiglu_q_selected(call.ctx.h, ptr(od), ptr(xd), ptr(g), ptr(u), ptr(d), int(qtype), n_embd,
+                                        n_ff, ptr(idx), n_idx, stream_ptr())
     call.finish(rc, sync=not _is_dev(out))

@@ -85,7 +85,9 @@ def test_quantisers_bitwise(pkg, orc, qt):
     x[64:96] = -x[64:96]
     got = (quant.quantize_q8_0 if qt == 8 else quant.quantize_q4_0)(x)
     ref = (orc.quantize_q8_0 if qt == 8 else orc.quantize_q4_0)(x)
-    assert np.array_equal(got, ref)
+    bs = 34 if qt == 8 else 18
+    bad = np.nonzero((got.reshape(-1, bs) != ref.reshape(-1, bs)).any(1))[0]
+    assert bad.size == 0, (bad[:8], got.reshape(-1, bs)[bad[0]], ref.reshape(-1, bs)[bad[0]], x[32 * bad[0]:32 * bad[0] + 32])
     assert np.array_equal(bits(quant.dequantize(got, qt, 1, x.size)), bits(orc.dequantize(ref, qt, 1, x.size)))
 
 
