@@ -3,6 +3,7 @@
 #include "pi_internal.h"
 
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 
 int pi_set_error(pi_ctx* ctx, int code, const std::string& msg) {
@@ -43,13 +44,13 @@ int pi_scratch(pi_ctx* ctx, cudaStream_t stream, size_t bytes, char** out) {
     return PI_OK;
 }
 
-PiProfScope::PiProfScope(pi_ctx* c, cudaStream_t s, const char* name) : ctx(c), st(s) {
+PiProfScope::PiProfScope(pi_ctx* c, cudaStream_t s, const char* nm) : ctx(c), st(s), name(nm) {
     if (!ctx->profiling) return;
     std::lock_guard<std::mutex> g(ctx->mu);
     for (auto& p : ctx->prof)
-        if (p.name == name) e = &p;
+        if (p.name == nm) e = &p;
     if (!e) {
-        ctx->prof.push_back(PiProfEntry{name});
+        ctx->prof.push_back(PiProfEntry{nm});
         e = &ctx->prof.back();
     }
     cudaEvent_t b, f;
@@ -62,6 +63,17 @@ PiProfScope::PiProfScope(pi_ctx* c, cudaStream_t s, const char* name) : ctx(c), 
 
 PiProfScope::~PiProfScope() {
     if (e) cudaEventRecord(e->end.back(), st);
+    // PI_DEBUG_SYNC=1: check and synchronise after every kernel of the layer
+    // path and name the one that failed.
+    static const bool debug_sync = [] {
+        const char* v = std::getenv("PI_DEBUG_SYNC");
+        return v && v[0] == '1';
+    }();
+    if (debug_sync) {
+        cudaError_t err = cudaGetLastError();
+        if (err == cudaSuccess) err = cudaStreamSynchronize(st);
+        if (err != cudaSuccess) std::fprintf(stderr, "[pi debug] after %s: %s\n", name, cudaGetErrorString(err));
+    }
 }
 
 extern "C" int pi_ctx_profile(pi_ctx* ctx, int enable) {

@@ -103,6 +103,7 @@ int pi_set_error(pi_ctx* ctx, int code, const std::string& msg);
 struct PiProfScope {
     pi_ctx* ctx;
     cudaStream_t st;
+    const char* name;
     PiProfEntry* e = nullptr;
     PiProfScope(pi_ctx* c, cudaStream_t s, const char* name);
     ~PiProfScope();

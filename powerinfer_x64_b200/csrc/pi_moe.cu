@@ -134,18 +134,178 @@ __global__ __launch_bounds__(128) void k_router(const float* __restrict__ xin, c
 }
 
 // ---------------------------------------------------------------------------
+// k_router_fast: certified logits. Warp = one router row (E expert rows +
+// row E, the shared-expert gate), lane l owns the contiguous slice
+// i in [CH*l, CH*l + CH) of the d inputs, CH = d/32. Per token the lane runs
+// the reference's own sequential f32 chain over its slice (c_l) and two
+// bound accumulators; a warp scan in f64 joins the slices. Besides the
+// logit L the kernel writes eps with
+//     |L - reference logit| <= eps,
+// where the reference logit is the sequential f32 sum of matvec_col_major_f32
+// (quant/mod.rs:921-935). Bound (u = 2^-24): the reference's error is at most
+// u * (sum_k |s_k| + sum_i |w_i x_i|) over its running sums s_k; here
+// |s_k| <= |S_start(l)| + |local running sum| + slack, S_start the exact
+// prefix at the slice start. Our own estimate has an error of the same form.
+// ---------------------------------------------------------------------------
+template <int CH>
+__global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ xin, const float* __restrict__ W,
+                                                     const float* __restrict__ bias, int T, int d, int E, int tpc,
+                                                     float* __restrict__ logits, float* __restrict__ eps) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 8 + warp;
+    if (e > E) return;
+    const float u = 5.9604644775390625e-08f;  // 2^-24
+    float w[CH];
+    const float* wr = W + (size_t)e * d + lane * CH;
+#pragma unroll
+    for (int q = 0; q < CH / 4; ++q) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(wr) + q);
+        w[4 * q] = v.x;
+        w[4 * q + 1] = v.y;
+        w[4 * q + 2] = v.z;
+        w[4 * q + 3] = v.w;
+    }
+    const float be = (bias && e < E) ? bias[e] : 0.0f;
+    const int t_end = min(T, (int)(blockIdx.y + 1) * tpc);
+    for (int t = blockIdx.y * tpc; t < t_end; ++t) {
+        const float* xr = xin + (size_t)t * d + lane * CH;
+        float s = 0.0f, absacc = 0.0f, A = 0.0f;
+#pragma unroll
+        for (int q = 0; q < CH / 4; ++q) {
+            const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * q);
+            const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float p = fmul(w[4 * q + j], xs4[j]);
+                s = fadd(s, p);
+                absacc += fabsf(s);
+                A += fabsf(p);
+            }
+        }
+        // exclusive prefix of the slice sums, in f64
+        double incl = (double)s;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const double v = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += v;
+        }
+        const double start = incl - (double)s;
+        const double total = __shfl_sync(0xffffffffu, incl, 31);
+        double bnd = (double)CH * fabs(start) + (double)absacc + 2.0 * (double)A + 5.0 * fabs((double)s) +
+                     (double)CH * (double)u * ((double)absacc + (double)A) * 32.0;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) bnd += __shfl_xor_sync(0xffffffffu, bnd, o);
+        if (lane == 0) {
+            float L = (float)total;
+            double ep = 2.02 * (double)u * bnd + (double)u * fabs((double)L) + 1e-30;
+            if (bias && e < E) {
+                L = fadd(L, be);
+                ep += 2.0 * (double)u * (fabs((double)L) + ep);
+            }
+            logits[(size_t)t * (E + 1) + e] = L;
+            eps[(size_t)t * (E + 1) + e] = (float)(ep * (1.0 + 1e-6));
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_router_exact_list: exact (reference-order) logits for the tokens listed
+// in list[0 .. *n_list). CTA = 32 router rows x one listed token at a time;
+// the 128 threads stage 32 x 128 tiles of the rows in shared memory (next
+// tile prefetched into registers), warp 0 runs one sequential chain per row
+// (d must be a multiple of 128). grid (ceil((E+1)/32), G), block 128.
+// ---------------------------------------------------------------------------
+constexpr int EX_CH = 128;
+__global__ __launch_bounds__(128) void k_router_exact_list(const float* __restrict__ xin, const float* __restrict__ W,
+                                                           const float* __restrict__ bias, int d, int E,
+                                                           const int32_t* __restrict__ list,
+                                                           const int32_t* __restrict__ n_list,
+                                                           float* __restrict__ logits) {
+    __shared__ float ws[2][32][EX_CH + 1];
+    __shared__ float xs[2][EX_CH];
+    const int n = *n_list;
+    const int row0 = blockIdx.x * 32;
+    const int nrow = min(32, E + 1 - row0);
+    const int tid = threadIdx.x;
+    const int ntiles = d / EX_CH;
+    for (int g = blockIdx.y; g < n; g += gridDim.y) {
+        const int t = list[g];
+        const float* xr = xin + (size_t)t * d;
+        float4 rw[8];
+        float rx;
+        auto load = [&](int tile) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int idx = tid + 128 * m;  // 1024 float4 = 32 rows x 32
+                const int r = idx >> 5, j = idx & 31;
+                rw[m] = (r < nrow) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(row0 + r) * d + tile * EX_CH) + j)
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+            rx = xr[tile * EX_CH + tid];
+        };
+        auto store = [&](int buf) {
+#pragma unroll
+            for (int m = 0; m < 8; ++m) {
+                const int idx = tid + 128 * m;
+                const int r = idx >> 5, j = idx & 31;
+                ws[buf][r][4 * j] = rw[m].x;
+                ws[buf][r][4 * j + 1] = rw[m].y;
+                ws[buf][r][4 * j + 2] = rw[m].z;
+                ws[buf][r][4 * j + 3] = rw[m].w;
+            }
+            xs[buf][tid] = rx;
+        };
+        __syncthreads();
+        load(0);
+        store(0);
+        __syncthreads();
+        float acc = 0.0f;
+        for (int tile = 0; tile < ntiles; ++tile) {
+            const int buf = tile & 1;
+            if (tile + 1 < ntiles) load(tile + 1);
+            if (tid < nrow) {
+                const float* wrow = ws[buf][tid];
+                const float* xv = xs[buf];
+#pragma unroll 8
+                for (int i = 0; i < EX_CH; ++i) acc = fadd(acc, fmul(wrow[i], xv[i]));
+            }
+            if (tile + 1 < ntiles) store(buf ^ 1);
+            __syncthreads();
+        }
+        if (tid < nrow) {
+            const int e = row0 + tid;
+            float v = acc;
+            if (bias && e < E) v = fadd(v, bias[e]);
+            logits[(size_t)t * (E + 1) + e] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // k_topk: one warp per token. E <= 32 * TK_PER_LANE.
 // ---------------------------------------------------------------------------
 constexpr int TK_PER_LANE = 16, TK_WARPS = 4;
-__global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits, int T, int E, int k,
+// Two modes:
+//  * eps != null (certify): select on the fast logits; if the selection is
+//    provably the reference's (every selected logit's interval lies above
+//    every other's by a margin that also rules out equal probabilities after
+//    rounding), write the routing; otherwise append the token to flag_list.
+//  * list != null (exact): route the listed tokens from their exact logits.
+__global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits,
+                                                        const float* __restrict__ eps, int T, int E, int k,
                                                         int has_shgate, int32_t* __restrict__ idx,
                                                         float* __restrict__ gates, float* __restrict__ shscale,
-                                                        int32_t* __restrict__ counts) {
+                                                        int32_t* __restrict__ counts,
+                                                        int32_t* __restrict__ flag_list,
+                                                        int32_t* __restrict__ n_flag,
+                                                        const int32_t* __restrict__ list,
+                                                        const int32_t* __restrict__ n_list) {
     __shared__ float s_p[TK_WARPS][32 * TK_PER_LANE];
     __shared__ int s_sel[TK_WARPS][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * TK_WARPS + warp;
-    if (t >= T) return;
+    const int n_tok = list ? *n_list : T;
+    for (int g = blockIdx.x * TK_WARPS + warp; g < n_tok; g += gridDim.x * TK_WARPS) {
+    const int t = list ? list[g] : g;
     const float* lr = logits + (size_t)t * (E + 1);
     float l[TK_PER_LANE];
     float m = -INFINITY;
@@ -201,6 +361,29 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
         if (lane == 0) s_sel[warp][r] = bi;
     }
     __syncwarp();
+    if (eps) {
+        const float* er = eps + (size_t)t * (E + 1);
+        float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < TK_PER_LANE; ++j) {
+            const int e = lane + 32 * j;
+            if (e >= E) continue;
+            const float ev = er[e];
+            if ((taken >> j) & 1u) lo = fminf(lo, l[j] - ev);
+            else hi = fmaxf(hi, l[j] + ev + 4e-6f * (1.0f + fabsf(l[j] - m)));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+            hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+        }
+        // lo - hi > 0 with a relative guard; the boundary must sit well inside exp's range
+        const bool cert = (lo > hi + 1e-6f * fabsf(hi)) && (lo - m > -80.0f);
+        if (!cert) {
+            if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
+            continue;
+        }
+    }
     // ascending sort of the k selected indices (model/mod.rs:1303)
     int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
     int rank = 0;
@@ -220,6 +403,7 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
         atomicAdd(&counts[e], 1);
     }
     if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -389,9 +573,11 @@ struct ExpertArgs {
 
 PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
 
-// Q8_0 gate+up: CTA = 32 rows of one expert (16 warps x 2 rows, gate and
+// Q8_0 gate+up: CTA = 16 rows of one expert (8 warps x 2 rows, gate and
 // up = 4 row-vectors per warp), CPL = d/512 16-byte chunks per lane per row
 // (lane l holds chunks l + 32c; chunks 2m, 2m+1 form 32-element block m).
+// 256 threads and ~70 KB of shared memory let two CTAs share an SM, so one
+// CTA's weight loads overlap another's arithmetic.
 //
 // The sums keep the reference's order exactly (matvec_q8_0_sse_range,
 // quant/mod.rs:835-871): per block an exact int32 dot, the term
@@ -399,24 +585,23 @@ PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot
 // Terms are staged in shared memory; lane (rv, token) of each warp then runs
 // the sequential chain for one (row-vector, token) pair. h is therefore the
 // reference's h bit for bit (up to its expf rounding), so the Q8_0
-// re-quantisation of h below makes the same integer choices.
-constexpr int GU_TB = 8;  // tokens per batch: 4 row-vectors x 8 tokens = 32 chains per warp
+// re-quantisation of h in k_down_q8 makes the same integer choices.
+constexpr int GU_TB = 8;    // tokens per batch: 4 row-vectors x 8 tokens = 32 chains per warp
+constexpr int GU_ROWS = 16; // rows per CTA
 template <int CPL>
-__global__ __launch_bounds__(512) void k_gateup_q8(ExpertArgs a) {
+__global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
     constexpr int NB = 16 * CPL;   // blocks per row
     constexpr int STRIDE = NB + 4; // padded chain stride (floats): conflict-free 16-byte reads
     extern __shared__ __align__(16) float smem[];
     float* terms = smem + (threadIdx.x >> 5) * (4 * GU_TB * STRIDE);
-    __shared__ float hbuf[GU_TB][33];
-    __shared__ float res[16][4][GU_TB];
+    __shared__ float res[8][4][GU_TB];
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
     const bool sh = (item.x == a.E);
     const int d = a.d, f = a.f, nb = d / 32;
-    const int row0 = blockIdx.x * 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int rA = row0 + 2 * warp;
+    const int rA = blockIdx.x * GU_ROWS + 2 * warp;
     const size_t mat = sh ? 0 : (size_t)item.x * f;
     const int8_t* G = (const int8_t*)(sh ? a.gs : a.g) + (mat + rA) * d;
     const int8_t* U = (const int8_t*)(sh ? a.us : a.u) + (mat + rA) * d;
@@ -478,39 +663,37 @@ __global__ __launch_bounds__(512) void k_gateup_q8(ExpertArgs a) {
         __syncwarp();
         if (lane < 2 * GU_TB) {
             const int r = lane / GU_TB, tk = lane % GU_TB;  // row rA + r
-            if (tk < nt) hbuf[tk][2 * warp + r] = swiglu_ref(res[warp][2 * r][tk], res[warp][2 * r + 1][tk]);
+            if (tk < nt)
+                a.hf[(size_t)(item.y + t0 + tk) * f + rA + r] = swiglu_ref(res[warp][2 * r][tk], res[warp][2 * r + 1][tk]);
         }
-        __syncthreads();
-        if (warp < nt) {
-            const int slot = item.y + t0 + warp;
-            float sc;
-            const int8_t q = warp_quant_q8(hbuf[warp][lane], &sc);
-            a.hq[(size_t)slot * f + row0 + lane] = q;
-            if (lane == 0) a.hs[(size_t)slot * (f / 32) + row0 / 32] = sc;
-        }
-        __syncthreads();
+        __syncwarp();
     }
 }
 
 template <int CPL>
 constexpr size_t gateup_q8_smem() {
-    return (size_t)16 * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
+    return (size_t)8 * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
 }
 
 // Q8_0 down: CTA = 128 output rows (8 warps x 16 rows), 4 lanes per row,
-// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass.
+// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass. The prologue
+// re-quantises the item's hidden vectors h to Q8_0 (quant/mod.rs:698-736, as
+// matvec_col_major does for the down projection) into shared memory.
 template <int CPQ>
 __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
+    constexpr int F = CPQ * 64;  // expert width
+    __shared__ __align__(16) int8_t s_hq[TG][F];
+    __shared__ float s_hs[TG][F / 32];
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
     const bool sh = (item.x == a.E);
-    const int d = a.d, f = a.f, fb = f / 32;
+    const int d = a.d, fb = F / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = lane & 3;
     const int rbase = blockIdx.x * 128 + warp * 16 + (lane >> 2);
     const size_t mat = sh ? 0 : (size_t)item.x * d;
-    const int8_t* D = (const int8_t*)(sh ? a.dns : a.dn) + mat * f;
+    const int8_t* D = (const int8_t*)(sh ? a.dns : a.dn) + mat * F;
     const __half* DD = (sh ? a.dsd : a.dd) + mat * fb;
     constexpr int BPQ = CPQ / 2;  // blocks per lane
     int4 w[2][CPQ];
@@ -519,14 +702,22 @@ __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
     for (int p = 0; p < 2; ++p) {
         const int row = rbase + 8 * p;
 #pragma unroll
-        for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)row * f + (q * CPQ + c) * 16);
+        for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)row * F + (q * CPQ + c) * 16);
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) sw[p][b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
     }
+    for (int m = warp; m < item.z * fb; m += 8) {
+        const int tk = m / fb, b = m % fb;
+        float sc;
+        const int8_t hq = warp_quant_q8(a.hf[(size_t)(item.y + tk) * F + b * 32 + lane], &sc);
+        s_hq[tk][b * 32 + lane] = hq;
+        if (lane == 0) s_hs[tk][b] = sc;
+    }
+    __syncthreads();
     for (int tk = 0; tk < item.z; ++tk) {
         const int slot = item.y + tk;
-        const int8_t* hr = a.hq + (size_t)slot * f + q * CPQ * 16;
-        const float* hsr = a.hs + (size_t)slot * fb + q * BPQ;
+        const int8_t* hr = &s_hq[tk][q * CPQ * 16];
+        const float* hsr = &s_hs[tk][q * BPQ];
         int4 hv[CPQ];
         float hsv[BPQ];
 #pragma unroll
@@ -791,6 +982,9 @@ struct FwdBufs {
     int8_t* xq;
     float* xs;
     float* logits;
+    float* eps;
+    int32_t* flag_list;
+    int32_t* n_flag;
     int32_t* idx;
     float* gates;
     float* shscale;
@@ -821,6 +1015,9 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
     f.xq = b.take<int8_t>(T * d);
     f.xs = b.take<float>(T * (d / 32));
     f.logits = b.take<float>(T * (E + 1));
+    f.eps = b.take<float>(T * (E + 1));
+    f.flag_list = b.take<int32_t>(T);
+    f.n_flag = b.take<int32_t>(1);
     f.idx = b.take<int32_t>(T * k);
     f.gates = b.take<float>(T * k);
     f.shscale = b.take<float>(T);
@@ -830,15 +1027,9 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
     f.slot_of = b.take<int32_t>(T * k);
     f.items = b.take<int4>(max_items(L, T));
     f.n_items = b.take<int32_t>(1);
-    if (L->qtype == PI_QT_Q8_0) {
-        f.hq = b.take<int8_t>(slots * F);
-        f.hs = b.take<float>(slots * (F / 32));
-        f.hf = nullptr;
-    } else {
-        f.hq = nullptr;
-        f.hs = nullptr;
-        f.hf = b.take<float>(slots * F);
-    }
+    f.hq = nullptr;
+    f.hs = nullptr;
+    f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     f.bytes = b.off + 256;
     return f;
@@ -866,16 +1057,35 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         PiProfScope ps(ctx, st, "k_prep");
         k_prep<<<(unsigned)T, 256, 0, st>>>(x, d, do_norm, 1e-6f, B.normed, (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
     }
-    dim3 rg((unsigned)((E + 1 + 127) / 128), (unsigned)((T + RT_TT - 1) / RT_TT));
-    {
-        PiProfScope ps(ctx, st, "k_router");
-        k_router<<<rg, 128, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, E + 1, B.logits);
-    }
+    // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
+    if (pi_cuda_check(ctx, cudaMemsetAsync(B.n_flag, 0, sizeof(int32_t), st), "memset flags")) return PI_ERR_CUDA;
+    {
+        PiProfScope ps(ctx, st, "k_router_fast");
+        const int64_t ctas_x = (E + 1 + 7) / 8;
+        const int tpc = (int)std::max<int64_t>(1, (T * ctas_x + 2 * ctx->sm_count - 1) / (2 * ctx->sm_count));
+        dim3 rg((unsigned)ctas_x, (unsigned)((T + tpc - 1) / tpc));
+        switch (d / 32) {
+            case 16: k_router_fast<16><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
+            case 32: k_router_fast<32><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
+            case 64: k_router_fast<64><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
+            case 128: k_router_fast<128><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be 512, 1024, 2048 or 4096");
+        }
+    }
+    const unsigned tk_blocks = (unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 4 * ctx->sm_count);
     {
         PiProfScope ps(ctx, st, "k_topk");
-        k_topk<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(
-            B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts);
+        k_topk<<<tk_blocks, TK_WARPS * 32, 0, st>>>(B.logits, B.eps, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx,
+                                                   gates, B.shscale, counts, B.flag_list, B.n_flag, nullptr, nullptr);
+    }
+    {
+        PiProfScope ps(ctx, st, "k_router_exact");
+        dim3 eg((unsigned)((E + 1 + 31) / 32), (unsigned)std::min<int64_t>(T, 64));
+        k_router_exact_list<<<eg, 128, 0, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag, B.logits);
+        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
+            B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
+            nullptr, B.flag_list, B.n_flag);
     }
     {
         PiProfScope ps(ctx, st, "k_dispatch");
@@ -912,7 +1122,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.hf = B.hf;
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
-    const dim3 gu((unsigned)(L->f / 32), ni), dn((unsigned)(L->d / 128), ni);
+    const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / 128), ni);
     if (q8) {
         {
         PiProfScope ps(ctx, st, "k_gateup");
@@ -925,7 +1135,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
                                  (int)gateup_q8_smem<C>());                                                   \
             attr = true;                                                                                      \
         }                                                                                                     \
-        k_gateup_q8<C><<<gu, 512, gateup_q8_smem<C>(), st>>>(a);                                             \
+        k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
         break;                                                                                                \
     }
             GU_Q8(1)

