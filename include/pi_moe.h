@@ -102,6 +102,21 @@ int pi_quantize_q4_0(pi_ctx* ctx, const float* x, int64_t n, void* out_raw, void
 int pi_matvec_col_major(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in,
                         int64_t n_out, void* stream);
 
+/* Allocation-free variant of pi_matvec_col_major for Q8_0 weights (no
+ * counterpart in the reference). For callers that cannot allocate device
+ * memory when they call -- e.g. a host whose allocator owns all device memory
+ * and forbids cudaMalloc on its hot path -- it needs no pi_ctx and calls no
+ * cudaMalloc/cudaFree: the quantised copy of x lives in a fixed device array
+ * that every GPU loading this library keeps until exit. Limit: n_in <= 16384
+ * (larger n_in returns PI_ERR_ARG); n_in % 32 == 0. Runs on the current
+ * device; its first call on a device looks up the array's address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (other streams
+ * or threads) race and must be serialised by the caller. Returns PI_OK,
+ * PI_ERR_ARG or PI_ERR_CUDA (no error string: there is no context). */
+int pi_matvec_col_major_q8_0_noalloc(float* y, const float* x, const void* raw, int64_t n_in, int64_t n_out,
+                                     void* stream);
+
 /* quant::matvec_col_major_select (src/quant/mod.rs:974-1068): y[s] = x . W[:, idx[s]].
  * idx: int64 device array. Out-of-range -> device error (pi_ctx_check -> PI_ERR_INDEX). */
 int pi_matvec_col_major_select(pi_ctx* ctx, float* y, const float* x, const void* raw, int qtype, int64_t n_in,

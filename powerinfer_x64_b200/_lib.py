@@ -54,6 +54,7 @@ SIGNATURES = {
     "pi_quantize_q8_0": (_INT, [_P, _P, _I64, _P, _P]),
     "pi_quantize_q4_0": (_INT, [_P, _P, _I64, _P, _P]),
     "pi_matvec_col_major": (_INT, [_P, _P, _P, _P, _INT, _I64, _I64, _P]),
+    "pi_matvec_col_major_q8_0_noalloc": (_INT, [_P, _P, _P, _I64, _I64, _P]),
     "pi_matvec_col_major_select": (_INT, [_P, _P, _P, _P, _INT, _I64, _I64, _P, _I64, _P]),
     "pi_matvec_col_major_sparse_input": (_INT, [_P, _P, _P, _P, _I64, _P, _INT, _I64, _I64, _P]),
     "pi_ffn_swiglu_q": (_INT, [_P, _P, _P, _P, _P, _P, _INT, _I64, _I64, _P]),

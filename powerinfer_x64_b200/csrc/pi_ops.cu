@@ -854,3 +854,65 @@ extern "C" int pi_synth_normal_host(uint64_t seed, uint64_t offset, int64_t n, f
     }
     return PI_OK;
 }
+
+// ===========================================================================
+// Allocation-free Q8_0 matvec.
+//
+// pi_matvec_col_major quantises x into scratch that its context allocates on
+// first use. Some hosts cannot allocate device memory at the point of the
+// call: an embedding whose allocator forbids cudaMalloc on its hot path (for
+// example a runtime that preallocates all device memory up front, or a
+// process that drives the GPU under a stream capture it does not own). For
+// them the variant below keeps its scratch -- the quantised copy of x -- in a
+// fixed file-scope device array, so the call allocates nothing and needs no
+// pi_ctx. Every GPU that loads this library reserves the array until exit.
+// ===========================================================================
+#include <mutex>
+
+namespace {
+constexpr int64_t PI_STATIC_MAX_N_IN = 16384;  // largest n_in the fixed scratch holds
+struct StaticScratch {
+    int8_t xq[PI_STATIC_MAX_N_IN];
+    float xs[PI_STATIC_MAX_N_IN / 32];
+};
+static __device__ __align__(256) StaticScratch g_static_scratch;
+
+// Device addresses of g_static_scratch, looked up once per device (the host
+// symbol is only a stand-in and must never be handed to a kernel).
+constexpr int PI_MAX_DEVICES = 64;
+std::mutex g_static_mu;
+StaticScratch* g_static_ptr[PI_MAX_DEVICES] = {};
+}  // namespace
+
+extern "C" int pi_matvec_col_major_q8_0_noalloc(float* y, const float* x, const void* raw, int64_t n_in,
+                                                int64_t n_out, void* stream) {
+    if (!y || !x || !raw || n_in <= 0 || n_out < 0 || n_in % 32) return PI_ERR_ARG;
+    if (n_in > PI_STATIC_MAX_N_IN) return PI_ERR_ARG;  // beyond the fixed scratch
+    if (n_out == 0) return PI_OK;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= PI_MAX_DEVICES) {
+        cudaGetLastError();
+        return PI_ERR_CUDA;
+    }
+    StaticScratch* scr;
+    {
+        std::lock_guard<std::mutex> g(g_static_mu);
+        if (!g_static_ptr[dev]) {
+            void* p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess || !p) {
+                cudaGetLastError();
+                return PI_ERR_CUDA;
+            }
+            g_static_ptr[dev] = static_cast<StaticScratch*>(p);
+        }
+        scr = g_static_ptr[dev];
+    }
+    cudaStream_t st = (cudaStream_t)stream;
+    // k_quant_act writes every byte of xq[0, n_in) and xs[0, n_in/32) before
+    // k_rows_q8 reads them, so nothing left by an earlier call is read.
+    k_quant_act<<<nblocks(n_in, 256), 256, 0, st>>>(x, n_in, scr->xq, scr->xs);
+    const size_t smem = (size_t)8 * (n_in / 32) * 4;  // <= 16 KiB for n_in <= 16384
+    k_rows_q8<<<nblocks(n_out, 8), 256, smem, st>>>(y, scr->xq, scr->xs, (const uint8_t*)raw, n_in, n_out, nullptr,
+                                                    n_out, nullptr);
+    return cudaGetLastError() == cudaSuccess ? PI_OK : PI_ERR_CUDA;
+}
