@@ -35,15 +35,18 @@ constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one wa
 
 // ---------------------------------------------------------------------------
 // k_prep: optional RMSNorm, then Q8_0 quantisation of the (normed) tokens.
-// grid T, block 256.
+// grid (T, ceil(d/256)), block 256: CTA (t, c) handles elements
+// [256c, 256c + 256) of token t (8 quant blocks, one per warp). With RMSNorm
+// every CTA of a token recomputes the token's 1/rms (identical value).
 // ---------------------------------------------------------------------------
 __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
                                               float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
                                               float* __restrict__ xs) {
     const int t = blockIdx.x;
     const float* xr = x + (size_t)t * d;
+    const int i = blockIdx.y * 256 + threadIdx.x;
     __shared__ float s_inv;
-    const float* src = xr;
+    float v = (i < d) ? xr[i] : 0.0f;
     if (do_norm) {
         // sum_squares_sse (simd.rs:116-137): 4 lane accumulators over
         // elements i = 4m + lane, then (l0 + l1) + (l2 + l3), then a scalar tail.
@@ -52,33 +55,26 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
             float acc = 0.0f;
             const int n4 = d & ~3;
             if (lane < 4)
-                for (int i = lane; i < n4; i += 4) acc = fadd(acc, fmul(xr[i], xr[i]));
+                for (int j = lane; j < n4; j += 4) acc = fadd(acc, fmul(xr[j], xr[j]));
             float a1 = __shfl_sync(0xffffffffu, acc, 1);
             float a2 = __shfl_sync(0xffffffffu, acc, 2);
             float a3 = __shfl_sync(0xffffffffu, acc, 3);
             if (lane == 0) {
                 float ss = fadd(fadd(acc, a1), fadd(a2, a3));
-                for (int i = n4; i < d; ++i) ss = fadd(ss, fmul(xr[i], xr[i]));
+                for (int j = n4; j < d; ++j) ss = fadd(ss, fmul(xr[j], xr[j]));
                 float rms = __fsqrt_rn(fadd(fdiv(ss, (float)d), eps));
                 s_inv = fdiv(1.0f, rms);
             }
         }
         __syncthreads();
-        const float inv = s_inv;
-        float* nr = normed + (size_t)t * d;
-        for (int i = threadIdx.x; i < d; i += blockDim.x) nr[i] = fmul(xr[i], inv);  // * weight (1.0) is exact
-        __syncthreads();
-        src = nr;
+        v = fmul(v, s_inv);  // * weight (1.0) is exact
+        if (i < d) normed[(size_t)t * d + i] = v;
     }
-    if (!do_quant) return;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nb = d / 32;
-    for (int b = warp; b < nb; b += blockDim.x / 32) {
-        float sc;
-        int8_t q = warp_quant_q8(src[b * 32 + lane], &sc);
-        xq[(size_t)t * d + b * 32 + lane] = q;
-        if (lane == 0) xs[(size_t)t * nb + b] = sc;
-    }
+    if (!do_quant || i >= d) return;  // d % 32 == 0: whole warps leave together
+    float sc;
+    const int8_t q = warp_quant_q8(v, &sc);
+    xq[(size_t)t * d + i] = q;
+    if ((threadIdx.x & 31) == 0) xs[(size_t)t * (d / 32) + i / 32] = sc;
 }
 
 // ---------------------------------------------------------------------------
@@ -147,16 +143,23 @@ __global__ __launch_bounds__(128) void k_router(const float* __restrict__ xin, c
 // |s_k| <= |S_start(l)| + |local running sum| + slack, S_start the exact
 // prefix at the slice start. Our own estimate has an error of the same form.
 // ---------------------------------------------------------------------------
+constexpr int RF_SMEM_FLOATS = 8704;  // staged tokens (32 slices of CH + 4 padding floats each)
 template <int CH>
 __global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ xin, const float* __restrict__ W,
                                                      const float* __restrict__ bias, int T, int d, int E, int tpc,
                                                      float* __restrict__ logits, float* __restrict__ eps) {
+    // tokens of this CTA are staged in shared memory, TS at a time; slice l of
+    // a token sits at l * (CH + 4) so the lanes' 16-byte reads hit distinct banks
+    constexpr int TSTRIDE = 32 * (CH + 4);
+    constexpr int TS = RF_SMEM_FLOATS / TSTRIDE;
+    static_assert(TS >= 1, "router slice too large");
+    __shared__ __align__(16) float xsm[RF_SMEM_FLOATS];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int e = blockIdx.x * 8 + warp;
-    if (e > E) return;
+    const bool active = e <= E;
     const float u = 5.9604644775390625e-08f;  // 2^-24
     float w[CH];
-    const float* wr = W + (size_t)e * d + lane * CH;
+    const float* wr = W + (size_t)(active ? e : E) * d + lane * CH;
 #pragma unroll
     for (int q = 0; q < CH / 4; ++q) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(wr) + q);
@@ -166,44 +169,57 @@ __global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ x
         w[4 * q + 3] = v.w;
     }
     const float be = (bias && e < E) ? bias[e] : 0.0f;
-    const int t_end = min(T, (int)(blockIdx.y + 1) * tpc);
-    for (int t = blockIdx.y * tpc; t < t_end; ++t) {
-        const float* xr = xin + (size_t)t * d + lane * CH;
-        float s = 0.0f, absacc = 0.0f, A = 0.0f;
-#pragma unroll
-        for (int q = 0; q < CH / 4; ++q) {
-            const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * q);
-            const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float p = fmul(w[4 * q + j], xs4[j]);
-                s = fadd(s, p);
-                absacc += fabsf(s);
-                A += fabsf(p);
-            }
+    const int t_beg = blockIdx.y * tpc, t_end = min(T, t_beg + tpc);
+    for (int c0 = t_beg; c0 < t_end; c0 += TS) {
+        const int nt = min(TS, t_end - c0);
+        __syncthreads();
+        for (int q = threadIdx.x; q < nt * (d / 4); q += blockDim.x) {
+            const int tt = q / (d / 4), i4 = q % (d / 4);
+            const float4 v = *reinterpret_cast<const float4*>(xin + (size_t)(c0 + tt) * d + 4 * i4);
+            const int i = 4 * i4;
+            *reinterpret_cast<float4*>(&xsm[tt * TSTRIDE + (i / CH) * (CH + 4) + i % CH]) = v;
         }
-        // exclusive prefix of the slice sums, in f64
-        double incl = (double)s;
+        __syncthreads();
+        if (!active) continue;
+        for (int tt = 0; tt < nt; ++tt) {
+            const int t = c0 + tt;
+            const float* xr = xsm + tt * TSTRIDE + lane * (CH + 4);
+            float s = 0.0f, absacc = 0.0f, A = 0.0f;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const double v = __shfl_up_sync(0xffffffffu, incl, o);
-            if (lane >= o) incl += v;
-        }
-        const double start = incl - (double)s;
-        const double total = __shfl_sync(0xffffffffu, incl, 31);
-        double bnd = (double)CH * fabs(start) + (double)absacc + 2.0 * (double)A + 5.0 * fabs((double)s) +
-                     (double)CH * (double)u * ((double)absacc + (double)A) * 32.0;
+            for (int q = 0; q < CH / 4; ++q) {
+                const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * q);
+                const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) bnd += __shfl_xor_sync(0xffffffffu, bnd, o);
-        if (lane == 0) {
-            float L = (float)total;
-            double ep = 2.02 * (double)u * bnd + (double)u * fabs((double)L) + 1e-30;
-            if (bias && e < E) {
-                L = fadd(L, be);
-                ep += 2.0 * (double)u * (fabs((double)L) + ep);
+                for (int j = 0; j < 4; ++j) {
+                    const float p = fmul(w[4 * q + j], xs4[j]);
+                    s = fadd(s, p);
+                    absacc += fabsf(s);
+                    A += fabsf(p);
+                }
             }
-            logits[(size_t)t * (E + 1) + e] = L;
-            eps[(size_t)t * (E + 1) + e] = (float)(ep * (1.0 + 1e-6));
+            // exclusive prefix of the slice sums, in f64
+            double incl = (double)s;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const double v = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += v;
+            }
+            const double start = incl - (double)s;
+            const double total = __shfl_sync(0xffffffffu, incl, 31);
+            double bnd = (double)CH * fabs(start) + (double)absacc + 2.0 * (double)A + 5.0 * fabs((double)s) +
+                         (double)CH * (double)u * ((double)absacc + (double)A) * 32.0;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) bnd += __shfl_xor_sync(0xffffffffu, bnd, o);
+            if (lane == 0) {
+                float L = (float)total;
+                double ep = 2.02 * (double)u * bnd + (double)u * fabs((double)L) + 1e-30;
+                if (bias && e < E) {
+                    L = fadd(L, be);
+                    ep += 2.0 * (double)u * (fabs((double)L) + ep);
+                }
+                logits[(size_t)t * (E + 1) + e] = L;
+                eps[(size_t)t * (E + 1) + e] = (float)(ep * (1.0 + 1e-6));
+            }
         }
     }
 }
@@ -675,15 +691,24 @@ constexpr size_t gateup_q8_smem() {
     return (size_t)8 * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
 }
 
+// Q8_0 h re-quantisation (quant/mod.rs:698-736, as the reference's down
+// matvec quantises its input): warp per 32-block of hf[slot][.].
+__global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __restrict__ hq,
+                          float* __restrict__ hs) {
+    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= nblk) return;
+    float sc;
+    hq[b * 32 + lane] = warp_quant_q8(hf[b * 32 + lane], &sc);
+    if (lane == 0) hs[b] = sc;
+}
+
 // Q8_0 down: CTA = 128 output rows (8 warps x 16 rows), 4 lanes per row,
-// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass. The prologue
-// re-quantises the item's hidden vectors h to Q8_0 (quant/mod.rs:698-736, as
-// matvec_col_major does for the down projection) into shared memory.
+// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass; the quantised h
+// of each slot comes from k_quant_h.
 template <int CPQ>
 __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
     constexpr int F = CPQ * 64;  // expert width
-    __shared__ __align__(16) int8_t s_hq[TG][F];
-    __shared__ float s_hs[TG][F / 32];
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -706,18 +731,10 @@ __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) sw[p][b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
     }
-    for (int m = warp; m < item.z * fb; m += 8) {
-        const int tk = m / fb, b = m % fb;
-        float sc;
-        const int8_t hq = warp_quant_q8(a.hf[(size_t)(item.y + tk) * F + b * 32 + lane], &sc);
-        s_hq[tk][b * 32 + lane] = hq;
-        if (lane == 0) s_hs[tk][b] = sc;
-    }
-    __syncthreads();
     for (int tk = 0; tk < item.z; ++tk) {
         const int slot = item.y + tk;
-        const int8_t* hr = &s_hq[tk][q * CPQ * 16];
-        const float* hsr = &s_hs[tk][q * BPQ];
+        const int8_t* hr = a.hq + (size_t)slot * F + q * CPQ * 16;
+        const float* hsr = a.hs + (size_t)slot * fb + q * BPQ;
         int4 hv[CPQ];
         float hsv[BPQ];
 #pragma unroll
@@ -873,7 +890,8 @@ __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, co
                                                  const float* __restrict__ shscale, int T, int k, int d,
                                                  int has_shared, int residual, float* __restrict__ out) {
     const int t = blockIdx.x;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    const int c = blockIdx.y * blockDim.x + threadIdx.x;
+    if (c < d) {
         float acc = 0.0f;
         for (int j = 0; j < k; ++j) {
             const int slot = slot_of[(size_t)t * k + j];
@@ -1027,8 +1045,8 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
     f.slot_of = b.take<int32_t>(T * k);
     f.items = b.take<int4>(max_items(L, T));
     f.n_items = b.take<int32_t>(1);
-    f.hq = nullptr;
-    f.hs = nullptr;
+    f.hq = b.take<int8_t>(slots * F);
+    f.hs = b.take<float>(slots * (F / 32));
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     f.bytes = b.off + 256;
@@ -1055,7 +1073,8 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
 
     if (do_norm || (q8 && !route_only)) {
         PiProfScope ps(ctx, st, "k_prep");
-        k_prep<<<(unsigned)T, 256, 0, st>>>(x, d, do_norm, 1e-6f, B.normed, (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
+        k_prep<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, d, do_norm, 1e-6f, B.normed,
+                                                                          (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
@@ -1145,6 +1164,12 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 512, 1024 or 2048");
         }
         }
+        {
+            PiProfScope ps(ctx, st, "k_quant_h");
+            const int64_t slots = T * k + (L->has_shared ? T : 0);
+            const int64_t nblk = slots * (L->f / 32);
+            k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
+        }
         PiProfScope ps(ctx, st, "k_down");
         switch (L->f / 64) {
             case 2: k_down_q8<2><<<dn, 256, 0, st>>>(a); break;
@@ -1173,7 +1198,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         }
     }
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<(unsigned)T, 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0,
+    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0,
                                             (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
     return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
 }
