@@ -117,5 +117,7 @@ size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T);
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st);
+// Rewrites a down-projection family into the lane-tiled order the down kernels read.
+int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs);
 int pi_repack_mats(pi_ctx* ctx, PiMats* m, const void* raw, int qtype, int64_t n, int64_t rows, int64_t cols,
                    int src_on_host, std::vector<void*>* allocs);

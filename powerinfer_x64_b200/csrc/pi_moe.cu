@@ -727,7 +727,7 @@ __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
     for (int p = 0; p < 2; ++p) {
         const int row = rbase + 8 * p;
 #pragma unroll
-        for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)row * F + (q * CPQ + c) * 16);
+        for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)(row >> 3) * 8 * F + (c * 32 + lane) * 16);
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) sw[p][b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
     }
@@ -860,7 +860,7 @@ __global__ __launch_bounds__(256) void k_down_q4(ExpertArgs a) {
         float sw[BPQ];
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) {
-            w[b] = ld_stream(D + (size_t)row * (f / 2) + (q * BPQ + b) * 16);
+            w[b] = ld_stream(D + (size_t)(row >> 3) * 8 * (f / 2) + (b * 32 + lane) * 16);
             sw[b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
         }
 #pragma unroll 1
@@ -935,6 +935,21 @@ __global__ void k_repack_q4(const uint8_t* __restrict__ src, int64_t nblk, uint8
     *reinterpret_cast<int4*>(q + b * 16) = make_int4(wv[0], wv[1], wv[2], wv[3]);
 }
 
+// Lane-tiled layout for the down projections. The down kernels read a row
+// with 4 lanes (quarter q of row r) and 8 rows per warp; storing each group of
+// 8 rows as [chunk c][lane = 4*(r%8) + q][16 B] makes the warp's c-th load one
+// contiguous 512-byte segment. Thread per 16-byte chunk.
+__global__ void k_tile_quarter_rows(const int4* __restrict__ src, int4* __restrict__ dst, int64_t n_rows,
+                                    int nch) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n_rows * nch) return;
+    const int64_t r = i / nch;
+    const int j = (int)(i % nch), cpq = nch / 4;
+    const int q = j / cpq, c = j % cpq;
+    const int lane = (int)(r & 7) * 4 + q;
+    dst[(r >> 3) * 8 * nch + (int64_t)c * 32 + lane] = src[i];
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -946,6 +961,25 @@ static int64_t gguf_bytes(int qtype, int64_t n) {
     if (qtype == PI_QT_Q4_0) return n / 32 * 18;
     if (qtype == PI_QT_F32) return n * 4;
     return -1;
+}
+
+int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs) {
+    const int64_t row_bytes = m->q_row_bytes();
+    if (row_bytes % 64 || m->rows % 8) return pi_set_error(ctx, PI_ERR_ARG, "down tiling: bad shape");
+    const int nch = (int)(row_bytes / 16);
+    const int64_t n_rows = m->n * m->rows;
+    void* dst = nullptr;
+    if (pi_cuda_check(ctx, cudaMalloc(&dst, (size_t)(n_rows * row_bytes)), "cudaMalloc(tiled)")) return PI_ERR_OOM;
+    k_tile_quarter_rows<<<(unsigned)((n_rows * nch + 255) / 256), 256>>>((const int4*)m->q, (int4*)dst, n_rows, nch);
+    if (pi_cuda_check(ctx, cudaDeviceSynchronize(), "tile down")) {
+        cudaFree(dst);
+        return PI_ERR_CUDA;
+    }
+    for (auto& p : *allocs)
+        if (p == m->q) p = dst;
+    cudaFree(m->q);
+    m->q = dst;
+    return PI_OK;
 }
 
 int pi_repack_mats(pi_ctx* ctx, PiMats* m, const void* raw, int qtype, int64_t n, int64_t rows, int64_t cols,
