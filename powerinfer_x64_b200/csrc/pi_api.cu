@@ -227,11 +227,15 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
     if (!rc) rc = pi_repack_mats(ctx, &L->up, D->up_exps, L->qtype, L->E, L->f, L->d, D->src_on_host, &L->allocs);
     if (!rc) rc = pi_repack_mats(ctx, &L->down, D->down_exps, L->qtype, L->E, L->d, L->f, D->src_on_host, &L->allocs);
     if (!rc) rc = pi_tile_down_mats(ctx, &L->down, &L->allocs);
+    if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->gate, &L->allocs);
+    if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->up, &L->allocs);
     if (has_sh) {
         if (!rc) rc = pi_repack_mats(ctx, &L->gate_sh, D->gate_shexp, L->qtype, 1, f_sh, L->d, D->src_on_host, &L->allocs);
         if (!rc) rc = pi_repack_mats(ctx, &L->up_sh, D->up_shexp, L->qtype, 1, f_sh, L->d, D->src_on_host, &L->allocs);
         if (!rc) rc = pi_repack_mats(ctx, &L->down_sh, D->down_shexp, L->qtype, 1, L->d, f_sh, D->src_on_host, &L->allocs);
         if (!rc) rc = pi_tile_down_mats(ctx, &L->down_sh, &L->allocs);
+        if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->gate_sh, &L->allocs);
+        if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->up_sh, &L->allocs);
     }
     if (rc) {
         pi_moe_layer_destroy(L);

@@ -119,5 +119,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
                cudaStream_t st);
 // Rewrites a down-projection family into the lane-tiled order the down kernels read.
 int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs);
+// Rewrites Q8_0 gate/up rows into the lane-tiled order k_gateup_q8 reads.
+int pi_tile_gateup_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs);
 int pi_repack_mats(pi_ctx* ctx, PiMats* m, const void* raw, int qtype, int64_t n, int64_t rows, int64_t cols,
                    int src_on_host, std::vector<void*>* allocs);

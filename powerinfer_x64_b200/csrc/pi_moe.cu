@@ -623,21 +623,28 @@ __global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
     const int8_t* U = (const int8_t*)(sh ? a.us : a.u) + (mat + rA) * d;
     const __half* GD = (sh ? a.gsd : a.gd) + (mat + rA) * nb;
     const __half* UD = (sh ? a.usd : a.ud) + (mat + rA) * nb;
+    // rows are lane-tiled (pi_tile_gateup_mats): the lane's c-th 16-byte load is
+    // half (c % 2) of block lane + 32 * (c / 2), and each load is a contiguous
+    // 512-byte segment of the row for the warp.
+    constexpr int BPL = CPL / 2;  // whole blocks per lane
     int4 w[4][CPL];
-    float sw[4][CPL];
+    float sw[4][BPL];
 #pragma unroll
     for (int c = 0; c < CPL; ++c) {
-        const int ch = lane + 32 * c;
-        w[0][c] = ld_stream(G + ch * 16);
-        w[1][c] = ld_stream(U + ch * 16);
-        w[2][c] = ld_stream(G + d + ch * 16);
-        w[3][c] = ld_stream(U + d + ch * 16);
-        sw[0][c] = __half2float(GD[ch >> 1]);
-        sw[1][c] = __half2float(UD[ch >> 1]);
-        sw[2][c] = __half2float(GD[nb + (ch >> 1)]);
-        sw[3][c] = __half2float(UD[nb + (ch >> 1)]);
+        const int off = (c * 32 + lane) * 16;
+        w[0][c] = ld_stream(G + off);
+        w[1][c] = ld_stream(U + off);
+        w[2][c] = ld_stream(G + d + off);
+        w[3][c] = ld_stream(U + d + off);
     }
-    const bool even = (lane & 1) == 0;
+#pragma unroll
+    for (int bb = 0; bb < BPL; ++bb) {
+        const int b = lane + 32 * bb;
+        sw[0][bb] = __half2float(GD[b]);
+        sw[1][bb] = __half2float(UD[b]);
+        sw[2][bb] = __half2float(GD[nb + b]);
+        sw[3][bb] = __half2float(UD[nb + b]);
+    }
     const int crv = lane >> 3, ctk = lane & 7;  // this lane's chain
     for (int t0 = 0; t0 < item.z; t0 += GU_TB) {
         const int nt = min(GU_TB, item.z - t0);
@@ -647,18 +654,23 @@ __global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
             const int8_t* xr = a.xq + (size_t)tok * d;
             const float* sr = a.xs + (size_t)tok * nb;
 #pragma unroll
-            for (int c = 0; c < CPL; ++c) {
-                const int ch = lane + 32 * c;
-                const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
-                const float sx = sr[ch >> 1];
+            for (int bb = 0; bb < BPL; ++bb) {
+                const int b = lane + 32 * bb;
+                const int4 x0 = *reinterpret_cast<const int4*>(xr + b * 32);
+                const int4 x1 = *reinterpret_cast<const int4*>(xr + b * 32 + 16);
+                const float sx = sr[b];
 #pragma unroll
                 for (int r = 0; r < 4; ++r) {
-                    int s = dp4a(w[r][c].x, xv.x, 0);
-                    s = dp4a(w[r][c].y, xv.y, s);
-                    s = dp4a(w[r][c].z, xv.z, s);
-                    s = dp4a(w[r][c].w, xv.w, s);
-                    s += __shfl_xor_sync(0xffffffffu, s, 1);
-                    if (even) terms[(r * GU_TB + tk) * STRIDE + (ch >> 1)] = fmul((float)s, fmul(sw[r][c], sx));
+                    const int4 w0 = w[r][2 * bb], w1 = w[r][2 * bb + 1];
+                    int s = dp4a(w0.x, x0.x, 0);
+                    s = dp4a(w0.y, x0.y, s);
+                    s = dp4a(w0.z, x0.z, s);
+                    s = dp4a(w0.w, x0.w, s);
+                    s = dp4a(w1.x, x1.x, s);
+                    s = dp4a(w1.y, x1.y, s);
+                    s = dp4a(w1.z, x1.z, s);
+                    s = dp4a(w1.w, x1.w, s);
+                    terms[(r * GU_TB + tk) * STRIDE + b] = fmul((float)s, fmul(sw[r][bb], sx));
                 }
             }
         }
@@ -950,6 +962,17 @@ __global__ void k_tile_quarter_rows(const int4* __restrict__ src, int4* __restri
     dst[(r >> 3) * 8 * nch + (int64_t)c * 32 + lane] = src[i];
 }
 
+// Lane-tiled layout for the Q8_0 gate/up rows: within each row, 16-byte
+// chunk (c * 32 + l) holds half (c % 2) of block l + 32 * (c / 2), so lane l
+// owns whole blocks and every warp load is contiguous. Thread per chunk.
+__global__ void k_tile_block_rows(const int4* __restrict__ src, int4* __restrict__ dst, int64_t n_rows, int nch) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;  // destination chunk
+    if (i >= n_rows * nch) return;
+    const int64_t r = i / nch;
+    const int n = (int)(i % nch), c = n / 32, l = n % 32;
+    dst[i] = src[r * nch + 2 * (l + 32 * (c / 2)) + (c % 2)];
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -972,6 +995,25 @@ int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs) {
     if (pi_cuda_check(ctx, cudaMalloc(&dst, (size_t)(n_rows * row_bytes)), "cudaMalloc(tiled)")) return PI_ERR_OOM;
     k_tile_quarter_rows<<<(unsigned)((n_rows * nch + 255) / 256), 256>>>((const int4*)m->q, (int4*)dst, n_rows, nch);
     if (pi_cuda_check(ctx, cudaDeviceSynchronize(), "tile down")) {
+        cudaFree(dst);
+        return PI_ERR_CUDA;
+    }
+    for (auto& p : *allocs)
+        if (p == m->q) p = dst;
+    cudaFree(m->q);
+    m->q = dst;
+    return PI_OK;
+}
+
+int pi_tile_gateup_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs) {
+    const int64_t row_bytes = m->q_row_bytes();
+    if (row_bytes % 1024) return pi_set_error(ctx, PI_ERR_ARG, "gate/up tiling: row must be a multiple of 1024 bytes");
+    const int nch = (int)(row_bytes / 16);
+    const int64_t n_rows = m->n * m->rows;
+    void* dst = nullptr;
+    if (pi_cuda_check(ctx, cudaMalloc(&dst, (size_t)(n_rows * row_bytes)), "cudaMalloc(tiled)")) return PI_ERR_OOM;
+    k_tile_block_rows<<<(unsigned)((n_rows * nch + 255) / 256), 256>>>((const int4*)m->q, (int4*)dst, n_rows, nch);
+    if (pi_cuda_check(ctx, cudaDeviceSynchronize(), "tile gate/up")) {
         cudaFree(dst);
         return PI_ERR_CUDA;
     }
@@ -1191,11 +1233,10 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
         break;                                                                                                \
     }
-            GU_Q8(1)
             GU_Q8(2)
             GU_Q8(4)
 #undef GU_Q8
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 512, 1024 or 2048");
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 1024 or 2048");
         }
         }
         {
