@@ -227,18 +227,20 @@ __global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ x
 // ---------------------------------------------------------------------------
 // k_router_exact_list: exact (reference-order) logits for the tokens listed
 // in list[0 .. *n_list). CTA = 32 router rows x one listed token at a time;
-// the 128 threads stage 32 x 128 tiles of the rows in shared memory (next
+// the 256 threads stage 32 x 256 tiles of the rows in shared memory (next
 // tile prefetched into registers), warp 0 runs one sequential chain per row
-// (d must be a multiple of 128). grid (ceil((E+1)/32), G), block 128.
+// (d must be a multiple of 256). grid (ceil((E+1)/32), G), block 256.
 // ---------------------------------------------------------------------------
-constexpr int EX_CH = 128;
-__global__ __launch_bounds__(128) void k_router_exact_list(const float* __restrict__ xin, const float* __restrict__ W,
+constexpr int EX_CH = 256, EX_THREADS = 256;
+constexpr size_t EX_SMEM = (size_t)2 * 32 * (EX_CH + 1) * 4 + (size_t)2 * EX_CH * 4;
+__global__ __launch_bounds__(EX_THREADS) void k_router_exact_list(const float* __restrict__ xin, const float* __restrict__ W,
                                                            const float* __restrict__ bias, int d, int E,
                                                            const int32_t* __restrict__ list,
                                                            const int32_t* __restrict__ n_list,
                                                            float* __restrict__ logits) {
-    __shared__ float ws[2][32][EX_CH + 1];
-    __shared__ float xs[2][EX_CH];
+    extern __shared__ float ex_sm[];
+    float(*ws)[32][EX_CH + 1] = reinterpret_cast<float(*)[32][EX_CH + 1]>(ex_sm);
+    float(*xs)[EX_CH] = reinterpret_cast<float(*)[EX_CH]>(ex_sm + 2 * 32 * (EX_CH + 1));
     const int n = *n_list;
     const int row0 = blockIdx.x * 32;
     const int nrow = min(32, E + 1 - row0);
@@ -252,8 +254,8 @@ __global__ __launch_bounds__(128) void k_router_exact_list(const float* __restri
         auto load = [&](int tile) {
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
-                const int idx = tid + 128 * m;  // 1024 float4 = 32 rows x 32
-                const int r = idx >> 5, j = idx & 31;
+                const int idx = tid + EX_THREADS * m;  // 2048 float4 = 32 rows x 64
+                const int r = idx >> 6, j = idx & 63;
                 rw[m] = (r < nrow) ? __ldg(reinterpret_cast<const float4*>(W + (size_t)(row0 + r) * d + tile * EX_CH) + j)
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
             }
@@ -262,8 +264,8 @@ __global__ __launch_bounds__(128) void k_router_exact_list(const float* __restri
         auto store = [&](int buf) {
 #pragma unroll
             for (int m = 0; m < 8; ++m) {
-                const int idx = tid + 128 * m;
-                const int r = idx >> 5, j = idx & 31;
+                const int idx = tid + EX_THREADS * m;
+                const int r = idx >> 6, j = idx & 63;
                 ws[buf][r][4 * j] = rw[m].x;
                 ws[buf][r][4 * j + 1] = rw[m].y;
                 ws[buf][r][4 * j + 2] = rw[m].z;
@@ -420,6 +422,96 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
     }
     if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
     }
+}
+
+// ---------------------------------------------------------------------------
+// k_topk_cert: certify-or-flag routing on the fast logits, one warp per token.
+// The selection is the k largest logits (ties to the lowest index); it is
+// certified when every selected logit's interval [L - eps, L + eps] lies above
+// every other's with a margin that also excludes equal probabilities after
+// rounding -- then the reference's selection (by probability, ties to the
+// lowest index) is the same set. Certified tokens get gates from the fast
+// logits (softmax sum as a tree: the gates carry a tolerance, not bit-exact);
+// the others are appended to flag_list for the exact path.
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(TK_WARPS * 32) void k_topk_cert(const float* __restrict__ logits,
+                                                             const float* __restrict__ eps, int T, int E, int k,
+                                                             int has_shgate, int32_t* __restrict__ idx,
+                                                             float* __restrict__ gates, float* __restrict__ shscale,
+                                                             int32_t* __restrict__ counts,
+                                                             int32_t* __restrict__ flag_list,
+                                                             int32_t* __restrict__ n_flag) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * TK_WARPS + warp;
+    if (t >= T) return;
+    const float* lr = logits + (size_t)t * (E + 1);
+    const float* er = eps + (size_t)t * (E + 1);
+    float l[TK_PER_LANE], ev[TK_PER_LANE];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        const int e = lane + 32 * j;
+        l[j] = (e < E) ? lr[e] : -INFINITY;
+        ev[j] = (e < E) ? er[e] : 0.0f;
+        m = fmaxf(m, l[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float es = 0.0f;
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j)
+        if (lane + 32 * j < E) es += __expf(l[j] - m);
+    es = warp_sum(es);
+    uint32_t taken = 0;
+    int my_sel = -1;
+    float my_l = 0.0f;
+    for (int r = 0; r < k; ++r) {
+        float bl = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < TK_PER_LANE; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E && !((taken >> j) & 1u) && (l[j] > bl || (l[j] == bl && e < bi))) { bl = l[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ol > bl || (ol == bl && oi < bi)) { bl = ol; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == r) { my_sel = bi; my_l = bl; }
+    }
+    float lo = INFINITY, hi = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < TK_PER_LANE; ++j) {
+        if (lane + 32 * j >= E) continue;
+        if ((taken >> j) & 1u) lo = fminf(lo, l[j] - ev[j]);
+        else hi = fmaxf(hi, l[j] + ev[j] + 4e-6f * (1.0f + fabsf(l[j] - m)));
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (!((lo > hi + 1e-6f * fabsf(hi)) && (lo - m > -80.0f))) {
+        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
+        return;
+    }
+    // ascending order of the selected experts (model/mod.rs:1303)
+    int rank = 0;
+    for (int r = 0; r < k; ++r) {
+        const int o = __shfl_sync(0xffffffffu, my_sel, r);
+        rank += (lane < k) && (o < my_sel);
+    }
+    const float p = (lane < k) ? __expf(my_l - m) / es : 0.0f;
+    const float ssum = warp_sum(p);
+    if (lane < k) {
+        idx[(size_t)t * k + rank] = my_sel;
+        gates[(size_t)t * k + rank] = ssum > 0.0f ? p / ssum : p;
+        atomicAdd(&counts[my_sel], 1);
+    }
+    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
 }
 
 // ---------------------------------------------------------------------------
@@ -1168,16 +1260,22 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             default: return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be 512, 1024, 2048 or 4096");
         }
     }
-    const unsigned tk_blocks = (unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 4 * ctx->sm_count);
     {
         PiProfScope ps(ctx, st, "k_topk");
-        k_topk<<<tk_blocks, TK_WARPS * 32, 0, st>>>(B.logits, B.eps, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx,
-                                                   gates, B.shscale, counts, B.flag_list, B.n_flag, nullptr, nullptr);
+        k_topk_cert<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(
+            B.logits, B.eps, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list,
+            B.n_flag);
     }
     {
         PiProfScope ps(ctx, st, "k_router_exact");
         dim3 eg((unsigned)((E + 1 + 31) / 32), (unsigned)std::min<int64_t>(T, 64));
-        k_router_exact_list<<<eg, 128, 0, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag, B.logits);
+        static bool ex_attr = false;
+        if (!ex_attr) {
+            cudaFuncSetAttribute(k_router_exact_list, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)EX_SMEM);
+            ex_attr = true;
+        }
+        k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
+                                                             B.logits);
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
             B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
             nullptr, B.flag_list, B.n_flag);
