@@ -284,7 +284,7 @@ __global__ __launch_bounds__(EX_THREADS) void k_router_exact_list(const float* _
             if (tid < nrow) {
                 const float* wrow = ws[buf][tid];
                 const float* xv = xs[buf];
-#pragma unroll 8
+#pragma unroll 32
                 for (int i = 0; i < EX_CH; ++i) acc = fadd(acc, fmul(wrow[i], xv[i]));
             }
             if (tile + 1 < ntiles) store(buf ^ 1);
