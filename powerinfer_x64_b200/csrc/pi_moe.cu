@@ -807,11 +807,13 @@ __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __
     if (lane == 0) hs[b] = sc;
 }
 
-// Q8_0 down: CTA = 128 output rows (8 warps x 16 rows), 4 lanes per row,
-// CPQ = f/64 chunks per lane; rows r and r+8 per warp pass; the quantised h
+// Q8_0 down: CTA = DN_ROWS output rows (8 warps x 8*DN_NP rows), 4 lanes per
+// row, CPQ = f/64 chunks per lane, 8 rows per warp pass; the quantised h
 // of each slot comes from k_quant_h.
+constexpr int DN_NP = 2;             // passes of 8 rows per warp
+constexpr int DN_ROWS = 64 * DN_NP;   // rows per CTA
 template <int CPQ>
-__global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
+__global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
     constexpr int F = CPQ * 64;  // expert width
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
@@ -820,25 +822,36 @@ __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
     const int d = a.d, fb = F / 32;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = lane & 3;
-    const int rbase = blockIdx.x * 128 + warp * 16 + (lane >> 2);
+    const int rbase = blockIdx.x * DN_ROWS + warp * 8 * DN_NP + (lane >> 2);
     const size_t mat = sh ? 0 : (size_t)item.x * d;
     const int8_t* D = (const int8_t*)(sh ? a.dns : a.dn) + mat * F;
     const __half* DD = (sh ? a.dsd : a.dd) + mat * fb;
     constexpr int BPQ = CPQ / 2;  // blocks per lane
-    int4 w[2][CPQ];
-    float sw[2][BPQ];
+    int4 w[DN_NP][CPQ];
+    float sw[DN_NP][BPQ];
 #pragma unroll
-    for (int p = 0; p < 2; ++p) {
+    for (int p = 0; p < DN_NP; ++p) {
         const int row = rbase + 8 * p;
 #pragma unroll
         for (int c = 0; c < CPQ; ++c) w[p][c] = ld_stream(D + (size_t)(row >> 3) * 8 * F + (c * 32 + lane) * 16);
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) sw[p][b] = __half2float(DD[(size_t)row * fb + q * BPQ + b]);
     }
+    // stage the item's quantised hidden vectors (the loads overlap the weight loads above)
+    __shared__ __align__(16) int8_t s_hq[TG][F];
+    __shared__ float s_hs[TG][F / 32];
+    for (int m = threadIdx.x; m < item.z * (F / 16); m += blockDim.x) {
+        const int tk = m / (F / 16), c = m % (F / 16);
+        *reinterpret_cast<int4*>(&s_hq[tk][16 * c]) =
+            *reinterpret_cast<const int4*>(a.hq + (size_t)(item.y + tk) * F + 16 * c);
+    }
+    for (int m = threadIdx.x; m < item.z * fb; m += blockDim.x)
+        s_hs[m / fb][m % fb] = a.hs[(size_t)(item.y + m / fb) * fb + m % fb];
+    __syncthreads();
     for (int tk = 0; tk < item.z; ++tk) {
         const int slot = item.y + tk;
-        const int8_t* hr = a.hq + (size_t)slot * F + q * CPQ * 16;
-        const float* hsr = a.hs + (size_t)slot * fb + q * BPQ;
+        const int8_t* hr = &s_hq[tk][q * CPQ * 16];
+        const float* hsr = &s_hs[tk][q * BPQ];
         int4 hv[CPQ];
         float hsv[BPQ];
 #pragma unroll
@@ -846,7 +859,7 @@ __global__ __launch_bounds__(256) void k_down_q8(ExpertArgs a) {
 #pragma unroll
         for (int b = 0; b < BPQ; ++b) hsv[b] = hsr[b];
 #pragma unroll
-        for (int p = 0; p < 2; ++p) {
+        for (int p = 0; p < DN_NP; ++p) {
             float acc = 0.f;
 #pragma unroll
             for (int b = 0; b < BPQ; ++b) {
@@ -1315,7 +1328,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.hf = B.hf;
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
-    const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / 128), ni);
+    const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / (q8 ? DN_ROWS : 128)), ni);
     if (q8) {
         {
         PiProfScope ps(ctx, st, "k_gateup");
