@@ -168,7 +168,7 @@ def reference_arm(args):
         torch.cuda.set_device(local)
     cfg = synth.C2
     tensors = cpu_layer_tensors(cfg)
-    sample = 8  # tokens per step: the reference handles tokens one by one, so this is a bounded sample
+    sample = args.tokens  # one step = the same 64-token batch the GPU arm processes
     x = synth.normal_host(synth.stream_seed(0, "x"), sample * cfg.d, 1.0).reshape(sample, cfg.d)
     run_cpu(cfg, tensors, x, args.warmup)
     times = run_cpu(cfg, tensors, x, args.steps)
@@ -180,7 +180,7 @@ def reference_arm(args):
         "config": {"workload": f"{cfg.name} (BASELINE config 2) T={args.tokens}; step = {sample}-token sample",
                    "tokens_per_step": sample},
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 3, "kind": "port",
-                         "sample": f"{sample} tokens of one C2 layer per step",
+                         "sample": f"{sample} tokens of one C2 layer per step (the whole step of the workload)",
                          "host_threads_available": os.cpu_count(),
                          "note": "C++ restatement of the reference CPU path (oracle/); reference threading: "
                                  "2 expert threads + shared expert on the caller"},
@@ -319,13 +319,13 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         tensors = cpu_layer_tensors(cfg, seed=0, layer=0)
-        sample = 16
+        sample = T
         xsmp = xs[0][:sample].cpu().numpy()
         run_cpu(cfg, tensors, xsmp, 1)
-        times = run_cpu(cfg, tensors, xsmp, 5)
+        times = run_cpu(cfg, tensors, xsmp, 10)
         med = statistics.median(times)
         cpu = {"value": sample / med, "unit": UNIT, "cores": 3, "kind": "port",
-               "sample": f"{sample} tokens of one C2 layer, median of 5 runs after 1 warm-up",
+               "sample": f"{sample} tokens of one C2 layer (one full step), median of 10 runs after 1 warm-up",
                "host_threads_available": os.cpu_count()}
 
     if rank == 0:
