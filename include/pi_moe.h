@@ -52,6 +52,8 @@ extern "C" {
 /* pi_moe_forward flags */
 #define PI_FWD_RMSNORM 1  /* apply RMSNorm (unit weight) before routing: model/mod.rs:1239 */
 #define PI_FWD_RESIDUAL 2 /* out = x + ffn(x): model/mod.rs:1627-1633                     */
+#define PI_FWD_FORCE_GEMV 4 /* expert products on the decode GEMV kernels                */
+#define PI_FWD_FORCE_GEMM 8 /* expert products on the tcgen05 prefill GEMM (Q4_0 only)    */
 
 typedef struct pi_ctx pi_ctx;
 typedef struct pi_moe_layer pi_moe_layer;

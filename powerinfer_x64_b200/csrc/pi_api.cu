@@ -253,7 +253,7 @@ static int moe_common(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, f
     if (T > (1 << 20)) return pi_set_error(ctx, PI_ERR_ARG, "moe: T too large");
     cudaStream_t st = (cudaStream_t)stream;
     char* scr;
-    if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T), &scr)) return rc;
+    if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T, flags), &scr)) return rc;
     return pi_moe_run(ctx, L, x, T, out, flags, idx, gates, counts, offsets, perm, scr, st);
 }
 

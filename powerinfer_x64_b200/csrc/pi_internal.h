@@ -112,8 +112,52 @@ int pi_cuda_check(pi_ctx* ctx, cudaError_t e, const char* what);
 // Returns scratch of at least `bytes` for `stream` (allocating if needed).
 int pi_scratch(pi_ctx* ctx, cudaStream_t stream, size_t bytes, char** out);
 
+// Device pointers and shapes handed to the expert kernels (decode GEMV and prefill GEMM).
+struct ExpertArgs {
+    // routed experts
+    const void* g;
+    const void* u;
+    const void* dn;
+    const __half* gd;
+    const __half* ud;
+    const __half* dd;
+    // shared expert (n = 1)
+    const void* gs;
+    const void* us;
+    const void* dns;
+    const __half* gsd;
+    const __half* usd;
+    const __half* dsd;
+    int E, d, f;  // f = routed and shared width (equal)
+    const int4* items;
+    const int32_t* n_items;
+    const int32_t* perm;
+    int n_routed;  // T*k
+    // activations
+    const int8_t* xq;  // Q8_0 path: quantised tokens [T][d]
+    const float* xs;   // Q8_0 path: scales [T][d/32]
+    const float* xf;   // Q4_0 path: f32 tokens [T][d]
+    // hidden
+    int8_t* hq;  // Q8_0: [slots][f]
+    float* hs;   // Q8_0: [slots][f/32]
+    float* hf;   // Q4_0: [slots][f]
+    float* y;    // [slots][d]
+};
+
+
+// Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): gate/up
+// GEMM + SwiGLU, then down GEMM into a.y, over work items of <= 128 slots.
+// xh/xl: expert-sorted activations split into f16 hi/lo [slots][d]; hh/hl: the
+// same for h [slots][f]. Returns a PI_* status.
+int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
+                       const __half* xl, __half* hh, __half* hl, cudaStream_t st);
+// Writes xh/xl[slot] = f16 hi/lo split of x[token(slot)] for all slots.
+int pi_prefill_permute(pi_ctx* ctx, const float* x, const int32_t* perm, int64_t n_routed, int64_t n_slots, int d,
+                       __half* xh, __half* xl, cudaStream_t st);
+constexpr int PI_GEMM_NT = 128;  // slots per prefill work item
+
 // Layer forward pieces (pi_moe.cu)
-size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T);
+size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st);

@@ -28,6 +28,7 @@
 #include "pi_internal.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace {
 
@@ -592,7 +593,7 @@ __device__ int block_sum_int(int v, int* red) {
 __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ idx, const int32_t* __restrict__ counts,
                                                   int T, int k, int E, int has_shared, int32_t* __restrict__ offsets,
                                                   int32_t* __restrict__ perm, int32_t* __restrict__ slot_of,
-                                                  int4* __restrict__ items, int32_t* __restrict__ n_items) {
+                                                  int4* __restrict__ items, int32_t* __restrict__ n_items, int tg) {
     __shared__ int red[8];
     __shared__ int s_wsum[8];
     const int e = blockIdx.x;
@@ -600,23 +601,23 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
     for (int i = threadIdx.x; i < e; i += blockDim.x) {
         int c = counts[i];
         s_off += c;
-        s_items += (c + TG - 1) / TG;
+        s_items += (c + tg - 1) / tg;
     }
     const int off = block_sum_int(s_off, red);
     const int ibase = block_sum_int(s_items, red);
     if (e == E) {  // shared-expert items + total item count
         int n_routed_items = ibase;
-        int nsh = has_shared ? (T + TG - 1) / TG : 0;
+        int nsh = has_shared ? (T + tg - 1) / tg : 0;
         for (int q = threadIdx.x; q < nsh; q += blockDim.x)
-            items[n_routed_items + q] = make_int4(E, T * k + q * TG, min(TG, T - q * TG), 0);
+            items[n_routed_items + q] = make_int4(E, T * k + q * tg, min(tg, T - q * tg), 0);
         if (threadIdx.x == 0) *n_items = n_routed_items + nsh;
         return;
     }
     const int cnt = counts[e];
     if (threadIdx.x == 0 && offsets) offsets[e] = off;
-    const int nI = (cnt + TG - 1) / TG;
+    const int nI = (cnt + tg - 1) / tg;
     for (int q = threadIdx.x; q < nI; q += blockDim.x)
-        items[ibase + q] = make_int4(e, off + q * TG, min(TG, cnt - q * TG), 0);
+        items[ibase + q] = make_int4(e, off + q * tg, min(tg, cnt - q * tg), 0);
     if (cnt == 0) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     int base = 0;
@@ -648,37 +649,6 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
 // ---------------------------------------------------------------------------
 // Expert GEMV kernels.
 // ---------------------------------------------------------------------------
-struct ExpertArgs {
-    // routed experts
-    const void* g;
-    const void* u;
-    const void* dn;
-    const __half* gd;
-    const __half* ud;
-    const __half* dd;
-    // shared expert (n = 1)
-    const void* gs;
-    const void* us;
-    const void* dns;
-    const __half* gsd;
-    const __half* usd;
-    const __half* dsd;
-    int E, d, f;  // f = routed and shared width (equal)
-    const int4* items;
-    const int32_t* n_items;
-    const int32_t* perm;
-    int n_routed;  // T*k
-    // activations
-    const int8_t* xq;  // Q8_0 path: quantised tokens [T][d]
-    const float* xs;   // Q8_0 path: scales [T][d/32]
-    const float* xf;   // Q4_0 path: f32 tokens [T][d]
-    // hidden
-    int8_t* hq;  // Q8_0: [slots][f]
-    float* hs;   // Q8_0: [slots][f/32]
-    float* hf;   // Q4_0: [slots][f]
-    float* y;    // [slots][d]
-};
-
 PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
 
 // Q8_0 gate+up: CTA = 16 rows of one expert (8 warps x 2 rows, gate and
@@ -1197,15 +1167,30 @@ struct FwdBufs {
     float* hs;
     float* hf;
     float* y;
+    __half *xh, *xl, *hh, *hl;
     size_t bytes;
 };
+
+// Prefill-sized batches take the tensor-core GEMM path (Q4_0 weights). The
+// environment variable PI_PREFILL=0/1 forces the choice (tests, benchmarks).
+bool use_gemm(const pi_moe_layer* L, int64_t T, int flags) {
+    if (L->qtype != PI_QT_Q4_0) return false;
+    if (flags & PI_FWD_FORCE_GEMV) return false;
+    if (flags & PI_FWD_FORCE_GEMM) return true;
+    static const int force = [] {
+        const char* v = std::getenv("PI_PREFILL");
+        return v ? (v[0] == '1' ? 1 : 0) : -1;
+    }();
+    if (force >= 0) return force == 1;
+    return T >= 128;
+}
 
 int64_t max_items(const pi_moe_layer* L, int64_t T) {
     const int64_t Tk = T * L->k;
     return std::min<int64_t>(L->E, Tk) + (Tk + TG - 1) / TG + (L->has_shared ? (T + TG - 1) / TG : 0) + 1;
 }
 
-FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
+FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     PiBump b{base};
     FwdBufs f;
     const int64_t d = L->d, F = L->f, E = L->E, k = L->k;
@@ -1230,17 +1215,25 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, char* base) {
     f.hs = b.take<float>(slots * (F / 32));
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
+    if (use_gemm(L, T, flags)) {
+        f.xh = b.take<__half>(slots * d);
+        f.xl = b.take<__half>(slots * d);
+        f.hh = b.take<__half>(slots * F);
+        f.hl = b.take<__half>(slots * F);
+    } else {
+        f.xh = f.xl = f.hh = f.hl = nullptr;
+    }
     f.bytes = b.off + 256;
     return f;
 }
 }  // namespace
 
-size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T) { return carve(L, T, nullptr).bytes; }
+size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags) { return carve(L, T, flags, nullptr).bytes; }
 
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st) {
-    FwdBufs B = carve(L, T, scratch);
+    FwdBufs B = carve(L, T, flags, scratch);
     const int d = (int)L->d, E = L->E, k = L->k;
     const bool q8 = L->qtype == PI_QT_Q8_0;
     const bool route_only = (out == nullptr);
@@ -1293,10 +1286,12 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
             nullptr, B.flag_list, B.n_flag);
     }
+    const bool gemm = !route_only && use_gemm(L, T, flags);
+    const int tg = gemm ? PI_GEMM_NT : TG;
     {
         PiProfScope ps(ctx, st, "k_dispatch");
         k_dispatch<<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
-                                                      perm, B.slot_of, B.items, B.n_items);
+                                                      perm, B.slot_of, B.items, B.n_items, tg);
     }
     if (route_only) return pi_cuda_check(ctx, cudaGetLastError(), "route") ? PI_ERR_CUDA : PI_OK;
 
@@ -1328,6 +1323,19 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.hf = B.hf;
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
+    if (gemm) {
+        const int64_t slots = T * k + (L->has_shared ? T : 0);
+        {
+            PiProfScope ps(ctx, st, "k_permute");
+            if (int rc = pi_prefill_permute(ctx, xin, perm, T * k, slots, d, B.xh, B.xl, st)) return rc;
+        }
+        if (int rc = pi_prefill_experts(ctx, a, L->qtype, ni, B.xh, B.xl, B.hh, B.hl, st)) return rc;
+        PiProfScope ps(ctx, st, "k_combine");
+        k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
+            x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,
+            out);
+        return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
+    }
     const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / (q8 ? DN_ROWS : 128)), ni);
     if (q8) {
         {

@@ -1,0 +1,372 @@
+// Prefill-sized expert products (Q4_0, T = 512..4096) on the
+// 5th-generation tensor cores: tcgen05.mma kind::f16 with f32 accumulators in
+// tensor memory (TMEM).
+//
+// The reference computes Q4_0 expert products as f32 dots of f32 activations
+// with dequantised weights (quant/mod.rs:958-969). One f16 pass (weights,
+// activations and h rounded to f16) gives ~5e-4 relative L2 but exceeds the
+// 2e-3 max-abs bar, and a Q4_0 block's scale is a per-row f16 that cannot be
+// factored out of the K sum. So every operand is split into f16 hi + lo parts
+// (v = hi + lo, lo = f16(v - hi)) and each k-step issues three MMAs,
+//     D += W_hi X_hi + W_lo X_hi + W_hi X_lo,
+// which keeps the products within ~2^-21 relative of the f32 result.
+//
+// Work item: (expert e, tile of 128 weight rows, <= 128 slots of e). The CTA
+// (128 threads) walks K in 64-element chunks with two shared-memory stages:
+//   * every thread dequantises one weight row of the chunk (Q4_0 nibbles,
+//     reference order, times the f16 block scale) into hi/lo f16 tiles and
+//     copies one slot row of the activations, both in the canonical K-major
+//     128-byte-swizzled layout the UMMA descriptors describe;
+//   * thread 0 issues the MMAs and a tcgen05.commit onto the stage's mbarrier,
+//     which tells the loaders when the stage may be overwritten.
+// The epilogue reads the accumulators with tcgen05.ld (warp w owns TMEM lanes
+// 32w..32w+31, one weight row per thread) and writes SwiGLU h (gate/up) or y
+// (down). All mbarrier waits are bounded (1 s) and report PI_DEVERR_TIMEOUT.
+#include "pi_common.cuh"
+#include "pi_internal.h"
+
+namespace {
+
+constexpr int NT = PI_GEMM_NT;  // slots per item (MMA N)
+constexpr int MT = 128;         // weight rows per item (MMA M)
+constexpr int KC = 64;          // K elements per chunk (one 128-byte swizzle atom)
+constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 128 bytes
+
+PI_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+PI_DEV uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+PI_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// true once the phase with this parity completed; false after ~1 s
+PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+        uint32_t done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (done) return true;
+        if ((i & 255) == 0) {
+            const uint64_t now = globaltimer_ns();
+            if (i == 0) t0 = now;
+            else if (now - t0 > 1000000000ull) return false;
+        }
+    }
+}
+
+// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
+// 1024 bytes (SBO = 1024), version 1 (sm_100).
+PI_DEV uint64_t umma_desc(const void* tile, uint32_t byte_offset) {
+    const uint32_t a = smem_u32(tile) + byte_offset;
+    uint64_t d = (uint64_t)((a >> 4) & 0x3FFF);
+    d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(1024 >> 4) << 32;  // SBO
+    d |= (uint64_t)1 << 46;            // version
+    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+    return d;
+}
+// instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = NT
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(MT >> 4) << 24);
+
+PI_DEV void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
+        : "memory");
+}
+PI_DEV void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+PI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+PI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+PI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// 32 consecutive f32 accumulator columns of this thread's TMEM lane
+PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// swizzled position of 16-byte chunk c (0..7) of row r in a K-major SW128 tile
+PI_DEV int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+
+PI_DEV uint32_t pack_h2(float a, float b) {
+    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
+}
+
+// one row x 64 K of Q4_0 weights -> hi/lo f16 tiles. nib: 32 bytes (blocks 2c, 2c+1
+// of the row), s0/s1 their scales. Reference value (nibble - 8) * d in f32.
+PI_DEV void dequant_row_q4(const int4 nib0, const int4 nib1, float s0, float s1, uint8_t* th, uint8_t* tl, int r) {
+    const uint32_t w[8] = {(uint32_t)nib0.x, (uint32_t)nib0.y, (uint32_t)nib0.z, (uint32_t)nib0.w,
+                           (uint32_t)nib1.x, (uint32_t)nib1.y, (uint32_t)nib1.z, (uint32_t)nib1.w};
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {  // chunk c = elements 8c .. 8c+7 = bytes 4c .. 4c+3
+        const uint32_t v = w[c];
+        const float sc = c < 4 ? s0 : s1;
+        float f[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = __fmul_rn((float)((int)((v >> (4 * j)) & 15u) - 8), sc);
+        uint4 hi, lo;
+        float h[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) h[j] = __half2float(__float2half_rn(f[j]));
+        hi = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
+        lo = make_uint4(pack_h2(f[0] - h[0], f[1] - h[1]), pack_h2(f[2] - h[2], f[3] - h[3]),
+                        pack_h2(f[4] - h[4], f[5] - h[5]), pack_h2(f[6] - h[6], f[7] - h[7]));
+        *reinterpret_cast<uint4*>(th + swz(r, c)) = hi;
+        *reinterpret_cast<uint4*>(tl + swz(r, c)) = lo;
+    }
+}
+
+// Q4_0 weight row r of a plain SoA matrix (nibbles [rows][K/2], scales [rows][K/32])
+struct Q4Plain {
+    const uint8_t* q;
+    const __half* d;
+    int K;
+    PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
+        const uint8_t* p = q + (size_t)r * (K / 2) + c * 32;
+        n0 = *reinterpret_cast<const int4*>(p);
+        n1 = *reinterpret_cast<const int4*>(p + 16);
+        s0 = __half2float(d[(size_t)r * (K / 32) + 2 * c]);
+        s1 = __half2float(d[(size_t)r * (K / 32) + 2 * c + 1]);
+    }
+};
+// Q4_0 down projection in the decode kernels' lane-tiled order (pi_tile_down_mats):
+// 16-byte chunk j of row r lives at (r/8)*8*nch + ((j % cpq)*32 + 4*(r%8) + j/cpq)*16.
+struct Q4Tiled {
+    const uint8_t* q;
+    const __half* d;
+    int K;
+    PI_DEV const uint8_t* chunk(int r, int j) const {
+        const int nch = K / 32, cpq = nch / 4;
+        return q + ((size_t)(r >> 3) * 8 * nch + (size_t)(j % cpq) * 32 + (r & 7) * 4 + j / cpq) * 16;
+    }
+    PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
+        n0 = *reinterpret_cast<const int4*>(chunk(r, 2 * c));
+        n1 = *reinterpret_cast<const int4*>(chunk(r, 2 * c + 1));
+        s0 = __half2float(d[(size_t)r * (K / 32) + 2 * c]);
+        s1 = __half2float(d[(size_t)r * (K / 32) + 2 * c + 1]);
+    }
+};
+
+// one activation row x 64 K (hi and lo, f16) -> swizzled tiles (zeros past n)
+PI_DEV void copy_act_row(const __half* xh, const __half* xl, int ld, int slot, bool valid, int c, uint8_t* th,
+                         uint8_t* tl, int r) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
+        if (valid) {
+            vh = *reinterpret_cast<const uint4*>(xh + (size_t)slot * ld + c * KC + q * 8);
+            vl = *reinterpret_cast<const uint4*>(xl + (size_t)slot * ld + c * KC + q * 8);
+        }
+        *reinterpret_cast<uint4*>(th + swz(r, q)) = vh;
+        *reinterpret_cast<uint4*>(tl + swz(r, q)) = vl;
+    }
+}
+
+// MODE 0: gate/up (two accumulators, 256 TMEM columns); MODE 1: down (one).
+template <int MODE>
+__global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half* __restrict__ xh,
+                                                     const __half* __restrict__ xl, __half* __restrict__ hh,
+                                                     __half* __restrict__ hl, uint32_t* err) {
+    constexpr int NMAT = MODE == 0 ? 2 : 1;             // weight matrices per item
+    constexpr int STAGE = (2 * NMAT + 2) * TILE_BYTES;  // W hi/lo per matrix + X hi/lo
+    constexpr uint32_t TCOLS = MODE == 0 ? 256 : 128;
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
+    __shared__ __align__(8) uint64_t bar[2];
+    __shared__ uint32_t s_tmem;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int it = blockIdx.y;
+    if (it >= *a.n_items) return;
+    const int4 item = a.items[it];
+    const bool sh = item.x == a.E;
+    const int row0 = blockIdx.x * MT;
+    const int K = MODE == 0 ? a.d : a.f;
+    const int nchunks = K / KC;
+
+    if (tid == 0) {
+        mbar_init(&bar[0], 1);
+        mbar_init(&bar[1], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(TCOLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+
+    // weight sources
+    const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
+    Q4Plain wg{}, wu{};
+    Q4Tiled wd{};
+    if (MODE == 0) {
+        wg = Q4Plain{(const uint8_t*)(sh ? a.gs : a.g) + mat * (a.d / 2), (sh ? a.gsd : a.gd) + mat * (a.d / 32), a.d};
+        wu = Q4Plain{(const uint8_t*)(sh ? a.us : a.u) + mat * (a.d / 2), (sh ? a.usd : a.ud) + mat * (a.d / 32), a.d};
+    } else {
+        wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32), a.f};
+    }
+    const __half* ah = MODE == 0 ? xh : hh;
+    const __half* al = MODE == 0 ? xl : hl;
+    const int ld = K;
+    const bool valid = tid < item.z;
+    const int slot = item.y + tid;
+    bool ok = true;
+
+    for (int c = 0; c < nchunks; ++c) {
+        const int s = c & 1;
+        if (c >= 2 && !mbar_wait(&bar[s], ((c - 2) >> 1) & 1)) { ok = false; break; }
+        uint8_t* st = sm + s * STAGE;
+        // weights: thread tid dequantises weight row row0 + tid of each matrix
+        int4 n0, n1;
+        float s0, s1;
+        if (MODE == 0) {
+            wg.load(row0 + tid, c, n0, n1, s0, s1);
+            dequant_row_q4(n0, n1, s0, s1, st, st + TILE_BYTES, tid);
+            wu.load(row0 + tid, c, n0, n1, s0, s1);
+            dequant_row_q4(n0, n1, s0, s1, st + 2 * TILE_BYTES, st + 3 * TILE_BYTES, tid);
+        } else {
+            wd.load(row0 + tid, c, n0, n1, s0, s1);
+            dequant_row_q4(n0, n1, s0, s1, st, st + TILE_BYTES, tid);
+        }
+        // activations: thread tid copies slot row tid
+        uint8_t* xt = st + 2 * NMAT * TILE_BYTES;
+        copy_act_row(ah, al, ld, slot, valid, c, xt, xt + TILE_BYTES, tid);
+        fence_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) {
+                const uint8_t* wh = st + 2 * m * TILE_BYTES;
+                const uint8_t* wl = wh + TILE_BYTES;
+                const uint32_t dcol = tmem + m * NT;
+#pragma unroll
+                for (int k = 0; k < KC / 16; ++k) {
+                    const uint64_t dwh = umma_desc(wh, 32 * k), dwl = umma_desc(wl, 32 * k);
+                    const uint64_t dxh = umma_desc(xt, 32 * k), dxl = umma_desc(xt + TILE_BYTES, 32 * k);
+                    mma_f16(dcol, dwh, dxh, (c > 0 || k > 0) ? 1u : 0u);
+                    mma_f16(dcol, dwl, dxh, 1u);
+                    mma_f16(dcol, dwh, dxl, 1u);
+                }
+            }
+            mma_commit(&bar[s]);
+        }
+    }
+    // all chunks issued: wait for the last commit of each stage in use
+    if (ok) {
+        const int last = nchunks - 1;
+        if (!mbar_wait(&bar[last & 1], (last >> 1) & 1)) ok = false;
+        if (ok && nchunks >= 2 && !mbar_wait(&bar[(last - 1) & 1], ((last - 1) >> 1) & 1)) ok = false;
+    }
+    if (!ok) {
+        if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
+    } else {
+        tc_fence_after();
+        // epilogue: thread = weight row row0 + tid (TMEM lane tid), 32 slots at a time
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const int row = row0 + tid;
+        for (int cb = 0; cb < NT; cb += 32) {
+            if (cb >= item.z) break;
+            float g[32];
+            tmem_ld32(tmem + lane_base + cb, g);
+            if (MODE == 0) {
+                float u[32];
+                tmem_ld32(tmem + lane_base + NT + cb, u);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    if (cb + j < item.z) {
+                        const float h = swiglu_ref(g[j], u[j]);
+                        const __half h1 = __float2half_rn(h);
+                        const size_t o = (size_t)(item.y + cb + j) * a.f + row;
+                        hh[o] = h1;
+                        hl[o] = __float2half_rn(h - __half2float(h1));
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (cb + j < item.z) a.y[(size_t)(item.y + cb + j) * a.d + row] = g[j];
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
+}
+
+__global__ void k_permute_split(const float* __restrict__ x, const int32_t* __restrict__ perm, int64_t n_routed,
+                                int64_t n_slots, int d, __half* __restrict__ xh, __half* __restrict__ xl) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= n_slots * d) return;
+    const int64_t slot = i / d, c = i % d;
+    const int64_t tok = slot < n_routed ? perm[slot] : slot - n_routed;
+    const float v = x[tok * d + c];
+    const __half h = __float2half_rn(v);
+    xh[i] = h;
+    xl[i] = __float2half_rn(v - __half2float(h));
+}
+
+template <int MODE>
+constexpr size_t gemm_smem() {
+    return (size_t)2 * ((MODE == 0 ? 4 : 2) + 2) * TILE_BYTES + 1024;
+}
+
+}  // namespace
+
+int pi_prefill_permute(pi_ctx* ctx, const float* x, const int32_t* perm, int64_t n_routed, int64_t n_slots, int d,
+                       __half* xh, __half* xl, cudaStream_t st) {
+    const int64_t n = n_slots * d;
+    k_permute_split<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, perm, n_routed, n_slots, d, xh, xl);
+    return pi_cuda_check(ctx, cudaGetLastError(), "prefill permute") ? PI_ERR_CUDA : PI_OK;
+}
+
+int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
+                       const __half* xl, __half* hh, __half* hl, cudaStream_t st) {
+    if (qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
+    if (a.d % MT || a.f % MT || a.d % KC || a.f % KC)
+        return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: n_embd and expert width must be multiples of 128");
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<0>());
+        cudaFuncSetAttribute(k_moe_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<1>());
+        attr = true;
+    }
+    {
+        PiProfScope ps(ctx, st, "k_gemm_gateup");
+        k_moe_gemm<0><<<dim3((unsigned)(a.f / MT), (unsigned)max_items), 128, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
+                                                                                                    ctx->dev_err);
+    }
+    {
+        PiProfScope ps(ctx, st, "k_gemm_down");
+        k_moe_gemm<1><<<dim3((unsigned)(a.d / MT), (unsigned)max_items), 128, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
+                                                                                                    ctx->dev_err);
+    }
+    return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
+}

@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import quant
-from ._lib import (PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_F32, Context, PiError, PiMoeLayerDesc, PI_ERR_ARG, lib,
+from ._lib import (PI_FWD_FORCE_GEMM, PI_FWD_FORCE_GEMV, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_F32, Context, PiError, PiMoeLayerDesc, PI_ERR_ARG, lib,
                    ptr, stream_ptr)
 
 
@@ -93,8 +93,12 @@ class MoeLayer:
         return o
 
     # -- forward -----------------------------------------------------------
-    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None):
-        """MoE FFN of tokens x [T, d] (device f32) -> out [T, d]."""
+    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None, path: str = "auto"):
+        """MoE FFN of tokens x [T, d] (device f32) -> out [T, d].
+
+        path: "auto" (tensor-core GEMM for prefill-sized Q4_0 batches, else GEMV),
+        "gemv" or "gemm" to force one.
+        """
         torch = _torch()
         xd = quant._f32(x)
         T = xd.numel() // self.n_embd
@@ -103,6 +107,7 @@ class MoeLayer:
         if T == 0:
             return out
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
+        flags |= {"auto": 0, "gemv": PI_FWD_FORCE_GEMV, "gemm": PI_FWD_FORCE_GEMM}[path]
         self.ctx.check(lib().pi_moe_forward(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, stream_ptr(stream)))
         return out
 

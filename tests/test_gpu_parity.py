@@ -263,6 +263,39 @@ def test_c3_shape_q4_zipf_parity(pkg, orc, torch):
     close(L.forward(x).cpu().numpy(), _oracle_layer(orc, c, t, x))
 
 
+@pytest.fixture(scope="module")
+def c3_layer(pkg, torch):
+    from powerinfer_x64_b200 import synth
+
+    return synth.moe_layer(synth.C3, seed=0, keep_tensors=True)
+
+
+def test_c3_prefill_gemm_vs_oracle(pkg, orc, torch, c3_layer):
+    """Prefill-sized batch: the tcgen05 GEMM path against the reference restatement."""
+    from powerinfer_x64_b200 import synth
+
+    c = synth.C3
+    L, t = c3_layer
+    x = synth.tokens_dev(c.d, 160, seed=3)
+    got = L.forward(x, path="gemm").cpu().numpy()
+    close(got, _oracle_layer(orc, c, t, x))
+
+
+@pytest.mark.parametrize("T", [512, 2048])
+def test_c3_prefill_gemm_vs_gemv(pkg, torch, c3_layer, T):
+    """Same inputs through both expert paths (Zipf-skewed routing: experts with
+    more than 128 tokens span several GEMM work items)."""
+    from powerinfer_x64_b200 import synth
+
+    L, _ = c3_layer
+    x = synth.tokens_dev(synth.C3.d, T, seed=4)
+    a = L.forward(x, path="gemm").cpu().numpy()
+    b = L.forward(x, path="gemv").cpu().numpy()
+    close(a, b)
+    r = L.route(x)
+    assert int(r["counts"].max()) > 128
+
+
 def test_c5_rmsnorm_residual_teacher_forced(pkg, orc, torch):
     """Two layers of the C5 stack: each GPU layer gets the oracle's previous output."""
     from powerinfer_x64_b200 import synth
