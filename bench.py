@@ -42,7 +42,9 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--tokens", type=int, default=64, help="tokens per step per GPU")
+    p.add_argument("--tokens", type=int, default=None, help="tokens per step per GPU (c2: 64, c3: 4096)")
+    p.add_argument("--config", default="c2", choices=["c2", "c3"],
+                   help="c2: decode Q8_0 (headline); c3: prefill Q4_0 with Zipf-skewed routing")
     p.add_argument("--layers", type=int, default=8, help="distinct layers cycled through")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -56,10 +58,14 @@ def q8_bytes(n):
     return n // 32 * 34
 
 
+def q_bytes(cfg, n):
+    return n // 32 * (34 if cfg.qtype == 8 else 18)
+
+
 def layer_bytes(cfg, U, T):
     """Algorithmic HBM bytes of one C2 layer pass: every routed expert's and the
     shared expert's weights once, the router and shared-gate vector, tokens in/out."""
-    per_mat = q8_bytes(cfg.d * cfg.f)
+    per_mat = q_bytes(cfg, cfg.d * cfg.f)
     gu = (U + (1 if cfg.shared else 0)) * 2 * per_mat
     dn = (U + (1 if cfg.shared else 0)) * per_mat
     router = cfg.E * cfg.d * 4 + (cfg.d * 4 if cfg.shared else 0)
@@ -168,7 +174,7 @@ def reference_arm(args):
         torch.cuda.set_device(local)
     cfg = synth.C2
     tensors = cpu_layer_tensors(cfg)
-    sample = args.tokens  # one step = the same 64-token batch the GPU arm processes
+    sample = args.tokens or 64  # one step = the same 64-token batch the GPU arm processes
     x = synth.normal_host(synth.stream_seed(0, "x"), sample * cfg.d, 1.0).reshape(sample, cfg.d)
     run_cpu(cfg, tensors, x, args.warmup)
     times = run_cpu(cfg, tensors, x, args.steps)
@@ -177,7 +183,7 @@ def reference_arm(args):
         "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} (BASELINE config 2) T={args.tokens}; step = {sample}-token sample",
+        "config": {"workload": f"{cfg.name} (BASELINE config 2) T={sample}; step = {sample} tokens",
                    "tokens_per_step": sample},
         "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 3, "kind": "port",
                          "sample": f"{sample} tokens of one C2 layer per step (the whole step of the workload)",
@@ -205,8 +211,10 @@ def main():
     rank, local, world = dist.init()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    cfg = synth.C2
-    T = args.tokens
+    cfg = {"c2": synth.C2, "c3": synth.C3}[args.config]
+    T = args.tokens or (64 if args.config == "c2" else 4096)
+    if args.config == "c3":
+        args.no_sweep = True
     ctx = Context.default(local)
 
     # layers + fixed per-layer tokens (each rank its own seed stream)
@@ -260,7 +268,7 @@ def main():
     b_gu = sum(layer_bytes(cfg, U, T)["gateup"] for U in Us)
     b_tot = sum(layer_bytes(cfg, U, T)["total"] for U in Us)
     gu_ms, gu_n = kern.get("k_gateup", (float("nan"), 0))
-    achieved = b_gu / (gu_ms / 1e3) / 1e9
+    achieved = b_gu / (gu_ms / 1e3) / 1e9 if gu_n else float("nan")
     traffic = None
     tf = ROOT / "profiles" / "ncu_traffic.json"
     if tf.exists():
@@ -269,6 +277,22 @@ def main():
         except Exception:
             traffic = None
     launches = sum(n for (_, n) in kern.values())
+    roofline = {"bound": "hbm", "kernel": "k_gateup", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
+                "algorithmic_bytes_per_launch": b_gu / args.steps,
+                "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1)}
+    if args.config == "c3":
+        # prefill: the gate/up GEMM is a dense contraction; FLOPs counted once
+        # (the kernel issues 3 f16 MMAs per product for f32-level accuracy)
+        tpeak = peaks.get("bf16_tflops", 1590.0)
+        slots = T * cfg.k + T
+        g_ms, g_n = kern.get("k_gemm_gateup", (float("nan"), 0))
+        flops = 2.0 * slots * 2 * cfg.f * cfg.d
+        ach_t = flops / (g_ms / max(g_n, 1) / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "k_gemm_gateup", "achieved": ach_t, "peak": tpeak, "unit": "TFLOP/s",
+                    "frac": ach_t / tpeak, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
+                    "traffic": None, "algorithmic_flops_per_launch": flops,
+                    "mma_issued_tflops": 3 * ach_t, "avg_launch_us": 1e3 * g_ms / max(g_n, 1)}
 
     # ---- end to end: host tokens in (pinned), host output back, per step ----
     xh = [x.cpu().pin_memory() for x in xs]
@@ -317,7 +341,7 @@ def main():
 
     # ---- CPU baseline (rank 0, N=1): the oracle, reference threading ----
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c2":
         tensors = cpu_layer_tensors(cfg, seed=0, layer=0)
         sample = T
         xsmp = xs[0][:sample].cpu().numpy()
@@ -332,15 +356,14 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8", "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> Q8_0)",
-            "config": {"workload": f"{cfg.name} (BASELINE config 2): d=2048 E=256 k=8 f=512 +shared, Q8_0",
+            "vs_baseline": None, "dtype": "int8" if args.config == "c2" else "f16x3->f32",
+            "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> " + ("Q8_0)" if args.config == "c2" else "Q4_0)"),
+            "config": {"workload": f"{cfg.name} (BASELINE config {'2' if args.config == 'c2' else '3'}): d=2048 "
+                                   f"E=256 k=8 f=512 +shared, {'Q8_0 decode' if args.config == 'c2' else 'Q4_0 prefill, Zipf router bias'}",
                        "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": f"dp{world} (replicas)",
                        "layers_cycled": args.layers, "l2": "inputs larger than L2: steps cycle through "
                        f"{args.layers} layers x {layer_bytes(cfg, 256, T)['total'] / 1e9:.2f} GB"},
-            "roofline": {"bound": "hbm", "kernel": "k_gateup", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
-                         "algorithmic_bytes_per_launch": b_gu / args.steps,
-                         "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1)},
+            "roofline": roofline,
             "layer_roofline": {"achieved_gbs": b_tot / (ms_max / 1e3) / 1e9,
                                "frac": b_tot / (ms_max / 1e3) / 1e9 / peak},
             "kernels_ms_per_step": {k: v[0] / max(v[1], 1) for k, v in kern.items()},

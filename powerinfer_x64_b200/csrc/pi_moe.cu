@@ -226,6 +226,67 @@ __global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ x
 }
 
 // ---------------------------------------------------------------------------
+// k_router_tiled: exact logits for prefill-sized batches. A register-tiled
+// SIMT product whose accumulators walk i in ascending order, one mul then
+// one add per step (no FMA): each logit is the reference's sequential f32 sum
+// (quant/mod.rs:921-935) bit for bit, and with T x (E+1) independent chains
+// the throughput, not the chain latency, sets the time.
+// CTA = 64 tokens x 64 rows (256 threads, 4 x 4 accumulators each), i staged
+// through shared memory 32 at a time.
+// ---------------------------------------------------------------------------
+constexpr int RTT = 64, RTE = 64, RTK = 32;
+__global__ __launch_bounds__(256) void k_router_tiled(const float* __restrict__ xin, const float* __restrict__ W,
+                                                      const float* __restrict__ bias, int T, int d, int E,
+                                                      float* __restrict__ logits) {
+    __shared__ __align__(16) float xs[RTK][RTT + 4];  // +4: fewer bank conflicts on the transposed stores
+    __shared__ __align__(16) float ws[RTK][RTE + 4];
+    const int tid = threadIdx.x;
+    const int t0 = blockIdx.x * RTT, e0 = blockIdx.y * RTE;
+    const int ti = (tid & 15) * 4, ei = (tid >> 4) * 4;  // this thread's 4 tokens x 4 rows
+    float acc[4][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
+    for (int k0 = 0; k0 < d; k0 += RTK) {
+        __syncthreads();
+        for (int q = tid; q < RTT * RTK / 4; q += 256) {  // transpose-stage: [i][token], [i][row]
+            const int r = q / (RTK / 4), i = 4 * (q % (RTK / 4));
+            const float4 xv = (t0 + r < T) ? *reinterpret_cast<const float4*>(xin + (size_t)(t0 + r) * d + k0 + i)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+            const float4 wv = (e0 + r <= E) ? *reinterpret_cast<const float4*>(W + (size_t)(e0 + r) * d + k0 + i)
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            xs[i][r] = xv.x; xs[i + 1][r] = xv.y; xs[i + 2][r] = xv.z; xs[i + 3][r] = xv.w;
+            ws[i][r] = wv.x; ws[i + 1][r] = wv.y; ws[i + 2][r] = wv.z; ws[i + 3][r] = wv.w;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int i = 0; i < RTK; ++i) {
+            const float4 xv = *reinterpret_cast<const float4*>(&xs[i][ti]);
+            const float4 wv = *reinterpret_cast<const float4*>(&ws[i][ei]);
+            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int a = 0; a < 4; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fadd(acc[a][b], fmul(wa[b], xa[a]));
+        }
+    }
+#pragma unroll
+    for (int a = 0; a < 4; ++a) {
+        const int t = t0 + ti + a;
+        if (t >= T) continue;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+            const int e = e0 + ei + b;
+            if (e > E) continue;
+            float v = acc[a][b];
+            if (bias && e < E) v = fadd(v, bias[e]);
+            logits[(size_t)t * (E + 1) + e] = v;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // k_router_exact_list: exact (reference-order) logits for the tokens listed
 // in list[0 .. *n_list). CTA = 32 router rows x one listed token at a time;
 // the 256 threads stage 32 x 256 tiles of the rows in shared memory (next
@@ -1216,8 +1277,7 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     if (use_gemm(L, T, flags)) {
-        f.xh = b.take<__half>(slots * d);
-        f.xl = b.take<__half>(slots * d);
+        f.xh = f.xl = nullptr;
         f.hh = b.take<__half>(slots * F);
         f.hl = b.take<__half>(slots * F);
     } else {
@@ -1253,6 +1313,18 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
     if (pi_cuda_check(ctx, cudaMemsetAsync(B.n_flag, 0, sizeof(int32_t), st), "memset flags")) return PI_ERR_CUDA;
+    if (T >= 256) {
+        // prefill-sized batch: exact logits for every token, exact selection
+        {
+            PiProfScope ps(ctx, st, "k_router_tiled");
+            dim3 rg((unsigned)((T + RTT - 1) / RTT), (unsigned)((E + 1 + RTE - 1) / RTE));
+            k_router_tiled<<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, B.logits);
+        }
+        PiProfScope ps(ctx, st, "k_topk");
+        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
+                 st>>>(B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts,
+                       nullptr, nullptr, nullptr, nullptr);
+    } else {
     {
         PiProfScope ps(ctx, st, "k_router_fast");
         const int64_t ctas_x = (E + 1 + 7) / 8;
@@ -1285,6 +1357,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
             B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
             nullptr, B.flag_list, B.n_flag);
+    }
     }
     const bool gemm = !route_only && use_gemm(L, T, flags);
     const int tg = gemm ? PI_GEMM_NT : TG;
@@ -1324,11 +1397,6 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
     if (gemm) {
-        const int64_t slots = T * k + (L->has_shared ? T : 0);
-        {
-            PiProfScope ps(ctx, st, "k_permute");
-            if (int rc = pi_prefill_permute(ctx, xin, perm, T * k, slots, d, B.xh, B.xl, st)) return rc;
-        }
         if (int rc = pi_prefill_experts(ctx, a, L->qtype, ni, B.xh, B.xl, B.hh, B.hl, st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
         k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(

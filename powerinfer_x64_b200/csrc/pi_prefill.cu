@@ -12,11 +12,12 @@
 // which keeps the products within ~2^-21 relative of the f32 result.
 //
 // Work item: (expert e, tile of 128 weight rows, <= 128 slots of e). The CTA
-// (128 threads) walks K in 64-element chunks with two shared-memory stages:
-//   * every thread dequantises one weight row of the chunk (Q4_0 nibbles,
-//     reference order, times the f16 block scale) into hi/lo f16 tiles and
-//     copies one slot row of the activations, both in the canonical K-major
-//     128-byte-swizzled layout the UMMA descriptors describe;
+// (256 threads) walks K in 64-element chunks with two shared-memory stages:
+//   * every thread dequantises half a weight row of the chunk (one Q4_0
+//     block: nibbles in reference order times the f16 block scale) into hi/lo
+//     f16 tiles and copies one slot row of the hi or lo activations, both in
+//     the canonical K-major 128-byte-swizzled layout of the UMMA descriptors,
+//     from registers loaded one chunk ahead;
 //   * thread 0 issues the MMAs and a tcgen05.commit onto the stage's mbarrier,
 //     which tells the loaders when the stage may be overwritten.
 // The epilogue reads the accumulators with tcgen05.ld (warp w owns TMEM lanes
@@ -114,27 +115,24 @@ PI_DEV uint32_t pack_h2(float a, float b) {
     return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
 }
 
-// one row x 64 K of Q4_0 weights -> hi/lo f16 tiles. nib: 32 bytes (blocks 2c, 2c+1
-// of the row), s0/s1 their scales. Reference value (nibble - 8) * d in f32.
-PI_DEV void dequant_row_q4(const int4 nib0, const int4 nib1, float s0, float s1, uint8_t* th, uint8_t* tl, int r) {
-    const uint32_t w[8] = {(uint32_t)nib0.x, (uint32_t)nib0.y, (uint32_t)nib0.z, (uint32_t)nib0.w,
-                           (uint32_t)nib1.x, (uint32_t)nib1.y, (uint32_t)nib1.z, (uint32_t)nib1.w};
+// half a row (one 32-element block, h = 0/1) x 64 K -> 4 swizzled chunks each of hi/lo
+PI_DEV void dequant_half_q4(const int4 nib, float sc, uint8_t* th, uint8_t* tl, int r, int h) {
+    const uint32_t w[4] = {(uint32_t)nib.x, (uint32_t)nib.y, (uint32_t)nib.z, (uint32_t)nib.w};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {  // chunk c = elements 8c .. 8c+7 = bytes 4c .. 4c+3
-        const uint32_t v = w[c];
-        const float sc = c < 4 ? s0 : s1;
-        float f[8];
+    for (int cc = 0; cc < 4; ++cc) {
+        const int c = 4 * h + cc;
+        const uint32_t v = w[cc];
+        float f[8], hv[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = __fmul_rn((float)((int)((v >> (4 * j)) & 15u) - 8), sc);
-        uint4 hi, lo;
-        float h[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) h[j] = __half2float(__float2half_rn(f[j]));
-        hi = make_uint4(pack_h2(h[0], h[1]), pack_h2(h[2], h[3]), pack_h2(h[4], h[5]), pack_h2(h[6], h[7]));
-        lo = make_uint4(pack_h2(f[0] - h[0], f[1] - h[1]), pack_h2(f[2] - h[2], f[3] - h[3]),
-                        pack_h2(f[4] - h[4], f[5] - h[5]), pack_h2(f[6] - h[6], f[7] - h[7]));
-        *reinterpret_cast<uint4*>(th + swz(r, c)) = hi;
-        *reinterpret_cast<uint4*>(tl + swz(r, c)) = lo;
+        for (int j = 0; j < 8; ++j) {
+            f[j] = __fmul_rn((float)((int)((v >> (4 * j)) & 15u) - 8), sc);
+            hv[j] = __half2float(__float2half_rn(f[j]));
+        }
+        *reinterpret_cast<uint4*>(th + swz(r, c)) =
+            make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]), pack_h2(hv[6], hv[7]));
+        *reinterpret_cast<uint4*>(tl + swz(r, c)) =
+            make_uint4(pack_h2(f[0] - hv[0], f[1] - hv[1]), pack_h2(f[2] - hv[2], f[3] - hv[3]),
+                       pack_h2(f[4] - hv[4], f[5] - hv[5]), pack_h2(f[6] - hv[6], f[7] - hv[7]));
     }
 }
 
@@ -143,6 +141,11 @@ struct Q4Plain {
     const uint8_t* q;
     const __half* d;
     int K;
+    // block 2c + h of row r: 16 nibble bytes and its scale
+    PI_DEV void load_half(int r, int c, int h, int4& n, float& sc) const {
+        n = *reinterpret_cast<const int4*>(q + (size_t)r * (K / 2) + c * 32 + 16 * h);
+        sc = __half2float(d[(size_t)r * (K / 32) + 2 * c + h]);
+    }
     PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
         const uint8_t* p = q + (size_t)r * (K / 2) + c * 32;
         n0 = *reinterpret_cast<const int4*>(p);
@@ -160,6 +163,10 @@ struct Q4Tiled {
     PI_DEV const uint8_t* chunk(int r, int j) const {
         const int nch = K / 32, cpq = nch / 4;
         return q + ((size_t)(r >> 3) * 8 * nch + (size_t)(j % cpq) * 32 + (r & 7) * 4 + j / cpq) * 16;
+    }
+    PI_DEV void load_half(int r, int c, int h, int4& n, float& sc) const {
+        n = *reinterpret_cast<const int4*>(chunk(r, 2 * c + h));
+        sc = __half2float(d[(size_t)r * (K / 32) + 2 * c + h]);
     }
     PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
         n0 = *reinterpret_cast<const int4*>(chunk(r, 2 * c));
@@ -185,10 +192,14 @@ PI_DEV void copy_act_row(const __half* xh, const __half* xl, int ld, int slot, b
 }
 
 // MODE 0: gate/up (two accumulators, 256 TMEM columns); MODE 1: down (one).
+// 256 threads: thread t handles row t % 128, half t / 128 (weights: one of the
+// chunk's two 32-element blocks; activations: the hi or the lo array), and
+// prefetches chunk c+1 into registers while chunk c is converted and multiplied.
+constexpr int GT = 256;
 template <int MODE>
-__global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half* __restrict__ xh,
-                                                     const __half* __restrict__ xl, __half* __restrict__ hh,
-                                                     __half* __restrict__ hl, uint32_t* err) {
+__global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* __restrict__ xh,
+                                                    const __half* __restrict__ xl, __half* __restrict__ hh,
+                                                    __half* __restrict__ hl, uint32_t* err) {
     constexpr int NMAT = MODE == 0 ? 2 : 1;             // weight matrices per item
     constexpr int STAGE = (2 * NMAT + 2) * TILE_BYTES;  // W hi/lo per matrix + X hi/lo
     constexpr uint32_t TCOLS = MODE == 0 ? 256 : 128;
@@ -197,6 +208,7 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & 127, h = tid >> 7;
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -221,7 +233,6 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
     tc_fence_after();
     const uint32_t tmem = s_tmem;
 
-    // weight sources
     const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
     Q4Plain wg{}, wu{};
     Q4Tiled wd{};
@@ -231,32 +242,69 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
     } else {
         wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32), a.f};
     }
-    const __half* ah = MODE == 0 ? xh : hh;
-    const __half* al = MODE == 0 ? xl : hl;
+    // activations: MODE 0 gathers the f32 token row of slot r (thread half h takes
+    // elements 32h .. 32h+31 of each chunk and writes both hi and lo); MODE 1
+    // copies the hi (h = 0) or lo (h = 1) f16 row of h for slot r.
     const int ld = K;
-    const bool valid = tid < item.z;
-    const int slot = item.y + tid;
-    bool ok = true;
+    const bool valid = r < item.z;
+    const int slot = item.y + (valid ? r : 0);
+    const float* xrow = nullptr;
+    const __half* hrow = nullptr;
+    if (MODE == 0) {
+        const int tok = slot < a.n_routed ? a.perm[slot] : slot - a.n_routed;
+        xrow = a.xf + (size_t)tok * a.d;
+    } else {
+        hrow = (h ? hl : hh) + (size_t)slot * ld;
+    }
 
+    // registers of the next chunk
+    int4 pn[NMAT];
+    float ps[NMAT];
+    uint4 pa[8];
+    auto prefetch = [&](int c) {
+        if (MODE == 0) {
+            wg.load_half(row0 + r, c, h, pn[0], ps[0]);
+            wu.load_half(row0 + r, c, h, pn[NMAT - 1], ps[NMAT - 1]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                pa[q] = valid ? *reinterpret_cast<const uint4*>(xrow + c * KC + 32 * h + 4 * q) : make_uint4(0, 0, 0, 0);
+        } else {
+            wd.load_half(row0 + r, c, h, pn[0], ps[0]);
+#pragma unroll
+            for (int q = 0; q < 8; ++q)
+                pa[q] = valid ? *reinterpret_cast<const uint4*>(hrow + c * KC + q * 8) : make_uint4(0, 0, 0, 0);
+        }
+    };
+    prefetch(0);
+    bool ok = true;
     for (int c = 0; c < nchunks; ++c) {
         const int s = c & 1;
         if (c >= 2 && !mbar_wait(&bar[s], ((c - 2) >> 1) & 1)) { ok = false; break; }
         uint8_t* st = sm + s * STAGE;
-        // weights: thread tid dequantises weight row row0 + tid of each matrix
-        int4 n0, n1;
-        float s0, s1;
-        if (MODE == 0) {
-            wg.load(row0 + tid, c, n0, n1, s0, s1);
-            dequant_row_q4(n0, n1, s0, s1, st, st + TILE_BYTES, tid);
-            wu.load(row0 + tid, c, n0, n1, s0, s1);
-            dequant_row_q4(n0, n1, s0, s1, st + 2 * TILE_BYTES, st + 3 * TILE_BYTES, tid);
-        } else {
-            wd.load(row0 + tid, c, n0, n1, s0, s1);
-            dequant_row_q4(n0, n1, s0, s1, st, st + TILE_BYTES, tid);
-        }
-        // activations: thread tid copies slot row tid
         uint8_t* xt = st + 2 * NMAT * TILE_BYTES;
-        copy_act_row(ah, al, ld, slot, valid, c, xt, xt + TILE_BYTES, tid);
+        // write chunk c from registers
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) dequant_half_q4(pn[m], ps[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, r, h);
+        if (MODE == 0) {
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {  // chunk 4h + m = floats 8m .. 8m+7 of this half
+                float f[8], hv[8];
+                const float4 v0 = *reinterpret_cast<const float4*>(&pa[2 * m]);
+                const float4 v1 = *reinterpret_cast<const float4*>(&pa[2 * m + 1]);
+                f[0] = v0.x; f[1] = v0.y; f[2] = v0.z; f[3] = v0.w; f[4] = v1.x; f[5] = v1.y; f[6] = v1.z; f[7] = v1.w;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) hv[j] = __half2float(__float2half_rn(f[j]));
+                const int cc = 4 * h + m;
+                *reinterpret_cast<uint4*>(xt + swz(r, cc)) =
+                    make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]), pack_h2(hv[6], hv[7]));
+                *reinterpret_cast<uint4*>(xt + TILE_BYTES + swz(r, cc)) =
+                    make_uint4(pack_h2(f[0] - hv[0], f[1] - hv[1]), pack_h2(f[2] - hv[2], f[3] - hv[3]),
+                               pack_h2(f[4] - hv[4], f[5] - hv[5]), pack_h2(f[6] - hv[6], f[7] - hv[7]));
+            }
+        } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(xt + h * TILE_BYTES + swz(r, q)) = pa[q];
+        }
         fence_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -277,8 +325,8 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
             }
             mma_commit(&bar[s]);
         }
+        if (c + 1 < nchunks) prefetch(c + 1);  // overlaps the MMAs just issued
     }
-    // all chunks issued: wait for the last commit of each stage in use
     if (ok) {
         const int last = nchunks - 1;
         if (!mbar_wait(&bar[last & 1], (last >> 1) & 1)) ok = false;
@@ -288,10 +336,12 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
         if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
     } else {
         tc_fence_after();
-        // epilogue: thread = weight row row0 + tid (TMEM lane tid), 32 slots at a time
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
-        const int row = row0 + tid;
-        for (int cb = 0; cb < NT; cb += 32) {
+        // epilogue: TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take
+        // slot columns [0, 64), warps 4-7 [64, 128)
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const int row = row0 + (warp & 3) * 32 + (tid & 31);
+        const int c0 = (warp >> 2) * (NT / 2);
+        for (int cb = c0; cb < c0 + NT / 2; cb += 32) {
             if (cb >= item.z) break;
             float g[32];
             tmem_ld32(tmem + lane_base + cb, g);
@@ -301,11 +351,11 @@ __global__ __launch_bounds__(128, 1) void k_moe_gemm(ExpertArgs a, const __half*
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if (cb + j < item.z) {
-                        const float h = swiglu_ref(g[j], u[j]);
-                        const __half h1 = __float2half_rn(h);
+                        const float hvv = g[j] / (1.0f + __expf(-g[j])) * u[j];  // tolerance path
+                        const __half h1 = __float2half_rn(hvv);
                         const size_t o = (size_t)(item.y + cb + j) * a.f + row;
                         hh[o] = h1;
-                        hl[o] = __float2half_rn(h - __half2float(h1));
+                        hl[o] = __float2half_rn(hvv - __half2float(h1));
                     }
                 }
             } else {
@@ -360,12 +410,12 @@ int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
-        k_moe_gemm<0><<<dim3((unsigned)(a.f / MT), (unsigned)max_items), 128, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
+        k_moe_gemm<0><<<dim3((unsigned)(a.f / MT), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
                                                                                                     ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_down");
-        k_moe_gemm<1><<<dim3((unsigned)(a.d / MT), (unsigned)max_items), 128, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
+        k_moe_gemm<1><<<dim3((unsigned)(a.d / MT), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
                                                                                                     ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
