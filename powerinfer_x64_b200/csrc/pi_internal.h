@@ -147,13 +147,12 @@ struct ExpertArgs {
 
 // Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): gate/up
 // GEMM + SwiGLU, then down GEMM into a.y, over work items of <= 128 slots.
-// xh/xl: expert-sorted activations split into f16 hi/lo [slots][d]; hh/hl: the
-// same for h [slots][f]. Returns a PI_* status.
+// The gate/up GEMM gathers the f32 tokens itself (a.xf via a.perm); hh/hl: the
+// SwiGLU output h split into f16 hi/lo [slots][f]. Returns a PI_* status.
 int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
                        const __half* xl, __half* hh, __half* hl, cudaStream_t st);
-// Writes xh/xl[slot] = f16 hi/lo split of x[token(slot)] for all slots.
-int pi_prefill_permute(pi_ctx* ctx, const float* x, const int32_t* perm, int64_t n_routed, int64_t n_slots, int d,
-                       __half* xh, __half* xl, cudaStream_t st);
+// n_embd and expert width the prefill GEMM tiles (whole 512-row / 128-row CTA blocks)
+inline bool pi_prefill_shape_ok(int64_t d, int64_t f) { return d % 512 == 0 && f % 128 == 0; }
 constexpr int PI_GEMM_NT = 128;  // slots per prefill work item
 
 // Layer forward pieces (pi_moe.cu)

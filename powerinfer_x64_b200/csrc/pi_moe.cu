@@ -1237,7 +1237,8 @@ struct FwdBufs {
 bool use_gemm(const pi_moe_layer* L, int64_t T, int flags) {
     if (L->qtype != PI_QT_Q4_0) return false;
     if (flags & PI_FWD_FORCE_GEMV) return false;
-    if (flags & PI_FWD_FORCE_GEMM) return true;
+    if (flags & PI_FWD_FORCE_GEMM) return true;  // PI_ERR_ARG on shapes the GEMM does not tile
+    if (!pi_prefill_shape_ok(L->d, L->f)) return false;
     static const int force = [] {
         const char* v = std::getenv("PI_PREFILL");
         return v ? (v[0] == '1' ? 1 : 0) : -1;

@@ -196,6 +196,7 @@ PI_DEV void copy_act_row(const __half* xh, const __half* xl, int ld, int slot, b
 // chunk's two 32-element blocks; activations: the hi or the lo array), and
 // prefetches chunk c+1 into registers while chunk c is converted and multiplied.
 constexpr int GT = 256;
+constexpr int GU_MPC = 1, DN_MPC = 4;  // 128-row m-tiles handled by one CTA (gate/up, down)
 template <int MODE>
 __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* __restrict__ xh,
                                                     const __half* __restrict__ xl, __half* __restrict__ hh,
@@ -213,7 +214,8 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
     const bool sh = item.x == a.E;
-    const int row0 = blockIdx.x * MT;
+    constexpr int mpc = MODE == 0 ? GU_MPC : DN_MPC;  // m-tiles per CTA
+    const int row0 = blockIdx.x * mpc * MT;
     const int K = MODE == 0 ? a.d : a.f;
     const int nchunks = K / KC;
 
@@ -261,36 +263,49 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     int4 pn[NMAT];
     float ps[NMAT];
     uint4 pa[8];
-    auto prefetch = [&](int c) {
+    // global iteration g = (m-tile mi, chunk c) of this CTA's MPC m-tiles
+    auto prefetch = [&](int g) {
+        const int mi = g / nchunks, c = g % nchunks;
+        const int wr = row0 + mi * MT + r;
         if (MODE == 0) {
-            wg.load_half(row0 + r, c, h, pn[0], ps[0]);
-            wu.load_half(row0 + r, c, h, pn[NMAT - 1], ps[NMAT - 1]);
+            wg.load_half(wr, c, h, pn[0], ps[0]);
+            wu.load_half(wr, c, h, pn[NMAT - 1], ps[NMAT - 1]);
 #pragma unroll
             for (int q = 0; q < 8; ++q)
                 pa[q] = valid ? *reinterpret_cast<const uint4*>(xrow + c * KC + 32 * h + 4 * q) : make_uint4(0, 0, 0, 0);
         } else {
-            wd.load_half(row0 + r, c, h, pn[0], ps[0]);
+            wd.load_half(wr, c, h, pn[0], ps[0]);
 #pragma unroll
             for (int q = 0; q < 8; ++q)
                 pa[q] = valid ? *reinterpret_cast<const uint4*>(hrow + c * KC + q * 8) : make_uint4(0, 0, 0, 0);
         }
     };
+    const int n_iter = mpc * nchunks;
     prefetch(0);
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-        const int s = c & 1;
-        if (c >= 2 && !mbar_wait(&bar[s], ((c - 2) >> 1) & 1)) { ok = false; break; }
+    for (int g = 0; g < n_iter && ok; ++g) {
+        const int s = g & 1, mi = g / nchunks, c = g % nchunks;
+        // take iteration g out of the prefetch registers and start loading g+1
+        // before converting g, so the loads overlap the conversion and the MMAs
+        int4 cn[NMAT];
+        float cs[NMAT];
+        uint4 ca[8];
+#pragma unroll
+        for (int m = 0; m < NMAT; ++m) { cn[m] = pn[m]; cs[m] = ps[m]; }
+#pragma unroll
+        for (int q = 0; q < 8; ++q) ca[q] = pa[q];
+        if (g + 1 < n_iter) prefetch(g + 1);
+        if (g >= 2 && !mbar_wait(&bar[s], ((g - 2) >> 1) & 1)) { ok = false; break; }
         uint8_t* st = sm + s * STAGE;
         uint8_t* xt = st + 2 * NMAT * TILE_BYTES;
-        // write chunk c from registers
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) dequant_half_q4(pn[m], ps[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, r, h);
+        for (int m = 0; m < NMAT; ++m) dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, r, h);
         if (MODE == 0) {
 #pragma unroll
             for (int m = 0; m < 4; ++m) {  // chunk 4h + m = floats 8m .. 8m+7 of this half
                 float f[8], hv[8];
-                const float4 v0 = *reinterpret_cast<const float4*>(&pa[2 * m]);
-                const float4 v1 = *reinterpret_cast<const float4*>(&pa[2 * m + 1]);
+                const float4 v0 = *reinterpret_cast<const float4*>(&ca[2 * m]);
+                const float4 v1 = *reinterpret_cast<const float4*>(&ca[2 * m + 1]);
                 f[0] = v0.x; f[1] = v0.y; f[2] = v0.z; f[3] = v0.w; f[4] = v1.x; f[5] = v1.y; f[6] = v1.z; f[7] = v1.w;
 #pragma unroll
                 for (int j = 0; j < 8; ++j) hv[j] = __half2float(__float2half_rn(f[j]));
@@ -303,7 +318,7 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
             }
         } else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(xt + h * TILE_BYTES + swz(r, q)) = pa[q];
+            for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(xt + h * TILE_BYTES + swz(r, q)) = ca[q];
         }
         fence_async_smem();
         __syncthreads();
@@ -325,33 +340,27 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
             }
             mma_commit(&bar[s]);
         }
-        if (c + 1 < nchunks) prefetch(c + 1);  // overlaps the MMAs just issued
-    }
-    if (ok) {
-        const int last = nchunks - 1;
-        if (!mbar_wait(&bar[last & 1], (last >> 1) & 1)) ok = false;
-        if (ok && nchunks >= 2 && !mbar_wait(&bar[(last - 1) & 1], ((last - 1) >> 1) & 1)) ok = false;
-    }
-    if (!ok) {
-        if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
-    } else {
+        if (c + 1 < nchunks) continue;
+        // last chunk of m-tile mi: wait for its MMAs, then the epilogue. The next
+        // m-tile's first MMA (issued after the next __syncthreads) overwrites TMEM.
+        if (!mbar_wait(&bar[s], (g >> 1) & 1)) { ok = false; break; }
         tc_fence_after();
-        // epilogue: TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take
-        // slot columns [0, 64), warps 4-7 [64, 128)
+        // TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take slot
+        // columns [0, 64), warps 4-7 [64, 128)
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int row = row0 + (warp & 3) * 32 + (tid & 31);
+        const int row = row0 + mi * MT + (warp & 3) * 32 + (tid & 31);
         const int c0 = (warp >> 2) * (NT / 2);
         for (int cb = c0; cb < c0 + NT / 2; cb += 32) {
             if (cb >= item.z) break;
-            float g[32];
-            tmem_ld32(tmem + lane_base + cb, g);
+            float gv[32];
+            tmem_ld32(tmem + lane_base + cb, gv);
             if (MODE == 0) {
                 float u[32];
                 tmem_ld32(tmem + lane_base + NT + cb, u);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if (cb + j < item.z) {
-                        const float hvv = g[j] / (1.0f + __expf(-g[j])) * u[j];  // tolerance path
+                        const float hvv = gv[j] / (1.0f + __expf(-gv[j])) * u[j];  // tolerance path
                         const __half h1 = __float2half_rn(hvv);
                         const size_t o = (size_t)(item.y + cb + j) * a.f + row;
                         hh[o] = h1;
@@ -361,26 +370,16 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
             } else {
 #pragma unroll
                 for (int j = 0; j < 32; ++j)
-                    if (cb + j < item.z) a.y[(size_t)(item.y + cb + j) * a.d + row] = g[j];
+                    if (cb + j < item.z) a.y[(size_t)(item.y + cb + j) * a.d + row] = gv[j];
             }
         }
+        tc_fence_before();
     }
+    if (!ok && tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
-}
-
-__global__ void k_permute_split(const float* __restrict__ x, const int32_t* __restrict__ perm, int64_t n_routed,
-                                int64_t n_slots, int d, __half* __restrict__ xh, __half* __restrict__ xl) {
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (i >= n_slots * d) return;
-    const int64_t slot = i / d, c = i % d;
-    const int64_t tok = slot < n_routed ? perm[slot] : slot - n_routed;
-    const float v = x[tok * d + c];
-    const __half h = __float2half_rn(v);
-    xh[i] = h;
-    xl[i] = __float2half_rn(v - __half2float(h));
 }
 
 template <int MODE>
@@ -390,18 +389,12 @@ constexpr size_t gemm_smem() {
 
 }  // namespace
 
-int pi_prefill_permute(pi_ctx* ctx, const float* x, const int32_t* perm, int64_t n_routed, int64_t n_slots, int d,
-                       __half* xh, __half* xl, cudaStream_t st) {
-    const int64_t n = n_slots * d;
-    k_permute_split<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(x, perm, n_routed, n_slots, d, xh, xl);
-    return pi_cuda_check(ctx, cudaGetLastError(), "prefill permute") ? PI_ERR_CUDA : PI_OK;
-}
-
 int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
                        const __half* xl, __half* hh, __half* hl, cudaStream_t st) {
     if (qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
-    if (a.d % MT || a.f % MT || a.d % KC || a.f % KC)
-        return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: n_embd and expert width must be multiples of 128");
+    static_assert(MT * DN_MPC == 512 && MT * GU_MPC == 128, "pi_prefill_shape_ok matches the CTA blocks");
+    if (!pi_prefill_shape_ok(a.d, a.f))
+        return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: n_embd must be a multiple of 512, expert width of 128");
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<0>());
@@ -410,12 +403,12 @@ int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
-        k_moe_gemm<0><<<dim3((unsigned)(a.f / MT), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
+        k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
                                                                                                     ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_down");
-        k_moe_gemm<1><<<dim3((unsigned)(a.d / MT), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
+        k_moe_gemm<1><<<dim3((unsigned)(a.d / (MT * DN_MPC)), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
                                                                                                     ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
