@@ -115,24 +115,37 @@ PI_DEV uint32_t pack_h2(float a, float b) {
     return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
 }
 
-// half a row (one 32-element block, h = 0/1) x 64 K -> 4 swizzled chunks each of hi/lo
-PI_DEV void dequant_half_q4(const int4 nib, float sc, uint8_t* th, uint8_t* tl, int r, int h) {
+// half a row (one 32-element block, h = 0/1) x 64 K -> 4 swizzled chunks each of hi/lo.
+// Packed f16 arithmetic: 0x6400 | n is the f16 value 1024 + n, so (0x6400 | n) - 1032 = n - 8
+// exactly; hi = rn(d * (n - 8)) is one rounding of the exact product, the same value as
+// rounding the f32 product (exact: 11 x 4 bits); lo = rn(d * (n - 8) - hi) by one fused
+// multiply-add, the same value as rounding the exact f32 difference.
+PI_DEV void dequant_half_q4(const int4 nib, __half sc, uint8_t* th, uint8_t* tl, int r, int h) {
     const uint32_t w[4] = {(uint32_t)nib.x, (uint32_t)nib.y, (uint32_t)nib.z, (uint32_t)nib.w};
+    const __half2 d2 = __half2half2(sc);
+    const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6408));  // 1032
 #pragma unroll
     for (int cc = 0; cc < 4; ++cc) {
         const int c = 4 * h + cc;
         const uint32_t v = w[cc];
-        float f[8], hv[8];
+        // t_j holds nibble j (bits 0..3) and nibble j + 4 (bits 16..19): elements j, j + 4
+        uint32_t t[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            f[j] = __fmul_rn((float)((int)((v >> (4 * j)) & 15u) - 8), sc);
-            hv[j] = __half2float(__float2half_rn(f[j]));
+        for (int j = 0; j < 4; ++j) t[j] = (v >> (4 * j)) & 0x000F000Fu;
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
+            // pair p = elements (2p, 2p + 1): low halves of t[2p], t[2p+1] for p < 2, high halves after
+            const uint32_t a = t[(2 * p) & 3], b = t[(2 * p + 1) & 3];
+            const uint32_t q = (p < 2 ? __byte_perm(a, b, 0x5410) : __byte_perm(a, b, 0x7632)) | 0x64006400u;
+            const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&q), off);
+            const __half2 hv = __hmul2(d2, qv);
+            const __half2 lv = __hfma2(d2, qv, __hneg2(hv));
+            hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
+            lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
         }
-        *reinterpret_cast<uint4*>(th + swz(r, c)) =
-            make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]), pack_h2(hv[6], hv[7]));
-        *reinterpret_cast<uint4*>(tl + swz(r, c)) =
-            make_uint4(pack_h2(f[0] - hv[0], f[1] - hv[1]), pack_h2(f[2] - hv[2], f[3] - hv[3]),
-                       pack_h2(f[4] - hv[4], f[5] - hv[5]), pack_h2(f[6] - hv[6], f[7] - hv[7]));
+        *reinterpret_cast<uint4*>(th + swz(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(tl + swz(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
@@ -142,16 +155,9 @@ struct Q4Plain {
     const __half* d;
     int K;
     // block 2c + h of row r: 16 nibble bytes and its scale
-    PI_DEV void load_half(int r, int c, int h, int4& n, float& sc) const {
+    PI_DEV void load_half(int r, int c, int h, int4& n, __half& sc) const {
         n = *reinterpret_cast<const int4*>(q + (size_t)r * (K / 2) + c * 32 + 16 * h);
-        sc = __half2float(d[(size_t)r * (K / 32) + 2 * c + h]);
-    }
-    PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
-        const uint8_t* p = q + (size_t)r * (K / 2) + c * 32;
-        n0 = *reinterpret_cast<const int4*>(p);
-        n1 = *reinterpret_cast<const int4*>(p + 16);
-        s0 = __half2float(d[(size_t)r * (K / 32) + 2 * c]);
-        s1 = __half2float(d[(size_t)r * (K / 32) + 2 * c + 1]);
+        sc = d[(size_t)r * (K / 32) + 2 * c + h];
     }
 };
 // Q4_0 down projection in the decode kernels' lane-tiled order (pi_tile_down_mats):
@@ -164,15 +170,9 @@ struct Q4Tiled {
         const int nch = K / 32, cpq = nch / 4;
         return q + ((size_t)(r >> 3) * 8 * nch + (size_t)(j % cpq) * 32 + (r & 7) * 4 + j / cpq) * 16;
     }
-    PI_DEV void load_half(int r, int c, int h, int4& n, float& sc) const {
+    PI_DEV void load_half(int r, int c, int h, int4& n, __half& sc) const {
         n = *reinterpret_cast<const int4*>(chunk(r, 2 * c + h));
-        sc = __half2float(d[(size_t)r * (K / 32) + 2 * c + h]);
-    }
-    PI_DEV void load(int r, int c, int4& n0, int4& n1, float& s0, float& s1) const {
-        n0 = *reinterpret_cast<const int4*>(chunk(r, 2 * c));
-        n1 = *reinterpret_cast<const int4*>(chunk(r, 2 * c + 1));
-        s0 = __half2float(d[(size_t)r * (K / 32) + 2 * c]);
-        s1 = __half2float(d[(size_t)r * (K / 32) + 2 * c + 1]);
+        sc = d[(size_t)r * (K / 32) + 2 * c + h];
     }
 };
 
@@ -261,7 +261,7 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
 
     // registers of the next chunk
     int4 pn[NMAT];
-    float ps[NMAT];
+    __half ps[NMAT];
     uint4 pa[8];
     // global iteration g = (m-tile mi, chunk c) of this CTA's MPC m-tiles
     auto prefetch = [&](int g) {
@@ -288,7 +288,7 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
         // take iteration g out of the prefetch registers and start loading g+1
         // before converting g, so the loads overlap the conversion and the MMAs
         int4 cn[NMAT];
-        float cs[NMAT];
+        __half cs[NMAT];
         uint4 ca[8];
 #pragma unroll
         for (int m = 0; m < NMAT; ++m) { cn[m] = pn[m]; cs[m] = ps[m]; }
@@ -303,18 +303,19 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
         if (MODE == 0) {
 #pragma unroll
             for (int m = 0; m < 4; ++m) {  // chunk 4h + m = floats 8m .. 8m+7 of this half
-                float f[8], hv[8];
-                const float4 v0 = *reinterpret_cast<const float4*>(&ca[2 * m]);
-                const float4 v1 = *reinterpret_cast<const float4*>(&ca[2 * m + 1]);
-                f[0] = v0.x; f[1] = v0.y; f[2] = v0.z; f[3] = v0.w; f[4] = v1.x; f[5] = v1.y; f[6] = v1.z; f[7] = v1.w;
+                const float* f = reinterpret_cast<const float*>(&ca[2 * m]);
+                uint32_t hi[4], lo[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) hv[j] = __half2float(__float2half_rn(f[j]));
+                for (int p = 0; p < 4; ++p) {
+                    const __half2 hv = __floats2half2_rn(f[2 * p], f[2 * p + 1]);
+                    const float2 hf = __half22float2(hv);
+                    const __half2 lv = __floats2half2_rn(f[2 * p] - hf.x, f[2 * p + 1] - hf.y);
+                    hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
+                    lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
+                }
                 const int cc = 4 * h + m;
-                *reinterpret_cast<uint4*>(xt + swz(r, cc)) =
-                    make_uint4(pack_h2(hv[0], hv[1]), pack_h2(hv[2], hv[3]), pack_h2(hv[4], hv[5]), pack_h2(hv[6], hv[7]));
-                *reinterpret_cast<uint4*>(xt + TILE_BYTES + swz(r, cc)) =
-                    make_uint4(pack_h2(f[0] - hv[0], f[1] - hv[1]), pack_h2(f[2] - hv[2], f[3] - hv[3]),
-                               pack_h2(f[4] - hv[4], f[5] - hv[5]), pack_h2(f[6] - hv[6], f[7] - hv[7]));
+                *reinterpret_cast<uint4*>(xt + swz(r, cc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(xt + TILE_BYTES + swz(r, cc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
             }
         } else {
 #pragma unroll
