@@ -111,10 +111,6 @@ PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
 // swizzled position of 16-byte chunk c (0..7) of row r in a K-major SW128 tile
 PI_DEV int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
 
-PI_DEV uint32_t pack_h2(float a, float b) {
-    return (uint32_t)__half_as_ushort(__float2half_rn(a)) | ((uint32_t)__half_as_ushort(__float2half_rn(b)) << 16);
-}
-
 // half a row (one 32-element block, h = 0/1) x 64 K -> 4 swizzled chunks each of hi/lo.
 // Packed f16 arithmetic: 0x6400 | n is the f16 value 1024 + n, so (0x6400 | n) - 1032 = n - 8
 // exactly; hi = rn(d * (n - 8)) is one rounding of the exact product, the same value as
@@ -176,25 +172,10 @@ struct Q4Tiled {
     }
 };
 
-// one activation row x 64 K (hi and lo, f16) -> swizzled tiles (zeros past n)
-PI_DEV void copy_act_row(const __half* xh, const __half* xl, int ld, int slot, bool valid, int c, uint8_t* th,
-                         uint8_t* tl, int r) {
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-        uint4 vh = make_uint4(0, 0, 0, 0), vl = make_uint4(0, 0, 0, 0);
-        if (valid) {
-            vh = *reinterpret_cast<const uint4*>(xh + (size_t)slot * ld + c * KC + q * 8);
-            vl = *reinterpret_cast<const uint4*>(xl + (size_t)slot * ld + c * KC + q * 8);
-        }
-        *reinterpret_cast<uint4*>(th + swz(r, q)) = vh;
-        *reinterpret_cast<uint4*>(tl + swz(r, q)) = vl;
-    }
-}
-
 // MODE 0: gate/up (two accumulators, 256 TMEM columns); MODE 1: down (one).
-// 256 threads: thread t handles row t % 128, half t / 128 (weights: one of the
-// chunk's two 32-element blocks; activations: the hi or the lo array), and
-// prefetches chunk c+1 into registers while chunk c is converted and multiplied.
+// 256 threads convert each 64-K chunk into the stage's swizzled tiles (thread
+// to data mapping below) and prefetch chunk c+1 into registers while chunk c is
+// converted and multiplied; thread 0 issues the MMAs.
 constexpr int GT = 256;
 constexpr int GU_MPC = 1, DN_MPC = 4;  // 128-row m-tiles handled by one CTA (gate/up, down)
 template <int MODE>
@@ -209,7 +190,6 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     __shared__ __align__(8) uint64_t bar[2];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5;
-    const int r = tid & 127, h = tid >> 7;
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -244,40 +224,53 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     } else {
         wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32), a.f};
     }
-    // activations: MODE 0 gathers the f32 token row of slot r (thread half h takes
-    // elements 32h .. 32h+31 of each chunk and writes both hi and lo); MODE 1
-    // copies the hi (h = 0) or lo (h = 1) f16 row of h for slot r.
-    const int ld = K;
-    const bool valid = r < item.z;
-    const int slot = item.y + (valid ? r : 0);
-    const float* xrow = nullptr;
-    const __half* hrow = nullptr;
-    if (MODE == 0) {
-        const int tok = slot < a.n_routed ? a.perm[slot] : slot - a.n_routed;
-        xrow = a.xf + (size_t)tok * a.d;
-    } else {
-        hrow = (h ? hl : hh) + (size_t)slot * ld;
+    // Loads are mapped so that a warp reads whole sectors and few lines:
+    //   weights: thread t takes row t / 2, block (2c + t % 2) of chunk c;
+    //   MODE 0 activations: thread t takes floats 4(t % 16) .. +3 of the chunk
+    //     for the 8 slots t / 16 + 16 i, gathered from their f32 token rows;
+    //   MODE 1 activations: thread t takes 16-byte piece t % 8 of the chunk of
+    //     the hi and the lo rows of the 4 slots t / 8 + 32 i.
+    const int rw = tid >> 1, hw = tid & 1;
+    constexpr int XR = MODE == 0 ? 8 : 4;  // slots per thread
+    const int xj = MODE == 0 ? (tid & 15) : (tid & 7);
+    const int xr0 = MODE == 0 ? (tid >> 4) : (tid >> 3), xrs = MODE == 0 ? 16 : 32;
+    const float* xrow[MODE == 0 ? XR : 1];
+    const __half* hrow[MODE == 0 ? 1 : XR];
+#pragma unroll
+    for (int i = 0; i < XR; ++i) {
+        const int rr = xr0 + xrs * i;
+        const bool v = rr < item.z;
+        const int slot = item.y + (v ? rr : 0);
+        if (MODE == 0) {
+            const int tok = slot < a.n_routed ? a.perm[slot] : slot - a.n_routed;
+            xrow[i] = v ? a.xf + (size_t)tok * a.d + 4 * xj : nullptr;
+        } else {
+            hrow[i] = v ? hh + (size_t)slot * K + 8 * xj : nullptr;
+        }
     }
+    const size_t hlo = (size_t)(hl - hh);  // hl = hh + hlo
 
     // registers of the next chunk
     int4 pn[NMAT];
     __half ps[NMAT];
-    uint4 pa[8];
+    uint4 pa[8];  // MODE 0: float4 of slot i; MODE 1: [2i] hi, [2i+1] lo of slot i
     // global iteration g = (m-tile mi, chunk c) of this CTA's MPC m-tiles
     auto prefetch = [&](int g) {
         const int mi = g / nchunks, c = g % nchunks;
-        const int wr = row0 + mi * MT + r;
+        const int wr = row0 + mi * MT + rw;
         if (MODE == 0) {
-            wg.load_half(wr, c, h, pn[0], ps[0]);
-            wu.load_half(wr, c, h, pn[NMAT - 1], ps[NMAT - 1]);
+            wg.load_half(wr, c, hw, pn[0], ps[0]);
+            wu.load_half(wr, c, hw, pn[NMAT - 1], ps[NMAT - 1]);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                pa[q] = valid ? *reinterpret_cast<const uint4*>(xrow + c * KC + 32 * h + 4 * q) : make_uint4(0, 0, 0, 0);
+            for (int i = 0; i < XR; ++i)
+                pa[i] = xrow[i] ? *reinterpret_cast<const uint4*>(xrow[i] + c * KC) : make_uint4(0, 0, 0, 0);
         } else {
-            wd.load_half(wr, c, h, pn[0], ps[0]);
+            wd.load_half(wr, c, hw, pn[0], ps[0]);
 #pragma unroll
-            for (int q = 0; q < 8; ++q)
-                pa[q] = valid ? *reinterpret_cast<const uint4*>(hrow + c * KC + q * 8) : make_uint4(0, 0, 0, 0);
+            for (int i = 0; i < XR; ++i) {
+                pa[2 * i] = hrow[i] ? *reinterpret_cast<const uint4*>(hrow[i] + c * KC) : make_uint4(0, 0, 0, 0);
+                pa[2 * i + 1] = hrow[i] ? *reinterpret_cast<const uint4*>(hrow[i] + hlo + c * KC) : make_uint4(0, 0, 0, 0);
+            }
         }
     };
     const int n_iter = mpc * nchunks;
@@ -299,27 +292,28 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
         uint8_t* st = sm + s * STAGE;
         uint8_t* xt = st + 2 * NMAT * TILE_BYTES;
 #pragma unroll
-        for (int m = 0; m < NMAT; ++m) dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, r, h);
+        for (int m = 0; m < NMAT; ++m)
+            dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, rw, hw);
         if (MODE == 0) {
 #pragma unroll
-            for (int m = 0; m < 4; ++m) {  // chunk 4h + m = floats 8m .. 8m+7 of this half
-                const float* f = reinterpret_cast<const float*>(&ca[2 * m]);
-                uint32_t hi[4], lo[4];
-#pragma unroll
-                for (int p = 0; p < 4; ++p) {
-                    const __half2 hv = __floats2half2_rn(f[2 * p], f[2 * p + 1]);
-                    const float2 hf = __half22float2(hv);
-                    const __half2 lv = __floats2half2_rn(f[2 * p] - hf.x, f[2 * p + 1] - hf.y);
-                    hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
-                    lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
-                }
-                const int cc = 4 * h + m;
-                *reinterpret_cast<uint4*>(xt + swz(r, cc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<uint4*>(xt + TILE_BYTES + swz(r, cc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            for (int i = 0; i < XR; ++i) {  // floats 4xj .. 4xj+3 of slot xr0 + 16i -> 8 bytes of hi and lo
+                const float* f = reinterpret_cast<const float*>(&ca[i]);
+                const __half2 h0 = __floats2half2_rn(f[0], f[1]), h1 = __floats2half2_rn(f[2], f[3]);
+                const float2 g0 = __half22float2(h0), g1 = __half22float2(h1);
+                const __half2 l0 = __floats2half2_rn(f[0] - g0.x, f[1] - g0.y), l1 = __floats2half2_rn(f[2] - g1.x, f[3] - g1.y);
+                const int o = swz(xr0 + xrs * i, xj >> 1) + 8 * (xj & 1);
+                *reinterpret_cast<uint2*>(xt + o) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+                *reinterpret_cast<uint2*>(xt + TILE_BYTES + o) =
+                    make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
             }
         } else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) *reinterpret_cast<uint4*>(xt + h * TILE_BYTES + swz(r, q)) = ca[q];
+            for (int i = 0; i < XR; ++i) {
+                const int o = swz(xr0 + xrs * i, xj);
+                *reinterpret_cast<uint4*>(xt + o) = ca[2 * i];
+                *reinterpret_cast<uint4*>(xt + TILE_BYTES + o) = ca[2 * i + 1];
+            }
         }
         fence_async_smem();
         __syncthreads();
