@@ -145,12 +145,12 @@ struct ExpertArgs {
 };
 
 
-// Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): gate/up
-// GEMM + SwiGLU, then down GEMM into a.y, over work items of <= 128 slots.
-// The gate/up GEMM gathers the f32 tokens itself (a.xf via a.perm); hh/hl: the
-// SwiGLU output h split into f16 hi/lo [slots][f]. Returns a PI_* status.
-int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
-                       const __half* xl, __half* hh, __half* hl, cudaStream_t st);
+// Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): splits the
+// slot-ordered tokens into f16 hi/lo xh/xl [n_slots][d], then the gate/up GEMM +
+// SwiGLU writes h as f16 hi/lo hh/hl [n_slots][f] and the down GEMM writes a.y,
+// over work items of <= 128 slots. Returns a PI_* status.
+int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, int64_t n_slots, __half* xh,
+                       __half* xl, __half* hh, __half* hl, cudaStream_t st);
 // n_embd and expert width the prefill GEMM tiles (whole 512-row / 128-row CTA blocks)
 inline bool pi_prefill_shape_ok(int64_t d, int64_t f) { return d % 512 == 0 && f % 128 == 0; }
 constexpr int PI_GEMM_NT = 128;  // slots per prefill work item

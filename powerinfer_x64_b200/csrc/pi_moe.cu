@@ -1278,7 +1278,8 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     if (use_gemm(L, T, flags)) {
-        f.xh = f.xl = nullptr;
+        f.xh = b.take<__half>(slots * d);
+        f.xl = b.take<__half>(slots * d);
         f.hh = b.take<__half>(slots * F);
         f.hl = b.take<__half>(slots * F);
     } else {
@@ -1398,7 +1399,8 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
     if (gemm) {
-        if (int rc = pi_prefill_experts(ctx, a, L->qtype, ni, B.xh, B.xl, B.hh, B.hl, st)) return rc;
+        const int64_t n_slots = T * k + (L->has_shared ? T : 0);
+        if (int rc = pi_prefill_experts(ctx, a, L->qtype, ni, n_slots, B.xh, B.xl, B.hh, B.hl, st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
         k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
             x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,

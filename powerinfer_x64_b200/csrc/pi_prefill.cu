@@ -23,6 +23,9 @@
 // The epilogue reads the accumulators with tcgen05.ld (warp w owns TMEM lanes
 // 32w..32w+31, one weight row per thread) and writes SwiGLU h (gate/up) or y
 // (down). All mbarrier waits are bounded (1 s) and report PI_DEVERR_TIMEOUT.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include "pi_common.cuh"
 #include "pi_internal.h"
 
@@ -91,6 +94,20 @@ PI_DEV void mma_commit(uint64_t* bar) {
 PI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 PI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 PI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+PI_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// 2-D tiled TMA load (no multicast) of box {64 f16, 128 rows} at element (x, y)
+PI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+PI_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
 
 // 32 consecutive f32 accumulator columns of this thread's TMEM lane
 PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
@@ -173,21 +190,29 @@ struct Q4Tiled {
 };
 
 // MODE 0: gate/up (two accumulators, 256 TMEM columns); MODE 1: down (one).
-// 256 threads convert each 64-K chunk into the stage's swizzled tiles (thread
-// to data mapping below) and prefetch chunk c+1 into registers while chunk c is
-// converted and multiplied; thread 0 issues the MMAs.
-constexpr int GT = 256;
+// Warp roles:
+//   0-7  converters: dequantise each 64-K weight chunk into one of two weight
+//        stages (thread t: row t / 2, block 2c + t % 2, loaded one chunk ahead
+//        into registers), then arrive on the stage's `full` barrier; after the
+//        last chunk of an m-tile they run its epilogue;
+//   8    TMA producer: streams the activation chunks (f16 hi and lo, already in
+//        slot order) into a three-deep ring;
+//   9    MMA issuer: waits for a weight stage and its activation slot, issues
+//        the MMAs and releases both with tcgen05.commit.
+constexpr int GT = 320;
+constexpr int XS = 3;  // activation ring depth
 constexpr int GU_MPC = 1, DN_MPC = 4;  // 128-row m-tiles handled by one CTA (gate/up, down)
 template <int MODE>
-__global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* __restrict__ xh,
-                                                    const __half* __restrict__ xl, __half* __restrict__ hh,
-                                                    __half* __restrict__ hl, uint32_t* err) {
-    constexpr int NMAT = MODE == 0 ? 2 : 1;             // weight matrices per item
-    constexpr int STAGE = (2 * NMAT + 2) * TILE_BYTES;  // W hi/lo per matrix + X hi/lo
+__global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_constant__ CUtensorMap map_hi,
+                                                    const __grid_constant__ CUtensorMap map_lo,
+                                                    __half* __restrict__ hh, __half* __restrict__ hl, uint32_t* err) {
+    constexpr int NMAT = MODE == 0 ? 2 : 1;         // weight matrices per item
+    constexpr int WSTAGE = 2 * NMAT * TILE_BYTES;   // W hi/lo per matrix
     constexpr uint32_t TCOLS = MODE == 0 ? 256 : 128;
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    __shared__ __align__(8) uint64_t bar[2];
+    uint8_t* xring = sm + 2 * WSTAGE;  // XS slots of {hi, lo} tiles
+    __shared__ __align__(8) uint64_t wbar[2], full[2], xfull[XS], xempty[XS];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5;
     const int it = blockIdx.y;
@@ -198,10 +223,17 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     const int row0 = blockIdx.x * mpc * MT;
     const int K = MODE == 0 ? a.d : a.f;
     const int nchunks = K / KC;
+    const int n_iter = mpc * nchunks;
 
     if (tid == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&wbar[i], 1);
+            mbar_init(&full[i], 8);  // one arrival per converter warp
+        }
+        for (int i = 0; i < XS; ++i) {
+            mbar_init(&xfull[i], 1);
+            mbar_init(&xempty[i], 1);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 0) {
@@ -214,182 +246,204 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __half* 
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-
-    const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
-    Q4Plain wg{}, wu{};
-    Q4Tiled wd{};
-    if (MODE == 0) {
-        wg = Q4Plain{(const uint8_t*)(sh ? a.gs : a.g) + mat * (a.d / 2), (sh ? a.gsd : a.gd) + mat * (a.d / 32), a.d};
-        wu = Q4Plain{(const uint8_t*)(sh ? a.us : a.u) + mat * (a.d / 2), (sh ? a.usd : a.ud) + mat * (a.d / 32), a.d};
-    } else {
-        wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32), a.f};
-    }
-    // Loads are mapped so that a warp reads whole sectors and few lines:
-    //   weights: thread t takes row t / 2, block (2c + t % 2) of chunk c;
-    //   MODE 0 activations: thread t takes floats 4(t % 16) .. +3 of the chunk
-    //     for the 8 slots t / 16 + 16 i, gathered from their f32 token rows;
-    //   MODE 1 activations: thread t takes 16-byte piece t % 8 of the chunk of
-    //     the hi and the lo rows of the 4 slots t / 8 + 32 i.
-    const int rw = tid >> 1, hw = tid & 1;
-    constexpr int XR = MODE == 0 ? 8 : 4;  // slots per thread
-    const int xj = MODE == 0 ? (tid & 15) : (tid & 7);
-    const int xr0 = MODE == 0 ? (tid >> 4) : (tid >> 3), xrs = MODE == 0 ? 16 : 32;
-    const float* xrow[MODE == 0 ? XR : 1];
-    const __half* hrow[MODE == 0 ? 1 : XR];
-#pragma unroll
-    for (int i = 0; i < XR; ++i) {
-        const int rr = xr0 + xrs * i;
-        const bool v = rr < item.z;
-        const int slot = item.y + (v ? rr : 0);
-        if (MODE == 0) {
-            const int tok = slot < a.n_routed ? a.perm[slot] : slot - a.n_routed;
-            xrow[i] = v ? a.xf + (size_t)tok * a.d + 4 * xj : nullptr;
-        } else {
-            hrow[i] = v ? hh + (size_t)slot * K + 8 * xj : nullptr;
-        }
-    }
-    const size_t hlo = (size_t)(hl - hh);  // hl = hh + hlo
-
-    // registers of the next chunk
-    int4 pn[NMAT];
-    __half ps[NMAT];
-    uint4 pa[8];  // MODE 0: float4 of slot i; MODE 1: [2i] hi, [2i+1] lo of slot i
-    // global iteration g = (m-tile mi, chunk c) of this CTA's MPC m-tiles
-    auto prefetch = [&](int g) {
-        const int mi = g / nchunks, c = g % nchunks;
-        const int wr = row0 + mi * MT + rw;
-        if (MODE == 0) {
-            wg.load_half(wr, c, hw, pn[0], ps[0]);
-            wu.load_half(wr, c, hw, pn[NMAT - 1], ps[NMAT - 1]);
-#pragma unroll
-            for (int i = 0; i < XR; ++i)
-                pa[i] = xrow[i] ? *reinterpret_cast<const uint4*>(xrow[i] + c * KC) : make_uint4(0, 0, 0, 0);
-        } else {
-            wd.load_half(wr, c, hw, pn[0], ps[0]);
-#pragma unroll
-            for (int i = 0; i < XR; ++i) {
-                pa[2 * i] = hrow[i] ? *reinterpret_cast<const uint4*>(hrow[i] + c * KC) : make_uint4(0, 0, 0, 0);
-                pa[2 * i + 1] = hrow[i] ? *reinterpret_cast<const uint4*>(hrow[i] + hlo + c * KC) : make_uint4(0, 0, 0, 0);
-            }
-        }
-    };
-    const int n_iter = mpc * nchunks;
-    prefetch(0);
     bool ok = true;
-    for (int g = 0; g < n_iter && ok; ++g) {
-        const int s = g & 1, mi = g / nchunks, c = g % nchunks;
-        // take iteration g out of the prefetch registers and start loading g+1
-        // before converting g, so the loads overlap the conversion and the MMAs
-        int4 cn[NMAT];
-        __half cs[NMAT];
-        uint4 ca[8];
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m) { cn[m] = pn[m]; cs[m] = ps[m]; }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) ca[q] = pa[q];
-        if (g + 1 < n_iter) prefetch(g + 1);
-        if (g >= 2 && !mbar_wait(&bar[s], ((g - 2) >> 1) & 1)) { ok = false; break; }
-        uint8_t* st = sm + s * STAGE;
-        uint8_t* xt = st + 2 * NMAT * TILE_BYTES;
-#pragma unroll
-        for (int m = 0; m < NMAT; ++m)
-            dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, rw, hw);
-        if (MODE == 0) {
-#pragma unroll
-            for (int i = 0; i < XR; ++i) {  // floats 4xj .. 4xj+3 of slot xr0 + 16i -> 8 bytes of hi and lo
-                const float* f = reinterpret_cast<const float*>(&ca[i]);
-                const __half2 h0 = __floats2half2_rn(f[0], f[1]), h1 = __floats2half2_rn(f[2], f[3]);
-                const float2 g0 = __half22float2(h0), g1 = __half22float2(h1);
-                const __half2 l0 = __floats2half2_rn(f[0] - g0.x, f[1] - g0.y), l1 = __floats2half2_rn(f[2] - g1.x, f[3] - g1.y);
-                const int o = swz(xr0 + xrs * i, xj >> 1) + 8 * (xj & 1);
-                *reinterpret_cast<uint2*>(xt + o) =
-                    make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
-                *reinterpret_cast<uint2*>(xt + TILE_BYTES + o) =
-                    make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
-            }
-        } else {
-#pragma unroll
-            for (int i = 0; i < XR; ++i) {
-                const int o = swz(xr0 + xrs * i, xj);
-                *reinterpret_cast<uint4*>(xt + o) = ca[2 * i];
-                *reinterpret_cast<uint4*>(xt + TILE_BYTES + o) = ca[2 * i + 1];
+
+    if (warp == 8) {
+        // activation producer: chunk g -> ring slot g % XS once the MMAs of chunk g - XS are done
+        if ((tid & 31) == 0) {
+            for (int g = 0; g < n_iter; ++g) {
+                const int slot = g % XS, use = g / XS;
+                if (use > 0 && !mbar_wait(&xempty[slot], (use - 1) & 1)) { ok = false; break; }
+                uint8_t* xt = xring + slot * 2 * TILE_BYTES;
+                mbar_expect_tx(&xfull[slot], 2 * TILE_BYTES);
+                const int xc = (g % nchunks) * KC;
+                tma_load_2d(xt, &map_hi, xc, item.y, &xfull[slot]);
+                tma_load_2d(xt + TILE_BYTES, &map_lo, xc, item.y, &xfull[slot]);
             }
         }
-        fence_async_smem();
-        __syncthreads();
-        if (tid == 0) {
-            tc_fence_after();
-#pragma unroll
-            for (int m = 0; m < NMAT; ++m) {
-                const uint8_t* wh = st + 2 * m * TILE_BYTES;
-                const uint8_t* wl = wh + TILE_BYTES;
-                const uint32_t dcol = tmem + m * NT;
-#pragma unroll
-                for (int k = 0; k < KC / 16; ++k) {
-                    const uint64_t dwh = umma_desc(wh, 32 * k), dwl = umma_desc(wl, 32 * k);
-                    const uint64_t dxh = umma_desc(xt, 32 * k), dxl = umma_desc(xt + TILE_BYTES, 32 * k);
-                    mma_f16(dcol, dwh, dxh, (c > 0 || k > 0) ? 1u : 0u);
-                    mma_f16(dcol, dwl, dxh, 1u);
-                    mma_f16(dcol, dwh, dxl, 1u);
+    } else if (warp == 9) {
+        if ((tid & 31) == 0) {
+            for (int g = 0; g < n_iter; ++g) {
+                const int s = g & 1, slot = g % XS, c = g % nchunks;
+                if (!mbar_wait(&full[s], (g >> 1) & 1) || !mbar_wait(&xfull[slot], (g / XS) & 1)) {
+                    ok = false;
+                    break;
                 }
-            }
-            mma_commit(&bar[s]);
-        }
-        if (c + 1 < nchunks) continue;
-        // last chunk of m-tile mi: wait for its MMAs, then the epilogue. The next
-        // m-tile's first MMA (issued after the next __syncthreads) overwrites TMEM.
-        if (!mbar_wait(&bar[s], (g >> 1) & 1)) { ok = false; break; }
-        tc_fence_after();
-        // TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take slot
-        // columns [0, 64), warps 4-7 [64, 128)
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const int row = row0 + mi * MT + (warp & 3) * 32 + (tid & 31);
-        const int c0 = (warp >> 2) * (NT / 2);
-        for (int cb = c0; cb < c0 + NT / 2; cb += 32) {
-            if (cb >= item.z) break;
-            float gv[32];
-            tmem_ld32(tmem + lane_base + cb, gv);
-            if (MODE == 0) {
-                float u[32];
-                tmem_ld32(tmem + lane_base + NT + cb, u);
+                tc_fence_after();
+                const uint8_t* st = sm + s * WSTAGE;
+                const uint8_t* xt = xring + slot * 2 * TILE_BYTES;
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    if (cb + j < item.z) {
-                        const float hvv = gv[j] / (1.0f + __expf(-gv[j])) * u[j];  // tolerance path
-                        const __half h1 = __float2half_rn(hvv);
-                        const size_t o = (size_t)(item.y + cb + j) * a.f + row;
-                        hh[o] = h1;
-                        hl[o] = __float2half_rn(hvv - __half2float(h1));
+                for (int m = 0; m < NMAT; ++m) {
+                    const uint8_t* wh = st + 2 * m * TILE_BYTES;
+                    const uint8_t* wl = wh + TILE_BYTES;
+                    const uint32_t dcol = tmem + m * NT;
+#pragma unroll
+                    for (int k = 0; k < KC / 16; ++k) {
+                        const uint64_t dwh = umma_desc(wh, 32 * k), dwl = umma_desc(wl, 32 * k);
+                        const uint64_t dxh = umma_desc(xt, 32 * k), dxl = umma_desc(xt + TILE_BYTES, 32 * k);
+                        mma_f16(dcol, dwh, dxh, (c > 0 || k > 0) ? 1u : 0u);
+                        mma_f16(dcol, dwl, dxh, 1u);
+                        mma_f16(dcol, dwh, dxl, 1u);
                     }
                 }
-            } else {
-#pragma unroll
-                for (int j = 0; j < 32; ++j)
-                    if (cb + j < item.z) a.y[(size_t)(item.y + cb + j) * a.d + row] = gv[j];
+                mma_commit(&wbar[s]);
+                mma_commit(&xempty[slot]);
             }
         }
-        tc_fence_before();
+    } else {
+        const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
+        Q4Plain wg{}, wu{};
+        Q4Tiled wd{};
+        if (MODE == 0) {
+            wg = Q4Plain{(const uint8_t*)(sh ? a.gs : a.g) + mat * (a.d / 2), (sh ? a.gsd : a.gd) + mat * (a.d / 32), a.d};
+            wu = Q4Plain{(const uint8_t*)(sh ? a.us : a.u) + mat * (a.d / 2), (sh ? a.usd : a.ud) + mat * (a.d / 32), a.d};
+        } else {
+            wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32),
+                         a.f};
+        }
+        // thread t dequantises row t / 2, block (2c + t % 2) of each chunk c: a warp reads whole sectors
+        const int rw = tid >> 1, hw = tid & 1;
+        int4 pn[NMAT];
+        __half ps[NMAT];
+        auto prefetch = [&](int g) {
+            const int wr = row0 + (g / nchunks) * MT + rw, c = g % nchunks;
+            if (MODE == 0) {
+                wg.load_half(wr, c, hw, pn[0], ps[0]);
+                wu.load_half(wr, c, hw, pn[NMAT - 1], ps[NMAT - 1]);
+            } else {
+                wd.load_half(wr, c, hw, pn[0], ps[0]);
+            }
+        };
+        prefetch(0);
+        for (int g = 0; g < n_iter; ++g) {
+            const int s = g & 1, mi = g / nchunks, c = g % nchunks;
+            int4 cn[NMAT];
+            __half cs[NMAT];
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m) { cn[m] = pn[m]; cs[m] = ps[m]; }
+            if (g + 1 < n_iter) prefetch(g + 1);
+            if (g >= 2 && !mbar_wait(&wbar[s], ((g - 2) >> 1) & 1)) { ok = false; break; }
+            uint8_t* st = sm + s * WSTAGE;
+#pragma unroll
+            for (int m = 0; m < NMAT; ++m)
+                dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, rw, hw);
+            fence_async_smem();
+            tc_fence_before();  // orders this warp's earlier TMEM reads (epilogue) before the next MMAs
+            __syncwarp();
+            if ((tid & 31) == 0) mbar_arrive(&full[s]);
+            if (c + 1 < nchunks) continue;
+            // last chunk of m-tile mi: wait for its MMAs, then the epilogue. The next
+            // m-tile's first MMA (issued once every converter warp has arrived on the next
+            // stage, i.e. after this epilogue) overwrites TMEM.
+            if (!mbar_wait(&wbar[s], (g >> 1) & 1)) { ok = false; break; }
+            tc_fence_after();
+            // TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take slot
+            // columns [0, 64), warps 4-7 [64, 128)
+            const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+            const int row = row0 + mi * MT + (warp & 3) * 32 + (tid & 31);
+            const int c0 = (warp >> 2) * (NT / 2);
+            for (int cb = c0; cb < c0 + NT / 2; cb += 32) {
+                if (cb >= item.z) break;
+                float gv[32];
+                tmem_ld32(tmem + lane_base + cb, gv);
+                if (MODE == 0) {
+                    float u[32];
+                    tmem_ld32(tmem + lane_base + NT + cb, u);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        if (cb + j < item.z) {
+                            const float hvv = gv[j] / (1.0f + __expf(-gv[j])) * u[j];  // tolerance path
+                            const __half h1 = __float2half_rn(hvv);
+                            const size_t o = (size_t)(item.y + cb + j) * a.f + row;
+                            hh[o] = h1;
+                            hl[o] = __float2half_rn(hvv - __half2float(h1));
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (cb + j < item.z) a.y[(size_t)(item.y + cb + j) * a.d + row] = gv[j];
+                }
+            }
+            tc_fence_before();
+        }
     }
-    if (!ok && tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
+    if (!ok) atomicOr(err, PI_DEVERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
 }
 
+// xh/xl[slot] = f16 hi/lo split of the f32 token row of slot (routed slots via
+// perm, then one slot per token for the shared expert); 8 elements per thread
+__global__ void k_split_slots(const float* __restrict__ x, const int32_t* __restrict__ perm, int n_routed,
+                              int64_t n_slots, int d, __half* __restrict__ xh, __half* __restrict__ xl) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int per = d / 8;
+    if (i >= n_slots * per) return;
+    const int64_t slot = i / per;
+    const int c = (int)(i % per) * 8;
+    const int64_t tok = slot < n_routed ? perm[slot] : slot - n_routed;
+    const float4 v0 = *reinterpret_cast<const float4*>(x + tok * d + c);
+    const float4 v1 = *reinterpret_cast<const float4*>(x + tok * d + c + 4);
+    const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t hi[4], lo[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+        const __half2 hv = __floats2half2_rn(f[2 * p], f[2 * p + 1]);
+        const float2 hf = __half22float2(hv);
+        const __half2 lv = __floats2half2_rn(f[2 * p] - hf.x, f[2 * p + 1] - hf.y);
+        hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
+        lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
+    }
+    *reinterpret_cast<uint4*>(xh + slot * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+    *reinterpret_cast<uint4*>(xl + slot * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+}
+
 template <int MODE>
 constexpr size_t gemm_smem() {
-    return (size_t)2 * ((MODE == 0 ? 4 : 2) + 2) * TILE_BYTES + 1024;
+    return (size_t)(2 * (MODE == 0 ? 4 : 2) + 2 * XS) * TILE_BYTES + 1024;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// f16 [rows][cols] row-major, box {64 columns, 128 rows}, 128-byte swizzle
+// (the UMMA K-major SW128 layout); rows past the end read as zeros
+bool make_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(__half)};
+    const cuuint32_t box[2] = {(cuuint32_t)KC, 128};
+    const cuuint32_t es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace
 
-int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, const __half* xh,
-                       const __half* xl, __half* hh, __half* hl, cudaStream_t st) {
+int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, int64_t n_slots, __half* xh,
+                       __half* xl, __half* hh, __half* hl, cudaStream_t st) {
     if (qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
     static_assert(MT * DN_MPC == 512 && MT * GU_MPC == 128, "pi_prefill_shape_ok matches the CTA blocks");
     if (!pi_prefill_shape_ok(a.d, a.f))
         return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: n_embd must be a multiple of 512, expert width of 128");
+    CUtensorMap mxh, mxl, mhh, mhl;
+    if (!make_map(&mxh, xh, n_slots, a.d) || !make_map(&mxl, xl, n_slots, a.d) || !make_map(&mhh, hh, n_slots, a.f) ||
+        !make_map(&mhl, hl, n_slots, a.f))
+        return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: cuTensorMapEncodeTiled failed");
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<0>());
@@ -397,14 +451,19 @@ int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_
         attr = true;
     }
     {
+        PiProfScope ps(ctx, st, "k_split_slots");
+        const int64_t n = n_slots * (a.d / 8);
+        k_split_slots<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.xf, a.perm, a.n_routed, n_slots, a.d, xh, xl);
+    }
+    {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
-        k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(a, xh, xl, hh, hl,
-                                                                                                    ctx->dev_err);
+        k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(
+            a, mxh, mxl, hh, hl, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_down");
-        k_moe_gemm<1><<<dim3((unsigned)(a.d / (MT * DN_MPC)), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(a, xh, xl, hh, hl,
-                                                                                                    ctx->dev_err);
+        k_moe_gemm<1><<<dim3((unsigned)(a.d / (MT * DN_MPC)), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(
+            a, mhh, mhl, hh, hl, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
 }
