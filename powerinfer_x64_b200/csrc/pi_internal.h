@@ -38,6 +38,8 @@ struct pi_moe_layer {
     bool has_shared = false, has_shared_gate = false, has_bias = false;
     float* router = nullptr;   // f32 [E + 1][d]; row E = shared-expert gate vector (zeros if absent)
     float* bias = nullptr;     // f32 [E] or null
+    float* router_t = nullptr; // f32 [d][ep]: rows 0..E-1 of router transposed, zero-padded to ep = ceil(E/128)*128
+    int64_t ep = 0;
     PiMats gate, up, down;     // routed experts: gate/up [E][f][d], down [E][d][f]
     PiMats gate_sh, up_sh, down_sh;  // shared expert (n = 1)
     std::vector<void*> allocs;
@@ -160,6 +162,8 @@ size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st);
+// Builds L->router_t from L->router (prefill router kernels).
+int pi_router_transpose(pi_ctx* ctx, pi_moe_layer* L);
 // Rewrites a down-projection family into the lane-tiled order the down kernels read.
 int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs);
 // Rewrites Q8_0 gate/up rows into the lane-tiled order k_gateup_q8 reads.

@@ -226,64 +226,115 @@ __global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ x
 }
 
 // ---------------------------------------------------------------------------
-// k_router_tiled: exact logits for prefill-sized batches. A register-tiled
-// SIMT product whose accumulators walk i in ascending order, one mul then
-// one add per step (no FMA): each logit is the reference's sequential f32 sum
-// (quant/mod.rs:921-935) bit for bit, and with T x (E+1) independent chains
-// the throughput, not the chain latency, sets the time.
-// CTA = 64 tokens x 64 rows (256 threads, 4 x 4 accumulators each), i staged
-// through shared memory 32 at a time.
+// k_router_wide: exact logits of the E expert rows for prefill-sized batches.
+// Each logit is the reference's sequential f32 sum (quant/mod.rs:921-935): the
+// accumulator walks i in ascending order, one rounded mul then one rounded add
+// per step (no FMA), bit for bit; with T x E independent chains the throughput,
+// not the chain latency, sets the time.
+// CTA = 32 tokens x 128 rows, 4 warps; warp w owns tokens 8w..8w+7, lane l rows
+// 4l..4l+3 (32 accumulators). Per i a warp reads its 128 router values with one
+// 16-byte shared load (router transposed to [d][ep], so the staging is
+// coalesced) and its 8 token values with two broadcast loads. The next
+// 32-i block is loaded into registers while the current one is consumed.
 // ---------------------------------------------------------------------------
-constexpr int RTT = 64, RTE = 64, RTK = 32;
-__global__ __launch_bounds__(256) void k_router_tiled(const float* __restrict__ xin, const float* __restrict__ W,
-                                                      const float* __restrict__ bias, int T, int d, int E,
-                                                      float* __restrict__ logits) {
-    __shared__ __align__(16) float xs[RTK][RTT + 4];  // +4: fewer bank conflicts on the transposed stores
-    __shared__ __align__(16) float ws[RTK][RTE + 4];
-    const int tid = threadIdx.x;
-    const int t0 = blockIdx.x * RTT, e0 = blockIdx.y * RTE;
-    const int ti = (tid & 15) * 4, ei = (tid >> 4) * 4;  // this thread's 4 tokens x 4 rows
-    float acc[4][4];
+constexpr int RW_ROWS = 128, RW_K = 32, RW_THREADS = 128;
+template <int TPW>  // tokens per warp
+__global__ __launch_bounds__(RW_THREADS) void k_router_wide(const float* __restrict__ xin, const float* __restrict__ Wt,
+                                                            int64_t ep, const float* __restrict__ bias,
+                                                            const float* __restrict__ wgate, int T, int d, int E,
+                                                            float* __restrict__ logits) {
+    constexpr int RW_TOK = 4 * TPW, RW_XS = RW_TOK + 4, XV = RW_TOK * RW_K / 4 / RW_THREADS;
+    __shared__ __align__(16) float ws[RW_K][RW_ROWS];
+    __shared__ __align__(16) float xs[RW_K][RW_XS];  // [i][token]
+    __shared__ __align__(16) float gs[RW_K];         // router row E (shared-expert gate)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * RW_TOK, e0 = blockIdx.y * RW_ROWS;
+    // the CTAs of row block 0 also run the gate row's chain: lane l < TPW of warp
+    // w for token TPW w + l
+    const bool gate = wgate != nullptr && blockIdx.y == 0;
+    float acc_g = 0.0f;
+    float4 gr = make_float4(0.f, 0.f, 0.f, 0.f);
+    float acc[TPW][4];
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < TPW; ++a)
 #pragma unroll
         for (int b = 0; b < 4; ++b) acc[a][b] = 0.0f;
-    for (int k0 = 0; k0 < d; k0 += RTK) {
-        __syncthreads();
-        for (int q = tid; q < RTT * RTK / 4; q += 256) {  // transpose-stage: [i][token], [i][row]
-            const int r = q / (RTK / 4), i = 4 * (q % (RTK / 4));
-            const float4 xv = (t0 + r < T) ? *reinterpret_cast<const float4*>(xin + (size_t)(t0 + r) * d + k0 + i)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 wv = (e0 + r <= E) ? *reinterpret_cast<const float4*>(W + (size_t)(e0 + r) * d + k0 + i)
-                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-            xs[i][r] = xv.x; xs[i + 1][r] = xv.y; xs[i + 2][r] = xv.z; xs[i + 3][r] = xv.w;
-            ws[i][r] = wv.x; ws[i + 1][r] = wv.y; ws[i + 2][r] = wv.z; ws[i + 3][r] = wv.w;
+    float4 wr[8], xr[XV];
+    auto load = [&](int k0) {
+        if (gate && tid < RW_K / 4) gr = __ldg(reinterpret_cast<const float4*>(wgate + k0 + 4 * tid));
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {  // [32 i][128 rows]: a warp reads one i-row of 512 bytes
+            const int q = tid + RW_THREADS * m, i = q >> 5, c4 = q & 31;
+            wr[m] = __ldg(reinterpret_cast<const float4*>(Wt + (size_t)(k0 + i) * ep + e0 + 4 * c4));
         }
+#pragma unroll
+        for (int m = 0; m < XV; ++m) {  // [RW_TOK tokens][32 i]
+            const int q = tid + RW_THREADS * m, tk = q >> 3, c4 = q & 7;
+            xr[m] = (t0 + tk < T) ? *reinterpret_cast<const float4*>(xin + (size_t)(t0 + tk) * d + k0 + 4 * c4)
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    };
+    load(0);
+    for (int k0 = 0; k0 < d; k0 += RW_K) {
         __syncthreads();
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+            const int q = tid + RW_THREADS * m;
+            *reinterpret_cast<float4*>(&ws[q >> 5][4 * (q & 31)]) = wr[m];
+        }
+#pragma unroll
+        for (int m = 0; m < XV; ++m) {
+            const int q = tid + RW_THREADS * m, tk = q >> 3, i = 4 * (q & 7);
+            xs[i][tk] = xr[m].x;
+            xs[i + 1][tk] = xr[m].y;
+            xs[i + 2][tk] = xr[m].z;
+            xs[i + 3][tk] = xr[m].w;
+        }
+        if (gate && tid < RW_K / 4) *reinterpret_cast<float4*>(&gs[4 * tid]) = gr;
+        __syncthreads();
+        if (k0 + RW_K < d) load(k0 + RW_K);
+        if (gate) {
 #pragma unroll 8
-        for (int i = 0; i < RTK; ++i) {
-            const float4 xv = *reinterpret_cast<const float4*>(&xs[i][ti]);
-            const float4 wv = *reinterpret_cast<const float4*>(&ws[i][ei]);
-            const float xa[4] = {xv.x, xv.y, xv.z, xv.w}, wa[4] = {wv.x, wv.y, wv.z, wv.w};
+            for (int i = 0; i < RW_K; ++i) acc_g = fadd(acc_g, fmul(gs[i], xs[i][TPW * warp + (lane % TPW)]));
+        }
+#pragma unroll 8
+        for (int i = 0; i < RW_K; ++i) {
+            const float4 wv = *reinterpret_cast<const float4*>(&ws[i][4 * lane]);
+            float x8[TPW];
 #pragma unroll
-            for (int a = 0; a < 4; ++a)
+            for (int v = 0; v < TPW / 4; ++v) {
+                const float4 xv = *reinterpret_cast<const float4*>(&xs[i][TPW * warp + 4 * v]);
+                x8[4 * v] = xv.x; x8[4 * v + 1] = xv.y; x8[4 * v + 2] = xv.z; x8[4 * v + 3] = xv.w;
+            }
+            const float w4[4] = {wv.x, wv.y, wv.z, wv.w};
 #pragma unroll
-                for (int b = 0; b < 4; ++b) acc[a][b] = fadd(acc[a][b], fmul(wa[b], xa[a]));
+            for (int a = 0; a < TPW; ++a)
+#pragma unroll
+                for (int b = 0; b < 4; ++b) acc[a][b] = fadd(acc[a][b], fmul(w4[b], x8[a]));
         }
     }
 #pragma unroll
-    for (int a = 0; a < 4; ++a) {
-        const int t = t0 + ti + a;
+    for (int a = 0; a < TPW; ++a) {
+        const int t = t0 + TPW * warp + a;
         if (t >= T) continue;
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-            const int e = e0 + ei + b;
-            if (e > E) continue;
+            const int e = e0 + 4 * lane + b;
+            if (e >= E) continue;
             float v = acc[a][b];
-            if (bias && e < E) v = fadd(v, bias[e]);
+            if (bias) v = fadd(v, bias[e]);
             logits[(size_t)t * (E + 1) + e] = v;
         }
     }
+    if (gate && lane < TPW && t0 + TPW * warp + lane < T) logits[(size_t)(t0 + TPW * warp + lane) * (E + 1) + E] = acc_g;
+}
+
+__global__ void k_transpose_rows(const float* __restrict__ src, int rows, int cols, int64_t ld_dst,
+                                 float* __restrict__ dst) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i >= (int64_t)rows * cols) return;
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    dst[(size_t)c * ld_dst + r] = src[i];
 }
 
 // ---------------------------------------------------------------------------
@@ -1290,6 +1341,17 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
 }
 }  // namespace
 
+int pi_router_transpose(pi_ctx* ctx, pi_moe_layer* L) {
+    L->ep = (L->E + RW_ROWS - 1) / RW_ROWS * RW_ROWS;
+    const size_t bytes = sizeof(float) * (size_t)L->d * L->ep;
+    if (pi_cuda_check(ctx, cudaMalloc((void**)&L->router_t, bytes), "cudaMalloc")) return PI_ERR_OOM;
+    L->allocs.push_back(L->router_t);
+    if (pi_cuda_check(ctx, cudaMemset(L->router_t, 0, bytes), "memset")) return PI_ERR_CUDA;
+    const int64_t n = (int64_t)L->E * L->d;
+    k_transpose_rows<<<(unsigned)((n + 255) / 256), 256>>>(L->router, L->E, (int)L->d, L->ep, L->router_t);
+    return pi_cuda_check(ctx, cudaDeviceSynchronize(), "router transpose") ? PI_ERR_CUDA : PI_OK;
+}
+
 size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags) { return carve(L, T, flags, nullptr).bytes; }
 
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
@@ -1318,9 +1380,11 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     if (T >= 256) {
         // prefill-sized batch: exact logits for every token, exact selection
         {
-            PiProfScope ps(ctx, st, "k_router_tiled");
-            dim3 rg((unsigned)((T + RTT - 1) / RTT), (unsigned)((E + 1 + RTE - 1) / RTE));
-            k_router_tiled<<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, B.logits);
+            PiProfScope ps(ctx, st, "k_router_wide");
+            dim3 rg((unsigned)((T + 31) / 32), (unsigned)(L->ep / RW_ROWS));
+            k_router_wide<8><<<rg, RW_THREADS, 0, st>>>(xin, L->router_t, L->ep, L->bias,
+                                                        L->has_shared_gate ? L->router + (size_t)E * d : nullptr,
+                                                        (int)T, d, E, B.logits);
         }
         PiProfScope ps(ctx, st, "k_topk");
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,

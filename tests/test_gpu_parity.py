@@ -281,6 +281,23 @@ def test_c3_prefill_gemm_vs_oracle(pkg, orc, torch, c3_layer):
     close(got, _oracle_layer(orc, c, t, x))
 
 
+@pytest.mark.parametrize("T", [256, 300])
+def test_c3_prefill_router_exact(pkg, orc, torch, c3_layer, T):
+    """Prefill-sized batches take the wide exact router: indices, counts,
+    offsets and permutation bit-exact against the reference restatement
+    (Zipf-biased logits, a ragged final token tile), the shared-expert gate
+    through the layer output."""
+    from powerinfer_x64_b200 import synth
+
+    c = synth.C3
+    L, t = c3_layer
+    x = synth.tokens_dev(c.d, T, seed=7)
+    ref_r = orc.moe_route(_host(x), _host(t["router"]), c.d, c.E, c.k, bias=_host(t["router_bias"]))
+    r = L.route(x)
+    _routing_equal(r, ref_r)
+    close(r["gates"].cpu().numpy(), ref_r["gates"], rel_l2=1e-6, max_abs=1e-6)
+
+
 @pytest.mark.parametrize("T", [512, 2048])
 def test_c3_prefill_gemm_vs_gemv(pkg, torch, c3_layer, T):
     """Same inputs through both expert paths (Zipf-skewed routing: experts with
@@ -310,14 +327,16 @@ def test_c5_rmsnorm_residual_teacher_forced(pkg, orc, torch):
         x = ref
 
 
-def test_routing_exact_fallback_on_ties(pkg, orc, torch):
+@pytest.mark.parametrize("T", [48, 300])
+def test_routing_exact_fallback_on_ties(pkg, orc, torch, T):
     """Pairs of identical router rows give exactly tied logits: such tokens cannot
     be certified by the fast router and must take the exact path, which breaks
-    the tie to the lowest expert index like the reference restatement."""
+    the tie to the lowest expert index like the reference restatement. At
+    T = 300 the wide exact router (64 of 128 tile rows live) takes the batch."""
     from powerinfer_x64_b200 import moe
 
     rng = np.random.default_rng(16)
-    d, E, k, f, T = 1024, 64, 4, 256, 48
+    d, E, k, f = 1024, 64, 4, 256
     router = (rng.standard_normal((E // 2, d)) * 0.02).astype(np.float32).repeat(2, axis=0).reshape(-1)
     g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
     x = rng.standard_normal((T, d)).astype(np.float32)
