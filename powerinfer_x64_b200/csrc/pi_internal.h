@@ -1,5 +1,6 @@
 // Internal (non-ABI) declarations shared by the library's translation units.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -31,6 +32,13 @@ struct PiMats {
     int64_t d_mat_elems() const { return rows * (cols / 32); }
 };
 
+// TMA descriptors of a Q4_0 layer's weights for the prefill GEMM:
+// [routed / shared][gate, up, down] raw nibbles and f16 scales.
+struct __align__(64) PiPrefillMaps {
+    CUtensorMap q[2][3];
+    CUtensorMap d[2][3];
+};
+
 struct pi_moe_layer {
     pi_ctx* ctx = nullptr;
     int64_t d = 0, f = 0, f_sh = 0;
@@ -42,6 +50,8 @@ struct pi_moe_layer {
     int64_t ep = 0;
     PiMats gate, up, down;     // routed experts: gate/up [E][f][d], down [E][d][f]
     PiMats gate_sh, up_sh, down_sh;  // shared expert (n = 1)
+    PiPrefillMaps maps;              // valid when maps_ok (Q4_0, prefill-GEMM shapes)
+    bool maps_ok = false;
     std::vector<void*> allocs;
 };
 
@@ -150,12 +160,14 @@ struct ExpertArgs {
 // Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): splits the
 // slot-ordered tokens into f16 hi/lo xh/xl [n_slots][d], then the gate/up GEMM +
 // SwiGLU writes h as f16 hi/lo hh/hl [n_slots][f] and the down GEMM writes a.y,
-// over work items of <= 128 slots. Returns a PI_* status.
-int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, int64_t n_slots, __half* xh,
-                       __half* xl, __half* hh, __half* hl, cudaStream_t st);
+// over work items of <= PI_GEMM_NT slots. Returns a PI_* status.
+int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t n_slots,
+                       __half* xh, __half* xl, __half* hh, __half* hl, cudaStream_t st);
+// Builds L->maps (layer create; no-op for layers the GEMM does not take).
+int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L);
 // n_embd and expert width the prefill GEMM tiles (whole 512-row / 128-row CTA blocks)
 inline bool pi_prefill_shape_ok(int64_t d, int64_t f) { return d % 512 == 0 && f % 128 == 0; }
-constexpr int PI_GEMM_NT = 128;  // slots per prefill work item
+constexpr int PI_GEMM_NT = 256;  // slots per prefill work item
 
 // Layer forward pieces (pi_moe.cu)
 size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);

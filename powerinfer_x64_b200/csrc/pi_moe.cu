@@ -1464,7 +1464,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const unsigned ni = (unsigned)max_items(L, T);
     if (gemm) {
         const int64_t n_slots = T * k + (L->has_shared ? T : 0);
-        if (int rc = pi_prefill_experts(ctx, a, L->qtype, ni, n_slots, B.xh, B.xl, B.hh, B.hl, st)) return rc;
+        if (int rc = pi_prefill_experts(ctx, L, a, ni, n_slots, B.xh, B.xl, B.hh, B.hl, st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
         k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
             x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,

@@ -11,18 +11,22 @@
 //     D += W_hi X_hi + W_lo X_hi + W_hi X_lo,
 // which keeps the products within ~2^-21 relative of the f32 result.
 //
-// Work item: (expert e, tile of 128 weight rows, <= 128 slots of e). The CTA
-// (256 threads) walks K in 64-element chunks with two shared-memory stages:
-//   * every thread dequantises half a weight row of the chunk (one Q4_0
-//     block: nibbles in reference order times the f16 block scale) into hi/lo
-//     f16 tiles and copies one slot row of the hi or lo activations, both in
-//     the canonical K-major 128-byte-swizzled layout of the UMMA descriptors,
-//     from registers loaded one chunk ahead;
-//   * thread 0 issues the MMAs and a tcgen05.commit onto the stage's mbarrier,
-//     which tells the loaders when the stage may be overwritten.
+// Work item: (expert e, <= 256 slots of e); a CTA takes one item and one (gate/up)
+// or four (down) 128-row m-tiles of the expert, walking K in 32-element chunks
+// (one Q4_0 block per row). MMA N is the item's slot count rounded up to 16.
+// Data movement is asynchronous throughout (TMA, no multicast):
+//   * raw Q4_0 nibbles [128 rows][16 B] per chunk and f16 scales [128 rows][8]
+//     per 8 chunks land in a ring (both weight layouts -- plain rows and the
+//     decode kernels' lane-tiled down rows -- are described as tensor maps);
+//   * converter warps dequantise them into f16 hi/lo tiles in the canonical
+//     K-major 64-byte-swizzled UMMA layout;
+//   * the activations (already split into f16 hi/lo, slot-major) are loaded by
+//     TMA straight into that layout;
+//   * one thread issues the MMAs; tcgen05.commit releases stages and slots.
 // The epilogue reads the accumulators with tcgen05.ld (warp w owns TMEM lanes
-// 32w..32w+31, one weight row per thread) and writes SwiGLU h (gate/up) or y
-// (down). All mbarrier waits are bounded (1 s) and report PI_DEVERR_TIMEOUT.
+// 32(w%4)..+31, one weight row per thread) and writes SwiGLU h as f16 hi/lo
+// (gate/up) or y (down). All mbarrier waits are bounded (1 s) and report
+// PI_DEVERR_TIMEOUT.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -31,10 +35,13 @@
 
 namespace {
 
-constexpr int NT = PI_GEMM_NT;  // slots per item (MMA N)
-constexpr int MT = 128;         // weight rows per item (MMA M)
-constexpr int KC = 64;          // K elements per chunk (one 128-byte swizzle atom)
-constexpr int TILE_BYTES = 128 * 128;  // 128 rows x 128 bytes
+constexpr int NTMAX = PI_GEMM_NT;  // slots per item (max MMA N)
+constexpr int MT = 128;            // weight rows per m-tile (MMA M)
+constexpr int KC = 32;             // K elements per chunk (one 64-byte swizzle atom row)
+constexpr int WTILE = MT * 64;     // 128 rows x 64 bytes
+constexpr int XTILE = NTMAX * 64;  // 256 rows x 64 bytes
+constexpr int RAWQ = MT * 16;      // raw nibbles of one matrix per chunk
+constexpr int RAWD = MT * 16;      // raw scales of one matrix per 8 chunks
 
 PI_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -66,25 +73,26 @@ PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
-// UMMA shared-memory descriptor: K-major, 128-byte swizzle, 8-row atoms of
-// 1024 bytes (SBO = 1024), version 1 (sm_100).
+// UMMA shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms of 512
+// bytes (SBO = 512), version 1 (sm_100). A k16 step inside the 64-byte row
+// advances the start address by 32 bytes.
 PI_DEV uint64_t umma_desc(const void* tile, uint32_t byte_offset) {
     const uint32_t a = smem_u32(tile) + byte_offset;
     uint64_t d = (uint64_t)((a >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;            // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(1024 >> 4) << 32;  // SBO
-    d |= (uint64_t)1 << 46;            // version
-    d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+    d |= (uint64_t)1 << 16;           // LBO (unused for swizzled K-major)
+    d |= (uint64_t)(512 >> 4) << 32;  // SBO
+    d |= (uint64_t)1 << 46;           // version
+    d |= (uint64_t)4 << 61;           // SWIZZLE_64B
     return d;
 }
-// instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = NT
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(NT >> 3) << 17) | ((uint32_t)(MT >> 4) << 24);
+// instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = n (16..256, n % 16 == 0)
+PI_DEV uint32_t idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MT >> 4) << 24); }
 
-PI_DEV void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t accumulate) {
+PI_DEV void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t accumulate) {
     asm volatile(
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(IDESC), "r"(accumulate)
+        "l"(da), "l"(db), "r"(id), "r"(accumulate)
         : "memory");
 }
 PI_DEV void mma_commit(uint64_t* bar) {
@@ -97,7 +105,10 @@ PI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" :
 PI_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
 }
-// 2-D tiled TMA load (no multicast) of box {64 f16, 128 rows} at element (x, y)
+PI_DEV void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// tiled TMA loads (no multicast) completing on an mbarrier
 PI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
@@ -105,8 +116,12 @@ PI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
-PI_DEV void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+PI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+        "[%6];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // 32 consecutive f32 accumulator columns of this thread's TMEM lane
@@ -125,21 +140,21 @@ PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
-// swizzled position of 16-byte chunk c (0..7) of row r in a K-major SW128 tile
-PI_DEV int swz(int r, int c) { return r * 128 + ((c ^ (r & 7)) << 4); }
+// swizzled position of 16-byte chunk c (0..3) of row r in a K-major SW64 tile
+PI_DEV int swz(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 
-// half a row (one 32-element block, h = 0/1) x 64 K -> 4 swizzled chunks each of hi/lo.
+// 16 elements of one Q4_0 block (8 nibble bytes: part p = 0/1 of the block)
+// -> swizzled 16-byte chunks 2p, 2p+1 of row r in the hi and lo tiles.
 // Packed f16 arithmetic: 0x6400 | n is the f16 value 1024 + n, so (0x6400 | n) - 1032 = n - 8
 // exactly; hi = rn(d * (n - 8)) is one rounding of the exact product, the same value as
 // rounding the f32 product (exact: 11 x 4 bits); lo = rn(d * (n - 8) - hi) by one fused
 // multiply-add, the same value as rounding the exact f32 difference.
-PI_DEV void dequant_half_q4(const int4 nib, __half sc, uint8_t* th, uint8_t* tl, int r, int h) {
-    const uint32_t w[4] = {(uint32_t)nib.x, (uint32_t)nib.y, (uint32_t)nib.z, (uint32_t)nib.w};
+PI_DEV void dequant_part_q4(const uint2 nib, __half sc, uint8_t* th, uint8_t* tl, int r, int p) {
+    const uint32_t w[2] = {nib.x, nib.y};
     const __half2 d2 = __half2half2(sc);
     const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6408));  // 1032
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) {
-        const int c = 4 * h + cc;
+    for (int cc = 0; cc < 2; ++cc) {
         const uint32_t v = w[cc];
         // t_j holds nibble j (bits 0..3) and nibble j + 4 (bits 16..19): elements j, j + 4
         uint32_t t[4];
@@ -147,74 +162,62 @@ PI_DEV void dequant_half_q4(const int4 nib, __half sc, uint8_t* th, uint8_t* tl,
         for (int j = 0; j < 4; ++j) t[j] = (v >> (4 * j)) & 0x000F000Fu;
         uint32_t hi[4], lo[4];
 #pragma unroll
-        for (int p = 0; p < 4; ++p) {
-            // pair p = elements (2p, 2p + 1): low halves of t[2p], t[2p+1] for p < 2, high halves after
-            const uint32_t a = t[(2 * p) & 3], b = t[(2 * p + 1) & 3];
-            const uint32_t q = (p < 2 ? __byte_perm(a, b, 0x5410) : __byte_perm(a, b, 0x7632)) | 0x64006400u;
-            const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&q), off);
+        for (int q = 0; q < 4; ++q) {
+            // pair q = elements (2q, 2q + 1): low halves of t[2q], t[2q+1] for q < 2, high halves after
+            const uint32_t a = t[(2 * q) & 3], b = t[(2 * q + 1) & 3];
+            const uint32_t u = (q < 2 ? __byte_perm(a, b, 0x5410) : __byte_perm(a, b, 0x7632)) | 0x64006400u;
+            const __half2 qv = __hsub2(*reinterpret_cast<const __half2*>(&u), off);
             const __half2 hv = __hmul2(d2, qv);
             const __half2 lv = __hfma2(d2, qv, __hneg2(hv));
-            hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
-            lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
+            hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
+            lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
         }
-        *reinterpret_cast<uint4*>(th + swz(r, c)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(tl + swz(r, c)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+        *reinterpret_cast<uint4*>(th + swz(r, 2 * p + cc)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(tl + swz(r, 2 * p + cc)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
     }
 }
 
-// Q4_0 weight row r of a plain SoA matrix (nibbles [rows][K/2], scales [rows][K/32])
-struct Q4Plain {
-    const uint8_t* q;
-    const __half* d;
-    int K;
-    // block 2c + h of row r: 16 nibble bytes and its scale
-    PI_DEV void load_half(int r, int c, int h, int4& n, __half& sc) const {
-        n = *reinterpret_cast<const int4*>(q + (size_t)r * (K / 2) + c * 32 + 16 * h);
-        sc = d[(size_t)r * (K / 32) + 2 * c + h];
-    }
-};
-// Q4_0 down projection in the decode kernels' lane-tiled order (pi_tile_down_mats):
-// 16-byte chunk j of row r lives at (r/8)*8*nch + ((j % cpq)*32 + 4*(r%8) + j/cpq)*16.
-struct Q4Tiled {
-    const uint8_t* q;
-    const __half* d;
-    int K;
-    PI_DEV const uint8_t* chunk(int r, int j) const {
-        const int nch = K / 32, cpq = nch / 4;
-        return q + ((size_t)(r >> 3) * 8 * nch + (size_t)(j % cpq) * 32 + (r & 7) * 4 + j / cpq) * 16;
-    }
-    PI_DEV void load_half(int r, int c, int h, int4& n, __half& sc) const {
-        n = *reinterpret_cast<const int4*>(chunk(r, 2 * c + h));
-        sc = d[(size_t)r * (K / 32) + 2 * c + h];
-    }
-};
-
-// MODE 0: gate/up (two accumulators, 256 TMEM columns); MODE 1: down (one).
-// Warp roles:
-//   0-7  converters: dequantise each 64-K weight chunk into one of two weight
-//        stages (thread t: row t / 2, block 2c + t % 2, loaded one chunk ahead
-//        into registers), then arrive on the stage's `full` barrier; after the
-//        last chunk of an m-tile they run its epilogue;
-//   8    TMA producer: streams the activation chunks (f16 hi and lo, already in
-//        slot order) into a three-deep ring;
+// Warp roles (GT = 352 threads):
+//   0-7  converters: dequantise chunk g's raw nibbles into weight stage g % WS,
+//        then arrive on the stage's `full` barrier and release the raw slot;
+//        after the last chunk of an m-tile they run its epilogue;
+//   8    activation producer: TMA of the hi/lo activation chunk into slot g % XS;
 //   9    MMA issuer: waits for a weight stage and its activation slot, issues
-//        the MMAs and releases both with tcgen05.commit.
-constexpr int GT = 320;
-constexpr int XS = 3;  // activation ring depth
+//        3 x (K/16) MMAs per matrix and releases both with tcgen05.commit;
+//   10   weight producer: TMA of raw nibbles (and every 8 chunks the scales)
+//        into raw slot g % RS.
+constexpr int GT = 352;
+constexpr int WS = 3;
 constexpr int GU_MPC = 1, DN_MPC = 4;  // 128-row m-tiles handled by one CTA (gate/up, down)
 template <int MODE>
-__global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_constant__ CUtensorMap map_hi,
+constexpr int xs_depth() { return MODE == 0 ? 3 : 4; }  // activation slots
+template <int MODE>
+constexpr int rs_depth() { return MODE == 0 ? 4 : 8; }  // raw weight slots (<= 9, see the weight producer)
+template <int MODE>
+constexpr size_t gemm_smem() {
+    constexpr int NMAT = MODE == 0 ? 2 : 1;
+    static_assert(rs_depth<MODE>() <= 9, "scale slot reuse");
+    return (size_t)WS * 2 * NMAT * WTILE + (size_t)xs_depth<MODE>() * 2 * XTILE + (size_t)rs_depth<MODE>() * NMAT * RAWQ +
+           (size_t)2 * NMAT * RAWD + 1024;
+}
+
+template <int MODE>
+__global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
+                                                    const __grid_constant__ CUtensorMap map_hi,
                                                     const __grid_constant__ CUtensorMap map_lo,
                                                     __half* __restrict__ hh, __half* __restrict__ hl, uint32_t* err) {
-    constexpr int NMAT = MODE == 0 ? 2 : 1;         // weight matrices per item
-    constexpr int WSTAGE = 2 * NMAT * TILE_BYTES;   // W hi/lo per matrix
-    constexpr uint32_t TCOLS = MODE == 0 ? 256 : 128;
+    constexpr int NMAT = MODE == 0 ? 2 : 1;  // weight matrices per item
+    constexpr int XS = xs_depth<MODE>(), RS = rs_depth<MODE>();
+    constexpr int WSTAGE = 2 * NMAT * WTILE;  // W hi/lo per matrix
+    constexpr uint32_t TCOLS = MODE == 0 ? 512 : 256;
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* xring = sm + 2 * WSTAGE;  // XS slots of {hi, lo} tiles
-    __shared__ __align__(8) uint64_t wbar[2], full[2], xfull[XS], xempty[XS];
+    uint8_t* xring = sm + WS * WSTAGE;             // XS slots of {hi, lo} activation tiles
+    uint8_t* qring = xring + XS * 2 * XTILE;       // RS slots of raw nibbles [NMAT][128][16]
+    uint8_t* dring = qring + RS * NMAT * RAWQ;     // 2 slots of raw scales [NMAT][128][8 x f16]
+    __shared__ __align__(8) uint64_t wfree[WS], full[WS], xfull[XS], xempty[XS], qfull[RS], qempty[RS];
     __shared__ uint32_t s_tmem;
-    const int tid = threadIdx.x, warp = tid >> 5;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -224,15 +227,20 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     const int K = MODE == 0 ? a.d : a.f;
     const int nchunks = K / KC;
     const int n_iter = mpc * nchunks;
+    const int nn = (item.z + 15) & ~15;  // MMA N
 
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
-            mbar_init(&wbar[i], 1);
+        for (int i = 0; i < WS; ++i) {
+            mbar_init(&wfree[i], 1);
             mbar_init(&full[i], 8);  // one arrival per converter warp
         }
         for (int i = 0; i < XS; ++i) {
             mbar_init(&xfull[i], 1);
             mbar_init(&xempty[i], 1);
+        }
+        for (int i = 0; i < RS; ++i) {
+            mbar_init(&qfull[i], 1);
+            mbar_init(&qempty[i], 8);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -249,106 +257,122 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     bool ok = true;
 
     if (warp == 8) {
-        // activation producer: chunk g -> ring slot g % XS once the MMAs of chunk g - XS are done
-        if ((tid & 31) == 0) {
+        // activation producer: chunk g -> slot g % XS once the MMAs of chunk g - XS are done
+        if (lane == 0) {
             for (int g = 0; g < n_iter; ++g) {
                 const int slot = g % XS, use = g / XS;
                 if (use > 0 && !mbar_wait(&xempty[slot], (use - 1) & 1)) { ok = false; break; }
-                uint8_t* xt = xring + slot * 2 * TILE_BYTES;
-                mbar_expect_tx(&xfull[slot], 2 * TILE_BYTES);
+                uint8_t* xt = xring + slot * 2 * XTILE;
+                mbar_expect_tx(&xfull[slot], 2 * XTILE);
                 const int xc = (g % nchunks) * KC;
                 tma_load_2d(xt, &map_hi, xc, item.y, &xfull[slot]);
-                tma_load_2d(xt + TILE_BYTES, &map_lo, xc, item.y, &xfull[slot]);
+                tma_load_2d(xt + XTILE, &map_lo, xc, item.y, &xfull[slot]);
+            }
+        }
+    } else if (warp == 10) {
+        // weight producer: raw nibbles of chunk g -> slot g % RS once the converters
+        // released chunk g - RS; scales of chunks 8j..8j+7 with chunk 8j into scale slot
+        // j % 2, last read by chunks 8j-16..8j-9 -- released in order before chunk
+        // 8j - RS, which this wait covers, because RS <= 9)
+        if (lane == 0) {
+            const int rb = sh ? 0 : item.x * (MODE == 0 ? a.f : a.d);  // expert's first row
+            for (int g = 0; g < n_iter; ++g) {
+                const int slot = g % RS, use = g / RS, mi = g / nchunks, c = g % nchunks;
+                if (use > 0 && !mbar_wait(&qempty[slot], (use - 1) & 1)) { ok = false; break; }
+                const bool scales = (c & 7) == 0;
+                mbar_expect_tx(&qfull[slot], NMAT * RAWQ + (scales ? NMAT * RAWD : 0));
+                const int r0 = rb + row0 + mi * MT;
+                uint8_t* qt = qring + slot * NMAT * RAWQ;
+                uint8_t* dt = dring + ((g >> 3) & 1) * NMAT * RAWD;
+#pragma unroll
+                for (int m = 0; m < NMAT; ++m) {
+                    const int w = MODE == 0 ? m : 2;  // gate, up, down
+                    const CUtensorMap* mq = sh ? &wm.q[1][w] : &wm.q[0][w];
+                    const CUtensorMap* md = sh ? &wm.d[1][w] : &wm.d[0][w];
+                    if (MODE == 0) {
+                        tma_load_2d(qt + m * RAWQ, mq, c * 16, r0, &qfull[slot]);
+                    } else {
+                        // lane-tiled rows: block c of row r at ((r/8)*8*nch + (c % cpq)*32 + (r%8)*4 + c/cpq) * 16 B
+                        const int cpq = nchunks / 4;
+                        tma_load_4d(qt + m * RAWQ, mq, (c / cpq) * 16, 0, c % cpq, r0 >> 3, &qfull[slot]);
+                    }
+                    if (scales) tma_load_2d(dt + m * RAWD, md, c, r0, &qfull[slot]);
+                }
             }
         }
     } else if (warp == 9) {
-        if ((tid & 31) == 0) {
+        if (lane == 0) {
+            const uint32_t id = idesc(nn);
             for (int g = 0; g < n_iter; ++g) {
-                const int s = g & 1, slot = g % XS, c = g % nchunks;
-                if (!mbar_wait(&full[s], (g >> 1) & 1) || !mbar_wait(&xfull[slot], (g / XS) & 1)) {
+                const int s = g % WS, slot = g % XS, c = g % nchunks;
+                if (!mbar_wait(&full[s], (g / WS) & 1) || !mbar_wait(&xfull[slot], (g / XS) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint8_t* st = sm + s * WSTAGE;
-                const uint8_t* xt = xring + slot * 2 * TILE_BYTES;
+                const uint8_t* xt = xring + slot * 2 * XTILE;
 #pragma unroll
                 for (int m = 0; m < NMAT; ++m) {
-                    const uint8_t* wh = st + 2 * m * TILE_BYTES;
-                    const uint8_t* wl = wh + TILE_BYTES;
-                    const uint32_t dcol = tmem + m * NT;
+                    const uint8_t* wh = st + 2 * m * WTILE;
+                    const uint8_t* wl = wh + WTILE;
+                    const uint32_t dcol = tmem + m * NTMAX;
 #pragma unroll
                     for (int k = 0; k < KC / 16; ++k) {
                         const uint64_t dwh = umma_desc(wh, 32 * k), dwl = umma_desc(wl, 32 * k);
-                        const uint64_t dxh = umma_desc(xt, 32 * k), dxl = umma_desc(xt + TILE_BYTES, 32 * k);
-                        mma_f16(dcol, dwh, dxh, (c > 0 || k > 0) ? 1u : 0u);
-                        mma_f16(dcol, dwl, dxh, 1u);
-                        mma_f16(dcol, dwh, dxl, 1u);
+                        const uint64_t dxh = umma_desc(xt, 32 * k), dxl = umma_desc(xt + XTILE, 32 * k);
+                        mma_f16(dcol, dwh, dxh, id, (c > 0 || k > 0) ? 1u : 0u);
+                        mma_f16(dcol, dwl, dxh, id, 1u);
+                        mma_f16(dcol, dwh, dxl, id, 1u);
                     }
                 }
-                mma_commit(&wbar[s]);
+                mma_commit(&wfree[s]);
                 mma_commit(&xempty[slot]);
             }
         }
     } else {
-        const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
-        Q4Plain wg{}, wu{};
-        Q4Tiled wd{};
-        if (MODE == 0) {
-            wg = Q4Plain{(const uint8_t*)(sh ? a.gs : a.g) + mat * (a.d / 2), (sh ? a.gsd : a.gd) + mat * (a.d / 32), a.d};
-            wu = Q4Plain{(const uint8_t*)(sh ? a.us : a.u) + mat * (a.d / 2), (sh ? a.usd : a.ud) + mat * (a.d / 32), a.d};
-        } else {
-            wd = Q4Tiled{(const uint8_t*)(sh ? a.dns : a.dn) + mat * (a.f / 2), (sh ? a.dsd : a.dd) + mat * (a.f / 32),
-                         a.f};
-        }
-        // thread t dequantises row t / 2, block (2c + t % 2) of each chunk c: a warp reads whole sectors
-        const int rw = tid >> 1, hw = tid & 1;
-        int4 pn[NMAT];
-        __half ps[NMAT];
-        auto prefetch = [&](int g) {
-            const int wr = row0 + (g / nchunks) * MT + rw, c = g % nchunks;
-            if (MODE == 0) {
-                wg.load_half(wr, c, hw, pn[0], ps[0]);
-                wu.load_half(wr, c, hw, pn[NMAT - 1], ps[NMAT - 1]);
-            } else {
-                wd.load_half(wr, c, hw, pn[0], ps[0]);
-            }
-        };
-        prefetch(0);
+        // converter thread t: row r = t / 2, elements 16p .. 16p+15 (p = t % 2) of the chunk's block
+        const int r = tid >> 1, p = tid & 1;
         for (int g = 0; g < n_iter; ++g) {
-            const int s = g & 1, mi = g / nchunks, c = g % nchunks;
-            int4 cn[NMAT];
-            __half cs[NMAT];
+            const int s = g % WS, slot = g % RS, mi = g / nchunks, c = g % nchunks;
+            if (!mbar_wait(&qfull[slot], (g / RS) & 1)) { ok = false; break; }
+            const uint8_t* qt = qring + slot * NMAT * RAWQ;
+            const uint8_t* dt = dring + ((g >> 3) & 1) * NMAT * RAWD;
+            uint2 nib[NMAT];
+            __half sc[NMAT];
 #pragma unroll
-            for (int m = 0; m < NMAT; ++m) { cn[m] = pn[m]; cs[m] = ps[m]; }
-            if (g + 1 < n_iter) prefetch(g + 1);
-            if (g >= 2 && !mbar_wait(&wbar[s], ((g - 2) >> 1) & 1)) { ok = false; break; }
+            for (int m = 0; m < NMAT; ++m) {
+                nib[m] = *reinterpret_cast<const uint2*>(qt + m * RAWQ + r * 16 + 8 * p);
+                sc[m] = *reinterpret_cast<const __half*>(dt + m * RAWD + r * 16 + (c & 7) * 2);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&qempty[slot]);
+            if (g >= WS && !mbar_wait(&wfree[s], ((g - WS) / WS) & 1)) { ok = false; break; }
             uint8_t* st = sm + s * WSTAGE;
 #pragma unroll
             for (int m = 0; m < NMAT; ++m)
-                dequant_half_q4(cn[m], cs[m], st + 2 * m * TILE_BYTES, st + (2 * m + 1) * TILE_BYTES, rw, hw);
+                dequant_part_q4(nib[m], sc[m], st + 2 * m * WTILE, st + (2 * m + 1) * WTILE, r, p);
             fence_async_smem();
             tc_fence_before();  // orders this warp's earlier TMEM reads (epilogue) before the next MMAs
             __syncwarp();
-            if ((tid & 31) == 0) mbar_arrive(&full[s]);
+            if (lane == 0) mbar_arrive(&full[s]);
             if (c + 1 < nchunks) continue;
             // last chunk of m-tile mi: wait for its MMAs, then the epilogue. The next
             // m-tile's first MMA (issued once every converter warp has arrived on the next
             // stage, i.e. after this epilogue) overwrites TMEM.
-            if (!mbar_wait(&wbar[s], (g >> 1) & 1)) { ok = false; break; }
+            if (!mbar_wait(&wfree[s], (g / WS) & 1)) { ok = false; break; }
             tc_fence_after();
-            // TMEM lane (warp % 4) * 32 + lane = weight row; warps 0-3 take slot
-            // columns [0, 64), warps 4-7 [64, 128)
+            // TMEM lane (warp % 4) * 32 + lane = weight row; warp / 4 takes slot columns [128 (warp / 4), +128)
             const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-            const int row = row0 + mi * MT + (warp & 3) * 32 + (tid & 31);
-            const int c0 = (warp >> 2) * (NT / 2);
-            for (int cb = c0; cb < c0 + NT / 2; cb += 32) {
+            const int row = row0 + mi * MT + (warp & 3) * 32 + lane;
+            const int c0 = (warp >> 2) * (NTMAX / 2);
+            for (int cb = c0; cb < c0 + NTMAX / 2; cb += 32) {
                 if (cb >= item.z) break;
                 float gv[32];
                 tmem_ld32(tmem + lane_base + cb, gv);
                 if (MODE == 0) {
                     float u[32];
-                    tmem_ld32(tmem + lane_base + NT + cb, u);
+                    tmem_ld32(tmem + lane_base + NTMAX + cb, u);
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         if (cb + j < item.z) {
@@ -390,20 +414,15 @@ __global__ void k_split_slots(const float* __restrict__ x, const int32_t* __rest
     const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
     uint32_t hi[4], lo[4];
 #pragma unroll
-    for (int p = 0; p < 4; ++p) {
-        const __half2 hv = __floats2half2_rn(f[2 * p], f[2 * p + 1]);
+    for (int q = 0; q < 4; ++q) {
+        const __half2 hv = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
         const float2 hf = __half22float2(hv);
-        const __half2 lv = __floats2half2_rn(f[2 * p] - hf.x, f[2 * p + 1] - hf.y);
-        hi[p] = *reinterpret_cast<const uint32_t*>(&hv);
-        lo[p] = *reinterpret_cast<const uint32_t*>(&lv);
+        const __half2 lv = __floats2half2_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
+        hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
+        lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
     }
     *reinterpret_cast<uint4*>(xh + slot * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
     *reinterpret_cast<uint4*>(xl + slot * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-}
-
-template <int MODE>
-constexpr size_t gemm_smem() {
-    return (size_t)(2 * (MODE == 0 ? 4 : 2) + 2 * XS) * TILE_BYTES + 1024;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -418,31 +437,80 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// f16 [rows][cols] row-major, box {64 columns, 128 rows}, 128-byte swizzle
-// (the UMMA K-major SW128 layout); rows past the end read as zeros
-bool make_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols) {
+bool encode(CUtensorMap* m, CUtensorMapDataType ty, int rank, const void* base, const cuuint64_t* dims,
+            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz) {
     auto fn = encode_fn();
     if (!fn) return false;
+    const cuuint32_t es[4] = {1, 1, 1, 1};
+    return fn(m, ty, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// f16 [rows][cols] row-major activations, box {32 columns, 256 rows}, 64-byte
+// swizzle (the UMMA K-major SW64 layout); rows past the end read as zeros
+bool act_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols) {
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(__half)};
-    const cuuint32_t box[2] = {(cuuint32_t)KC, 128};
-    const cuuint32_t es[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, es,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)NTMAX};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+// Raw Q4_0 nibbles of a plain family [rows][K/2] (box: 16 bytes x 128 rows) and
+// the f16 scales [rows][K/32] of any family (box: 8 scales x 128 rows).
+bool plain_q_map(CUtensorMap* m, const PiMats& w) {
+    const int64_t rows = w.n * w.rows;
+    const cuuint64_t dims[2] = {(cuuint64_t)(w.cols / 2), (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(w.cols / 2)};
+    const cuuint32_t box[2] = {16, (cuuint32_t)MT};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+bool scale_map(CUtensorMap* m, const PiMats& w) {
+    const int64_t rows = w.n * w.rows;
+    const cuuint64_t dims[2] = {(cuuint64_t)(w.cols / 32), (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)(w.cols / 32) * sizeof(__half)};
+    const cuuint32_t box[2] = {8, (cuuint32_t)MT};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, w.d, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+// Lane-tiled down rows (pi_tile_down_mats): 16-byte block j of row r at
+// ((r/8)*8*nch + (j % cpq)*32 + (r%8)*4 + j/cpq) * 16, nch = K/32, cpq = nch/4, as
+// a 4-D byte tensor {64 (j/cpq, byte), 8 (r%8), cpq (j%cpq), rows/8 (r/8)}; the box
+// {16, 8, 1, 16} is block j of 128 consecutive rows, landing as [128 rows][16 B].
+bool tiled_q_map(CUtensorMap* m, const PiMats& w) {
+    const int64_t rows = w.n * w.rows, nch = w.cols / 32, cpq = nch / 4;
+    const cuuint64_t dims[4] = {64, 8, (cuuint64_t)cpq, (cuuint64_t)(rows / 8)};
+    const cuuint64_t strides[3] = {64, 512, (cuuint64_t)(8 * nch * 16)};
+    const cuuint32_t box[4] = {16, 8, 1, (cuuint32_t)(MT / 8)};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace
 
-int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_items, int64_t n_slots, __half* xh,
-                       __half* xl, __half* hh, __half* hl, cudaStream_t st) {
-    if (qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
+int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L) {
+    L->maps_ok = false;
+    if (L->qtype != PI_QT_Q4_0 || !pi_prefill_shape_ok(L->d, L->f)) return PI_OK;
+    PiPrefillMaps& M = L->maps;
+    bool ok = plain_q_map(&M.q[0][0], L->gate) && plain_q_map(&M.q[0][1], L->up) && tiled_q_map(&M.q[0][2], L->down) &&
+              scale_map(&M.d[0][0], L->gate) && scale_map(&M.d[0][1], L->up) && scale_map(&M.d[0][2], L->down);
+    if (ok && L->has_shared)
+        ok = plain_q_map(&M.q[1][0], L->gate_sh) && plain_q_map(&M.q[1][1], L->up_sh) &&
+             tiled_q_map(&M.q[1][2], L->down_sh) && scale_map(&M.d[1][0], L->gate_sh) &&
+             scale_map(&M.d[1][1], L->up_sh) && scale_map(&M.d[1][2], L->down_sh);
+    if (!ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: cuTensorMapEncodeTiled failed for the weights");
+    L->maps_ok = true;
+    return PI_OK;
+}
+
+int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t n_slots,
+                       __half* xh, __half* xl, __half* hh, __half* hl, cudaStream_t st) {
+    if (L->qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
     static_assert(MT * DN_MPC == 512 && MT * GU_MPC == 128, "pi_prefill_shape_ok matches the CTA blocks");
-    if (!pi_prefill_shape_ok(a.d, a.f))
-        return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: n_embd must be a multiple of 512, expert width of 128");
+    if (!pi_prefill_shape_ok(a.d, a.f) || (L->has_shared && L->f_sh != L->f))
+        return pi_set_error(ctx, PI_ERR_ARG,
+                            "prefill GEMM: n_embd must be a multiple of 512, expert widths equal and a multiple of 128");
+    if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: weight tensor maps unavailable");
     CUtensorMap mxh, mxl, mhh, mhl;
-    if (!make_map(&mxh, xh, n_slots, a.d) || !make_map(&mxl, xl, n_slots, a.d) || !make_map(&mhh, hh, n_slots, a.f) ||
-        !make_map(&mhl, hl, n_slots, a.f))
+    if (!act_map(&mxh, xh, n_slots, a.d) || !act_map(&mxl, xl, n_slots, a.d) || !act_map(&mhh, hh, n_slots, a.f) ||
+        !act_map(&mhl, hl, n_slots, a.f))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: cuTensorMapEncodeTiled failed");
     static bool attr = false;
     if (!attr) {
@@ -458,12 +526,12 @@ int pi_prefill_experts(pi_ctx* ctx, const ExpertArgs& a, int qtype, int64_t max_
     {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
         k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(
-            a, mxh, mxl, hh, hl, ctx->dev_err);
+            a, L->maps, mxh, mxl, hh, hl, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_down");
         k_moe_gemm<1><<<dim3((unsigned)(a.d / (MT * DN_MPC)), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(
-            a, mhh, mhl, hh, hl, ctx->dev_err);
+            a, L->maps, mhh, mhl, hh, hl, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
 }
