@@ -223,7 +223,7 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
         if (!rc && pi_cuda_check(ctx, cudaMemcpy(L->bias, D->router_bias, sizeof(float) * L->E, kind), "bias"))
             rc = PI_ERR_CUDA;
     }
-    if (!rc) rc = pi_router_transpose(ctx, L);
+    if (!rc) rc = pi_router_prepare(ctx, L);
     if (!rc) rc = pi_repack_mats(ctx, &L->gate, D->gate_exps, L->qtype, L->E, L->f, L->d, D->src_on_host, &L->allocs);
     if (!rc) rc = pi_repack_mats(ctx, &L->up, D->up_exps, L->qtype, L->E, L->f, L->d, D->src_on_host, &L->allocs);
     if (!rc) rc = pi_repack_mats(ctx, &L->down, D->down_exps, L->qtype, L->E, L->d, L->f, D->src_on_host, &L->allocs);

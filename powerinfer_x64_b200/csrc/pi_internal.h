@@ -48,6 +48,14 @@ struct pi_moe_layer {
     float* bias = nullptr;     // f32 [E] or null
     float* router_t = nullptr; // f32 [d][ep]: rows 0..E-1 of router transposed, zero-padded to ep = ceil(E/128)*128
     int64_t ep = 0;
+    // tensor-core router (prefill): rows 0..E-1 of router scaled by 2^rs and split into
+    // f16 hi/lo [E][d], with upper bounds of the row 2-norms (unscaled)
+    bool router_tc = false;
+    __half* router_h = nullptr;
+    __half* router_l = nullptr;
+    float* router_nrm = nullptr;
+    int router_rs = 0;
+    CUtensorMap rmap_h, rmap_l;
     PiMats gate, up, down;     // routed experts: gate/up [E][f][d], down [E][d][f]
     PiMats gate_sh, up_sh, down_sh;  // shared expert (n = 1)
     PiPrefillMaps maps;              // valid when maps_ok (Q4_0, prefill-GEMM shapes)
@@ -174,8 +182,15 @@ size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st);
-// Builds L->router_t from L->router (prefill router kernels).
-int pi_router_transpose(pi_ctx* ctx, pi_moe_layer* L);
+// Builds L->router_t and the tensor-core router operands from L->router (prefill router kernels).
+int pi_router_prepare(pi_ctx* ctx, pi_moe_layer* L);
+// Fast router logits on tensor cores (pi_prefill.cu): logits[t][e] (stride E + 1),
+// e < E, from the tokens split into f16 hi/lo xh/xl [T][d]; the error against the
+// reference's logits is bounded by the caller's interval arithmetic.
+int pi_router_logits_tc(pi_ctx* ctx, const pi_moe_layer* L, const __half* xh, const __half* xl, int64_t T,
+                        float* logits, cudaStream_t st);
+// Builds the tensor maps of the tensor-core router operands (layer create).
+bool pi_router_maps(pi_moe_layer* L);
 // Rewrites a down-projection family into the lane-tiled order the down kernels read.
 int pi_tile_down_mats(pi_ctx* ctx, PiMats* m, std::vector<void*>* allocs);
 // Rewrites Q8_0 gate/up rows into the lane-tiled order k_gateup_q8 reads.

@@ -628,6 +628,258 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk_cert(const float* __rest
 }
 
 // ---------------------------------------------------------------------------
+// Certified tensor-core routing for prefill batches.
+//
+// k_split_tokens: x [T][d] -> f16 hi/lo xh, xl (x = hi + lo + r, |r| <= 2^-22 |x|
+// plus 2^-25 where lo is subnormal) and an upper bound of ||x_t||_2 (+inf when
+// a value is not finite or |x| >= 2^15, which sends the token to the exact path).
+// grid T, block 256.
+// ---------------------------------------------------------------------------
+constexpr int KC_ROUTER = 32, TC_PER_LANE = 8, TC_WARPS = 4, RCH = 64, RPF = 8;
+__global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ x, int d, __half* __restrict__ xh,
+                                                      __half* __restrict__ xl, float* __restrict__ xnorm) {
+    __shared__ double red[8];
+    __shared__ int s_bad;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+    const float* xr = x + (size_t)t * d;
+    double ss = 0.0;
+    bool bad = false;
+    for (int c = tid * 8; c < d; c += 256 * 8) {
+        const float4 v0 = *reinterpret_cast<const float4*>(xr + c);
+        const float4 v1 = *reinterpret_cast<const float4*>(xr + c + 4);
+        const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half2 hv = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
+            const float2 hf = __half22float2(hv);
+            const __half2 lv = __floats2half2_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
+            hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
+            lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            ss += (double)f[j] * (double)f[j];
+            bad |= !(fabsf(f[j]) < 32768.0f);
+        }
+        *reinterpret_cast<uint4*>(xh + (size_t)t * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(xl + (size_t)t * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    if (bad) s_bad = 1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        // the f64 sum is within ~2^-40 relative; 1 + 2^-20 covers it and the f32 rounding
+        xnorm[t] = s_bad ? INFINITY : __double2float_ru(__dsqrt_ru(tot) * (1.0 + 0x1p-20));
+    }
+}
+
+// ---------------------------------------------------------------------------
+// k_router_cand: one warp per token. From the fast logits l_e (tensor cores) it
+// builds intervals [l_e - eps_e, l_e + eps_e] that contain the reference's
+// logit (sequential f32 sum, quant/mod.rs:921-935, then + bias), with
+//   eps_e = 2 ((4d + 64) u ||x|| ||w_e|| + 2^-23 sqrt(d) (||w_e|| + 2^-rs ||x||))
+//           + 2^-21 (|l_e| + |b_e|),  u = 2^-24:
+// the reference's own error (<= d u sum |x_i w_i|), the tensor-core sums (at
+// most 17 units of 2^-23 per k16 step relative to the magnitudes involved),
+// the hi/lo representation (12 u |x_i w_i|, and 2^-25 where a part is
+// subnormal), and the final f32 operations; sum |x_i w_i| <= ||x|| ||w_e||.
+// Every expert whose upper end reaches the k-th largest lower end is a
+// candidate (the true top-k are among them, at most 31 kept); each lane then
+// runs the reference's exact chain for one candidate (one more lane for the
+// shared-expert gate row), and the top-k is taken on the exact logits. The
+// token is certified when the k-th exact logit clears both the next candidate
+// and every non-candidate's upper end by 2^-16 (1 + |l_k - max|), so that the
+// reference's choice by rounded probability (ties to the lowest index) is the
+// same. Certified tokens get idx (ascending), gates from the exact logits and
+// the shared gate; the others are appended to flag_list for the exact path.
+// ---------------------------------------------------------------------------
+__global__ __launch_bounds__(TC_WARPS * 32) void k_router_cand(
+    const float* __restrict__ logits, const float* __restrict__ xnorm, const float* __restrict__ wnrm, int rs,
+    const float* __restrict__ xin, const float* __restrict__ W, const float* __restrict__ bias, int T, int d, int E,
+    int k, int has_shgate, int32_t* __restrict__ idx, float* __restrict__ gates, float* __restrict__ shscale,
+    int32_t* __restrict__ counts, int32_t* __restrict__ flag_list, int32_t* __restrict__ n_flag) {
+    __shared__ int s_c[TC_WARPS][32];
+    __shared__ __align__(16) float s_w[TC_WARPS][32][RCH + 4];  // +4: a warp's 16-byte loads of 32 rows hit distinct banks
+    __shared__ __align__(16) float s_x[TC_WARPS][RCH];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * TC_WARPS + warp;
+    if (t >= T) return;
+    const float nx = xnorm[t];
+    const float* lr = logits + (size_t)t * (E + 1);
+    const float c1 = 2.0f * (4.0f * d + 64.0f) * 0x1p-24f;
+    const float cab = 2.0f * sqrtf((float)d) * 0x1p-23f;
+    const float sx = ldexpf(nx, -rs);
+    float lo_[TC_PER_LANE], up_[TC_PER_LANE];
+    bool bad = !(nx < INFINITY);
+#pragma unroll
+    for (int j = 0; j < TC_PER_LANE; ++j) {
+        const int e = lane + 32 * j;
+        lo_[j] = up_[j] = -INFINITY;
+        if (e < E) {
+            const float l = lr[e], b = bias ? fabsf(bias[e]) : 0.0f, wn = wnrm[e];
+            const float eps = c1 * nx * wn + cab * (wn + sx) + 0x1p-21f * (fabsf(l) + b);
+            lo_[j] = l - eps;
+            up_[j] = l + eps;
+            bad |= !(fabsf(l) < INFINITY) || !(eps < INFINITY);
+        }
+    }
+    // tau = k-th largest lower end
+    uint32_t taken = 0;
+    float tau = -INFINITY;
+    for (int r = 0; r < k; ++r) {
+        float bl = -INFINITY;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int j = 0; j < TC_PER_LANE; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E && !((taken >> j) & 1u) && (lo_[j] > bl || (lo_[j] == bl && e < bi))) { bl = lo_[j]; bi = e; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ol > bl || (ol == bl && oi < bi)) { bl = ol; bi = oi; }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        tau = bl;
+    }
+    // candidates: upper end >= tau
+    int nc = 0;
+    float maxout = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < TC_PER_LANE; ++j) {
+        const int e = lane + 32 * j;
+        const bool cand = e < E && up_[j] >= tau;
+        const unsigned bal = __ballot_sync(0xffffffffu, cand);
+        const int pos = nc + __popc(bal & ((1u << lane) - 1u));
+        if (cand && pos < 31) s_c[warp][pos] = e;
+        nc += __popc(bal);
+        if (e < E && !cand) maxout = fmaxf(maxout, up_[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) maxout = fmaxf(maxout, __shfl_xor_sync(0xffffffffu, maxout, o));
+    bad |= nc > 31;
+    if (__any_sync(0xffffffffu, bad)) {
+        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
+        return;
+    }
+    __syncwarp();
+    // exact chains (reference order, no FMA): lane j < nc -> candidate j, lane nc -> gate row.
+    // The warp stages RCH-wide pieces of its rows (coalesced loads) and of x in shared memory.
+    const int nrows = nc + (has_shgate ? 1 : 0);
+    const int row = lane < nc ? s_c[warp][lane] : ((lane == nc && has_shgate) ? E : -1);
+    const float* xr = xin + (size_t)t * d;
+    float acc = 0.0f;
+    // lane's share of a piece: float4 q = lane + 32 m (m < RPF) of the nrows x RCH/4 grid,
+    // loaded one piece ahead; source pointers and shared offsets are fixed per lane
+    // (nrows <= 32: rows beyond the first 32 RPF / (RCH / 4) are staged without prefetch)
+    const float* src[RPF];
+    float* dst[RPF];
+    int nmine = 0;
+#pragma unroll
+    for (int m = 0; m < RPF; ++m) {
+        const int q = lane + 32 * m;
+        const int r = q / (RCH / 4), c4 = q % (RCH / 4);
+        const bool v = q < nrows * (RCH / 4);
+        const int rid = v ? (r < nc ? s_c[warp][r] : E) : 0;
+        src[m] = W + (size_t)rid * d + 4 * c4;
+        dst[m] = &s_w[warp][v ? r : 0][4 * c4];
+        nmine += v;
+    }
+    float4 pw[RPF], px;
+    auto fetch = [&](int i0) {
+#pragma unroll
+        for (int m = 0; m < RPF; ++m)
+            if (m < nmine) pw[m] = __ldg(reinterpret_cast<const float4*>(src[m] + i0));
+        if (lane < RCH / 4) px = *reinterpret_cast<const float4*>(xr + i0 + 4 * lane);
+    };
+    fetch(0);
+    for (int i0 = 0; i0 < d; i0 += RCH) {
+        __syncwarp();
+#pragma unroll
+        for (int m = 0; m < RPF; ++m)
+            if (m < nmine) *reinterpret_cast<float4*>(dst[m]) = pw[m];
+        for (int q = lane + 32 * RPF; q < nrows * (RCH / 4); q += 32) {  // rows beyond the prefetched share
+            const int r = q / (RCH / 4), c4 = q % (RCH / 4);
+            const int rid = r < nc ? s_c[warp][r] : E;
+            *reinterpret_cast<float4*>(&s_w[warp][r][4 * c4]) =
+                __ldg(reinterpret_cast<const float4*>(W + (size_t)rid * d + i0 + 4 * c4));
+        }
+        if (lane < RCH / 4) *reinterpret_cast<float4*>(&s_x[warp][4 * lane]) = px;
+        __syncwarp();
+        if (i0 + RCH < d) fetch(i0 + RCH);
+        if (row >= 0) {
+            const float* wr = s_w[warp][lane];
+#pragma unroll 4
+            for (int i = 0; i < RCH; i += 4) {
+                const float4 wv = *reinterpret_cast<const float4*>(wr + i);
+                const float4 xv = *reinterpret_cast<const float4*>(&s_x[warp][i]);
+                acc = fadd(acc, fmul(wv.x, xv.x));
+                acc = fadd(acc, fmul(wv.y, xv.y));
+                acc = fadd(acc, fmul(wv.z, xv.z));
+                acc = fadd(acc, fmul(wv.w, xv.w));
+            }
+        }
+    }
+    if (row >= 0 && row < E && bias) acc = fadd(acc, bias[row]);
+    const float gl = __shfl_sync(0xffffffffu, acc, nc < 32 ? nc : 0);  // gate row's logit
+    // top-k on the exact logits (ties to the lowest index)
+    const float myv = lane < nc ? acc : -INFINITY;
+    const int myi = lane < nc ? row : 0x7fffffff;
+    float m = myv;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    bool sel = false;
+    float lk = -INFINITY;
+    for (int r = 0; r < k; ++r) {
+        float bv = sel ? -INFINITY : myv;
+        int bi = sel ? 0x7fffffff : myi;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+        }
+        if (lane < nc && myi == bi) sel = true;
+        lk = bv;
+    }
+    float nxt = (lane < nc && !sel) ? myv : -INFINITY;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) nxt = fmaxf(nxt, __shfl_xor_sync(0xffffffffu, nxt, o));
+    const float delta = 0x1p-16f * (1.0f + fabsf(lk - m));
+    if (!(lk - nxt > delta && lk - maxout > delta)) {
+        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
+        return;
+    }
+    // ascending order of the selected experts (model/mod.rs:1303), gates from the exact logits
+    const unsigned selm = __ballot_sync(0xffffffffu, sel);
+    int rank = 0;
+    for (unsigned b = selm; b; b &= b - 1) {
+        const int ln = __ffs(b) - 1;
+        rank += __shfl_sync(0xffffffffu, myi, ln) < myi;
+    }
+    const float p = sel ? exp_cr(fsub(myv, m)) : 0.0f;
+    float ssum = 0.0f;
+    for (int r = 0; r < k; ++r) {  // sequential, ascending expert order
+        const unsigned b = __ballot_sync(0xffffffffu, sel && rank == r);
+        ssum = fadd(ssum, __shfl_sync(0xffffffffu, p, __ffs(b) - 1));
+    }
+    if (sel) {
+        idx[(size_t)t * k + rank] = myi;
+        gates[(size_t)t * k + rank] = ssum > 0.0f ? fdiv(p, ssum) : p;
+        atomicAdd(&counts[myi], 1);
+    }
+    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(gl) : 1.0f;
+}
+
+// ---------------------------------------------------------------------------
 // k_topk_api: MoeRouter::route of the standalone operator API
 // (moe/mod.rs:69-108): top-k by logit (ties to the lowest index), ordered by
 // descending logit, then ops::softmax over the k selected (ops.rs:160-180:
@@ -1280,8 +1532,20 @@ struct FwdBufs {
     float* hf;
     float* y;
     __half *xh, *xl, *hh, *hl;
+    __half *xth, *xtl;  // tensor-core router: tokens split into f16 hi/lo
+    float* xnorm;
     size_t bytes;
 };
+
+// Prefill-sized batches route with the certified tensor-core router (when the
+// layer supports it); PI_ROUTER=wide forces the exact SIMT router instead.
+bool use_router_tc(const pi_moe_layer* L, int64_t T) {
+    static const bool wide = [] {
+        const char* v = std::getenv("PI_ROUTER");
+        return v && v[0] == 'w';
+    }();
+    return T >= 256 && L->router_tc && !wide;
+}
 
 // Prefill-sized batches take the tensor-core GEMM path (Q4_0 weights). The
 // environment variable PI_PREFILL=0/1 forces the choice (tests, benchmarks).
@@ -1336,12 +1600,20 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     } else {
         f.xh = f.xl = f.hh = f.hl = nullptr;
     }
+    if (use_router_tc(L, T)) {
+        f.xth = b.take<__half>(T * d);
+        f.xtl = b.take<__half>(T * d);
+        f.xnorm = b.take<float>(T);
+    } else {
+        f.xth = f.xtl = nullptr;
+        f.xnorm = nullptr;
+    }
     f.bytes = b.off + 256;
     return f;
 }
 }  // namespace
 
-int pi_router_transpose(pi_ctx* ctx, pi_moe_layer* L) {
+int pi_router_prepare(pi_ctx* ctx, pi_moe_layer* L) {
     L->ep = (L->E + RW_ROWS - 1) / RW_ROWS * RW_ROWS;
     const size_t bytes = sizeof(float) * (size_t)L->d * L->ep;
     if (pi_cuda_check(ctx, cudaMalloc((void**)&L->router_t, bytes), "cudaMalloc")) return PI_ERR_OOM;
@@ -1349,7 +1621,45 @@ int pi_router_transpose(pi_ctx* ctx, pi_moe_layer* L) {
     if (pi_cuda_check(ctx, cudaMemset(L->router_t, 0, bytes), "memset")) return PI_ERR_CUDA;
     const int64_t n = (int64_t)L->E * L->d;
     k_transpose_rows<<<(unsigned)((n + 255) / 256), 256>>>(L->router, L->E, (int)L->d, L->ep, L->router_t);
-    return pi_cuda_check(ctx, cudaDeviceSynchronize(), "router transpose") ? PI_ERR_CUDA : PI_OK;
+    if (pi_cuda_check(ctx, cudaDeviceSynchronize(), "router transpose")) return PI_ERR_CUDA;
+
+    // tensor-core router operands: W 2^rs = hi + lo in f16, with max |W| 2^rs in [2^12, 2^13)
+    // (no overflow; lo parts of all but tiny elements stay normal); row norms rounded up
+    L->router_tc = false;
+    if (L->E > 256 || L->E % 16 || L->d % KC_ROUTER || L->E > 32 * TC_PER_LANE) return PI_OK;
+    std::vector<float> w((size_t)n);
+    if (pi_cuda_check(ctx, cudaMemcpy(w.data(), L->router, sizeof(float) * n, cudaMemcpyDeviceToHost), "router"))
+        return PI_ERR_CUDA;
+    double amax = 0.0;
+    for (float v : w) amax = std::max(amax, (double)std::fabs(v));
+    if (!(amax > 0.0) || !std::isfinite(amax)) return PI_OK;
+    int ex = 0;
+    std::frexp(amax, &ex);  // amax in [2^(ex-1), 2^ex)
+    L->router_rs = 13 - ex;
+    std::vector<__half> hi((size_t)n), lo((size_t)n);
+    std::vector<float> nrm((size_t)L->E);
+    for (int64_t e = 0; e < L->E; ++e) {
+        double ss = 0.0;
+        for (int64_t i = 0; i < L->d; ++i) {
+            const size_t j = (size_t)(e * L->d + i);
+            const float v = std::ldexp(w[j], L->router_rs);  // exact (power of two, no overflow)
+            hi[j] = __float2half_rn(v);
+            lo[j] = __float2half_rn(v - __half2float(hi[j]));
+            ss += (double)w[j] * (double)w[j];
+        }
+        nrm[(size_t)e] = (float)(std::sqrt(ss) * (1.0 + 1e-6));  // above the f64 value, which is within 1e-12
+    }
+    auto up = [&](void** dst, const void* src, size_t b) {
+        if (pi_cuda_check(ctx, cudaMalloc(dst, b), "cudaMalloc")) return PI_ERR_OOM;
+        L->allocs.push_back(*dst);
+        return pi_cuda_check(ctx, cudaMemcpy(*dst, src, b, cudaMemcpyHostToDevice), "router copy") ? PI_ERR_CUDA
+                                                                                                      : PI_OK;
+    };
+    if (int rc = up((void**)&L->router_h, hi.data(), sizeof(__half) * n)) return rc;
+    if (int rc = up((void**)&L->router_l, lo.data(), sizeof(__half) * n)) return rc;
+    if (int rc = up((void**)&L->router_nrm, nrm.data(), sizeof(float) * L->E)) return rc;
+    L->router_tc = pi_router_maps(L);
+    return PI_OK;
 }
 
 size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags) { return carve(L, T, flags, nullptr).bytes; }
@@ -1377,7 +1687,35 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
     if (pi_cuda_check(ctx, cudaMemsetAsync(B.n_flag, 0, sizeof(int32_t), st), "memset flags")) return PI_ERR_CUDA;
-    if (T >= 256) {
+    if (use_router_tc(L, T)) {
+        // prefill-sized batch: fast logits on tensor cores, exact chains for the
+        // candidates of each token, the exact path for tokens that stay uncertain
+        {
+            PiProfScope ps(ctx, st, "k_split_tokens");
+            k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
+        }
+        if (int rc = pi_router_logits_tc(ctx, L, B.xth, B.xtl, T, B.logits, st)) return rc;
+        {
+            PiProfScope ps(ctx, st, "k_router_cand");
+            k_router_cand<<<(unsigned)((T + TC_WARPS - 1) / TC_WARPS), TC_WARPS * 32, 0, st>>>(
+                B.logits, B.xnorm, L->router_nrm, L->router_rs, xin, L->router, L->bias, (int)T, d, E, k,
+                L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
+        }
+        {
+            PiProfScope ps(ctx, st, "k_router_exact");
+            dim3 eg((unsigned)((E + 1 + 31) / 32), (unsigned)std::min<int64_t>(T, 64));
+            static bool ex_attr = false;
+            if (!ex_attr) {
+                cudaFuncSetAttribute(k_router_exact_list, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)EX_SMEM);
+                ex_attr = true;
+            }
+            k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
+                                                                 B.logits);
+            k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
+                B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
+                nullptr, B.flag_list, B.n_flag);
+        }
+    } else if (T >= 256) {
         // prefill-sized batch: exact logits for every token, exact selection
         {
             PiProfScope ps(ctx, st, "k_router_wide");

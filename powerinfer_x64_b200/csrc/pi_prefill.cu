@@ -483,6 +483,124 @@ bool tiled_q_map(CUtensorMap* m, const PiMats& w) {
     return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
+// ---------------------------------------------------------------------------
+// k_router_gemm: fast router logits for prefill batches. A = tokens [128][K],
+// B = router rows [NR][K] (scaled by 2^rs), both split into f16 hi/lo and
+// streamed by TMA (K-major SW64, 32-K chunks) through an RG-deep ring.
+// Two accumulators keep the error analysis simple: Dh = sum Ah Bh, and
+// Dl = sum (Al Bh + Ah Bl), whose terms are ~2^-11 smaller; the logit is
+// (Dh + Dl) 2^-rs + bias. Warp 0 loads, warp 1 issues MMAs, warps 2-5 read
+// TMEM (warp w: lanes 32 (w % 4) .. +31 = tokens) and store the logits.
+// grid (ceil(T / 128), E / NR).
+// ---------------------------------------------------------------------------
+constexpr int RG = 4;
+__global__ __launch_bounds__(192, 1) void k_router_gemm(const __grid_constant__ CUtensorMap mxh,
+                                                        const __grid_constant__ CUtensorMap mxl,
+                                                        const __grid_constant__ CUtensorMap mwh,
+                                                        const __grid_constant__ CUtensorMap mwl, int T, int d, int E,
+                                                        int nr, float unscale, const float* __restrict__ bias,
+                                                        float* __restrict__ logits, uint32_t* err) {
+    extern __shared__ __align__(1024) uint8_t sm_raw[];
+    uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
+    const int stage = 2 * (MT + nr) * 64;  // A hi/lo + B hi/lo
+    __shared__ __align__(8) uint64_t full[RG], empty[RG], done;
+    __shared__ uint32_t s_tmem;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int t0 = blockIdx.x * MT, e0 = blockIdx.y * nr;
+    const int nchunks = d / KC;
+    const uint32_t tcols = nr <= 64 ? 128 : (nr <= 128 ? 256 : 512);
+    if (tid == 0) {
+        for (int i = 0; i < RG; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], 1);
+        }
+        mbar_init(&done, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(tcols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c % RG, use = c / RG;
+                if (use > 0 && !mbar_wait(&empty[slot], (use - 1) & 1)) { ok = false; break; }
+                uint8_t* st = sm + slot * stage;
+                mbar_expect_tx(&full[slot], stage);
+                tma_load_2d(st, &mxh, c * KC, t0, &full[slot]);
+                tma_load_2d(st + MT * 64, &mxl, c * KC, t0, &full[slot]);
+                tma_load_2d(st + 2 * MT * 64, &mwh, c * KC, e0, &full[slot]);
+                tma_load_2d(st + 2 * MT * 64 + nr * 64, &mwl, c * KC, e0, &full[slot]);
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            const uint32_t id = idesc(nr);
+            for (int c = 0; c < nchunks; ++c) {
+                const int slot = c % RG;
+                if (!mbar_wait(&full[slot], (c / RG) & 1)) { ok = false; break; }
+                tc_fence_after();
+                const uint8_t* st = sm + slot * stage;
+                const uint8_t *ah = st, *al = st + MT * 64, *bh = st + 2 * MT * 64, *bl = bh + nr * 64;
+#pragma unroll
+                for (int k = 0; k < KC / 16; ++k) {
+                    const uint32_t acc = (c > 0 || k > 0) ? 1u : 0u;
+                    mma_f16(tmem, umma_desc(ah, 32 * k), umma_desc(bh, 32 * k), id, acc);
+                    mma_f16(tmem + nr, umma_desc(al, 32 * k), umma_desc(bh, 32 * k), id, acc);
+                    mma_f16(tmem + nr, umma_desc(ah, 32 * k), umma_desc(bl, 32 * k), id, 1u);
+                }
+                mma_commit(&empty[slot]);
+            }
+            mma_commit(&done);
+        }
+    } else {
+        if (mbar_wait(&done, 0)) {
+            tc_fence_after();
+            const int q = warp & 3;
+            const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+            const int t = t0 + q * 32 + lane;
+            for (int cb = 0; cb < nr; cb += 32) {
+                float vh[32], vl[32];
+                tmem_ld32(tmem + lane_base + cb, vh);
+                tmem_ld32(tmem + lane_base + nr + cb, vl);
+                if (t < T) {
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int e = e0 + cb + j;
+                        float v = (vh[j] + vl[j]) * unscale;
+                        if (bias) v += bias[e];
+                        logits[(size_t)t * (E + 1) + e] = v;
+                    }
+                }
+            }
+        } else {
+            ok = false;
+        }
+    }
+    if (!ok) atomicOr(err, PI_DEVERR_TIMEOUT);
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tcols) : "memory");
+}
+
+// f16 [rows][cols] row-major, box {32 columns, box_rows rows}, SW64
+bool kmajor_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * sizeof(__half)};
+    const cuuint32_t box[2] = {(cuuint32_t)KC, (cuuint32_t)box_rows};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+int router_rows_per_cta(int E) { return E % 128 == 0 ? 128 : E; }
+
 }  // namespace
 
 int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L) {
@@ -534,4 +652,28 @@ int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, 
             a, L->maps, mhh, mhl, hh, hl, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
+}
+
+bool pi_router_maps(pi_moe_layer* L) {
+    const int nr = router_rows_per_cta(L->E);
+    return kmajor_map(&L->rmap_h, L->router_h, L->E, L->d, nr) && kmajor_map(&L->rmap_l, L->router_l, L->E, L->d, nr);
+}
+
+int pi_router_logits_tc(pi_ctx* ctx, const pi_moe_layer* L, const __half* xh, const __half* xl, int64_t T,
+                        float* logits, cudaStream_t st) {
+    const int nr = router_rows_per_cta(L->E);
+    CUtensorMap mxh, mxl;
+    if (!kmajor_map(&mxh, xh, T, L->d, MT) || !kmajor_map(&mxl, xl, T, L->d, MT))
+        return pi_set_error(ctx, PI_ERR_CUDA, "router: cuTensorMapEncodeTiled failed");
+    const size_t smem = (size_t)RG * 2 * (MT + nr) * 64 + 1024;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_router_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(RG * 2 * (MT + 256) * 64 + 1024));
+        attr = true;
+    }
+    PiProfScope ps(ctx, st, "k_router_gemm");
+    k_router_gemm<<<dim3((unsigned)((T + MT - 1) / MT), (unsigned)(L->E / nr)), 192, smem, st>>>(
+        mxh, mxl, L->rmap_h, L->rmap_l, (int)T, (int)L->d, L->E, nr, ldexpf(1.0f, -L->router_rs), L->bias, logits,
+        ctx->dev_err);
+    return pi_cuda_check(ctx, cudaGetLastError(), "router GEMM") ? PI_ERR_CUDA : PI_OK;
 }
