@@ -165,12 +165,12 @@ struct ExpertArgs {
 };
 
 
-// Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): splits the
-// slot-ordered tokens into f16 hi/lo xh/xl [n_slots][d], then the gate/up GEMM +
-// SwiGLU writes h as f16 hi/lo hh/hl [n_slots][f] and the down GEMM writes a.y,
-// over work items of <= PI_GEMM_NT slots. Returns a PI_* status.
+// Prefill expert products on tcgen05 tensor cores (pi_prefill.cu): the gate/up
+// GEMM gathers each slot's token row from the token-major f16 hi/lo split
+// xth/xtl [T][d] and writes SwiGLU h as f16 hi/lo hh/hl [n_slots][f]; the down
+// GEMM writes a.y, over work items of <= PI_GEMM_NT slots. Returns a PI_* status.
 int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t n_slots,
-                       __half* xh, __half* xl, __half* hh, __half* hl, cudaStream_t st);
+                       const __half* xth, const __half* xtl, int64_t T, __half* hh, __half* hl, cudaStream_t st);
 // Builds L->maps (layer create; no-op for layers the GEMM does not take).
 int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L);
 // n_embd and expert width the prefill GEMM tiles (whole 512-row / 128-row CTA blocks)

@@ -1593,14 +1593,13 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     if (use_gemm(L, T, flags)) {
-        f.xh = b.take<__half>(slots * d);
-        f.xl = b.take<__half>(slots * d);
+        f.xh = f.xl = nullptr;
         f.hh = b.take<__half>(slots * F);
         f.hl = b.take<__half>(slots * F);
     } else {
         f.xh = f.xl = f.hh = f.hl = nullptr;
     }
-    if (use_router_tc(L, T)) {
+    if (use_router_tc(L, T) || use_gemm(L, T, flags)) {
         f.xth = b.take<__half>(T * d);
         f.xtl = b.take<__half>(T * d);
         f.xnorm = b.take<float>(T);
@@ -1802,7 +1801,11 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const unsigned ni = (unsigned)max_items(L, T);
     if (gemm) {
         const int64_t n_slots = T * k + (L->has_shared ? T : 0);
-        if (int rc = pi_prefill_experts(ctx, L, a, ni, n_slots, B.xh, B.xl, B.hh, B.hl, st)) return rc;
+        if (!use_router_tc(L, T)) {  // the router did not split the tokens
+            PiProfScope ps(ctx, st, "k_split_tokens");
+            k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
+        }
+        if (int rc = pi_prefill_experts(ctx, L, a, ni, n_slots, B.xth, B.xtl, T, B.hh, B.hl, st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
         k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
             x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,

@@ -205,6 +205,7 @@ template <int MODE>
 __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
                                                     const __grid_constant__ CUtensorMap map_hi,
                                                     const __grid_constant__ CUtensorMap map_lo,
+                                                    const __half* __restrict__ xth, const __half* __restrict__ xtl,
                                                     __half* __restrict__ hh, __half* __restrict__ hl, uint32_t* err) {
     constexpr int NMAT = MODE == 0 ? 2 : 1;  // weight matrices per item
     constexpr int XS = xs_depth<MODE>(), RS = rs_depth<MODE>();
@@ -217,6 +218,7 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     uint8_t* dring = qring + RS * NMAT * RAWQ;     // 2 slots of raw scales [NMAT][128][8 x f16]
     __shared__ __align__(8) uint64_t wfree[WS], full[WS], xfull[XS], xempty[XS], qfull[RS], qempty[RS];
     __shared__ uint32_t s_tmem;
+    __shared__ int s_tok[MODE == 0 ? NTMAX : 1];  // gate/up: token of each slot row
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
@@ -235,7 +237,7 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
             mbar_init(&full[i], 8);  // one arrival per converter warp
         }
         for (int i = 0; i < XS; ++i) {
-            mbar_init(&xfull[i], 1);
+            mbar_init(&xfull[i], MODE == 0 ? 8 : 1);  // gate/up: one arrival per converter warp
             mbar_init(&xempty[i], 1);
         }
         for (int i = 0; i < RS; ++i) {
@@ -257,8 +259,9 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     bool ok = true;
 
     if (warp == 8) {
-        // activation producer: chunk g -> slot g % XS once the MMAs of chunk g - XS are done
-        if (lane == 0) {
+        // down: activation producer, the slot-major h rows of chunk g as one TMA tile into
+        // slot g % XS once the MMAs of chunk g - XS are done (gate/up: the converters gather)
+        if (MODE == 1 && lane == 0) {
             for (int g = 0; g < n_iter; ++g) {
                 const int slot = g % XS, use = g / XS;
                 if (use > 0 && !mbar_wait(&xempty[slot], (use - 1) & 1)) { ok = false; break; }
@@ -333,8 +336,46 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     } else {
         // converter thread t: row r = t / 2, elements 16p .. 16p+15 (p = t % 2) of the chunk's block
         const int r = tid >> 1, p = tid & 1;
+        if (MODE == 0) {
+            for (int rr = tid; rr < nn; rr += 256) {
+                const int sl = item.y + (rr < item.z ? rr : 0);
+                s_tok[rr] = sl < a.n_routed ? a.perm[sl] : sl - a.n_routed;
+            }
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+        }
+        // gate/up activations: the converters gather chunk g's token rows (16-byte cp.async
+        // per row piece, one commit group per chunk) into slot g % XS and publish it one
+        // chunk later (wait_group, proxy fence, one arrival per warp); the last chunk at once
+        auto publish = [&](int gx) {
+            fence_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xfull[gx % XS]);
+        };
         for (int g = 0; g < n_iter; ++g) {
             const int s = g % WS, slot = g % RS, mi = g / nchunks, c = g % nchunks;
+            if (MODE == 0) {
+                const int xs_ = g % XS, xuse = g / XS;
+                if (xuse > 0 && !mbar_wait(&xempty[xs_], (xuse - 1) & 1)) { ok = false; break; }
+                uint8_t* xt = xring + xs_ * 2 * XTILE;
+                for (int q = tid; q < nn * 4; q += 256) {
+                    const int row = q >> 2, pc = q & 3;
+                    const size_t off = (size_t)s_tok[row] * a.d + c * KC + 8 * pc;
+                    const uint32_t dh = smem_u32(xt + swz(row, pc));
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dh), "l"(xth + off) : "memory");
+                    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dh + XTILE), "l"(xtl + off) : "memory");
+                }
+                asm volatile("cp.async.commit_group;" ::: "memory");
+                if (g + 1 < n_iter) {
+                    if (g >= 1) {
+                        asm volatile("cp.async.wait_group 1;" ::: "memory");
+                        publish(g - 1);
+                    }
+                } else {
+                    asm volatile("cp.async.wait_group 0;" ::: "memory");
+                    if (g >= 1) publish(g - 1);
+                    publish(g);
+                }
+            }
             if (!mbar_wait(&qfull[slot], (g / RS) & 1)) { ok = false; break; }
             const uint8_t* qt = qring + slot * NMAT * RAWQ;
             const uint8_t* dt = dring + ((g >> 3) & 1) * NMAT * RAWD;
@@ -397,32 +438,6 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
-}
-
-// xh/xl[slot] = f16 hi/lo split of the f32 token row of slot (routed slots via
-// perm, then one slot per token for the shared expert); 8 elements per thread
-__global__ void k_split_slots(const float* __restrict__ x, const int32_t* __restrict__ perm, int n_routed,
-                              int64_t n_slots, int d, __half* __restrict__ xh, __half* __restrict__ xl) {
-    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    const int per = d / 8;
-    if (i >= n_slots * per) return;
-    const int64_t slot = i / per;
-    const int c = (int)(i % per) * 8;
-    const int64_t tok = slot < n_routed ? perm[slot] : slot - n_routed;
-    const float4 v0 = *reinterpret_cast<const float4*>(x + tok * d + c);
-    const float4 v1 = *reinterpret_cast<const float4*>(x + tok * d + c + 4);
-    const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t hi[4], lo[4];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const __half2 hv = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
-        const float2 hf = __half22float2(hv);
-        const __half2 lv = __floats2half2_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
-        hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
-        lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
-    }
-    *reinterpret_cast<uint4*>(xh + slot * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-    *reinterpret_cast<uint4*>(xl + slot * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -619,16 +634,15 @@ int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L) {
 }
 
 int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t n_slots,
-                       __half* xh, __half* xl, __half* hh, __half* hl, cudaStream_t st) {
+                       const __half* xth, const __half* xtl, int64_t T, __half* hh, __half* hl, cudaStream_t st) {
     if (L->qtype != PI_QT_Q4_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill GEMM: Q4_0 weights only");
     static_assert(MT * DN_MPC == 512 && MT * GU_MPC == 128, "pi_prefill_shape_ok matches the CTA blocks");
     if (!pi_prefill_shape_ok(a.d, a.f) || (L->has_shared && L->f_sh != L->f))
         return pi_set_error(ctx, PI_ERR_ARG,
                             "prefill GEMM: n_embd must be a multiple of 512, expert widths equal and a multiple of 128");
     if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: weight tensor maps unavailable");
-    CUtensorMap mxh, mxl, mhh, mhl;
-    if (!act_map(&mxh, xh, n_slots, a.d) || !act_map(&mxl, xl, n_slots, a.d) || !act_map(&mhh, hh, n_slots, a.f) ||
-        !act_map(&mhl, hl, n_slots, a.f))
+    CUtensorMap mhh, mhl;
+    if (!act_map(&mhh, hh, n_slots, a.f) || !act_map(&mhl, hl, n_slots, a.f))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: cuTensorMapEncodeTiled failed");
     static bool attr = false;
     if (!attr) {
@@ -637,19 +651,14 @@ int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, 
         attr = true;
     }
     {
-        PiProfScope ps(ctx, st, "k_split_slots");
-        const int64_t n = n_slots * (a.d / 8);
-        k_split_slots<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a.xf, a.perm, a.n_routed, n_slots, a.d, xh, xl);
-    }
-    {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
         k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(
-            a, L->maps, mxh, mxl, hh, hl, ctx->dev_err);
+            a, L->maps, mhh, mhl, xth, xtl, hh, hl, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_down");
         k_moe_gemm<1><<<dim3((unsigned)(a.d / (MT * DN_MPC)), (unsigned)max_items), GT, gemm_smem<1>(), st>>>(
-            a, L->maps, mhh, mhl, hh, hl, ctx->dev_err);
+            a, L->maps, mhh, mhl, xth, xtl, hh, hl, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill GEMM") ? PI_ERR_CUDA : PI_OK;
 }
