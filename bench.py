@@ -42,9 +42,10 @@ def parse():
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    p.add_argument("--tokens", type=int, default=None, help="tokens per step per GPU (c2: 64, c3: 4096)")
-    p.add_argument("--config", default="c2", choices=["c2", "c3"],
-                   help="c2: decode Q8_0 (headline); c3: prefill Q4_0 with Zipf-skewed routing")
+    p.add_argument("--tokens", type=int, default=None, help="tokens per step per GPU (c2: 64, c3: 4096, c5: 8192)")
+    p.add_argument("--config", default="c2", choices=["c2", "c3", "c5"],
+                   help="c2: decode Q8_0 (headline); c3: prefill Q4_0 with Zipf-skewed routing; "
+                        "c5: one layer of the Q8_0 stack (RMSNorm + residual), prefill-sized")
     p.add_argument("--layers", type=int, default=8, help="distinct layers cycled through")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -211,10 +212,11 @@ def main():
     rank, local, world = dist.init()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    cfg = {"c2": synth.C2, "c3": synth.C3}[args.config]
-    T = args.tokens or (64 if args.config == "c2" else 4096)
-    if args.config == "c3":
+    cfg = {"c2": synth.C2, "c3": synth.C3, "c5": synth.C5}[args.config]
+    T = args.tokens or {"c2": 64, "c3": 4096, "c5": 8192}[args.config]
+    if args.config != "c2":
         args.no_sweep = True
+    fwd_kw = dict(rmsnorm=True, residual=True) if args.config == "c5" else {}
     ctx = Context.default(local)
 
     # layers + fixed per-layer tokens (each rank its own seed stream)
@@ -232,7 +234,7 @@ def main():
     stream = torch.cuda.current_stream()
 
     def step(i):
-        layers[i % args.layers].forward(xs[i % args.layers], out=out)
+        layers[i % args.layers].forward(xs[i % args.layers], out=out, **fwd_kw)
 
     for i in range(args.warmup):
         step(i)
@@ -293,6 +295,18 @@ def main():
                     "frac": ach_t / tpeak, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
                     "traffic": None, "algorithmic_flops_per_launch": flops,
                     "mma_issued_tflops": 3 * ach_t, "avg_launch_us": 1e3 * g_ms / max(g_n, 1)}
+    if args.config == "c5":
+        # Q8_0 prefill: exact int8 block products (f16 MMAs of the int8 values, one per
+        # product), judged against the int8 dense tensor peak (no measured int8 figure
+        # exists for this pool: nominal 4.5 POPS)
+        slots = T * cfg.k + T
+        g_ms, g_n = kern.get("k_gemm_q8_gateup", (float("nan"), 0))
+        ops = 2.0 * slots * 2 * cfg.f * cfg.d
+        ach_t = ops / (g_ms / max(g_n, 1) / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "k_gemm_q8_gateup", "achieved": ach_t, "peak": 4500.0,
+                    "unit": "TOPS (int8)", "frac": ach_t / 4500.0, "peak_source": "nominal int8 dense (no measured int8 peak)",
+                    "frac_of_measured_bf16": ach_t / peaks.get("bf16_tflops", 1590.0), "traffic": None,
+                    "algorithmic_ops_per_launch": ops, "avg_launch_us": 1e3 * g_ms / max(g_n, 1)}
 
     # ---- end to end: host tokens in (pinned), host output back, per step ----
     xh = [x.cpu().pin_memory() for x in xs]
@@ -301,7 +315,7 @@ def main():
 
     def e2e_step(i):
         xd.copy_(xh[i % args.layers], non_blocking=True)
-        layers[i % args.layers].forward(xd, out=out)
+        layers[i % args.layers].forward(xd, out=out, **fwd_kw)
         oh.copy_(out, non_blocking=True)
 
     for i in range(args.warmup):
@@ -356,10 +370,11 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8" if args.config == "c2" else "f16x3->f32",
-            "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> " + ("Q8_0)" if args.config == "c2" else "Q4_0)"),
-            "config": {"workload": f"{cfg.name} (BASELINE config {'2' if args.config == 'c2' else '3'}): d=2048 "
-                                   f"E=256 k=8 f=512 +shared, {'Q8_0 decode' if args.config == 'c2' else 'Q4_0 prefill, Zipf router bias'}",
+            "vs_baseline": None, "dtype": "f16x3->f32" if args.config == "c3" else "int8",
+            "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> " + ("Q4_0)" if args.config == "c3" else "Q8_0)"),
+            "config": {"workload": f"{cfg.name} (BASELINE config {args.config[1]}): d=2048 "
+                                   f"E=256 k=8 f=512 +shared, " + {"c2": "Q8_0 decode", "c3": "Q4_0 prefill, Zipf router bias",
+                                                                   "c5": "Q8_0 prefill, one layer of the 40-layer stack, RMSNorm + residual"}[args.config],
                        "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": f"dp{world} (replicas)",
                        "layers_cycled": args.layers, "l2": "inputs larger than L2: steps cycle through "
                        f"{args.layers} layers x {layer_bytes(cfg, 256, T)['total'] / 1e9:.2f} GB"},

@@ -175,7 +175,13 @@ int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, 
 int pi_prefill_prepare(pi_ctx* ctx, pi_moe_layer* L);
 // n_embd and expert width the prefill GEMM tiles (whole 512-row / 128-row CTA blocks)
 inline bool pi_prefill_shape_ok(int64_t d, int64_t f) { return d % 512 == 0 && f % 128 == 0; }
-constexpr int PI_GEMM_NT = 256;  // slots per prefill work item
+constexpr int PI_GEMM_NT = 256;     // slots per prefill work item (Q4_0)
+constexpr int PI_GEMM_NT_Q8 = 128;  // slots per prefill work item (Q8_0)
+// Exact Q8_0 prefill expert products (pi_prefill_q8.cu): gate/up + SwiGLU + Q8_0 h
+// into a.hq/a.hs, then down into a.y, over work items of <= PI_GEMM_NT_Q8 slots.
+int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items,
+                          cudaStream_t st);
+bool pi_prefill_q8_shape_ok(int64_t d, int64_t f);
 
 // Layer forward pieces (pi_moe.cu)
 size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);

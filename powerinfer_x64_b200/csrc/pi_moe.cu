@@ -36,46 +36,58 @@ constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one wa
 
 // ---------------------------------------------------------------------------
 // k_prep: optional RMSNorm, then Q8_0 quantisation of the (normed) tokens.
-// grid (T, ceil(d/256)), block 256: CTA (t, c) handles elements
-// [256c, 256c + 256) of token t (8 quant blocks, one per warp). With RMSNorm
-// every CTA of a token recomputes the token's 1/rms (identical value).
+// grid T, block 256, dynamic shared memory d floats: the CTA stages its token
+// row, four lanes run the reference's four sum-of-squares chains once, then
+// every warp normalises and quantises 32-element blocks (one block per warp
+// per pass).
 // ---------------------------------------------------------------------------
 __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
                                               float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
                                               float* __restrict__ xs) {
-    const int t = blockIdx.x;
-    const float* xr = x + (size_t)t * d;
-    const int i = blockIdx.y * 256 + threadIdx.x;
+    extern __shared__ float s_row[];
     __shared__ float s_inv;
-    float v = (i < d) ? xr[i] : 0.0f;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    const float* xr = x + (size_t)t * d;
+    for (int c = tid; c < d / 4; c += 256)
+        *reinterpret_cast<float4*>(&s_row[4 * c]) = *reinterpret_cast<const float4*>(xr + 4 * c);
+    __syncthreads();
+    float inv = 1.0f;
     if (do_norm) {
         // sum_squares_sse (simd.rs:116-137): 4 lane accumulators over
         // elements i = 4m + lane, then (l0 + l1) + (l2 + l3), then a scalar tail.
-        if (threadIdx.x < 32) {
-            const int lane = threadIdx.x;
+        if (tid < 32) {
+            const int lane = tid;
             float acc = 0.0f;
             const int n4 = d & ~3;
             if (lane < 4)
-                for (int j = lane; j < n4; j += 4) acc = fadd(acc, fmul(xr[j], xr[j]));
-            float a1 = __shfl_sync(0xffffffffu, acc, 1);
-            float a2 = __shfl_sync(0xffffffffu, acc, 2);
-            float a3 = __shfl_sync(0xffffffffu, acc, 3);
+#pragma unroll 8
+                for (int j = lane; j < n4; j += 4) acc = fadd(acc, fmul(s_row[j], s_row[j]));
+            const float a1 = __shfl_sync(0xffffffffu, acc, 1);
+            const float a2 = __shfl_sync(0xffffffffu, acc, 2);
+            const float a3 = __shfl_sync(0xffffffffu, acc, 3);
             if (lane == 0) {
                 float ss = fadd(fadd(acc, a1), fadd(a2, a3));
-                for (int j = n4; j < d; ++j) ss = fadd(ss, fmul(xr[j], xr[j]));
-                float rms = __fsqrt_rn(fadd(fdiv(ss, (float)d), eps));
+                for (int j = n4; j < d; ++j) ss = fadd(ss, fmul(s_row[j], s_row[j]));
+                const float rms = __fsqrt_rn(fadd(fdiv(ss, (float)d), eps));
                 s_inv = fdiv(1.0f, rms);
             }
         }
         __syncthreads();
-        v = fmul(v, s_inv);  // * weight (1.0) is exact
-        if (i < d) normed[(size_t)t * d + i] = v;
+        inv = s_inv;
     }
-    if (!do_quant || i >= d) return;  // d % 32 == 0: whole warps leave together
-    float sc;
-    const int8_t q = warp_quant_q8(v, &sc);
-    xq[(size_t)t * d + i] = q;
-    if ((threadIdx.x & 31) == 0) xs[(size_t)t * (d / 32) + i / 32] = sc;
+    for (int i = tid; i < d; i += 256) {  // d % 32 == 0: a warp covers one quant block per pass
+        float v = s_row[i];
+        if (do_norm) {
+            v = fmul(v, inv);  // * weight (1.0) is exact
+            normed[(size_t)t * d + i] = v;
+        }
+        if (do_quant) {
+            float sc;
+            const int8_t q = warp_quant_q8(v, &sc);
+            xq[(size_t)t * d + i] = q;
+            if ((tid & 31) == 0) xs[(size_t)t * (d / 32) + i / 32] = sc;
+        }
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1550,10 +1562,10 @@ bool use_router_tc(const pi_moe_layer* L, int64_t T) {
 // Prefill-sized batches take the tensor-core GEMM path (Q4_0 weights). The
 // environment variable PI_PREFILL=0/1 forces the choice (tests, benchmarks).
 bool use_gemm(const pi_moe_layer* L, int64_t T, int flags) {
-    if (L->qtype != PI_QT_Q4_0) return false;
+    if (L->qtype != PI_QT_Q4_0 && L->qtype != PI_QT_Q8_0) return false;
     if (flags & PI_FWD_FORCE_GEMV) return false;
     if (flags & PI_FWD_FORCE_GEMM) return true;  // PI_ERR_ARG on shapes the GEMM does not tile
-    if (!pi_prefill_shape_ok(L->d, L->f)) return false;
+    if (L->qtype == PI_QT_Q4_0 ? !pi_prefill_shape_ok(L->d, L->f) : !pi_prefill_q8_shape_ok(L->d, L->f)) return false;
     static const int force = [] {
         const char* v = std::getenv("PI_PREFILL");
         return v ? (v[0] == '1' ? 1 : 0) : -1;
@@ -1592,14 +1604,14 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hs = b.take<float>(slots * (F / 32));
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
-    if (use_gemm(L, T, flags)) {
+    if (use_gemm(L, T, flags) && L->qtype == PI_QT_Q4_0) {
         f.xh = f.xl = nullptr;
         f.hh = b.take<__half>(slots * F);
         f.hl = b.take<__half>(slots * F);
     } else {
         f.xh = f.xl = f.hh = f.hl = nullptr;
     }
-    if (use_router_tc(L, T) || use_gemm(L, T, flags)) {
+    if (use_router_tc(L, T) || (use_gemm(L, T, flags) && L->qtype == PI_QT_Q4_0)) {
         f.xth = b.take<__half>(T * d);
         f.xtl = b.take<__half>(T * d);
         f.xnorm = b.take<float>(T);
@@ -1680,7 +1692,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
 
     if (do_norm || (q8 && !route_only)) {
         PiProfScope ps(ctx, st, "k_prep");
-        k_prep<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, d, do_norm, 1e-6f, B.normed,
+        k_prep<<<(unsigned)T, 256, sizeof(float) * d, st>>>(x, d, do_norm, 1e-6f, B.normed,
                                                                           (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
@@ -1763,7 +1775,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     }
     }
     const bool gemm = !route_only && use_gemm(L, T, flags);
-    const int tg = gemm ? PI_GEMM_NT : TG;
+    const int tg = gemm ? (q8 ? PI_GEMM_NT_Q8 : PI_GEMM_NT) : TG;
     {
         PiProfScope ps(ctx, st, "k_dispatch");
         k_dispatch<<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
@@ -1799,6 +1811,14 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.hf = B.hf;
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T);
+    if (gemm && q8) {
+        if (int rc = pi_prefill_experts_q8(ctx, L, a, ni, st)) return rc;
+        PiProfScope ps(ctx, st, "k_combine");
+        k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
+            x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,
+            out);
+        return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
+    }
     if (gemm) {
         const int64_t n_slots = T * k + (L->has_shared ? T : 0);
         if (!use_router_tc(L, T)) {  // the router did not split the tokens

@@ -27,13 +27,12 @@
 // 32(w%4)..+31, one weight row per thread) and writes SwiGLU h as f16 hi/lo
 // (gate/up) or y (down). All mbarrier waits are bounded (1 s) and report
 // PI_DEVERR_TIMEOUT.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include "pi_common.cuh"
+#include "pi_tc.cuh"
+// pi_tc.cuh (pi_common.cuh) comes first: it names the quant types that pi_moe.h defines as macros
 #include "pi_internal.h"
 
 namespace {
+using namespace pitc;
 
 constexpr int NTMAX = PI_GEMM_NT;  // slots per item (max MMA N)
 constexpr int MT = 128;            // weight rows per m-tile (MMA M)
@@ -42,106 +41,6 @@ constexpr int WTILE = MT * 64;     // 128 rows x 64 bytes
 constexpr int XTILE = NTMAX * 64;  // 256 rows x 64 bytes
 constexpr int RAWQ = MT * 16;      // raw nibbles of one matrix per chunk
 constexpr int RAWD = MT * 16;      // raw scales of one matrix per 8 chunks
-
-PI_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-PI_DEV uint64_t globaltimer_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-PI_DEV void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-// true once the phase with this parity completed; false after ~1 s
-PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    uint64_t t0 = 0;
-    for (uint32_t i = 0;; ++i) {
-        uint32_t done;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(done)
-            : "r"(a), "r"(parity)
-            : "memory");
-        if (done) return true;
-        if ((i & 255) == 0) {
-            const uint64_t now = globaltimer_ns();
-            if (i == 0) t0 = now;
-            else if (now - t0 > 1000000000ull) return false;
-        }
-    }
-}
-
-// UMMA shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms of 512
-// bytes (SBO = 512), version 1 (sm_100). A k16 step inside the 64-byte row
-// advances the start address by 32 bytes.
-PI_DEV uint64_t umma_desc(const void* tile, uint32_t byte_offset) {
-    const uint32_t a = smem_u32(tile) + byte_offset;
-    uint64_t d = (uint64_t)((a >> 4) & 0x3FFF);
-    d |= (uint64_t)1 << 16;           // LBO (unused for swizzled K-major)
-    d |= (uint64_t)(512 >> 4) << 32;  // SBO
-    d |= (uint64_t)1 << 46;           // version
-    d |= (uint64_t)4 << 61;           // SWIZZLE_64B
-    return d;
-}
-// instruction descriptor: f16 x f16 -> f32, both K-major, M = 128, N = n (16..256, n % 16 == 0)
-PI_DEV uint32_t idesc(int n) { return (1u << 4) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(MT >> 4) << 24); }
-
-PI_DEV void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t id, uint32_t accumulate) {
-    asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(id), "r"(accumulate)
-        : "memory");
-}
-PI_DEV void mma_commit(uint64_t* bar) {
-    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-                 : "memory");
-}
-PI_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-PI_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-PI_DEV void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-PI_DEV void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-PI_DEV void mbar_arrive(uint64_t* bar) {
-    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-// tiled TMA loads (no multicast) completing on an mbarrier
-PI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-            smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-PI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-        "[%6];" ::"r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
-        : "memory");
-}
-
-// 32 consecutive f32 accumulator columns of this thread's TMEM lane
-PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-        "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// swizzled position of 16-byte chunk c (0..3) of row r in a K-major SW64 tile
-PI_DEV int swz(int r, int c) { return r * 64 + ((c ^ ((r >> 1) & 3)) << 4); }
 
 // 16 elements of one Q4_0 block (8 nibble bytes: part p = 0/1 of the block)
 // -> swizzled 16-byte chunks 2p, 2p+1 of row r in the hi and lo tiles.
@@ -438,27 +337,6 @@ __global__ __launch_bounds__(GT, 1) void k_moe_gemm(ExpertArgs a, const __grid_c
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TCOLS) : "memory");
-}
-
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
-        void* p = nullptr;
-        cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) != cudaSuccess ||
-            q != cudaDriverEntryPointSuccess)
-            p = nullptr;
-        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-    }();
-    return fn;
-}
-
-bool encode(CUtensorMap* m, CUtensorMapDataType ty, int rank, const void* base, const cuuint64_t* dims,
-            const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle swz) {
-    auto fn = encode_fn();
-    if (!fn) return false;
-    const cuuint32_t es[4] = {1, 1, 1, 1};
-    return fn(m, ty, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
-              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // f16 [rows][cols] row-major activations, box {32 columns, 256 rows}, 64-byte

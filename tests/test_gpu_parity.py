@@ -313,6 +313,36 @@ def test_c3_prefill_gemm_vs_gemv(pkg, torch, c3_layer, T):
     assert int(r["counts"].max()) > 128
 
 
+@pytest.mark.parametrize("T", [40, 300])
+def test_q8_prefill_gemm_bit_exact(pkg, orc, torch, T):
+    """Q8_0 prefill GEMM (int8 block sums exact on the tensor cores, scales in
+    block order, SwiGLU and Q8_0 h in the epilogue) is bit-exact with the
+    reference restatement. A top-1 layer makes the renormalised gate exactly 1,
+    so the layer output is the expert FFN output itself; T = 300 also takes the
+    tensor-core router and multi-item experts."""
+    from powerinfer_x64_b200 import moe
+
+    rng = np.random.default_rng(21)
+    d, E, k, f = 1024, 8, 1, 256
+    router = (rng.standard_normal(E * d) * 0.02).astype(np.float32)
+    g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
+    x = rng.standard_normal((T, d)).astype(np.float32)
+    L = moe.MoeLayer(router, g, u, dn, 8, d, f, E, k)
+    got = L.forward(torch.from_numpy(x).cuda(), path="gemm").cpu().numpy()
+    ref = orc.moe_layer(x, d, f, E, k, 8, router, g, u, dn, threads=1)
+    close(got, ref)
+    assert np.array_equal(bits(got), bits(ref)), f"{np.count_nonzero(bits(got) != bits(ref))} outputs differ"
+
+
+def test_q8_prefill_gemm_vs_gemv(pkg, torch, c2_layer):
+    """A batch large enough for multi-item experts: GEMM and GEMV paths agree."""
+    from powerinfer_x64_b200 import synth
+
+    L, _ = c2_layer
+    x = synth.tokens_dev(synth.C2.d, 1024, seed=12)
+    close(L.forward(x, path="gemm").cpu().numpy(), L.forward(x, path="gemv").cpu().numpy())
+
+
 def test_c5_rmsnorm_residual_teacher_forced(pkg, orc, torch):
     """Two layers of the C5 stack: each GPU layer gets the oracle's previous output."""
     from powerinfer_x64_b200 import synth
