@@ -1574,9 +1574,13 @@ bool use_gemm(const pi_moe_layer* L, int64_t T, int flags) {
     return T >= 128;
 }
 
-int64_t max_items(const pi_moe_layer* L, int64_t T) {
+// Upper bound of the work items k_dispatch writes for item size tg: one partial
+// item per used expert plus full ones, and the shared expert's items. The expert
+// kernels launch this many CTA rows; rows past the realised count exit at once,
+// so the bound is kept tight (each launched CTA occupies an SM while it checks).
+int64_t max_items(const pi_moe_layer* L, int64_t T, int tg) {
     const int64_t Tk = T * L->k;
-    return std::min<int64_t>(L->E, Tk) + (Tk + TG - 1) / TG + (L->has_shared ? (T + TG - 1) / TG : 0) + 1;
+    return std::min<int64_t>(L->E, Tk) + Tk / tg + (L->has_shared ? (T + tg - 1) / tg : 0) + 1;
 }
 
 FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
@@ -1598,7 +1602,7 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.offsets = b.take<int32_t>(E);
     f.perm = b.take<int32_t>(T * k);
     f.slot_of = b.take<int32_t>(T * k);
-    f.items = b.take<int4>(max_items(L, T));
+    f.items = b.take<int4>(max_items(L, T, TG));  // TG is the smallest item size
     f.n_items = b.take<int32_t>(1);
     f.hq = b.take<int8_t>(slots * F);
     f.hs = b.take<float>(slots * (F / 32));
@@ -1810,7 +1814,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.hs = B.hs;
     a.hf = B.hf;
     a.y = B.y;
-    const unsigned ni = (unsigned)max_items(L, T);
+    const unsigned ni = (unsigned)max_items(L, T, tg);
     if (gemm && q8) {
         if (int rc = pi_prefill_experts_q8(ctx, L, a, ni, st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
