@@ -238,7 +238,7 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
         if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->gate_sh, &L->allocs);
         if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->up_sh, &L->allocs);
     }
-    if (!rc) rc = pi_prefill_prepare(ctx, L);
+    if (!rc) rc = L->qtype == PI_QT_Q8_0 ? pi_prefill_prepare_q8(ctx, L) : pi_prefill_prepare(ctx, L);
     if (rc) {
         pi_moe_layer_destroy(L);
         return rc;

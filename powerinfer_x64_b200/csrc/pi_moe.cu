@@ -1816,7 +1816,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     a.y = B.y;
     const unsigned ni = (unsigned)max_items(L, T, tg);
     if (gemm && q8) {
-        if (int rc = pi_prefill_experts_q8(ctx, L, a, ni, st)) return rc;
+        if (int rc = pi_prefill_experts_q8(ctx, L, a, ni, T, T * k + (L->has_shared ? T : 0), st)) return rc;
         PiProfScope ps(ctx, st, "k_combine");
         k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
             x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,

@@ -16,14 +16,19 @@
 // the reference's ffn_swiglu_q does before its down matvec (quant/mod.rs:1184-1249);
 // the down kernel writes y.
 //
-// Warp roles (QT = 672 threads, one CTA per SM):
+// Data movement (TMA, no multicast) runs in groups of 4 blocks (128 K bytes):
+// weight rows of both lane-tiled layouts as 2-D / 4-D boxes, the gate/up
+// token rows by tile::gather4 from the token-major Q8_0 activations, the down
+// kernel's slot-major h rows as one box.
+//
+// Warp roles (QT = 832 threads, one CTA per SM):
 //   0-15  epilogue: warp w owns TMEM lanes 32 (w % 4) .. +31 (weight rows) and
 //         slot columns 32 (w / 4) .. +31;
-//   16-19 converters: thread c fetches weight row c and slot row c of block
-//         g + RQ - 1 with cp.async, converts block g to f16 tiles (64-byte
-//         swizzled K-major) and publishes the block's scales;
-//   20    MMA issuer.
-// Every mbarrier wait is bounded (1 s) and reports PI_DEVERR_TIMEOUT.
+//   16-23 converters: thread c < 128 converts weight row c, c >= 128 slot row
+//         c - 128, of each block from the raw group into an f16 tile row
+//         (64-byte swizzled K-major) and publishes the row's block scale;
+//   24    MMA issuer;  25 TMA producer.
+// Every mbarrier wait is bounded and reports PI_DEVERR_TIMEOUT.
 #include "pi_tc.cuh"
 // pi_tc.cuh (pi_common.cuh) comes first: it names the quant types that pi_moe.h defines as macros
 #include "pi_internal.h"
@@ -32,14 +37,16 @@ namespace {
 using namespace pitc;
 
 constexpr int QN = PI_GEMM_NT_Q8;  // slots per item (max MMA N)
-constexpr int NEPI = 16, NCONV = 4;
-constexpr int QT = (NEPI + NCONV + 1) * 32;
-constexpr int RQ = 8;              // raw blocks in flight per converter thread
+constexpr int NEPI = 16, NCONV = 8;
+constexpr int QT = (NEPI + NCONV + 2) * 32;
+constexpr int G4 = 4;              // blocks per raw group
+constexpr int RG = 3;              // raw groups in flight
 constexpr int TS = 3;              // f16 tile stages
 constexpr int DB = 4;              // TMEM block buffers of QN columns
 constexpr int TILE = 128 * 64;     // 128 rows x 32 f16
-constexpr int RAW = 128 * 32 * 2 + 128 * 4 * 2;  // W and X int8 rows, W scale pair, X scale
-constexpr size_t QSMEM = (size_t)RQ * RAW + (size_t)TS * 2 * TILE + 1024;
+constexpr int RAWW = 128 * G4 * 32;  // weight rows of a group (16 KB)
+constexpr int RAWG = 2 * RAWW;       // + activation rows
+constexpr size_t QSMEM = (size_t)RG * RAWG + (size_t)TS * 2 * TILE + 1024;
 
 // 32 int8 (two 16-byte words) -> 32 exact f16 in swizzled row r of a SW64 tile:
 // 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128, so subtracting 1152 gives b.
@@ -62,22 +69,18 @@ PI_DEV void int8_row_to_f16(const uint4 a, const uint4 b, uint8_t* tile, int r) 
     }
 }
 
-PI_DEV void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-PI_DEV void cp_async4(void* dst, const void* src) {
-    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-
 // MODE 0: gate/up (+ SwiGLU, Q8_0 h); MODE 1: down (y).
 template <int MODE>
-__global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* err) {
+__global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
+                                                       const __grid_constant__ CUtensorMap mx, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* tiles = sm;                    // TS stages of {W tile, X tile}
-    uint8_t* raws = sm + TS * 2 * TILE;     // RQ stages of raw int8 rows and scales
+    uint8_t* tiles = sm;                 // TS stages of {W tile, X tile}
+    uint8_t* raws = sm + TS * 2 * TILE;  // RG groups of {W rows, X rows}
     __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[DB];
-    __shared__ float s_dw[DB][128], s_dx[DB][QN];
+    __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG];
+    __shared__ __align__(16) float s_dw[DB][128];
+    __shared__ __align__(16) float s_dx[DB][QN];
     __shared__ uint32_t s_tmem;
     __shared__ int s_row[QN];  // gate/up: token of each slot column; down: slot
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -86,7 +89,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
     const int4 item = a.items[it];
     const bool sh = item.x == a.E;
     const int K = MODE == 0 ? a.d : a.f;
-    const int nb = K / 32;
+    const int nb = K / 32, ng = nb / G4;
     const int nn = (item.z + 15) & ~15;
 
     if (tid == 0) {
@@ -98,6 +101,10 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
             mbar_init(&d_full[i], 1);
             mbar_init(&d_free[i], NEPI);
             mbar_init(&scl_full[i], NCONV);
+        }
+        for (int i = 0; i < RG; ++i) {
+            mbar_init(&raw_full[i], 1);
+            mbar_init(&raw_free[i], NCONV);
         }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
@@ -116,84 +123,109 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     bool ok = true;
+    const int mrow = sh ? 0 : item.x * (MODE == 0 ? a.f : a.d);  // expert's first row in its family
 
-    if (warp >= NEPI && warp < NEPI + NCONV) {
-        // ---- converters: thread c owns weight row c and slot row c ----
-        const int c = tid - NEPI * 32;
-        const size_t mat = sh ? 0 : (size_t)item.x * (MODE == 0 ? a.f : a.d);
-        const int8_t* wq;
-        const __half* wd;
-        int wr;  // row within the family (all experts)
-        if (MODE == 0) {
-            const bool up = c >= 64;
-            wq = (const int8_t*)(up ? (sh ? a.us : a.u) : (sh ? a.gs : a.g));
-            wd = up ? (sh ? a.usd : a.ud) : (sh ? a.gsd : a.gd);
-            wr = (int)mat + blockIdx.x * 64 + (c & 63);
-        } else {
-            wq = (const int8_t*)(sh ? a.dns : a.dn);
-            wd = sh ? a.dsd : a.dd;
-            wr = (int)mat + blockIdx.x * 128 + c;
-        }
-        const int xrow = s_row[c];
-        auto issue = [&](int g) {
-            uint8_t* rs = raws + (g % RQ) * RAW;
-            const int8_t* p0;
-            const int8_t* p1;
-            if (MODE == 0) {
-                // lane-tiled gate/up rows: half h of block B at ((B/32)*64 + h*32 + B%32) * 16 bytes
-                const int8_t* row = wq + (size_t)wr * a.d;
-                p0 = row + (size_t)((g >> 5) * 64 + (g & 31)) * 16;
-                p1 = p0 + 512;
-            } else {
-                // lane-tiled down rows: 16-byte chunk j of row r at ((r/8)*8*nch + (j%cpq)*32 + (r%8)*4 + j/cpq) * 16
-                const int nch = a.f / 16, cpq = nch / 4, j = 2 * g;
-                const size_t base = (size_t)(wr >> 3) * 8 * nch + (size_t)(wr & 7) * 4 + j / cpq;
-                p0 = wq + (base + (size_t)(j % cpq) * 32) * 16;
-                p1 = wq + (base + (size_t)(j % cpq + 1) * 32) * 16;
+    if (warp == NEPI + NCONV + 1) {
+        // ---- TMA producer: group q -> raw slot q % RG once the converters released q - RG ----
+        for (int q = 0; q < ng; ++q) {
+            const int slot = q % RG, use = q / RG;
+            int w_ok = 1;
+            if (lane == 0) {
+                if (use > 0 && !mbar_wait(&raw_free[slot], (use - 1) & 1)) w_ok = 0;
+                else mbar_expect_tx(&raw_full[slot], RAWG);
             }
-            cp_async16(rs + c * 32, p0);
-            cp_async16(rs + c * 32 + 16, p1);
-            cp_async4(rs + 2 * 128 * 32 + c * 4, wd + (size_t)wr * nb + (g & ~1));  // scale pair
+            if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
+            uint8_t* rw = raws + slot * RAWG;
+            uint8_t* rx = rw + RAWW;
             if (MODE == 0) {
-                const int8_t* xr = a.xq + (size_t)xrow * a.d + g * 32;
-                cp_async16(rs + 128 * 32 + c * 32, xr);
-                cp_async16(rs + 128 * 32 + c * 32 + 16, xr + 16);
-                cp_async4(rs + 2 * 128 * 32 + 512 + c * 4, a.xs + (size_t)xrow * nb + g);
+                if (lane == 0) {
+                    // lane-tiled gate/up rows: half h of block B at ((B/32)*64 + h*32 + B%32) * 16 bytes,
+                    // so the first halves of blocks 4q..4q+3 are 64 contiguous bytes, the second ones +512
+                    const int b0 = G4 * q, x0 = ((b0 >> 5) * 64 + (b0 & 31)) * 16;
+                    const int r0 = mrow + blockIdx.x * 64;
+                    const CUtensorMap* mg = sh ? &wm.q[1][0] : &wm.q[0][0];
+                    const CUtensorMap* mu = sh ? &wm.q[1][1] : &wm.q[0][1];
+                    tma_load_2d(rw, mg, x0, r0, &raw_full[slot]);
+                    tma_load_2d(rw + 64 * 64, mg, x0 + 512, r0, &raw_full[slot]);
+                    tma_load_2d(rw + 2 * 64 * 64, mu, x0, r0, &raw_full[slot]);
+                    tma_load_2d(rw + 3 * 64 * 64, mu, x0 + 512, r0, &raw_full[slot]);
+                }
+                __syncwarp();
+                const int* tk = &s_row[4 * lane];  // 32 lanes x 4 rows = the 128 slot rows
+                tma_gather4(rx + lane * 4 * 128, &mx, q * 128, tk[0], tk[1], tk[2], tk[3], &raw_full[slot]);
+            } else if (lane == 0) {
+                // lane-tiled down rows: chunk j of row r at ((r/8)*8*nch + (j%cpq)*32 + (r%8)*4 + j/cpq) * 16,
+                // blocks 4q..4q+3 = chunks 8q..8q+7 = all j%cpq with j/cpq = q (cpq = 8)
+                const CUtensorMap* md = sh ? &wm.q[1][2] : &wm.q[0][2];
+                tma_load_4d(rw, md, q * 16, 0, 0, (mrow + blockIdx.x * 128) >> 3, &raw_full[slot]);
+                tma_load_2d(rx, &mx, q * 128, item.y, &raw_full[slot]);
+            }
+        }
+    } else if (warp >= NEPI && warp < NEPI + NCONV) {
+        // ---- converters: thread c < 128 converts weight row c, c >= 128 slot row c - 128 ----
+        const int c = tid - NEPI * 32, row = c & 127;
+        const bool isx = c >= 128;
+        // this row's block scales, 4 per group, loaded one group ahead
+        const void* scp;
+        if (!isx) {
+            const __half* wd;
+            int wr;
+            if (MODE == 0) {
+                const bool up = row >= 64;
+                wd = up ? (sh ? a.usd : a.ud) : (sh ? a.gsd : a.gd);
+                wr = mrow + blockIdx.x * 64 + (row & 63);
             } else {
-                const int8_t* hr = a.hq + (size_t)xrow * a.f + g * 32;
-                cp_async16(rs + 128 * 32 + c * 32, hr);
-                cp_async16(rs + 128 * 32 + c * 32 + 16, hr + 16);
-                cp_async4(rs + 2 * 128 * 32 + 512 + c * 4, a.hs + (size_t)xrow * nb + g);
+                wd = sh ? a.dsd : a.dd;
+                wr = mrow + blockIdx.x * 128 + row;
+            }
+            scp = wd + (size_t)wr * nb;
+        } else {
+            scp = (MODE == 0 ? a.xs + (size_t)s_row[row] * nb : a.hs + (size_t)s_row[row] * nb);
+        }
+        auto load_sc = [&](int q, float (&v)[G4]) {
+            if (isx) {
+                const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(scp) + G4 * q);
+                v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+            } else {
+                const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(scp) + G4 * q);
+                const __half2 h0 = *reinterpret_cast<const __half2*>(&h.x), h1 = *reinterpret_cast<const __half2*>(&h.y);
+                v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
             }
         };
-        for (int g = 0; g < RQ - 1 && g < nb; ++g) {
-            issue(g);
-            asm volatile("cp.async.commit_group;" ::: "memory");
-        }
-        for (int g = 0; g < nb; ++g) {
-            if (g + RQ - 1 < nb) issue(g + RQ - 1);
-            asm volatile("cp.async.commit_group;" ::: "memory");
-            asm volatile("cp.async.wait_group %0;" ::"n"(RQ - 1) : "memory");
-            const int ts = g % TS, db = g % DB;
-            if (g >= TS && !mbar_wait(&tile_free[ts], (g / TS - 1) & 1)) { ok = false; break; }
-            if (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1)) { ok = false; break; }
-            const uint8_t* rs = raws + (g % RQ) * RAW;
-            uint8_t* wt = tiles + ts * 2 * TILE;
-            int8_row_to_f16(*reinterpret_cast<const uint4*>(rs + c * 32), *reinterpret_cast<const uint4*>(rs + c * 32 + 16),
-                            wt, c);
-            int8_row_to_f16(*reinterpret_cast<const uint4*>(rs + 128 * 32 + c * 32),
-                            *reinterpret_cast<const uint4*>(rs + 128 * 32 + c * 32 + 16), wt + TILE, c);
-            const __half2 dpair = *reinterpret_cast<const __half2*>(rs + 2 * 128 * 32 + c * 4);
-            s_dw[db][c] = __half2float((g & 1) ? __high2half(dpair) : __low2half(dpair));
-            s_dx[db][c] = *reinterpret_cast<const float*>(rs + 2 * 128 * 32 + 512 + c * 4);
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&tile_full[ts]);
-                mbar_arrive(&scl_full[db]);
+        // raw position of this row's 32 bytes of block i (two 16-byte halves)
+        auto raw_half = [&](const uint8_t* rg, int i, int h) -> const uint8_t* {
+            if (isx) return rg + RAWW + row * 128 + 32 * i + 16 * h;
+            if (MODE == 0) return rg + (row >> 6) * 2 * 64 * 64 + h * 64 * 64 + (row & 63) * 64 + 16 * i;
+            return rg + (row >> 3) * 1024 + (2 * i + h) * 128 + (row & 7) * 16;  // [r/8][chunk][r%8][16 B]
+        };
+        float sc_cur[G4], sc_nxt[G4];
+        load_sc(0, sc_cur);
+        for (int q = 0; q < ng && ok; ++q) {
+            const int slot = q % RG;
+            if (q + 1 < ng) load_sc(q + 1, sc_nxt);
+            if (!mbar_wait(&raw_full[slot], (q / RG) & 1)) { ok = false; break; }
+            const uint8_t* rg = raws + slot * RAWG;
+#pragma unroll
+            for (int i = 0; i < G4; ++i) {
+                const int g = G4 * q + i, ts = g % TS, db = g % DB;
+                if (g >= TS && !mbar_wait(&tile_free[ts], (g / TS - 1) & 1)) { ok = false; break; }
+                if (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1)) { ok = false; break; }
+                int8_row_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, 0)),
+                                *reinterpret_cast<const uint4*>(raw_half(rg, i, 1)),
+                                tiles + ts * 2 * TILE + (isx ? TILE : 0), row);
+                (isx ? s_dx[db] : s_dw[db])[row] = sc_cur[i];
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    mbar_arrive(&tile_full[ts]);
+                    mbar_arrive(&scl_full[db]);
+                }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&raw_free[slot]);
+#pragma unroll
+            for (int i = 0; i < G4; ++i) sc_cur[i] = sc_nxt[i];
         }
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
     } else if (warp == NEPI + NCONV) {
         // ---- MMA issuer ----
         if (lane == 0) {
@@ -216,9 +248,9 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
         }
     } else {
         // ---- epilogue: rows 32 (w % 4) + lane, slot columns 32 (w / 4) .. +31 ----
-        const int q = warp & 3, cg = warp >> 2, rl = 32 * q + lane;
+        const int q4 = warp & 3, cg = warp >> 2, rl = 32 * q4 + lane;
         const bool live = 32 * cg < item.z;
-        const uint32_t lane_base = (uint32_t)(32 * q) << 16;
+        const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
         float acc[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
@@ -230,11 +262,21 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
             }
             tc_fence_after();
             if (live) {
-                float v[32];
-                tmem_ld32(tmem + lane_base + db * QN + 32 * cg, v);
                 const float dw = s_dw[db][rl];
 #pragma unroll
-                for (int j = 0; j < 32; ++j) acc[j] = fadd(acc[j], fmul(v[j], fmul(dw, s_dx[db][32 * cg + j])));
+                for (int hh = 0; hh < 2; ++hh) {
+                    float v[16];
+                    tmem_ld16(tmem + lane_base + db * QN + 32 * cg + 16 * hh, v);
+#pragma unroll
+                    for (int j4 = 0; j4 < 4; ++j4) {
+                        const float4 dx = *reinterpret_cast<const float4*>(&s_dx[db][32 * cg + 16 * hh + 4 * j4]);
+                        float* ac = &acc[16 * hh + 4 * j4];
+                        ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw, dx.x)));
+                        ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw, dx.y)));
+                        ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw, dx.z)));
+                        ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw, dx.w)));
+                    }
+                }
             }
             tc_fence_before();
             __syncwarp();
@@ -244,13 +286,13 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
             // up rows (quarters 2, 3) hand their sums to the gate rows through shared memory
             float* s_up = reinterpret_cast<float*>(raws);  // the raw ring is idle now
             asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
-            if (q >= 2 && live) {
+            if (q4 >= 2 && live) {
 #pragma unroll
-                for (int j = 0; j < 32; ++j) s_up[(32 * (q - 2) + lane) * (QN + 1) + 32 * cg + j] = acc[j];
+                for (int j = 0; j < 32; ++j) s_up[(32 * (q4 - 2) + lane) * (QN + 1) + 32 * cg + j] = acc[j];
             }
             asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
-            if (q < 2 && live) {
-                const int f0 = blockIdx.x * 64 + 32 * q;  // first h row of this warp = one Q8_0 block
+            if (q4 < 2 && live) {
+                const int f0 = blockIdx.x * 64 + 32 * q4;  // first h row of this warp = one Q8_0 block
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     const int col = 32 * cg + j;
@@ -278,17 +320,62 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, uint32_t* e
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * QN) : "memory");
 }
 
+// Q8_0 weight rows for the TMA producer: gate/up [rows][d] bytes (box 64 B x 64 rows),
+// lane-tiled down rows as {64 B, 8, cpq, rows/8} (box {16, 8, cpq, 16}).
+bool q8_gateup_map(CUtensorMap* m, const PiMats& w) {
+    const cuuint64_t dims[2] = {(cuuint64_t)w.cols, (cuuint64_t)(w.n * w.rows)};
+    const cuuint64_t strides[1] = {(cuuint64_t)w.cols};
+    const cuuint32_t box[2] = {64, 64};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+bool q8_down_map(CUtensorMap* m, const PiMats& w) {
+    const int64_t rows = w.n * w.rows, nch = w.cols / 16, cpq = nch / 4;
+    const cuuint64_t dims[4] = {64, 8, (cuuint64_t)cpq, (cuuint64_t)(rows / 8)};
+    const cuuint64_t strides[3] = {64, 512, (cuuint64_t)(8 * nch * 16)};
+    const cuuint32_t box[4] = {16, 8, (cuuint32_t)cpq, 16};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+// int8 activations [rows][cols]: gate/up gathers 128-byte rows (box one row high),
+// down loads 128 slot rows x 128 bytes
+bool q8_act_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t cols, int box_rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)cols};
+    const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 }  // namespace
 
-bool pi_prefill_q8_shape_ok(int64_t d, int64_t f) { return d % 1024 == 0 && f % 64 == 0 && d % 128 == 0; }
+bool pi_prefill_q8_shape_ok(int64_t d, int64_t f) {
+    // gate/up lane tiling needs d % 1024; down: 8 chunks per quarter row (f = 512) so that a
+    // 4-block group is one 4-D box; 64-row gate/up and 128-row down tiles
+    return d % 1024 == 0 && f == 512 && d % 128 == 0;
+}
 
-int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items,
-                          cudaStream_t st) {
+int pi_prefill_prepare_q8(pi_ctx* ctx, pi_moe_layer* L) {
+    L->maps_ok = false;
+    if (L->qtype != PI_QT_Q8_0 || !pi_prefill_q8_shape_ok(L->d, L->f)) return PI_OK;
+    PiPrefillMaps& M = L->maps;
+    bool ok = q8_gateup_map(&M.q[0][0], L->gate) && q8_gateup_map(&M.q[0][1], L->up) && q8_down_map(&M.q[0][2], L->down);
+    if (ok && L->has_shared)
+        ok = q8_gateup_map(&M.q[1][0], L->gate_sh) && q8_gateup_map(&M.q[1][1], L->up_sh) &&
+             q8_down_map(&M.q[1][2], L->down_sh);
+    if (!ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed for the weights");
+    L->maps_ok = true;
+    return PI_OK;
+}
+
+int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t T,
+                          int64_t n_slots, cudaStream_t st) {
     if (L->qtype != PI_QT_Q8_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: Q8_0 weights only");
     if (!pi_prefill_q8_shape_ok(a.d, a.f) || (L->has_shared && L->f_sh != L->f))
         return pi_set_error(ctx, PI_ERR_ARG,
-                            "prefill Q8_0 GEMM: n_embd must be a multiple of 1024, expert widths equal and a multiple of 64");
-    static_assert((size_t)RQ * RAW >= (size_t)64 * (QN + 1) * 4, "the up-row exchange fits in the raw ring");
+                            "prefill Q8_0 GEMM: n_embd must be a multiple of 1024 and the expert widths 512");
+    if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: weight tensor maps unavailable");
+    static_assert((size_t)RG * RAWG >= (size_t)64 * (QN + 1) * 4, "the up-row exchange fits in the raw ring");
+    CUtensorMap mxg, mhq;
+    if (!q8_act_map(&mxg, a.xq, T, a.d, 1) || !q8_act_map(&mhq, a.hq, n_slots, a.f, 128))
+        return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
     static bool attr = false;
     if (!attr) {
         cudaFuncSetAttribute(k_moe_gemm_q8<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
@@ -297,11 +384,13 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
-        k_moe_gemm_q8<0><<<dim3((unsigned)(a.f / 64), (unsigned)max_items), QT, QSMEM, st>>>(a, ctx->dev_err);
+        k_moe_gemm_q8<0><<<dim3((unsigned)(a.f / 64), (unsigned)max_items), QT, QSMEM, st>>>(a, L->maps, mxg,
+                                                                                           ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_down");
-        k_moe_gemm_q8<1><<<dim3((unsigned)(a.d / 128), (unsigned)max_items), QT, QSMEM, st>>>(a, ctx->dev_err);
+        k_moe_gemm_q8<1><<<dim3((unsigned)(a.d / 128), (unsigned)max_items), QT, QSMEM, st>>>(a, L->maps, mhq,
+                                                                                            ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill Q8_0 GEMM") ? PI_ERR_CUDA : PI_OK;
 }

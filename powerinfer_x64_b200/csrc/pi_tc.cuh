@@ -18,10 +18,12 @@ PI_DEV uint64_t globaltimer_ns() {
 PI_DEV void mbar_init(uint64_t* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
-// true once the phase with this parity completed; false after ~1 s
+// true once the phase with this parity completed; false after about a second
+// (2^31 SM cycles: the SM's own cycle counter is cheap to read, unlike the
+// global timer, so the bound costs nothing on the fast path)
 PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
-    uint64_t t0 = 0;
+    long long t0 = 0;
     for (uint32_t i = 0;; ++i) {
         uint32_t done;
         asm volatile(
@@ -30,10 +32,10 @@ PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
             : "r"(a), "r"(parity)
             : "memory");
         if (done) return true;
-        if ((i & 255) == 0) {
-            const uint64_t now = globaltimer_ns();
+        if ((i & 1023) == 0) {
+            const long long now = clock64();
             if (i == 0) t0 = now;
-            else if (now - t0 > 1000000000ull) return false;
+            else if (now - t0 > (1ll << 31)) return false;
         }
     }
 }
@@ -81,6 +83,14 @@ PI_DEV void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
+// four rows (y0..y3) of a box one row high, landing as consecutive rows at dst
+PI_DEV void tma_gather4(void* dst, const CUtensorMap* map, int x, int y0, int y1, int y2, int y3, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+        "%4, %5, %6}], [%7];" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3), "r"(smem_u32(bar))
+        : "memory");
+}
 PI_DEV void tma_load_4d(void* dst, const CUtensorMap* map, int x, int y, int z, int w, uint64_t* bar) {
     asm volatile(
         "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
@@ -103,6 +113,18 @@ PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+// 16 consecutive f32 accumulator columns of this thread's TMEM lane
+PI_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+    uint32_t r[16];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 // swizzled position of 16-byte chunk c (0..3) of row r in a K-major SW64 tile

@@ -323,7 +323,7 @@ def test_q8_prefill_gemm_bit_exact(pkg, orc, torch, T):
     from powerinfer_x64_b200 import moe
 
     rng = np.random.default_rng(21)
-    d, E, k, f = 1024, 8, 1, 256
+    d, E, k, f = 1024, 8, 1, 512
     router = (rng.standard_normal(E * d) * 0.02).astype(np.float32)
     g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
     x = rng.standard_normal((T, d)).astype(np.float32)
