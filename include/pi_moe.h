@@ -178,6 +178,48 @@ int pi_moe_route(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, in
 int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, float* out, int32_t flags,
                    void* stream);
 
+/* ---- Expert parallelism (config 5: experts sharded over the GPUs of a box) ----
+ * No reference counterpart: the reference runs the whole layer in one process
+ * (model/mod.rs:1245-1571). These calls split pi_moe_forward into the stages
+ * around the two exchanges, which the caller performs (NCCL all-to-all-v, or
+ * any transport); the result equals pi_moe_forward on the same tokens bit for
+ * bit, because every expert row and the combine order are unchanged.
+ *
+ * A layer for rank r of `world` holds experts [first_expert, first_expert +
+ * n_local) with n_local = E / world and first_expert = r * n_local; desc->
+ * gate/up/down_exps then hold those n_local experts (GGUF bytes), the router,
+ * bias and shared expert are the full ones. Q8_0 experts only. */
+int pi_moe_layer_create_ep(pi_ctx* ctx, const pi_moe_layer_desc* desc, int32_t first_expert, int32_t n_local,
+                           pi_moe_layer** out);
+
+/* Stage 1, on every rank for its home tokens x [T][d]: RMSNorm (flags), Q8_0
+ * quantisation and routing, then the send layout. Slot (t, j) (expert idx[t][j])
+ * goes to rank idx / n_local as one row: send_xq [T*k][d] int8, send_xs
+ * [T*k][d/32] f32 (token t's Q8_0 activations), send_eid [T*k] (expert id local
+ * to the destination); rows are grouped by destination rank (ascending), slot
+ * order within a rank; send_counts [world] rows per rank; slot_row [T*k] the row
+ * of each slot. Also idx/gates [T][k], shscale [T] (shared-expert gate) and the
+ * home tokens' own Q8_0 activations xq [T][d], xs [T][d/32] (for the shared
+ * expert). All device pointers, caller-allocated. */
+int pi_moe_ep_route(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, int32_t flags, int32_t world,
+                    int32_t* idx, float* gates, float* shscale, int8_t* xq, float* xs, int32_t* send_counts,
+                    int8_t* send_xq, float* send_xs, int32_t* send_eid, int32_t* slot_row, void* stream);
+
+/* Stage 2: expert SwiGLU products of n_rows Q8_0 rows (xq [n][d], xs [n][d/32]):
+ * y [n][d] f32, row i through the held expert eid[i] (local id), or through the
+ * shared expert for every row when eid == NULL. Prefill-sized row counts use the
+ * tensor-core GEMM, others the GEMV kernels. */
+int pi_moe_experts_q8(pi_ctx* ctx, pi_moe_layer* layer, int64_t n_rows, const int8_t* xq, const float* xs,
+                      const int32_t* eid, float* y, void* stream);
+
+/* Stage 3, on the home rank: out [T][d] = sum over j (ascending expert) of
+ * gates[t][j] * y_back[slot_row[t*k + j]] + shscale[t] * y_shared[t] (y_shared may
+ * be NULL: no shared expert) + x (PI_FWD_RESIDUAL), in the reference's order
+ * (model/mod.rs:1525-1534, :1627-1633). y_back [T*k][d] are the stage-2 rows sent back. */
+int pi_moe_ep_combine(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, int32_t flags, const float* gates,
+                      const float* shscale, const int32_t* slot_row, const float* y_back, const float* y_shared,
+                      float* out, void* stream);
+
 /* MoeRouter::route of the standalone operator API (src/moe/mod.rs:69-108)
  * for T tokens: router f32 expert-major [E][d] (row e = column e of the
  * reference's row-major [d, E] gate), logits summed sequentially, top-k by

@@ -176,9 +176,11 @@ extern "C" void pi_moe_layer_destroy(pi_moe_layer* L) {
     delete L;
 }
 
-extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_moe_layer** out) {
+static int layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, int e_first, int n_exp, pi_moe_layer** out) {
     if (!ctx || !D || !out) return PI_ERR_ARG;
     *out = nullptr;
+    if (e_first < 0 || n_exp < 1 || e_first + n_exp > D->n_expert)
+        return pi_set_error(ctx, PI_ERR_ARG, "moe layer: held experts must lie in [0, n_expert)");
     if (D->qtype != PI_QT_Q8_0 && D->qtype != PI_QT_Q4_0)
         return pi_set_error(ctx, PI_ERR_ARG, "moe layer: expert weights must be Q8_0 or Q4_0");
     if (D->n_expert < 1 || D->n_expert > 512 || D->n_expert_used < 1 || D->n_expert_used > D->n_expert ||
@@ -197,6 +199,8 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
     L->f = D->n_ff_exp;
     L->f_sh = f_sh;
     L->E = D->n_expert;
+    L->e_first = e_first;
+    L->n_exp = n_exp;
     L->k = D->n_expert_used;
     L->qtype = D->qtype;
     L->has_shared = has_sh;
@@ -224,9 +228,9 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
             rc = PI_ERR_CUDA;
     }
     if (!rc) rc = pi_router_prepare(ctx, L);
-    if (!rc) rc = pi_repack_mats(ctx, &L->gate, D->gate_exps, L->qtype, L->E, L->f, L->d, D->src_on_host, &L->allocs);
-    if (!rc) rc = pi_repack_mats(ctx, &L->up, D->up_exps, L->qtype, L->E, L->f, L->d, D->src_on_host, &L->allocs);
-    if (!rc) rc = pi_repack_mats(ctx, &L->down, D->down_exps, L->qtype, L->E, L->d, L->f, D->src_on_host, &L->allocs);
+    if (!rc) rc = pi_repack_mats(ctx, &L->gate, D->gate_exps, L->qtype, L->n_exp, L->f, L->d, D->src_on_host, &L->allocs);
+    if (!rc) rc = pi_repack_mats(ctx, &L->up, D->up_exps, L->qtype, L->n_exp, L->f, L->d, D->src_on_host, &L->allocs);
+    if (!rc) rc = pi_repack_mats(ctx, &L->down, D->down_exps, L->qtype, L->n_exp, L->d, L->f, D->src_on_host, &L->allocs);
     if (!rc) rc = pi_tile_down_mats(ctx, &L->down, &L->allocs);
     if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->gate, &L->allocs);
     if (!rc && L->qtype == PI_QT_Q8_0) rc = pi_tile_gateup_mats(ctx, &L->up, &L->allocs);
@@ -247,16 +251,73 @@ extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_m
     return PI_OK;
 }
 
+extern "C" int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, pi_moe_layer** out) {
+    return layer_create(ctx, D, 0, D ? D->n_expert : 0, out);
+}
+
+extern "C" int pi_moe_layer_create_ep(pi_ctx* ctx, const pi_moe_layer_desc* D, int32_t first_expert, int32_t n_local,
+                                      pi_moe_layer** out) {
+    if (D && D->qtype != PI_QT_Q8_0 && ctx)
+        return pi_set_error(ctx, PI_ERR_ARG, "expert-parallel layer: Q8_0 experts only");
+    return layer_create(ctx, D, first_expert, n_local, out);
+}
+
 static int moe_common(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags,
                       int32_t* idx, float* gates, int32_t* counts, int32_t* offsets, int32_t* perm, void* stream) {
     if (!ctx || !L) return PI_ERR_ARG;
     if (T < 0 || (T > 0 && !x)) return pi_set_error(ctx, PI_ERR_ARG, "moe: bad token batch");
     if (T == 0) return PI_OK;
     if (T > (1 << 20)) return pi_set_error(ctx, PI_ERR_ARG, "moe: T too large");
+    if (out && L->n_exp != L->E)
+        return pi_set_error(ctx, PI_ERR_ARG, "moe forward: the layer holds a subset of the experts (use the pi_moe_ep_* calls)");
     cudaStream_t st = (cudaStream_t)stream;
     char* scr;
     if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T, flags), &scr)) return rc;
     return pi_moe_run(ctx, L, x, T, out, flags, idx, gates, counts, offsets, perm, scr, st);
+}
+
+extern "C" int pi_moe_ep_route(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int32_t flags, int32_t world,
+                               int32_t* idx, float* gates, float* shscale, int8_t* xq, float* xs, int32_t* send_counts,
+                               int8_t* send_xq, float* send_xs, int32_t* send_eid, int32_t* slot_row, void* stream) {
+    if (!ctx || !L) return PI_ERR_ARG;
+    if (T < 0 || (T > 0 && !x) || world < 1 || world > 64 || L->E % world || L->n_exp != L->E / world ||
+        L->qtype != PI_QT_Q8_0)
+        return pi_set_error(ctx, PI_ERR_ARG, "ep route: Q8_0 layer holding E/world experts, 1 <= world <= 64");
+    if (T > (1 << 20)) return pi_set_error(ctx, PI_ERR_ARG, "ep route: T too large");
+    cudaStream_t st = (cudaStream_t)stream;
+    if (T == 0) {
+        return pi_cuda_check(ctx, cudaMemsetAsync(send_counts, 0, sizeof(int32_t) * world, st), "ep counts")
+                   ? PI_ERR_CUDA
+                   : PI_OK;
+    }
+    const int f = (flags & (PI_FWD_RMSNORM | PI_FWD_RESIDUAL)) | PI_FWD_FORCE_GEMV | PI_FWD_KEEP_Q8;
+    char* scr;
+    // + the send-order token list
+    if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T, f) + 256 + sizeof(int32_t) * T * L->k, &scr)) return rc;
+    return pi_moe_ep_route_run(ctx, L, x, T, f, world, idx, gates, shscale, xq, xs, send_counts, send_xq, send_xs,
+                               send_eid, slot_row, scr, st);
+}
+
+extern "C" int pi_moe_experts_q8(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* xq, const float* xs,
+                                 const int32_t* eid, float* y, void* stream) {
+    if (!ctx || !L) return PI_ERR_ARG;
+    if (n_rows < 0 || n_rows > (1 << 24) || L->qtype != PI_QT_Q8_0 || (!eid && !L->has_shared))
+        return pi_set_error(ctx, PI_ERR_ARG, "experts: Q8_0 layer; eid = NULL needs a shared expert");
+    if (n_rows == 0) return PI_OK;
+    cudaStream_t st = (cudaStream_t)stream;
+    char* scr;
+    if (int rc = pi_scratch(ctx, st, pi_moe_rows_scratch_bytes(L, n_rows), &scr)) return rc;
+    return pi_moe_rows_run(ctx, L, n_rows, xq, xs, eid, y, scr, st);
+}
+
+extern "C" int pi_moe_ep_combine(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int32_t flags,
+                                 const float* gates, const float* shscale, const int32_t* slot_row, const float* y_back,
+                                 const float* y_shared, float* out, void* stream) {
+    if (!ctx || !L) return PI_ERR_ARG;
+    if (T < 0) return pi_set_error(ctx, PI_ERR_ARG, "ep combine: bad token batch");
+    if (T == 0) return PI_OK;
+    return pi_moe_ep_combine_run(ctx, L, x, T, flags, gates, shscale, slot_row, y_back, y_shared, out,
+                                 (cudaStream_t)stream);
 }
 
 extern "C" int pi_moe_route(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int32_t* idx, float* gates,

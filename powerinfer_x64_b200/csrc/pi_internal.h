@@ -42,7 +42,9 @@ struct __align__(64) PiPrefillMaps {
 struct pi_moe_layer {
     pi_ctx* ctx = nullptr;
     int64_t d = 0, f = 0, f_sh = 0;
-    int E = 0, k = 0, qtype = 0;
+    int E = 0, k = 0, qtype = 0;  // E: experts the router scores
+    // expert-parallel layers hold experts [e_first, e_first + n_exp) of the E; others all E
+    int e_first = 0, n_exp = 0;
     bool has_shared = false, has_shared_gate = false, has_bias = false;
     float* router = nullptr;   // f32 [E + 1][d]; row E = shared-expert gate vector (zeros if absent)
     float* bias = nullptr;     // f32 [E] or null
@@ -56,7 +58,7 @@ struct pi_moe_layer {
     float* router_nrm = nullptr;
     int router_rs = 0;
     CUtensorMap rmap_h, rmap_l;
-    PiMats gate, up, down;     // routed experts: gate/up [E][f][d], down [E][d][f]
+    PiMats gate, up, down;     // held routed experts: gate/up [n_exp][f][d], down [n_exp][d][f]
     PiMats gate_sh, up_sh, down_sh;  // shared expert (n = 1)
     PiPrefillMaps maps;              // valid when maps_ok (Q4_0, prefill-GEMM shapes)
     bool maps_ok = false;
@@ -190,6 +192,19 @@ size_t pi_moe_scratch_bytes(const pi_moe_layer* L, int64_t T, int flags);
 int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out, int flags, int32_t* idx_out,
                float* gates_out, int32_t* counts_out, int32_t* offsets_out, int32_t* perm_out, char* scratch,
                cudaStream_t st);
+// Internal forward flag: keep the Q8_0 activations of a routing-only run (expert parallelism).
+constexpr int PI_FWD_KEEP_Q8 = 1 << 30;
+// Expert-parallel stages (pi_moe.cu); buffers as documented at the C ABI.
+int pi_moe_ep_route_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int flags, int world,
+                        int32_t* idx, float* gates, float* shscale, int8_t* xq, float* xs, int32_t* send_counts,
+                        int8_t* send_xq, float* send_xs, int32_t* send_eid, int32_t* slot_row, char* scratch,
+                        cudaStream_t st);
+size_t pi_moe_rows_scratch_bytes(const pi_moe_layer* L, int64_t n_rows);
+int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* xq, const float* xs,
+                    const int32_t* eid, float* y, char* scratch, cudaStream_t st);
+int pi_moe_ep_combine_run(pi_ctx* ctx, const pi_moe_layer* L, const float* x, int64_t T, int flags, const float* gates,
+                          const float* shscale, const int32_t* slot_row, const float* y_back, const float* y_shared,
+                          float* out, cudaStream_t st);
 // Builds L->router_t and the tensor-core router operands from L->router (prefill router kernels).
 int pi_router_prepare(pi_ctx* ctx, pi_moe_layer* L);
 // Fast router logits on tensor cores (pi_prefill.cu): logits[t][e] (stride E + 1),

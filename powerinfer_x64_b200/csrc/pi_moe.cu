@@ -1155,7 +1155,9 @@ __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __
 
 // Q8_0 down: CTA = DN_ROWS output rows (8 warps x 8*DN_NP rows), 4 lanes per
 // row, CPQ = f/64 chunks per lane, 8 rows per warp pass; the quantised h
-// of each slot comes from k_quant_h.
+// of each slot comes from k_quant_h. Each output is the reference's sequential
+// sum of block terms (float)sumi * (d_w * d_h) in ascending block order
+// (quant/mod.rs:877-899), bit for bit.
 constexpr int DN_NP = 2;             // passes of 8 rows per warp
 constexpr int DN_ROWS = 64 * DN_NP;   // rows per CTA
 template <int CPQ>
@@ -1206,7 +1208,9 @@ __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
         for (int b = 0; b < BPQ; ++b) hsv[b] = hsr[b];
 #pragma unroll
         for (int p = 0; p < DN_NP; ++p) {
-            float acc = 0.f;
+            // block terms of this lane's quarter (blocks q*BPQ .. q*BPQ + BPQ - 1), then the
+            // reference's sequential sum over all blocks in ascending order, gathered by shuffles
+            float term[BPQ];
 #pragma unroll
             for (int b = 0; b < BPQ; ++b) {
                 int s = 0;
@@ -1218,10 +1222,14 @@ __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
                     s = dp4a(wv.z, xv.z, s);
                     s = dp4a(wv.w, xv.w, s);
                 }
-                acc += (float)s * (sw[p][b] * hsv[b]);
+                term[b] = fmul((float)s, fmul(sw[p][b], hsv[b]));
             }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+            float acc = 0.f;
+#pragma unroll
+            for (int src = 0; src < 4; ++src)
+#pragma unroll
+                for (int b = 0; b < BPQ; ++b)
+                    acc = fadd(acc, __shfl_sync(0xffffffffu, term[b], (lane & ~3) | src));
             if (q == 0) a.y[(size_t)slot * d + rbase + 8 * p] = acc;
         }
     }
@@ -1348,10 +1356,12 @@ __global__ __launch_bounds__(256) void k_down_q4(ExpertArgs a) {
 // k_combine: out[t] = (x[t] +) sum_j gates[t][j] * y[slot(t,j)] + s_t * y_sh[t],
 // experts ascending, each step o = o + g * y (no FMA), as model/mod.rs:1525-1534.
 // ---------------------------------------------------------------------------
+// y_sh: the shared expert's rows [T][d], or null for rows T*k .. T*k+T-1 of y.
 __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, const float* __restrict__ y,
                                                  const float* __restrict__ gates, const int32_t* __restrict__ slot_of,
-                                                 const float* __restrict__ shscale, int T, int k, int d,
-                                                 int has_shared, int residual, float* __restrict__ out) {
+                                                 const float* __restrict__ shscale, const float* __restrict__ y_sh,
+                                                 int T, int k, int d, int has_shared, int residual,
+                                                 float* __restrict__ out) {
     const int t = blockIdx.x;
     const int c = blockIdx.y * blockDim.x + threadIdx.x;
     if (c < d) {
@@ -1360,9 +1370,92 @@ __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, co
             const int slot = slot_of[(size_t)t * k + j];
             acc = fadd(acc, fmul(gates[(size_t)t * k + j], y[(size_t)slot * d + c]));
         }
-        if (has_shared) acc = fadd(acc, fmul(shscale[t], y[((size_t)T * k + t) * d + c]));
+        if (has_shared)
+            acc = fadd(acc, fmul(shscale[t], y_sh ? y_sh[(size_t)t * d + c] : y[((size_t)T * k + t) * d + c]));
         out[(size_t)t * d + c] = residual ? fadd(x[(size_t)t * d + c], acc) : acc;
     }
+}
+
+// ---------------------------------------------------------------------------
+// Expert parallelism (no reference counterpart: the reference runs one process).
+// Rank r holds experts [r P, (r + 1) P), P = E / world. Each home (token, j) slot
+// is sent to its expert's rank as one Q8_0 row (the token's quantised
+// activations, as every rank would quantise them) with the expert's local id.
+// ---------------------------------------------------------------------------
+// counts[r] = #slots whose expert lies on rank r. One CTA.
+__global__ __launch_bounds__(1024) void k_ep_count(const int32_t* __restrict__ idx, int n, int per_rank, int world,
+                                                   int32_t* __restrict__ counts) {
+    __shared__ int c[64];
+    for (int i = threadIdx.x; i < world; i += blockDim.x) c[i] = 0;
+    __syncthreads();
+    for (int s = threadIdx.x; s < n; s += blockDim.x) atomicAdd(&c[idx[s] / per_rank], 1);
+    __syncthreads();
+    for (int i = threadIdx.x; i < world; i += blockDim.x) counts[i] = c[i];
+}
+
+// CTA r lays out rank r's slots contiguously in slot order (stable), after
+// those of ranks < r: send_tok / send_eid per position, slot_row per slot.
+__global__ __launch_bounds__(1024) void k_ep_scatter(const int32_t* __restrict__ idx, int n, int k, int per_rank,
+                                                     const int32_t* __restrict__ counts, int32_t* __restrict__ send_tok,
+                                                     int32_t* __restrict__ send_eid, int32_t* __restrict__ slot_row) {
+    __shared__ int s_w[32];
+    __shared__ int s_base;
+    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    if (threadIdx.x == 0) {
+        int b = 0;
+        for (int i = 0; i < r; ++i) b += counts[i];
+        s_base = b;
+    }
+    __syncthreads();
+    int run = s_base;
+    for (int s0 = 0; s0 < n; s0 += blockDim.x) {
+        const int s = s0 + threadIdx.x;
+        const bool mine = s < n && idx[s] / per_rank == r;
+        const unsigned bal = __ballot_sync(0xffffffffu, mine);
+        if (lane == 0) s_w[warp] = __popc(bal);
+        __syncthreads();
+        int before = 0, total = 0;
+        for (int w = 0; w < nw; ++w) {
+            if (w < warp) before += s_w[w];
+            total += s_w[w];
+        }
+        if (mine) {
+            const int pos = run + before + __popc(bal & ((1u << lane) - 1u));
+            send_tok[pos] = s / k;
+            send_eid[pos] = idx[s] - r * per_rank;
+            slot_row[s] = pos;
+        }
+        run += total;
+        __syncthreads();
+    }
+}
+
+// send rows: send_xq[p] = xq[send_tok[p]] (d bytes), send_xs[p] = xs[send_tok[p]] (d/32 floats)
+__global__ void k_ep_gather(const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                            const int32_t* __restrict__ send_tok, int64_t n_rows, int d, int8_t* __restrict__ send_xq,
+                            float* __restrict__ send_xs) {
+    const int64_t p = blockIdx.x;
+    if (p >= n_rows) return;
+    const int64_t t = send_tok[p];
+    for (int c = threadIdx.x; c < d / 16; c += blockDim.x)
+        reinterpret_cast<int4*>(send_xq + p * d)[c] = reinterpret_cast<const int4*>(xq + t * d)[c];
+    for (int c = threadIdx.x; c < d / 32; c += blockDim.x) send_xs[p * (d / 32) + c] = xs[t * (d / 32) + c];
+}
+
+// expert-id histogram of the given rows
+__global__ void k_ep_hist(const int32_t* __restrict__ eid, int64_t n, int32_t* __restrict__ counts) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i < n) atomicAdd(&counts[eid[i]], 1);
+}
+
+// y_rows[r] = y[slot of row r] (routed rows: slot_of[r]; shared-expert rows: n + r)
+__global__ void k_rows_from_slots(const float* __restrict__ y, const int32_t* __restrict__ slot_of, int64_t n, int d,
+                                  int shared, float* __restrict__ out) {
+    const int64_t r = blockIdx.x;
+    if (r >= n) return;
+    const int64_t s = shared ? n + r : slot_of[r];
+    for (int c = threadIdx.x; c < d / 4; c += blockDim.x)
+        reinterpret_cast<float4*>(out + r * d)[c] = reinterpret_cast<const float4*>(y + s * d)[c];
 }
 
 // ---------------------------------------------------------------------------
@@ -1628,6 +1721,106 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
 }
 }  // namespace
 
+// Expert kernel arguments for a dispatch over `n_routed` routed slots (then the
+// shared expert's slots); item.x == E_items marks the shared expert.
+ExpertArgs expert_args(const pi_moe_layer* L, int E_items, const FwdBufs& B, const int32_t* perm, int64_t n_routed,
+                       const float* xin) {
+    ExpertArgs a;
+    a.g = L->gate.q;
+    a.u = L->up.q;
+    a.dn = L->down.q;
+    a.gd = L->gate.d;
+    a.ud = L->up.d;
+    a.dd = L->down.d;
+    a.gs = L->gate_sh.q;
+    a.us = L->up_sh.q;
+    a.dns = L->down_sh.q;
+    a.gsd = L->gate_sh.d;
+    a.usd = L->up_sh.d;
+    a.dsd = L->down_sh.d;
+    a.E = E_items;
+    a.d = (int)L->d;
+    a.f = (int)L->f;
+    a.items = B.items;
+    a.n_items = B.n_items;
+    a.perm = perm;
+    a.n_routed = (int)n_routed;
+    a.xq = B.xq;
+    a.xs = B.xs;
+    a.xf = xin;
+    a.hq = B.hq;
+    a.hs = B.hs;
+    a.hf = B.hf;
+    a.y = B.y;
+    return a;
+}
+
+// Expert SwiGLU products of the dispatched work items into a.y (slot order):
+// the tensor-core GEMMs for prefill-sized batches, the GEMV kernels otherwise.
+// T: token rows behind the slots (Q4_0 GEMM: B.xth/B.xtl hold their f16 split).
+int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t T, int64_t n_slots, unsigned ni,
+                bool gemm, const FwdBufs& B, cudaStream_t st) {
+    const bool q8 = L->qtype == PI_QT_Q8_0;
+    const int d = (int)L->d;
+    if (gemm && q8) return pi_prefill_experts_q8(ctx, L, a, ni, T, n_slots, st);
+    if (gemm) return pi_prefill_experts(ctx, L, a, ni, n_slots, B.xth, B.xtl, T, B.hh, B.hl, st);
+    const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / (q8 ? DN_ROWS : 128)), ni);
+    if (q8) {
+        {
+        PiProfScope ps(ctx, st, "k_gateup");
+        switch (d / 512) {
+#define GU_Q8(C)                                                                                              \
+    case C: {                                                                                                 \
+        static bool attr = false;                                                                             \
+        if (!attr) {                                                                                          \
+            cudaFuncSetAttribute(k_gateup_q8<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
+                                 (int)gateup_q8_smem<C>());                                                   \
+            attr = true;                                                                                      \
+        }                                                                                                     \
+        k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
+        break;                                                                                                \
+    }
+            GU_Q8(2)
+            GU_Q8(4)
+#undef GU_Q8
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 1024 or 2048");
+        }
+        }
+        {
+            PiProfScope ps(ctx, st, "k_quant_h");
+            const int64_t nblk = n_slots * (L->f / 32);
+            k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
+        }
+        PiProfScope ps(ctx, st, "k_down");
+        switch (L->f / 64) {
+            case 2: k_down_q8<2><<<dn, 256, 0, st>>>(a); break;
+            case 4: k_down_q8<4><<<dn, 256, 0, st>>>(a); break;
+            case 8: k_down_q8<8><<<dn, 256, 0, st>>>(a); break;
+            case 16: k_down_q8<16><<<dn, 256, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128..1024 (x2)");
+        }
+    } else {
+        {
+        PiProfScope ps(ctx, st, "k_gateup");
+        switch (d / 1024) {
+            case 1: k_gateup_q4<1><<<gu, 512, 0, st>>>(a); break;
+            case 2: k_gateup_q4<2><<<gu, 512, 0, st>>>(a); break;
+            case 4: k_gateup_q4<4><<<gu, 512, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: n_embd must be 1024, 2048 or 4096");
+        }
+        }
+        PiProfScope ps(ctx, st, "k_down");
+        switch (L->f / 128) {
+            case 1: k_down_q4<1><<<dn, 256, 0, st>>>(a); break;
+            case 2: k_down_q4<2><<<dn, 256, 0, st>>>(a); break;
+            case 4: k_down_q4<4><<<dn, 256, 0, st>>>(a); break;
+            case 8: k_down_q4<8><<<dn, 256, 0, st>>>(a); break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: expert width must be 128..1024 (x2)");
+        }
+    }
+    return pi_cuda_check(ctx, cudaGetLastError(), "experts") ? PI_ERR_CUDA : PI_OK;
+}
+
 int pi_router_prepare(pi_ctx* ctx, pi_moe_layer* L) {
     L->ep = (L->E + RW_ROWS - 1) / RW_ROWS * RW_ROWS;
     const size_t bytes = sizeof(float) * (size_t)L->d * L->ep;
@@ -1694,10 +1887,11 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     int32_t* offsets = offsets_out ? offsets_out : B.offsets;
     int32_t* perm = perm_out ? perm_out : B.perm;
 
-    if (do_norm || (q8 && !route_only)) {
+    const bool quant = q8 && (!route_only || (flags & PI_FWD_KEEP_Q8));
+    if (do_norm || quant) {
         PiProfScope ps(ctx, st, "k_prep");
-        k_prep<<<(unsigned)T, 256, sizeof(float) * d, st>>>(x, d, do_norm, 1e-6f, B.normed,
-                                                                          (q8 && !route_only) ? 1 : 0, B.xq, B.xs);
+        k_prep<<<(unsigned)T, 256, sizeof(float) * d, st>>>(x, d, do_norm, 1e-6f, B.normed, quant ? 1 : 0, B.xq,
+                                                             B.xs);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
@@ -1787,114 +1981,89 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     }
     if (route_only) return pi_cuda_check(ctx, cudaGetLastError(), "route") ? PI_ERR_CUDA : PI_OK;
 
-    ExpertArgs a;
-    a.g = L->gate.q;
-    a.u = L->up.q;
-    a.dn = L->down.q;
-    a.gd = L->gate.d;
-    a.ud = L->up.d;
-    a.dd = L->down.d;
-    a.gs = L->gate_sh.q;
-    a.us = L->up_sh.q;
-    a.dns = L->down_sh.q;
-    a.gsd = L->gate_sh.d;
-    a.usd = L->up_sh.d;
-    a.dsd = L->down_sh.d;
-    a.E = E;
-    a.d = d;
-    a.f = (int)L->f;
-    a.items = B.items;
-    a.n_items = B.n_items;
-    a.perm = perm;
-    a.n_routed = (int)(T * k);
-    a.xq = B.xq;
-    a.xs = B.xs;
-    a.xf = xin;
-    a.hq = B.hq;
-    a.hs = B.hs;
-    a.hf = B.hf;
-    a.y = B.y;
+    const int64_t n_slots = T * k + (L->has_shared ? T : 0);
+    ExpertArgs a = expert_args(L, E, B, perm, T * k, xin);
     const unsigned ni = (unsigned)max_items(L, T, tg);
-    if (gemm && q8) {
-        if (int rc = pi_prefill_experts_q8(ctx, L, a, ni, T, T * k + (L->has_shared ? T : 0), st)) return rc;
-        PiProfScope ps(ctx, st, "k_combine");
-        k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
-            x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,
-            out);
-        return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
+    if (gemm && !q8 && !use_router_tc(L, T)) {  // the router did not split the tokens
+        PiProfScope ps(ctx, st, "k_split_tokens");
+        k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
     }
-    if (gemm) {
-        const int64_t n_slots = T * k + (L->has_shared ? T : 0);
-        if (!use_router_tc(L, T)) {  // the router did not split the tokens
-            PiProfScope ps(ctx, st, "k_split_tokens");
-            k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
-        }
-        if (int rc = pi_prefill_experts(ctx, L, a, ni, n_slots, B.xth, B.xtl, T, B.hh, B.hl, st)) return rc;
-        PiProfScope ps(ctx, st, "k_combine");
-        k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
-            x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0, (flags & PI_FWD_RESIDUAL) ? 1 : 0,
-            out);
-        return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
-    }
-    const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / (q8 ? DN_ROWS : 128)), ni);
-    if (q8) {
-        {
-        PiProfScope ps(ctx, st, "k_gateup");
-        switch (d / 512) {
-#define GU_Q8(C)                                                                                              \
-    case C: {                                                                                                 \
-        static bool attr = false;                                                                             \
-        if (!attr) {                                                                                          \
-            cudaFuncSetAttribute(k_gateup_q8<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
-                                 (int)gateup_q8_smem<C>());                                                   \
-            attr = true;                                                                                      \
-        }                                                                                                     \
-        k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
-        break;                                                                                                \
-    }
-            GU_Q8(2)
-            GU_Q8(4)
-#undef GU_Q8
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: n_embd must be 1024 or 2048");
-        }
-        }
-        {
-            PiProfScope ps(ctx, st, "k_quant_h");
-            const int64_t slots = T * k + (L->has_shared ? T : 0);
-            const int64_t nblk = slots * (L->f / 32);
-            k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
-        }
-        PiProfScope ps(ctx, st, "k_down");
-        switch (L->f / 64) {
-            case 2: k_down_q8<2><<<dn, 256, 0, st>>>(a); break;
-            case 4: k_down_q8<4><<<dn, 256, 0, st>>>(a); break;
-            case 8: k_down_q8<8><<<dn, 256, 0, st>>>(a); break;
-            case 16: k_down_q8<16><<<dn, 256, 0, st>>>(a); break;
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128..1024 (x2)");
-        }
-    } else {
-        {
-        PiProfScope ps(ctx, st, "k_gateup");
-        switch (d / 1024) {
-            case 1: k_gateup_q4<1><<<gu, 512, 0, st>>>(a); break;
-            case 2: k_gateup_q4<2><<<gu, 512, 0, st>>>(a); break;
-            case 4: k_gateup_q4<4><<<gu, 512, 0, st>>>(a); break;
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: n_embd must be 1024, 2048 or 4096");
-        }
-        }
-        PiProfScope ps(ctx, st, "k_down");
-        switch (L->f / 128) {
-            case 1: k_down_q4<1><<<dn, 256, 0, st>>>(a); break;
-            case 2: k_down_q4<2><<<dn, 256, 0, st>>>(a); break;
-            case 4: k_down_q4<4><<<dn, 256, 0, st>>>(a); break;
-            case 8: k_down_q4<8><<<dn, 256, 0, st>>>(a); break;
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q4_0 layer: expert width must be 128..1024 (x2)");
-        }
-    }
+    if (int rc = run_experts(ctx, L, a, T, n_slots, ni, gemm, B, st)) return rc;
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale, (int)T, k, d, L->has_shared ? 1 : 0,
-                                            (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
+    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale,
+                                                                           nullptr, (int)T, k, d,
+                                                                           L->has_shared ? 1 : 0,
+                                                                           (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
     return pi_cuda_check(ctx, cudaGetLastError(), "moe forward") ? PI_ERR_CUDA : PI_OK;
+}
+
+
+int pi_moe_ep_route_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int flags, int world,
+                        int32_t* idx, float* gates, float* shscale, int8_t* xq, float* xs, int32_t* send_counts,
+                        int8_t* send_xq, float* send_xs, int32_t* send_eid, int32_t* slot_row, char* scratch,
+                        cudaStream_t st) {
+    // routing only; the Q8_0 activations stay in scratch
+    if (int rc = pi_moe_run(ctx, L, x, T, nullptr, flags, idx, gates, nullptr, nullptr, nullptr, scratch, st)) return rc;
+    const FwdBufs B = carve(L, T, flags, scratch);
+    int32_t* send_tok = reinterpret_cast<int32_t*>(scratch + ((B.bytes + 255) & ~(size_t)255));
+    const int d = (int)L->d, k = L->k, n = (int)(T * k), per_rank = L->n_exp;
+    PiProfScope ps(ctx, st, "k_ep_layout");
+    k_ep_count<<<1, 1024, 0, st>>>(idx, n, per_rank, world, send_counts);
+    k_ep_scatter<<<(unsigned)world, 1024, 0, st>>>(idx, n, k, per_rank, send_counts, send_tok, send_eid, slot_row);
+    k_ep_gather<<<(unsigned)n, 128, 0, st>>>(B.xq, B.xs, send_tok, n, d, send_xq, send_xs);
+    if (xq && pi_cuda_check(ctx, cudaMemcpyAsync(xq, B.xq, (size_t)T * d, cudaMemcpyDeviceToDevice, st), "xq"))
+        return PI_ERR_CUDA;
+    if (xs && pi_cuda_check(ctx, cudaMemcpyAsync(xs, B.xs, sizeof(float) * T * (d / 32), cudaMemcpyDeviceToDevice, st),
+                            "xs"))
+        return PI_ERR_CUDA;
+    if (shscale &&
+        pi_cuda_check(ctx, cudaMemcpyAsync(shscale, B.shscale, sizeof(float) * T, cudaMemcpyDeviceToDevice, st), "sh"))
+        return PI_ERR_CUDA;
+    return pi_cuda_check(ctx, cudaGetLastError(), "ep route") ? PI_ERR_CUDA : PI_OK;
+}
+
+namespace {
+bool rows_gemm(const pi_moe_layer* L, int64_t n_rows) {
+    return L->qtype == PI_QT_Q8_0 && pi_prefill_q8_shape_ok(L->d, L->f) && L->maps_ok && n_rows >= 128;
+}
+}  // namespace
+
+size_t pi_moe_rows_scratch_bytes(const pi_moe_layer* L, int64_t n_rows) {
+    return carve(L, n_rows, rows_gemm(L, n_rows) ? PI_FWD_FORCE_GEMM : PI_FWD_FORCE_GEMV, nullptr).bytes;
+}
+
+int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* xq, const float* xs,
+                    const int32_t* eid, float* y, char* scratch, cudaStream_t st) {
+    const bool gemm = rows_gemm(L, n_rows), shared_only = eid == nullptr;
+    const FwdBufs B = carve(L, n_rows, gemm ? PI_FWD_FORCE_GEMM : PI_FWD_FORCE_GEMV, scratch);
+    const int En = L->n_exp, d = (int)L->d, tg = gemm ? PI_GEMM_NT_Q8 : TG;
+    if (pi_cuda_check(ctx, cudaMemsetAsync(B.counts, 0, sizeof(int32_t) * En, st), "memset counts")) return PI_ERR_CUDA;
+    if (!shared_only) k_ep_hist<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(eid, n_rows, B.counts);
+    {
+        PiProfScope ps(ctx, st, "k_dispatch");
+        k_dispatch<<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
+                                                       shared_only ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
+                                                       B.n_items, tg);
+    }
+    ExpertArgs a = expert_args(L, En, B, B.perm, n_rows, nullptr);
+    a.xq = xq;
+    a.xs = xs;
+    const int64_t n_slots = shared_only ? 2 * n_rows : n_rows;
+    const unsigned ni = (unsigned)(std::min<int64_t>(En, n_rows) + 2 * ((n_rows + tg - 1) / tg) + 1);
+    if (int rc = run_experts(ctx, L, a, n_rows, n_slots, ni, gemm, B, st)) return rc;
+    k_rows_from_slots<<<(unsigned)n_rows, 256, 0, st>>>(B.y, B.slot_of, n_rows, d, shared_only ? 1 : 0, y);
+    return pi_cuda_check(ctx, cudaGetLastError(), "experts") ? PI_ERR_CUDA : PI_OK;
+}
+
+int pi_moe_ep_combine_run(pi_ctx* ctx, const pi_moe_layer* L, const float* x, int64_t T, int flags, const float* gates,
+                          const float* shscale, const int32_t* slot_row, const float* y_back, const float* y_shared,
+                          float* out, cudaStream_t st) {
+    const int d = (int)L->d;
+    PiProfScope ps(ctx, st, "k_combine");
+    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
+        x, y_back, gates, slot_row, shscale, y_shared, (int)T, L->k, d, (L->has_shared && y_shared) ? 1 : 0,
+        (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
+    return pi_cuda_check(ctx, cudaGetLastError(), "ep combine") ? PI_ERR_CUDA : PI_OK;
 }
 
 extern "C" int pi_router_topk_softmax(pi_ctx* ctx, const float* x, int64_t T, const float* router, int64_t d,

@@ -1,0 +1,170 @@
+"""Expert parallelism for the MoE layer.
+
+Rank r of `world` holds experts [r*P, (r+1)*P), P = E / world, plus the full
+router and the shared expert; tokens are data-parallel (each rank routes its
+own home tokens). One layer forward is
+
+  1. ``pi_moe_ep_route``   home tokens -> routing + one Q8_0 row per (token, j)
+                           slot, grouped by the slot expert's rank;
+  2. exchange              all-to-all-v of the rows (and their local expert ids);
+  3. ``pi_moe_experts_q8`` the held experts over the received rows;
+  4. exchange              all-to-all-v of the expert outputs back to the home rank;
+  5. ``pi_moe_experts_q8`` the shared expert over the home tokens, and
+     ``pi_moe_ep_combine`` the gate-weighted sum in ascending expert order.
+
+Every expert row is computed exactly as the one-GPU layer computes it and the
+combine order is the reference's, so the result equals ``MoeLayer.forward`` on
+the same tokens bit for bit, at any world size. The reference has no
+counterpart (it runs one process, model/mod.rs:1245-1571).
+
+``RowExchange`` is the transport: torch.distributed all_to_all_single (NCCL over
+NVLink on GPUs; gloo in the CPU tests of the bookkeeping).
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import quant
+from ._lib import PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_Q8_0, Context, PiError, PI_ERR_ARG, PiMoeLayerDesc, lib, ptr, \
+    stream_ptr
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+class RowExchange:
+    """All-to-all-v of row blocks over a process group (identity for one rank).
+
+    ``counts(send_counts)`` exchanges the per-destination row counts and returns
+    (send_splits, recv_splits) as host lists; ``rows(send, send_splits,
+    recv_splits)`` sends rows [sum(send_splits), ...] (grouped by destination,
+    ascending rank) and returns the received rows grouped by source rank.
+    """
+
+    def __init__(self, group=None):
+        import torch.distributed as dist
+
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+
+    def counts(self, send_counts):
+        torch = _torch()
+        import torch.distributed as dist
+
+        send = [int(v) for v in send_counts.cpu().tolist()]
+        if self.world == 1:
+            return send, list(send)
+        sc = send_counts.to(torch.int64)
+        rc = torch.empty_like(sc)
+        dist.all_to_all_single(rc, sc, group=self.group)
+        return send, [int(v) for v in rc.cpu().tolist()]
+
+    def rows(self, send, send_splits, recv_splits):
+        torch = _torch()
+        import torch.distributed as dist
+
+        if self.world == 1:
+            return send[: sum(recv_splits)]
+        out = torch.empty((sum(recv_splits),) + tuple(send.shape[1:]), dtype=send.dtype, device=send.device)
+        dist.all_to_all_single(out, send[: sum(send_splits)], output_split_sizes=recv_splits,
+                               input_split_sizes=send_splits, group=self.group)
+        return out
+
+
+class EPMoeLayer:
+    """One MoE layer sharded by experts over `world` ranks (Q8_0 experts).
+
+    gate/up/down_exps hold this rank's experts only (GGUF bytes of experts
+    [rank*P, (rank+1)*P)); router, router_bias and shared are the full tensors.
+    """
+
+    def __init__(self, router, gate_exps, up_exps, down_exps, n_embd: int, n_ff: int, n_expert: int, top_k: int,
+                 rank: int, world: int, shared=None, router_bias=None, exchange: RowExchange | None = None,
+                 device: int | None = None):
+        torch = _torch()
+        if n_expert % world:
+            raise PiError(PI_ERR_ARG, "n_expert must be a multiple of the world size")
+        self.ctx = Context.default(device)
+        self.d, self.f, self.E, self.k = n_embd, n_ff, n_expert, top_k
+        self.rank, self.world, self.P = rank, world, n_expert // world
+        self.has_shared = shared is not None
+        self.exchange = exchange or RowExchange()
+        keep = []
+
+        def dev(a, dt):
+            t = quant._dev(a, dt)
+            keep.append(t)
+            return ptr(t)
+
+        desc = PiMoeLayerDesc()
+        desc.n_embd, desc.n_ff_exp, desc.n_ff_shexp = n_embd, n_ff, n_ff
+        desc.n_expert, desc.n_expert_used, desc.qtype, desc.src_on_host = n_expert, top_k, PI_QT_Q8_0, 0
+        desc.router = dev(router, np.float32)
+        desc.router_bias = dev(router_bias, np.float32) if router_bias is not None else None
+        desc.gate_exps, desc.up_exps, desc.down_exps = (dev(gate_exps, np.uint8), dev(up_exps, np.uint8),
+                                                        dev(down_exps, np.uint8))
+        if shared is not None:
+            g, u, d_, gi = shared
+            desc.gate_shexp, desc.up_shexp, desc.down_shexp = dev(g, np.uint8), dev(u, np.uint8), dev(d_, np.uint8)
+            desc.gate_inp_shexp = dev(gi, np.float32) if gi is not None else None
+        h = C.c_void_p()
+        torch.cuda.synchronize()
+        self.ctx.check(lib().pi_moe_layer_create_ep(self.ctx.h, C.byref(desc), rank * self.P, self.P, C.byref(h)))
+        self.h = h
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                lib().pi_moe_layer_destroy(self.h)
+        except Exception:
+            pass
+
+    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False):
+        """MoE FFN of the home tokens x [T, d] (device f32) -> out [T, d]."""
+        torch = _torch()
+        L, s = lib(), stream_ptr()
+        xd = quant._f32(x)
+        T, d, k = xd.numel() // self.d, self.d, self.k
+        if out is None:
+            out = torch.empty((T, d), dtype=torch.float32, device="cuda")
+        flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
+        dv = xd.device
+        e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dv)
+        idx, gates, shscale = e(T * k, dt=torch.int32), e(T * k), e(max(T, 1))
+        xq, xs = e(T, d, dt=torch.int8), e(T, d // 32)
+        send_counts = e(self.world, dt=torch.int32)
+        send_xq, send_xs = e(T * k, d, dt=torch.int8), e(T * k, d // 32)
+        send_eid, slot_row = e(T * k, dt=torch.int32), e(T * k, dt=torch.int32)
+        self.ctx.check(L.pi_moe_ep_route(self.ctx.h, self.h, ptr(xd), T, flags, self.world, ptr(idx), ptr(gates),
+                                         ptr(shscale), ptr(xq), ptr(xs), ptr(send_counts), ptr(send_xq), ptr(send_xs),
+                                         ptr(send_eid), ptr(slot_row), s))
+        ex = self.exchange
+        send_splits, recv_splits = ex.counts(send_counts)
+        r_xq = ex.rows(send_xq, send_splits, recv_splits)
+        r_xs = ex.rows(send_xs, send_splits, recv_splits)
+        r_eid = ex.rows(send_eid, send_splits, recv_splits)
+        n_recv = sum(recv_splits)
+        y = e(max(n_recv, 1), d)
+        self.ctx.check(L.pi_moe_experts_q8(self.ctx.h, self.h, n_recv, ptr(r_xq), ptr(r_xs), ptr(r_eid), ptr(y), s))
+        y_back = ex.rows(y, recv_splits, send_splits)
+        y_sh = None
+        if self.has_shared and T:
+            y_sh = e(T, d)
+            self.ctx.check(L.pi_moe_experts_q8(self.ctx.h, self.h, T, ptr(xq), ptr(xs), None, ptr(y_sh), s))
+        self.ctx.check(L.pi_moe_ep_combine(self.ctx.h, self.h, ptr(xd), T, flags, ptr(gates), ptr(shscale),
+                                           ptr(slot_row), ptr(y_back), ptr(y_sh) if y_sh is not None else None,
+                                           ptr(out), s))
+        return out
+
+
+def local_expert_bytes(exps, n_expert: int, rank: int, world: int):
+    """GGUF bytes of experts [rank*P, (rank+1)*P) out of an [E] expert tensor (equal slices)."""
+    b = exps.reshape(-1)
+    per = b.numel() // n_expert if hasattr(b, "numel") else b.size // n_expert
+    P = n_expert // world
+    return b[rank * P * per:(rank + 1) * P * per]
