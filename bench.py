@@ -219,13 +219,25 @@ def main():
     fwd_kw = dict(rmsnorm=True, residual=True) if args.config == "c5" else {}
     ctx = Context.default(local)
 
-    # layers + fixed per-layer tokens (each rank its own seed stream)
+    # layers + fixed per-layer tokens (each rank its own seed stream). c5: one model
+    # (same weights on every rank) sharded by experts over the ranks, tokens per rank
     layers, xs, routing = [], [], []
     for li in range(args.layers):
-        L = synth.moe_layer(cfg, seed=rank, layer=li)
         x = synth.tokens_dev(cfg.d, T, seed=rank, layer=li)
-        r = L.route(x)
-        U = int((r["counts"] > 0).sum().item())
+        if args.config == "c5":
+            from powerinfer_x64_b200.ep import EPMoeLayer, local_expert_bytes
+
+            t = synth.moe_tensors(cfg, seed=0, layer=li)
+            loc = lambda a: local_expert_bytes(a, cfg.E, rank, world).clone()
+            L = EPMoeLayer(t["router"], loc(t["gate_exps"]), loc(t["up_exps"]), loc(t["down_exps"]), cfg.d, cfg.f,
+                           cfg.E, cfg.k, rank=rank, world=world, shared=t["shared"])
+            del t
+            torch.cuda.empty_cache()
+            U = cfg.E
+        else:
+            L = synth.moe_layer(cfg, seed=rank, layer=li)
+            r = L.route(x)
+            U = int((r["counts"] > 0).sum().item())
         layers.append(L)
         xs.append(x)
         routing.append(U)
@@ -375,7 +387,9 @@ def main():
             "config": {"workload": f"{cfg.name} (BASELINE config {args.config[1]}): d=2048 "
                                    f"E=256 k=8 f=512 +shared, " + {"c2": "Q8_0 decode", "c3": "Q4_0 prefill, Zipf router bias",
                                                                    "c5": "Q8_0 prefill, one layer of the 40-layer stack, RMSNorm + residual"}[args.config],
-                       "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": f"dp{world} (replicas)",
+                       "tokens_per_step_per_gpu": T, "global_batch": T * world,
+                       "parallelism": (f"ep{world} (experts sharded {cfg.E // world} per GPU, tokens data-parallel, "
+                                       "NCCL all-to-all-v dispatch/combine)") if args.config == "c5" else f"dp{world} (replicas)",
                        "layers_cycled": args.layers, "l2": "inputs larger than L2: steps cycle through "
                        f"{args.layers} layers x {layer_bytes(cfg, 256, T)['total'] / 1e9:.2f} GB"},
             "roofline": roofline,

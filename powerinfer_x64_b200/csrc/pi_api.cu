@@ -292,8 +292,10 @@ extern "C" int pi_moe_ep_route(pi_ctx* ctx, pi_moe_layer* L, const float* x, int
     }
     const int f = (flags & (PI_FWD_RMSNORM | PI_FWD_RESIDUAL)) | PI_FWD_FORCE_GEMV | PI_FWD_KEEP_Q8;
     char* scr;
-    // + the send-order token list
-    if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T, f) + 256 + sizeof(int32_t) * T * L->k, &scr)) return rc;
+    // + the send-order token list and the per-chunk counts
+    const size_t n = (size_t)T * L->k, nchunk = (n + 1023) / 1024;
+    if (int rc = pi_scratch(ctx, st, pi_moe_scratch_bytes(L, T, f) + 512 + sizeof(int32_t) * (n + 64 + nchunk * world), &scr))
+        return rc;
     return pi_moe_ep_route_run(ctx, L, x, T, f, world, idx, gates, shscale, xq, xs, send_counts, send_xq, send_xs,
                                send_eid, slot_row, scr, st);
 }

@@ -1382,51 +1382,58 @@ __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, co
 // is sent to its expert's rank as one Q8_0 row (the token's quantised
 // activations, as every rank would quantise them) with the expert's local id.
 // ---------------------------------------------------------------------------
-// counts[r] = #slots whose expert lies on rank r. One CTA.
-__global__ __launch_bounds__(1024) void k_ep_count(const int32_t* __restrict__ idx, int n, int per_rank, int world,
-                                                   int32_t* __restrict__ counts) {
+// Layout in three passes over chunks of EPC slots: per-(chunk, rank) counts,
+// an exclusive scan in (rank, chunk) order (also the per-rank totals), then a
+// stable scatter: rank r's slots are contiguous after those of ranks < r, in
+// slot order.
+constexpr int EPC = 1024;
+__global__ __launch_bounds__(EPC) void k_ep_chunk_count(const int32_t* __restrict__ idx, int n, int per_rank,
+                                                        int world, int32_t* __restrict__ cc) {
     __shared__ int c[64];
     for (int i = threadIdx.x; i < world; i += blockDim.x) c[i] = 0;
     __syncthreads();
-    for (int s = threadIdx.x; s < n; s += blockDim.x) atomicAdd(&c[idx[s] / per_rank], 1);
+    const int s = blockIdx.x * EPC + threadIdx.x;
+    if (s < n) atomicAdd(&c[idx[s] / per_rank], 1);
     __syncthreads();
-    for (int i = threadIdx.x; i < world; i += blockDim.x) counts[i] = c[i];
+    for (int i = threadIdx.x; i < world; i += blockDim.x) cc[(size_t)blockIdx.x * world + i] = c[i];
 }
 
-// CTA r lays out rank r's slots contiguously in slot order (stable), after
-// those of ranks < r: send_tok / send_eid per position, slot_row per slot.
-__global__ __launch_bounds__(1024) void k_ep_scatter(const int32_t* __restrict__ idx, int n, int k, int per_rank,
-                                                     const int32_t* __restrict__ counts, int32_t* __restrict__ send_tok,
-                                                     int32_t* __restrict__ send_eid, int32_t* __restrict__ slot_row) {
-    __shared__ int s_w[32];
-    __shared__ int s_base;
-    const int r = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    if (threadIdx.x == 0) {
-        int b = 0;
-        for (int i = 0; i < r; ++i) b += counts[i];
-        s_base = b;
+// cc [nchunk][world] counts -> exclusive offsets in (rank, chunk) order; counts[r] totals. One thread.
+__global__ void k_ep_scan(int32_t* __restrict__ cc, int nchunk, int world, int32_t* __restrict__ counts) {
+    int run = 0;
+    for (int r = 0; r < world; ++r) {
+        const int start = run;
+        for (int ch = 0; ch < nchunk; ++ch) {
+            const int v = cc[(size_t)ch * world + r];
+            cc[(size_t)ch * world + r] = run;
+            run += v;
+        }
+        counts[r] = run - start;
     }
+}
+
+__global__ __launch_bounds__(EPC) void k_ep_scatter(const int32_t* __restrict__ idx, int n, int k, int per_rank,
+                                                    int world, const int32_t* __restrict__ cc,
+                                                    int32_t* __restrict__ send_tok, int32_t* __restrict__ send_eid,
+                                                    int32_t* __restrict__ slot_row) {
+    __shared__ int s_w[64][EPC / 32];  // per rank, per warp counts
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = EPC / 32;
+    const int s = blockIdx.x * EPC + threadIdx.x;
+    const int r = s < n ? idx[s] / per_rank : -1;
+    for (int i = threadIdx.x; i < world * nw; i += blockDim.x) s_w[i / nw][i % nw] = 0;
     __syncthreads();
-    int run = s_base;
-    for (int s0 = 0; s0 < n; s0 += blockDim.x) {
-        const int s = s0 + threadIdx.x;
-        const bool mine = s < n && idx[s] / per_rank == r;
-        const unsigned bal = __ballot_sync(0xffffffffu, mine);
-        if (lane == 0) s_w[warp] = __popc(bal);
-        __syncthreads();
-        int before = 0, total = 0;
-        for (int w = 0; w < nw; ++w) {
-            if (w < warp) before += s_w[w];
-            total += s_w[w];
-        }
-        if (mine) {
-            const int pos = run + before + __popc(bal & ((1u << lane) - 1u));
-            send_tok[pos] = s / k;
-            send_eid[pos] = idx[s] - r * per_rank;
-            slot_row[s] = pos;
-        }
-        run += total;
-        __syncthreads();
+    // rank of this slot among the chunk's slots of the same destination (warp-aggregated)
+    const unsigned same = __match_any_sync(0xffffffffu, r);
+    const int in_warp = __popc(same & ((1u << lane) - 1u));
+    if (r >= 0 && in_warp == 0) s_w[r][warp] = __popc(same);
+    __syncthreads();
+    if (r >= 0) {
+        int before = 0;
+        for (int w = 0; w < warp; ++w) before += s_w[r][w];
+        const int pos = cc[(size_t)blockIdx.x * world + r] + before + in_warp;
+        send_tok[pos] = s / k;
+        send_eid[pos] = idx[s] - r * per_rank;
+        slot_row[s] = pos;
     }
 }
 
@@ -2007,9 +2014,12 @@ int pi_moe_ep_route_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T,
     const FwdBufs B = carve(L, T, flags, scratch);
     int32_t* send_tok = reinterpret_cast<int32_t*>(scratch + ((B.bytes + 255) & ~(size_t)255));
     const int d = (int)L->d, k = L->k, n = (int)(T * k), per_rank = L->n_exp;
+    const int nchunk = (n + EPC - 1) / EPC;
+    int32_t* cc = send_tok + ((n + 63) & ~63);  // [nchunk][world]
     PiProfScope ps(ctx, st, "k_ep_layout");
-    k_ep_count<<<1, 1024, 0, st>>>(idx, n, per_rank, world, send_counts);
-    k_ep_scatter<<<(unsigned)world, 1024, 0, st>>>(idx, n, k, per_rank, send_counts, send_tok, send_eid, slot_row);
+    k_ep_chunk_count<<<(unsigned)nchunk, EPC, 0, st>>>(idx, n, per_rank, world, cc);
+    k_ep_scan<<<1, 1, 0, st>>>(cc, nchunk, world, send_counts);
+    k_ep_scatter<<<(unsigned)nchunk, EPC, 0, st>>>(idx, n, k, per_rank, world, cc, send_tok, send_eid, slot_row);
     k_ep_gather<<<(unsigned)n, 128, 0, st>>>(B.xq, B.xs, send_tok, n, d, send_xq, send_xs);
     if (xq && pi_cuda_check(ctx, cudaMemcpyAsync(xq, B.xq, (size_t)T * d, cudaMemcpyDeviceToDevice, st), "xq"))
         return PI_ERR_CUDA;
@@ -2028,14 +2038,32 @@ bool rows_gemm(const pi_moe_layer* L, int64_t n_rows) {
 }
 }  // namespace
 
-size_t pi_moe_rows_scratch_bytes(const pi_moe_layer* L, int64_t n_rows) {
-    return carve(L, n_rows, rows_gemm(L, n_rows) ? PI_FWD_FORCE_GEMM : PI_FWD_FORCE_GEMV, nullptr).bytes;
+// Scratch of an expert pass over n given rows: one routed slot per row, or (shared
+// expert) slots n .. 2n - 1; dispatch arrays and the hidden / output rows only.
+FwdBufs carve_rows(const pi_moe_layer* L, int64_t n, char* base) {
+    PiBump b{base};
+    FwdBufs f{};
+    const int64_t d = L->d, F = L->f, slots = 2 * n;
+    f.counts = b.take<int32_t>(L->n_exp);
+    f.offsets = b.take<int32_t>(L->n_exp);
+    f.perm = b.take<int32_t>(n);
+    f.slot_of = b.take<int32_t>(n);
+    f.items = b.take<int4>(std::min<int64_t>(L->n_exp, n) + 2 * ((n + TG - 1) / TG) + 1);
+    f.n_items = b.take<int32_t>(1);
+    f.hq = b.take<int8_t>(slots * F);
+    f.hs = b.take<float>(slots * (F / 32));
+    f.hf = b.take<float>(slots * F);
+    f.y = b.take<float>(slots * d);
+    f.bytes = b.off + 256;
+    return f;
 }
+
+size_t pi_moe_rows_scratch_bytes(const pi_moe_layer* L, int64_t n_rows) { return carve_rows(L, n_rows, nullptr).bytes; }
 
 int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* xq, const float* xs,
                     const int32_t* eid, float* y, char* scratch, cudaStream_t st) {
     const bool gemm = rows_gemm(L, n_rows), shared_only = eid == nullptr;
-    const FwdBufs B = carve(L, n_rows, gemm ? PI_FWD_FORCE_GEMM : PI_FWD_FORCE_GEMV, scratch);
+    const FwdBufs B = carve_rows(L, n_rows, scratch);
     const int En = L->n_exp, d = (int)L->d, tg = gemm ? PI_GEMM_NT_Q8 : TG;
     if (pi_cuda_check(ctx, cudaMemsetAsync(B.counts, 0, sizeof(int32_t) * En, st), "memset counts")) return PI_ERR_CUDA;
     if (!shared_only) k_ep_hist<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(eid, n_rows, B.counts);
