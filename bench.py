@@ -252,8 +252,7 @@ def main():
         step(i)
     torch.cuda.synchronize()
 
-    # ---- timed region (device time, kernel timing live via CUDA events) ----
-    ctx.profile(True)
+    # ---- timed region (device time with CUDA events, no per-kernel events inside) ----
     dist.barrier(local)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -265,6 +264,12 @@ def main():
         torch.cuda.synchronize()
     dist.barrier(local)
     ms = e0.elapsed_time(e1)
+    # ---- the same steps again with per-kernel CUDA events (kernel breakdown, roofline) ----
+    ctx.profile(True)
+    torch.cuda.synchronize()
+    for i in range(args.steps):
+        step(i)
+    torch.cuda.synchronize()
     kern = ctx.profile_read()
     ctx.profile(False)
     ms_max = dist.max_over_ranks(ms, device=dev)

@@ -1224,12 +1224,16 @@ __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
                 }
                 term[b] = fmul((float)s, fmul(sw[p][b], hsv[b]));
             }
+            // the running sum passes lane to lane: quarter src adds its terms, then hands on
             float acc = 0.f;
 #pragma unroll
-            for (int src = 0; src < 4; ++src)
+            for (int src = 0; src < 4; ++src) {
+                if (q == src) {
 #pragma unroll
-                for (int b = 0; b < BPQ; ++b)
-                    acc = fadd(acc, __shfl_sync(0xffffffffu, term[b], (lane & ~3) | src));
+                    for (int b = 0; b < BPQ; ++b) acc = fadd(acc, term[b]);
+                }
+                acc = __shfl_sync(0xffffffffu, acc, (lane & ~3) | src);
+            }
             if (q == 0) a.y[(size_t)slot * d + rbase + 8 * p] = acc;
         }
     }
