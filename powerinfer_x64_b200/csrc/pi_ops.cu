@@ -319,16 +319,36 @@ PI_DEV float q4dot16(const int4 wv, const float* __restrict__ x) {
     return s;
 }
 
+// gate and up blocks against the same 32 activations (one pass over x)
+PI_DEV void q4dot16x2(const int4 wg, const int4 wu, const float* __restrict__ x, float& sg, float& su) {
+    const uint32_t g4[4] = {(uint32_t)wg.x, (uint32_t)wg.y, (uint32_t)wg.z, (uint32_t)wg.w};
+    const uint32_t u4[4] = {(uint32_t)wu.x, (uint32_t)wu.y, (uint32_t)wu.z, (uint32_t)wu.w};
+    sg = 0.f;
+    su = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const float4 xa = *reinterpret_cast<const float4*>(x + 8 * i);
+        const float4 xb = *reinterpret_cast<const float4*>(x + 8 * i + 4);
+        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            sg += nibf((g4[i] >> (4 * j)) & 15u) * xv[j];
+            su += nibf((u4[i] >> (4 * j)) & 15u) * xv[j];
+        }
+    }
+}
+
 template <int BPL>
 __global__ __launch_bounds__(256) void k_sf_gateup_q4(const uint8_t* __restrict__ G, const uint8_t* __restrict__ U,
                                                       const __half* __restrict__ GD, const __half* __restrict__ UD,
-                                                      const uint32_t* __restrict__ mask, const float* __restrict__ x,
-                                                      int t0, int64_t n_embd, int64_t n_ff, float* __restrict__ h) {
+                                                      const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
+                                                      const int32_t* __restrict__ n_list, const float* __restrict__ x,
+                                                      int t0, int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t s = blockIdx.x * 8LL + warp;
-    if (s >= n_ff) return;
+    const int64_t li = blockIdx.x * 8LL + warp;
+    if (li >= *n_list) return;
+    const int64_t s = list[li];
     uint32_t m = mask[s];
-    if (!m) return;
     const int64_t nb = n_embd / 32;
     int4 wg[BPL], wu[BPL];
     float sg[BPL], su[BPL];
@@ -345,15 +365,16 @@ __global__ __launch_bounds__(256) void k_sf_gateup_q4(const uint8_t* __restrict_
         m &= m - 1;
         const float* xr = x + (int64_t)(t0 + t) * n_embd;
         float ag = 0.f, au = 0.f;
-#pragma unroll
+#pragma unroll 1
         for (int c = 0; c < BPL; ++c) {
-            const float* xb = xr + (lane + 32 * c) * 32;
-            ag += sg[c] * q4dot16(wg[c], xb);
-            au += su[c] * q4dot16(wu[c], xb);
+            float dg, du;
+            q4dot16x2(wg[c], wu[c], xr + (lane + 32 * c) * 32, dg, du);
+            ag += sg[c] * dg;
+            au += su[c] * du;
         }
         ag = warp_sum(ag);
         au = warp_sum(au);
-        if (lane == 0) h[(int64_t)t * n_ff + s] = swiglu_ref(ag, au);
+        if (lane == 0) gu[(int64_t)t * n_ff + s] = make_float2(ag, au);
     }
 }
 
@@ -361,13 +382,15 @@ template <int CPL>
 __global__ __launch_bounds__(256) void k_sf_gateup_q8(const int8_t* __restrict__ G, const int8_t* __restrict__ U,
                                                       const __half* __restrict__ GD, const __half* __restrict__ UD,
                                                       const uint32_t* __restrict__ mask,
+                                                      const int32_t* __restrict__ list,
+                                                      const int32_t* __restrict__ n_list,
                                                       const int8_t* __restrict__ xq, const float* __restrict__ xs,
-                                                      int t0, int64_t n_embd, int64_t n_ff, float* __restrict__ h) {
+                                                      int t0, int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t s = blockIdx.x * 8LL + warp;
-    if (s >= n_ff) return;
+    const int64_t li = blockIdx.x * 8LL + warp;
+    if (li >= *n_list) return;
+    const int64_t s = list[li];
     uint32_t m = mask[s];
-    if (!m) return;
     const int64_t nb = n_embd / 32;
     int4 wg[CPL], wu[CPL];
     float sg[CPL], su[CPL];
@@ -406,39 +429,62 @@ __global__ __launch_bounds__(256) void k_sf_gateup_q8(const int8_t* __restrict__
         }
         ag = warp_sum(ag);
         au = warp_sum(au);
-        if (lane == 0) h[(int64_t)t * n_ff + s] = swiglu_ref(ag, au);
+        if (lane == 0) gu[(int64_t)t * n_ff + s] = make_float2(ag, au);
     }
 }
 
-// down, neuron-major: CTA = (column tile of 1024 outputs, neuron split);
-// thread owns 4 consecutive columns; y accumulated with atomicAdd over splits.
+// Active-neuron list of a pass: list[0 .. *n_list) = the neurons with a mask bit
+// (any order: every neuron is independent, and the down sums are split anyway).
+__global__ void k_sf_compact(const uint32_t* __restrict__ mask, int64_t n_ff, int32_t* __restrict__ list,
+                             int32_t* __restrict__ n_list) {
+    const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (s < n_ff && mask[s]) list[atomicAdd(n_list, 1)] = (int32_t)s;
+}
+
+// h = SwiGLU(g, u) (quant/mod.rs:1196-1199) of every active (token, neuron), kept
+// out of the product kernels: the reference exp's double-precision evaluation
+// needs many registers. grid (ceil(n_ff / 256), nt).
+__global__ void k_sf_swiglu(const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
+                            const int32_t* __restrict__ n_list, const float2* __restrict__ gu, int64_t n_ff,
+                            float* __restrict__ h) {
+    const int64_t li = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const int t = blockIdx.y;
+    if (li >= *n_list) return;
+    const int64_t s = list[li];
+    if (!((mask[s] >> t) & 1u)) return;
+    const float2 v = gu[(int64_t)t * n_ff + s];
+    h[(int64_t)t * n_ff + s] = swiglu_ref(v.x, v.y);
+}
+
+// down, neuron-major: CTA = (column tile of 1024 outputs, chunk of SFD active
+// neurons); thread owns 4 consecutive columns; y accumulated with atomicAdd
+// over the chunks.
+constexpr int SFD = 16;
 template <int QT>
 __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
-                                                 const uint32_t* __restrict__ mask, const float* __restrict__ h,
-                                                 int t0, int nt, int64_t n_embd, int64_t n_ff, int64_t per_split,
-                                                 float* __restrict__ y) {
+                                                 const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
+                                                 const int32_t* __restrict__ n_list, const float* __restrict__ h,
+                                                 int t0, int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y) {
     const int64_t c = blockIdx.x * 1024LL + threadIdx.x * 4;
-    if (c >= n_embd) return;
-    const int64_t s_beg = blockIdx.y * per_split, s_end = min(n_ff, s_beg + per_split);
+    const int n_act = *n_list;
+    const int i0 = blockIdx.y * SFD;
+    if (c >= n_embd || i0 >= n_act) return;
+    const int i1 = min(n_act, i0 + SFD);
     float acc[SF_TMAX][4];
 #pragma unroll
     for (int t = 0; t < SF_TMAX; ++t)
 #pragma unroll
         for (int q = 0; q < 4; ++q) acc[t][q] = 0.f;
-    int64_t cur_g = -1;
-    float sc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t s = s_beg; s < s_end; ++s) {
-        uint32_t m = mask[s];
-        if (!m) continue;
-        const int64_t g = s >> 5;
-        if (g != cur_g) {
-            const uint2 sv = *reinterpret_cast<const uint2*>(DS + g * n_embd + c);
-            sc[0] = __half2float(__ushort_as_half((uint16_t)(sv.x & 0xffff)));
-            sc[1] = __half2float(__ushort_as_half((uint16_t)(sv.x >> 16)));
-            sc[2] = __half2float(__ushort_as_half((uint16_t)(sv.y & 0xffff)));
-            sc[3] = __half2float(__ushort_as_half((uint16_t)(sv.y >> 16)));
-            cur_g = g;
-        }
+#pragma unroll 4
+    for (int i = i0; i < i1; ++i) {
+        const int64_t s = list[i];
+        const uint32_t m = mask[s];
+        const uint2 sv = *reinterpret_cast<const uint2*>(DS + (s >> 5) * n_embd + c);
+        float sc[4];
+        sc[0] = __half2float(__ushort_as_half((uint16_t)(sv.x & 0xffff)));
+        sc[1] = __half2float(__ushort_as_half((uint16_t)(sv.x >> 16)));
+        sc[2] = __half2float(__ushort_as_half((uint16_t)(sv.y & 0xffff)));
+        sc[3] = __half2float(__ushort_as_half((uint16_t)(sv.y >> 16)));
         float w[4];
         if (QT == PI_QT_Q4_0) {
             const uint16_t v = *reinterpret_cast<const uint16_t*>(DQ + s * (n_embd / 2) + c / 2);
@@ -769,11 +815,15 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
     cudaStream_t st = ST(stream);
     const int64_t d = F->n_embd, n_ff = F->n_ff;
     char* scr;
-    const size_t need = (size_t)n_ff * 4 + (size_t)SF_TMAX * n_ff * 4 + (size_t)T * d + (size_t)T * (d / 32) * 4 + 4096;
+    const size_t need = (size_t)n_ff * 4 * 2 + (size_t)SF_TMAX * n_ff * 4 * 3 + (size_t)T * d + (size_t)T * (d / 32) * 4 +
+                        8192;
     if (int rc = pi_scratch(ctx, st, need, &scr)) return rc;
     PiBump b{scr};
     uint32_t* mask = b.take<uint32_t>(n_ff);
+    int32_t* list = b.take<int32_t>(n_ff);
+    int32_t* n_list = b.take<int32_t>(1);
     float* h = b.take<float>((size_t)SF_TMAX * n_ff);
+    float2* gu = b.take<float2>((size_t)SF_TMAX * n_ff);
     int8_t* xq = nullptr;
     float* xs = nullptr;
     if (F->qtype == PI_QT_Q8_0) {
@@ -782,35 +832,48 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
     }
     if (pi_cuda_check(ctx, cudaMemsetAsync(out, 0, sizeof(float) * T * d, st), "memset")) return PI_ERR_CUDA;
-    const int64_t splits = std::max<int64_t>(1, std::min<int64_t>(n_ff / 32, (ctx->sm_count * 2 + 3) / 4));
-    const int64_t per_split = ((n_ff + splits - 1) / splits + 31) / 32 * 32;
-    const int64_t nsplit = (n_ff + per_split - 1) / per_split;
     for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
-        if (pi_cuda_check(ctx, cudaMemsetAsync(mask, 0, sizeof(uint32_t) * n_ff, st), "memset")) return PI_ERR_CUDA;
-        k_sf_mask<<<dim3(32, nt), 256, 0, st>>>(ptr, idx, (int)t0, nt, n_ff, mask, ctx->dev_err);
+        if (pi_cuda_check(ctx, cudaMemsetAsync(mask, 0, sizeof(uint32_t) * (n_ff + 1 + n_ff) , st), "memset"))
+            return PI_ERR_CUDA;
+        {
+            PiProfScope ps(ctx, st, "k_sf_mask");
+            k_sf_mask<<<dim3(32, nt), 256, 0, st>>>(ptr, idx, (int)t0, nt, n_ff, mask, ctx->dev_err);
+            k_sf_compact<<<nblocks(n_ff, 256), 256, 0, st>>>(mask, n_ff, list, n_list);
+        }
         const unsigned gblocks = nblocks(n_ff, 8);
-        if (F->qtype == PI_QT_Q4_0) {
-            const uint8_t* G = (const uint8_t*)F->gate.q;
-            const uint8_t* U = (const uint8_t*)F->up.q;
-            switch (d / 1024) {
-                case 1: k_sf_gateup_q4<1><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
-                case 2: k_sf_gateup_q4<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
-                case 4: k_sf_gateup_q4<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, x, (int)t0, d, n_ff, h); break;
+        {
+            PiProfScope ps(ctx, st, "k_sf_gateup");
+            if (F->qtype == PI_QT_Q4_0) {
+                const uint8_t* G = (const uint8_t*)F->gate.q;
+                const uint8_t* U = (const uint8_t*)F->up.q;
+                switch (d / 1024) {
+                    case 1: k_sf_gateup_q4<1><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
+                    case 2: k_sf_gateup_q4<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
+                    case 4: k_sf_gateup_q4<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
+                }
+            } else {
+                const int8_t* G = (const int8_t*)F->gate.q;
+                const int8_t* U = (const int8_t*)F->up.q;
+                switch (d / 512) {
+                    case 2: k_sf_gateup_q8<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
+                    case 4: k_sf_gateup_q8<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
+                    case 8: k_sf_gateup_q8<8><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
+                }
             }
-            k_sf_down<PI_QT_Q4_0><<<dim3((unsigned)(d / 1024), (unsigned)nsplit), 256, 0, st>>>(
-                (const uint8_t*)F->down_q, F->down_d, mask, h, (int)t0, nt, d, n_ff, per_split, out);
-        } else {
-            const int8_t* G = (const int8_t*)F->gate.q;
-            const int8_t* U = (const int8_t*)F->up.q;
-            switch (d / 512) {
-                case 2: k_sf_gateup_q8<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
-                case 4: k_sf_gateup_q8<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
-                case 8: k_sf_gateup_q8<8><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, xq, xs, (int)t0, d, n_ff, h); break;
-            }
+            k_sf_swiglu<<<dim3(nblocks(n_ff, 256), nt), 256, 0, st>>>(mask, list, n_list, gu, n_ff, h);
+        }
+        if (F->qtype == PI_QT_Q8_0)
             k_sf_requant_dense<<<dim3(nblocks(n_ff, 256), nt), 256, 0, st>>>(ptr, (int)t0, nt, n_ff, h);
-            k_sf_down<PI_QT_Q8_0><<<dim3((unsigned)(d / 1024), (unsigned)nsplit), 256, 0, st>>>(
-                (const uint8_t*)F->down_q, F->down_d, mask, h, (int)t0, nt, d, n_ff, per_split, out);
+        {
+            PiProfScope ps(ctx, st, "k_sf_down");
+            const dim3 dg((unsigned)(d / 1024), (unsigned)((n_ff + SFD - 1) / SFD));
+            if (F->qtype == PI_QT_Q4_0)
+                k_sf_down<PI_QT_Q4_0><<<dg, 256, 0, st>>>((const uint8_t*)F->down_q, F->down_d, mask, list, n_list, h,
+                                                          (int)t0, nt, d, n_ff, out);
+            else
+                k_sf_down<PI_QT_Q8_0><<<dg, 256, 0, st>>>((const uint8_t*)F->down_q, F->down_d, mask, list, n_list, h,
+                                                          (int)t0, nt, d, n_ff, out);
         }
         LAUNCH_CHECK("sparse ffn");
     }
