@@ -8,7 +8,8 @@
 // exactly to f16 and multiplied with tcgen05.mma kind::f16: every product and
 // every partial sum of a block is an integer below 2^20, so the f32 result in
 // TMEM is exactly (float)sumi_b. One MMA group per 32-element block writes a
-// fresh accumulator into one of DB TMEM buffers; epilogue warps apply the
+// fresh accumulator; a stage carries PB = 2 blocks (one handshake for both) into
+// the two column halves of one of DB TMEM buffers; epilogue warps apply each
 // block's scales and add it to f32 registers in block order, so each output is
 // the reference's own sequence of roundings. The gate/up kernel stacks 64 gate
 // rows over the same 64 up rows in one 128-row tile, applies the reference's
@@ -41,12 +42,14 @@ constexpr int NEPI = 16, NCONV = 8;
 constexpr int QT = (NEPI + NCONV + 2) * 32;
 constexpr int G4 = 4;              // blocks per raw group
 constexpr int RG = 3;              // raw groups in flight
-constexpr int TS = 3;              // f16 tile stages
-constexpr int DB = 4;              // TMEM block buffers of QN columns
+constexpr int PB = 2;              // blocks per stage (one handshake)
+constexpr int TS = 3;              // f16 tile stages of PB blocks
+constexpr int DB = 2;              // TMEM buffers of PB x QN columns
 constexpr int TILE = 128 * 64;     // 128 rows x 32 f16
+constexpr int STAGE = PB * 2 * TILE;  // {W tile, X tile} per block
 constexpr int RAWW = 128 * G4 * 32;  // weight rows of a group (16 KB)
 constexpr int RAWG = 2 * RAWW;       // + activation rows
-constexpr size_t QSMEM = (size_t)RG * RAWG + (size_t)TS * 2 * TILE + 1024;
+constexpr size_t QSMEM = (size_t)RG * RAWG + (size_t)TS * STAGE + 1024;
 
 // 32 int8 (two 16-byte words) -> 32 exact f16 in swizzled row r of a SW64 tile:
 // 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128, so subtracting 1152 gives b.
@@ -75,12 +78,12 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                                                        const __grid_constant__ CUtensorMap mx, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* tiles = sm;                 // TS stages of {W tile, X tile}
-    uint8_t* raws = sm + TS * 2 * TILE;  // RG groups of {W rows, X rows}
+    uint8_t* tiles = sm;              // TS stages of PB x {W tile, X tile}
+    uint8_t* raws = sm + TS * STAGE;  // RG groups of {W rows, X rows}
     __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[DB];
     __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG];
-    __shared__ __align__(16) float s_dw[DB][128];
-    __shared__ __align__(16) float s_dx[DB][QN];
+    __shared__ __align__(16) float s_dw[DB][PB][128];
+    __shared__ __align__(16) float s_dx[DB][PB][QN];
     __shared__ uint32_t s_tmem;
     __shared__ int s_row[QN];  // gate/up: token of each slot column; down: slot
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -89,7 +92,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     const int4 item = a.items[it];
     const bool sh = item.x == a.E;
     const int K = MODE == 0 ? a.d : a.f;
-    const int nb = K / 32, ng = nb / G4;
+    const int nb = K / 32, ng = nb / G4, np = nb / PB;
     const int nn = (item.z + 15) & ~15;
 
     if (tid == 0) {
@@ -114,7 +117,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(DB * QN)
+                     "r"(DB * PB * QN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -206,14 +209,18 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             if (!mbar_wait(&raw_full[slot], (q / RG) & 1)) { ok = false; break; }
             const uint8_t* rg = raws + slot * RAWG;
 #pragma unroll
-            for (int i = 0; i < G4; ++i) {
-                const int g = G4 * q + i, ts = g % TS, db = g % DB;
+            for (int pi = 0; pi < G4 / PB; ++pi) {
+                const int g = (G4 / PB) * q + pi, ts = g % TS, db = g % DB;  // g: stage (block pair) index
                 if (g >= TS && !mbar_wait(&tile_free[ts], (g / TS - 1) & 1)) { ok = false; break; }
                 if (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1)) { ok = false; break; }
-                int8_row_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, 0)),
-                                *reinterpret_cast<const uint4*>(raw_half(rg, i, 1)),
-                                tiles + ts * 2 * TILE + (isx ? TILE : 0), row);
-                (isx ? s_dx[db] : s_dw[db])[row] = sc_cur[i];
+#pragma unroll
+                for (int b = 0; b < PB; ++b) {
+                    const int i = PB * pi + b;
+                    int8_row_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, 0)),
+                                    *reinterpret_cast<const uint4*>(raw_half(rg, i, 1)),
+                                    tiles + ts * STAGE + b * 2 * TILE + (isx ? TILE : 0), row);
+                    (isx ? s_dx[db][b] : s_dw[db][b])[row] = sc_cur[i];
+                }
                 fence_async_smem();
                 __syncwarp();
                 if (lane == 0) {
@@ -230,7 +237,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         // ---- MMA issuer ----
         if (lane == 0) {
             const uint32_t id = idesc(nn);
-            for (int g = 0; g < nb; ++g) {
+            for (int g = 0; g < np; ++g) {
                 const int ts = g % TS, db = g % DB;
                 if (!mbar_wait(&tile_full[ts], (g / TS) & 1) ||
                     (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1))) {
@@ -238,10 +245,13 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                     break;
                 }
                 tc_fence_after();
-                const uint8_t* wt = tiles + ts * 2 * TILE;
-                const uint32_t dcol = tmem + db * QN;
-                mma_f16(dcol, umma_desc(wt, 0), umma_desc(wt + TILE, 0), id, 0u);
-                mma_f16(dcol, umma_desc(wt, 32), umma_desc(wt + TILE, 32), id, 1u);
+#pragma unroll
+                for (int b = 0; b < PB; ++b) {  // block b -> a fresh accumulator in column half b
+                    const uint8_t* wt = tiles + ts * STAGE + b * 2 * TILE;
+                    const uint32_t dcol = tmem + (db * PB + b) * QN;
+                    mma_f16(dcol, umma_desc(wt, 0), umma_desc(wt + TILE, 0), id, 0u);
+                    mma_f16(dcol, umma_desc(wt, 32), umma_desc(wt + TILE, 32), id, 1u);
+                }
                 mma_commit(&tile_free[ts]);
                 mma_commit(&d_full[db]);
             }
@@ -254,7 +264,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         float acc[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-        for (int g = 0; g < nb; ++g) {
+        for (int g = 0; g < np; ++g) {
             const int db = g % DB;
             if (!mbar_wait(&d_full[db], (g / DB) & 1) || !mbar_wait(&scl_full[db], (g / DB) & 1)) {
                 ok = false;
@@ -262,19 +272,22 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             }
             tc_fence_after();
             if (live) {
-                const float dw = s_dw[db][rl];
 #pragma unroll
-                for (int hh = 0; hh < 2; ++hh) {
-                    float v[16];
-                    tmem_ld16(tmem + lane_base + db * QN + 32 * cg + 16 * hh, v);
+                for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
+                    const float dw = s_dw[db][b][rl];
 #pragma unroll
-                    for (int j4 = 0; j4 < 4; ++j4) {
-                        const float4 dx = *reinterpret_cast<const float4*>(&s_dx[db][32 * cg + 16 * hh + 4 * j4]);
-                        float* ac = &acc[16 * hh + 4 * j4];
-                        ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw, dx.x)));
-                        ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw, dx.y)));
-                        ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw, dx.z)));
-                        ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw, dx.w)));
+                    for (int hh = 0; hh < 2; ++hh) {
+                        float v[16];
+                        tmem_ld16(tmem + lane_base + (db * PB + b) * QN + 32 * cg + 16 * hh, v);
+#pragma unroll
+                        for (int j4 = 0; j4 < 4; ++j4) {
+                            const float4 dx = *reinterpret_cast<const float4*>(&s_dx[db][b][32 * cg + 16 * hh + 4 * j4]);
+                            float* ac = &acc[16 * hh + 4 * j4];
+                            ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw, dx.x)));
+                            ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw, dx.y)));
+                            ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw, dx.z)));
+                            ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw, dx.w)));
+                        }
                     }
                 }
             }
@@ -317,7 +330,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * QN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * PB * QN) : "memory");
 }
 
 // Q8_0 weight rows for the TMA producer: gate/up [rows][d] bytes (box 64 B x 64 rows),
