@@ -275,260 +275,326 @@ __global__ void k_pred_layer(const float* __restrict__ in, int64_t T, int64_t n_
 // --------------------------------------------------------------------------
 // Hot-neuron sparse FFN (C-ABI pi_sparse_ffn_*).
 // --------------------------------------------------------------------------
-constexpr int SF_TMAX = 8;  // tokens per mask pass
+constexpr int SF_TMAX = 8;             // tokens per pass (one byte of mask bits per neuron)
+constexpr int SF_GPC = 2;              // 32-neuron groups per down CTA
+constexpr int64_t SF_MAX_FF = 131072;  // the pass plan keeps a byte per neuron in shared memory
 
-// mask[s] bit t (t < SF_TMAX within the pass) = neuron s active for token t0+t.
-__global__ void k_sf_mask(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx, int t0, int nt,
-                          int64_t n_ff, uint32_t* __restrict__ mask, uint32_t* err) {
-    const int t = blockIdx.y;
-    if (t >= nt) return;
-    const int64_t beg = ptr[t0 + t], end = ptr[t0 + t + 1];
-    const int64_t cnt = end - beg;
-    if (cnt >= n_ff) {  // dense path (quant/mod.rs:1221-1223)
-        for (int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; s < n_ff; s += gridDim.x * (int64_t)blockDim.x)
-            atomicOr(&mask[s], 1u << t);
-        return;
-    }
-    for (int64_t q = beg + blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < end; q += gridDim.x * (int64_t)blockDim.x) {
+// Pass plan (one CTA of 1024 threads) for tokens t0 .. t0+nt-1 of the CSR index
+// lists: mask[s] bit t = neuron s active for token t0+t (one byte per neuron);
+// list[0 .. n) = the active neurons in ascending order; gofs[g] = list position of
+// the first active neuron of 32-neuron group g, gofs[n_ff / 32] = n. A token whose
+// list covers all n_ff neurons takes every neuron (quant/mod.rs:1221-1223). The
+// pass's output rows are zeroed here for the down kernel's atomics.
+__global__ __launch_bounds__(1024) void k_sf_plan(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
+                                                  int t0, int nt, int64_t n_ff, int64_t n_embd, uint8_t* __restrict__ mask,
+                                                  int32_t* __restrict__ list, int32_t* __restrict__ gofs,
+                                                  float* __restrict__ out, uint32_t* err) {
+    extern __shared__ uint32_t sf_sm[];
+    __shared__ int32_t wsum[32];
+    __shared__ int64_t s_ptr[SF_TMAX + 1];
+    const int ng = (int)(n_ff / 32);
+    uint32_t* bits = sf_sm;  // byte s = token bits of neuron s
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid <= nt) s_ptr[tid] = ptr[t0 + tid];
+    for (int i = tid; i < n_ff / 4; i += 1024) bits[i] = 0;
+    float4* o4 = reinterpret_cast<float4*>(out + (int64_t)t0 * n_embd);
+    for (int64_t i = tid; i < nt * n_embd / 4; i += 1024) o4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    uint32_t dense = 0;  // token bits of the complete lists, in every byte
+    for (int t = 0; t < nt; ++t)
+        if (s_ptr[t + 1] - s_ptr[t] >= n_ff) dense |= 0x01010101u << t;
+    for (int64_t q = s_ptr[0] + tid; q < s_ptr[nt]; q += 1024) {  // every token's entries at once
+        int t = 0;
+        while (q >= s_ptr[t + 1]) ++t;
+        if ((dense >> t) & 1u) continue;
         const int64_t s = idx[q];
         if (s < 0 || s >= n_ff) { atomicOr(err, PI_DEVERR_INDEX); continue; }
-        atomicOr(&mask[s], 1u << t);
+        atomicOr(&bits[s >> 2], 1u << (8 * (s & 3) + t));
     }
+    __syncthreads();
+    int carry = 0;  // thread per group: 32 mask bytes -> count -> exclusive scan -> list
+    for (int g0 = 0; g0 < ng; g0 += 1024) {
+        const int g = g0 + tid;
+        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
+        uint32_t act = 0;
+        if (g < ng) {
+            w0 = *reinterpret_cast<const uint4*>(bits + 8 * g);
+            w1 = *reinterpret_cast<const uint4*>(bits + 8 * g + 4);
+            const uint32_t w[8] = {w0.x | dense, w0.y | dense, w0.z | dense, w0.w | dense,
+                                   w1.x | dense, w1.y | dense, w1.z | dense, w1.w | dense};
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+                const uint32_t nz = __vcmpne4(w[k], 0u);  // 0xff per active neuron
+                act |= ((nz & 1u) | ((nz >> 7) & 2u) | ((nz >> 14) & 4u) | ((nz >> 21) & 8u)) << (4 * k);
+            }
+            uint4* m4 = reinterpret_cast<uint4*>(mask + 32 * (int64_t)g);
+            m4[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            m4[1] = make_uint4(w[4], w[5], w[6], w[7]);
+        }
+        const int v = __popc(act);
+        int x = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, x, o);
+            if (lane >= o) x += y;
+        }
+        if (lane == 31) wsum[warp] = x;
+        __syncthreads();
+        if (warp == 0) {
+            int z = wsum[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, z, o);
+                if (lane >= o) z += y;
+            }
+            wsum[lane] = z;
+        }
+        __syncthreads();
+        if (g < ng) {
+            int pos = carry + (warp ? wsum[warp - 1] : 0) + x - v;
+            gofs[g] = pos;
+            for (uint32_t a = act; a; a &= a - 1) list[pos++] = 32 * g + __ffs(a) - 1;
+        }
+        carry += wsum[31];
+        __syncthreads();
+    }
+    if (tid == 0) gofs[ng] = carry;
 }
 
 // gate/up for masked neurons: warp per neuron, BPL blocks per lane
 // (n_embd = 32 * 32 * BPL). Q4_0 (f32 x) and Q8_0 (quantised x) variants.
 PI_DEV float nibf(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616.0f; }
-PI_DEV float q4dot16(const int4 wv, const float* __restrict__ x) {
-    const uint32_t wd[4] = {(uint32_t)wv.x, (uint32_t)wv.y, (uint32_t)wv.z, (uint32_t)wv.w};
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-        const float4 xa = *reinterpret_cast<const float4*>(x + 8 * i);
-        const float4 xb = *reinterpret_cast<const float4*>(x + 8 * i + 4);
-        const uint32_t v = wd[i];
-        s += nibf(v & 15u) * xa.x;
-        s += nibf((v >> 4) & 15u) * xa.y;
-        s += nibf((v >> 8) & 15u) * xa.z;
-        s += nibf((v >> 12) & 15u) * xa.w;
-        s += nibf((v >> 16) & 15u) * xb.x;
-        s += nibf((v >> 20) & 15u) * xb.y;
-        s += nibf((v >> 24) & 15u) * xb.z;
-        s += nibf(v >> 28) * xb.w;
-    }
-    return s;
-}
-
 // gate and up blocks against the same 32 activations (one pass over x)
 PI_DEV void q4dot16x2(const int4 wg, const int4 wu, const float* __restrict__ x, float& sg, float& su) {
-    const uint32_t g4[4] = {(uint32_t)wg.x, (uint32_t)wg.y, (uint32_t)wg.z, (uint32_t)wg.w};
-    const uint32_t u4[4] = {(uint32_t)wu.x, (uint32_t)wu.y, (uint32_t)wu.z, (uint32_t)wu.w};
+    uint32_t g0 = wg.x, g1 = wg.y, g2 = wg.z, g3 = wg.w, u0 = wu.x, u1 = wu.y, u2 = wu.z, u3 = wu.w;
     sg = 0.f;
     su = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
+#pragma unroll 1
+    for (int i = 0; i < 4; ++i) {  // rolled (register pressure): word i of each block is g0 / u0
         const float4 xa = *reinterpret_cast<const float4*>(x + 8 * i);
         const float4 xb = *reinterpret_cast<const float4*>(x + 8 * i + 4);
         const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-            sg += nibf((g4[i] >> (4 * j)) & 15u) * xv[j];
-            su += nibf((u4[i] >> (4 * j)) & 15u) * xv[j];
+            sg += nibf((g0 >> (4 * j)) & 15u) * xv[j];
+            su += nibf((u0 >> (4 * j)) & 15u) * xv[j];
         }
+        g0 = g1; g1 = g2; g2 = g3;
+        u0 = u1; u1 = u2; u2 = u3;
+    }
+}
+
+// gate/up for the pass's active neurons: CTA = SF_NPC list entries, one warp per
+// (entry, chunk of the row); the chunks' partial dots are summed in chunk order and
+// the first SF_NPC threads write (g, u).
+// Q4_0: chunk = 32 blocks (1024 inputs) and each token's f32 activations are staged
+// in shared memory with 32-float blocks 36 floats apart, so the lanes' float4 reads
+// (lane = block) fall in distinct banks. Q8_0: chunk = 512 inputs of the quantised
+// activations (lane = 16 bytes, two lanes per block).
+constexpr int SF_NPC = 4;
+PI_DEV void sf_finish(const float2 (*part)[8], int nch, const int* s_s, const uint8_t* s_m, int t, int64_t n_ff,
+                      float2* __restrict__ gu) {
+    const int n = threadIdx.x;
+    if (n < SF_NPC && ((s_m[n] >> t) & 1u)) {
+        float g = 0.f, u = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            g += part[n][c].x;
+            u += part[n][c].y;
+        }
+        gu[(int64_t)t * n_ff + s_s[n]] = make_float2(g, u);
     }
 }
 
 template <int BPL>
-__global__ __launch_bounds__(256) void k_sf_gateup_q4(const uint8_t* __restrict__ G, const uint8_t* __restrict__ U,
-                                                      const __half* __restrict__ GD, const __half* __restrict__ UD,
-                                                      const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
-                                                      const int32_t* __restrict__ n_list, const float* __restrict__ x,
-                                                      int t0, int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
+__global__ __launch_bounds__(SF_NPC * BPL * 32) void k_sf_gateup_q4(
+    const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
+    const __half* __restrict__ UD, const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
+    const int32_t* __restrict__ n_list, const float* __restrict__ x, int t0, int nt, int64_t n_embd, int64_t n_ff,
+    float2* __restrict__ gu) {
+    __shared__ __align__(16) float xsm[BPL * 32 * 36];
+    __shared__ float2 part[SF_NPC][8];
+    __shared__ int s_s[SF_NPC];
+    __shared__ uint8_t s_m[SF_NPC];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t li = blockIdx.x * 8LL + warp;
-    if (li >= *n_list) return;
-    const int64_t s = list[li];
-    uint32_t m = mask[s];
-    const int64_t nb = n_embd / 32;
-    int4 wg[BPL], wu[BPL];
-    float sg[BPL], su[BPL];
-#pragma unroll
-    for (int c = 0; c < BPL; ++c) {
-        const int64_t b = lane + 32 * c;
-        wg[c] = ld_stream(G + s * (n_embd / 2) + b * 16);
-        wu[c] = ld_stream(U + s * (n_embd / 2) + b * 16);
-        sg[c] = __half2float(GD[s * nb + b]);
-        su[c] = __half2float(UD[s * nb + b]);
+    const int nw = warp / BPL, c = warp % BPL;
+    const int n_act = *n_list;
+    if (blockIdx.x * (int64_t)SF_NPC >= n_act) return;  // whole CTA
+    const int64_t li = blockIdx.x * (int64_t)SF_NPC + nw;
+    const int64_t nb = n_embd / 32, b = lane + 32 * c;
+    uint32_t m = 0;
+    int64_t s = 0;
+    int4 wg = make_int4(0, 0, 0, 0), wu = wg;
+    float sg = 0.f, su = 0.f;
+    if (li < n_act) {
+        s = list[li];
+        m = mask[s];
+        wg = ld_stream(G + s * (n_embd / 2) + b * 16);
+        wu = ld_stream(U + s * (n_embd / 2) + b * 16);
+        sg = __half2float(GD[s * nb + b]);
+        su = __half2float(UD[s * nb + b]);
     }
-    while (m) {
-        const int t = __ffs(m) - 1;
-        m &= m - 1;
-        const float* xr = x + (int64_t)(t0 + t) * n_embd;
-        float ag = 0.f, au = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < BPL; ++c) {
+    if (c == 0 && lane == 0) {
+        s_s[nw] = (int)s;
+        s_m[nw] = (uint8_t)m;
+    }
+    for (int t = 0; t < nt; ++t) {
+        if (!__syncthreads_or((m >> t) & 1u)) continue;  // also: the previous token is finished
+        const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)(t0 + t) * n_embd);
+        for (int k = threadIdx.x; k < BPL * 256; k += SF_NPC * BPL * 32)
+            *reinterpret_cast<float4*>(&xsm[36 * (k >> 3) + 4 * (k & 7)]) = xr[k];
+        __syncthreads();
+        if ((m >> t) & 1u) {
             float dg, du;
-            q4dot16x2(wg[c], wu[c], xr + (lane + 32 * c) * 32, dg, du);
-            ag += sg[c] * dg;
-            au += su[c] * du;
+            q4dot16x2(wg, wu, xsm + 36 * b, dg, du);
+            dg = warp_sum(sg * dg);
+            du = warp_sum(su * du);
+            if (lane == 0) part[nw][c] = make_float2(dg, du);
         }
-        ag = warp_sum(ag);
-        au = warp_sum(au);
-        if (lane == 0) gu[(int64_t)t * n_ff + s] = make_float2(ag, au);
+        __syncthreads();
+        sf_finish(part, BPL, s_s, s_m, t, n_ff, gu);
     }
 }
 
 template <int CPL>
-__global__ __launch_bounds__(256) void k_sf_gateup_q8(const int8_t* __restrict__ G, const int8_t* __restrict__ U,
-                                                      const __half* __restrict__ GD, const __half* __restrict__ UD,
-                                                      const uint32_t* __restrict__ mask,
-                                                      const int32_t* __restrict__ list,
-                                                      const int32_t* __restrict__ n_list,
-                                                      const int8_t* __restrict__ xq, const float* __restrict__ xs,
-                                                      int t0, int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
+__global__ __launch_bounds__(2 * CPL * 32) void k_sf_gateup_q8(
+    const int8_t* __restrict__ G, const int8_t* __restrict__ U, const __half* __restrict__ GD,
+    const __half* __restrict__ UD, const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
+    const int32_t* __restrict__ n_list, const int8_t* __restrict__ xq, const float* __restrict__ xs, int t0, int nt,
+    int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
+    constexpr int NPC = 2;  // list entries per CTA (CPL warps each)
+    __shared__ float2 part[SF_NPC][8];
+    __shared__ int s_s[SF_NPC];
+    __shared__ uint8_t s_m[SF_NPC];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int64_t li = blockIdx.x * 8LL + warp;
-    if (li >= *n_list) return;
-    const int64_t s = list[li];
-    uint32_t m = mask[s];
-    const int64_t nb = n_embd / 32;
-    int4 wg[CPL], wu[CPL];
-    float sg[CPL], su[CPL];
-#pragma unroll
-    for (int c = 0; c < CPL; ++c) {
-        const int64_t ch = lane + 32 * c;
-        wg[c] = ld_stream(G + s * n_embd + ch * 16);
-        wu[c] = ld_stream(U + s * n_embd + ch * 16);
-        sg[c] = __half2float(GD[s * nb + (ch >> 1)]);
-        su[c] = __half2float(UD[s * nb + (ch >> 1)]);
-    }
-    const bool even = (lane & 1) == 0;
-    while (m) {
-        const int t = __ffs(m) - 1;
-        m &= m - 1;
-        const int8_t* xr = xq + (int64_t)(t0 + t) * n_embd;
-        const float* sr = xs + (int64_t)(t0 + t) * nb;
-        float ag = 0.f, au = 0.f;
-#pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-            const int64_t ch = lane + 32 * c;
-            const int4 xv = *reinterpret_cast<const int4*>(xr + ch * 16);
-            const float sx = even ? sr[ch >> 1] : 0.f;
-            int a = dp4a(wg[c].x, xv.x, 0);
-            a = dp4a(wg[c].y, xv.y, a);
-            a = dp4a(wg[c].z, xv.z, a);
-            a = dp4a(wg[c].w, xv.w, a);
-            int b = dp4a(wu[c].x, xv.x, 0);
-            b = dp4a(wu[c].y, xv.y, b);
-            b = dp4a(wu[c].z, xv.z, b);
-            b = dp4a(wu[c].w, xv.w, b);
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            b += __shfl_xor_sync(0xffffffffu, b, 1);
-            ag += (float)a * (sg[c] * sx);
-            au += (float)b * (su[c] * sx);
-        }
-        ag = warp_sum(ag);
-        au = warp_sum(au);
-        if (lane == 0) gu[(int64_t)t * n_ff + s] = make_float2(ag, au);
-    }
-}
-
-// Active-neuron list of a pass: list[0 .. *n_list) = the neurons with a mask bit
-// (any order: every neuron is independent, and the down sums are split anyway).
-__global__ void k_sf_compact(const uint32_t* __restrict__ mask, int64_t n_ff, int32_t* __restrict__ list,
-                             int32_t* __restrict__ n_list) {
-    const int64_t s = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    if (s < n_ff && mask[s]) list[atomicAdd(n_list, 1)] = (int32_t)s;
-}
-
-// h = SwiGLU(g, u) (quant/mod.rs:1196-1199) of every active (token, neuron), kept
-// out of the product kernels: the reference exp's double-precision evaluation
-// needs many registers. grid (ceil(n_ff / 256), nt).
-__global__ void k_sf_swiglu(const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
-                            const int32_t* __restrict__ n_list, const float2* __restrict__ gu, int64_t n_ff,
-                            float* __restrict__ h) {
-    const int64_t li = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
-    const int t = blockIdx.y;
-    if (li >= *n_list) return;
-    const int64_t s = list[li];
-    if (!((mask[s] >> t) & 1u)) return;
-    const float2 v = gu[(int64_t)t * n_ff + s];
-    h[(int64_t)t * n_ff + s] = swiglu_ref(v.x, v.y);
-}
-
-// down, neuron-major: CTA = (column tile of 1024 outputs, chunk of SFD active
-// neurons); thread owns 4 consecutive columns; y accumulated with atomicAdd
-// over the chunks.
-constexpr int SFD = 16;
-template <int QT>
-__global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
-                                                 const uint32_t* __restrict__ mask, const int32_t* __restrict__ list,
-                                                 const int32_t* __restrict__ n_list, const float* __restrict__ h,
-                                                 int t0, int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y) {
-    const int64_t c = blockIdx.x * 1024LL + threadIdx.x * 4;
+    const int nw = warp / CPL, c = warp % CPL;
     const int n_act = *n_list;
-    const int i0 = blockIdx.y * SFD;
-    if (c >= n_embd || i0 >= n_act) return;
-    const int i1 = min(n_act, i0 + SFD);
-    float acc[SF_TMAX][4];
-#pragma unroll
-    for (int t = 0; t < SF_TMAX; ++t)
-#pragma unroll
-        for (int q = 0; q < 4; ++q) acc[t][q] = 0.f;
-#pragma unroll 4
-    for (int i = i0; i < i1; ++i) {
-        const int64_t s = list[i];
-        const uint32_t m = mask[s];
-        const uint2 sv = *reinterpret_cast<const uint2*>(DS + (s >> 5) * n_embd + c);
-        float sc[4];
-        sc[0] = __half2float(__ushort_as_half((uint16_t)(sv.x & 0xffff)));
-        sc[1] = __half2float(__ushort_as_half((uint16_t)(sv.x >> 16)));
-        sc[2] = __half2float(__ushort_as_half((uint16_t)(sv.y & 0xffff)));
-        sc[3] = __half2float(__ushort_as_half((uint16_t)(sv.y >> 16)));
-        float w[4];
-        if (QT == PI_QT_Q4_0) {
-            const uint16_t v = *reinterpret_cast<const uint16_t*>(DQ + s * (n_embd / 2) + c / 2);
-            w[0] = nibf(v & 15u) * sc[0];
-            w[1] = nibf((v >> 4) & 15u) * sc[1];
-            w[2] = nibf((v >> 8) & 15u) * sc[2];
-            w[3] = nibf((v >> 12) & 15u) * sc[3];
-        } else {
-            const uint32_t v = *reinterpret_cast<const uint32_t*>(DQ + s * n_embd + c);
-            w[0] = (float)(int8_t)(v & 0xff) * sc[0];
-            w[1] = (float)(int8_t)((v >> 8) & 0xff) * sc[1];
-            w[2] = (float)(int8_t)((v >> 16) & 0xff) * sc[2];
-            w[3] = (float)(int8_t)(v >> 24) * sc[3];
+    if (blockIdx.x * (int64_t)NPC >= n_act) return;
+    const int64_t li = blockIdx.x * (int64_t)NPC + nw;
+    const int64_t nb = n_embd / 32, ch = lane + 32 * c;
+    uint32_t m = 0;
+    int64_t s = 0;
+    int4 wg = make_int4(0, 0, 0, 0), wu = wg;
+    float sg = 0.f, su = 0.f;
+    if (li < n_act) {
+        s = list[li];
+        m = mask[s];
+        wg = ld_stream(G + s * n_embd + ch * 16);
+        wu = ld_stream(U + s * n_embd + ch * 16);
+        sg = __half2float(GD[s * nb + (ch >> 1)]);
+        su = __half2float(UD[s * nb + (ch >> 1)]);
+    }
+    if (threadIdx.x < SF_NPC) s_m[threadIdx.x] = 0;
+    __syncthreads();
+    if (c == 0 && lane == 0) {
+        s_s[nw] = (int)s;
+        s_m[nw] = (uint8_t)m;
+    }
+    for (int t = 0; t < nt; ++t) {
+        if ((m >> t) & 1u) {
+            const int4 xv = *reinterpret_cast<const int4*>(xq + (int64_t)(t0 + t) * n_embd + ch * 16);
+            const float sx = (lane & 1) == 0 ? xs[(int64_t)(t0 + t) * nb + (ch >> 1)] : 0.f;
+            int a = dp4a(wg.x, xv.x, 0);
+            a = dp4a(wg.y, xv.y, a);
+            a = dp4a(wg.z, xv.z, a);
+            a = dp4a(wg.w, xv.w, a);
+            int bb = dp4a(wu.x, xv.x, 0);
+            bb = dp4a(wu.y, xv.y, bb);
+            bb = dp4a(wu.z, xv.z, bb);
+            bb = dp4a(wu.w, xv.w, bb);
+            a += __shfl_xor_sync(0xffffffffu, a, 1);
+            bb += __shfl_xor_sync(0xffffffffu, bb, 1);
+            const float dg = warp_sum((float)a * (sg * sx)), du = warp_sum((float)bb * (su * sx));
+            if (lane == 0) part[nw][c] = make_float2(dg, du);
         }
+        __syncthreads();
+        sf_finish(part, CPL, s_s, s_m, t, n_ff, gu);
+        __syncthreads();
+    }
+}
+
+// down, neuron-major, over the pass plan: CTA = (512 output columns, SF_GPC
+// 32-neuron groups); thread owns 2 consecutive columns. The CTA first stages its
+// groups' active neurons, h = SwiGLU(g, u) (quant/mod.rs:1196-1199) of every
+// (token, neuron) and the thread's block scales of each group, then runs over the
+// neurons with independent weight loads; y is accumulated with float2 atomics over
+// the group chunks. Q8_0 weights and a token whose list is complete: the reference
+// then takes the dense ffn_swiglu_q, whose down projection re-quantises h to Q8_0
+// blocks (quant/mod.rs:1203), so such a token's h is replaced by its Q8_0 value q * d.
+template <int QT, int NTM>
+__global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
+                                                 const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
+                                                 const int32_t* __restrict__ gofs, const float2* __restrict__ gu,
+                                                 const int64_t* __restrict__ ptr, int t0, int nt, int64_t n_embd,
+                                                 int64_t n_ff, float* __restrict__ y) {
+    __shared__ int32_t s_list[SF_GPC * 32];
+    __shared__ float s_h[NTM][SF_GPC * 32];
+    __shared__ float2 s_sc[SF_GPC][256];
+    const int ng = (int)(n_ff / 32);
+    const int g0 = blockIdx.y * SF_GPC, g1 = min(ng, g0 + SF_GPC);
+    const int i0 = gofs[g0], n = gofs[g1] - i0;
+    if (n == 0) return;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t c = blockIdx.x * 512LL + 2 * tid;
+    if (tid < n) {
+        const int s = list[i0 + tid];
+        s_list[tid] = s;
+        const uint32_t m = mask[s];
 #pragma unroll
-        for (int t = 0; t < SF_TMAX; ++t) {
-            if ((m >> t) & 1u) {
-                const float hv = h[(int64_t)t * n_ff + s];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) acc[t][q] += hv * w[q];
+        for (int t = 0; t < NTM; ++t) {
+            float h = 0.f;
+            if (t < nt && ((m >> t) & 1u)) {
+                const float2 v = gu[(int64_t)t * n_ff + s];
+                h = swiglu_ref(v.x, v.y);
+            }
+            s_h[t][tid] = h;
+        }
+    }
+    for (int gi = 0; gi < g1 - g0; ++gi) {
+        float2 sc = make_float2(0.f, 0.f);
+        if (gofs[g0 + gi + 1] > gofs[g0 + gi])
+            sc = __half22float2(*reinterpret_cast<const __half2*>(DS + (int64_t)(g0 + gi) * n_embd + c));
+        s_sc[gi][tid] = sc;
+    }
+    if (QT == PI_QT_Q8_0) {
+        __syncthreads();
+        for (int t = 0; t < nt && t < NTM; ++t) {
+            if (ptr[t0 + t + 1] - ptr[t0 + t] < n_ff) continue;
+            if (warp < g1 - g0) {  // dense: group warp's 32 neurons are list entries 32 warp .. +31
+                float sc;
+                const int8_t q = warp_quant_q8(s_h[t][32 * warp + lane], &sc);
+                s_h[t][32 * warp + lane] = fmul((float)q, sc);
             }
         }
     }
-    for (int t = 0; t < nt; ++t)
+    __syncthreads();
+    float acc[NTM][2];
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (acc[t][q] != 0.f) atomicAdd(&y[(int64_t)(t0 + t) * n_embd + c + q], acc[t][q]);
-}
-
-// Q8_0 weights, token with a full index list: the reference then takes the
-// dense ffn_swiglu_q (quant/mod.rs:1221-1223), whose down projection
-// re-quantises h to Q8_0 blocks (quant/mod.rs:1203). Replace such a token's h
-// by its Q8_0 value q * d so the f32 down kernel sums the same quantities.
-__global__ void k_sf_requant_dense(const int64_t* __restrict__ ptr, int t0, int nt, int64_t n_ff,
-                                   float* __restrict__ h) {
-    const int t = blockIdx.y;
-    if (t >= nt || ptr[t0 + t + 1] - ptr[t0 + t] < n_ff) return;
-    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (b * 32 >= n_ff) return;
-    float* hr = h + (int64_t)t * n_ff + b * 32;
-    float sc;
-    const int8_t q = warp_quant_q8(hr[lane], &sc);
-    hr[lane] = fmul((float)q, sc);
+    for (int t = 0; t < NTM; ++t) acc[t][0] = acc[t][1] = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < n; ++i) {
+        const int s = s_list[i];
+        const float2 sc = s_sc[(s >> 5) - g0][tid];
+        float w0, w1;
+        if (QT == PI_QT_Q4_0) {
+            const uint32_t v = DQ[(int64_t)s * (n_embd / 2) + (c >> 1)];
+            w0 = nibf(v & 15u) * sc.x;
+            w1 = nibf(v >> 4) * sc.y;
+        } else {
+            const uint32_t v = *reinterpret_cast<const uint16_t*>(DQ + (int64_t)s * n_embd + c);
+            w0 = (float)(int8_t)(v & 0xffu) * sc.x;
+            w1 = (float)(int8_t)(v >> 8) * sc.y;
+        }
+#pragma unroll
+        for (int t = 0; t < NTM; ++t) {
+            const float hv = s_h[t][i];
+            acc[t][0] += hv * w0;
+            acc[t][1] += hv * w1;
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < NTM; ++t)
+        if (t < nt && (acc[t][0] != 0.f || acc[t][1] != 0.f))
+            atomicAdd(reinterpret_cast<float2*>(y + (int64_t)(t0 + t) * n_embd + c), make_float2(acc[t][0], acc[t][1]));
 }
 
 // Repack GGUF down [ne0=n_ff, ne1=n_embd] to neuron-major. Thread per
@@ -760,8 +826,9 @@ extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const voi
     if (qtype != PI_QT_Q4_0 && qtype != PI_QT_Q8_0)
         return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: weights must be Q4_0 or Q8_0");
     const int64_t unit = qtype == PI_QT_Q4_0 ? 1024 : 512;
-    if (n_embd % unit || n_embd / unit > 4 || n_embd / unit < 1 || n_ff % 32 || n_embd % 1024)
-        return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: n_embd must be 1024/2048/4096, n_ff % 32 == 0");
+    if (n_embd % unit || n_embd / unit > 4 || n_embd / unit < 1 || n_ff % 32 || n_embd % 1024 || n_ff > SF_MAX_FF)
+        return pi_set_error(ctx, PI_ERR_ARG,
+                            "sparse ffn: n_embd must be 1024/2048/4096, n_ff % 32 == 0 and n_ff <= 131072");
     cudaSetDevice(ctx->device);
     pi_sparse_ffn* F = new pi_sparse_ffn();
     F->ctx = ctx;
@@ -813,16 +880,15 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
     if (T < 0 || (T > 0 && (!x || !ptr || !out))) return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: bad argument");
     if (T == 0) return PI_OK;
     cudaStream_t st = ST(stream);
-    const int64_t d = F->n_embd, n_ff = F->n_ff;
+    const int64_t d = F->n_embd, n_ff = F->n_ff, ng = n_ff / 32;
     char* scr;
-    const size_t need = (size_t)n_ff * 4 * 2 + (size_t)SF_TMAX * n_ff * 4 * 3 + (size_t)T * d + (size_t)T * (d / 32) * 4 +
-                        8192;
+    const size_t need = (size_t)n_ff * 4 * 2 + (size_t)(ng + 1) * 4 + (size_t)SF_TMAX * n_ff * 8 + (size_t)T * d +
+                        (size_t)T * (d / 32) * 4 + 8192;
     if (int rc = pi_scratch(ctx, st, need, &scr)) return rc;
     PiBump b{scr};
-    uint32_t* mask = b.take<uint32_t>(n_ff);
+    uint8_t* mask = b.take<uint8_t>(n_ff);
     int32_t* list = b.take<int32_t>(n_ff);
-    int32_t* n_list = b.take<int32_t>(1);
-    float* h = b.take<float>((size_t)SF_TMAX * n_ff);
+    int32_t* gofs = b.take<int32_t>(ng + 1);
     float2* gu = b.take<float2>((size_t)SF_TMAX * n_ff);
     int8_t* xq = nullptr;
     float* xs = nullptr;
@@ -831,49 +897,57 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         xs = b.take<float>(T * (d / 32));
         k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
     }
-    if (pi_cuda_check(ctx, cudaMemsetAsync(out, 0, sizeof(float) * T * d, st), "memset")) return PI_ERR_CUDA;
+    const int plan_smem = (int)n_ff;
+    static bool plan_attr = false;
+    if (!plan_attr) {
+        cudaFuncSetAttribute(k_sf_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SF_MAX_FF);
+        plan_attr = true;
+    }
     for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
-        if (pi_cuda_check(ctx, cudaMemsetAsync(mask, 0, sizeof(uint32_t) * (n_ff + 1 + n_ff) , st), "memset"))
-            return PI_ERR_CUDA;
         {
             PiProfScope ps(ctx, st, "k_sf_mask");
-            k_sf_mask<<<dim3(32, nt), 256, 0, st>>>(ptr, idx, (int)t0, nt, n_ff, mask, ctx->dev_err);
-            k_sf_compact<<<nblocks(n_ff, 256), 256, 0, st>>>(mask, n_ff, list, n_list);
+            k_sf_plan<<<1, 1024, plan_smem, st>>>(ptr, idx, (int)t0, nt, n_ff, d, mask, list, gofs, out, ctx->dev_err);
         }
-        const unsigned gblocks = nblocks(n_ff, 8);
+        const int32_t* n_list = gofs + ng;
         {
             PiProfScope ps(ctx, st, "k_sf_gateup");
+            const unsigned gq4 = (unsigned)((n_ff + SF_NPC - 1) / SF_NPC), gq8 = (unsigned)((n_ff + 1) / 2);
             if (F->qtype == PI_QT_Q4_0) {
                 const uint8_t* G = (const uint8_t*)F->gate.q;
                 const uint8_t* U = (const uint8_t*)F->up.q;
+#define SF_GU4(B) k_sf_gateup_q4<B><<<gq4, SF_NPC * B * 32, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, nt, d, n_ff, gu)
                 switch (d / 1024) {
-                    case 1: k_sf_gateup_q4<1><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
-                    case 2: k_sf_gateup_q4<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
-                    case 4: k_sf_gateup_q4<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, d, n_ff, gu); break;
+                    case 1: SF_GU4(1); break;
+                    case 2: SF_GU4(2); break;
+                    case 4: SF_GU4(4); break;
                 }
+#undef SF_GU4
             } else {
                 const int8_t* G = (const int8_t*)F->gate.q;
                 const int8_t* U = (const int8_t*)F->up.q;
+#define SF_GU8(C) k_sf_gateup_q8<C><<<gq8, 2 * C * 32, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, nt, d, n_ff, gu)
                 switch (d / 512) {
-                    case 2: k_sf_gateup_q8<2><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
-                    case 4: k_sf_gateup_q8<4><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
-                    case 8: k_sf_gateup_q8<8><<<gblocks, 256, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, d, n_ff, gu); break;
+                    case 2: SF_GU8(2); break;
+                    case 4: SF_GU8(4); break;
+                    case 8: SF_GU8(8); break;
                 }
+#undef SF_GU8
             }
-            k_sf_swiglu<<<dim3(nblocks(n_ff, 256), nt), 256, 0, st>>>(mask, list, n_list, gu, n_ff, h);
         }
-        if (F->qtype == PI_QT_Q8_0)
-            k_sf_requant_dense<<<dim3(nblocks(n_ff, 256), nt), 256, 0, st>>>(ptr, (int)t0, nt, n_ff, h);
         {
             PiProfScope ps(ctx, st, "k_sf_down");
-            const dim3 dg((unsigned)(d / 1024), (unsigned)((n_ff + SFD - 1) / SFD));
-            if (F->qtype == PI_QT_Q4_0)
-                k_sf_down<PI_QT_Q4_0><<<dg, 256, 0, st>>>((const uint8_t*)F->down_q, F->down_d, mask, list, n_list, h,
-                                                          (int)t0, nt, d, n_ff, out);
-            else
-                k_sf_down<PI_QT_Q8_0><<<dg, 256, 0, st>>>((const uint8_t*)F->down_q, F->down_d, mask, list, n_list, h,
-                                                          (int)t0, nt, d, n_ff, out);
+            const dim3 dg((unsigned)(d / 512), (unsigned)((ng + SF_GPC - 1) / SF_GPC));
+            const uint8_t* DQ = (const uint8_t*)F->down_q;
+#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, mask, list, gofs, gu, ptr, (int)t0, nt, d, n_ff, out)
+            if (F->qtype == PI_QT_Q4_0) {
+                if (nt == 1) SF_DOWN(PI_QT_Q4_0, 1);
+                else SF_DOWN(PI_QT_Q4_0, SF_TMAX);
+            } else {
+                if (nt == 1) SF_DOWN(PI_QT_Q8_0, 1);
+                else SF_DOWN(PI_QT_Q8_0, SF_TMAX);
+            }
+#undef SF_DOWN
         }
         LAUNCH_CHECK("sparse ffn");
     }

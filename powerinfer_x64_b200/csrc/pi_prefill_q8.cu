@@ -41,23 +41,26 @@ constexpr int QN = PI_GEMM_NT_Q8;  // slots per item (max MMA N)
 constexpr int NEPI = 16, NCONV = 8;
 constexpr int QT = (NEPI + NCONV + 2) * 32;
 constexpr int G4 = 4;              // blocks per raw group
-constexpr int RG = 3;              // raw groups in flight
+constexpr int RG = 2;              // raw groups in flight
 constexpr int PB = 2;              // blocks per stage (one handshake)
-constexpr int TS = 3;              // f16 tile stages of PB blocks
+constexpr int TS = 4;              // f16 tile stages of PB blocks
 constexpr int DB = 2;              // TMEM buffers of PB x QN columns
+constexpr int SB = 4;              // block-scale buffers (stages)
 constexpr int TILE = 128 * 64;     // 128 rows x 32 f16
 constexpr int STAGE = PB * 2 * TILE;  // {W tile, X tile} per block
 constexpr int RAWW = 128 * G4 * 32;  // weight rows of a group (16 KB)
 constexpr int RAWG = 2 * RAWW;       // + activation rows
+static_assert(G4 == 2 * PB, "a raw group fills two stages");
 constexpr size_t QSMEM = (size_t)RG * RAWG + (size_t)TS * STAGE + 1024;
 
-// 32 int8 (two 16-byte words) -> 32 exact f16 in swizzled row r of a SW64 tile:
-// 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128, so subtracting 1152 gives b.
-PI_DEV void int8_row_to_f16(const uint4 a, const uint4 b, uint8_t* tile, int r) {
-    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+// 16 int8 (one 16-byte word) -> 16 exact f16, the 16-byte chunks c0 and c0 + 1 of
+// swizzled row r of a SW64 tile: 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128,
+// so subtracting 1152 gives b.
+PI_DEV void int8x16_to_f16(const uint4 a, uint8_t* tile, int r, int c0) {
+    const uint32_t w[4] = {a.x, a.y, a.z, a.w};
     const __half2 off = __half2half2(__ushort_as_half((unsigned short)0x6480));  // 1152
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {  // 16-byte chunk c = elements 8c .. 8c+7
+    for (int c = 0; c < 2; ++c) {  // chunk c0 + c = elements 8c .. 8c+7 of the word
         uint32_t h[4];
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
@@ -68,7 +71,7 @@ PI_DEV void int8_row_to_f16(const uint4 a, const uint4 b, uint8_t* tile, int r) 
             h[2 * j] = *reinterpret_cast<const uint32_t*>(&l2);
             h[2 * j + 1] = *reinterpret_cast<const uint32_t*>(&h2);
         }
-        *reinterpret_cast<uint4*>(tile + swz(r, c)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(tile + swz(r, c0 + c)) = make_uint4(h[0], h[1], h[2], h[3]);
     }
 }
 
@@ -80,10 +83,10 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
     uint8_t* tiles = sm;              // TS stages of PB x {W tile, X tile}
     uint8_t* raws = sm + TS * STAGE;  // RG groups of {W rows, X rows}
-    __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[DB];
+    __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[SB], scl_free[SB];
     __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG];
-    __shared__ __align__(16) float s_dw[DB][PB][128];
-    __shared__ __align__(16) float s_dx[DB][PB][QN];
+    __shared__ __align__(16) float s_dw[SB][PB][128];
+    __shared__ __align__(16) float s_dx[SB][PB][QN];
     __shared__ uint32_t s_tmem;
     __shared__ int s_row[QN];  // gate/up: token of each slot column; down: slot
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -103,7 +106,10 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         for (int i = 0; i < DB; ++i) {
             mbar_init(&d_full[i], 1);
             mbar_init(&d_free[i], NEPI);
+        }
+        for (int i = 0; i < SB; ++i) {
             mbar_init(&scl_full[i], NCONV);
+            mbar_init(&scl_free[i], NEPI);
         }
         for (int i = 0; i < RG; ++i) {
             mbar_init(&raw_full[i], 1);
@@ -201,35 +207,61 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             if (MODE == 0) return rg + (row >> 6) * 2 * 64 * 64 + h * 64 * 64 + (row & 63) * 64 + 16 * i;
             return rg + (row >> 3) * 1024 + (2 * i + h) * 128 + (row & 7) * 16;  // [r/8][chunk][r%8][16 B]
         };
+        // Chunk j (0..7) of this row's group -> (block i, half h). The order is rotated per row
+        // so that the 32 lanes of a load touch distinct shared-memory banks: activation rows
+        // are 128 bytes apart (chunk 2i + h), gate/up weight rows 64 bytes apart (chunk i of
+        // half h), down weight rows already interleave 8 rows per 128 bytes.
+        auto chunk_of = [&](int j, int& i, int& h) {
+            if (isx) {
+                const int k = (j + row) & 7;
+                i = k >> 1;
+                h = k & 1;
+            } else if (MODE == 0) {
+                i = (j + (row >> 1)) & 3;
+                h = j >> 2;
+            } else {
+                i = j >> 1;
+                h = j & 1;
+            }
+        };
         float sc_cur[G4], sc_nxt[G4];
         load_sc(0, sc_cur);
         for (int q = 0; q < ng && ok; ++q) {
             const int slot = q % RG;
             if (q + 1 < ng) load_sc(q + 1, sc_nxt);
             if (!mbar_wait(&raw_full[slot], (q / RG) & 1)) { ok = false; break; }
+#pragma unroll
+            for (int pi = 0; pi < G4 / PB; ++pi) {  // the group's stages: tiles and scale buffers free
+                const int g = (G4 / PB) * q + pi;
+                if (g >= TS && !mbar_wait(&tile_free[g % TS], (g / TS - 1) & 1)) ok = false;
+                if (g >= SB && !mbar_wait(&scl_free[g % SB], (g / SB - 1) & 1)) ok = false;
+            }
+            if (!ok) break;
             const uint8_t* rg = raws + slot * RAWG;
 #pragma unroll
-            for (int pi = 0; pi < G4 / PB; ++pi) {
-                const int g = (G4 / PB) * q + pi, ts = g % TS, db = g % DB;  // g: stage (block pair) index
-                if (g >= TS && !mbar_wait(&tile_free[ts], (g / TS - 1) & 1)) { ok = false; break; }
-                if (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1)) { ok = false; break; }
-#pragma unroll
-                for (int b = 0; b < PB; ++b) {
-                    const int i = PB * pi + b;
-                    int8_row_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, 0)),
-                                    *reinterpret_cast<const uint4*>(raw_half(rg, i, 1)),
-                                    tiles + ts * STAGE + b * 2 * TILE + (isx ? TILE : 0), row);
-                    (isx ? s_dx[db][b] : s_dw[db][b])[row] = sc_cur[i];
-                }
-                fence_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    mbar_arrive(&tile_full[ts]);
-                    mbar_arrive(&scl_full[db]);
-                }
+            for (int j = 0; j < 2 * G4; ++j) {
+                int i, h;
+                chunk_of(j, i, h);
+                const int g = (G4 / PB) * q + i / PB;
+                int8x16_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, h)),
+                               tiles + (g % TS) * STAGE + (i % PB) * 2 * TILE + (isx ? TILE : 0), row, 2 * h);
             }
+#pragma unroll
+            for (int i = 0; i < G4; ++i) {
+                const int sb = ((G4 / PB) * q + i / PB) % SB;
+                (isx ? s_dx[sb][i % PB] : s_dw[sb][i % PB])[row] = sc_cur[i];
+            }
+            fence_async_smem();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&raw_free[slot]);
+            if (lane == 0) {
+#pragma unroll
+                for (int pi = 0; pi < G4 / PB; ++pi) {
+                    const int g = (G4 / PB) * q + pi;
+                    mbar_arrive(&tile_full[g % TS]);
+                    mbar_arrive(&scl_full[g % SB]);
+                }
+                mbar_arrive(&raw_free[slot]);
+            }
 #pragma unroll
             for (int i = 0; i < G4; ++i) sc_cur[i] = sc_nxt[i];
         }
@@ -265,8 +297,8 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
 #pragma unroll
         for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
         for (int g = 0; g < np; ++g) {
-            const int db = g % DB;
-            if (!mbar_wait(&d_full[db], (g / DB) & 1) || !mbar_wait(&scl_full[db], (g / DB) & 1)) {
+            const int db = g % DB, sb = g % SB;
+            if (!mbar_wait(&d_full[db], (g / DB) & 1) || !mbar_wait(&scl_full[sb], (g / SB) & 1)) {
                 ok = false;
                 break;
             }
@@ -274,14 +306,14 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             if (live) {
 #pragma unroll
                 for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
-                    const float dw = s_dw[db][b][rl];
+                    const float dw = s_dw[sb][b][rl];
 #pragma unroll
                     for (int hh = 0; hh < 2; ++hh) {
                         float v[16];
                         tmem_ld16(tmem + lane_base + (db * PB + b) * QN + 32 * cg + 16 * hh, v);
 #pragma unroll
                         for (int j4 = 0; j4 < 4; ++j4) {
-                            const float4 dx = *reinterpret_cast<const float4*>(&s_dx[db][b][32 * cg + 16 * hh + 4 * j4]);
+                            const float4 dx = *reinterpret_cast<const float4*>(&s_dx[sb][b][32 * cg + 16 * hh + 4 * j4]);
                             float* ac = &acc[16 * hh + 4 * j4];
                             ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw, dx.x)));
                             ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw, dx.y)));
@@ -293,7 +325,10 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&d_free[db]);
+            if (lane == 0) {
+                mbar_arrive(&d_free[db]);
+                mbar_arrive(&scl_free[sb]);
+            }
         }
         if (MODE == 0) {
             // up rows (quarters 2, 3) hand their sums to the gate rows through shared memory
