@@ -24,7 +24,8 @@
 // The expert kernels stream each weight row from HBM exactly once per work
 // item with 16-byte coalesced loads and keep it in registers while looping
 // over the item's tokens (decode-sized T: HBM-bound).
-#include "pi_common.cuh"
+#include "pi_tc.cuh"
+// pi_tc.cuh (pi_common.cuh) comes first: it names the quant types that pi_moe.h defines as macros
 #include "pi_internal.h"
 
 #include <algorithm>
@@ -350,6 +351,74 @@ __global__ void k_transpose_rows(const float* __restrict__ src, int rows, int co
 }
 
 // ---------------------------------------------------------------------------
+// k_router_dec: exact logits of every token for decode-sized batches. Each logit
+// is the reference's sequential f32 chain (quant/mod.rs:921-935): one rounded mul
+// then one rounded add per input, ascending, bit for bit. T x (E + 1) chains run
+// side by side, so the chain latency (d dependent adds) sets the time. CTA = R
+// router rows (row E = the shared-expert gate) x TK tokens; lane = (row, token),
+// a warp covering R rows x 32/R tokens. The CTA's whole slice (R rows and TK token
+// rows, row pitch d + 4 floats so a lane's 16-byte reads of its own row fall in
+// distinct banks) arrives by bulk copies issued by separate threads, in RD_NC
+// chunks of the inputs with one mbarrier each, so the chains start once the first
+// chunk has landed while the rest is in flight; a lane then gets
+// four steps' weights and inputs from two 16-byte shared loads. The wait is
+// bounded (PI_DEVERR_TIMEOUT).
+// ---------------------------------------------------------------------------
+constexpr int RD_NC = 4;  // chunks of the inputs, one mbarrier each
+template <int R, int TK>
+constexpr size_t rd_smem(int d) { return sizeof(float) * (size_t)(R + TK) * (d + 4); }
+template <int R, int TK>
+__global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__ xin, const float* __restrict__ W,
+                                                       const float* __restrict__ bias, int T, int d, int E,
+                                                       float* __restrict__ logits, uint32_t* err) {
+    extern __shared__ __align__(16) float rd_sm[];
+    __shared__ __align__(8) uint64_t full[RD_NC];
+    const int tid = threadIdx.x;
+    const int e0 = blockIdx.x * R, t0 = blockIdx.y * TK;
+    const int nt = min(TK, T - t0), nrow = min(R, E + 1 - e0);
+    const int pitch = d + 4, dc = d / RD_NC;
+    if (tid == 0) {
+        for (int c = 0; c < RD_NC; ++c) pitc::mbar_init(&full[c], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int c = 0; c < RD_NC; ++c) pitc::mbar_expect_tx(&full[c], (uint32_t)((nrow + nt) * dc * 4));
+    }
+    __syncthreads();
+    // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens
+    for (int q = tid; q < (R + TK) * RD_NC; q += TK * R) {
+        const int row = q % (R + TK), c = q / (R + TK);
+        const float* src = nullptr;
+        if (row < nrow) src = W + (int64_t)(e0 + row) * d;
+        else if (row >= R && row - R < nt) src = xin + (int64_t)(t0 + row - R) * d;
+        if (src) pitc::bulk_load(rd_sm + row * pitch + c * dc, src + c * dc, (uint32_t)dc * 4, &full[c]);
+    }
+    const int r = tid % R, tk = tid / R;
+    const bool live = r < nrow && tk < nt;
+    const float* wr = rd_sm + r * pitch;
+    const float* xv = rd_sm + (R + tk) * pitch;
+    float acc = 0.0f;
+    for (int c = 0; c < RD_NC; ++c) {
+        if (!pitc::mbar_wait(&full[c], 0)) {
+            if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
+            return;
+        }
+        if (!live) continue;
+#pragma unroll 8
+        for (int i = c * dc; i < (c + 1) * dc; i += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(wr + i);
+            const float4 x4 = *reinterpret_cast<const float4*>(xv + i);
+            acc = fadd(acc, fmul(w4.x, x4.x));
+            acc = fadd(acc, fmul(w4.y, x4.y));
+            acc = fadd(acc, fmul(w4.z, x4.z));
+            acc = fadd(acc, fmul(w4.w, x4.w));
+        }
+    }
+    if (!live) return;
+    const int e = e0 + r;
+    if (bias && e < E) acc = fadd(acc, bias[e]);
+    logits[(size_t)(t0 + tk) * (E + 1) + e] = acc;
+}
+
+// ---------------------------------------------------------------------------
 // k_router_exact_list: exact (reference-order) logits for the tokens listed
 // in list[0 .. *n_list). CTA = 32 router rows x one listed token at a time;
 // the 256 threads stage 32 x 256 tiles of the rows in shared memory (next
@@ -469,8 +538,10 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
     __syncwarp();
     // exp_sum: sequential sum in expert order (model/mod.rs:1282)
     float es = 0.0f;
-    if (lane == 0)
+    if (lane == 0) {
+#pragma unroll 16
         for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
+    }
     es = __shfl_sync(0xffffffffu, es, 0);
     float pr[TK_PER_LANE];
 #pragma unroll
@@ -1943,6 +2014,32 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             k_router_wide<8><<<rg, RW_THREADS, 0, st>>>(xin, L->router_t, L->ep, L->bias,
                                                         L->has_shared_gate ? L->router + (size_t)E * d : nullptr,
                                                         (int)T, d, E, B.logits);
+        }
+        PiProfScope ps(ctx, st, "k_topk");
+        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
+                 st>>>(B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts,
+                       nullptr, nullptr, nullptr, nullptr);
+    } else if (L->d % 128 == 0 && L->d <= 4096) {
+        // decode-sized batch: exact logits of every token, one chain per lane
+        {
+            PiProfScope ps(ctx, st, "k_router_dec");
+            static bool rd_attr = false;
+            if (!rd_attr) {
+                cudaFuncSetAttribute(k_router_dec<16, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)rd_smem<16, 8>(2048));
+                cudaFuncSetAttribute(k_router_dec<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)rd_smem<8, 4>(4096));
+                rd_attr = true;
+            }
+            if (d <= 2048) {
+                dim3 rg((unsigned)((E + 1 + 15) / 16), (unsigned)((T + 7) / 8));
+                k_router_dec<16, 8><<<rg, 128, rd_smem<16, 8>(d), st>>>(xin, L->router, L->bias, (int)T, d, E,
+                                                                        B.logits, ctx->dev_err);
+            } else {
+                dim3 rg((unsigned)((E + 1 + 7) / 8), (unsigned)((T + 3) / 4));
+                k_router_dec<8, 4><<<rg, 32, rd_smem<8, 4>(d), st>>>(xin, L->router, L->bias, (int)T, d, E,
+                                                                     B.logits, ctx->dev_err);
+            }
         }
         PiProfScope ps(ctx, st, "k_topk");
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,

@@ -40,6 +40,15 @@ PI_DEV bool mbar_wait(uint64_t* bar, uint32_t parity) {
     }
 }
 
+// Plain bulk copy global -> shared (no multicast) of `bytes` (a multiple of 16, both
+// addresses 16-byte aligned), completing on `bar` as transaction bytes.
+PI_DEV void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // UMMA shared-memory descriptor: K-major, 64-byte swizzle, 8-row atoms of 512
 // bytes (SBO = 512), version 1 (sm_100). A k16 step inside the 64-byte row
 // advances the start address by 32 bytes.
@@ -115,17 +124,6 @@ PI_DEV void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 // 16 consecutive f32 accumulator columns of this thread's TMEM lane
-// acc[0..1] += v[0..1] * (dw * dx[0..1]) with each product and sum rounded to nearest
-// f32 on its own (no FMA): the packed f32x2 ops of sm_100 round every lane like the
-// scalar mul.rn / add.rn they replace.
-PI_DEV void acc_scaled2(float& a0, float& a1, float v0, float v1, float dw, float dx0, float dx1) {
-    asm("{\n\t.reg .b64 A, V, W, X;\n\t"
-        "mov.b64 A, {%0, %1};\n\tmov.b64 V, {%2, %3};\n\tmov.b64 W, {%4, %4};\n\tmov.b64 X, {%5, %6};\n\t"
-        "mul.rn.f32x2 X, W, X;\n\tmul.rn.f32x2 X, V, X;\n\tadd.rn.f32x2 A, A, X;\n\t"
-        "mov.b64 {%0, %1}, A;\n\t}"
-        : "+f"(a0), "+f"(a1)
-        : "f"(v0), "f"(v1), "f"(dw), "f"(dx0), "f"(dx1));
-}
 PI_DEV void tmem_ld16(uint32_t taddr, float (&v)[16]) {
     uint32_t r[16];
     asm volatile(
