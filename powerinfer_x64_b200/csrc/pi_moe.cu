@@ -144,101 +144,6 @@ __global__ __launch_bounds__(128) void k_router(const float* __restrict__ xin, c
 }
 
 // ---------------------------------------------------------------------------
-// k_router_fast: certified logits. Warp = one router row (E expert rows +
-// row E, the shared-expert gate), lane l owns the contiguous slice
-// i in [CH*l, CH*l + CH) of the d inputs, CH = d/32. Per token the lane runs
-// the reference's own sequential f32 chain over its slice (c_l) and two
-// bound accumulators; a warp scan in f64 joins the slices. Besides the
-// logit L the kernel writes eps with
-//     |L - reference logit| <= eps,
-// where the reference logit is the sequential f32 sum of matvec_col_major_f32
-// (quant/mod.rs:921-935). Bound (u = 2^-24): the reference's error is at most
-// u * (sum_k |s_k| + sum_i |w_i x_i|) over its running sums s_k; here
-// |s_k| <= |S_start(l)| + |local running sum| + slack, S_start the exact
-// prefix at the slice start. Our own estimate has an error of the same form.
-// ---------------------------------------------------------------------------
-constexpr int RF_SMEM_FLOATS = 8704;  // staged tokens (32 slices of CH + 4 padding floats each)
-template <int CH>
-__global__ __launch_bounds__(256) void k_router_fast(const float* __restrict__ xin, const float* __restrict__ W,
-                                                     const float* __restrict__ bias, int T, int d, int E, int tpc,
-                                                     float* __restrict__ logits, float* __restrict__ eps) {
-    // tokens of this CTA are staged in shared memory, TS at a time; slice l of
-    // a token sits at l * (CH + 4) so the lanes' 16-byte reads hit distinct banks
-    constexpr int TSTRIDE = 32 * (CH + 4);
-    constexpr int TS = RF_SMEM_FLOATS / TSTRIDE;
-    static_assert(TS >= 1, "router slice too large");
-    __shared__ __align__(16) float xsm[RF_SMEM_FLOATS];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int e = blockIdx.x * 8 + warp;
-    const bool active = e <= E;
-    const float u = 5.9604644775390625e-08f;  // 2^-24
-    float w[CH];
-    const float* wr = W + (size_t)(active ? e : E) * d + lane * CH;
-#pragma unroll
-    for (int q = 0; q < CH / 4; ++q) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(wr) + q);
-        w[4 * q] = v.x;
-        w[4 * q + 1] = v.y;
-        w[4 * q + 2] = v.z;
-        w[4 * q + 3] = v.w;
-    }
-    const float be = (bias && e < E) ? bias[e] : 0.0f;
-    const int t_beg = blockIdx.y * tpc, t_end = min(T, t_beg + tpc);
-    for (int c0 = t_beg; c0 < t_end; c0 += TS) {
-        const int nt = min(TS, t_end - c0);
-        __syncthreads();
-        for (int q = threadIdx.x; q < nt * (d / 4); q += blockDim.x) {
-            const int tt = q / (d / 4), i4 = q % (d / 4);
-            const float4 v = *reinterpret_cast<const float4*>(xin + (size_t)(c0 + tt) * d + 4 * i4);
-            const int i = 4 * i4;
-            *reinterpret_cast<float4*>(&xsm[tt * TSTRIDE + (i / CH) * (CH + 4) + i % CH]) = v;
-        }
-        __syncthreads();
-        if (!active) continue;
-        for (int tt = 0; tt < nt; ++tt) {
-            const int t = c0 + tt;
-            const float* xr = xsm + tt * TSTRIDE + lane * (CH + 4);
-            float s = 0.0f, absacc = 0.0f, A = 0.0f;
-#pragma unroll
-            for (int q = 0; q < CH / 4; ++q) {
-                const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * q);
-                const float xs4[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    const float p = fmul(w[4 * q + j], xs4[j]);
-                    s = fadd(s, p);
-                    absacc += fabsf(s);
-                    A += fabsf(p);
-                }
-            }
-            // exclusive prefix of the slice sums, in f64
-            double incl = (double)s;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const double v = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += v;
-            }
-            const double start = incl - (double)s;
-            const double total = __shfl_sync(0xffffffffu, incl, 31);
-            double bnd = (double)CH * fabs(start) + (double)absacc + 2.0 * (double)A + 5.0 * fabs((double)s) +
-                         (double)CH * (double)u * ((double)absacc + (double)A) * 32.0;
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) bnd += __shfl_xor_sync(0xffffffffu, bnd, o);
-            if (lane == 0) {
-                float L = (float)total;
-                double ep = 2.02 * (double)u * bnd + (double)u * fabs((double)L) + 1e-30;
-                if (bias && e < E) {
-                    L = fadd(L, be);
-                    ep += 2.0 * (double)u * (fabs((double)L) + ep);
-                }
-                logits[(size_t)t * (E + 1) + e] = L;
-                eps[(size_t)t * (E + 1) + e] = (float)(ep * (1.0 + 1e-6));
-            }
-        }
-    }
-}
-
-// ---------------------------------------------------------------------------
 // k_router_wide: exact logits of the E expert rows for prefill-sized batches.
 // Each logit is the reference's sequential f32 sum (quant/mod.rs:921-935): the
 // accumulator walks i in ascending order, one rounded mul then one rounded add
@@ -497,19 +402,11 @@ __global__ __launch_bounds__(EX_THREADS) void k_router_exact_list(const float* _
 // k_topk: one warp per token. E <= 32 * TK_PER_LANE.
 // ---------------------------------------------------------------------------
 constexpr int TK_PER_LANE = 16, TK_WARPS = 4;
-// Two modes:
-//  * eps != null (certify): select on the fast logits; if the selection is
-//    provably the reference's (every selected logit's interval lies above
-//    every other's by a margin that also rules out equal probabilities after
-//    rounding), write the routing; otherwise append the token to flag_list.
-//  * list != null (exact): route the listed tokens from their exact logits.
-__global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits,
-                                                        const float* __restrict__ eps, int T, int E, int k,
+// Routes every token from its exact logits, or (list != null) the listed tokens.
+__global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits, int T, int E, int k,
                                                         int has_shgate, int32_t* __restrict__ idx,
                                                         float* __restrict__ gates, float* __restrict__ shscale,
                                                         int32_t* __restrict__ counts,
-                                                        int32_t* __restrict__ flag_list,
-                                                        int32_t* __restrict__ n_flag,
                                                         const int32_t* __restrict__ list,
                                                         const int32_t* __restrict__ n_list) {
     __shared__ float s_p[TK_WARPS][32 * TK_PER_LANE];
@@ -575,29 +472,6 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
         if (lane == 0) s_sel[warp][r] = bi;
     }
     __syncwarp();
-    if (eps) {
-        const float* er = eps + (size_t)t * (E + 1);
-        float lo = INFINITY, hi = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < TK_PER_LANE; ++j) {
-            const int e = lane + 32 * j;
-            if (e >= E) continue;
-            const float ev = er[e];
-            if ((taken >> j) & 1u) lo = fminf(lo, l[j] - ev);
-            else hi = fmaxf(hi, l[j] + ev + 4e-6f * (1.0f + fabsf(l[j] - m)));
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-            hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-        }
-        // lo - hi > 0 with a relative guard; the boundary must sit well inside exp's range
-        const bool cert = (lo > hi + 1e-6f * fabsf(hi)) && (lo - m > -80.0f);
-        if (!cert) {
-            if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
-            continue;
-        }
-    }
     // ascending sort of the k selected indices (model/mod.rs:1303)
     int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
     int rank = 0;
@@ -620,95 +494,6 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
     }
 }
 
-// ---------------------------------------------------------------------------
-// k_topk_cert: certify-or-flag routing on the fast logits, one warp per token.
-// The selection is the k largest logits (ties to the lowest index); it is
-// certified when every selected logit's interval [L - eps, L + eps] lies above
-// every other's with a margin that also excludes equal probabilities after
-// rounding -- then the reference's selection (by probability, ties to the
-// lowest index) is the same set. Certified tokens get gates from the fast
-// logits (softmax sum as a tree: the gates carry a tolerance, not bit-exact);
-// the others are appended to flag_list for the exact path.
-// ---------------------------------------------------------------------------
-__global__ __launch_bounds__(TK_WARPS * 32) void k_topk_cert(const float* __restrict__ logits,
-                                                             const float* __restrict__ eps, int T, int E, int k,
-                                                             int has_shgate, int32_t* __restrict__ idx,
-                                                             float* __restrict__ gates, float* __restrict__ shscale,
-                                                             int32_t* __restrict__ counts,
-                                                             int32_t* __restrict__ flag_list,
-                                                             int32_t* __restrict__ n_flag) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * TK_WARPS + warp;
-    if (t >= T) return;
-    const float* lr = logits + (size_t)t * (E + 1);
-    const float* er = eps + (size_t)t * (E + 1);
-    float l[TK_PER_LANE], ev[TK_PER_LANE];
-    float m = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        const int e = lane + 32 * j;
-        l[j] = (e < E) ? lr[e] : -INFINITY;
-        ev[j] = (e < E) ? er[e] : 0.0f;
-        m = fmaxf(m, l[j]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float es = 0.0f;
-#pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j)
-        if (lane + 32 * j < E) es += __expf(l[j] - m);
-    es = warp_sum(es);
-    uint32_t taken = 0;
-    int my_sel = -1;
-    float my_l = 0.0f;
-    for (int r = 0; r < k; ++r) {
-        float bl = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < TK_PER_LANE; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u) && (l[j] > bl || (l[j] == bl && e < bi))) { bl = l[j]; bi = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ol > bl || (ol == bl && oi < bi)) { bl = ol; bi = oi; }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        if (lane == r) { my_sel = bi; my_l = bl; }
-    }
-    float lo = INFINITY, hi = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        if (lane + 32 * j >= E) continue;
-        if ((taken >> j) & 1u) lo = fminf(lo, l[j] - ev[j]);
-        else hi = fmaxf(hi, l[j] + ev[j] + 4e-6f * (1.0f + fabsf(l[j] - m)));
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        lo = fminf(lo, __shfl_xor_sync(0xffffffffu, lo, o));
-        hi = fmaxf(hi, __shfl_xor_sync(0xffffffffu, hi, o));
-    }
-    if (!((lo > hi + 1e-6f * fabsf(hi)) && (lo - m > -80.0f))) {
-        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
-        return;
-    }
-    // ascending order of the selected experts (model/mod.rs:1303)
-    int rank = 0;
-    for (int r = 0; r < k; ++r) {
-        const int o = __shfl_sync(0xffffffffu, my_sel, r);
-        rank += (lane < k) && (o < my_sel);
-    }
-    const float p = (lane < k) ? __expf(my_l - m) / es : 0.0f;
-    const float ssum = warp_sum(p);
-    if (lane < k) {
-        idx[(size_t)t * k + rank] = my_sel;
-        gates[(size_t)t * k + rank] = ssum > 0.0f ? p / ssum : p;
-        atomicAdd(&counts[my_sel], 1);
-    }
-    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
-}
 
 // ---------------------------------------------------------------------------
 // Certified tensor-core routing for prefill batches.
@@ -1224,6 +1009,124 @@ __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __
     if (lane == 0) hs[b] = sc;
 }
 
+// Q8_0 down, streamed: a persistent CTA per SM walks work units u = (item, block of
+// DS_ROWS output rows), u = blockIdx.x, blockIdx.x + gridDim.x, ... A producer
+// thread bulk-copies each unit's inputs into a ring of DS_NS shared-memory stages
+// (the 64 rows are one contiguous 8-row-group run of the lane-tiled layout, their
+// f16 block scales, and the item's quantised h rows and scales) onto the stage's
+// mbarrier, so HBM streams continuously while 8 consumer warps compute; a warp
+// releases the stage on a second mbarrier. Warp w owns rows 8w .. 8w+7 of the unit,
+// 4 lanes per row as in k_down_q8; block terms go to shared memory and lane c sums
+// chain c = (row, token) over the row's blocks in ascending order (quant/mod.rs:
+// 877-899), bit for bit. Every wait is bounded (PI_DEVERR_TIMEOUT).
+constexpr int DS_ROWS = 64, DS_NS = 4, DS_THREADS = 9 * 32;
+template <int CPQ>
+struct DSL {
+    static constexpr int F = CPQ * 64, FB = F / 32, BPQ = CPQ / 2, TS = FB + 1;
+    static constexpr int W = DS_ROWS * F, S = DS_ROWS * FB * 2, H = TG * F, HS = TG * FB * 4;
+    static constexpr int STAGE = W + S + H + HS;
+    static constexpr size_t SMEM = (size_t)DS_NS * STAGE + sizeof(float) * 8 * 32 * TS;
+};
+template <int CPQ>
+__global__ __launch_bounds__(DS_THREADS, 1) void k_down_q8s(ExpertArgs a, uint32_t* err) {
+    using L = DSL<CPQ>;
+    constexpr int F = L::F, FB = L::FB, BPQ = L::BPQ, TS = L::TS;
+    extern __shared__ __align__(128) uint8_t ds_sm[];
+    __shared__ __align__(8) uint64_t full[DS_NS], empty[DS_NS];
+    __shared__ int4 meta[DS_NS];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int d = a.d, nrb = d / DS_ROWS;
+    const int n_units = *a.n_items * nrb;
+    if (tid == 0) {
+        for (int s = 0; s < DS_NS; ++s) {
+            pitc::mbar_init(&full[s], 1);
+            pitc::mbar_init(&empty[s], 8);
+        }
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncthreads();
+    bool ok = true;
+    if (warp == 8) {
+        if (lane == 0) {
+            int k = 0;
+            for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++k) {
+                const int s = k % DS_NS;
+                if (k >= DS_NS && !pitc::mbar_wait(&empty[s], ((k / DS_NS) - 1) & 1)) { ok = false; break; }
+                const int4 item = a.items[u / nrb];
+                const int rb = u % nrb;
+                meta[s] = make_int4(item.x, item.y, item.z, rb);
+                const bool sh = item.x == a.E;
+                const size_t row0 = (sh ? 0 : (size_t)item.x * d) + (size_t)rb * DS_ROWS;
+                uint8_t* st = ds_sm + (size_t)s * L::STAGE;
+                pitc::mbar_expect_tx(&full[s], (uint32_t)(L::W + L::S + item.z * (F + FB * 4)));
+                pitc::bulk_load(st, (const int8_t*)(sh ? a.dns : a.dn) + row0 * F, L::W, &full[s]);
+                pitc::bulk_load(st + L::W, (sh ? a.dsd : a.dd) + row0 * FB, L::S, &full[s]);
+                pitc::bulk_load(st + L::W + L::S, a.hq + (size_t)item.y * F, (uint32_t)(item.z * F), &full[s]);
+                pitc::bulk_load(st + L::W + L::S + L::H, a.hs + (size_t)item.y * FB, (uint32_t)(item.z * FB * 4),
+                                &full[s]);
+            }
+        }
+    } else {
+        float* terms = reinterpret_cast<float*>(ds_sm + (size_t)DS_NS * L::STAGE) + warp * 32 * TS;
+        const int q = lane & 3, r8 = lane >> 2;
+        int k = 0;
+        for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++k) {
+            const int s = k % DS_NS;
+            if (!pitc::mbar_wait(&full[s], (k / DS_NS) & 1)) { ok = false; break; }
+            const int4 m = meta[s];
+            const uint8_t* st = ds_sm + (size_t)s * L::STAGE;
+            // quarter q walks its blocks rotated by q (block (b + q) % BPQ at step b): the four
+            // quarters of a row then read h chunks in distinct banks; only shared-memory
+            // addresses rotate, registers stay statically indexed
+            int4 w[CPQ];
+            float sw[BPQ];
+#pragma unroll
+            for (int c = 0; c < CPQ; ++c)
+                w[c] = *reinterpret_cast<const int4*>(st + warp * 8 * F + (((c + 2 * q) % CPQ) * 32 + lane) * 16);
+            const __half* sc = reinterpret_cast<const __half*>(st + L::W) + (warp * 8 + r8) * FB + q * BPQ;
+#pragma unroll
+            for (int b = 0; b < BPQ; ++b) sw[b] = __half2float(sc[(b + q) % BPQ]);
+            const int8_t* hq = reinterpret_cast<const int8_t*>(st + L::W + L::S);
+            const float* hs = reinterpret_cast<const float*>(st + L::W + L::S + L::H);
+            constexpr int DTB = 4;  // tokens per batch: 8 rows x 4 tokens = 32 chains
+            for (int t0 = 0; t0 < m.z; t0 += DTB) {
+                const int nt = min(DTB, m.z - t0);
+                for (int j = 0; j < nt; ++j) {
+                    const int8_t* hr = hq + (t0 + j) * F + q * CPQ * 16;
+                    const float* hsr = hs + (t0 + j) * FB + q * BPQ;
+                    float* tr = terms + (r8 * DTB + j) * TS + q * BPQ;
+#pragma unroll
+                    for (int b = 0; b < BPQ; ++b) {
+                        const int br = (b + q) % BPQ;
+                        int sum = 0;
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int4 wv = w[2 * b + h], xv = *reinterpret_cast<const int4*>(hr + (2 * br + h) * 16);
+                            sum = dp4a(wv.x, xv.x, sum);
+                            sum = dp4a(wv.y, xv.y, sum);
+                            sum = dp4a(wv.z, xv.z, sum);
+                            sum = dp4a(wv.w, xv.w, sum);
+                        }
+                        tr[br] = fmul((float)sum, fmul(sw[b], hsr[br]));
+                    }
+                }
+                __syncwarp();
+                const int j = lane % DTB, rr = lane / DTB;
+                if (j < nt) {
+                    const float* tp = terms + lane * TS;
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int b = 0; b < FB; ++b) acc = fadd(acc, tp[b]);
+                    a.y[(size_t)(m.y + t0 + j) * d + m.w * DS_ROWS + warp * 8 + rr] = acc;
+                }
+                __syncwarp();
+            }
+            if (lane == 0) pitc::mbar_arrive(&empty[s]);
+        }
+    }
+    if (!ok) atomicOr(err, PI_DEVERR_TIMEOUT);
+}
+
 // Q8_0 down: CTA = DN_ROWS output rows (8 warps x 8*DN_NP rows), 4 lanes per
 // row, CPQ = f/64 chunks per lane, 8 rows per warp pass; the quantised h
 // of each slot comes from k_quant_h. Each output is the reference's sequential
@@ -1231,6 +1134,8 @@ __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __
 // (quant/mod.rs:877-899), bit for bit.
 constexpr int DN_NP = 2;             // passes of 8 rows per warp
 constexpr int DN_ROWS = 64 * DN_NP;   // rows per CTA
+// term buffer of k_down_q8<CPQ>: 8 warps x 32 chains x (2 CPQ + 4) floats
+constexpr size_t dn_smem(int cpq) { return sizeof(float) * 8 * 32 * (2 * cpq + 4); }
 template <int CPQ>
 __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
     constexpr int F = CPQ * 64;  // expert width
@@ -1242,6 +1147,7 @@ __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int q = lane & 3;
     const int rbase = blockIdx.x * DN_ROWS + warp * 8 * DN_NP + (lane >> 2);
+    static_assert(DN_NP * 8 <= 32, "a warp's rows x one token fit its 32 chains");
     const size_t mat = sh ? 0 : (size_t)item.x * d;
     const int8_t* D = (const int8_t*)(sh ? a.dns : a.dn) + mat * F;
     const __half* DD = (sh ? a.dsd : a.dd) + mat * fb;
@@ -1267,46 +1173,53 @@ __global__ __launch_bounds__(256, 2) void k_down_q8(ExpertArgs a) {
     for (int m = threadIdx.x; m < item.z * fb; m += blockDim.x)
         s_hs[m / fb][m % fb] = a.hs[(size_t)(item.y + m / fb) * fb + m % fb];
     __syncthreads();
-    for (int tk = 0; tk < item.z; ++tk) {
-        const int slot = item.y + tk;
-        const int8_t* hr = &s_hq[tk][q * CPQ * 16];
-        const float* hsr = &s_hs[tk][q * BPQ];
-        int4 hv[CPQ];
-        float hsv[BPQ];
+    // block terms go to shared memory; lane c then sums chain c = (row, token) over the
+    // row's FB terms in ascending block order (quant/mod.rs:877-899)
+    constexpr int FB = 4 * BPQ, TS = FB + 4;  // blocks per row, padded term stride
+    constexpr int DTB = 32 / (8 * DN_NP);      // tokens per batch: 32 chains per warp
+    extern __shared__ __align__(16) float dn_terms[];
+    float* terms = dn_terms + warp * 32 * TS;
+    const int r8 = lane >> 2;
+    for (int t0 = 0; t0 < item.z; t0 += DTB) {
+        const int nt = min(DTB, item.z - t0);
+        for (int j = 0; j < nt; ++j) {
+            const int8_t* hr = &s_hq[t0 + j][q * CPQ * 16];
+            const float* hsr = &s_hs[t0 + j][q * BPQ];
+            int4 hv[CPQ];
+            float hsv[BPQ];
 #pragma unroll
-        for (int c = 0; c < CPQ; ++c) hv[c] = *reinterpret_cast<const int4*>(hr + c * 16);
+            for (int c = 0; c < CPQ; ++c) hv[c] = *reinterpret_cast<const int4*>(hr + c * 16);
 #pragma unroll
-        for (int b = 0; b < BPQ; ++b) hsv[b] = hsr[b];
+            for (int b = 0; b < BPQ; ++b) hsv[b] = hsr[b];
 #pragma unroll
-        for (int p = 0; p < DN_NP; ++p) {
-            // block terms of this lane's quarter (blocks q*BPQ .. q*BPQ + BPQ - 1), then the
-            // reference's sequential sum over all blocks in ascending order, gathered by shuffles
-            float term[BPQ];
+            for (int p = 0; p < DN_NP; ++p) {
+                float* tr = terms + ((p * 8 + r8) * DTB + j) * TS + q * BPQ;
 #pragma unroll
-            for (int b = 0; b < BPQ; ++b) {
-                int s = 0;
+                for (int b = 0; b < BPQ; ++b) {
+                    int sum = 0;
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                    const int4 wv = w[p][2 * b + h], xv = hv[2 * b + h];
-                    s = dp4a(wv.x, xv.x, s);
-                    s = dp4a(wv.y, xv.y, s);
-                    s = dp4a(wv.z, xv.z, s);
-                    s = dp4a(wv.w, xv.w, s);
+                    for (int h = 0; h < 2; ++h) {
+                        const int4 wv = w[p][2 * b + h], xv = hv[2 * b + h];
+                        sum = dp4a(wv.x, xv.x, sum);
+                        sum = dp4a(wv.y, xv.y, sum);
+                        sum = dp4a(wv.z, xv.z, sum);
+                        sum = dp4a(wv.w, xv.w, sum);
+                    }
+                    tr[b] = fmul((float)sum, fmul(sw[p][b], hsv[b]));
                 }
-                term[b] = fmul((float)s, fmul(sw[p][b], hsv[b]));
             }
-            // the running sum passes lane to lane: quarter src adds its terms, then hands on
-            float acc = 0.f;
-#pragma unroll
-            for (int src = 0; src < 4; ++src) {
-                if (q == src) {
-#pragma unroll
-                    for (int b = 0; b < BPQ; ++b) acc = fadd(acc, term[b]);
-                }
-                acc = __shfl_sync(0xffffffffu, acc, (lane & ~3) | src);
-            }
-            if (q == 0) a.y[(size_t)slot * d + rbase + 8 * p] = acc;
         }
+        __syncwarp();
+        const int j = lane % DTB, pr = lane / DTB;  // chain: token t0 + j, row pass pr / 8, row pr % 8
+        if (j < nt) {
+            const float* tp = terms + lane * TS;
+            float acc = 0.0f;
+#pragma unroll
+            for (int b = 0; b < FB; ++b) acc = fadd(acc, tp[b]);
+            const int row = blockIdx.x * DN_ROWS + warp * 8 * DN_NP + (pr % 8) + 8 * (pr / 8);
+            a.y[(size_t)(item.y + t0 + j) * d + row] = acc;
+        }
+        __syncwarp();
     }
 }
 
@@ -1702,7 +1615,6 @@ struct FwdBufs {
     int8_t* xq;
     float* xs;
     float* logits;
-    float* eps;
     int32_t* flag_list;
     int32_t* n_flag;
     int32_t* idx;
@@ -1767,7 +1679,6 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.xq = b.take<int8_t>(T * d);
     f.xs = b.take<float>(T * (d / 32));
     f.logits = b.take<float>(T * (E + 1));
-    f.eps = b.take<float>(T * (E + 1));
     f.flag_list = b.take<int32_t>(T);
     f.n_flag = b.take<int32_t>(1);
     f.idx = b.take<int32_t>(T * k);
@@ -1874,11 +1785,32 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
             k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
         }
         PiProfScope ps(ctx, st, "k_down");
+        if (L->f / 64 <= 8) {  // streamed down: persistent CTAs fed by bulk copies
+            static bool ds_attr = false;
+            if (!ds_attr) {
+                cudaFuncSetAttribute(k_down_q8s<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<2>::SMEM);
+                cudaFuncSetAttribute(k_down_q8s<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<4>::SMEM);
+                cudaFuncSetAttribute(k_down_q8s<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<8>::SMEM);
+                ds_attr = true;
+            }
+            const unsigned g = (unsigned)std::min<int64_t>((int64_t)ni * (L->d / DS_ROWS), ctx->sm_count);
+            switch (L->f / 64) {
+                case 2: k_down_q8s<2><<<g, DS_THREADS, DSL<2>::SMEM, st>>>(a, ctx->dev_err); break;
+                case 4: k_down_q8s<4><<<g, DS_THREADS, DSL<4>::SMEM, st>>>(a, ctx->dev_err); break;
+                case 8: k_down_q8s<8><<<g, DS_THREADS, DSL<8>::SMEM, st>>>(a, ctx->dev_err); break;
+            }
+            return pi_cuda_check(ctx, cudaGetLastError(), "experts") ? PI_ERR_CUDA : PI_OK;
+        }
+        static bool dn_attr = false;
+        if (!dn_attr) {  // CPQ = 16: term buffer + staged h above the default 48 KB
+            cudaFuncSetAttribute(k_down_q8<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem(16));
+            dn_attr = true;
+        }
         switch (L->f / 64) {
-            case 2: k_down_q8<2><<<dn, 256, 0, st>>>(a); break;
-            case 4: k_down_q8<4><<<dn, 256, 0, st>>>(a); break;
-            case 8: k_down_q8<8><<<dn, 256, 0, st>>>(a); break;
-            case 16: k_down_q8<16><<<dn, 256, 0, st>>>(a); break;
+            case 2: k_down_q8<2><<<dn, 256, dn_smem(2), st>>>(a); break;
+            case 4: k_down_q8<4><<<dn, 256, dn_smem(4), st>>>(a); break;
+            case 8: k_down_q8<8><<<dn, 256, dn_smem(8), st>>>(a); break;
+            case 16: k_down_q8<16><<<dn, 256, dn_smem(16), st>>>(a); break;
             default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128..1024 (x2)");
         }
     } else {
@@ -2003,8 +1935,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
                                                                  B.logits);
             k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
-                B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
-                nullptr, B.flag_list, B.n_flag);
+                B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
         }
     } else if (T >= 256) {
         // prefill-sized batch: exact logits for every token, exact selection
@@ -2017,8 +1948,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         }
         PiProfScope ps(ctx, st, "k_topk");
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
-                 st>>>(B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts,
-                       nullptr, nullptr, nullptr, nullptr);
+                 st>>>(B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
     } else if (L->d % 128 == 0 && L->d <= 4096) {
         // decode-sized batch: exact logits of every token, one chain per lane
         {
@@ -2043,42 +1973,9 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         }
         PiProfScope ps(ctx, st, "k_topk");
         k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
-                 st>>>(B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts,
-                       nullptr, nullptr, nullptr, nullptr);
+                 st>>>(B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
     } else {
-    {
-        PiProfScope ps(ctx, st, "k_router_fast");
-        const int64_t ctas_x = (E + 1 + 7) / 8;
-        const int tpc = (int)std::max<int64_t>(1, (T * ctas_x + 2 * ctx->sm_count - 1) / (2 * ctx->sm_count));
-        dim3 rg((unsigned)ctas_x, (unsigned)((T + tpc - 1) / tpc));
-        switch (d / 32) {
-            case 16: k_router_fast<16><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
-            case 32: k_router_fast<32><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
-            case 64: k_router_fast<64><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
-            case 128: k_router_fast<128><<<rg, 256, 0, st>>>(xin, L->router, L->bias, (int)T, d, E, tpc, B.logits, B.eps); break;
-            default: return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be 512, 1024, 2048 or 4096");
-        }
-    }
-    {
-        PiProfScope ps(ctx, st, "k_topk");
-        k_topk_cert<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(
-            B.logits, B.eps, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list,
-            B.n_flag);
-    }
-    {
-        PiProfScope ps(ctx, st, "k_router_exact");
-        dim3 eg((unsigned)((E + 1 + 31) / 32), (unsigned)std::min<int64_t>(T, 64));
-        static bool ex_attr = false;
-        if (!ex_attr) {
-            cudaFuncSetAttribute(k_router_exact_list, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)EX_SMEM);
-            ex_attr = true;
-        }
-        k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
-                                                             B.logits);
-        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
-            B.logits, nullptr, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr,
-            nullptr, B.flag_list, B.n_flag);
-    }
+        return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be a multiple of 128, at most 4096");
     }
     const bool gemm = !route_only && use_gemm(L, T, flags);
     const int tg = gemm ? (q8 ? PI_GEMM_NT_Q8 : PI_GEMM_NT) : TG;
