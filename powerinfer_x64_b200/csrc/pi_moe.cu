@@ -399,99 +399,116 @@ __global__ __launch_bounds__(EX_THREADS) void k_router_exact_list(const float* _
 }
 
 // ---------------------------------------------------------------------------
-// k_topk: one warp per token. E <= 32 * TK_PER_LANE.
+// k_topk: one warp per token, NPL = ceil(E / 32) experts per lane.
 // ---------------------------------------------------------------------------
-constexpr int TK_PER_LANE = 16, TK_WARPS = 4;
+constexpr int TK_WARPS = 4, TK_PER_LANE = 16;  // E <= 32 * TK_PER_LANE
 // Routes every token from its exact logits, or (list != null) the listed tokens.
+// Top-k by probability with ties to the lowest expert index: a round takes the
+// largest key with redux.sync max (keys: probability bits + 2, order-preserving
+// for non-negative floats; 1 for NaN, 0 for taken) and then the lowest index
+// holding it with redux.sync min.
+template <int NPL>
 __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits, int T, int E, int k,
                                                         int has_shgate, int32_t* __restrict__ idx,
                                                         float* __restrict__ gates, float* __restrict__ shscale,
                                                         int32_t* __restrict__ counts,
                                                         const int32_t* __restrict__ list,
                                                         const int32_t* __restrict__ n_list) {
-    __shared__ float s_p[TK_WARPS][32 * TK_PER_LANE];
+    __shared__ float s_p[TK_WARPS][32 * NPL];
     __shared__ int s_sel[TK_WARPS][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tok = list ? *n_list : T;
     for (int g = blockIdx.x * TK_WARPS + warp; g < n_tok; g += gridDim.x * TK_WARPS) {
-    const int t = list ? list[g] : g;
-    const float* lr = logits + (size_t)t * (E + 1);
-    float l[TK_PER_LANE];
-    float m = -INFINITY;
+        const int t = list ? list[g] : g;
+        const float* lr = logits + (size_t)t * (E + 1);
+        float l[NPL];
+        float m = -INFINITY;
 #pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        l[j] = (e < E) ? lr[e] : -INFINITY;
-        if (e < E) m = fmaxf(m, l[j]);
-    }
+        for (int j = 0; j < NPL; ++j) {
+            const int e = lane + 32 * j;
+            l[j] = (e < E) ? lr[e] : -INFINITY;
+            if (e < E) m = fmaxf(m, l[j]);
+        }
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    float* p = s_p[warp];
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        float* p = s_p[warp];
 #pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        if (e < E) p[e] = exp_cr(fsub(l[j], m));
-    }
-    __syncwarp();
-    // exp_sum: sequential sum in expert order (model/mod.rs:1282)
-    float es = 0.0f;
-    if (lane == 0) {
+        for (int j = 0; j < NPL; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E) p[e] = exp_cr(fsub(l[j], m));
+        }
+        __syncwarp();
+        // exp_sum: sequential sum in expert order (model/mod.rs:1282)
+        float es = 0.0f;
+        if (lane == 0) {
 #pragma unroll 16
-        for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
-    }
-    es = __shfl_sync(0xffffffffu, es, 0);
-    float pr[TK_PER_LANE];
-#pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        pr[j] = (e < E) ? fdiv(p[e], es) : -INFINITY;
-    }
-    __syncwarp();
-#pragma unroll
-    for (int j = 0; j < TK_PER_LANE; ++j) {
-        int e = lane + 32 * j;
-        if (e < E) p[e] = pr[j];
-    }
-    // top-k by probability, ties broken to the lowest expert index
-    uint32_t taken = 0;
-    for (int r = 0; r < k; ++r) {
-        float bp = -INFINITY;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int j = 0; j < TK_PER_LANE; ++j) {
-            int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u) && (pr[j] > bp || (pr[j] == bp && e < bi))) { bp = pr[j]; bi = e; }
+            for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
         }
+        es = __shfl_sync(0xffffffffu, es, 0);
+        float pr[NPL];
+        uint32_t key[NPL];
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            float op = __shfl_xor_sync(0xffffffffu, bp, o);
-            int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+        for (int j = 0; j < NPL; ++j) {
+            const int e = lane + 32 * j;
+            pr[j] = (e < E) ? fdiv(p[e], es) : 0.0f;
+            key[j] = (e < E) ? (pr[j] == pr[j] ? __float_as_uint(pr[j]) + 2u : 1u) : 0u;
         }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        if (lane == 0) s_sel[warp][r] = bi;
+        __syncwarp();
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) {
+            const int e = lane + 32 * j;
+            if (e < E) p[e] = pr[j];
+        }
+        for (int r = 0; r < k; ++r) {
+            uint32_t mk = 0;
+#pragma unroll
+            for (int j = 0; j < NPL; ++j) mk = max(mk, key[j]);
+            mk = __reduce_max_sync(0xffffffffu, mk);
+            uint32_t me = 0xffffffffu;
+#pragma unroll
+            for (int j = NPL - 1; j >= 0; --j)
+                if (key[j] == mk) me = lane + 32 * j;
+            const int bi = (int)__reduce_min_sync(0xffffffffu, me);
+            if ((bi & 31) == lane) {
+#pragma unroll
+                for (int j = 0; j < NPL; ++j)
+                    if (j == (bi >> 5)) key[j] = 0;
+            }
+            if (lane == 0) s_sel[warp][r] = bi;
+        }
+        __syncwarp();
+        // ascending sort of the k selected indices (model/mod.rs:1303)
+        const int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
+        int rank = 0;
+        for (int r = 0; r < k; ++r) rank += (s_sel[warp][r] < mine);
+        __syncwarp();
+        if (lane < k) s_sel[warp][rank] = mine;
+        __syncwarp();
+        float ssum = 0.0f;
+        if (lane == 0)
+            for (int r = 0; r < k; ++r) ssum = fadd(ssum, p[s_sel[warp][r]]);
+        ssum = __shfl_sync(0xffffffffu, ssum, 0);
+        if (lane < k) {
+            const int e = s_sel[warp][lane];
+            const float pe = p[e];
+            idx[(size_t)t * k + lane] = e;
+            gates[(size_t)t * k + lane] = (ssum > 0.0f) ? fdiv(pe, ssum) : pe;
+            atomicAdd(&counts[e], 1);
+        }
+        if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
     }
-    __syncwarp();
-    // ascending sort of the k selected indices (model/mod.rs:1303)
-    int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
-    int rank = 0;
-    for (int r = 0; r < k; ++r) rank += (s_sel[warp][r] < mine);
-    __syncwarp();
-    if (lane < k) s_sel[warp][rank] = mine;
-    __syncwarp();
-    float ssum = 0.0f;
-    if (lane == 0)
-        for (int r = 0; r < k; ++r) ssum = fadd(ssum, p[s_sel[warp][r]]);
-    ssum = __shfl_sync(0xffffffffu, ssum, 0);
-    if (lane < k) {
-        int e = s_sel[warp][lane];
-        float pe = p[e];
-        idx[(size_t)t * k + lane] = e;
-        gates[(size_t)t * k + lane] = (ssum > 0.0f) ? fdiv(pe, ssum) : pe;
-        atomicAdd(&counts[e], 1);
-    }
-    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
-    }
+}
+
+// k_topk for E experts (E <= 512).
+void launch_topk(unsigned grid, cudaStream_t st, const float* logits, int T, int E, int k, int has_shgate,
+                 int32_t* idx, float* gates, float* shscale, int32_t* counts, const int32_t* list,
+                 const int32_t* n_list) {
+#define TOPK(N) k_topk<N><<<grid, TK_WARPS * 32, 0, st>>>(logits, T, E, k, has_shgate, idx, gates, shscale, counts, list, n_list)
+    if (E <= 64) TOPK(2);
+    else if (E <= 128) TOPK(4);
+    else if (E <= 256) TOPK(8);
+    else TOPK(16);
+#undef TOPK
 }
 
 
@@ -1934,8 +1951,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             }
             k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
                                                                  B.logits);
-            k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), TK_WARPS * 32, 0, st>>>(
-                B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
+            launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), st, B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
         }
     } else if (T >= 256) {
         // prefill-sized batch: exact logits for every token, exact selection
@@ -1947,8 +1963,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
                                                         (int)T, d, E, B.logits);
         }
         PiProfScope ps(ctx, st, "k_topk");
-        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
-                 st>>>(B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
+        launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st, B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
     } else if (L->d % 128 == 0 && L->d <= 4096) {
         // decode-sized batch: exact logits of every token, one chain per lane
         {
@@ -1972,8 +1987,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             }
         }
         PiProfScope ps(ctx, st, "k_topk");
-        k_topk<<<(unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), TK_WARPS * 32, 0,
-                 st>>>(B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
+        launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st, B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
     } else {
         return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be a multiple of 128, at most 4096");
     }
