@@ -256,74 +256,6 @@ __global__ void k_transpose_rows(const float* __restrict__ src, int rows, int co
 }
 
 // ---------------------------------------------------------------------------
-// k_router_dec: exact logits of every token for decode-sized batches. Each logit
-// is the reference's sequential f32 chain (quant/mod.rs:921-935): one rounded mul
-// then one rounded add per input, ascending, bit for bit. T x (E + 1) chains run
-// side by side, so the chain latency (d dependent adds) sets the time. CTA = R
-// router rows (row E = the shared-expert gate) x TK tokens; lane = (row, token),
-// a warp covering R rows x 32/R tokens. The CTA's whole slice (R rows and TK token
-// rows, row pitch d + 4 floats so a lane's 16-byte reads of its own row fall in
-// distinct banks) arrives by bulk copies issued by separate threads, in RD_NC
-// chunks of the inputs with one mbarrier each, so the chains start once the first
-// chunk has landed while the rest is in flight; a lane then gets
-// four steps' weights and inputs from two 16-byte shared loads. The wait is
-// bounded (PI_DEVERR_TIMEOUT).
-// ---------------------------------------------------------------------------
-constexpr int RD_NC = 4;  // chunks of the inputs, one mbarrier each
-template <int R, int TK>
-constexpr size_t rd_smem(int d) { return sizeof(float) * (size_t)(R + TK) * (d + 4); }
-template <int R, int TK>
-__global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__ xin, const float* __restrict__ W,
-                                                       const float* __restrict__ bias, int T, int d, int E,
-                                                       float* __restrict__ logits, uint32_t* err) {
-    extern __shared__ __align__(16) float rd_sm[];
-    __shared__ __align__(8) uint64_t full[RD_NC];
-    const int tid = threadIdx.x;
-    const int e0 = blockIdx.x * R, t0 = blockIdx.y * TK;
-    const int nt = min(TK, T - t0), nrow = min(R, E + 1 - e0);
-    const int pitch = d + 4, dc = d / RD_NC;
-    if (tid == 0) {
-        for (int c = 0; c < RD_NC; ++c) pitc::mbar_init(&full[c], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-        for (int c = 0; c < RD_NC; ++c) pitc::mbar_expect_tx(&full[c], (uint32_t)((nrow + nt) * dc * 4));
-    }
-    __syncthreads();
-    // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens
-    for (int q = tid; q < (R + TK) * RD_NC; q += TK * R) {
-        const int row = q % (R + TK), c = q / (R + TK);
-        const float* src = nullptr;
-        if (row < nrow) src = W + (int64_t)(e0 + row) * d;
-        else if (row >= R && row - R < nt) src = xin + (int64_t)(t0 + row - R) * d;
-        if (src) pitc::bulk_load(rd_sm + row * pitch + c * dc, src + c * dc, (uint32_t)dc * 4, &full[c]);
-    }
-    const int r = tid % R, tk = tid / R;
-    const bool live = r < nrow && tk < nt;
-    const float* wr = rd_sm + r * pitch;
-    const float* xv = rd_sm + (R + tk) * pitch;
-    float acc = 0.0f;
-    for (int c = 0; c < RD_NC; ++c) {
-        if (!pitc::mbar_wait(&full[c], 0)) {
-            if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
-            return;
-        }
-        if (!live) continue;
-#pragma unroll 8
-        for (int i = c * dc; i < (c + 1) * dc; i += 4) {
-            const float4 w4 = *reinterpret_cast<const float4*>(wr + i);
-            const float4 x4 = *reinterpret_cast<const float4*>(xv + i);
-            acc = fadd(acc, fmul(w4.x, x4.x));
-            acc = fadd(acc, fmul(w4.y, x4.y));
-            acc = fadd(acc, fmul(w4.z, x4.z));
-            acc = fadd(acc, fmul(w4.w, x4.w));
-        }
-    }
-    if (!live) return;
-    const int e = e0 + r;
-    if (bias && e < E) acc = fadd(acc, bias[e]);
-    logits[(size_t)(t0 + tk) * (E + 1) + e] = acc;
-}
-
-// ---------------------------------------------------------------------------
 // k_router_exact_list: exact (reference-order) logits for the tokens listed
 // in list[0 .. *n_list). CTA = 32 router rows x one listed token at a time;
 // the 256 threads stage 32 x 256 tiles of the rows in shared memory (next
@@ -408,6 +340,88 @@ constexpr int TK_WARPS = 4, TK_PER_LANE = 16;  // E <= 32 * TK_PER_LANE
 // for non-negative floats; 1 for NaN, 0 for taken) and then the lowest index
 // holding it with redux.sync min.
 template <int NPL>
+PI_DEV void topk_token(const float* __restrict__ logits, int t, int E, int k, int has_shgate,
+                       int32_t* __restrict__ idx, float* __restrict__ gates, float* __restrict__ shscale,
+                       int32_t* __restrict__ counts, float* p, int* sel, int lane) {
+    const float* lr = logits + (size_t)t * (E + 1);
+    float l[NPL];
+    float m = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        l[j] = (e < E) ? __ldcg(lr + e) : -INFINITY;
+        if (e < E) m = fmaxf(m, l[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) p[e] = exp_cr(fsub(l[j], m));
+    }
+    __syncwarp();
+    // exp_sum: sequential sum in expert order (model/mod.rs:1282)
+    float es = 0.0f;
+    if (lane == 0) {
+#pragma unroll 16
+        for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
+    }
+    es = __shfl_sync(0xffffffffu, es, 0);
+    float pr[NPL];
+    uint32_t key[NPL];
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        pr[j] = (e < E) ? fdiv(p[e], es) : 0.0f;
+        key[j] = (e < E) ? (pr[j] == pr[j] ? __float_as_uint(pr[j]) + 2u : 1u) : 0u;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < NPL; ++j) {
+        const int e = lane + 32 * j;
+        if (e < E) p[e] = pr[j];
+    }
+    for (int r = 0; r < k; ++r) {
+        uint32_t mk = 0;
+#pragma unroll
+        for (int j = 0; j < NPL; ++j) mk = max(mk, key[j]);
+        mk = __reduce_max_sync(0xffffffffu, mk);
+        uint32_t me = 0xffffffffu;
+#pragma unroll
+        for (int j = NPL - 1; j >= 0; --j)
+            if (key[j] == mk) me = lane + 32 * j;
+        const int bi = (int)__reduce_min_sync(0xffffffffu, me);
+        if ((bi & 31) == lane) {
+#pragma unroll
+            for (int j = 0; j < NPL; ++j)
+                if (j == (bi >> 5)) key[j] = 0;
+        }
+        if (lane == 0) sel[r] = bi;
+    }
+    __syncwarp();
+    // ascending sort of the k selected indices (model/mod.rs:1303)
+    const int mine = (lane < k) ? sel[lane] : 0x7fffffff;
+    int rank = 0;
+    for (int r = 0; r < k; ++r) rank += (sel[r] < mine);
+    __syncwarp();
+    if (lane < k) sel[rank] = mine;
+    __syncwarp();
+    float ssum = 0.0f;
+    if (lane == 0)
+        for (int r = 0; r < k; ++r) ssum = fadd(ssum, p[sel[r]]);
+    ssum = __shfl_sync(0xffffffffu, ssum, 0);
+    if (lane < k) {
+        const int e = sel[lane];
+        const float pe = p[e];
+        idx[(size_t)t * k + lane] = e;
+        gates[(size_t)t * k + lane] = (ssum > 0.0f) ? fdiv(pe, ssum) : pe;
+        atomicAdd(&counts[e], 1);
+    }
+    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(__ldcg(lr + E)) : 1.0f;
+    __syncwarp();
+}
+
+template <int NPL>
 __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict__ logits, int T, int E, int k,
                                                         int has_shgate, int32_t* __restrict__ idx,
                                                         float* __restrict__ gates, float* __restrict__ shscale,
@@ -418,85 +432,9 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
     __shared__ int s_sel[TK_WARPS][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n_tok = list ? *n_list : T;
-    for (int g = blockIdx.x * TK_WARPS + warp; g < n_tok; g += gridDim.x * TK_WARPS) {
-        const int t = list ? list[g] : g;
-        const float* lr = logits + (size_t)t * (E + 1);
-        float l[NPL];
-        float m = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            l[j] = (e < E) ? lr[e] : -INFINITY;
-            if (e < E) m = fmaxf(m, l[j]);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        float* p = s_p[warp];
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E) p[e] = exp_cr(fsub(l[j], m));
-        }
-        __syncwarp();
-        // exp_sum: sequential sum in expert order (model/mod.rs:1282)
-        float es = 0.0f;
-        if (lane == 0) {
-#pragma unroll 16
-            for (int e = 0; e < E; ++e) es = fadd(es, p[e]);
-        }
-        es = __shfl_sync(0xffffffffu, es, 0);
-        float pr[NPL];
-        uint32_t key[NPL];
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            pr[j] = (e < E) ? fdiv(p[e], es) : 0.0f;
-            key[j] = (e < E) ? (pr[j] == pr[j] ? __float_as_uint(pr[j]) + 2u : 1u) : 0u;
-        }
-        __syncwarp();
-#pragma unroll
-        for (int j = 0; j < NPL; ++j) {
-            const int e = lane + 32 * j;
-            if (e < E) p[e] = pr[j];
-        }
-        for (int r = 0; r < k; ++r) {
-            uint32_t mk = 0;
-#pragma unroll
-            for (int j = 0; j < NPL; ++j) mk = max(mk, key[j]);
-            mk = __reduce_max_sync(0xffffffffu, mk);
-            uint32_t me = 0xffffffffu;
-#pragma unroll
-            for (int j = NPL - 1; j >= 0; --j)
-                if (key[j] == mk) me = lane + 32 * j;
-            const int bi = (int)__reduce_min_sync(0xffffffffu, me);
-            if ((bi & 31) == lane) {
-#pragma unroll
-                for (int j = 0; j < NPL; ++j)
-                    if (j == (bi >> 5)) key[j] = 0;
-            }
-            if (lane == 0) s_sel[warp][r] = bi;
-        }
-        __syncwarp();
-        // ascending sort of the k selected indices (model/mod.rs:1303)
-        const int mine = (lane < k) ? s_sel[warp][lane] : 0x7fffffff;
-        int rank = 0;
-        for (int r = 0; r < k; ++r) rank += (s_sel[warp][r] < mine);
-        __syncwarp();
-        if (lane < k) s_sel[warp][rank] = mine;
-        __syncwarp();
-        float ssum = 0.0f;
-        if (lane == 0)
-            for (int r = 0; r < k; ++r) ssum = fadd(ssum, p[s_sel[warp][r]]);
-        ssum = __shfl_sync(0xffffffffu, ssum, 0);
-        if (lane < k) {
-            const int e = s_sel[warp][lane];
-            const float pe = p[e];
-            idx[(size_t)t * k + lane] = e;
-            gates[(size_t)t * k + lane] = (ssum > 0.0f) ? fdiv(pe, ssum) : pe;
-            atomicAdd(&counts[e], 1);
-        }
-        if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(lr[E]) : 1.0f;
-    }
+    for (int g = blockIdx.x * TK_WARPS + warp; g < n_tok; g += gridDim.x * TK_WARPS)
+        topk_token<NPL>(logits, list ? list[g] : g, E, k, has_shgate, idx, gates, shscale, counts, s_p[warp],
+                        s_sel[warp], lane);
 }
 
 // k_topk for E experts (E <= 512).
@@ -510,6 +448,95 @@ void launch_topk(unsigned grid, cudaStream_t st, const float* logits, int T, int
     else TOPK(16);
 #undef TOPK
 }
+
+// ---------------------------------------------------------------------------
+// k_router_dec: exact logits of every token for decode-sized batches. Each logit
+// is the reference's sequential f32 chain (quant/mod.rs:921-935): one rounded mul
+// then one rounded add per input, ascending, bit for bit. T x (E + 1) chains run
+// side by side, so the chain latency (d dependent adds) sets the time. CTA = R
+// router rows (row E = the shared-expert gate) x TK tokens; lane = (row, token),
+// a warp covering R rows x 32/R tokens. The CTA's whole slice (R rows and TK token
+// rows, row pitch d + 4 floats so a lane's 16-byte reads of its own row fall in
+// distinct banks) arrives by bulk copies issued by separate threads, in RD_NC
+// chunks of the inputs with one mbarrier each, so the chains start once the first
+// chunk has landed while the rest is in flight; a lane then gets
+// four steps' weights and inputs from two 16-byte shared loads. The wait is
+// bounded (PI_DEVERR_TIMEOUT). The last CTA to finish a token group (a ticket per
+// group, taken after the logits are written and fenced) then routes the group's
+// tokens (topk_token, warp per token), which saves the separate top-k launch.
+// ---------------------------------------------------------------------------
+constexpr int RD_NC = 4;  // chunks of the inputs, one mbarrier each
+template <int R, int TK>
+constexpr size_t rd_smem(int d) { return sizeof(float) * (size_t)(R + TK) * (d + 4); }
+template <int R, int TK, int NPL, bool FUSE>
+__global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__ xin, const float* __restrict__ W,
+                                                       const float* __restrict__ bias, int T, int d, int E,
+                                                       float* __restrict__ logits, int k, int has_shgate,
+                                                       int32_t* __restrict__ idx, float* __restrict__ gates,
+                                                       float* __restrict__ shscale, int32_t* __restrict__ counts,
+                                                       int32_t* __restrict__ tickets, int fuse, uint32_t* err) {
+    static_assert(!FUSE || TK * R == TK_WARPS * 32, "one warp per top-k token slot");
+    extern __shared__ __align__(16) float rd_sm[];
+    __shared__ __align__(8) uint64_t full[RD_NC];
+    const int tid = threadIdx.x;
+    const int e0 = blockIdx.x * R, t0 = blockIdx.y * TK;
+    const int nt = min(TK, T - t0), nrow = min(R, E + 1 - e0);
+    const int pitch = d + 4, dc = d / RD_NC;
+    if (tid == 0) {
+        for (int c = 0; c < RD_NC; ++c) pitc::mbar_init(&full[c], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int c = 0; c < RD_NC; ++c) pitc::mbar_expect_tx(&full[c], (uint32_t)((nrow + nt) * dc * 4));
+    }
+    __syncthreads();
+    // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens
+    for (int q = tid; q < (R + TK) * RD_NC; q += TK * R) {
+        const int row = q % (R + TK), c = q / (R + TK);
+        const float* src = nullptr;
+        if (row < nrow) src = W + (int64_t)(e0 + row) * d;
+        else if (row >= R && row - R < nt) src = xin + (int64_t)(t0 + row - R) * d;
+        if (src) pitc::bulk_load(rd_sm + row * pitch + c * dc, src + c * dc, (uint32_t)dc * 4, &full[c]);
+    }
+    const int r = tid % R, tk = tid / R;
+    const bool live = r < nrow && tk < nt;
+    const float* wr = rd_sm + r * pitch;
+    const float* xv = rd_sm + (R + tk) * pitch;
+    float acc = 0.0f;
+    for (int c = 0; c < RD_NC; ++c) {
+        if (!pitc::mbar_wait(&full[c], 0)) {
+            if (tid == 0) atomicOr(err, PI_DEVERR_TIMEOUT);
+            return;
+        }
+        if (!live) continue;
+#pragma unroll 8
+        for (int i = c * dc; i < (c + 1) * dc; i += 4) {
+            const float4 w4 = *reinterpret_cast<const float4*>(wr + i);
+            const float4 x4 = *reinterpret_cast<const float4*>(xv + i);
+            acc = fadd(acc, fmul(w4.x, x4.x));
+            acc = fadd(acc, fmul(w4.y, x4.y));
+            acc = fadd(acc, fmul(w4.z, x4.z));
+            acc = fadd(acc, fmul(w4.w, x4.w));
+        }
+    }
+    if (live) {
+        const int e = e0 + r;
+        if (bias && e < E) acc = fadd(acc, bias[e]);
+        logits[(size_t)(t0 + tk) * (E + 1) + e] = acc;
+    }
+    if (!FUSE || !fuse) return;
+    __shared__ float s_p[TK_WARPS][32 * NPL];
+    __shared__ int s_sel[TK_WARPS][32];
+    __shared__ int s_last;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_last = atomicAdd(&tickets[blockIdx.y], 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int j = warp; j < nt; j += TK_WARPS)
+        topk_token<NPL>(logits, t0 + j, E, k, has_shgate, idx, gates, shscale, counts, s_p[warp], s_sel[warp], lane);
+}
+
 
 
 // ---------------------------------------------------------------------------
@@ -1697,7 +1724,7 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.xs = b.take<float>(T * (d / 32));
     f.logits = b.take<float>(T * (E + 1));
     f.flag_list = b.take<int32_t>(T);
-    f.n_flag = b.take<int32_t>(1);
+    f.n_flag = b.take<int32_t>(2 + (T + 7) / 8);  // [0] flagged tokens, [1..] router tickets
     f.idx = b.take<int32_t>(T * k);
     f.gates = b.take<float>(T * k);
     f.shscale = b.take<float>(T);
@@ -1926,7 +1953,8 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
-    if (pi_cuda_check(ctx, cudaMemsetAsync(B.n_flag, 0, sizeof(int32_t), st), "memset flags")) return PI_ERR_CUDA;
+    if (pi_cuda_check(ctx, cudaMemsetAsync(B.n_flag, 0, sizeof(int32_t) * (2 + (T + 7) / 8), st), "memset flags"))
+        return PI_ERR_CUDA;
     if (use_router_tc(L, T)) {
         // prefill-sized batch: fast logits on tensor cores, exact chains for the
         // candidates of each token, the exact path for tokens that stay uncertain
@@ -1968,26 +1996,46 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         // decode-sized batch: exact logits of every token, one chain per lane
         {
             PiProfScope ps(ctx, st, "k_router_dec");
-            static bool rd_attr = false;
-            if (!rd_attr) {
-                cudaFuncSetAttribute(k_router_dec<16, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)rd_smem<16, 8>(2048));
-                cudaFuncSetAttribute(k_router_dec<8, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)rd_smem<8, 4>(4096));
-                rd_attr = true;
-            }
+            const int hs = L->has_shared_gate ? 1 : 0;
+            int32_t* tickets = B.n_flag + 1;
+            // small batches: router + top-k in one launch (the last CTA of a token group
+            // routes it); larger ones route in a separate launch with a warp per token
+            const int fuse = T <= 8 ? 1 : 0;
             if (d <= 2048) {
                 dim3 rg((unsigned)((E + 1 + 15) / 16), (unsigned)((T + 7) / 8));
-                k_router_dec<16, 8><<<rg, 128, rd_smem<16, 8>(d), st>>>(xin, L->router, L->bias, (int)T, d, E,
-                                                                        B.logits, ctx->dev_err);
+#define RD16(N)                                                                                               \
+    {                                                                                                         \
+        static bool attr = false;                                                                             \
+        if (!attr) {                                                                                          \
+            cudaFuncSetAttribute(k_router_dec<16, 8, N, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
+                                 (int)rd_smem<16, 8>(2048));                                                  \
+            attr = true;                                                                                      \
+        }                                                                                                     \
+        k_router_dec<16, 8, N, true><<<rg, 128, rd_smem<16, 8>(d), st>>>(xin, L->router, L->bias, (int)T, d, \
+                                                                         E, B.logits, k, hs, idx, gates,      \
+                                                                         B.shscale, counts, tickets, fuse,    \
+                                                                         ctx->dev_err);                       \
+    }
+                if (E <= 64) RD16(2) else if (E <= 128) RD16(4) else if (E <= 256) RD16(8) else RD16(16)
+#undef RD16
+                if (!fuse)
+                    launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
+                                B.logits, (int)T, E, k, hs, idx, gates, B.shscale, counts, nullptr, nullptr);
             } else {
+                static bool attr = false;
+                if (!attr) {
+                    cudaFuncSetAttribute(k_router_dec<8, 4, 16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)rd_smem<8, 4>(4096));
+                    attr = true;
+                }
                 dim3 rg((unsigned)((E + 1 + 7) / 8), (unsigned)((T + 3) / 4));
-                k_router_dec<8, 4><<<rg, 32, rd_smem<8, 4>(d), st>>>(xin, L->router, L->bias, (int)T, d, E,
-                                                                     B.logits, ctx->dev_err);
+                k_router_dec<8, 4, 16, false><<<rg, 32, rd_smem<8, 4>(d), st>>>(
+                    xin, L->router, L->bias, (int)T, d, E, B.logits, k, hs, idx, gates, B.shscale, counts, tickets, 0,
+                    ctx->dev_err);
+                launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
+                            B.logits, (int)T, E, k, hs, idx, gates, B.shscale, counts, nullptr, nullptr);
             }
         }
-        PiProfScope ps(ctx, st, "k_topk");
-        launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st, B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, nullptr, nullptr);
     } else {
         return pi_set_error(ctx, PI_ERR_ARG, "router: n_embd must be a multiple of 128, at most 4096");
     }
