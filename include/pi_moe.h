@@ -165,7 +165,8 @@ typedef struct pi_moe_layer_desc {
 int pi_moe_layer_create(pi_ctx* ctx, const pi_moe_layer_desc* desc, pi_moe_layer** out);
 void pi_moe_layer_destroy(pi_moe_layer* layer);
 
-/* Routing only: model/mod.rs:1254-1312 for T tokens x [T][d] (f32, device).
+/* Routing only: model/mod.rs:1254-1312 for T tokens x [T][d] (f32, device, 16-byte
+ * aligned: the kernels read token rows with 16-byte loads; PI_ERR_ARG otherwise).
  * idx/gates [T][k] (ascending expert per token; renormalised gates),
  * counts/offsets [E], perm [T*k] (perm[offsets[e]+r] = r-th token routed to e,
  * tokens ascending). Any output pointer may be NULL. */
@@ -174,7 +175,7 @@ int pi_moe_route(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, in
 
 /* Full MoE FFN for T tokens: router -> top-k -> dispatch -> expert SwiGLU ->
  * gate-weighted combine + sigmoid-gated shared expert
- * (model/mod.rs:1245-1571). out [T][d] f32. flags: PI_FWD_*. */
+ * (model/mod.rs:1245-1571). out [T][d] f32. x and out 16-byte aligned. flags: PI_FWD_*. */
 int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, float* out, int32_t flags,
                    void* stream);
 

@@ -268,6 +268,8 @@ static int moe_common(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, f
     if (T < 0 || (T > 0 && !x)) return pi_set_error(ctx, PI_ERR_ARG, "moe: bad token batch");
     if (T == 0) return PI_OK;
     if (T > (1 << 20)) return pi_set_error(ctx, PI_ERR_ARG, "moe: T too large");
+    if (((uintptr_t)x | (uintptr_t)out) & 15)  // the kernels read and write token rows with 16-byte accesses
+        return pi_set_error(ctx, PI_ERR_ARG, "moe: x and out must be 16-byte aligned");
     if (out && L->n_exp != L->E)
         return pi_set_error(ctx, PI_ERR_ARG, "moe forward: the layer holds a subset of the experts (use the pi_moe_ep_* calls)");
     cudaStream_t st = (cudaStream_t)stream;
@@ -318,6 +320,8 @@ extern "C" int pi_moe_ep_combine(pi_ctx* ctx, pi_moe_layer* L, const float* x, i
     if (!ctx || !L) return PI_ERR_ARG;
     if (T < 0) return pi_set_error(ctx, PI_ERR_ARG, "ep combine: bad token batch");
     if (T == 0) return PI_OK;
+    if (((uintptr_t)x | (uintptr_t)out | (uintptr_t)y_back | (uintptr_t)y_shared) & 15)
+        return pi_set_error(ctx, PI_ERR_ARG, "ep combine: x, out and the expert rows must be 16-byte aligned");
     return pi_moe_ep_combine_run(ctx, L, x, T, flags, gates, shscale, slot_row, y_back, y_shared, out,
                                  (cudaStream_t)stream);
 }

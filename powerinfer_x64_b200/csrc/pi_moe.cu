@@ -895,28 +895,45 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
     for (int q = threadIdx.x; q < nI; q += blockDim.x)
         items[ibase + q] = make_int4(e, off + q * tg, min(tg, cnt - q * tg), 0);
     if (cnt == 0) return;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // slots of expert e in ascending token order: each thread checks DPT consecutive
+    // tokens per round, a block scan of the per-thread match counts gives the ranks
+    constexpr int DPT = 4;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int base = 0;
-    for (int t0 = 0; t0 < T; t0 += blockDim.x) {
-        const int t = t0 + threadIdx.x;
-        int jsel = -1;
-        if (t < T)
-            for (int j = 0; j < k; ++j)
-                if (idx[(size_t)t * k + j] == e) jsel = j;
-        const unsigned bal = __ballot_sync(0xffffffffu, jsel >= 0);
-        const int wrank = __popc(bal & ((1u << lane) - 1u));
-        __syncthreads();
-        if (lane == 0) s_wsum[warp] = __popc(bal);
+    for (int t0 = 0; t0 < T; t0 += blockDim.x * DPT) {
+        int jsel[DPT], mine = 0;
+#pragma unroll
+        for (int q = 0; q < DPT; ++q) {
+            const int t = t0 + threadIdx.x * DPT + q;
+            jsel[q] = -1;
+            if (t < T)
+                for (int j = 0; j < k; ++j)
+                    if (idx[(size_t)t * k + j] == e) jsel[q] = j;
+            mine += jsel[q] >= 0;
+        }
+        int incl = mine;  // inclusive warp scan of the match counts
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += y;
+        }
+        __syncthreads();  // s_wsum of the previous round is consumed
+        if (lane == 31) s_wsum[warp] = incl;
         __syncthreads();
         int before = 0, total = 0;
-        for (int w = 0; w < (int)(blockDim.x >> 5); ++w) {
+        for (int w = 0; w < nw; ++w) {
             if (w < warp) before += s_wsum[w];
             total += s_wsum[w];
         }
-        if (jsel >= 0) {
-            const int slot = off + base + before + wrank;
-            perm[slot] = t;
-            slot_of[(size_t)t * k + jsel] = slot;
+        int slot = off + base + before + incl - mine;
+#pragma unroll
+        for (int q = 0; q < DPT; ++q) {
+            if (jsel[q] >= 0) {
+                const int t = t0 + threadIdx.x * DPT + q;
+                perm[slot] = t;
+                slot_of[(size_t)t * k + jsel[q]] = slot;
+                ++slot;
+            }
         }
         base += total;
     }
@@ -1394,18 +1411,37 @@ __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, co
                                                  const float* __restrict__ shscale, const float* __restrict__ y_sh,
                                                  int T, int k, int d, int has_shared, int residual,
                                                  float* __restrict__ out) {
+    // thread = 4 consecutive columns (16-byte loads); each column's sum keeps the
+    // reference order: routed experts ascending, then the shared expert, then x
     const int t = blockIdx.x;
-    const int c = blockIdx.y * blockDim.x + threadIdx.x;
-    if (c < d) {
-        float acc = 0.0f;
-        for (int j = 0; j < k; ++j) {
-            const int slot = slot_of[(size_t)t * k + j];
-            acc = fadd(acc, fmul(gates[(size_t)t * k + j], y[(size_t)slot * d + c]));
-        }
-        if (has_shared)
-            acc = fadd(acc, fmul(shscale[t], y_sh ? y_sh[(size_t)t * d + c] : y[((size_t)T * k + t) * d + c]));
-        out[(size_t)t * d + c] = residual ? fadd(x[(size_t)t * d + c], acc) : acc;
+    const int c = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
+    if (c >= d) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < k; ++j) {
+        const int slot = slot_of[(size_t)t * k + j];
+        const float g = gates[(size_t)t * k + j];
+        const float4 v = *reinterpret_cast<const float4*>(y + (size_t)slot * d + c);
+        acc.x = fadd(acc.x, fmul(g, v.x));
+        acc.y = fadd(acc.y, fmul(g, v.y));
+        acc.z = fadd(acc.z, fmul(g, v.z));
+        acc.w = fadd(acc.w, fmul(g, v.w));
     }
+    if (has_shared) {
+        const float g = shscale[t];
+        const float4 v = *reinterpret_cast<const float4*>(y_sh ? y_sh + (size_t)t * d + c : y + ((size_t)T * k + t) * d + c);
+        acc.x = fadd(acc.x, fmul(g, v.x));
+        acc.y = fadd(acc.y, fmul(g, v.y));
+        acc.z = fadd(acc.z, fmul(g, v.z));
+        acc.w = fadd(acc.w, fmul(g, v.w));
+    }
+    if (residual) {
+        const float4 xv = *reinterpret_cast<const float4*>(x + (size_t)t * d + c);
+        acc.x = fadd(xv.x, acc.x);
+        acc.y = fadd(xv.y, acc.y);
+        acc.z = fadd(xv.z, acc.z);
+        acc.w = fadd(xv.w, acc.w);
+    }
+    *reinterpret_cast<float4*>(out + (size_t)t * d + c) = acc;
 }
 
 // ---------------------------------------------------------------------------
@@ -2057,7 +2093,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     }
     if (int rc = run_experts(ctx, L, a, T, n_slots, ni, gemm, B, st)) return rc;
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale,
+    k_combine<<<dim3((unsigned)T, (unsigned)((d + 1023) / 1024)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale,
                                                                            nullptr, (int)T, k, d,
                                                                            L->has_shared ? 1 : 0,
                                                                            (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
@@ -2148,7 +2184,7 @@ int pi_moe_ep_combine_run(pi_ctx* ctx, const pi_moe_layer* L, const float* x, in
                           float* out, cudaStream_t st) {
     const int d = (int)L->d;
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<dim3((unsigned)T, (unsigned)((d + 255) / 256)), 256, 0, st>>>(
+    k_combine<<<dim3((unsigned)T, (unsigned)((d + 1023) / 1024)), 256, 0, st>>>(
         x, y_back, gates, slot_row, shscale, y_shared, (int)T, L->k, d, (L->has_shared && y_shared) ? 1 : 0,
         (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
     return pi_cuda_check(ctx, cudaGetLastError(), "ep combine") ? PI_ERR_CUDA : PI_OK;
