@@ -491,3 +491,20 @@ def test_moe_forward_api(pkg):
     # all experts equal -> output = single expert output (weights sum to 1)
     single = moe.expert_forward(np.array([1, 0, 0, 0], np.float32), *ew.get_expert(0), n_embd, f)
     assert np.allclose(out, single, rtol=1e-6)
+
+
+@pytest.mark.gpu
+def test_forward_rejects_misaligned_rows(pkg, torch):
+    """The layer kernels read and write token rows with 16-byte accesses: a token
+    batch that starts off a 16-byte boundary is refused with PI_ERR_ARG instead of
+    reaching the GPU."""
+    from powerinfer_x64_b200 import PiError, synth
+
+    c = synth.C1
+    L = synth.moe_layer(c, seed=1)
+    buf = torch.zeros(4 * c.d + 1, dtype=torch.float32, device="cuda")
+    with pytest.raises(PiError):
+        L.forward(buf[1:].view(4, c.d))
+    out = L.forward(buf[: 4 * c.d].view(4, c.d))
+    torch.cuda.synchronize()
+    assert tuple(out.shape) == (4, c.d)
