@@ -303,13 +303,25 @@ __global__ __launch_bounds__(1024) void k_sf_plan(const int64_t* __restrict__ pt
     uint32_t dense = 0;  // token bits of the complete lists, in every byte
     for (int t = 0; t < nt; ++t)
         if (s_ptr[t + 1] - s_ptr[t] >= n_ff) dense |= 0x01010101u << t;
-    for (int64_t q = s_ptr[0] + tid; q < s_ptr[nt]; q += 1024) {  // every token's entries at once
-        int t = 0;
-        while (q >= s_ptr[t + 1]) ++t;
-        if ((dense >> t) & 1u) continue;
-        const int64_t s = idx[q];
-        if (s < 0 || s >= n_ff) { atomicOr(err, PI_DEVERR_INDEX); continue; }
-        atomicOr(&bits[s >> 2], 1u << (8 * (s & 3) + t));
+    // every token's entries at once, four loads in flight per thread
+    for (int64_t q0 = s_ptr[0] + tid; q0 < s_ptr[nt]; q0 += 4 * 1024) {
+        int64_t sv[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t q = q0 + u * 1024;
+            sv[u] = q < s_ptr[nt] ? __ldg(idx + q) : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int64_t q = q0 + u * 1024;
+            if (q >= s_ptr[nt]) break;
+            int t = 0;
+            while (q >= s_ptr[t + 1]) ++t;
+            if ((dense >> t) & 1u) continue;
+            const int64_t s = sv[u];
+            if (s < 0 || s >= n_ff) { atomicOr(err, PI_DEVERR_INDEX); continue; }
+            atomicOr(&bits[s >> 2], 1u << (8 * (s & 3) + t));
+        }
     }
     __syncthreads();
     int carry = 0;  // thread per group: 32 mask bytes -> count -> exclusive scan -> list
