@@ -9,8 +9,9 @@ own home tokens). One layer forward is
   2. exchange              all-to-all-v of the rows (and their local expert ids);
   3. ``pi_moe_experts_q8`` the held experts over the received rows;
   4. exchange              all-to-all-v of the expert outputs back to the home rank;
-  5. ``pi_moe_experts_q8`` the shared expert over the home tokens, and
-     ``pi_moe_ep_combine`` the gate-weighted sum in ascending expert order.
+  5. ``pi_moe_ep_combine`` the gate-weighted sum in ascending expert order, with the
+     shared expert (``pi_moe_experts_q8`` over the home tokens), which runs on a side
+     stream from step 1 on, overlapping the exchanges and the routed experts.
 
 Every expert row is computed exactly as the one-GPU layer computes it and the
 combine order is the reference's, so the result equals ``MoeLayer.forward`` on
@@ -143,6 +144,19 @@ class EPMoeLayer:
         self.ctx.check(L.pi_moe_ep_route(self.ctx.h, self.h, ptr(xd), T, flags, self.world, ptr(idx), ptr(gates),
                                          ptr(shscale), ptr(xq), ptr(xs), ptr(send_counts), ptr(send_xq), ptr(send_xs),
                                          ptr(send_eid), ptr(slot_row), s))
+        # the shared expert needs only the home tokens: it runs on a side stream while
+        # the counts and rows are exchanged and the routed experts run
+        y_sh = None
+        if self.has_shared and T:
+            y_sh = e(T, d)
+            cur = torch.cuda.current_stream()
+            self._side = getattr(self, "_side", None) or torch.cuda.Stream(device=dv)
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self.ctx.check(L.pi_moe_experts_q8(self.ctx.h, self.h, T, ptr(xq), ptr(xs), None, ptr(y_sh),
+                                                   stream_ptr(self._side)))
+            for t_ in (xq, xs, y_sh):
+                t_.record_stream(self._side)
         ex = self.exchange
         send_splits, recv_splits = ex.counts(send_counts)
         r_xq = ex.rows(send_xq, send_splits, recv_splits)
@@ -152,10 +166,8 @@ class EPMoeLayer:
         y = e(max(n_recv, 1), d)
         self.ctx.check(L.pi_moe_experts_q8(self.ctx.h, self.h, n_recv, ptr(r_xq), ptr(r_xs), ptr(r_eid), ptr(y), s))
         y_back = ex.rows(y, recv_splits, send_splits)
-        y_sh = None
-        if self.has_shared and T:
-            y_sh = e(T, d)
-            self.ctx.check(L.pi_moe_experts_q8(self.ctx.h, self.h, T, ptr(xq), ptr(xs), None, ptr(y_sh), s))
+        if y_sh is not None:
+            torch.cuda.current_stream().wait_stream(self._side)
         self.ctx.check(L.pi_moe_ep_combine(self.ctx.h, self.h, ptr(xd), T, flags, ptr(gates), ptr(shscale),
                                            ptr(slot_row), ptr(y_back), ptr(y_sh) if y_sh is not None else None,
                                            ptr(out), s))
