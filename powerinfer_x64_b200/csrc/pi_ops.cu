@@ -527,8 +527,9 @@ __global__ __launch_bounds__(2 * CPL * 32) void k_sf_gateup_q8(
 // down, neuron-major, over the pass plan: CTA = (512 output columns, SF_GPC
 // 32-neuron groups); thread owns 2 consecutive columns. The CTA first stages its
 // groups' active neurons, h = SwiGLU(g, u) (quant/mod.rs:1196-1199) of every
-// (token, neuron) and the thread's block scales of each group, then runs over the
-// neurons with independent weight loads; y is accumulated with float2 atomics over
+// (token, neuron) and the thread's block scales of each group, while the neurons'
+// weight slices are copied into shared memory (cp.async); then it runs over the
+// neurons from shared memory; y is accumulated with float2 atomics over
 // the group chunks. Q8_0 weights and a token whose list is complete: the reference
 // then takes the dense ffn_swiglu_q, whose down projection re-quantises h to Q8_0
 // blocks (quant/mod.rs:1203), so such a token's h is replaced by its Q8_0 value q * d.
@@ -541,6 +542,8 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
     __shared__ int32_t s_list[SF_GPC * 32];
     __shared__ float s_h[NTM][SF_GPC * 32];
     __shared__ float2 s_sc[SF_GPC][256];
+    constexpr int RB = QT == PI_QT_Q4_0 ? 256 : 512;  // bytes of a neuron's 512 columns
+    __shared__ __align__(16) uint8_t s_w[SF_GPC * 32][RB];
     const int ng = (int)(n_ff / 32);
     const int g0 = blockIdx.y * SF_GPC, g1 = min(ng, g0 + SF_GPC);
     const int i0 = gofs[g0], n = gofs[g1] - i0;
@@ -561,6 +564,19 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
             s_h[t][tid] = h;
         }
     }
+    __syncthreads();
+    {  // the active neurons' weight slices, copied in while the scales and h are prepared
+        const int64_t rowb = QT == PI_QT_Q4_0 ? n_embd / 2 : n_embd;
+        const int64_t cb = blockIdx.x * (int64_t)RB;
+        for (int q = tid; q < n * (RB / 16); q += 256) {
+            const int i = q / (RB / 16), ch = q % (RB / 16);
+            const uint32_t sa = (uint32_t)__cvta_generic_to_shared(&s_w[i][16 * ch]);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa),
+                         "l"(DQ + (int64_t)s_list[i] * rowb + cb + 16 * ch)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     for (int gi = 0; gi < g1 - g0; ++gi) {
         float2 sc = make_float2(0.f, 0.f);
         if (gofs[g0 + gi + 1] > gofs[g0 + gi])
@@ -578,6 +594,7 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
             }
         }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
     float acc[NTM][2];
 #pragma unroll
@@ -588,11 +605,11 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
         const float2 sc = s_sc[(s >> 5) - g0][tid];
         float w0, w1;
         if (QT == PI_QT_Q4_0) {
-            const uint32_t v = DQ[(int64_t)s * (n_embd / 2) + (c >> 1)];
+            const uint32_t v = s_w[i][tid];
             w0 = nibf(v & 15u) * sc.x;
             w1 = nibf(v >> 4) * sc.y;
         } else {
-            const uint32_t v = *reinterpret_cast<const uint16_t*>(DQ + (int64_t)s * n_embd + c);
+            const uint32_t v = *reinterpret_cast<const uint16_t*>(&s_w[i][2 * tid]);
             w0 = (float)(int8_t)(v & 0xffu) * sc.x;
             w1 = (float)(int8_t)(v >> 8) * sc.y;
         }
