@@ -866,6 +866,7 @@ __device__ int block_sum_int(int v, int* red) {
     return s;
 }
 
+template <int DPT>  // tokens ranked per thread per round
 __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ idx, const int32_t* __restrict__ counts,
                                                   int T, int k, int E, int has_shared, int32_t* __restrict__ offsets,
                                                   int32_t* __restrict__ perm, int32_t* __restrict__ slot_of,
@@ -897,7 +898,6 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
     if (cnt == 0) return;
     // slots of expert e in ascending token order: each thread checks DPT consecutive
     // tokens per round, a block scan of the per-thread match counts gives the ranks
-    constexpr int DPT = 4;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     int base = 0;
     for (int t0 = 0; t0 < T; t0 += blockDim.x * DPT) {
@@ -2079,7 +2079,11 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const int tg = gemm ? (q8 ? PI_GEMM_NT_Q8 : PI_GEMM_NT) : TG;
     {
         PiProfScope ps(ctx, st, "k_dispatch");
-        k_dispatch<<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
+        if ((int)T >= 8192)
+            k_dispatch<4><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
+                                                      perm, B.slot_of, B.items, B.n_items, tg);
+        else
+            k_dispatch<1><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
                                                       perm, B.slot_of, B.items, B.n_items, tg);
     }
     if (route_only) return pi_cuda_check(ctx, cudaGetLastError(), "route") ? PI_ERR_CUDA : PI_OK;
@@ -2165,7 +2169,12 @@ int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* 
     if (!shared_only) k_ep_hist<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(eid, n_rows, B.counts);
     {
         PiProfScope ps(ctx, st, "k_dispatch");
-        k_dispatch<<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
+        if ((int)n_rows >= 8192)
+            k_dispatch<4><<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
+                                                       shared_only ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
+                                                       B.n_items, tg);
+        else
+            k_dispatch<1><<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
                                                        shared_only ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
                                                        B.n_items, tg);
     }
