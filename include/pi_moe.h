@@ -143,7 +143,7 @@ int pi_ffn_swiglu_q_selected(pi_ctx* ctx, float* out, const float* x, const void
 
 typedef struct pi_moe_layer_desc {
     int64_t n_embd;         /* d                                                   */
-    int64_t n_ff_exp;       /* expert SwiGLU width f (expert_intermediate_size)    */
+    int64_t n_ff_exp;       /* expert SwiGLU width f: 128, 256, 512 or 1024         */
     int64_t n_ff_shexp;     /* shared-expert width; the reference uses n_ff_exp    */
     int32_t n_expert;       /* E                                                   */
     int32_t n_expert_used;  /* k                                                   */

@@ -188,6 +188,8 @@ static int layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, int e_first, in
         return pi_set_error(ctx, PI_ERR_ARG, "moe layer: need 1 <= k <= min(E, 32), E <= 512");
     if (!D->router || !D->gate_exps || !D->up_exps || !D->down_exps)
         return pi_set_error(ctx, PI_ERR_ARG, "moe layer: missing router or expert tensors");
+    if (D->n_ff_exp != 128 && D->n_ff_exp != 256 && D->n_ff_exp != 512 && D->n_ff_exp != 1024)
+        return pi_set_error(ctx, PI_ERR_ARG, "moe layer: expert width must be 128, 256, 512 or 1024");
     const bool has_sh = D->gate_shexp && D->up_shexp && D->down_shexp;
     const int64_t f_sh = D->n_ff_shexp ? D->n_ff_shexp : D->n_ff_exp;
     if (has_sh && f_sh != D->n_ff_exp)

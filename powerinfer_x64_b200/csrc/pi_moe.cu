@@ -2,28 +2,35 @@
 //
 // Reference path being replaced: model/mod.rs:1245-1571 (one token at a
 // time, two CPU threads of quant::ffn_swiglu_q calls). Here one call runs a
-// whole batch of T tokens through six kernels on one stream:
+// whole batch of T tokens through a few kernels on one stream:
 //
 //   k_prep        RMSNorm (optional, ops.rs:13-27 lane order) + Q8_0
 //                 activation quantiser (quant/mod.rs:698-736), per token.
-//   k_router      exact router logits: the reference's sequential f32 sum
-//                 (quant/mod.rs:921-935) per (token, expert), plus the
-//                 shared-expert gate dot (model/mod.rs:1500-1509) as row E.
-//   k_topk        softmax -> top-k (ties to the lowest index) -> ascending
-//                 sort -> renormalised gates (model/mod.rs:1278-1312).
+//   routing       router logits in the reference's sequential f32 order
+//                 (quant/mod.rs:921-935), row E = the shared-expert gate
+//                 (model/mod.rs:1500-1509), then softmax -> top-k (ties to the
+//                 lowest index) -> ascending sort -> renormalised gates
+//                 (model/mod.rs:1278-1312):
+//                   decode    k_router_dec (one exact chain per lane; for T <= 8
+//                             it also runs the top-k) + k_topk;
+//                   prefill   tensor-core logits certified by an error bound
+//                             (pi_prefill.cu) + k_router_cand, exact chains for
+//                             the uncertain tokens (k_router_exact_list);
+//                             k_router_wide when forced or E > 256.
 //   k_dispatch    per-expert counts, offsets, stable token permutation and
 //                 the work-item list for the expert kernels (no reference
 //                 counterpart: the reference loops token by token).
-//   k_gateup_*    gate+up GEMV over the tokens of each work item, SwiGLU,
-//                 and (Q8_0) re-quantisation of h (quant/mod.rs:1179-1204).
-//   k_down_*      down-projection GEMV per routed (token, expert) slot.
+//   experts       decode: k_gateup_* (gate+up GEMV, SwiGLU), k_quant_h (Q8_0
+//                 re-quantisation of h, quant/mod.rs:1179-1204), k_down_q8s /
+//                 k_down_q4; prefill: the tcgen05 GEMMs of pi_prefill.cu and
+//                 pi_prefill_q8.cu.
 //   k_combine     ascending-expert gate-weighted sum + sigmoid-gated shared
 //                 expert + optional residual (model/mod.rs:1525-1534,
 //                 :1627-1633), in the reference's exact f32 order.
 //
-// The expert kernels stream each weight row from HBM exactly once per work
-// item with 16-byte coalesced loads and keep it in registers while looping
-// over the item's tokens (decode-sized T: HBM-bound).
+// The decode expert kernels stream each weight row from HBM once per work item
+// with 16-byte coalesced loads (gate/up into registers, down through a bulk-copy
+// ring in shared memory) and loop over the item's tokens: HBM-bound.
 #include "pi_tc.cuh"
 // pi_tc.cuh (pi_common.cuh) comes first: it names the quant types that pi_moe.h defines as macros
 #include "pi_internal.h"
@@ -1865,7 +1872,8 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
             k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
         }
         PiProfScope ps(ctx, st, "k_down");
-        if (L->f / 64 <= 8) {  // streamed down: persistent CTAs fed by bulk copies
+        const int cpq = L->f % 64 ? 0 : (int)(L->f / 64);  // 16-byte chunks per quarter row
+        if (cpq == 2 || cpq == 4 || cpq == 8) {  // streamed down: persistent CTAs fed by bulk copies
             static bool ds_attr = false;
             if (!ds_attr) {
                 cudaFuncSetAttribute(k_down_q8s<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<2>::SMEM);
@@ -1874,7 +1882,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
                 ds_attr = true;
             }
             const unsigned g = (unsigned)std::min<int64_t>((int64_t)ni * (L->d / DS_ROWS), ctx->sm_count);
-            switch (L->f / 64) {
+            switch (cpq) {
                 case 2: k_down_q8s<2><<<g, DS_THREADS, DSL<2>::SMEM, st>>>(a, ctx->dev_err); break;
                 case 4: k_down_q8s<4><<<g, DS_THREADS, DSL<4>::SMEM, st>>>(a, ctx->dev_err); break;
                 case 8: k_down_q8s<8><<<g, DS_THREADS, DSL<8>::SMEM, st>>>(a, ctx->dev_err); break;
@@ -1886,13 +1894,9 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
             cudaFuncSetAttribute(k_down_q8<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem(16));
             dn_attr = true;
         }
-        switch (L->f / 64) {
-            case 2: k_down_q8<2><<<dn, 256, dn_smem(2), st>>>(a); break;
-            case 4: k_down_q8<4><<<dn, 256, dn_smem(4), st>>>(a); break;
-            case 8: k_down_q8<8><<<dn, 256, dn_smem(8), st>>>(a); break;
-            case 16: k_down_q8<16><<<dn, 256, dn_smem(16), st>>>(a); break;
-            default: return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128..1024 (x2)");
-        }
+        if (cpq != 16)  // widths 128, 256, 512 took the streamed kernel above
+            return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128, 256, 512 or 1024");
+        k_down_q8<16><<<dn, 256, dn_smem(16), st>>>(a);
     } else {
         {
         PiProfScope ps(ctx, st, "k_gateup");
