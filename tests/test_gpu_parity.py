@@ -508,3 +508,16 @@ def test_forward_rejects_misaligned_rows(pkg, torch):
     out = L.forward(buf[: 4 * c.d].view(4, c.d))
     torch.cuda.synchronize()
     assert tuple(out.shape) == (4, c.d)
+
+
+@pytest.mark.gpu
+def test_layer_rejects_unsupported_expert_width(pkg, orc, torch):
+    """Expert widths outside 128, 256, 512, 1024 are refused when the layer is built."""
+    from powerinfer_x64_b200 import PiError, moe
+
+    rng = np.random.default_rng(3)
+    d, E, k, f = 1024, 4, 2, 192
+    router = (rng.standard_normal(E * d) * 0.02).astype(np.float32)
+    g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
+    with pytest.raises(PiError):
+        moe.MoeLayer(router, g, u, dn, 8, d, f, E, k)
