@@ -5,7 +5,7 @@
  * The entry points replace, one for one, the reference's Rust operator
  * functions on this path (citations: file:line in the reference project).
  * The Rust side keeps its `quant`, `moe` and `predictor` signatures and calls
- * these through a thin `extern "C"` block.
+ * these through a thin `extern "C"` block on the Rust side.
  *
  * Conventions
  *   - Every function returns an int status: PI_OK (0) or one of PI_ERR_*.
@@ -114,7 +114,9 @@ int pi_matvec_col_major(pi_ctx* ctx, float* y, const float* x, const void* raw, 
  * device; its first call on a device looks up the array's address
  * (cudaGetSymbolAddress), so make that first call before any stream capture.
  * All calls share the one array: calls that overlap on the GPU (other streams
- * or threads) race and must be serialised by the caller. Returns PI_OK,
+ * or threads) race and must be serialised by the caller. The looked-up address
+ * is kept per device ordinal for the life of the process, so the entry point
+ * must not be used after a cudaDeviceReset of that device. Returns PI_OK,
  * PI_ERR_ARG or PI_ERR_CUDA (no error string: there is no context). */
 int pi_matvec_col_major_q8_0_noalloc(float* y, const float* x, const void* raw, int64_t n_in, int64_t n_out,
                                      void* stream);
@@ -142,7 +144,7 @@ int pi_ffn_swiglu_q_selected(pi_ctx* ctx, float* out, const float* x, const void
 /* ---- MoE layer (weights repacked once into an HBM-resident layout) ----- */
 
 typedef struct pi_moe_layer_desc {
-    int64_t n_embd;         /* d                                                   */
+    int64_t n_embd;         /* d: Q8_0 1024 or 2048; Q4_0 1024, 2048 or 4096         */
     int64_t n_ff_exp;       /* expert SwiGLU width f: 128, 256, 512 or 1024         */
     int64_t n_ff_shexp;     /* shared-expert width; the reference uses n_ff_exp    */
     int32_t n_expert;       /* E                                                   */

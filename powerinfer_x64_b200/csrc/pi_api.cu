@@ -5,6 +5,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <map>
 
 int pi_set_error(pi_ctx* ctx, int code, const std::string& msg) {
     if (ctx) {
@@ -18,6 +19,22 @@ int pi_cuda_check(pi_ctx* ctx, cudaError_t e, const char* what) {
     if (e == cudaSuccess) return PI_OK;
     std::string m = std::string(what) + ": " + cudaGetErrorString(e);
     return pi_set_error(ctx, e == cudaErrorMemoryAllocation ? PI_ERR_OOM : PI_ERR_CUDA, m);
+}
+
+// The dynamic shared-memory limit is an attribute of a kernel on one device, so
+// it is raised once per (kernel, current device) and again whenever a launch
+// needs more than was set; the record is shared by every thread of the process.
+void pi_smem_attr(const void* fn, size_t bytes) {
+    if (bytes <= 48 * 1024) return;
+    static std::mutex mu;
+    static std::map<std::pair<const void*, int>, size_t> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> g(mu);
+    size_t& have = done[{fn, dev}];
+    if (have >= bytes) return;
+    if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) == cudaSuccess) have = bytes;
+    else cudaGetLastError();  // the launch that follows reports the failure
 }
 
 int pi_scratch(pi_ctx* ctx, cudaStream_t stream, size_t bytes, char** out) {
@@ -190,6 +207,13 @@ static int layer_create(pi_ctx* ctx, const pi_moe_layer_desc* D, int e_first, in
         return pi_set_error(ctx, PI_ERR_ARG, "moe layer: missing router or expert tensors");
     if (D->n_ff_exp != 128 && D->n_ff_exp != 256 && D->n_ff_exp != 512 && D->n_ff_exp != 1024)
         return pi_set_error(ctx, PI_ERR_ARG, "moe layer: expert width must be 128, 256, 512 or 1024");
+    // the decode kernels are instantiated for these widths (Q8_0 gate/up by n_embd / 512,
+    // Q4_0 by n_embd / 1024): any other n_embd would sum only part of each row
+    if (D->qtype == PI_QT_Q8_0 ? (D->n_embd != 1024 && D->n_embd != 2048)
+                               : (D->n_embd != 1024 && D->n_embd != 2048 && D->n_embd != 4096))
+        return pi_set_error(ctx, PI_ERR_ARG,
+                            D->qtype == PI_QT_Q8_0 ? "moe layer: Q8_0 n_embd must be 1024 or 2048"
+                                                   : "moe layer: Q4_0 n_embd must be 1024, 2048 or 4096");
     const bool has_sh = D->gate_shexp && D->up_shexp && D->down_shexp;
     const int64_t f_sh = D->n_ff_shexp ? D->n_ff_shexp : D->n_ff_exp;
     if (has_sh && f_sh != D->n_ff_exp)

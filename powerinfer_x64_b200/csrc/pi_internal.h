@@ -131,6 +131,9 @@ struct PiProfScope {
     ~PiProfScope();
 };
 int pi_cuda_check(pi_ctx* ctx, cudaError_t e, const char* what);
+// Raises fn's dynamic shared-memory limit to `bytes` on the current device (once per
+// kernel and device; no-op at or below the 48 KB default).
+void pi_smem_attr(const void* fn, size_t bytes);
 // Returns scratch of at least `bytes` for `stream` (allocating if needed).
 int pi_scratch(pi_ctx* ctx, cudaStream_t stream, size_t bytes, char** out);
 

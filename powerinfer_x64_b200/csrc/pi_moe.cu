@@ -1851,12 +1851,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
         switch (d / 512) {
 #define GU_Q8(C)                                                                                              \
     case C: {                                                                                                 \
-        static bool attr = false;                                                                             \
-        if (!attr) {                                                                                          \
-            cudaFuncSetAttribute(k_gateup_q8<C>, cudaFuncAttributeMaxDynamicSharedMemorySize,                 \
-                                 (int)gateup_q8_smem<C>());                                                   \
-            attr = true;                                                                                      \
-        }                                                                                                     \
+        pi_smem_attr((const void*)k_gateup_q8<C>, gateup_q8_smem<C>());                                       \
         k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
         break;                                                                                                \
     }
@@ -1874,13 +1869,9 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
         PiProfScope ps(ctx, st, "k_down");
         const int cpq = L->f % 64 ? 0 : (int)(L->f / 64);  // 16-byte chunks per quarter row
         if (cpq == 2 || cpq == 4 || cpq == 8) {  // streamed down: persistent CTAs fed by bulk copies
-            static bool ds_attr = false;
-            if (!ds_attr) {
-                cudaFuncSetAttribute(k_down_q8s<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<2>::SMEM);
-                cudaFuncSetAttribute(k_down_q8s<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<4>::SMEM);
-                cudaFuncSetAttribute(k_down_q8s<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)DSL<8>::SMEM);
-                ds_attr = true;
-            }
+            pi_smem_attr((const void*)k_down_q8s<2>, DSL<2>::SMEM);
+            pi_smem_attr((const void*)k_down_q8s<4>, DSL<4>::SMEM);
+            pi_smem_attr((const void*)k_down_q8s<8>, DSL<8>::SMEM);
             const unsigned g = (unsigned)std::min<int64_t>((int64_t)ni * (L->d / DS_ROWS), ctx->sm_count);
             switch (cpq) {
                 case 2: k_down_q8s<2><<<g, DS_THREADS, DSL<2>::SMEM, st>>>(a, ctx->dev_err); break;
@@ -1889,11 +1880,8 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
             }
             return pi_cuda_check(ctx, cudaGetLastError(), "experts") ? PI_ERR_CUDA : PI_OK;
         }
-        static bool dn_attr = false;
-        if (!dn_attr) {  // CPQ = 16: term buffer + staged h above the default 48 KB
-            cudaFuncSetAttribute(k_down_q8<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dn_smem(16));
-            dn_attr = true;
-        }
+        // CPQ = 16: term buffer + staged h above the default 48 KB
+        pi_smem_attr((const void*)k_down_q8<16>, dn_smem(16));
         if (cpq != 16)  // widths 128, 256, 512 took the streamed kernel above
             return pi_set_error(ctx, PI_ERR_ARG, "Q8_0 layer: expert width must be 128, 256, 512 or 1024");
         k_down_q8<16><<<dn, 256, dn_smem(16), st>>>(a);
@@ -2012,11 +2000,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         {
             PiProfScope ps(ctx, st, "k_router_exact");
             dim3 eg((unsigned)((E + 1 + 31) / 32), (unsigned)std::min<int64_t>(T, 64));
-            static bool ex_attr = false;
-            if (!ex_attr) {
-                cudaFuncSetAttribute(k_router_exact_list, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)EX_SMEM);
-                ex_attr = true;
-            }
+            pi_smem_attr((const void*)k_router_exact_list, EX_SMEM);
             k_router_exact_list<<<eg, EX_THREADS, EX_SMEM, st>>>(xin, L->router, L->bias, d, E, B.flag_list, B.n_flag,
                                                                  B.logits);
             launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 16), st, B.logits, (int)T, E, k, L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
@@ -2045,12 +2029,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
                 dim3 rg((unsigned)((E + 1 + 15) / 16), (unsigned)((T + 7) / 8));
 #define RD16(N)                                                                                               \
     {                                                                                                         \
-        static bool attr = false;                                                                             \
-        if (!attr) {                                                                                          \
-            cudaFuncSetAttribute(k_router_dec<16, 8, N, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,   \
-                                 (int)rd_smem<16, 8>(2048));                                                  \
-            attr = true;                                                                                      \
-        }                                                                                                     \
+        pi_smem_attr((const void*)k_router_dec<16, 8, N, true>, rd_smem<16, 8>(2048));                        \
         k_router_dec<16, 8, N, true><<<rg, 128, rd_smem<16, 8>(d), st>>>(xin, L->router, L->bias, (int)T, d, \
                                                                          E, B.logits, k, hs, idx, gates,      \
                                                                          B.shscale, counts, tickets, fuse,    \
@@ -2062,12 +2041,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
                     launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
                                 B.logits, (int)T, E, k, hs, idx, gates, B.shscale, counts, nullptr, nullptr);
             } else {
-                static bool attr = false;
-                if (!attr) {
-                    cudaFuncSetAttribute(k_router_dec<8, 4, 16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)rd_smem<8, 4>(4096));
-                    attr = true;
-                }
+                pi_smem_attr((const void*)k_router_dec<8, 4, 16, false>, rd_smem<8, 4>(4096));
                 dim3 rg((unsigned)((E + 1 + 7) / 8), (unsigned)((T + 3) / 4));
                 k_router_dec<8, 4, 16, false><<<rg, 32, rd_smem<8, 4>(d), st>>>(
                     xin, L->router, L->bias, (int)T, d, E, B.logits, k, hs, idx, gates, B.shscale, counts, tickets, 0,

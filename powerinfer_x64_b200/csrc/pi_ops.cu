@@ -723,8 +723,7 @@ static int run_rows(pi_ctx* ctx, float* y, const float* x, const void* raw, int 
         k_quant_act<<<nblocks(n_in, 256), 256, 0, st>>>(x, n_in, xq, xs);
         const size_t smem = (size_t)8 * (n_in / 32) * 4;
         if (smem > 200 * 1024) return pi_set_error(ctx, PI_ERR_ARG, "matvec: n_in too large");
-        if (smem > 48 * 1024)
-            cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        pi_smem_attr((const void*)k_rows_q8, smem);
         k_rows_q8<<<nblocks(n_rows, 8), 256, smem, st>>>(y, xq, xs, (const uint8_t*)raw, n_in, n_out, idx, n_rows,
                                                          ctx->dev_err);
     } else {
@@ -792,7 +791,7 @@ static int ffn_core(pi_ctx* ctx, float* out, const float* x, const void* g, cons
         float* xs = b.take<float>(n_embd / 32);
         k_quant_act<<<nblocks(n_embd, 256), 256, 0, st>>>(x, n_embd, xq, xs);
         const size_t smem = (size_t)8 * (n_embd / 32) * 4;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        pi_smem_attr((const void*)k_rows_q8, smem);
         k_rows_q8<<<nblocks(n_sel, 8), 256, smem, st>>>(gv, xq, xs, (const uint8_t*)g, n_embd, n_ff, idx, n_sel,
                                                         ctx->dev_err);
         k_rows_q8<<<nblocks(n_sel, 8), 256, smem, st>>>(uv, xq, xs, (const uint8_t*)u, n_embd, n_ff, idx, n_sel,
@@ -813,7 +812,7 @@ static int ffn_core(pi_ctx* ctx, float* out, const float* x, const void* g, cons
         float* hs = b.take<float>(n_ff / 32);
         k_quant_act<<<nblocks(n_ff, 256), 256, 0, st>>>(gv, n_ff, hq, hs);
         const size_t smem = (size_t)8 * (n_ff / 32) * 4;
-        if (smem > 48 * 1024) cudaFuncSetAttribute(k_rows_q8, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        pi_smem_attr((const void*)k_rows_q8, smem);
         k_rows_q8<<<nblocks(n_embd, 8), 256, smem, st>>>(out, hq, hs, (const uint8_t*)dn, n_ff, n_embd, nullptr,
                                                          n_embd, ctx->dev_err);
     } else {
@@ -927,11 +926,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
     }
     const int plan_smem = (int)n_ff;
-    static bool plan_attr = false;
-    if (!plan_attr) {
-        cudaFuncSetAttribute(k_sf_plan, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)SF_MAX_FF);
-        plan_attr = true;
-    }
+    pi_smem_attr((const void*)k_sf_plan, SF_MAX_FF);
     for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
         {

@@ -522,12 +522,8 @@ int pi_prefill_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, 
     CUtensorMap mhh, mhl;
     if (!act_map(&mhh, hh, n_slots, a.f) || !act_map(&mhl, hl, n_slots, a.f))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill GEMM: cuTensorMapEncodeTiled failed");
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_moe_gemm<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<0>());
-        cudaFuncSetAttribute(k_moe_gemm<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gemm_smem<1>());
-        attr = true;
-    }
+    pi_smem_attr((const void*)k_moe_gemm<0>, gemm_smem<0>());
+    pi_smem_attr((const void*)k_moe_gemm<1>, gemm_smem<1>());
     {
         PiProfScope ps(ctx, st, "k_gemm_gateup");
         k_moe_gemm<0><<<dim3((unsigned)(a.f / (MT * GU_MPC)), (unsigned)max_items), GT, gemm_smem<0>(), st>>>(
@@ -553,11 +549,7 @@ int pi_router_logits_tc(pi_ctx* ctx, const pi_moe_layer* L, const __half* xh, co
     if (!kmajor_map(&mxh, xh, T, L->d, MT) || !kmajor_map(&mxl, xl, T, L->d, MT))
         return pi_set_error(ctx, PI_ERR_CUDA, "router: cuTensorMapEncodeTiled failed");
     const size_t smem = (size_t)RG * 2 * (MT + nr) * 64 + 1024;
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_router_gemm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)(RG * 2 * (MT + 256) * 64 + 1024));
-        attr = true;
-    }
+    pi_smem_attr((const void*)k_router_gemm, RG * 2 * (MT + 256) * 64 + 1024);
     PiProfScope ps(ctx, st, "k_router_gemm");
     k_router_gemm<<<dim3((unsigned)((T + MT - 1) / MT), (unsigned)(L->E / nr)), 192, smem, st>>>(
         mxh, mxl, L->rmap_h, L->rmap_l, (int)T, (int)L->d, L->E, nr, ldexpf(1.0f, -L->router_rs), L->bias, logits,

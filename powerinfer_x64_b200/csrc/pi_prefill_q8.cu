@@ -424,12 +424,8 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     CUtensorMap mxg, mhq;
     if (!q8_act_map(&mxg, a.xq, T, a.d, 1) || !q8_act_map(&mhq, a.hq, n_slots, a.f, 128))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
-    static bool attr = false;
-    if (!attr) {
-        cudaFuncSetAttribute(k_moe_gemm_q8<0>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
-        cudaFuncSetAttribute(k_moe_gemm_q8<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)QSMEM);
-        attr = true;
-    }
+    pi_smem_attr((const void*)k_moe_gemm_q8<0>, QSMEM);
+    pi_smem_attr((const void*)k_moe_gemm_q8<1>, QSMEM);
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
         k_moe_gemm_q8<0><<<dim3((unsigned)(a.f / 64), (unsigned)max_items), QT, QSMEM, st>>>(a, L->maps, mxg,

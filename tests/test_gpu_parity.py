@@ -521,3 +521,19 @@ def test_layer_rejects_unsupported_expert_width(pkg, orc, torch):
     g, u, dn = (orc.quantize_q8_0((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
     with pytest.raises(PiError):
         moe.MoeLayer(router, g, u, dn, 8, d, f, E, k)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("qt,d", [(8, 1152), (8, 4096), (2, 1152), (2, 1536)])
+def test_layer_rejects_unsupported_n_embd(pkg, orc, torch, qt, d):
+    """n_embd outside the widths the decode kernels are built for (Q8_0: 1024, 2048;
+    Q4_0: 1024, 2048, 4096) is refused when the layer is built, not summed in part."""
+    from powerinfer_x64_b200 import PiError, moe
+
+    rng = np.random.default_rng(4)
+    E, k, f = 4, 2, 256
+    router = (rng.standard_normal(E * d) * 0.02).astype(np.float32)
+    qz = orc.quantize_q8_0 if qt == 8 else orc.quantize_q4_0
+    g, u, dn = (qz((rng.standard_normal(E * f * d) * 0.02).astype(np.float32)) for _ in range(3))
+    with pytest.raises(PiError):
+        moe.MoeLayer(router, g, u, dn, qt, d, f, E, k)
