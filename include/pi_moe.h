@@ -181,6 +181,14 @@ int pi_moe_route(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, in
 int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, float* out, int32_t flags,
                    void* stream);
 
+/* pi_moe_forward that also returns the routing the forward used (after the
+ * optional RMSNorm): idx/gates [T][k], counts/offsets [E], perm [T*k], as
+ * pi_moe_route documents; any of them may be NULL. Same reference lines as
+ * pi_moe_forward (model/mod.rs:1239-1633); the reference has no separate
+ * call, its routing lives inside the token loop (:1254-1312). */
+int pi_moe_forward_routed(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, float* out, int32_t flags,
+                          int32_t* idx, float* gates, int32_t* counts, int32_t* offsets, int32_t* perm, void* stream);
+
 /* ---- Expert parallelism (config 5: experts sharded over the GPUs of a box) ----
  * No reference counterpart: the reference runs the whole layer in one process
  * (model/mod.rs:1245-1571). These calls split pi_moe_forward into the stages

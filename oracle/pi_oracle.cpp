@@ -32,6 +32,7 @@
 #include <thread>
 #include <algorithm>
 #include <numeric>
+#include <mutex>
 #include <smmintrin.h>
 #include <pmmintrin.h>
 
@@ -529,10 +530,31 @@ static void route_one(const float* x, const uint8_t* router, const float* bias, 
     }
 }
 
-void or_moe_route(const float* x, int64_t T, const uint8_t* router, const float* bias, int64_t d, int E, int k,
-                  float* logits, int32_t* idx, float* gates, int32_t* counts, int32_t* offsets, int32_t* perm) {
-    for (int64_t t = 0; t < T; ++t)
-        route_one(x + t * d, router, bias, d, E, k, logits ? logits + t * E : nullptr, idx + t * k, gates + t * k);
+// Runs fn(t0, t1) over token ranges on `threads` host threads (0 = all cores).
+// Tokens are independent in the reference's loop (model/mod.rs:1234), so the
+// split changes no result; it only lets the checker keep up with GPU-sized batches.
+}  // extern "C"
+template <typename F>
+static void over_tokens(int64_t T, int threads, F fn) {
+    int n = threads > 0 ? threads : (int)std::max(1u, std::thread::hardware_concurrency());
+    if (n <= 1 || T < 2) { fn(0, T); return; }
+    n = (int)std::min<int64_t>(n, T);
+    std::vector<std::thread> pool;
+    for (int i = 0; i < n; ++i) {
+        const int64_t t0 = T * i / n, t1 = T * (i + 1) / n;
+        pool.emplace_back([=] { fn(t0, t1); });
+    }
+    for (auto& th : pool) th.join();
+}
+extern "C" {
+
+void or_moe_route_mt(const float* x, int64_t T, const uint8_t* router, const float* bias, int64_t d, int E, int k,
+                     float* logits, int32_t* idx, float* gates, int32_t* counts, int32_t* offsets, int32_t* perm,
+                     int threads) {
+    over_tokens(T, threads, [&](int64_t t0, int64_t t1) {
+        for (int64_t t = t0; t < t1; ++t)
+            route_one(x + t * d, router, bias, d, E, k, logits ? logits + t * E : nullptr, idx + t * k, gates + t * k);
+    });
     if (!counts) return;
     for (int e = 0; e < E; ++e) counts[e] = 0;
     for (int64_t t = 0; t < T * k; ++t) counts[idx[t]]++;
@@ -542,6 +564,50 @@ void or_moe_route(const float* x, int64_t T, const uint8_t* router, const float*
     std::vector<int32_t> fill(offsets, offsets + E);
     for (int64_t t = 0; t < T; ++t)
         for (int j = 0; j < k; ++j) perm[fill[idx[t * k + j]]++] = (int32_t)t;
+}
+
+void or_moe_route(const float* x, int64_t T, const uint8_t* router, const float* bias, int64_t d, int E, int k,
+                  float* logits, int32_t* idx, float* gates, int32_t* counts, int32_t* offsets, int32_t* perm) {
+    or_moe_route_mt(x, T, router, bias, d, E, k, logits, idx, gates, counts, offsets, perm, 1);
+}
+
+// MoeRouter::route of the standalone operator API (moe/mod.rs:69-108) for T tokens:
+//   logits[j] = sum_i x[i] * gate[i*E + j], sequential in i (ops::matvec_t, ops.rs:251-259);
+//   the top_k largest logits (select_nth_unstable_by leaves equal logits in an
+//   unspecified order: this restatement keeps the lowest index), ordered by
+//   descending logit (a stable sort: equal logits stay in ascending index order);
+//   weights = ops::softmax of the selected logits (ops.rs:160-180: max, v = exp(v - max)
+//   with a sequential sum, then v *= 1/sum).
+// gate: row-major [d][E]; idx/weights: [T][k] in the reference's output order.
+void or_moe_api_route(const float* x, int64_t T, const float* gate, int64_t d, int E, int k, int32_t* idx,
+                      float* weights, int threads) {
+    over_tokens(T, threads, [&](int64_t t0, int64_t t1) {
+        std::vector<float> logits(E);
+        std::vector<int> order(E);
+        for (int64_t t = t0; t < t1; ++t) {
+            const float* xt = x + t * d;
+            for (int j = 0; j < E; ++j) {
+                float sum = 0.0f;
+                for (int64_t i = 0; i < d; ++i) sum += xt[i] * gate[i * E + j];
+                logits[j] = sum;
+            }
+            std::iota(order.begin(), order.end(), 0);
+            std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return logits[a] > logits[b]; });
+            float mx = -INFINITY;
+            for (int j = 0; j < k; ++j) mx = std::fmax(mx, logits[order[j]]);
+            std::vector<float> w(k);
+            float sum = 0.0f;
+            for (int j = 0; j < k; ++j) {
+                w[j] = std::exp(logits[order[j]] - mx);
+                sum += w[j];
+            }
+            const float inv = 1.0f / sum;
+            for (int j = 0; j < k; ++j) {
+                idx[t * k + j] = order[j];
+                weights[t * k + j] = w[j] * inv;
+            }
+        }
+    });
 }
 
 // ---------------------------------------------------------------------------
@@ -626,6 +692,19 @@ int or_moe_layer(const OrMoeLayer* L, const float* x_in, int64_t T, float* out, 
         else std::memcpy(o, ffn.data(), sizeof(float) * d);
     }
     return 0;
+}
+
+// The same layer for a batch of independent tokens spread over host threads
+// (each token runs the single-threaded path, so the outputs equal or_moe_layer's).
+int or_moe_layer_mt(const OrMoeLayer* L, const float* x_in, int64_t T, float* out, int residual, int rmsnorm,
+                    float eps, int threads) {
+    int rc = 0;
+    std::mutex mu;
+    over_tokens(T, threads, [&](int64_t t0, int64_t t1) {
+        int r = or_moe_layer(L, x_in + t0 * L->d, t1 - t0, out + t0 * L->d, 1, residual, rmsnorm, eps);
+        if (r) { std::lock_guard<std::mutex> g(mu); rc = r; }
+    });
+    return rc;
 }
 
 // Hot-neuron sparse dense FFN for a batch of tokens, each with its own

@@ -160,7 +160,8 @@ def ffn_swiglu_q_selected(x, g, u, d, qtype, n_embd, n_ff, idx):
     return out
 
 
-def moe_route(x, router, d, E, k, bias=None):
+def moe_route(x, router, d, E, k, bias=None, threads=0):
+    """Routing of T tokens (model/mod.rs:1254-1312); threads: 0 = all host cores."""
     x = _f32(x).reshape(-1, d)
     T = x.shape[0]
     router, bias = _f32(router), (None if bias is None else _f32(bias))
@@ -170,14 +171,18 @@ def moe_route(x, router, d, E, k, bias=None):
     counts = np.empty(E, np.int32)
     offsets = np.empty(E, np.int32)
     perm = np.empty(T * k, np.int32)
-    lib().or_moe_route(_p(x), C.c_int64(T), _p(router), _p(bias), C.c_int64(d), C.c_int(E), C.c_int(k), _p(logits),
-                       _p(idx), _p(gates), _p(counts), _p(offsets), _p(perm))
+    lib().or_moe_route_mt(_p(x), C.c_int64(T), _p(router), _p(bias), C.c_int64(d), C.c_int(E), C.c_int(k),
+                          _p(logits), _p(idx), _p(gates), _p(counts), _p(offsets), _p(perm), C.c_int(threads))
     return dict(logits=logits, idx=idx, gates=gates, counts=counts, offsets=offsets, perm=perm)
 
 
 def moe_layer(x, d, f, E, k, qtype, router, gate_exps, up_exps, down_exps, shared=None, bias=None, threads=1,
-              residual=False, rmsnorm=False, eps=1e-6):
-    """Full MoE layer on T tokens (one at a time, as the reference)."""
+              residual=False, rmsnorm=False, eps=1e-6, token_threads=None):
+    """Full MoE layer on T tokens (one at a time, as the reference).
+
+    threads: 1 = single thread, 0 = the reference's own threading per token.
+    token_threads: if given, tokens are spread over that many host threads
+    (0 = all cores), each running the single-threaded path (same outputs)."""
     x = _f32(x).reshape(-1, d)
     keep = [_f32(router), _u8(gate_exps), _u8(up_exps), _u8(down_exps)]
     L = OrMoeLayer(d=d, f=f, f_sh=f, E=E, k=k, qtype=qtype)
@@ -194,8 +199,12 @@ def moe_layer(x, d, f, E, k, qtype, router, gate_exps, up_exps, down_exps, share
         if gi is not None:
             L.shared_gate = _p(sh[3])
     out = np.empty_like(x)
-    rc = lib().or_moe_layer(C.byref(L), _p(x), C.c_int64(x.shape[0]), _p(out), C.c_int(threads),
-                            C.c_int(1 if residual else 0), C.c_int(1 if rmsnorm else 0), C.c_float(eps))
+    if token_threads is not None:
+        rc = lib().or_moe_layer_mt(C.byref(L), _p(x), C.c_int64(x.shape[0]), _p(out), C.c_int(1 if residual else 0),
+                                   C.c_int(1 if rmsnorm else 0), C.c_float(eps), C.c_int(token_threads))
+    else:
+        rc = lib().or_moe_layer(C.byref(L), _p(x), C.c_int64(x.shape[0]), _p(out), C.c_int(threads),
+                                C.c_int(1 if residual else 0), C.c_int(1 if rmsnorm else 0), C.c_float(eps))
     if rc:
         raise ValueError(rc)
     return out
@@ -231,3 +240,16 @@ def predictor(a, W1, b1, W2, b2):
     lib().or_predictor(_p(a), _p(W1), _p(b1), _p(W2), _p(b2), C.c_int64(n_in), C.c_int64(n_hidden),
                        C.c_int64(n_out), _p(probs))
     return probs
+
+
+def moe_api_route(x, gate, d, E, k, threads=0):
+    """MoeRouter::route (moe/mod.rs:69-108) for T tokens over a row-major [d, E]
+    gate: (indices [T, k] in descending-logit order, softmax weights [T, k])."""
+    x = _f32(x).reshape(-1, d)
+    T = x.shape[0]
+    g = _f32(gate)
+    idx = np.empty((T, k), np.int32)
+    w = np.empty((T, k), np.float32)
+    lib().or_moe_api_route(_p(x), C.c_int64(T), _p(g), C.c_int64(d), C.c_int(E), C.c_int(k), _p(idx), _p(w),
+                           C.c_int(threads))
+    return idx, w

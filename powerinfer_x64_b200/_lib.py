@@ -63,6 +63,7 @@ SIGNATURES = {
     "pi_moe_layer_destroy": (None, [_P]),
     "pi_moe_route": (_INT, [_P, _P, _P, _I64, _P, _P, _P, _P, _P, _P]),
     "pi_moe_forward": (_INT, [_P, _P, _P, _I64, _P, _I32, _P]),
+    "pi_moe_forward_routed": (_INT, [_P, _P, _P, _I64, _P, _I32, _P, _P, _P, _P, _P, _P]),
     "pi_moe_layer_create_ep": (_INT, [_P, C.POINTER(PiMoeLayerDesc), _I32, _I32, C.POINTER(_P)]),
     "pi_moe_ep_route": (_INT, [_P, _P, _P, _I64, _I32, _I32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "pi_moe_experts_q8": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _P]),

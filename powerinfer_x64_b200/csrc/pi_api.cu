@@ -362,3 +362,10 @@ extern "C" int pi_moe_forward(pi_ctx* ctx, pi_moe_layer* L, const float* x, int6
     if (!out && T > 0) return pi_set_error(ctx, PI_ERR_ARG, "moe: null output");
     return moe_common(ctx, L, x, T, out, flags, nullptr, nullptr, nullptr, nullptr, nullptr, stream);
 }
+
+extern "C" int pi_moe_forward_routed(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* out,
+                                     int32_t flags, int32_t* idx, float* gates, int32_t* counts, int32_t* offsets,
+                                     int32_t* perm, void* stream) {
+    if (!out && T > 0) return pi_set_error(ctx, PI_ERR_ARG, "moe: null output");
+    return moe_common(ctx, L, x, T, out, flags, idx, gates, counts, offsets, perm, stream);
+}

@@ -111,6 +111,31 @@ class MoeLayer:
         self.ctx.check(lib().pi_moe_forward(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, stream_ptr(stream)))
         return out
 
+    def forward_routed(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None,
+                       path: str = "auto"):
+        """``forward`` that also returns the routing it used: (out, dict(idx, gates,
+        counts, offsets, perm)) as ``route`` returns them, computed on the
+        (optionally RMS-normed) tokens the forward itself routed."""
+        torch = _torch()
+        xd = quant._f32(x)
+        T = xd.numel() // self.n_embd
+        E, k = self.n_expert, self.top_k
+        if out is None:
+            out = torch.empty((T, self.n_embd), dtype=torch.float32, device="cuda")
+        o = dict(idx=torch.empty((T, k), dtype=torch.int32, device="cuda"),
+                 gates=torch.empty((T, k), dtype=torch.float32, device="cuda"),
+                 counts=torch.zeros(E, dtype=torch.int32, device="cuda"),
+                 offsets=torch.zeros(E, dtype=torch.int32, device="cuda"),
+                 perm=torch.empty(T * k, dtype=torch.int32, device="cuda"))
+        if T == 0:
+            return out, o
+        flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
+        flags |= {"auto": 0, "gemv": PI_FWD_FORCE_GEMV, "gemm": PI_FWD_FORCE_GEMM}[path]
+        self.ctx.check(lib().pi_moe_forward_routed(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, ptr(o["idx"]),
+                                                   ptr(o["gates"]), ptr(o["counts"]), ptr(o["offsets"]),
+                                                   ptr(o["perm"]), stream_ptr(stream)))
+        return out, o
+
 
 # --------------------------------------------------------------------------
 # src/moe operator API
