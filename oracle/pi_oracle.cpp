@@ -720,6 +720,52 @@ int or_sparse_ffn(const float* x, int64_t T, const uint8_t* gate_raw, const uint
     return 0;
 }
 
+// ---------------------------------------------------------------------------
+// Host generator of the benchmark's synthetic inputs (no reference counterpart:
+// the reference publishes no data for this path). Value i of a stream is a
+// Box-Muller normal from SplitMix64 outputs 2*(i/2) and 2*(i/2)+1
+// (SplitMix64 as model/mod.rs:2041-2061), cos for even i, sin for odd i,
+// scaled by stdv. It lets the CPU legs build their inputs without the GPU
+// library.
+// ---------------------------------------------------------------------------
+static inline uint64_t sm64_at(uint64_t seed, uint64_t j) {
+    uint64_t z = seed + (j + 1) * 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static inline float synth_one(uint64_t seed, uint64_t i, float stdv) {
+    const uint64_t m = i >> 1;
+    const double u1 = 1.0 - (double)(sm64_at(seed, 2 * m) >> 11) * (1.0 / 9007199254740992.0);
+    const double u2 = (double)(sm64_at(seed, 2 * m + 1) >> 11) * (1.0 / 9007199254740992.0);
+    const double r = std::sqrt(-2.0 * std::log(u1));
+    const double th = 6.283185307179586 * u2;
+    const double v = (i & 1) ? r * std::sin(th) : r * std::cos(th);
+    return (float)(v * (double)stdv);
+}
+
+void or_synth_normal(uint64_t seed, uint64_t offset, int64_t n, float stdv, float* out, int threads) {
+    over_tokens(n, threads, [&](int64_t a, int64_t b) {
+        for (int64_t k = a; k < b; ++k) out[k] = synth_one(seed, offset + (uint64_t)k, stdv);
+    });
+}
+
+// n_mats [rows x cols] matrices ~ N(0, stdv) from one stream, quantised with this
+// file's Q8_0 (qtype 8) or Q4_0 (qtype 2) weight quantiser into GGUF bytes.
+void or_synth_quant(uint64_t seed, int64_t n_mats, int64_t rows, int64_t cols, int qtype, float stdv, uint8_t* out,
+                    int threads) {
+    const int64_t n = n_mats * rows * cols, nblk = n / 32, bb = qtype == QT_Q8_0 ? 34 : 18;
+    over_tokens(nblk, threads, [&](int64_t b0, int64_t b1) {
+        float buf[32];
+        for (int64_t b = b0; b < b1; ++b) {
+            for (int i = 0; i < 32; ++i) buf[i] = synth_one(seed, (uint64_t)(b * 32 + i), stdv);
+            if (qtype == QT_Q8_0) or_quantize_q8_0(buf, 32, out + b * bb);
+            else or_quantize_q4_0(buf, 32, out + b * bb);
+        }
+    });
+}
+
 // Predictor::predict / predict_hot: predictor/mod.rs:63-95 (ndarray dot is
 // a sequential sum per output row here). W1 [hidden x in], W2 [out x hidden].
 void or_predictor(const float* a, const float* W1, const float* b1, const float* W2, const float* b2, int64_t n_in,

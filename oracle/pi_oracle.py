@@ -253,3 +253,63 @@ def moe_api_route(x, gate, d, E, k, threads=0):
     lib().or_moe_api_route(_p(x), C.c_int64(T), _p(g), C.c_int64(d), C.c_int(E), C.c_int(k), _p(idx), _p(w),
                            C.c_int(threads))
     return idx, w
+
+
+# ---------------------------------------------------------------------------
+# Host-side synthetic inputs (the benchmark's seeded generator, restated so the
+# CPU legs never load the GPU library): one SplitMix64 stream per tensor, stream
+# seed = SplitMix64 output `tensor id` of (config seed + 7919 * layer).
+# ---------------------------------------------------------------------------
+_GAMMA = np.uint64(0x9E3779B97F4A7C15)
+TENSOR_IDS = dict(router=1, gate_exps=2, up_exps=3, down_exps=4, gate_shexp=5, up_shexp=6, down_shexp=7,
+                  gate_inp_shexp=8, x=9, bias=10, mask=11)
+
+
+def splitmix_at(seed: int, j):
+    with np.errstate(over="ignore"):
+        j = np.asarray(j, dtype=np.uint64)
+        z = np.uint64(seed) + (j + np.uint64(1)) * _GAMMA
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+        return z ^ (z >> np.uint64(31))
+
+
+def stream_seed(seed: int, name: str, layer: int = 0) -> int:
+    return int(splitmix_at(seed + 7919 * layer, TENSOR_IDS[name]))
+
+
+def synth_normal(seed: int, n: int, std: float, offset: int = 0, threads: int = 0) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    lib().or_synth_normal(C.c_uint64(seed), C.c_uint64(offset), C.c_int64(n), C.c_float(std), _p(out),
+                          C.c_int(threads))
+    return out
+
+
+def synth_quant(seed: int, n_mats: int, rows: int, cols: int, qtype: int, std: float = 0.02,
+                threads: int = 0) -> np.ndarray:
+    out = np.empty(n_mats * rows * cols // 32 * (34 if qtype == QT_Q8_0 else 18), np.uint8)
+    lib().or_synth_quant(C.c_uint64(seed), C.c_int64(n_mats), C.c_int64(rows), C.c_int64(cols), C.c_int(qtype),
+                         C.c_float(std), _p(out), C.c_int(threads))
+    return out
+
+
+def zipf_bias(seed: int, E: int) -> np.ndarray:
+    keys = splitmix_at(stream_seed(seed, "bias"), np.arange(E))
+    rank = np.empty(E, np.int64)
+    rank[np.argsort(keys, kind="stable")] = np.arange(E)
+    return (2.0 * np.log(1.0 / (rank + 1.0))).astype(np.float32)
+
+
+def moe_tensors_host(d, E, f, qtype, shared, zipf=False, seed=0, layer=0):
+    """Host GGUF tensors of one synthetic MoE layer: the same streams the GPU
+    generator draws for (seed, layer)."""
+    s = lambda n: stream_seed(seed, n, layer)
+    t = dict(router=synth_normal(s("router"), E * d, 0.02),
+             gate_exps=synth_quant(s("gate_exps"), E, f, d, qtype),
+             up_exps=synth_quant(s("up_exps"), E, f, d, qtype),
+             down_exps=synth_quant(s("down_exps"), E, d, f, qtype),
+             shared=None, router_bias=zipf_bias(seed, E) if zipf else None)
+    if shared:
+        t["shared"] = (synth_quant(s("gate_shexp"), 1, f, d, qtype), synth_quant(s("up_shexp"), 1, f, d, qtype),
+                       synth_quant(s("down_shexp"), 1, d, f, qtype), synth_normal(s("gate_inp_shexp"), d, 0.02))
+    return t
