@@ -1,22 +1,24 @@
-"""MoE-layer benchmark (BASELINE metric: MoE-layer tokens/s on B200).
+"""MoE-layer benchmark (BASELINE metric: MoE-layer tokens/s on 1/2/4/8 B200).
 
-Workload (N=1 headline): BASELINE config 2, the Qwen3.5-35B-A3B-shaped decode
-MoE layer (d=2048, 256 experts, top-8, expert width 512, shared expert, Q8_0),
-T=64 tokens per step and per GPU. One step = one MoE-layer forward
-(router -> top-k -> dispatch -> expert SwiGLU -> combine) over T tokens. The
-steps cycle through L distinct layers (default 8 x 0.86 GB of weights, far
-larger than the 126 MB L2), so no step reads weights another step left in L2.
+Default workload (every N): BASELINE config 5, one layer of the 40-layer
+Qwen3.5-35B-A3B-shaped Q8_0 stack (d=2048, 256 experts, top-8, expert width
+512, shared expert; RMSNorm before the layer, residual after), T=8192 home
+tokens per GPU, experts sharded over the N ranks (expert parallelism,
+EPMoeLayer; at N=1 one rank holds all 256). One step = one layer forward over
+the rank's T tokens. Steps cycle through L distinct layers (default 8 x 0.86 GB
+of weights at N=1, far larger than the 126 MB L2).
+
+At N=1 the line also carries the config-2 decode sweep (T = 1, 4, 16, 64) and
+its HBM fraction under "decode_c2".
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-
-For N > 1 (torchrun, one process per GPU) every rank runs its own replica on
-its own T tokens (tokens are data-parallel, no collective on the path):
-weak scaling; time = max over ranks of the device-timed region.
+                  [--config c5|c2|c3|c4]
 
 --impl reference times the reference's CPU path on the host: the C++
 restatement in oracle/ (the Rust reference cannot be built in this image),
 with the reference's own threading (2 expert threads + the shared expert on
-the calling thread), on a bounded token sample per step.
+the calling thread), on a bounded token sample per step, with inputs built on
+the host by the oracle's own generator (no GPU library is loaded).
 """
 from __future__ import annotations
 
@@ -43,10 +45,11 @@ def parse():
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", default="ours", choices=["ours", "reference"])
     p.add_argument("--tokens", type=int, default=None, help="tokens per step per GPU (c2: 64, c3: 4096, c5: 8192)")
-    p.add_argument("--config", default="c2", choices=["c2", "c3", "c4", "c5"],
+    p.add_argument("--config", default="c5", choices=["c2", "c3", "c4", "c5"],
                    help="c2: decode Q8_0 (headline); c3: prefill Q4_0 with Zipf-skewed routing; "
                         "c4: hot-neuron sparse FFN (Q4_0, 15%% of 12288 neurons per token); "
-                        "c5: one layer of the Q8_0 stack (RMSNorm + residual), prefill-sized")
+                        "c5 (default): one layer of the Q8_0 stack (RMSNorm + residual), T=8192 per GPU, expert-parallel")
+    p.add_argument("--sample", type=int, default=None, help="reference arm: tokens per step (default 32)")
     p.add_argument("--layers", type=int, default=8, help="distinct layers cycled through")
     p.add_argument("--no-sweep", action="store_true")
     p.add_argument("--no-cpu-baseline", action="store_true")
@@ -130,68 +133,103 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# reference arm / CPU baseline: the oracle's restatement of the reference
+# workload description shared by both arms (the driver compares the configs)
 # ---------------------------------------------------------------------------
-def cpu_layer_tensors(cfg, seed=0, layer=0):
-    """Host copies of one layer's tensors (generated on the GPU when one is present)."""
-    import torch
-
-    from powerinfer_x64_b200 import synth
-
-    if torch.cuda.is_available():
-        t = synth.moe_tensors(cfg, seed, layer)
-        h = lambda a: None if a is None else a.cpu().numpy()
-        out = dict(router=h(t["router"]), gate_exps=h(t["gate_exps"]), up_exps=h(t["up_exps"]),
-                   down_exps=h(t["down_exps"]), shared=tuple(h(a) for a in t["shared"]) if cfg.shared else None)
-        del t
-        torch.cuda.empty_cache()
-        return out
-    raise RuntimeError("the CPU baseline uses GPU-generated inputs")
+CFG = {
+    "c2": dict(name="c2_decode_q8", d=2048, E=256, k=8, f=512, qtype=8, shared=True, zipf=False, T=64, norm=False),
+    "c3": dict(name="c3_prefill_q4", d=2048, E=256, k=8, f=512, qtype=2, shared=True, zipf=True, T=4096, norm=False),
+    "c5": dict(name="c5_stack_q8", d=2048, E=256, k=8, f=512, qtype=8, shared=True, zipf=False, T=8192, norm=True),
+}
 
 
-def run_cpu(cfg, tensors, x, reps):
+def workload_config(cname, T, world, layers):
+    c = CFG[cname]
+    kind = {"c2": "Q8_0 decode", "c3": "Q4_0 prefill, Zipf router bias",
+            "c5": "Q8_0, one layer of the 40-layer stack, RMSNorm before + residual after"}[cname]
+    par = (f"ep{world} (experts sharded {c['E'] // world} per GPU, tokens data-parallel)" if cname == "c5"
+           else f"dp{world} (replicas)")
+    return {"workload": f"{c['name']} (BASELINE config {cname[1]}): d=2048 E=256 k=8 f=512 +shared expert, {kind}",
+            "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": par, "layers_cycled": layers,
+            "l2": f"inputs larger than L2: steps cycle through {layers} layers of "
+                  f"{(0.86 if c['qtype'] == 8 else 0.45):.2f} GB of expert weights each"}
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the oracle's restatement of the reference,
+# inputs built on the host by the oracle's generator (no GPU library loaded)
+# ---------------------------------------------------------------------------
+def _oracle():
     sys.path.insert(0, str(ROOT / "oracle"))
     import pi_oracle as orc
 
+    return orc
+
+
+def host_layer(cname, seed=0, layer=0):
+    c = CFG[cname]
+    return _oracle().moe_tensors_host(c["d"], c["E"], c["f"], c["qtype"], c["shared"], zipf=c["zipf"], seed=seed,
+                                      layer=layer)
+
+
+def host_tokens(cname, n, rank=0, layer=0):
+    """The first n tokens of the GPU arm's token stream of (rank, layer)."""
+    orc = _oracle()
+    d = CFG[cname]["d"]
+    return orc.synth_normal(orc.stream_seed(rank, "x", layer), n * d, 1.0).reshape(n, d)
+
+
+def run_cpu(cname, t, x):
+    """One timed pass of the oracle over the tokens x, reference threading."""
+    orc = _oracle()
+    c = CFG[cname]
     orc.set_threads(0)
+    t0 = time.perf_counter()
+    orc.moe_layer(x, c["d"], c["f"], c["E"], c["k"], c["qtype"], t["router"], t["gate_exps"], t["up_exps"],
+                  t["down_exps"], shared=t["shared"], bias=t["router_bias"], threads=0, residual=c["norm"],
+                  rmsnorm=c["norm"])
+    return time.perf_counter() - t0
+
+
+def cpu_sample(cname, T, sample, steps, warmup):
+    """Times `steps` passes of `sample` tokens each (cycling through the GPU arm's
+    first T tokens of layer 0) after `warmup` untimed passes; returns (times, desc)."""
+    t = host_layer(cname)
+    n = min(T, sample * max(1, steps + warmup))
+    xs = host_tokens(cname, n)
     times = []
-    for _ in range(reps):
-        t0 = time.perf_counter()
-        orc.moe_layer(x, cfg.d, cfg.f, cfg.E, cfg.k, cfg.qtype, tensors["router"], tensors["gate_exps"],
-                      tensors["up_exps"], tensors["down_exps"], shared=tensors["shared"], threads=0)
-        times.append(time.perf_counter() - t0)
-    return times
+    for i in range(warmup + steps):
+        j = (i * sample) % n
+        dt = run_cpu(cname, t, xs[j:j + sample])
+        if i >= warmup:
+            times.append(dt)
+    desc = (f"{sample} tokens per step of layer 0 of the {CFG[cname]['name']} workload (its tokens cycled), "
+            f"reference threading: 2 expert threads + the shared expert on the caller; time scales linearly "
+            f"with tokens (the reference routes and runs each token on its own)")
+    return times, desc
 
 
 def reference_arm(args):
-    import numpy as np
-    import torch
-
-    from powerinfer_x64_b200 import dist, synth
+    from powerinfer_x64_b200 import dist  # pure-Python helpers; loads no GPU library
 
     rank, local, world = dist.env_rank()
     if rank != 0:
         return 0
-    if torch.cuda.is_available():
-        torch.cuda.set_device(local)
-    cfg = synth.C2
-    tensors = cpu_layer_tensors(cfg)
-    sample = args.tokens or 64  # one step = the same 64-token batch the GPU arm processes
-    x = synth.normal_host(synth.stream_seed(0, "x"), sample * cfg.d, 1.0).reshape(sample, cfg.d)
-    run_cpu(cfg, tensors, x, args.warmup)
-    times = run_cpu(cfg, tensors, x, args.steps)
+    cname = args.config if args.config in CFG else "c5"
+    T = args.tokens or CFG[cname]["T"]
+    sample = args.sample or {"c2": 64, "c3": 8, "c5": 32}[cname]
+    times, desc = cpu_sample(cname, T, sample, args.steps, args.warmup)
     tps = sample * len(times) / sum(times)
     line = {
         "impl": "reference", "metric": METRIC, "value": tps, "unit": UNIT, "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * sum(times) / len(times),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": f"{cfg.name} (BASELINE config 2) T={sample}; step = {sample} tokens",
-                   "tokens_per_step": sample},
-        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 3, "kind": "port",
-                         "sample": f"{sample} tokens of one C2 layer per step (the whole step of the workload)",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8" if cname != "c3" else "f32",
+        "data": "synthetic (seeded SplitMix64 + Box-Muller on the host; weights N(0,0.02) -> "
+                + ("Q4_0)" if cname == "c3" else "Q8_0)"),
+        "config": workload_config(cname, T, world, args.layers),
+        "cpu_baseline": {"value": tps, "unit": UNIT, "cores": 3, "kind": "port", "sample": desc,
                          "host_threads_available": os.cpu_count(),
-                         "note": "C++ restatement of the reference CPU path (oracle/); reference threading: "
-                                 "2 expert threads + shared expert on the caller"},
+                         "note": "C++ restatement of the reference CPU path (oracle/); the Rust reference cannot be "
+                                 "built here (no Rust toolchain); the reference's MoE path uses at most 3 threads"},
         "e2e": {"value": tps, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -276,36 +314,103 @@ def main_c4(args):
     return 0
 
 
+
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def load_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except Exception:
+        return {}
+
+
+def time_steps(step, steps, stream):
+    import torch
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        step(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def decode_sweep(args, ctx, dev, peak):
+    """BASELINE config 2 on this GPU: T = 1, 4, 16, 64 tokens per step through
+    layers cycled like the headline; the layer's HBM fraction, and the dominant
+    kernel's (k_gateup) roofline at T = 64."""
+    import torch
+
+    from powerinfer_x64_b200 import synth
+
+    cfg = synth.C2
+    nl = max(args.layers, 4)
+    layers = [synth.moe_layer(cfg, seed=0, layer=li) for li in range(nl)]
+    stream = torch.cuda.current_stream()
+    res = {}
+    for T in (1, 4, 16, 64):
+        xs = [synth.tokens_dev(cfg.d, T, seed=100, layer=li) for li in range(nl)]
+        Us = [int((layers[li].route(xs[li])["counts"] > 0).sum().item()) for li in range(nl)]
+        out = torch.empty((T, cfg.d), dtype=torch.float32, device=dev)
+        step = lambda i: layers[i % nl].forward(xs[i % nl], out=out)
+        for i in range(max(args.warmup, 3)):
+            step(i)
+        torch.cuda.synchronize()
+        n = max(args.steps, 50)
+        ms = time_steps(step, n, stream)
+        byt = sum(layer_bytes(cfg, Us[i % nl], T)["total"] for i in range(n))
+        r = {"tokens_per_s": T * n / (ms / 1e3), "us_per_layer": 1e3 * ms / n,
+             "layer_hbm_gbs": byt / (ms / 1e3) / 1e9, "layer_frac_of_peak": byt / (ms / 1e3) / 1e9 / peak}
+        if T == 64:
+            ctx.profile(True)
+            for i in range(n):
+                step(i)
+            torch.cuda.synchronize()
+            kern = ctx.profile_read()
+            ctx.profile(False)
+            gu_ms, gu_n = kern.get("k_gateup", (float("nan"), 0))
+            b_gu = sum(layer_bytes(cfg, Us[i % nl], T)["gateup"] for i in range(n))
+            ach = b_gu / (gu_ms / 1e3) / 1e9
+            r["k_gateup"] = {"achieved_gbs": ach, "frac": ach / peak, "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1),
+                             "algorithmic_bytes_per_launch": b_gu / max(gu_n, 1)}
+            r["kernels_ms_per_step"] = {k: v[0] / n for k, v in kern.items()}
+        res[f"T{T}"] = r
+    del layers
+    torch.cuda.empty_cache()
+    return res
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         return reference_arm(args)
     if args.config == "c4":
         return main_c4(args)
-    import numpy as np
     import torch
 
     from powerinfer_x64_b200 import Context, dist, synth
+    from powerinfer_x64_b200.pipeline import HostPipeline
 
     rank, local, world = dist.init()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    cfg = {"c2": synth.C2, "c3": synth.C3, "c5": synth.C5}[args.config]
-    T = args.tokens or {"c2": 64, "c3": 4096, "c5": 8192}[args.config]
-    if args.config != "c2":
-        args.no_sweep = True
-    fwd_kw = dict(rmsnorm=True, residual=True) if args.config == "c5" else {}
+    cname = args.config
+    cfg = {"c2": synth.C2, "c3": synth.C3, "c5": synth.C5}[cname]
+    T = args.tokens or CFG[cname]["T"]
+    fwd_kw = dict(rmsnorm=True, residual=True) if cname == "c5" else {}
     ctx = Context.default(local)
+    peaks = load_peaks()
+    peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
 
-    # layers + fixed per-layer tokens (each rank its own seed stream). c5: one model
-    # (same weights on every rank) sharded by experts over the ranks, tokens per rank
+    # layers + fixed per-layer tokens (each rank its own token stream). c5: one model
+    # (the same weights on every rank) sharded by experts over the ranks
     layers, xs, routing = [], [], []
     for li in range(args.layers):
         x = synth.tokens_dev(cfg.d, T, seed=rank, layer=li)
-        if args.config == "c5":
+        if cname == "c5":
             from powerinfer_x64_b200.ep import EPMoeLayer, local_expert_bytes
 
             t = synth.moe_tensors(cfg, seed=0, layer=li)
@@ -317,8 +422,7 @@ def main():
             U = cfg.E
         else:
             L = synth.moe_layer(cfg, seed=rank, layer=li)
-            r = L.route(x)
-            U = int((r["counts"] > 0).sum().item())
+            U = int((L.route(x)["counts"] > 0).sum().item())
         layers.append(L)
         xs.append(x)
         routing.append(U)
@@ -333,19 +437,16 @@ def main():
         step(i)
     torch.cuda.synchronize()
 
-    # ---- timed region (device time with CUDA events, no per-kernel events inside) ----
+    # ---- timed region: device time with CUDA events, no per-kernel events inside ----
     dist.barrier(local)
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        e0.record(stream)
-        for i in range(args.steps):
-            step(i)
-        e1.record(stream)
-        torch.cuda.synchronize()
+        ms = time_steps(step, args.steps, stream)
     dist.barrier(local)
-    ms = e0.elapsed_time(e1)
-    # ---- the same steps again with per-kernel CUDA events (kernel breakdown, roofline) ----
+    ms_max = dist.max_over_ranks(ms, device=dev)
+    value = world * T * args.steps / (ms_max / 1e3)
+
+    # ---- the same steps again with a CUDA-event pair around every launch ----
     ctx.profile(True)
     torch.cuda.synchronize()
     for i in range(args.steps):
@@ -353,144 +454,111 @@ def main():
     torch.cuda.synchronize()
     kern = ctx.profile_read()
     ctx.profile(False)
-    ms_max = dist.max_over_ranks(ms, device=dev)
-    value = world * T * args.steps / (ms_max / 1e3)
-
-    # per-kernel averages, roofline of the dominant kernel (gate/up GEMV)
-    peaks = {}
-    try:
-        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
-    except Exception:
-        pass
-    peak = peaks.get("hbm_gbs", 6650.0)
-    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
-    Us = [routing[i % args.layers] for i in range(args.steps)]
-    b_gu = sum(layer_bytes(cfg, U, T)["gateup"] for U in Us)
-    b_tot = sum(layer_bytes(cfg, U, T)["total"] for U in Us)
-    gu_ms, gu_n = kern.get("k_gateup", (float("nan"), 0))
-    achieved = b_gu / (gu_ms / 1e3) / 1e9 if gu_n else float("nan")
-    traffic = None
-    tf = ROOT / "profiles" / "ncu_traffic.json"
-    if tf.exists():
-        try:
-            traffic = json.loads(tf.read_text()).get("k_gateup_c2_T64_bytes_per_launch")
-        except Exception:
-            traffic = None
     launches = sum(n for (_, n) in kern.values())
-    roofline = {"bound": "hbm", "kernel": "k_gateup", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_source": peak_src, "traffic": traffic,
-                "algorithmic_bytes_per_launch": b_gu / args.steps,
-                "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1)}
-    if args.config == "c3":
-        # prefill: the gate/up GEMM is a dense contraction; FLOPs counted once
-        # (the kernel issues 3 f16 MMAs per product for f32-level accuracy)
+
+    if cname == "c5":
+        # Q8_0 prefill: exact int8 block products on the tensor cores; useful int8
+        # ops of the gate/up GEMM (routed + shared slots of this rank's tokens, which
+        # is also the all-rank average of the slots each rank's experts receive)
+        slots = T * cfg.k + T
+        g_ms, g_n = kern.get("k_gemm_q8_gateup", (float("nan"), 0))
+        ops = 2.0 * slots * 2 * cfg.f * cfg.d
+        ach = ops / (g_ms / args.steps / 1e3) / 1e12
+        ipeak = peaks.get("int8_tops", 4500.0)
+        roofline = {"bound": "tensor", "kernel": "k_gemm_q8_gateup", "achieved": ach, "peak": ipeak,
+                    "unit": "TOPS (int8)", "frac": ach / ipeak,
+                    "peak_source": "measured" if "int8_tops" in peaks else "nominal int8 dense (no measured int8 peak)",
+                    "frac_of_measured_bf16": ach / peaks.get("bf16_tflops", 1590.0), "traffic": None,
+                    "algorithmic_ops_per_step": ops, "avg_launch_us": 1e3 * g_ms / max(g_n, 1),
+                    "launches_per_step": g_n / args.steps}
+        lops = 2.0 * slots * 3 * cfg.f * cfg.d
+        layer_roof = {"useful_int8_tops": lops / (ms_max / args.steps / 1e3) / 1e12,
+                      "frac_of_int8_peak": lops / (ms_max / args.steps / 1e3) / 1e12 / ipeak}
+    elif cname == "c3":
         tpeak = peaks.get("bf16_tflops", 1590.0)
         slots = T * cfg.k + T
         g_ms, g_n = kern.get("k_gemm_gateup", (float("nan"), 0))
         flops = 2.0 * slots * 2 * cfg.f * cfg.d
-        ach_t = flops / (g_ms / max(g_n, 1) / 1e3) / 1e12
-        roofline = {"bound": "tensor", "kernel": "k_gemm_gateup", "achieved": ach_t, "peak": tpeak, "unit": "TFLOP/s",
-                    "frac": ach_t / tpeak, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
-                    "traffic": None, "algorithmic_flops_per_launch": flops,
-                    "mma_issued_tflops": 3 * ach_t, "avg_launch_us": 1e3 * g_ms / max(g_n, 1)}
-    if args.config == "c5":
-        # Q8_0 prefill: exact int8 block products (f16 MMAs of the int8 values, one per
-        # product), judged against the int8 dense tensor peak (no measured int8 figure
-        # exists for this pool: nominal 4.5 POPS)
-        slots = T * cfg.k + T
-        g_ms, g_n = kern.get("k_gemm_q8_gateup", (float("nan"), 0))
-        ops = 2.0 * slots * 2 * cfg.f * cfg.d
-        ach_t = ops / (g_ms / args.steps / 1e3) / 1e12  # routed + shared launches of a step
-        roofline = {"bound": "tensor", "kernel": "k_gemm_q8_gateup", "achieved": ach_t, "peak": 4500.0,
-                    "unit": "TOPS (int8)", "frac": ach_t / 4500.0, "peak_source": "nominal int8 dense (no measured int8 peak)",
-                    "frac_of_measured_bf16": ach_t / peaks.get("bf16_tflops", 1590.0), "traffic": None,
-                    "algorithmic_ops_per_step": ops, "avg_launch_us": 1e3 * g_ms / max(g_n, 1),
-                    "launches_per_step": g_n / args.steps}
+        ach = flops / (g_ms / max(g_n, 1) / 1e3) / 1e12
+        roofline = {"bound": "tensor", "kernel": "k_gemm_gateup", "achieved": ach, "peak": tpeak, "unit": "TFLOP/s",
+                    "frac": ach / tpeak, "peak_source": "measured" if "bf16_tflops" in peaks else "fallback",
+                    "traffic": None, "algorithmic_flops_per_launch": flops, "mma_issued_tflops": 3 * ach,
+                    "avg_launch_us": 1e3 * g_ms / max(g_n, 1)}
+        layer_roof = None
+    else:
+        Us = [routing[i % args.layers] for i in range(args.steps)]
+        b_gu = sum(layer_bytes(cfg, U, T)["gateup"] for U in Us)
+        b_tot = sum(layer_bytes(cfg, U, T)["total"] for U in Us)
+        gu_ms, gu_n = kern.get("k_gateup", (float("nan"), 0))
+        ach = b_gu / (gu_ms / 1e3) / 1e9 if gu_n else float("nan")
+        traffic = None
+        tf = ROOT / "profiles" / "ncu_traffic.json"
+        if tf.exists():
+            try:
+                traffic = json.loads(tf.read_text()).get("k_gateup_c2_T64_bytes_per_launch")
+            except Exception:
+                traffic = None
+        roofline = {"bound": "hbm", "kernel": "k_gateup", "achieved": ach, "peak": peak, "unit": "GB/s",
+                    "frac": ach / peak, "peak_source": peak_src, "traffic": traffic,
+                    "algorithmic_bytes_per_launch": b_gu / args.steps, "avg_launch_us": 1e3 * gu_ms / max(gu_n, 1)}
+        layer_roof = {"achieved_gbs": b_tot / (ms_max / 1e3) / 1e9, "frac": b_tot / (ms_max / 1e3) / 1e9 / peak}
 
-    # ---- end to end: host tokens in (pinned), host output back, per step ----
+    # ---- end to end through the public API: pinned host tokens in, host output back,
+    # every step; copies of neighbouring steps overlap compute (HostPipeline) ----
     xh = [x.cpu().pin_memory() for x in xs]
-    oh = torch.empty((T, cfg.d), dtype=torch.float32).pin_memory()
-    xd = torch.empty((T, cfg.d), dtype=torch.float32, device=dev)
+    oh = [torch.empty((T, cfg.d), dtype=torch.float32).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(layers[0], T, cfg.d, **fwd_kw)
 
-    def e2e_step(i):
-        xd.copy_(xh[i % args.layers], non_blocking=True)
-        layers[i % args.layers].forward(xd, out=out, **fwd_kw)
-        oh.copy_(out, non_blocking=True)
+    def e2e_run(i0, n):
+        for i in range(i0, i0 + n):
+            pipe.layer = layers[i % args.layers]
+            pipe.run([xh[i % args.layers]], [oh[i % 2]])
 
-    for i in range(args.warmup):
-        e2e_step(i)
+    e2e_run(0, args.warmup)
+    torch.cuda.synchronize()
     dist.barrier(local)
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i)
+    e2e_run(args.warmup, args.steps)
     f1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = dist.max_over_ranks(f0.elapsed_time(f1), device=dev)
     e2e_val = world * T * args.steps / (e2e_ms / 1e3)
 
-    # ---- decode batch sweep (T in 1, 4, 16, 64) ----
-    sweep = []
-    if not args.no_sweep:
-        for Ts in (1, 4, 16, 64):
-            xs_s = [synth.tokens_dev(cfg.d, Ts, seed=rank + 100, layer=li) for li in range(args.layers)]
-            Us_s = [int((layers[li].route(xs_s[li])["counts"] > 0).sum().item()) for li in range(args.layers)]
-            os_ = torch.empty((Ts, cfg.d), dtype=torch.float32, device=dev)
-            for i in range(args.warmup):
-                layers[i % args.layers].forward(xs_s[i % args.layers], out=os_)
-            torch.cuda.synchronize()
-            g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            g0.record(stream)
-            for i in range(args.steps):
-                layers[i % args.layers].forward(xs_s[i % args.layers], out=os_)
-            g1.record(stream)
-            torch.cuda.synchronize()
-            sm = g0.elapsed_time(g1)
-            byt = sum(layer_bytes(cfg, Us_s[i % args.layers], Ts)["total"] for i in range(args.steps))
-            sweep.append({"T": Ts, "tokens_per_s": Ts * args.steps / (sm / 1e3), "us_per_layer": 1e3 * sm / args.steps,
-                          "layer_hbm_gbs": byt / (sm / 1e3) / 1e9,
-                          "layer_frac_of_peak": byt / (sm / 1e3) / 1e9 / peak})
+    extra = {}
+    if world == 1 and cname == "c5" and not args.no_sweep:
+        extra["decode_c2"] = decode_sweep(args, ctx, dev, peak)
 
-    # ---- CPU baseline (rank 0, N=1): the oracle, reference threading ----
+    # ---- CPU baseline (rank 0, N=1): the oracle, reference threading, host inputs ----
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and args.config == "c2":
-        tensors = cpu_layer_tensors(cfg, seed=0, layer=0)
-        sample = T
-        xsmp = xs[0][:sample].cpu().numpy()
-        run_cpu(cfg, tensors, xsmp, 1)
-        times = run_cpu(cfg, tensors, xsmp, 10)
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        sample = {"c2": 64, "c3": 8, "c5": 64}[cname]
+        times, desc = cpu_sample(cname, T, sample, 5, 1)
         med = statistics.median(times)
-        cpu = {"value": sample / med, "unit": UNIT, "cores": 3, "kind": "port",
-               "sample": f"{sample} tokens of one C2 layer (one full step), median of 10 runs after 1 warm-up",
+        cpu = {"value": sample / med, "unit": UNIT, "cores": 3, "kind": "port", "sample": desc + "; median of 5",
                "host_threads_available": os.cpu_count()}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16x3->f32" if args.config == "c3" else "int8",
-            "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> " + ("Q4_0)" if args.config == "c3" else "Q8_0)"),
-            "config": {"workload": f"{cfg.name} (BASELINE config {args.config[1]}): d=2048 "
-                                   f"E=256 k=8 f=512 +shared, " + {"c2": "Q8_0 decode", "c3": "Q4_0 prefill, Zipf router bias",
-                                                                   "c5": "Q8_0 prefill, one layer of the 40-layer stack, RMSNorm + residual"}[args.config],
-                       "tokens_per_step_per_gpu": T, "global_batch": T * world,
-                       "parallelism": (f"ep{world} (experts sharded {cfg.E // world} per GPU, tokens data-parallel, "
-                                       "NCCL all-to-all-v dispatch/combine)") if args.config == "c5" else f"dp{world} (replicas)",
-                       "layers_cycled": args.layers, "l2": "inputs larger than L2: steps cycle through "
-                       f"{args.layers} layers x {layer_bytes(cfg, 256, T)['total'] / 1e9:.2f} GB"},
+            "vs_baseline": None, "dtype": "f16x3->f32" if cname == "c3" else "int8",
+            "data": "synthetic (seeded SplitMix64 + Box-Muller; weights N(0,0.02) -> "
+                    + ("Q4_0)" if cname == "c3" else "Q8_0)"),
+            "config": workload_config(cname, T, world, args.layers),
             "roofline": roofline,
-            "layer_roofline": {"achieved_gbs": b_tot / (ms_max / 1e3) / 1e9,
-                               "frac": b_tot / (ms_max / 1e3) / 1e9 / peak},
+            "layer_roofline": layer_roof,
             "kernels_ms_per_step": {k: v[0] / args.steps for k, v in kern.items()},
             "kernel_launches_per_step": {k: v[1] / args.steps for k, v in kern.items()},
             "cpu_baseline": cpu,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": T * cfg.d * 4,
-                    "d2h_bytes_per_step": T * cfg.d * 4},
+                    "d2h_bytes_per_step": T * cfg.d * 4, "ms_per_step": e2e_ms / args.steps,
+                    "overlap": "host->device and device->host copies of neighbouring steps overlap compute"},
             "gpu_launches": launches,
             "clocks": clk.summary(),
-            "sweep": sweep,
         }
+        line.update(extra)
         print(json.dumps(line), flush=True)
     return 0
 
