@@ -167,6 +167,11 @@ struct ExpertArgs {
     float* hs;   // Q8_0: [slots][f/32]
     float* hf;   // Q4_0: [slots][f]
     float* y;    // [slots][d]
+    // Q8_0 prefill GEMM: activations in slot order as exact f16 [slots][d] with their
+    // block scales [slots][d/32], and h as exact f16 [slots][f] (scales in hs)
+    __half* xsl;
+    float* xssl;
+    __half* h16;
 };
 
 

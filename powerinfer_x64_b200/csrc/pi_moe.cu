@@ -892,16 +892,21 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
     if (e == E) {  // shared-expert items + total item count
         int n_routed_items = ibase;
         int nsh = has_shared ? (T + tg - 1) / tg : 0;
-        for (int q = threadIdx.x; q < nsh; q += blockDim.x)
-            items[n_routed_items + q] = make_int4(E, T * k + q * tg, min(tg, T - q * tg), 0);
+        for (int q = threadIdx.x; q < nsh; q += blockDim.x) {
+            const int lo = (int)((int64_t)T * q / nsh), hi = (int)((int64_t)T * (q + 1) / nsh);
+            items[n_routed_items + q] = make_int4(E, T * k + lo, hi - lo, 0);
+        }
         if (threadIdx.x == 0) *n_items = n_routed_items + nsh;
         return;
     }
     const int cnt = counts[e];
     if (threadIdx.x == 0 && offsets) offsets[e] = off;
+    // cnt slots in nI items of balanced sizes (each <= tg)
     const int nI = (cnt + tg - 1) / tg;
-    for (int q = threadIdx.x; q < nI; q += blockDim.x)
-        items[ibase + q] = make_int4(e, off + q * tg, min(tg, cnt - q * tg), 0);
+    for (int q = threadIdx.x; q < nI; q += blockDim.x) {
+        const int lo = (int)((int64_t)cnt * q / nI), hi = (int)((int64_t)cnt * (q + 1) / nI);
+        items[ibase + q] = make_int4(e, off + lo, hi - lo, 0);
+    }
     if (cnt == 0) return;
     // slots of expert e in ascending token order: each thread checks DPT consecutive
     // tokens per round, a block scan of the per-thread match counts gives the ranks
@@ -1720,6 +1725,8 @@ struct FwdBufs {
     __half *xh, *xl, *hh, *hl;
     __half *xth, *xtl;  // tensor-core router: tokens split into f16 hi/lo
     float* xnorm;
+    __half *xsl, *h16;  // Q8_0 prefill GEMM: slot-major f16 activations and h
+    float* xssl;
     size_t bytes;
 };
 
@@ -1781,6 +1788,14 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hs = b.take<float>(slots * (F / 32));
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
+    if (use_gemm(L, T, flags) && L->qtype == PI_QT_Q8_0) {
+        f.xsl = b.take<__half>(slots * d);
+        f.xssl = b.take<float>(slots * (d / 32));
+        f.h16 = b.take<__half>(slots * F);
+    } else {
+        f.xsl = f.h16 = nullptr;
+        f.xssl = nullptr;
+    }
     if (use_gemm(L, T, flags) && L->qtype == PI_QT_Q4_0) {
         f.xh = f.xl = nullptr;
         f.hh = b.take<__half>(slots * F);
@@ -1832,6 +1847,9 @@ ExpertArgs expert_args(const pi_moe_layer* L, int E_items, const FwdBufs& B, con
     a.hs = B.hs;
     a.hf = B.hf;
     a.y = B.y;
+    a.xsl = B.xsl;
+    a.xssl = B.xssl;
+    a.h16 = B.h16;
     return a;
 }
 
@@ -2132,6 +2150,11 @@ FwdBufs carve_rows(const pi_moe_layer* L, int64_t n, char* base) {
     f.hs = b.take<float>(slots * (F / 32));
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
+    if (rows_gemm(L, n)) {
+        f.xsl = b.take<__half>(slots * d);
+        f.xssl = b.take<float>(slots * (d / 32));
+        f.h16 = b.take<__half>(slots * F);
+    }
     f.bytes = b.off + 256;
     return f;
 }

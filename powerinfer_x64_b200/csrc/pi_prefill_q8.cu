@@ -4,31 +4,37 @@
 // The reference's Q8_0 matvec (quant/mod.rs:939-957) quantises the activations
 // to Q8_0 and sums, block by block in ascending order,
 //     acc += (float)sumi_b * (d_w,b * d_x,b),   sumi_b = sum_{k in b} q_w q_x,
-// in f32 starting from 0. Here the int8 values of both operands are converted
-// exactly to f16 and multiplied with tcgen05.mma kind::f16: every product and
-// every partial sum of a block is an integer below 2^20, so the f32 result in
-// TMEM is exactly (float)sumi_b. One MMA group per 32-element block writes a
-// fresh accumulator; a stage carries PB = 2 blocks (one handshake for both) into
-// the two column halves of one of DB TMEM buffers; epilogue warps apply each
-// block's scales and add it to f32 registers in block order, so each output is
-// the reference's own sequence of roundings. The gate/up kernel stacks 64 gate
-// rows over the same 64 up rows in one 128-row tile, applies the reference's
-// SwiGLU and quantises h to Q8_0 per 32 rows (a warp's 32 lanes), exactly as
-// the reference's ffn_swiglu_q does before its down matvec (quant/mod.rs:1184-1249);
-// the down kernel writes y.
+// in f32 starting from 0. Here the int8 values of both operands are held as
+// exact f16 and multiplied with tcgen05.mma kind::f16: every product and every
+// partial sum of a block is an integer below 2^20, so the f32 result in TMEM is
+// exactly (float)sumi_b. One MMA pair per 32-element block writes a fresh
+// accumulator; epilogue warps apply each block's scales and add it to f32
+// registers in block order, so each output is the reference's own sequence of
+// roundings. The gate/up kernel applies the reference's SwiGLU and quantises h
+// to Q8_0 per 32 rows, exactly as ffn_swiglu_q does before its down matvec
+// (quant/mod.rs:1184-1249); the down kernel writes y.
 //
-// Data movement (TMA, no multicast) runs in groups of 4 blocks (128 K bytes):
-// weight rows of both lane-tiled layouts as 2-D / 4-D boxes, the gate/up
-// token rows by tile::gather4 from the token-major Q8_0 activations, the down
-// kernel's slot-major h rows as one box.
+// Orientation: the token rows of a work item (<= 128 slots) are the MMA's M
+// side and 128 weight rows its N side, so a TMEM lane is one slot and a thread
+// of the epilogue owns one slot: its activation scale is one register per
+// block, the weight scales are broadcast float4 loads, and a 32-row Q8_0 block
+// of h lies in one thread's registers.
 //
-// Warp roles (QT = 832 threads, one CTA per SM):
-//   0-15  epilogue: warp w owns TMEM lanes 32 (w % 4) .. +31 (weight rows) and
-//         slot columns 32 (w / 4) .. +31;
-//   16-23 converters: thread c < 128 converts weight row c, c >= 128 slot row
-//         c - 128, of each block from the raw group into an f16 tile row
-//         (64-byte swizzled K-major) and publishes the row's block scale;
-//   24    MMA issuer;  25 TMA producer.
+// Operands:
+//   A (slots)   f16 rows [slots][K], slot-major (k_slot_rows writes the gate/up
+//               activations in slot order; the gate/up epilogue writes h so),
+//               loaded by TMA with the 64-byte swizzle the MMA reads;
+//   B (weights) int8 rows of the lane-tiled decode layouts, loaded raw by TMA in
+//               groups of 4 blocks and turned into exact f16 by converter warps.
+//
+// The kernel is persistent: a CTA walks tiles (work item, 128 weight rows) and
+// its pipeline runs on across tile boundaries. Warp roles (QT = 448 threads):
+//   0-7   epilogue: warp w owns slots 32 (w % 4) .. +31 (TMEM lanes) and, for
+//         gate/up, gate columns 32 (w / 4) .. +31 with their up columns (+64),
+//         for down, columns 64 (w / 4) .. +63;
+//   8-11  converters: thread c converts weight row c of each block and
+//         publishes its block scale;
+//   12    MMA issuer;  13 TMA producer.
 // Every mbarrier wait is bounded and reports PI_DEVERR_TIMEOUT.
 #include "pi_tc.cuh"
 // pi_tc.cuh (pi_common.cuh) comes first: it names the quant types that pi_moe.h defines as macros
@@ -37,21 +43,24 @@
 namespace {
 using namespace pitc;
 
-constexpr int QN = PI_GEMM_NT_Q8;  // slots per item (max MMA N)
-constexpr int NEPI = 16, NCONV = 8;
+constexpr int QN = PI_GEMM_NT_Q8;  // slots per work item (MMA M)
+constexpr int TN = 128;            // weight rows per tile (MMA N)
+constexpr int NEPI = 8, NCONV = 4;
 constexpr int QT = (NEPI + NCONV + 2) * 32;
-constexpr int G4 = 4;              // blocks per raw group
-constexpr int RG = 2;              // raw groups in flight
+constexpr int G4 = 4;              // blocks per raw weight group
+constexpr int RG = 3;              // raw weight groups in flight
 constexpr int PB = 2;              // blocks per stage (one handshake)
-constexpr int TS = 4;              // f16 tile stages of PB blocks
-constexpr int DB = 2;              // TMEM buffers of PB x QN columns
-constexpr int SB = 4;              // block-scale buffers (stages)
+constexpr int TS = 4;              // operand stages of PB blocks
+constexpr int DB = 2;              // TMEM buffers of PB x TN columns
+constexpr int SB = 4;              // weight-scale stages
+constexpr int SG = 4;              // activation-scale groups
 constexpr int TILE = 128 * 64;     // 128 rows x 32 f16
-constexpr int STAGE = PB * 2 * TILE;  // {W tile, X tile} per block
-constexpr int RAWW = 128 * G4 * 32;  // weight rows of a group (16 KB)
-constexpr int RAWG = 2 * RAWW;       // + activation rows
+constexpr int STAGE = PB * 2 * TILE;  // {A tile, B tile} per block
+constexpr int RAWW = TN * G4 * 32;    // weight rows of a group (16 KB)
+constexpr int DXG = QN * G4 * 4;      // activation scales of a group (2 KB)
 static_assert(G4 == 2 * PB, "a raw group fills two stages");
-constexpr size_t QSMEM = (size_t)RG * RAWG + (size_t)TS * STAGE + 1024;
+static_assert(QN == 128, "the MMA M side is 128 slots");
+constexpr size_t QSMEM = (size_t)TS * STAGE + (size_t)RG * RAWW + (size_t)SG * DXG + 1024;
 
 // 16 int8 (one 16-byte word) -> 16 exact f16, the 16-byte chunks c0 and c0 + 1 of
 // swizzled row r of a SW64 tile: 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128,
@@ -75,32 +84,61 @@ PI_DEV void int8x16_to_f16(const uint4 a, uint8_t* tile, int r, int c0) {
     }
 }
 
-// MODE 0: gate/up (+ SwiGLU, Q8_0 h); MODE 1: down (y).
+// The Q8_0 activation quantiser (quant/mod.rs:698-736) on 32 values held by one
+// thread: amax -> d = amax/127 -> id = 1/d -> q = clamp(round(x*id)); the stored
+// scale is f16(d). Same arithmetic as warp_quant_q8, without the shuffles.
+PI_DEV float quant_block32(const float (&x)[32], int8_t (&q)[32]) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float a = fabsf(x[i]);
+        amax = (a == a) ? fmaxf(amax, a) : amax;
+    }
+    const float d = fdiv(amax, 127.0f);
+    const float id = (d != 0.0f) ? fdiv(1.0f, d) : 0.0f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float r = roundf(fmul(x[i], id));
+        q[i] = (int8_t)((r != r) ? 0 : (int)fminf(127.0f, fmaxf(-127.0f, r)));
+    }
+    return __half2float(__float2half_rn(d));
+}
+
+struct TileRef {
+    int4 item;
+    int mt;
+};
+
+// MODE 0: gate/up (+ SwiGLU, Q8_0 h as exact f16); MODE 1: down (y).
 template <int MODE>
 __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
-                                                       const __grid_constant__ CUtensorMap mx, uint32_t* err) {
+                                                       const __grid_constant__ CUtensorMap mact,
+                                                       const __grid_constant__ CUtensorMap mscl, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* tiles = sm;              // TS stages of PB x {W tile, X tile}
-    uint8_t* raws = sm + TS * STAGE;  // RG groups of {W rows, X rows}
+    uint8_t* tiles = sm;                      // TS stages of PB x {A tile, B tile}
+    uint8_t* raws = sm + TS * STAGE;          // RG raw weight groups
+    float* s_dx = reinterpret_cast<float*>(raws + RG * RAWW);  // SG groups of [QN slots][G4 blocks]
     __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[SB], scl_free[SB];
-    __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG];
-    __shared__ __align__(16) float s_dw[SB][PB][128];
-    __shared__ __align__(16) float s_dx[SB][PB][QN];
+    __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG], dx_full[SG], dx_free[SG];
+    __shared__ __align__(16) float s_dw[SB][PB][TN];
     __shared__ uint32_t s_tmem;
-    __shared__ int s_row[QN];  // gate/up: token of each slot column; down: slot
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int it = blockIdx.y;
-    if (it >= *a.n_items) return;
-    const int4 item = a.items[it];
-    const bool sh = item.x == a.E;
     const int K = MODE == 0 ? a.d : a.f;
-    const int nb = K / 32, ng = nb / G4, np = nb / PB;
-    const int nn = (item.z + 15) & ~15;
+    const int nb = K / 32, ng = nb / G4;
+    const int MT = MODE == 0 ? a.f / 64 : a.d / TN;  // weight-row tiles per item
+    const int n_tiles = *a.n_items * MT;
+    if ((int)blockIdx.x >= n_tiles) return;
+    auto tile_at = [&](int t) {
+        TileRef r;
+        r.item = a.items[t / MT];
+        r.mt = t % MT;
+        return r;
+    };
 
     if (tid == 0) {
         for (int i = 0; i < TS; ++i) {
-            mbar_init(&tile_full[i], NCONV);
+            mbar_init(&tile_full[i], NCONV + 1);
             mbar_init(&tile_free[i], 1);
         }
         for (int i = 0; i < DB; ++i) {
@@ -115,15 +153,15 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_free[i], NCONV);
         }
+        for (int i = 0; i < SG; ++i) {
+            mbar_init(&dx_full[i], 1);
+            mbar_init(&dx_free[i], NEPI);
+        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    for (int r = tid; r < QN; r += QT) {
-        const int sl = item.y + (r < item.z ? r : 0);
-        s_row[r] = MODE == 1 ? sl : (sl < a.n_routed ? a.perm[sl] : sl - a.n_routed);
     }
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(DB * PB * QN)
+                     "r"(DB * PB * TN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -132,240 +170,287 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     bool ok = true;
-    const int mrow = sh ? 0 : item.x * (MODE == 0 ? a.f : a.d);  // expert's first row in its family
 
     if (warp == NEPI + NCONV + 1) {
-        // ---- TMA producer: group q -> raw slot q % RG once the converters released q - RG ----
-        for (int q = 0; q < ng; ++q) {
-            const int slot = q % RG, use = q / RG;
-            int w_ok = 1;
-            if (lane == 0) {
-                if (use > 0 && !mbar_wait(&raw_free[slot], (use - 1) & 1)) w_ok = 0;
-                else mbar_expect_tx(&raw_full[slot], RAWG);
-            }
-            if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
-            uint8_t* rw = raws + slot * RAWG;
-            uint8_t* rx = rw + RAWW;
-            if (MODE == 0) {
+        // ---- TMA producer: raw weight groups, activation tiles, activation scales ----
+        int g = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const TileRef tr = tile_at(t);
+            const bool sh = tr.item.x == a.E;
+            const int mrow = (sh ? 0 : tr.item.x * (MODE == 0 ? a.f : a.d));
+            for (int q = 0; q < ng; ++q, ++g) {
+                const int slot = g % RG;
+                int w_ok = 1;
                 if (lane == 0) {
-                    // lane-tiled gate/up rows: half h of block B at ((B/32)*64 + h*32 + B%32) * 16 bytes,
-                    // so the first halves of blocks 4q..4q+3 are 64 contiguous bytes, the second ones +512
-                    const int b0 = G4 * q, x0 = ((b0 >> 5) * 64 + (b0 & 31)) * 16;
-                    const int r0 = mrow + blockIdx.x * 64;
-                    const CUtensorMap* mg = sh ? &wm.q[1][0] : &wm.q[0][0];
-                    const CUtensorMap* mu = sh ? &wm.q[1][1] : &wm.q[0][1];
-                    tma_load_2d(rw, mg, x0, r0, &raw_full[slot]);
-                    tma_load_2d(rw + 64 * 64, mg, x0 + 512, r0, &raw_full[slot]);
-                    tma_load_2d(rw + 2 * 64 * 64, mu, x0, r0, &raw_full[slot]);
-                    tma_load_2d(rw + 3 * 64 * 64, mu, x0 + 512, r0, &raw_full[slot]);
+                    if (g >= RG && !mbar_wait(&raw_free[slot], (g / RG - 1) & 1)) w_ok = 0;
+                    else {
+                        mbar_expect_tx(&raw_full[slot], RAWW);
+                        uint8_t* rw = raws + slot * RAWW;
+                        if (MODE == 0) {
+                            // lane-tiled gate/up rows: half h of block B at ((B/32)*64 + h*32 + B%32) * 16
+                            // bytes, so the first halves of blocks 4q..4q+3 are 64 contiguous bytes, the
+                            // second ones +512
+                            const int b0 = G4 * q, x0 = ((b0 >> 5) * 64 + (b0 & 31)) * 16;
+                            const int r0 = mrow + tr.mt * 64;
+                            const CUtensorMap* mg = sh ? &wm.q[1][0] : &wm.q[0][0];
+                            const CUtensorMap* mu = sh ? &wm.q[1][1] : &wm.q[0][1];
+                            tma_load_2d(rw, mg, x0, r0, &raw_full[slot]);
+                            tma_load_2d(rw + 64 * 64, mg, x0 + 512, r0, &raw_full[slot]);
+                            tma_load_2d(rw + 2 * 64 * 64, mu, x0, r0, &raw_full[slot]);
+                            tma_load_2d(rw + 3 * 64 * 64, mu, x0 + 512, r0, &raw_full[slot]);
+                        } else {
+                            // lane-tiled down rows: chunk j of row r at ((r/8)*8*nch + (j%cpq)*32 + (r%8)*4
+                            // + j/cpq) * 16, blocks 4q..4q+3 = chunks 8q..8q+7 = all j%cpq with j/cpq = q
+                            const CUtensorMap* md = sh ? &wm.q[1][2] : &wm.q[0][2];
+                            tma_load_4d(rw, md, q * 16, 0, 0, (mrow + tr.mt * TN) >> 3, &raw_full[slot]);
+                        }
+                    }
+                    for (int pi = 0; pi < G4 / PB && w_ok; ++pi) {
+                        const int s = (G4 / PB) * g + pi, ts = s % TS;
+                        if (s >= TS && !mbar_wait(&tile_free[ts], (s / TS - 1) & 1)) { w_ok = 0; break; }
+                        mbar_expect_tx(&tile_full[ts], PB * TILE);
+                        for (int b = 0; b < PB; ++b)
+                            tma_load_2d(tiles + ts * STAGE + b * 2 * TILE, &mact, (G4 * q + PB * pi + b) * 32,
+                                        tr.item.y, &tile_full[ts]);
+                    }
+                    if (w_ok) {
+                        const int sg = g % SG;
+                        if (g >= SG && !mbar_wait(&dx_free[sg], (g / SG - 1) & 1)) w_ok = 0;
+                        else {
+                            mbar_expect_tx(&dx_full[sg], DXG);
+                            tma_load_2d(s_dx + sg * (DXG / 4), &mscl, G4 * q, tr.item.y, &dx_full[sg]);
+                        }
+                    }
                 }
-                __syncwarp();
-                const int* tk = &s_row[4 * lane];  // 32 lanes x 4 rows = the 128 slot rows
-                tma_gather4(rx + lane * 4 * 128, &mx, q * 128, tk[0], tk[1], tk[2], tk[3], &raw_full[slot]);
-            } else if (lane == 0) {
-                // lane-tiled down rows: chunk j of row r at ((r/8)*8*nch + (j%cpq)*32 + (r%8)*4 + j/cpq) * 16,
-                // blocks 4q..4q+3 = chunks 8q..8q+7 = all j%cpq with j/cpq = q (cpq = 8)
-                const CUtensorMap* md = sh ? &wm.q[1][2] : &wm.q[0][2];
-                tma_load_4d(rw, md, q * 16, 0, 0, (mrow + blockIdx.x * 128) >> 3, &raw_full[slot]);
-                tma_load_2d(rx, &mx, q * 128, item.y, &raw_full[slot]);
+                if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
             }
         }
+        // let the last copies land before the CTA can exit (bounded; only matters after a timeout)
+        if (lane == 0 && g > 0) {
+            mbar_wait(&raw_full[(g - 1) % RG], ((g - 1) / RG) & 1);
+            mbar_wait(&dx_full[(g - 1) % SG], ((g - 1) / SG) & 1);
+        }
     } else if (warp >= NEPI && warp < NEPI + NCONV) {
-        // ---- converters: thread c < 128 converts weight row c, c >= 128 slot row c - 128 ----
-        const int c = tid - NEPI * 32, row = c & 127;
-        const bool isx = c >= 128;
-        // this row's block scales, 4 per group, loaded one group ahead
-        const void* scp;
-        if (!isx) {
+        // ---- converters: thread c converts weight row c of every block of a group ----
+        const int row = tid - NEPI * 32;
+        int g = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const TileRef tr = tile_at(t);
+            const bool sh = tr.item.x == a.E;
+            const int mrow = (sh ? 0 : tr.item.x * (MODE == 0 ? a.f : a.d));
             const __half* wd;
             int wr;
             if (MODE == 0) {
                 const bool up = row >= 64;
                 wd = up ? (sh ? a.usd : a.ud) : (sh ? a.gsd : a.gd);
-                wr = mrow + blockIdx.x * 64 + (row & 63);
+                wr = mrow + tr.mt * 64 + (row & 63);
             } else {
                 wd = sh ? a.dsd : a.dd;
-                wr = mrow + blockIdx.x * 128 + row;
+                wr = mrow + tr.mt * TN + row;
             }
-            scp = wd + (size_t)wr * nb;
-        } else {
-            scp = (MODE == 0 ? a.xs + (size_t)s_row[row] * nb : a.hs + (size_t)s_row[row] * nb);
-        }
-        auto load_sc = [&](int q, float (&v)[G4]) {
-            if (isx) {
-                const float4 f = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(scp) + G4 * q);
-                v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-            } else {
-                const uint2 h = *reinterpret_cast<const uint2*>(reinterpret_cast<const __half*>(scp) + G4 * q);
+            const __half* scp = wd + (size_t)wr * nb;
+            auto load_sc = [&](int q, float (&v)[G4]) {
+                const uint2 h = *reinterpret_cast<const uint2*>(scp + G4 * q);
                 const __half2 h0 = *reinterpret_cast<const __half2*>(&h.x), h1 = *reinterpret_cast<const __half2*>(&h.y);
                 v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
-            }
-        };
-        // raw position of this row's 32 bytes of block i (two 16-byte halves)
-        auto raw_half = [&](const uint8_t* rg, int i, int h) -> const uint8_t* {
-            if (isx) return rg + RAWW + row * 128 + 32 * i + 16 * h;
-            if (MODE == 0) return rg + (row >> 6) * 2 * 64 * 64 + h * 64 * 64 + (row & 63) * 64 + 16 * i;
-            return rg + (row >> 3) * 1024 + (2 * i + h) * 128 + (row & 7) * 16;  // [r/8][chunk][r%8][16 B]
-        };
-        // Chunk j (0..7) of this row's group -> (block i, half h). The order is rotated per row
-        // so that the 32 lanes of a load touch distinct shared-memory banks: activation rows
-        // are 128 bytes apart (chunk 2i + h), gate/up weight rows 64 bytes apart (chunk i of
-        // half h), down weight rows already interleave 8 rows per 128 bytes.
-        auto chunk_of = [&](int j, int& i, int& h) {
-            if (isx) {
-                const int k = (j + row) & 7;
-                i = k >> 1;
-                h = k & 1;
-            } else if (MODE == 0) {
-                i = (j + (row >> 1)) & 3;
-                h = j >> 2;
-            } else {
-                i = j >> 1;
-                h = j & 1;
-            }
-        };
-        float sc_cur[G4], sc_nxt[G4];
-        load_sc(0, sc_cur);
-        for (int q = 0; q < ng && ok; ++q) {
-            const int slot = q % RG;
-            if (q + 1 < ng) load_sc(q + 1, sc_nxt);
-            if (!mbar_wait(&raw_full[slot], (q / RG) & 1)) { ok = false; break; }
-#pragma unroll
-            for (int pi = 0; pi < G4 / PB; ++pi) {  // the group's stages: tiles and scale buffers free
-                const int g = (G4 / PB) * q + pi;
-                if (g >= TS && !mbar_wait(&tile_free[g % TS], (g / TS - 1) & 1)) ok = false;
-                if (g >= SB && !mbar_wait(&scl_free[g % SB], (g / SB - 1) & 1)) ok = false;
-            }
-            if (!ok) break;
-            const uint8_t* rg = raws + slot * RAWG;
-#pragma unroll
-            for (int j = 0; j < 2 * G4; ++j) {
-                int i, h;
-                chunk_of(j, i, h);
-                const int g = (G4 / PB) * q + i / PB;
-                int8x16_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, h)),
-                               tiles + (g % TS) * STAGE + (i % PB) * 2 * TILE + (isx ? TILE : 0), row, 2 * h);
-            }
-#pragma unroll
-            for (int i = 0; i < G4; ++i) {
-                const int sb = ((G4 / PB) * q + i / PB) % SB;
-                (isx ? s_dx[sb][i % PB] : s_dw[sb][i % PB])[row] = sc_cur[i];
-            }
-            fence_async_smem();
-            __syncwarp();
-            if (lane == 0) {
-#pragma unroll
-                for (int pi = 0; pi < G4 / PB; ++pi) {
-                    const int g = (G4 / PB) * q + pi;
-                    mbar_arrive(&tile_full[g % TS]);
-                    mbar_arrive(&scl_full[g % SB]);
+            };
+            // raw position of this row's 16-byte half h of block i
+            auto raw_half = [&](const uint8_t* rg, int i, int h) -> const uint8_t* {
+                if (MODE == 0) return rg + (row >> 6) * 2 * 64 * 64 + h * 64 * 64 + (row & 63) * 64 + 16 * i;
+                return rg + (row >> 3) * 1024 + (2 * i + h) * 128 + (row & 7) * 16;  // [r/8][chunk][r%8][16 B]
+            };
+            // Chunk j (0..7) of this row's group -> (block i, half h), rotated per row so that
+            // the lanes of a load touch distinct shared-memory banks (gate/up rows are 64 bytes
+            // apart; down rows already interleave 8 rows per 128 bytes)
+            auto chunk_of = [&](int j, int& i, int& h) {
+                if (MODE == 0) {
+                    i = (j + (row >> 1)) & 3;
+                    h = j >> 2;
+                } else {
+                    i = j >> 1;
+                    h = j & 1;
                 }
-                mbar_arrive(&raw_free[slot]);
-            }
+            };
+            float sc_cur[G4], sc_nxt[G4];
+            load_sc(0, sc_cur);
+            for (int q = 0; q < ng; ++q, ++g) {
+                const int slot = g % RG;
+                if (q + 1 < ng) load_sc(q + 1, sc_nxt);
+                if (!mbar_wait(&raw_full[slot], (g / RG) & 1)) { ok = false; break; }
 #pragma unroll
-            for (int i = 0; i < G4; ++i) sc_cur[i] = sc_nxt[i];
+                for (int pi = 0; pi < G4 / PB; ++pi) {  // the group's stages: tiles and scale buffers free
+                    const int s = (G4 / PB) * g + pi;
+                    if (s >= TS && !mbar_wait(&tile_free[s % TS], (s / TS - 1) & 1)) ok = false;
+                    if (s >= SB && !mbar_wait(&scl_free[s % SB], (s / SB - 1) & 1)) ok = false;
+                }
+                if (!ok) break;
+                const uint8_t* rg = raws + slot * RAWW;
+#pragma unroll
+                for (int j = 0; j < 2 * G4; ++j) {
+                    int i, h;
+                    chunk_of(j, i, h);
+                    const int s = (G4 / PB) * g + i / PB;
+                    int8x16_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, h)),
+                                   tiles + (s % TS) * STAGE + (i % PB) * 2 * TILE + TILE, row, 2 * h);
+                }
+#pragma unroll
+                for (int i = 0; i < G4; ++i) s_dw[((G4 / PB) * g + i / PB) % SB][i % PB][row] = sc_cur[i];
+                fence_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+#pragma unroll
+                    for (int pi = 0; pi < G4 / PB; ++pi) {
+                        const int s = (G4 / PB) * g + pi;
+                        mbar_arrive(&tile_full[s % TS]);
+                        mbar_arrive(&scl_full[s % SB]);
+                    }
+                    mbar_arrive(&raw_free[slot]);
+                }
+#pragma unroll
+                for (int i = 0; i < G4; ++i) sc_cur[i] = sc_nxt[i];
+            }
         }
     } else if (warp == NEPI + NCONV) {
-        // ---- MMA issuer ----
+        // ---- MMA issuer: per block a fresh accumulator of 128 slots x 128 weight rows ----
         if (lane == 0) {
-            const uint32_t id = idesc(nn);
-            for (int g = 0; g < np; ++g) {
-                const int ts = g % TS, db = g % DB;
-                if (!mbar_wait(&tile_full[ts], (g / TS) & 1) ||
-                    (g >= DB && !mbar_wait(&d_free[db], (g / DB - 1) & 1))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
+            const uint32_t id = idesc(TN);
+            int s = 0;
+            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+                for (int p = 0; p < nb / PB; ++p, ++s) {
+                    const int ts = s % TS, db = s % DB;
+                    if (!mbar_wait(&tile_full[ts], (s / TS) & 1) ||
+                        (s >= DB && !mbar_wait(&d_free[db], (s / DB - 1) & 1))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
 #pragma unroll
-                for (int b = 0; b < PB; ++b) {  // block b -> a fresh accumulator in column half b
-                    const uint8_t* wt = tiles + ts * STAGE + b * 2 * TILE;
-                    const uint32_t dcol = tmem + (db * PB + b) * QN;
-                    mma_f16(dcol, umma_desc(wt, 0), umma_desc(wt + TILE, 0), id, 0u);
-                    mma_f16(dcol, umma_desc(wt, 32), umma_desc(wt + TILE, 32), id, 1u);
+                    for (int b = 0; b < PB; ++b) {
+                        const uint8_t* at = tiles + ts * STAGE + b * 2 * TILE;
+                        const uint32_t dcol = tmem + (db * PB + b) * TN;
+                        mma_f16(dcol, umma_desc(at, 0), umma_desc(at + TILE, 0), id, 0u);
+                        mma_f16(dcol, umma_desc(at, 32), umma_desc(at + TILE, 32), id, 1u);
+                    }
+                    mma_commit(&tile_free[ts]);
+                    mma_commit(&d_full[db]);
                 }
-                mma_commit(&tile_free[ts]);
-                mma_commit(&d_full[db]);
             }
         }
     } else {
-        // ---- epilogue: rows 32 (w % 4) + lane, slot columns 32 (w / 4) .. +31 ----
-        const int q4 = warp & 3, cg = warp >> 2, rl = 32 * q4 + lane;
-        const bool live = 32 * cg < item.z;
+        // ---- epilogue: slot 32 (w % 4) + lane; columns by w / 4 ----
+        const int q4 = warp & 3, m = warp >> 2, srow = 32 * q4 + lane;
         const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
-        float acc[32];
+        const int c0 = MODE == 0 ? 32 * m : 64 * m, c1 = MODE == 0 ? 64 + 32 * m : 64 * m + 32;
+        int g = 0, s = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            const TileRef tr = tile_at(t);
+            const bool live = 32 * q4 < tr.item.z;
+            float acc[64];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = 0.0f;
-        for (int g = 0; g < np; ++g) {
-            const int db = g % DB, sb = g % SB;
-            if (!mbar_wait(&d_full[db], (g / DB) & 1) || !mbar_wait(&scl_full[sb], (g / SB) & 1)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            if (live) {
+            for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+            for (int q = 0; q < ng && ok; ++q, ++g) {
+                const int sg = g % SG;
+                if (!mbar_wait(&dx_full[sg], (g / SG) & 1)) { ok = false; break; }
+                const float4 dx4 = *reinterpret_cast<const float4*>(s_dx + sg * (DXG / 4) + srow * G4);
+                const float dxv[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
+                for (int pi = 0; pi < G4 / PB; ++pi, ++s) {
+                    const int db = s % DB, sb = s % SB;
+                    if (!mbar_wait(&d_full[db], (s / DB) & 1) || !mbar_wait(&scl_full[sb], (s / SB) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    if (live) {
 #pragma unroll
-                for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
-                    const float dw = s_dw[sb][b][rl];
+                        for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
+                            const float dx = dxv[PB * pi + b];
 #pragma unroll
-                    for (int hh = 0; hh < 2; ++hh) {
-                        float v[16];
-                        tmem_ld16(tmem + lane_base + (db * PB + b) * QN + 32 * cg + 16 * hh, v);
+                            for (int hh = 0; hh < 2; ++hh) {
+                                float v[32];
+                                const int cb = hh ? c1 : c0;
+                                tmem_ld32(tmem + lane_base + (db * PB + b) * TN + cb, v);
 #pragma unroll
-                        for (int j4 = 0; j4 < 4; ++j4) {
-                            const float4 dx = *reinterpret_cast<const float4*>(&s_dx[sb][b][32 * cg + 16 * hh + 4 * j4]);
-                            float* ac = &acc[16 * hh + 4 * j4];
-                            ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw, dx.x)));
-                            ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw, dx.y)));
-                            ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw, dx.z)));
-                            ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw, dx.w)));
+                                for (int j4 = 0; j4 < 8; ++j4) {
+                                    const float4 dw = *reinterpret_cast<const float4*>(&s_dw[sb][b][cb + 4 * j4]);
+                                    float* ac = &acc[32 * hh + 4 * j4];
+                                    ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw.x, dx)));
+                                    ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw.y, dx)));
+                                    ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw.z, dx)));
+                                    ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw.w, dx)));
+                                }
+                            }
                         }
                     }
-                }
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) {
-                mbar_arrive(&d_free[db]);
-                mbar_arrive(&scl_free[sb]);
-            }
-        }
-        if (MODE == 0) {
-            // up rows (quarters 2, 3) hand their sums to the gate rows through shared memory
-            float* s_up = reinterpret_cast<float*>(raws);  // the raw ring is idle now
-            asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
-            if (q4 >= 2 && live) {
-#pragma unroll
-                for (int j = 0; j < 32; ++j) s_up[(32 * (q4 - 2) + lane) * (QN + 1) + 32 * cg + j] = acc[j];
-            }
-            asm volatile("bar.sync 1, %0;" ::"n"(NEPI * 32) : "memory");
-            if (q4 < 2 && live) {
-                const int f0 = blockIdx.x * 64 + 32 * q4;  // first h row of this warp = one Q8_0 block
-#pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    const int col = 32 * cg + j;
-                    if (col < item.z) {  // warp-uniform
-                        const float h = swiglu_ref(acc[j], s_up[rl * (QN + 1) + col]);
-                        float sc;
-                        const int8_t hq = warp_quant_q8(h, &sc);
-                        const size_t slot = (size_t)item.y + col;
-                        a.hq[slot * a.f + f0 + lane] = hq;
-                        if (lane == 0) a.hs[slot * (a.f / 32) + f0 / 32] = sc;
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) {
+                        mbar_arrive(&d_free[db]);
+                        mbar_arrive(&scl_free[sb]);
                     }
                 }
+                __syncwarp();
+                if (lane == 0 && ok) mbar_arrive(&dx_free[sg]);
             }
-        } else if (live) {
-            const int row = blockIdx.x * 128 + rl;
+            if (!ok || !live || srow >= tr.item.z) continue;
+            const size_t slot = (size_t)tr.item.y + srow;
+            if (MODE == 0) {
+                // h rows f0 .. f0 + 31 of this slot: one Q8_0 block of the reference's h
+                float h[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-                if (32 * cg + j < item.z) a.y[(size_t)(item.y + 32 * cg + j) * a.d + row] = acc[j];
+                for (int j = 0; j < 32; ++j) h[j] = swiglu_ref(acc[j], acc[32 + j]);
+                int8_t hq[32];
+                const float sc = quant_block32(h, hq);
+                const int f0 = tr.mt * 64 + 32 * m;
+                uint4* dst = reinterpret_cast<uint4*>(a.h16 + slot * a.f + f0);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const __half2 p = __halves2half2(__int2half_rn(hq[8 * c + 2 * e]), __int2half_rn(hq[8 * c + 2 * e + 1]));
+                        w[e] = *reinterpret_cast<const uint32_t*>(&p);
+                    }
+                    dst[c] = make_uint4(w[0], w[1], w[2], w[3]);
+                }
+                a.hs[slot * (a.f / 32) + f0 / 32] = sc;
+            } else {
+                float4* dst = reinterpret_cast<float4*>(a.y + slot * a.d + tr.mt * TN + 64 * m);
+#pragma unroll
+                for (int j4 = 0; j4 < 16; ++j4)
+                    dst[j4] = make_float4(acc[4 * j4], acc[4 * j4 + 1], acc[4 * j4 + 2], acc[4 * j4 + 3]);
+            }
         }
     }
     if (!ok) atomicOr(err, PI_DEVERR_TIMEOUT);
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * PB * QN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * PB * TN) : "memory");
+}
+
+// Gate/up activations in slot order: slot s < n_routed holds token perm[s], slot
+// n_routed + t the shared expert's token t. Q8_0 values become exact f16; the
+// block scales are copied alongside. One CTA per slot, 16 values per thread.
+__global__ __launch_bounds__(128) void k_slot_rows(const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                                                   const int32_t* __restrict__ perm, int n_routed, int d,
+                                                   __half* __restrict__ xsl, float* __restrict__ xssl) {
+    const int s = blockIdx.x;
+    const int tok = s < n_routed ? perm[s] : s - n_routed;
+    const int8_t* src = xq + (size_t)tok * d;
+    __half* dst = xsl + (size_t)s * d;
+    for (int c = threadIdx.x; c < d / 16; c += blockDim.x) {
+        const int4 v = *reinterpret_cast<const int4*>(src + 16 * c);
+        const int8_t* b = reinterpret_cast<const int8_t*>(&v);
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            const __half2 p = __halves2half2(__int2half_rn(b[2 * e]), __int2half_rn(b[2 * e + 1]));
+            w[e] = *reinterpret_cast<const uint32_t*>(&p);
+        }
+        reinterpret_cast<uint4*>(dst + 16 * c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        reinterpret_cast<uint4*>(dst + 16 * c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    for (int c = threadIdx.x; c < d / 32; c += blockDim.x) xssl[(size_t)s * (d / 32) + c] = xs[(size_t)tok * (d / 32) + c];
 }
 
 // Q8_0 weight rows for the TMA producer: gate/up [rows][d] bytes (box 64 B x 64 rows),
@@ -383,13 +468,20 @@ bool q8_down_map(CUtensorMap* m, const PiMats& w) {
     const cuuint32_t box[4] = {16, 8, (cuuint32_t)cpq, 16};
     return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, w.q, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
-// int8 activations [rows][cols]: gate/up gathers 128-byte rows (box one row high),
-// down loads 128 slot rows x 128 bytes
-bool q8_act_map(CUtensorMap* m, const int8_t* base, int64_t rows, int64_t cols, int box_rows) {
+// slot-major f16 activations [rows][cols]: 128 rows x 32 values per box, 64-byte swizzle
+// (the K-major tile layout the MMA descriptors read)
+bool act16_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols) {
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)cols};
-    const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
-    return encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
+    const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    const cuuint32_t box[2] = {32, 128};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+// slot-major f32 block scales [rows][nb]: 128 rows x 4 blocks per box
+bool scale_map(CUtensorMap* m, const float* base, int64_t rows, int64_t nb) {
+    const cuuint64_t dims[2] = {(cuuint64_t)nb, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)nb * 4};
+    const cuuint32_t box[2] = {4, 128};
+    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace
@@ -420,21 +512,28 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
         return pi_set_error(ctx, PI_ERR_ARG,
                             "prefill Q8_0 GEMM: n_embd must be a multiple of 1024 and the expert widths 512");
     if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: weight tensor maps unavailable");
-    static_assert((size_t)RG * RAWG >= (size_t)64 * (QN + 1) * 4, "the up-row exchange fits in the raw ring");
-    CUtensorMap mxg, mhq;
-    if (!q8_act_map(&mxg, a.xq, T, a.d, 1) || !q8_act_map(&mhq, a.hq, n_slots, a.f, 128))
+    if (!a.xsl || !a.xssl || !a.h16) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: slot buffers missing");
+    (void)T;
+    CUtensorMap mx, mxs, mh, mhs;
+    if (!act16_map(&mx, a.xsl, n_slots, a.d) || !scale_map(&mxs, a.xssl, n_slots, a.d / 32) ||
+        !act16_map(&mh, a.h16, n_slots, a.f) || !scale_map(&mhs, a.hs, n_slots, a.f / 32))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
     pi_smem_attr((const void*)k_moe_gemm_q8<0>, QSMEM);
     pi_smem_attr((const void*)k_moe_gemm_q8<1>, QSMEM);
     {
+        PiProfScope ps(ctx, st, "k_slot_rows");
+        k_slot_rows<<<(unsigned)n_slots, 128, 0, st>>>(a.xq, a.xs, a.perm, a.n_routed, a.d, a.xsl, a.xssl);
+    }
+    const int64_t sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
+    {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
-        k_moe_gemm_q8<0><<<dim3((unsigned)(a.f / 64), (unsigned)max_items), QT, QSMEM, st>>>(a, L->maps, mxg,
-                                                                                           ctx->dev_err);
+        const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.f / 64), sms);
+        k_moe_gemm_q8<0><<<g, QT, QSMEM, st>>>(a, L->maps, mx, mxs, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_down");
-        k_moe_gemm_q8<1><<<dim3((unsigned)(a.d / 128), (unsigned)max_items), QT, QSMEM, st>>>(a, L->maps, mhq,
-                                                                                            ctx->dev_err);
+        const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.d / TN), sms);
+        k_moe_gemm_q8<1><<<g, QT, QSMEM, st>>>(a, L->maps, mh, mhs, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill Q8_0 GEMM") ? PI_ERR_CUDA : PI_OK;
 }
