@@ -53,7 +53,12 @@ extern "C" {
 #define PI_FWD_RMSNORM 1  /* apply RMSNorm (unit weight) before routing: model/mod.rs:1239 */
 #define PI_FWD_RESIDUAL 2 /* out = x + ffn(x): model/mod.rs:1627-1633                     */
 #define PI_FWD_FORCE_GEMV 4 /* expert products on the decode GEMV kernels                */
-#define PI_FWD_FORCE_GEMM 8 /* expert products on the tcgen05 prefill GEMM (Q4_0 only)    */
+#define PI_FWD_FORCE_GEMM 8 /* expert products on the tcgen05 prefill GEMM                 */
+/* Q8_0 prefill GEMM: each block term is added with one fused multiply-add
+ * (acc + sumi * (d_w * d_x) rounded once) instead of the reference's separate
+ * multiply and add. Results stay within the parity tolerance (rel-L2 1e-3)
+ * but are no longer bit-identical to the reference's f32 sums. */
+#define PI_FWD_FAST_SUM 16
 
 typedef struct pi_ctx pi_ctx;
 typedef struct pi_moe_layer pi_moe_layer;

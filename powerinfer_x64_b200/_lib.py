@@ -14,7 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpi_moe.so"
 
 PI_OK, PI_ERR_ARG, PI_ERR_INDEX, PI_ERR_SHORT, PI_ERR_OOM, PI_ERR_CUDA, PI_ERR_TIMEOUT = range(7)
 PI_QT_F32, PI_QT_F16, PI_QT_Q4_0, PI_QT_Q8_0 = 0, 1, 2, 8
-PI_FWD_RMSNORM, PI_FWD_RESIDUAL, PI_FWD_FORCE_GEMV, PI_FWD_FORCE_GEMM = 1, 2, 4, 8
+PI_FWD_RMSNORM, PI_FWD_RESIDUAL, PI_FWD_FORCE_GEMV, PI_FWD_FORCE_GEMM, PI_FWD_FAST_SUM = 1, 2, 4, 8, 16
 
 _P = C.c_void_p
 _I64 = C.c_int64

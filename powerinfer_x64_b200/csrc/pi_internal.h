@@ -190,7 +190,7 @@ constexpr int PI_GEMM_NT_Q8 = 128;  // slots per prefill work item (Q8_0)
 // Exact Q8_0 prefill expert products (pi_prefill_q8.cu): gate/up + SwiGLU + Q8_0 h
 // into a.hq/a.hs, then down into a.y, over work items of <= PI_GEMM_NT_Q8 slots.
 int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t T,
-                          int64_t n_slots, cudaStream_t st);
+                          int64_t n_slots, int flags, cudaStream_t st);
 // Builds L->maps for a Q8_0 layer (layer create; no-op for layers the GEMM does not take).
 int pi_prefill_prepare_q8(pi_ctx* ctx, pi_moe_layer* L);
 bool pi_prefill_q8_shape_ok(int64_t d, int64_t f);

@@ -952,6 +952,105 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
 }
 
 // ---------------------------------------------------------------------------
+// Large-batch dispatch: the same outputs as k_dispatch (offsets, the stable
+// permutation, slot_of, balanced work items) from a chunked counting sort.
+//   k_disp_count   per chunk of DC tokens, per-expert counts (cc[chunk][e]);
+//   k_disp_scan    per expert an exclusive scan over chunks, offsets and items;
+//   k_disp_scatter per chunk a bitmask [e][token] in shared memory: the rank of
+//                  (token t, expert e) in the chunk is the popcount of e's bits
+//                  below t, so slots stay in ascending token order.
+// ---------------------------------------------------------------------------
+constexpr int DC = 256;        // tokens per dispatch chunk (one per thread)
+constexpr int DC_MAXE = 512;   // experts a dispatch CTA keeps in shared memory
+
+__global__ __launch_bounds__(DC) void k_disp_count(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                   int32_t* __restrict__ cc) {
+    __shared__ int h[DC_MAXE];
+    for (int e = threadIdx.x; e < E; e += DC) h[e] = 0;
+    __syncthreads();
+    const int t = blockIdx.x * DC + threadIdx.x;
+    if (t < T)
+        for (int j = 0; j < k; ++j) {
+            const int e = idx[(size_t)t * k + j];
+            if ((unsigned)e < (unsigned)E) atomicAdd(&h[e], 1);
+        }
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += DC) cc[(size_t)blockIdx.x * E + e] = h[e];
+}
+
+__global__ __launch_bounds__(512) void k_disp_scan(int32_t* __restrict__ cc, int nchunk, int T, int k, int E,
+                                                   int has_shared, int tg, int32_t* __restrict__ offsets,
+                                                   int4* __restrict__ items, int32_t* __restrict__ n_items) {
+    __shared__ int s_w[16], s_wi[16];
+    const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
+    int cnt = 0;
+    if (e < E)
+        for (int c = 0; c < nchunk; ++c) {
+            const int v = cc[(size_t)c * E + e];
+            cc[(size_t)c * E + e] = cnt;
+            cnt += v;
+        }
+    const int ni = (cnt + tg - 1) / tg;
+    int a = cnt, b = ni;  // inclusive block scans of counts and item counts
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int ya = __shfl_up_sync(0xffffffffu, a, o), yb = __shfl_up_sync(0xffffffffu, b, o);
+        if (lane >= o) { a += ya; b += yb; }
+    }
+    if (lane == 31) { s_w[warp] = a; s_wi[warp] = b; }
+    __syncthreads();
+    int pa = 0, pb = 0, ta = 0, tb = 0;
+    for (int w = 0; w < 16; ++w) {
+        if (w < warp) { pa += s_w[w]; pb += s_wi[w]; }
+        ta += s_w[w];
+        tb += s_wi[w];
+    }
+    const int off = pa + a - cnt, ibase = pb + b - ni;
+    if (e < E) {
+        if (offsets) offsets[e] = off;
+        for (int q = 0; q < ni; ++q) {
+            const int lo = (int)((int64_t)cnt * q / ni), hi = (int)((int64_t)cnt * (q + 1) / ni);
+            items[ibase + q] = make_int4(e, off + lo, hi - lo, 0);
+        }
+    }
+    const int nsh = has_shared ? (T + tg - 1) / tg : 0;
+    for (int q = threadIdx.x; q < nsh; q += blockDim.x) {
+        const int lo = (int)((int64_t)T * q / nsh), hi = (int)((int64_t)T * (q + 1) / nsh);
+        items[tb + q] = make_int4(E, T * k + lo, hi - lo, 0);
+    }
+    if (threadIdx.x == 0) *n_items = tb + nsh;
+    (void)ta;
+}
+
+__global__ __launch_bounds__(DC) void k_disp_scatter(const int32_t* __restrict__ idx, int T, int k, int E,
+                                                     const int32_t* __restrict__ cc,
+                                                     const int32_t* __restrict__ offsets, int32_t* __restrict__ perm,
+                                                     int32_t* __restrict__ slot_of) {
+    __shared__ uint32_t mask[DC_MAXE * (DC / 32)];
+    for (int i = threadIdx.x; i < E * (DC / 32); i += DC) mask[i] = 0;
+    __syncthreads();
+    const int t = blockIdx.x * DC + threadIdx.x, w = threadIdx.x >> 5;
+    const uint32_t bit = 1u << (threadIdx.x & 31);
+    if (t < T)
+        for (int j = 0; j < k; ++j) {
+            const int e = idx[(size_t)t * k + j];
+            if ((unsigned)e < (unsigned)E) atomicOr(&mask[e * (DC / 32) + w], bit);
+        }
+    __syncthreads();
+    if (t >= T) return;
+    for (int j = 0; j < k; ++j) {
+        const int e = idx[(size_t)t * k + j];
+        if ((unsigned)e >= (unsigned)E) continue;
+        const uint32_t* me = &mask[e * (DC / 32)];
+        int r = __popc(me[w] & (bit - 1));
+        for (int x = 0; x < w; ++x) r += __popc(me[x]);
+        const int slot = offsets[e] + cc[(size_t)blockIdx.x * E + e] + r;
+        perm[slot] = t;
+        slot_of[(size_t)t * k + j] = slot;
+    }
+}
+
+// ---------------------------------------------------------------------------
 // Expert GEMV kernels.
 // ---------------------------------------------------------------------------
 PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
@@ -1727,6 +1826,7 @@ struct FwdBufs {
     float* xnorm;
     __half *xsl, *h16;  // Q8_0 prefill GEMM: slot-major f16 activations and h
     float* xssl;
+    int32_t* disp_cc;   // large-batch dispatch: per-chunk expert counts
     size_t bytes;
 };
 
@@ -1764,6 +1864,27 @@ int64_t max_items(const pi_moe_layer* L, int64_t T, int tg) {
     return std::min<int64_t>(L->E, Tk) + Tk / tg + (L->has_shared ? (T + tg - 1) / tg : 0) + 1;
 }
 
+// Dispatch of T tokens x k experts (see k_dispatch): the chunked counting sort for
+// large batches (cc: scratch of ceil(T / DC) * E ints), the per-expert kernel otherwise.
+void launch_dispatch(cudaStream_t st, const int32_t* idx, const int32_t* counts, int T, int k, int E, int has_shared,
+                     int32_t* offsets, int32_t* perm, int32_t* slot_of, int4* items, int32_t* n_items, int tg,
+                     int32_t* cc) {
+    if (cc && (int64_t)T * k >= 4096 && E <= DC_MAXE) {
+        const int nchunk = (T + DC - 1) / DC;
+        int32_t* offs = offsets ? offsets : cc + (size_t)nchunk * E;  // offsets are needed by the scatter
+        k_disp_count<<<(unsigned)nchunk, DC, 0, st>>>(idx, T, k, E, cc);
+        k_disp_scan<<<1, 512, 0, st>>>(cc, nchunk, T, k, E, has_shared, tg, offs, items, n_items);
+        k_disp_scatter<<<(unsigned)nchunk, DC, 0, st>>>(idx, T, k, E, cc, offs, perm, slot_of);
+        return;
+    }
+    if (T >= 8192)
+        k_dispatch<4><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, T, k, E, has_shared, offsets, perm, slot_of,
+                                                         items, n_items, tg);
+    else
+        k_dispatch<1><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, T, k, E, has_shared, offsets, perm, slot_of,
+                                                         items, n_items, tg);
+}
+
 FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     PiBump b{base};
     FwdBufs f;
@@ -1783,6 +1904,7 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.perm = b.take<int32_t>(T * k);
     f.slot_of = b.take<int32_t>(T * k);
     f.items = b.take<int4>(max_items(L, T, TG));  // TG is the smallest item size
+    f.disp_cc = b.take<int32_t>(((T + DC - 1) / DC + 1) * E);
     f.n_items = b.take<int32_t>(1);
     f.hq = b.take<int8_t>(slots * F);
     f.hs = b.take<float>(slots * (F / 32));
@@ -1857,10 +1979,10 @@ ExpertArgs expert_args(const pi_moe_layer* L, int E_items, const FwdBufs& B, con
 // the tensor-core GEMMs for prefill-sized batches, the GEMV kernels otherwise.
 // T: token rows behind the slots (Q4_0 GEMM: B.xth/B.xtl hold their f16 split).
 int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t T, int64_t n_slots, unsigned ni,
-                bool gemm, const FwdBufs& B, cudaStream_t st) {
+                bool gemm, const FwdBufs& B, cudaStream_t st, int flags = 0) {
     const bool q8 = L->qtype == PI_QT_Q8_0;
     const int d = (int)L->d;
-    if (gemm && q8) return pi_prefill_experts_q8(ctx, L, a, ni, T, n_slots, st);
+    if (gemm && q8) return pi_prefill_experts_q8(ctx, L, a, ni, T, n_slots, flags, st);
     if (gemm) return pi_prefill_experts(ctx, L, a, ni, n_slots, B.xth, B.xtl, T, B.hh, B.hl, st);
     const dim3 gu((unsigned)(L->f / (q8 ? GU_ROWS : 32)), ni), dn((unsigned)(L->d / (q8 ? DN_ROWS : 128)), ni);
     if (q8) {
@@ -2075,12 +2197,8 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const int tg = gemm ? (q8 ? PI_GEMM_NT_Q8 : PI_GEMM_NT) : TG;
     {
         PiProfScope ps(ctx, st, "k_dispatch");
-        if ((int)T >= 8192)
-            k_dispatch<4><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
-                                                      perm, B.slot_of, B.items, B.n_items, tg);
-        else
-            k_dispatch<1><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets,
-                                                      perm, B.slot_of, B.items, B.n_items, tg);
+        launch_dispatch(st, idx, counts, (int)T, k, E, L->has_shared ? 1 : 0, offsets, perm, B.slot_of, B.items,
+                        B.n_items, tg, B.disp_cc);
     }
     if (route_only) return pi_cuda_check(ctx, cudaGetLastError(), "route") ? PI_ERR_CUDA : PI_OK;
 
@@ -2091,7 +2209,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         PiProfScope ps(ctx, st, "k_split_tokens");
         k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
     }
-    if (int rc = run_experts(ctx, L, a, T, n_slots, ni, gemm, B, st)) return rc;
+    if (int rc = run_experts(ctx, L, a, T, n_slots, ni, gemm, B, st, flags)) return rc;
     PiProfScope ps(ctx, st, "k_combine");
     k_combine<<<dim3((unsigned)T, (unsigned)((d + 1023) / 1024)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale,
                                                                            nullptr, (int)T, k, d,
@@ -2145,6 +2263,7 @@ FwdBufs carve_rows(const pi_moe_layer* L, int64_t n, char* base) {
     f.perm = b.take<int32_t>(n);
     f.slot_of = b.take<int32_t>(n);
     f.items = b.take<int4>(std::min<int64_t>(L->n_exp, n) + 2 * ((n + TG - 1) / TG) + 1);
+    f.disp_cc = b.take<int32_t>(((n + DC - 1) / DC + 1) * L->n_exp);
     f.n_items = b.take<int32_t>(1);
     f.hq = b.take<int8_t>(slots * F);
     f.hs = b.take<float>(slots * (F / 32));
@@ -2170,14 +2289,9 @@ int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* 
     if (!shared_only) k_ep_hist<<<(unsigned)((n_rows + 255) / 256), 256, 0, st>>>(eid, n_rows, B.counts);
     {
         PiProfScope ps(ctx, st, "k_dispatch");
-        if ((int)n_rows >= 8192)
-            k_dispatch<4><<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
-                                                       shared_only ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
-                                                       B.n_items, tg);
-        else
-            k_dispatch<1><<<(unsigned)(En + 1), 256, 0, st>>>(shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En,
-                                                       shared_only ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
-                                                       B.n_items, tg);
+        // the shared expert alone needs only its items (no routed slots to sort)
+        launch_dispatch(st, shared_only ? B.perm : eid, B.counts, (int)n_rows, 1, En, shared_only ? 1 : 0, B.offsets,
+                        B.perm, B.slot_of, B.items, B.n_items, tg, shared_only ? nullptr : B.disp_cc);
     }
     ExpertArgs a = expert_args(L, En, B, B.perm, n_rows, nullptr);
     a.xq = xq;

@@ -110,7 +110,7 @@ struct TileRef {
 };
 
 // MODE 0: gate/up (+ SwiGLU, Q8_0 h as exact f16); MODE 1: down (y).
-template <int MODE>
+template <int MODE, bool FAST>
 __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
                                                        const __grid_constant__ CUtensorMap mact,
                                                        const __grid_constant__ CUtensorMap mscl, uint32_t* err) {
@@ -352,9 +352,9 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                 const int sg = g % SG;
                 if (!mbar_wait(&dx_full[sg], (g / SG) & 1)) { ok = false; break; }
                 const float4 dx4 = *reinterpret_cast<const float4*>(s_dx + sg * (DXG / 4) + srow * G4);
-                const float dxv[4] = {dx4.x, dx4.y, dx4.z, dx4.w};
                 for (int pi = 0; pi < G4 / PB; ++pi, ++s) {
                     const int db = s % DB, sb = s % SB;
+                    const float dxs[PB] = {pi ? dx4.z : dx4.x, pi ? dx4.w : dx4.y};  // blocks 2 pi, 2 pi + 1
                     if (!mbar_wait(&d_full[db], (s / DB) & 1) || !mbar_wait(&scl_full[sb], (s / SB) & 1)) {
                         ok = false;
                         break;
@@ -363,7 +363,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                     if (live) {
 #pragma unroll
                         for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
-                            const float dx = dxv[PB * pi + b];
+                            const float dx = dxs[b];
 #pragma unroll
                             for (int hh = 0; hh < 2; ++hh) {
                                 float v[32];
@@ -373,10 +373,12 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                                 for (int j4 = 0; j4 < 8; ++j4) {
                                     const float4 dw = *reinterpret_cast<const float4*>(&s_dw[sb][b][cb + 4 * j4]);
                                     float* ac = &acc[32 * hh + 4 * j4];
-                                    ac[0] = fadd(ac[0], fmul(v[4 * j4], fmul(dw.x, dx)));
-                                    ac[1] = fadd(ac[1], fmul(v[4 * j4 + 1], fmul(dw.y, dx)));
-                                    ac[2] = fadd(ac[2], fmul(v[4 * j4 + 2], fmul(dw.z, dx)));
-                                    ac[3] = fadd(ac[3], fmul(v[4 * j4 + 3], fmul(dw.w, dx)));
+                                    const float w4[4] = {dw.x, dw.y, dw.z, dw.w};
+#pragma unroll
+                                    for (int e = 0; e < 4; ++e) {
+                                        if (FAST) ac[e] = __fmaf_rn(v[4 * j4 + e], fmul(w4[e], dx), ac[e]);
+                                        else ac[e] = fadd(ac[e], fmul(v[4 * j4 + e], fmul(w4[e], dx)));
+                                    }
                                 }
                             }
                         }
@@ -506,7 +508,7 @@ int pi_prefill_prepare_q8(pi_ctx* ctx, pi_moe_layer* L) {
 }
 
 int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t max_items, int64_t T,
-                          int64_t n_slots, cudaStream_t st) {
+                          int64_t n_slots, int flags, cudaStream_t st) {
     if (L->qtype != PI_QT_Q8_0) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: Q8_0 weights only");
     if (!pi_prefill_q8_shape_ok(a.d, a.f) || (L->has_shared && L->f_sh != L->f))
         return pi_set_error(ctx, PI_ERR_ARG,
@@ -518,8 +520,11 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     if (!act16_map(&mx, a.xsl, n_slots, a.d) || !scale_map(&mxs, a.xssl, n_slots, a.d / 32) ||
         !act16_map(&mh, a.h16, n_slots, a.f) || !scale_map(&mhs, a.hs, n_slots, a.f / 32))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
-    pi_smem_attr((const void*)k_moe_gemm_q8<0>, QSMEM);
-    pi_smem_attr((const void*)k_moe_gemm_q8<1>, QSMEM);
+    const bool fast = (flags & PI_FWD_FAST_SUM) != 0;
+    auto gu = fast ? k_moe_gemm_q8<0, true> : k_moe_gemm_q8<0, false>;
+    auto dn = fast ? k_moe_gemm_q8<1, true> : k_moe_gemm_q8<1, false>;
+    pi_smem_attr((const void*)gu, QSMEM);
+    pi_smem_attr((const void*)dn, QSMEM);
     {
         PiProfScope ps(ctx, st, "k_slot_rows");
         k_slot_rows<<<(unsigned)n_slots, 128, 0, st>>>(a.xq, a.xs, a.perm, a.n_routed, a.d, a.xsl, a.xssl);
@@ -528,12 +533,12 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
         const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.f / 64), sms);
-        k_moe_gemm_q8<0><<<g, QT, QSMEM, st>>>(a, L->maps, mx, mxs, ctx->dev_err);
+        gu<<<g, QT, QSMEM, st>>>(a, L->maps, mx, mxs, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_down");
         const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.d / TN), sms);
-        k_moe_gemm_q8<1><<<g, QT, QSMEM, st>>>(a, L->maps, mh, mhs, ctx->dev_err);
+        dn<<<g, QT, QSMEM, st>>>(a, L->maps, mh, mhs, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill Q8_0 GEMM") ? PI_ERR_CUDA : PI_OK;
 }

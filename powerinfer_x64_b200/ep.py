@@ -28,7 +28,7 @@ import ctypes as C
 import numpy as np
 
 from . import quant
-from ._lib import PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_Q8_0, Context, PiError, PI_ERR_ARG, PiMoeLayerDesc, lib, ptr, \
+from ._lib import PI_FWD_FAST_SUM, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_Q8_0, Context, PiError, PI_ERR_ARG, PiMoeLayerDesc, lib, ptr, \
     stream_ptr
 
 
@@ -125,7 +125,7 @@ class EPMoeLayer:
         except Exception:
             pass
 
-    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False):
+    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False, fast: bool = False):
         """MoE FFN of the home tokens x [T, d] (device f32) -> out [T, d]."""
         torch = _torch()
         L, s = lib(), stream_ptr()
@@ -134,6 +134,13 @@ class EPMoeLayer:
         if out is None:
             out = torch.empty((T, d), dtype=torch.float32, device="cuda")
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
+        flags |= PI_FWD_FAST_SUM if fast else 0
+        if self.world == 1:
+            # one rank holds every expert: nothing to exchange, the fused layer forward
+            # (routed and shared experts in the same grouped launches) is the whole step
+            if T:
+                self.ctx.check(L.pi_moe_forward(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, s))
+            return out
         dv = xd.device
         e = lambda *shape, dt=torch.float32: torch.empty(shape, dtype=dt, device=dv)
         idx, gates, shscale = e(T * k, dt=torch.int32), e(T * k), e(max(T, 1))

@@ -17,7 +17,7 @@ from dataclasses import dataclass
 import numpy as np
 
 from . import quant
-from ._lib import (PI_FWD_FORCE_GEMM, PI_FWD_FORCE_GEMV, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_F32, Context, PiError, PiMoeLayerDesc, PI_ERR_ARG, lib,
+from ._lib import (PI_FWD_FAST_SUM, PI_FWD_FORCE_GEMM, PI_FWD_FORCE_GEMV, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_F32, Context, PiError, PiMoeLayerDesc, PI_ERR_ARG, lib,
                    ptr, stream_ptr)
 
 
@@ -93,11 +93,14 @@ class MoeLayer:
         return o
 
     # -- forward -----------------------------------------------------------
-    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None, path: str = "auto"):
+    def forward(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None, path: str = "auto",
+                fast: bool = False):
         """MoE FFN of tokens x [T, d] (device f32) -> out [T, d].
 
         path: "auto" (tensor-core GEMM for prefill-sized Q4_0 batches, else GEMV),
-        "gemv" or "gemm" to force one.
+        "gemv" or "gemm" to force one. fast: the Q8_0 prefill GEMM adds each block
+        term with a fused multiply-add (PI_FWD_FAST_SUM; within the parity tolerance,
+        not bit-identical).
         """
         torch = _torch()
         xd = quant._f32(x)
@@ -108,11 +111,12 @@ class MoeLayer:
             return out
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
         flags |= {"auto": 0, "gemv": PI_FWD_FORCE_GEMV, "gemm": PI_FWD_FORCE_GEMM}[path]
+        flags |= PI_FWD_FAST_SUM if fast else 0
         self.ctx.check(lib().pi_moe_forward(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, stream_ptr(stream)))
         return out
 
     def forward_routed(self, x, out=None, rmsnorm: bool = False, residual: bool = False, stream=None,
-                       path: str = "auto"):
+                       path: str = "auto", fast: bool = False):
         """``forward`` that also returns the routing it used: (out, dict(idx, gates,
         counts, offsets, perm)) as ``route`` returns them, computed on the
         (optionally RMS-normed) tokens the forward itself routed."""
@@ -131,6 +135,7 @@ class MoeLayer:
             return out, o
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
         flags |= {"auto": 0, "gemv": PI_FWD_FORCE_GEMV, "gemm": PI_FWD_FORCE_GEMM}[path]
+        flags |= PI_FWD_FAST_SUM if fast else 0
         self.ctx.check(lib().pi_moe_forward_routed(self.ctx.h, self.h, ptr(xd), T, ptr(out), flags, ptr(o["idx"]),
                                                    ptr(o["gates"]), ptr(o["counts"]), ptr(o["offsets"]),
                                                    ptr(o["perm"]), stream_ptr(stream)))

@@ -131,14 +131,17 @@ def test_c3_baseline_sizes_vs_oracle(pkg, orc, torch, c3, T):
                                         hot_counts=counts[hot].tolist(), rel_l2=rl2, max_abs_over_rms=ma))
 
 
-def test_c5_T8192_vs_oracle(pkg, orc, torch):
+@pytest.mark.parametrize("fast", [False, True])
+def test_c5_T8192_vs_oracle(pkg, orc, torch, fast):
+    """fast: the grouped GEMM adds the block terms with fused multiply-adds
+    (PI_FWD_FAST_SUM); the bars are the same."""
     from powerinfer_x64_b200 import synth
 
     c = synth.C5
     T = 8192
     L, t = synth.moe_layer(c, seed=0, layer=0, keep_tensors=True)
     x = synth.tokens_dev(c.d, T, seed=0, layer=0)
-    out, r = L.forward_routed(x, rmsnorm=True, residual=True)
+    out, r = L.forward_routed(x, rmsnorm=True, residual=True, fast=fast)
     xh = _host(x)
     normed = np.stack([orc.rms_norm(row, np.ones(c.d, np.float32)) for row in xh])
     ref = orc.moe_route(normed, _host(t["router"]), c.d, c.E, c.k)
@@ -149,7 +152,7 @@ def test_c5_T8192_vs_oracle(pkg, orc, torch):
     want = _oracle_layer(orc, c, t, xh[pick], residual=True, rmsnorm=True)
     rl2, ma = close(got - xh[pick], want - xh[pick])
     same = float(np.mean(got.view(np.uint32) == want.view(np.uint32)))
-    _report("c5_T8192_parity.json", dict(T=T, routing_bit_exact=True, sample=len(pick), rel_l2=rl2,
+    _report(f"c5_T8192{'_fast' if fast else ''}_parity.json", dict(T=T, routing_bit_exact=True, sample=len(pick), rel_l2=rl2,
                                          max_abs_over_rms=ma, bitwise_equal_fraction=same))
 
 
