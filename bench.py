@@ -146,7 +146,8 @@ def workload_config(cname, T, world, layers):
     c = CFG[cname]
     kind = {"c2": "Q8_0 decode", "c3": "Q4_0 prefill, Zipf router bias",
             "c5": "Q8_0, one layer of the 40-layer stack, RMSNorm before + residual after"}[cname]
-    par = (f"ep{world} (experts sharded {c['E'] // world} per GPU, tokens data-parallel)" if cname == "c5"
+    par = (f"ep{world} (experts sharded {c['E'] // world} per GPU, tokens data-parallel, rows pushed over NVLink "
+           "peer memory)" if cname == "c5"
            else f"dp{world} (replicas)")
     return {"workload": f"{c['name']} (BASELINE config {cname[1]}): d=2048 E=256 k=8 f=512 +shared expert, {kind}",
             "tokens_per_step_per_gpu": T, "global_batch": T * world, "parallelism": par, "layers_cycled": layers,
@@ -408,6 +409,11 @@ def main():
     # layers + fixed per-layer tokens (each rank its own token stream). c5: one model
     # (the same weights on every rank) sharded by experts over the ranks
     layers, xs, routing = [], [], []
+    comm = None
+    if cname == "c5" and world > 1:
+        from powerinfer_x64_b200.ep import EPComm
+
+        comm = EPComm(rank, world, T, cfg.d, cfg.k)  # the NVLink data plane shared by every layer
     for li in range(args.layers):
         x = synth.tokens_dev(cfg.d, T, seed=rank, layer=li)
         if cname == "c5":
@@ -416,7 +422,7 @@ def main():
             t = synth.moe_tensors(cfg, seed=0, layer=li)
             loc = lambda a: local_expert_bytes(a, cfg.E, rank, world).clone()
             L = EPMoeLayer(t["router"], loc(t["gate_exps"]), loc(t["up_exps"]), loc(t["down_exps"]), cfg.d, cfg.f,
-                           cfg.E, cfg.k, rank=rank, world=world, shared=t["shared"])
+                           cfg.E, cfg.k, rank=rank, world=world, shared=t["shared"], comm=comm)
             del t
             torch.cuda.empty_cache()
             U = cfg.E
@@ -510,9 +516,10 @@ def main():
     pipe = HostPipeline(layers[0], T, cfg.d, **fwd_kw)
 
     def e2e_run(i0, n):
-        for i in range(i0, i0 + n):
-            pipe.layer = layers[i % args.layers]
-            pipe.run([xh[i % args.layers]], [oh[i % 2]])
+        idx = range(i0, i0 + n)
+        pipe.run([xh[i % args.layers] for i in idx], [oh[i % 2] for i in idx],
+                 layers=[layers[i % args.layers] for i in idx])
+        pipe.finish()
 
     e2e_run(0, args.warmup)
     torch.cuda.synchronize()

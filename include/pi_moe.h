@@ -63,6 +63,10 @@ extern "C" {
 typedef struct pi_ctx pi_ctx;
 typedef struct pi_moe_layer pi_moe_layer;
 typedef struct pi_sparse_ffn pi_sparse_ffn;
+typedef struct pi_ep_comm pi_ep_comm;
+
+#define PI_EP_MAX_WORLD 64    /* ranks of one expert-parallel group          */
+#define PI_EP_HANDLE_BYTES 64 /* bytes of one rank's exported memory handle  */
 
 /* ---- context ----------------------------------------------------------
  * Replaces GpuDevice::new / GpuResources::init (src/cuda/mod.rs:193-218,
@@ -235,6 +239,43 @@ int pi_moe_experts_q8(pi_ctx* ctx, pi_moe_layer* layer, int64_t n_rows, const in
 int pi_moe_ep_combine(pi_ctx* ctx, pi_moe_layer* layer, const float* x, int64_t T, int32_t flags, const float* gates,
                       const float* shscale, const int32_t* slot_row, const float* y_back, const float* y_shared,
                       float* out, void* stream);
+
+/* ---- expert parallelism over NVLink peer memory --------------------------
+ * No counterpart in the reference, which runs one process (model/mod.rs:
+ * 1245-1571); multi-GPU is only planned there. One rank per GPU; each holds
+ * E / world experts (pi_moe_layer_create_ep with first_expert = rank * E / world).
+ *
+ * pi_ep_comm_create allocates this rank's exchange memory (about
+ * world * max_tokens * (3 + 2 * n_embd) * 2 bytes, plus local scratch);
+ * pi_ep_comm_ipc_handle exports it (PI_EP_HANDLE_BYTES bytes); the host
+ * gathers every rank's handle in rank order (any host collective) and passes
+ * them to pi_ep_comm_open, which maps the peers. One comm serves every layer of
+ * the group; the ranks must call pi_moe_ep_forward the same number of times, in
+ * the same order. */
+int pi_ep_comm_create(pi_ctx* ctx, int32_t rank, int32_t world, int64_t max_tokens, int64_t n_embd, int32_t top_k,
+                      pi_ep_comm** out);
+int pi_ep_comm_ipc_handle(pi_ep_comm* comm, void* handle_out);
+int pi_ep_comm_open(pi_ep_comm* comm, const void* handles);
+void pi_ep_comm_destroy(pi_ep_comm* comm);
+
+/* One expert-parallel MoE layer forward of this rank's T home tokens (T <= the
+ * comm's max_tokens): routing, one Q8_0 row per (token, rank holding one of its
+ * experts) stored into that rank's memory, the held experts over every row
+ * received, the shared expert over the home tokens, one gate-weighted partial
+ * row per (token, rank) stored back, and the combine in ascending rank order
+ * (= ascending expert order), then the shared expert and x (PI_FWD_RESIDUAL).
+ * Outputs match pi_moe_forward to f32 rounding: the partial rows regroup the
+ * reference's left-to-right combine sum (model/mod.rs:1525-1534) by rank.
+ * Waits between ranks give up after about a second: pi_ctx_check then reports
+ * PI_ERR_TIMEOUT. flags: PI_FWD_RMSNORM | PI_FWD_RESIDUAL | PI_FWD_FAST_SUM. */
+int pi_moe_ep_forward(pi_ctx* ctx, pi_moe_layer* layer, pi_ep_comm* comm, const float* x, int64_t T, float* out,
+                      int32_t flags, void* stream);
+
+/* Test hook (no reference counterpart): advances the comm's epoch by n with no
+ * exchange, so the next pi_moe_ep_forward waits for acknowledgements that never
+ * arrive. Its waits give up after about a second each and pi_ctx_check returns
+ * PI_ERR_TIMEOUT; nothing faults. The comm is out of step afterwards. */
+int pi_ep_comm_debug_skip(pi_ep_comm* comm, int32_t n);
 
 /* MoeRouter::route of the standalone operator API (src/moe/mod.rs:69-108)
  * for T tokens: router f32 expert-major [E][d] (row e = column e of the

@@ -14,6 +14,7 @@ LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libpi_moe.so"
 
 PI_OK, PI_ERR_ARG, PI_ERR_INDEX, PI_ERR_SHORT, PI_ERR_OOM, PI_ERR_CUDA, PI_ERR_TIMEOUT = range(7)
 PI_QT_F32, PI_QT_F16, PI_QT_Q4_0, PI_QT_Q8_0 = 0, 1, 2, 8
+PI_EP_MAX_WORLD, PI_EP_HANDLE_BYTES = 64, 64
 PI_FWD_RMSNORM, PI_FWD_RESIDUAL, PI_FWD_FORCE_GEMV, PI_FWD_FORCE_GEMM, PI_FWD_FAST_SUM = 1, 2, 4, 8, 16
 
 _P = C.c_void_p
@@ -69,6 +70,12 @@ SIGNATURES = {
     "pi_moe_experts_q8": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _P]),
     "pi_moe_ep_combine": (_INT, [_P, _P, _P, _I64, _I32, _P, _P, _P, _P, _P, _P, _P]),
     "pi_router_topk_softmax": (_INT, [_P, _P, _I64, _P, _I64, _I32, _I32, _P, _P, _P]),
+    "pi_ep_comm_create": (_INT, [_P, _I32, _I32, _I64, _I64, _I32, C.POINTER(_P)]),
+    "pi_ep_comm_ipc_handle": (_INT, [_P, _P]),
+    "pi_ep_comm_open": (_INT, [_P, _P]),
+    "pi_ep_comm_destroy": (None, [_P]),
+    "pi_moe_ep_forward": (_INT, [_P, _P, _P, _P, _I64, _P, _I32, _P]),
+    "pi_ep_comm_debug_skip": (_INT, [_P, _I32]),
     "pi_sparse_ffn_create": (_INT, [_P, _P, _P, _P, _I32, _I64, _I64, _I32, C.POINTER(_P)]),
     "pi_sparse_ffn_destroy": (None, [_P]),
     "pi_sparse_ffn_forward": (_INT, [_P, _P, _P, _I64, _P, _P, _P, _P]),

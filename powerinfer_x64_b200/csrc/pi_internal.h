@@ -172,6 +172,14 @@ struct ExpertArgs {
     __half* xsl;
     float* xssl;
     __half* h16;
+    // slot -> activation row: routed slot s < n_routed reads row perm[s]; shared slot
+    // n_routed + t reads row sh_row0 + t. With n_routed_dev set, n_routed is *n_routed_dev
+    // (known only on the device).
+    const int32_t* n_routed_dev = nullptr;
+    int sh_row0 = 0;
+    int n_sh = 0;  // shared-expert slots
+    const int8_t* xq_sh = nullptr;  // Q8_0 GEMM: shared-expert rows from here (row t) when set
+    const float* xs_sh = nullptr;
 };
 
 
@@ -213,6 +221,29 @@ int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* 
 int pi_moe_ep_combine_run(pi_ctx* ctx, const pi_moe_layer* L, const float* x, int64_t T, int flags, const float* gates,
                           const float* shscale, const int32_t* slot_row, const float* y_back, const float* y_shared,
                           float* out, cudaStream_t st);
+// Expert-parallel forward over NVLink peer memory (pi_ep.cu) uses these two passes:
+// the home tokens' routing with their Q8_0 rows kept, and the held experts over the
+// received rows (row r carries up to k local expert ids eid[r*k + j], ascending, -1 for
+// none) plus the shared expert over n_home home rows. Both carve from `scratch`.
+struct PiEpHome {
+    int32_t* idx;
+    float* gates;
+    float* shscale;
+    int8_t* xq;
+    float* xs;
+};
+size_t pi_moe_ep_home_bytes(const pi_moe_layer* L, int64_t T, int flags);
+int pi_moe_ep_home(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int flags, char* scratch, PiEpHome* H,
+                   cudaStream_t st);
+struct PiRowsOut {
+    float* y;            // [slots][d]: routed slots, then the shared expert's
+    int32_t* slot_of;    // [n_rows * k]
+    int32_t* n_routed;   // device: routed slots (the shared expert's slot of home row t is *n_routed + t)
+};
+size_t pi_moe_rows_multi_bytes(const pi_moe_layer* L, int64_t n_rows, int k, int64_t n_home);
+int pi_moe_rows_multi_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, int k, const int8_t* xq, const float* xs,
+                          const int32_t* eid, int64_t n_home, const int8_t* xq_home, const float* xs_home, int flags,
+                          char* scratch, PiRowsOut* out, cudaStream_t st);
 // Builds L->router_t and the tensor-core router operands from L->router (prefill router kernels).
 int pi_router_prepare(pi_ctx* ctx, pi_moe_layer* L);
 // Fast router logits on tensor cores (pi_prefill.cu): logits[t][e] (stride E + 1),

@@ -978,9 +978,12 @@ __global__ __launch_bounds__(DC) void k_disp_count(const int32_t* __restrict__ i
     for (int e = threadIdx.x; e < E; e += DC) cc[(size_t)blockIdx.x * E + e] = h[e];
 }
 
+// Shared-expert items cover n_sh slots starting at T*k, or (n_routed_out != NULL) right
+// after the realised routed slots, whose count is then written to *n_routed_out.
 __global__ __launch_bounds__(512) void k_disp_scan(int32_t* __restrict__ cc, int nchunk, int T, int k, int E,
-                                                   int has_shared, int tg, int32_t* __restrict__ offsets,
-                                                   int4* __restrict__ items, int32_t* __restrict__ n_items) {
+                                                   int n_sh, int tg, int32_t* __restrict__ offsets,
+                                                   int4* __restrict__ items, int32_t* __restrict__ n_items,
+                                                   int32_t* __restrict__ n_routed_out) {
     __shared__ int s_w[16], s_wi[16];
     const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
     int cnt = 0;
@@ -1013,13 +1016,16 @@ __global__ __launch_bounds__(512) void k_disp_scan(int32_t* __restrict__ cc, int
             items[ibase + q] = make_int4(e, off + lo, hi - lo, 0);
         }
     }
-    const int nsh = has_shared ? (T + tg - 1) / tg : 0;
+    const int nsh = (n_sh + tg - 1) / tg;
+    const int sbase = n_routed_out ? ta : T * k;
     for (int q = threadIdx.x; q < nsh; q += blockDim.x) {
-        const int lo = (int)((int64_t)T * q / nsh), hi = (int)((int64_t)T * (q + 1) / nsh);
-        items[tb + q] = make_int4(E, T * k + lo, hi - lo, 0);
+        const int lo = (int)((int64_t)n_sh * q / nsh), hi = (int)((int64_t)n_sh * (q + 1) / nsh);
+        items[tb + q] = make_int4(E, sbase + lo, hi - lo, 0);
     }
-    if (threadIdx.x == 0) *n_items = tb + nsh;
-    (void)ta;
+    if (threadIdx.x == 0) {
+        *n_items = tb + nsh;
+        if (n_routed_out) *n_routed_out = ta;
+    }
 }
 
 __global__ __launch_bounds__(DC) void k_disp_scatter(const int32_t* __restrict__ idx, int T, int k, int E,
@@ -1865,15 +1871,17 @@ int64_t max_items(const pi_moe_layer* L, int64_t T, int tg) {
 }
 
 // Dispatch of T tokens x k experts (see k_dispatch): the chunked counting sort for
-// large batches (cc: scratch of ceil(T / DC) * E ints), the per-expert kernel otherwise.
+// large batches (cc: scratch of (ceil(T / DC) + 1) * E ints), the per-expert kernel
+// otherwise. n_sh: shared-expert slots (default T); n_routed_dev: see k_disp_scan.
 void launch_dispatch(cudaStream_t st, const int32_t* idx, const int32_t* counts, int T, int k, int E, int has_shared,
                      int32_t* offsets, int32_t* perm, int32_t* slot_of, int4* items, int32_t* n_items, int tg,
-                     int32_t* cc) {
-    if (cc && (int64_t)T * k >= 4096 && E <= DC_MAXE) {
+                     int32_t* cc, int n_sh = -1, int32_t* n_routed_dev = nullptr) {
+    if (cc && ((int64_t)T * k >= 4096 || n_routed_dev) && E <= DC_MAXE) {
         const int nchunk = (T + DC - 1) / DC;
         int32_t* offs = offsets ? offsets : cc + (size_t)nchunk * E;  // offsets are needed by the scatter
         k_disp_count<<<(unsigned)nchunk, DC, 0, st>>>(idx, T, k, E, cc);
-        k_disp_scan<<<1, 512, 0, st>>>(cc, nchunk, T, k, E, has_shared, tg, offs, items, n_items);
+        k_disp_scan<<<1, 512, 0, st>>>(cc, nchunk, T, k, E, has_shared ? (n_sh >= 0 ? n_sh : T) : 0, tg, offs, items,
+                                       n_items, n_routed_dev);
         k_disp_scatter<<<(unsigned)nchunk, DC, 0, st>>>(idx, T, k, E, cc, offs, perm, slot_of);
         return;
     }
@@ -1972,6 +1980,9 @@ ExpertArgs expert_args(const pi_moe_layer* L, int E_items, const FwdBufs& B, con
     a.xsl = B.xsl;
     a.xssl = B.xssl;
     a.h16 = B.h16;
+    a.n_routed_dev = nullptr;
+    a.sh_row0 = 0;
+    a.n_sh = 0;
     return a;
 }
 
@@ -2204,6 +2215,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
 
     const int64_t n_slots = T * k + (L->has_shared ? T : 0);
     ExpertArgs a = expert_args(L, E, B, perm, T * k, xin);
+    a.n_sh = L->has_shared ? (int)T : 0;
     const unsigned ni = (unsigned)max_items(L, T, tg);
     if (gemm && !q8 && !use_router_tc(L, T)) {  // the router did not split the tokens
         PiProfScope ps(ctx, st, "k_split_tokens");
@@ -2294,6 +2306,7 @@ int pi_moe_rows_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, const int8_t* 
                         B.perm, B.slot_of, B.items, B.n_items, tg, shared_only ? nullptr : B.disp_cc);
     }
     ExpertArgs a = expert_args(L, En, B, B.perm, n_rows, nullptr);
+    a.n_sh = shared_only ? (int)n_rows : 0;
     a.xq = xq;
     a.xs = xs;
     const int64_t n_slots = shared_only ? 2 * n_rows : n_rows;
@@ -2328,4 +2341,83 @@ extern "C" int pi_router_topk_softmax(pi_ctx* ctx, const float* x, int64_t T, co
     k_router<<<rg, 128, 0, st>>>(x, router, nullptr, (int)T, (int)d, E, E, logits);
     k_topk_api<<<(unsigned)((T + TK_WARPS - 1) / TK_WARPS), TK_WARPS * 32, 0, st>>>(logits, (int)T, E, k, idx, weights);
     return pi_cuda_check(ctx, cudaGetLastError(), "router") ? PI_ERR_CUDA : PI_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel passes used by the NVLink data plane (pi_ep.cu).
+// ---------------------------------------------------------------------------
+namespace {
+int ep_home_flags(int flags) {
+    return (flags & (PI_FWD_RMSNORM | PI_FWD_RESIDUAL)) | PI_FWD_FORCE_GEMV | PI_FWD_KEEP_Q8;
+}
+
+FwdBufs carve_multi(const pi_moe_layer* L, int64_t n_rows, int k, int64_t n_home, char* base) {
+    PiBump b{base};
+    FwdBufs f{};
+    const int64_t d = L->d, F = L->f, En = L->n_exp, nr = n_rows * k, slots = nr + n_home;
+    f.offsets = b.take<int32_t>(En);
+    f.perm = b.take<int32_t>(nr);
+    f.slot_of = b.take<int32_t>(nr);
+    f.items = b.take<int4>(En + nr / PI_GEMM_NT_Q8 + n_home / PI_GEMM_NT_Q8 + 4);
+    f.n_items = b.take<int32_t>(1);
+    f.counts = b.take<int32_t>(1);  // the routed-slot count (device)
+    f.disp_cc = b.take<int32_t>(((n_rows + DC - 1) / DC + 1) * En);
+    f.hs = b.take<float>(slots * (F / 32));
+    f.y = b.take<float>(slots * d);
+    f.xsl = b.take<__half>(slots * d);
+    f.xssl = b.take<float>(slots * (d / 32));
+    f.h16 = b.take<__half>(slots * F);
+    f.bytes = b.off + 256;
+    return f;
+}
+}  // namespace
+
+size_t pi_moe_ep_home_bytes(const pi_moe_layer* L, int64_t T, int flags) {
+    return pi_moe_scratch_bytes(L, T, ep_home_flags(flags));
+}
+
+int pi_moe_ep_home(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, int flags, char* scratch, PiEpHome* H,
+                   cudaStream_t st) {
+    const int f = ep_home_flags(flags);
+    const FwdBufs B = carve(L, T, f, scratch);
+    H->idx = B.idx;
+    H->gates = B.gates;
+    H->shscale = B.shscale;
+    H->xq = B.xq;
+    H->xs = B.xs;
+    if (T == 0) return PI_OK;
+    return pi_moe_run(ctx, L, x, T, nullptr, f, nullptr, nullptr, nullptr, nullptr, nullptr, scratch, st);
+}
+
+size_t pi_moe_rows_multi_bytes(const pi_moe_layer* L, int64_t n_rows, int k, int64_t n_home) {
+    return carve_multi(L, n_rows, k, n_home, nullptr).bytes;
+}
+
+int pi_moe_rows_multi_run(pi_ctx* ctx, pi_moe_layer* L, int64_t n_rows, int k, const int8_t* xq, const float* xs,
+                          const int32_t* eid, int64_t n_home, const int8_t* xq_home, const float* xs_home, int flags,
+                          char* scratch, PiRowsOut* out, cudaStream_t st) {
+    if (L->qtype != PI_QT_Q8_0 || !L->maps_ok)
+        return pi_set_error(ctx, PI_ERR_ARG, "ep experts: Q8_0 layer of the prefill GEMM shapes");
+    const FwdBufs B = carve_multi(L, n_rows, k, n_home, scratch);
+    const int En = L->n_exp, tg = PI_GEMM_NT_Q8;
+    const int64_t n_sh = L->has_shared ? n_home : 0;
+    {
+        PiProfScope ps(ctx, st, "k_dispatch");
+        launch_dispatch(st, eid, nullptr, (int)n_rows, k, En, n_sh > 0 ? 1 : 0, B.offsets, B.perm, B.slot_of, B.items,
+                        B.n_items, tg, B.disp_cc, (int)n_sh, B.counts);
+    }
+    ExpertArgs a = expert_args(L, En, B, B.perm, 0, nullptr);
+    a.xq = xq;
+    a.xs = xs;
+    a.n_routed_dev = B.counts;
+    a.n_sh = (int)n_sh;
+    a.xq_sh = xq_home;
+    a.xs_sh = xs_home;
+    const int64_t n_slots = n_rows * k + n_sh;
+    const unsigned ni = (unsigned)(En + n_rows * k / tg + n_sh / tg + 4);
+    if (int rc = run_experts(ctx, L, a, n_rows, n_slots, ni, true, B, st, flags)) return rc;
+    out->y = B.y;
+    out->slot_of = B.slot_of;
+    out->n_routed = B.counts;
+    return pi_cuda_check(ctx, cudaGetLastError(), "ep experts") ? PI_ERR_CUDA : PI_OK;
 }

@@ -430,14 +430,24 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * PB * TN) : "memory");
 }
 
-// Gate/up activations in slot order: slot s < n_routed holds token perm[s], slot
-// n_routed + t the shared expert's token t. Q8_0 values become exact f16; the
-// block scales are copied alongside. One CTA per slot, 16 values per thread.
+// Gate/up activations in slot order: slot s < n_routed holds row perm[s], slot
+// n_routed + t (t < n_sh) the shared expert's row sh_row0 + t; CTAs past the
+// realised slots exit. Q8_0 values become exact f16; the block scales are copied
+// alongside. One CTA per slot, 16 values per thread.
 __global__ __launch_bounds__(128) void k_slot_rows(const int8_t* __restrict__ xq, const float* __restrict__ xs,
-                                                   const int32_t* __restrict__ perm, int n_routed, int d,
-                                                   __half* __restrict__ xsl, float* __restrict__ xssl) {
+                                                   const int8_t* __restrict__ xq_sh, const float* __restrict__ xs_sh,
+                                                   const int32_t* __restrict__ perm, int n_routed,
+                                                   const int32_t* __restrict__ n_routed_dev, int sh_row0, int n_sh,
+                                                   int d, __half* __restrict__ xsl, float* __restrict__ xssl) {
     const int s = blockIdx.x;
-    const int tok = s < n_routed ? perm[s] : s - n_routed;
+    if (n_routed_dev) n_routed = *n_routed_dev;
+    if (s >= n_routed + n_sh) return;
+    const bool sh = s >= n_routed;
+    const int tok = sh ? sh_row0 + s - n_routed : perm[s];
+    if (sh && xq_sh) {  // the shared expert's rows live in their own array
+        xq = xq_sh;
+        xs = xs_sh;
+    }
     const int8_t* src = xq + (size_t)tok * d;
     __half* dst = xsl + (size_t)s * d;
     for (int c = threadIdx.x; c < d / 16; c += blockDim.x) {
@@ -527,7 +537,8 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     pi_smem_attr((const void*)dn, QSMEM);
     {
         PiProfScope ps(ctx, st, "k_slot_rows");
-        k_slot_rows<<<(unsigned)n_slots, 128, 0, st>>>(a.xq, a.xs, a.perm, a.n_routed, a.d, a.xsl, a.xssl);
+        k_slot_rows<<<(unsigned)n_slots, 128, 0, st>>>(a.xq, a.xs, a.xq_sh, a.xs_sh, a.perm, a.n_routed,
+                                                       a.n_routed_dev, a.sh_row0, a.n_sh, a.d, a.xsl, a.xssl);
     }
     const int64_t sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
     {

@@ -2,24 +2,24 @@
 
 Rank r of `world` holds experts [r*P, (r+1)*P), P = E / world, plus the full
 router and the shared expert; tokens are data-parallel (each rank routes its
-own home tokens). One layer forward is
+own home tokens). The reference has no counterpart (it runs one process,
+model/mod.rs:1245-1571).
 
-  1. ``pi_moe_ep_route``   home tokens -> routing + one Q8_0 row per (token, j)
-                           slot, grouped by the slot expert's rank;
-  2. exchange              all-to-all-v of the rows (and their local expert ids);
-  3. ``pi_moe_experts_q8`` the held experts over the received rows;
-  4. exchange              all-to-all-v of the expert outputs back to the home rank;
-  5. ``pi_moe_ep_combine`` the gate-weighted sum in ascending expert order, with the
-     shared expert (``pi_moe_experts_q8`` over the home tokens), which runs on a side
-     stream from step 1 on, overlapping the exchanges and the routed experts.
+Two transports carry a layer forward:
 
-Every expert row is computed exactly as the one-GPU layer computes it and the
-combine order is the reference's, so the result equals ``MoeLayer.forward`` on
-the same tokens bit for bit, at any world size. The reference has no
-counterpart (it runs one process, model/mod.rs:1245-1571).
-
-``RowExchange`` is the transport: torch.distributed all_to_all_single (NCCL over
-NVLink on GPUs; gloo in the CPU tests of the bookkeeping).
+* ``EPComm`` (the default on GPUs): NVLink peer memory, one C call per layer
+  (``pi_moe_ep_forward``). Each home token's Q8_0 row goes once to every rank
+  holding one of its experts; the destination runs its experts over all rows it
+  received (and the shared expert over its home tokens) in one grouped GEMM,
+  sums gate x output per row and stores that one partial row back; the home rank
+  adds the partials in ascending rank order. No host synchronisation, no
+  collective library; results equal ``MoeLayer.forward`` up to the regrouping
+  of the combine sum by rank.
+* ``RowExchange``: torch.distributed all_to_all_single over the staged calls
+  ``pi_moe_ep_route`` / ``pi_moe_experts_q8`` / ``pi_moe_ep_combine`` (one row per
+  (token, expert) slot, outputs returned per slot, the combine in the
+  reference's order: bit for bit the one-GPU layer). Used when no comm is given,
+  and by the gloo tests of the exchange bookkeeping on CPU.
 """
 from __future__ import annotations
 
@@ -28,7 +28,7 @@ import ctypes as C
 import numpy as np
 
 from . import quant
-from ._lib import PI_FWD_FAST_SUM, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_Q8_0, Context, PiError, PI_ERR_ARG, PiMoeLayerDesc, lib, ptr, \
+from ._lib import PI_EP_HANDLE_BYTES, PI_FWD_FAST_SUM, PI_FWD_RESIDUAL, PI_FWD_RMSNORM, PI_QT_Q8_0, Context, PiError, PI_ERR_ARG, PiMoeLayerDesc, lib, ptr, \
     stream_ptr
 
 
@@ -77,6 +77,41 @@ class RowExchange:
         return out
 
 
+class EPComm:
+    """This rank's exchange memory for expert-parallel layers over NVLink (pi_ep_comm).
+
+    Every rank of the group builds one (collectively: the constructor exchanges the
+    exported memory handles over ``group`` with all_gather_object) and passes it to
+    each of its EPMoeLayer objects; one comm serves every layer. max_tokens bounds
+    the home tokens of one forward.
+    """
+
+    def __init__(self, rank: int, world: int, max_tokens: int, n_embd: int, top_k: int, group=None,
+                 device: int | None = None):
+        import torch.distributed as dist
+
+        self.ctx = Context.default(device)
+        self.rank, self.world, self.max_tokens = rank, world, max_tokens
+        h = C.c_void_p()
+        self.ctx.check(lib().pi_ep_comm_create(self.ctx.h, rank, world, max_tokens, n_embd, top_k, C.byref(h)))
+        self.h = h
+        buf = (C.c_char * PI_EP_HANDLE_BYTES)()
+        self.ctx.check(lib().pi_ep_comm_ipc_handle(h, buf))
+        handles = [bytes(buf)]
+        if world > 1:
+            handles = [None] * world
+            dist.all_gather_object(handles, bytes(buf), group=group)
+        allh = (C.c_char * (PI_EP_HANDLE_BYTES * world)).from_buffer_copy(b"".join(handles))
+        self.ctx.check(lib().pi_ep_comm_open(h, allh))
+
+    def __del__(self):
+        try:
+            if getattr(self, "h", None):
+                lib().pi_ep_comm_destroy(self.h)
+        except Exception:
+            pass
+
+
 class EPMoeLayer:
     """One MoE layer sharded by experts over `world` ranks (Q8_0 experts).
 
@@ -86,7 +121,7 @@ class EPMoeLayer:
 
     def __init__(self, router, gate_exps, up_exps, down_exps, n_embd: int, n_ff: int, n_expert: int, top_k: int,
                  rank: int, world: int, shared=None, router_bias=None, exchange: RowExchange | None = None,
-                 device: int | None = None):
+                 device: int | None = None, comm: EPComm | None = None):
         torch = _torch()
         if n_expert % world:
             raise PiError(PI_ERR_ARG, "n_expert must be a multiple of the world size")
@@ -95,6 +130,7 @@ class EPMoeLayer:
         self.rank, self.world, self.P = rank, world, n_expert // world
         self.has_shared = shared is not None
         self.exchange = exchange or RowExchange()
+        self.comm = comm  # NVLink data plane (pi_moe_ep_forward); None: the all-to-all exchange
         keep = []
 
         def dev(a, dt):
@@ -135,6 +171,11 @@ class EPMoeLayer:
             out = torch.empty((T, d), dtype=torch.float32, device="cuda")
         flags = (PI_FWD_RMSNORM if rmsnorm else 0) | (PI_FWD_RESIDUAL if residual else 0)
         flags |= PI_FWD_FAST_SUM if fast else 0
+        if self.comm is not None:
+            if T > self.comm.max_tokens:
+                raise PiError(PI_ERR_ARG, "more home tokens than the comm's max_tokens")
+            self.ctx.check(L.pi_moe_ep_forward(self.ctx.h, self.h, self.comm.h, ptr(xd), T, ptr(out), flags, s))
+            return out
         if self.world == 1:
             # one rank holds every expert: nothing to exchange, the fused layer forward
             # (routed and shared experts in the same grouped launches) is the whole step

@@ -34,13 +34,15 @@ class HostPipeline:
         self.in_ready, self.done, self.copied = ev(), ev(), ev()
         self.n = 0  # batches issued so far (buffer reuse is ordered across run() calls)
 
-    def run(self, xs_host, outs_host):
-        """Issues every batch; returns when all are queued. ``outs_host`` are valid
-        after ``torch.cuda.current_stream().synchronize()`` (the compute stream
-        waits for the last device->host copy)."""
+    def run(self, xs_host, outs_host, layers=None):
+        """Issues every batch (batch i through ``layers[i]`` when given, else the
+        pipeline's layer); returns when all are queued. ``outs_host`` are valid
+        after ``finish()`` and a synchronisation of the compute stream."""
         torch = _torch()
         comp = torch.cuda.current_stream()
-        for xh, oh in zip(xs_host, outs_host):
+        for k, (xh, oh) in enumerate(zip(xs_host, outs_host)):
+            if layers is not None:
+                self.layer = layers[k]
             i, s = self.n, self.n % self.depth
             with torch.cuda.stream(self.h2d):
                 if i >= self.depth:
@@ -57,5 +59,8 @@ class HostPipeline:
                 oh.copy_(self.yout[s], non_blocking=True)
                 self.copied[s].record(self.d2h)
             self.n += 1
-        comp.wait_stream(self.d2h)
         return outs_host
+
+    def finish(self):
+        """Makes the compute stream wait for every device->host copy issued so far."""
+        _torch().cuda.current_stream().wait_stream(self.d2h)
