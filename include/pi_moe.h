@@ -285,6 +285,20 @@ int pi_ep_comm_debug_skip(pi_ep_comm* comm, int32_t n);
 int pi_router_topk_softmax(pi_ctx* ctx, const float* x, int64_t T, const float* router, int64_t d, int32_t E,
                            int32_t k, int32_t* idx, float* weights, void* stream);
 
+/* ---- device hot-neuron lists (CSR) for the sparse FFN ------------------
+ * Predictor::predict_hot (src/predictor/mod.rs:87-95) turned into the lists the
+ * sparse FFN takes, on the device: for token t the blocks b with
+ * probs[t][b] >= threshold, ascending, block b = neurons [b*block, (b+1)*block)
+ * clipped to n_ff (the predictor's output is blocks of 64 neurons,
+ * src/predictor/mod.rs:15). ptr [T+1], idx int64 with room for T * n_ff. */
+int pi_hot_lists_from_probs(pi_ctx* ctx, const float* probs, int64_t T, int64_t n_blocks, float threshold,
+                            int64_t block, int64_t n_ff, int64_t* ptr, int64_t* idx, void* stream);
+/* One static hot list (a HotNeuronIndex layer after Model::set_hot_index's sort
+ * and dedup, src/model/mod.rs:1743-1761) for each of T tokens: ptr [T+1],
+ * idx [T*n]. */
+int pi_hot_lists_broadcast(pi_ctx* ctx, const int64_t* list, int64_t n, int64_t T, int64_t* ptr, int64_t* idx,
+                           void* stream);
+
 /* ---- hot-neuron sparse dense FFN --------------------------------------- */
 
 /* Dense SwiGLU FFN weights for the sparse path (model/mod.rs:1573-1612):

@@ -80,6 +80,8 @@ SIGNATURES = {
     "pi_sparse_ffn_destroy": (None, [_P]),
     "pi_sparse_ffn_forward": (_INT, [_P, _P, _P, _I64, _P, _P, _P, _P]),
     "pi_predictor_forward": (_INT, [_P, _P, _I64, _P, _P, _P, _P, _I64, _I64, _I64, _P, _P]),
+    "pi_hot_lists_from_probs": (_INT, [_P, _P, _I64, _I64, C.c_float, _I64, _I64, _P, _P, _P]),
+    "pi_hot_lists_broadcast": (_INT, [_P, _P, _I64, _I64, _P, _P, _P]),
     "pi_synth_normal": (_INT, [_P, C.c_uint64, C.c_uint64, _I64, C.c_float, _P, _P]),
     "pi_synth_normal_host": (_INT, [C.c_uint64, C.c_uint64, _I64, C.c_float, _P]),
 }

@@ -994,6 +994,80 @@ extern "C" int pi_predictor_forward(pi_ctx* ctx, const float* a, int64_t T, cons
     return PI_OK;
 }
 
+// --------------------------------------------------------------------------
+// Device hot-neuron lists for the sparse FFN (CSR: ptr [T+1], idx ascending per token).
+//   from predictor probabilities: Predictor::predict_hot (predictor/mod.rs:87-95,
+//   blocks with p >= threshold, ascending) with block b covering neurons
+//   [b * block, (b + 1) * block) of n_ff (predictor/mod.rs:15: blocks of 64);
+//   from a static list (a HotNeuronIndex layer, model/mod.rs:1743-1761): the same
+//   list for every token.
+// One CTA walks the tokens in order and keeps the running offset.
+// --------------------------------------------------------------------------
+__global__ __launch_bounds__(1024) void k_hot_from_probs(const float* __restrict__ probs, int T, int n_blocks,
+                                                         float threshold, int block, int64_t n_ff,
+                                                         int64_t* __restrict__ ptr, int64_t* __restrict__ idx) {
+    __shared__ int64_t s_scan[1024];
+    __shared__ int64_t s_base;
+    if (threadIdx.x == 0) {
+        s_base = 0;
+        ptr[0] = 0;
+    }
+    __syncthreads();
+    for (int t = 0; t < T; ++t) {
+        for (int b0 = 0; b0 < n_blocks; b0 += 1024) {
+            const int b = b0 + threadIdx.x;
+            int64_t n = 0;
+            if (b < n_blocks) {
+                const float p = probs[(size_t)t * n_blocks + b];
+                const int64_t lo = (int64_t)b * block, hi = min((int64_t)(b + 1) * block, n_ff);
+                if (p >= threshold && lo < hi) n = hi - lo;
+            }
+            s_scan[threadIdx.x] = n;
+            __syncthreads();
+            for (int o = 1; o < 1024; o <<= 1) {  // inclusive scan of the blocks' neuron counts
+                const int64_t v = threadIdx.x >= (unsigned)o ? s_scan[threadIdx.x - o] : 0;
+                __syncthreads();
+                s_scan[threadIdx.x] += v;
+                __syncthreads();
+            }
+            const int64_t at = s_base + s_scan[threadIdx.x] - n;
+            for (int64_t j = 0; j < n; ++j) idx[at + j] = (int64_t)b * block + j;
+            __syncthreads();
+            if (threadIdx.x == 0) s_base += s_scan[1023];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) ptr[t + 1] = s_base;
+    }
+}
+
+__global__ void k_hot_broadcast(const int64_t* __restrict__ list, int64_t n, int T, int64_t* __restrict__ ptr,
+                                int64_t* __restrict__ idx) {
+    const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    if (i <= T) ptr[i] = i * n;
+    if (i < (int64_t)T * n) idx[i] = list[i % n];
+}
+
+extern "C" int pi_hot_lists_from_probs(pi_ctx* ctx, const float* probs, int64_t T, int64_t n_blocks, float threshold,
+                                       int64_t block, int64_t n_ff, int64_t* ptr, int64_t* idx, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (T < 0 || T > (1 << 20) || n_blocks < 1 || block < 1 || n_ff < 1 || !ptr || (T > 0 && (!probs || !idx)))
+        return pi_set_error(ctx, PI_ERR_ARG, "hot lists: bad sizes or pointers");
+    k_hot_from_probs<<<1, 1024, 0, ST(stream)>>>(probs, (int)T, (int)n_blocks, threshold, (int)block, n_ff, ptr, idx);
+    LAUNCH_CHECK("hot lists");
+    return PI_OK;
+}
+
+extern "C" int pi_hot_lists_broadcast(pi_ctx* ctx, const int64_t* list, int64_t n, int64_t T, int64_t* ptr,
+                                      int64_t* idx, void* stream) {
+    if (!ctx) return PI_ERR_ARG;
+    if (T < 0 || T > (1 << 20) || n < 0 || !ptr || (n > 0 && T > 0 && (!list || !idx)))
+        return pi_set_error(ctx, PI_ERR_ARG, "hot lists: bad sizes or pointers");
+    const int64_t m = std::max<int64_t>(T * n, T + 1);
+    k_hot_broadcast<<<nblocks(m, 256), 256, 0, ST(stream)>>>(list, n, (int)T, ptr, idx);
+    LAUNCH_CHECK("hot lists");
+    return PI_OK;
+}
+
 extern "C" int pi_synth_normal(pi_ctx* ctx, uint64_t seed, uint64_t offset, int64_t n, float stdv, float* out,
                                void* stream) {
     if (!ctx) return PI_ERR_ARG;

@@ -7,7 +7,12 @@
   (quant::ffn_swiglu_q_selected per token) on the GPU, with weights repacked
   once (down projection neuron-major).
 * ``blocks_to_indices`` expands predictor block ids to the neuron index list
-  the sparse FFN takes (64 neurons per block).
+  the sparse FFN takes (64 neurons per block); ``hot_lists_from_probs`` does the
+  same on the device for a batch, and ``SparseFFN.forward_predicted`` chains
+  predictor probabilities -> lists -> sparse FFN without leaving the device.
+* ``HotNeuronIndex`` — activation/mod.rs:246-325, the profiler's per-layer hot
+  lists, applied as Model::set_hot_index does (model/mod.rs:1743-1802);
+  ``SparseFFN.forward_hot`` runs one static list for every token.
 """
 from __future__ import annotations
 
@@ -135,3 +140,115 @@ class SparseFFN:
         self.ctx.check(lib().pi_sparse_ffn_forward(self.ctx.h, self.h, ptr(xd), T, ptr(csr[0]), ptr(csr[1]), ptr(out),
                                                    stream_ptr(stream)))
         return out
+
+
+# --------------------------------------------------------------------------
+# Hot-neuron lists on the device
+# --------------------------------------------------------------------------
+def hot_lists_from_probs(probs, threshold: float, n_ff: int, block: int = 64, stream=None):
+    """Predictor::predict_hot (predictor/mod.rs:87-95) for every token of a device
+    probability matrix [T, n_blocks], expanded to neuron ids (block b = neurons
+    [b*block, (b+1)*block) below n_ff), as device CSR (ptr [T+1], idx) int64."""
+    torch = _torch()
+    p = quant._f32(probs)
+    T, nb = (p.shape[0], p.shape[1]) if p.dim() == 2 else (1, p.numel())
+    ptr_ = torch.empty(T + 1, dtype=torch.int64, device=p.device)
+    idx = torch.empty(max(T * n_ff, 1), dtype=torch.int64, device=p.device)
+    ctx = Context.default()
+    ctx.check(lib().pi_hot_lists_from_probs(ctx.h, ptr(p), T, nb, float(threshold), block, n_ff, ptr(ptr_), ptr(idx),
+                                            stream_ptr(stream)))
+    return ptr_, idx
+
+
+def hot_lists_broadcast(hot_list, T: int, stream=None):
+    """One static hot list for each of T tokens, as device CSR (ptr, idx)."""
+    torch = _torch()
+    lst = torch.as_tensor(np.asarray(hot_list, np.int64)).cuda()
+    n = lst.numel()
+    ptr_ = torch.empty(T + 1, dtype=torch.int64, device="cuda")
+    idx = torch.empty(max(T * n, 1), dtype=torch.int64, device="cuda")
+    ctx = Context.default()
+    ctx.check(lib().pi_hot_lists_broadcast(ctx.h, ptr(lst), n, T, ptr(ptr_), ptr(idx), stream_ptr(stream)))
+    return ptr_, idx
+
+
+class HotNeuronIndex:
+    """activation/mod.rs:246-330: per-layer hot neuron lists (JSON), loaded the way
+    Model::set_hot_index does (model/mod.rs:1743-1761): each list sorted and
+    de-duplicated, then validated against the model's layer widths."""
+
+    def __init__(self, version: int, threshold: float, min_hotness: float, total_samples: int, layers: list):
+        self.version, self.threshold, self.min_hotness, self.total_samples = version, threshold, min_hotness, \
+            total_samples
+        self.layers = [dict(layer_idx=int(l["layer_idx"]), hot_indices=sorted(set(int(i) for i in l["hot_indices"])),
+                            n_ff=int(l["n_ff"])) for l in layers]
+
+    @classmethod
+    def load(cls, path) -> "HotNeuronIndex":
+        import json
+        from pathlib import Path
+
+        d = json.loads(Path(path).read_text())
+        return cls(d["version"], d["threshold"], d["min_hotness"], d["total_samples"], d["layers"])
+
+    def save(self, path) -> None:
+        import json
+        from pathlib import Path
+
+        Path(path).parent.mkdir(parents=True, exist_ok=True)
+        Path(path).write_text(json.dumps(dict(version=self.version, threshold=self.threshold,
+                                              min_hotness=self.min_hotness, total_samples=self.total_samples,
+                                              layers=self.layers), indent=2))
+
+    def layer(self, layer_idx: int):
+        """The entry of `layer_idx` or None (activation/mod.rs:265-270)."""
+        return next((l for l in self.layers if l["layer_idx"] == layer_idx), None)
+
+    def validate_against_dims(self, layer_dims) -> None:
+        """activation/mod.rs:287-325: every entry names a layer of the model once, with
+        the model's width and indices inside it."""
+        seen = [False] * len(layer_dims)
+        for l in self.layers:
+            li = l["layer_idx"]
+            if li >= len(layer_dims):
+                raise PiError(PI_ERR_ARG, f"hot index layer {li} is out of range for model with {len(layer_dims)} layers")
+            if seen[li]:
+                raise PiError(PI_ERR_ARG, f"hot index contains duplicate entries for layer {li}")
+            seen[li] = True
+            if l["n_ff"] != layer_dims[li]:
+                raise PiError(PI_ERR_ARG, f"hot index layer {li} expects width {l['n_ff']}, but model layer width is "
+                                          f"{layer_dims[li]}")
+            bad = [i for i in l["hot_indices"] if i >= l["n_ff"]]
+            if bad:
+                raise PiError(PI_ERR_ARG, f"hot index layer {li} contains out-of-range index {bad[0]} for width "
+                                          f"{l['n_ff']}")
+
+    def sparse_hot_indices(self, layer_idx: int, dense_width: int):
+        """model/mod.rs:1799-1802: the layer's list when it is narrower than the dense
+        width, else None (the dense path)."""
+        l = self.layer(layer_idx)
+        if l is None or len(l["hot_indices"]) >= dense_width:
+            return None
+        return l["hot_indices"]
+
+
+def _sparse_forward_predicted(self, x, probs, threshold: float, block: int = 64, out=None, stream=None):
+    """The FFN over the neurons the predictor marks hot for each token: device
+    probabilities [T, n_blocks] -> device CSR lists -> the sparse FFN, with no
+    host round trip."""
+    csr = hot_lists_from_probs(probs, threshold, self.n_ff, block, stream=stream)
+    return self.forward(x, csr=csr, out=out, stream=stream)
+
+
+def _sparse_forward_hot(self, x, hot_list, out=None, stream=None):
+    """The FFN over one static hot list for every token (a HotNeuronIndex layer)."""
+    xd = quant._f32(x)
+    T = xd.numel() // self.n_embd
+    lst = np.asarray(hot_list, np.int64)
+    if lst.size and (lst.min() < 0 or lst.max() >= self.n_ff):
+        raise PiError(2, "hot index out of range for the FFN width")
+    return self.forward(xd, csr=hot_lists_broadcast(lst, T, stream=stream), out=out, stream=stream)
+
+
+SparseFFN.forward_predicted = _sparse_forward_predicted
+SparseFFN.forward_hot = _sparse_forward_hot

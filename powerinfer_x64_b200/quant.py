@@ -61,6 +61,8 @@ def _dev(a, dtype):
     if isinstance(a, (bytes, bytearray, memoryview)):
         a = np.frombuffer(a, dtype=np.uint8)
     arr = np.ascontiguousarray(np.asarray(a, dtype=dtype))
+    if not arr.flags.writeable:  # e.g. a window of a read-only memory map: upload a copy
+        arr = arr.copy()
     return torch.from_numpy(arr).cuda()
 
 
