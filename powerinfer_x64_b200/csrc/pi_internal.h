@@ -78,6 +78,7 @@ struct pi_sparse_ffn {
     //   Q8_0: q [n_ff][n_embd] int8, same scale layout
     void* down_q = nullptr;
     __half* down_d = nullptr;
+    uint8_t* mask = nullptr;  // [n_ff] token bits of the current pass, zero between passes
     std::vector<void*> allocs;
 };
 

@@ -276,323 +276,289 @@ __global__ void k_pred_layer(const float* __restrict__ in, int64_t T, int64_t n_
 // Hot-neuron sparse FFN (C-ABI pi_sparse_ffn_*).
 // --------------------------------------------------------------------------
 constexpr int SF_TMAX = 8;             // tokens per pass (one byte of mask bits per neuron)
-constexpr int SF_GPC = 2;              // 32-neuron groups per down CTA
-constexpr int64_t SF_MAX_FF = 131072;  // the pass plan keeps a byte per neuron in shared memory
+constexpr int64_t SF_MAX_FF = 131072;  // neurons a layer may have
+constexpr int SF_GU_WARPS = 16;        // warps of a gate/up CTA (one CTA per SM)
 
-// Pass plan (one CTA of 1024 threads) for tokens t0 .. t0+nt-1 of the CSR index
-// lists: mask[s] bit t = neuron s active for token t0+t (one byte per neuron);
-// list[0 .. n) = the active neurons in ascending order; gofs[g] = list position of
-// the first active neuron of 32-neuron group g, gofs[n_ff / 32] = n. A token whose
-// list covers all n_ff neurons takes every neuron (quant/mod.rs:1221-1223). The
-// pass's output rows are zeroed here for the down kernel's atomics.
-__global__ __launch_bounds__(1024) void k_sf_plan(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
-                                                  int t0, int nt, int64_t n_ff, int64_t n_embd, uint8_t* __restrict__ mask,
-                                                  int32_t* __restrict__ list, int32_t* __restrict__ gofs,
-                                                  float* __restrict__ out, uint32_t* err) {
-    extern __shared__ uint32_t sf_sm[];
-    __shared__ int32_t wsum[32];
-    __shared__ int64_t s_ptr[SF_TMAX + 1];
-    const int ng = (int)(n_ff / 32);
-    uint32_t* bits = sf_sm;  // byte s = token bits of neuron s
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    if (tid <= nt) s_ptr[tid] = ptr[t0 + tid];
-    for (int i = tid; i < n_ff / 4; i += 1024) bits[i] = 0;
-    float4* o4 = reinterpret_cast<float4*>(out + (int64_t)t0 * n_embd);
-    for (int64_t i = tid; i < nt * n_embd / 4; i += 1024) o4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    __syncthreads();
-    uint32_t dense = 0;  // token bits of the complete lists, in every byte
+// Tokens t of the pass whose list covers all n_ff neurons take every neuron
+// (quant/mod.rs:1221-1223): their bits, one per token.
+PI_DEV uint32_t sf_dense_bits(const int64_t* __restrict__ ptr, int t0, int nt, int64_t n_ff) {
+    uint32_t dense = 0;
     for (int t = 0; t < nt; ++t)
-        if (s_ptr[t + 1] - s_ptr[t] >= n_ff) dense |= 0x01010101u << t;
-    // every token's entries at once, four loads in flight per thread
-    for (int64_t q0 = s_ptr[0] + tid; q0 < s_ptr[nt]; q0 += 4 * 1024) {
-        int64_t sv[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t q = q0 + u * 1024;
-            sv[u] = q < s_ptr[nt] ? __ldg(idx + q) : -1;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            const int64_t q = q0 + u * 1024;
-            if (q >= s_ptr[nt]) break;
-            int t = 0;
-            while (q >= s_ptr[t + 1]) ++t;
-            if ((dense >> t) & 1u) continue;
-            const int64_t s = sv[u];
-            if (s < 0 || s >= n_ff) { atomicOr(err, PI_DEVERR_INDEX); continue; }
-            atomicOr(&bits[s >> 2], 1u << (8 * (s & 3) + t));
-        }
-    }
-    __syncthreads();
-    int carry = 0;  // thread per group: 32 mask bytes -> count -> exclusive scan -> list
-    for (int g0 = 0; g0 < ng; g0 += 1024) {
-        const int g = g0 + tid;
-        uint4 w0 = make_uint4(0, 0, 0, 0), w1 = w0;
-        uint32_t act = 0;
-        if (g < ng) {
-            w0 = *reinterpret_cast<const uint4*>(bits + 8 * g);
-            w1 = *reinterpret_cast<const uint4*>(bits + 8 * g + 4);
-            const uint32_t w[8] = {w0.x | dense, w0.y | dense, w0.z | dense, w0.w | dense,
-                                   w1.x | dense, w1.y | dense, w1.z | dense, w1.w | dense};
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-                const uint32_t nz = __vcmpne4(w[k], 0u);  // 0xff per active neuron
-                act |= ((nz & 1u) | ((nz >> 7) & 2u) | ((nz >> 14) & 4u) | ((nz >> 21) & 8u)) << (4 * k);
-            }
-            uint4* m4 = reinterpret_cast<uint4*>(mask + 32 * (int64_t)g);
-            m4[0] = make_uint4(w[0], w[1], w[2], w[3]);
-            m4[1] = make_uint4(w[4], w[5], w[6], w[7]);
-        }
-        const int v = __popc(act);
-        int x = v;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const int y = __shfl_up_sync(0xffffffffu, x, o);
-            if (lane >= o) x += y;
-        }
-        if (lane == 31) wsum[warp] = x;
-        __syncthreads();
-        if (warp == 0) {
-            int z = wsum[lane];
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int y = __shfl_up_sync(0xffffffffu, z, o);
-                if (lane >= o) z += y;
-            }
-            wsum[lane] = z;
-        }
-        __syncthreads();
-        if (g < ng) {
-            int pos = carry + (warp ? wsum[warp - 1] : 0) + x - v;
-            gofs[g] = pos;
-            for (uint32_t a = act; a; a &= a - 1) list[pos++] = 32 * g + __ffs(a) - 1;
-        }
-        carry += wsum[31];
-        __syncthreads();
-    }
-    if (tid == 0) gofs[ng] = carry;
+        if (ptr[t0 + t + 1] - ptr[t0 + t] >= n_ff) dense |= 1u << t;
+    return dense;
 }
 
-// gate/up for masked neurons: warp per neuron, BPL blocks per lane
-// (n_embd = 32 * 32 * BPL). Q4_0 (f32 x) and Q8_0 (quantised x) variants.
+// Marks the pass's (token, neuron) pairs: bit t of mask byte s = neuron s in token
+// t0 + t's list, and zeroes h of the pass. The mask starts zero and the gate/up
+// kernel clears every byte it claims, so it is zero again for the next pass.
+__global__ __launch_bounds__(256) void k_sf_mark(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
+                                                 int t0, int nt, int64_t n_ff, uint32_t* __restrict__ mask32,
+                                                 float* __restrict__ h, uint32_t* __restrict__ err) {
+    int64_t bnd[SF_TMAX + 1];
+#pragma unroll
+    for (int t = 0; t <= SF_TMAX; ++t) bnd[t] = t <= nt ? ptr[t0 + t] : 0;
+    const int64_t gid = blockIdx.x * (int64_t)blockDim.x + threadIdx.x, gsz = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = gid; i < nt * n_ff / 4; i += gsz) reinterpret_cast<float4*>(h)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t e = bnd[0] + gid; e < bnd[nt]; e += gsz) {
+        int t = 0;
+        while (e >= bnd[t + 1]) ++t;
+        const int64_t sn = idx[e];
+        if (sn < 0 || sn >= n_ff) {
+            atomicOr(err, PI_DEVERR_INDEX);
+            continue;
+        }
+        atomicOr(&mask32[sn >> 2], 1u << (8 * (sn & 3) + t));
+    }
+}
+
 PI_DEV float nibf(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616.0f; }
-// gate and up blocks against the same 32 activations (one pass over x)
-PI_DEV void q4dot16x2(const int4 wg, const int4 wu, const float* __restrict__ x, float& sg, float& su) {
-    uint32_t g0 = wg.x, g1 = wg.y, g2 = wg.z, g3 = wg.w, u0 = wu.x, u1 = wu.y, u2 = wu.z, u3 = wu.w;
-    sg = 0.f;
-    su = 0.f;
-#pragma unroll 1
-    for (int i = 0; i < 4; ++i) {  // rolled (register pressure): word i of each block is g0 / u0
-        const float4 xa = *reinterpret_cast<const float4*>(x + 8 * i);
-        const float4 xb = *reinterpret_cast<const float4*>(x + 8 * i + 4);
-        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            sg += nibf((g0 >> (4 * j)) & 15u) * xv[j];
-            su += nibf((u0 >> (4 * j)) & 15u) * xv[j];
-        }
-        g0 = g1; g1 = g2; g2 = g3;
-        u0 = u1; u1 = u2; u2 = u3;
-    }
-}
-
-// gate/up for the pass's active neurons: CTA = SF_NPC list entries, one warp per
-// (entry, chunk of the row); the chunks' partial dots are summed in chunk order and
-// the first SF_NPC threads write (g, u).
-// Q4_0: chunk = 32 blocks (1024 inputs) and each token's f32 activations are staged
-// in shared memory with 32-float blocks 36 floats apart, so the lanes' float4 reads
-// (lane = block) fall in distinct banks. Q8_0: chunk = 512 inputs of the quantised
-// activations (lane = 16 bytes, two lanes per block).
-constexpr int SF_NPC = 4;
-PI_DEV void sf_finish(const float2 (*part)[8], int nch, const int* s_s, const uint8_t* s_m, int t, int64_t n_ff,
-                      float2* __restrict__ gu) {
-    const int n = threadIdx.x;
-    if (n < SF_NPC && ((s_m[n] >> t) & 1u)) {
-        float g = 0.f, u = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            g += part[n][c].x;
-            u += part[n][c].y;
-        }
-        gu[(int64_t)t * n_ff + s_s[n]] = make_float2(g, u);
-    }
-}
-
-template <int BPL>
-__global__ __launch_bounds__(SF_NPC * BPL * 32) void k_sf_gateup_q4(
+// gate/up of every marked (token, neuron) pair, h = SwiGLU(g, u) (quant/mod.rs:1196-1199)
+// into h[t][n] (0 where the pair is not marked); the pass's output rows are zeroed
+// for the down kernel's atomics. Persistent: one CTA per SM stages the pass's
+// activations once; warp w walks neurons w, w + W, ... and streams each marked
+// neuron's gate and up rows once for all of its tokens.
+// Q4_0: x f32, staged with 32-float blocks 36 floats apart (lane l reads blocks
+// l + 32 j with float4 loads in distinct banks); the reference dequantises the
+// whole matrix and sums in f32 (quant/mod.rs:958-969).
+// Q8_0: x quantised to Q8_0 (quant/mod.rs:698-736), int8 block dots, block terms
+// (float)sumi * (d_w * d_x) (quant/mod.rs:819-899).
+template <int QT, int BPL>  // BPL: blocks per lane (n_embd = 32 * 32 * BPL)
+__global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
     const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
-    const __half* __restrict__ UD, const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
-    const int32_t* __restrict__ n_list, const float* __restrict__ x, int t0, int nt, int64_t n_embd, int64_t n_ff,
-    float2* __restrict__ gu) {
-    __shared__ __align__(16) float xsm[BPL * 32 * 36];
-    __shared__ float2 part[SF_NPC][8];
-    __shared__ int s_s[SF_NPC];
-    __shared__ uint8_t s_m[SF_NPC];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = warp / BPL, c = warp % BPL;
-    const int n_act = *n_list;
-    if (blockIdx.x * (int64_t)SF_NPC >= n_act) return;  // whole CTA
-    const int64_t li = blockIdx.x * (int64_t)SF_NPC + nw;
-    const int64_t nb = n_embd / 32, b = lane + 32 * c;
-    uint32_t m = 0;
-    int64_t s = 0;
-    int4 wg = make_int4(0, 0, 0, 0), wu = wg;
-    float sg = 0.f, su = 0.f;
-    if (li < n_act) {
-        s = list[li];
-        m = mask[s];
-        wg = ld_stream(G + s * (n_embd / 2) + b * 16);
-        wu = ld_stream(U + s * (n_embd / 2) + b * 16);
-        sg = __half2float(GD[s * nb + b]);
-        su = __half2float(UD[s * nb + b]);
-    }
-    if (c == 0 && lane == 0) {
-        s_s[nw] = (int)s;
-        s_m[nw] = (uint8_t)m;
-    }
-    for (int t = 0; t < nt; ++t) {
-        if (!__syncthreads_or((m >> t) & 1u)) continue;  // also: the previous token is finished
-        const float4* xr = reinterpret_cast<const float4*>(x + (int64_t)(t0 + t) * n_embd);
-        for (int k = threadIdx.x; k < BPL * 256; k += SF_NPC * BPL * 32)
-            *reinterpret_cast<float4*>(&xsm[36 * (k >> 3) + 4 * (k & 7)]) = xr[k];
-        __syncthreads();
-        if ((m >> t) & 1u) {
-            float dg, du;
-            q4dot16x2(wg, wu, xsm + 36 * b, dg, du);
-            dg = warp_sum(sg * dg);
-            du = warp_sum(su * du);
-            if (lane == 0) part[nw][c] = make_float2(dg, du);
+    const __half* __restrict__ UD, uint8_t* __restrict__ mask, const float* __restrict__ x,
+    const int8_t* __restrict__ xq, const float* __restrict__ xs, const int64_t* __restrict__ ptr,
+    const int64_t* __restrict__ idx, int t0, int nt, int64_t n_ff, float* __restrict__ h, float* __restrict__ y) {
+    extern __shared__ __align__(16) float sf_x[];
+    constexpr int NB = 32 * BPL;  // blocks per row
+    constexpr int64_t D = 32 * NB;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    // stage the pass's activations; zero its output rows
+    if (QT == PI_QT_Q4_0) {
+        for (int k = tid; k < nt * (int)D / 4; k += blockDim.x) {
+            const int t = k / ((int)D / 4), r = k % ((int)D / 4);
+            const float4 v = reinterpret_cast<const float4*>(x + (int64_t)(t0 + t) * D)[r];
+            *reinterpret_cast<float4*>(&sf_x[(size_t)t * NB * 36 + 36 * (r >> 3) + 4 * (r & 7)]) = v;
         }
-        __syncthreads();
-        sf_finish(part, BPL, s_s, s_m, t, n_ff, gu);
+    } else {
+        int8_t* s8 = reinterpret_cast<int8_t*>(sf_x);
+        float* ssc = sf_x + nt * D / 4;
+        for (int k = tid; k < nt * (int)D / 16; k += blockDim.x)
+            reinterpret_cast<int4*>(s8)[k] = reinterpret_cast<const int4*>(xq + (int64_t)t0 * D)[k];
+        for (int k = tid; k < nt * NB; k += blockDim.x) ssc[k] = xs[(int64_t)t0 * NB + k];
     }
-}
-
-template <int CPL>
-__global__ __launch_bounds__(2 * CPL * 32) void k_sf_gateup_q8(
-    const int8_t* __restrict__ G, const int8_t* __restrict__ U, const __half* __restrict__ GD,
-    const __half* __restrict__ UD, const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
-    const int32_t* __restrict__ n_list, const int8_t* __restrict__ xq, const float* __restrict__ xs, int t0, int nt,
-    int64_t n_embd, int64_t n_ff, float2* __restrict__ gu) {
-    constexpr int NPC = 2;  // list entries per CTA (CPL warps each)
-    __shared__ float2 part[SF_NPC][8];
-    __shared__ int s_s[SF_NPC];
-    __shared__ uint8_t s_m[SF_NPC];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nw = warp / CPL, c = warp % CPL;
-    const int n_act = *n_list;
-    if (blockIdx.x * (int64_t)NPC >= n_act) return;
-    const int64_t li = blockIdx.x * (int64_t)NPC + nw;
-    const int64_t nb = n_embd / 32, ch = lane + 32 * c;
-    uint32_t m = 0;
-    int64_t s = 0;
-    int4 wg = make_int4(0, 0, 0, 0), wu = wg;
-    float sg = 0.f, su = 0.f;
-    if (li < n_act) {
-        s = list[li];
-        m = mask[s];
-        wg = ld_stream(G + s * n_embd + ch * 16);
-        wu = ld_stream(U + s * n_embd + ch * 16);
-        sg = __half2float(GD[s * nb + (ch >> 1)]);
-        su = __half2float(UD[s * nb + (ch >> 1)]);
+    {
+        float4* o4 = reinterpret_cast<float4*>(y + (int64_t)t0 * D);
+        for (int64_t k = blockIdx.x * (int64_t)blockDim.x + tid; k < nt * D / 4; k += (int64_t)gridDim.x * blockDim.x)
+            o4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    if (threadIdx.x < SF_NPC) s_m[threadIdx.x] = 0;
+    const uint32_t dense = sf_dense_bits(ptr, t0, nt, n_ff);
     __syncthreads();
-    if (c == 0 && lane == 0) {
-        s_s[nw] = (int)s;
-        s_m[nw] = (uint8_t)m;
-    }
-    for (int t = 0; t < nt; ++t) {
-        if ((m >> t) & 1u) {
-            const int4 xv = *reinterpret_cast<const int4*>(xq + (int64_t)(t0 + t) * n_embd + ch * 16);
-            const float sx = (lane & 1) == 0 ? xs[(int64_t)(t0 + t) * nb + (ch >> 1)] : 0.f;
-            int a = dp4a(wg.x, xv.x, 0);
-            a = dp4a(wg.y, xv.y, a);
-            a = dp4a(wg.z, xv.z, a);
-            a = dp4a(wg.w, xv.w, a);
-            int bb = dp4a(wu.x, xv.x, 0);
-            bb = dp4a(wu.y, xv.y, bb);
-            bb = dp4a(wu.z, xv.z, bb);
-            bb = dp4a(wu.w, xv.w, bb);
-            a += __shfl_xor_sync(0xffffffffu, a, 1);
-            bb += __shfl_xor_sync(0xffffffffu, bb, 1);
-            const float dg = warp_sum((float)a * (sg * sx)), du = warp_sum((float)bb * (su * sx));
-            if (lane == 0) part[nw][c] = make_float2(dg, du);
+    const int64_t W = (int64_t)gridDim.x * SF_GU_WARPS;
+    constexpr int WPB = QT == PI_QT_Q4_0 ? 1 : 2;  // 16-byte words per block
+    // Work: without a complete list in the pass, the list entries (e = e0 + i W over
+    // every token's list), each claiming its neuron's mask byte (the first claim of a
+    // neuron gets its token bits and runs it; later ones get 0); with a complete list,
+    // every neuron n = n0 + i W. 32 items at a time: lane i takes item i, then the warp
+    // runs the claimed neurons one after another.
+    const int64_t e0 = ptr[t0], e1 = ptr[t0 + nt];
+    const int64_t n_items = dense ? n_ff : e1 - e0;
+    uint32_t* mask32 = reinterpret_cast<uint32_t*>(mask);
+    for (int64_t i0 = blockIdx.x * (int64_t)SF_GU_WARPS + warp; i0 < n_items; i0 += 32 * W) {
+        const int64_t ii = i0 + lane * W;
+        uint32_t mi = 0;
+        int64_t ni = 0;
+        if (ii < n_items) {
+            if (dense) {
+                ni = ii;
+                mi = (mask[ni] | dense) & ((1u << nt) - 1u);
+                mask[ni] = 0;
+            } else {
+                ni = idx[e0 + ii];
+                if (ni >= 0 && ni < n_ff) {
+                    const int sh = 8 * (int)(ni & 3);
+                    mi = (atomicAnd(&mask32[ni >> 2], ~(0xFFu << sh)) >> sh) & 0xFFu;
+                }
+            }
         }
-        __syncthreads();
-        sf_finish(part, CPL, s_s, s_m, t, n_ff, gu);
-        __syncthreads();
+        uint32_t act = __ballot_sync(0xffffffffu, mi != 0);
+        int4 wg[BPL][WPB], wu[BPL][WPB];
+        float dg[BPL], du[BPL];
+        auto load = [&](int64_t n) {
+#pragma unroll
+            for (int j = 0; j < BPL; ++j) {
+                const int b = lane + 32 * j;
+#pragma unroll
+                for (int k = 0; k < WPB; ++k) {
+                    wg[j][k] = ld_stream(G + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
+                    wu[j][k] = ld_stream(U + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
+                }
+                dg[j] = __half2float(GD[n * NB + b]);
+                du[j] = __half2float(UD[n * NB + b]);
+            }
+        };
+        if (!act) continue;
+        int li = __ffs(act) - 1;
+        load(__shfl_sync(0xffffffffu, ni, li));
+        while (act) {
+            act &= act - 1;
+            const int64_t n = __shfl_sync(0xffffffffu, ni, li);
+            const uint32_t m = __shfl_sync(0xffffffffu, mi, li);
+            // this neuron's rows are in registers: compute every marked token
+            float part_g[SF_TMAX], part_u[SF_TMAX];
+#pragma unroll
+            for (int t = 0; t < SF_TMAX; ++t) part_g[t] = part_u[t] = 0.f;
+            if (QT == PI_QT_Q4_0) {
+                // each nibble is decoded once and used by every marked token
+#pragma unroll
+                for (int j = 0; j < BPL; ++j) {
+                    const int b = lane + 32 * j;
+                    float bg[SF_TMAX], bu[SF_TMAX];
+#pragma unroll
+                    for (int t = 0; t < SF_TMAX; ++t) bg[t] = bu[t] = 0.f;
+                    uint32_t g0 = wg[j][0].x, g1 = wg[j][0].y, g2 = wg[j][0].z, g3 = wg[j][0].w;
+                    uint32_t u0 = wu[j][0].x, u1 = wu[j][0].y, u2 = wu[j][0].z, u3 = wu[j][0].w;
+#pragma unroll 1
+                    for (int i = 0; i < 4; ++i) {  // word i = elements 8i .. 8i+7 (byte k: 2k low, 2k+1 high)
+                        float fg[8], fu[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            fg[e] = nibf((g0 >> (4 * e)) & 15u);
+                            fu[e] = nibf((u0 >> (4 * e)) & 15u);
+                        }
+#pragma unroll
+                        for (int t = 0; t < SF_TMAX; ++t) {
+                            if (t >= nt || !((m >> t) & 1u)) continue;
+                            const float* xb = sf_x + (size_t)t * NB * 36 + 36 * b + 8 * i;
+                            const float4 xa = *reinterpret_cast<const float4*>(xb);
+                            const float4 xc = *reinterpret_cast<const float4*>(xb + 4);
+                            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                bg[t] += fg[e] * xv[e];
+                                bu[t] += fu[e] * xv[e];
+                            }
+                        }
+                        g0 = g1; g1 = g2; g2 = g3;
+                        u0 = u1; u1 = u2; u2 = u3;
+                    }
+#pragma unroll
+                    for (int t = 0; t < SF_TMAX; ++t) {
+                        part_g[t] += dg[j] * bg[t];
+                        part_u[t] += du[j] * bu[t];
+                    }
+                }
+            } else {
+#pragma unroll
+                for (int t = 0; t < SF_TMAX; ++t) {
+                    if (t >= nt || !((m >> t) & 1u)) continue;
+                    float sg = 0.f, su = 0.f;
+#pragma unroll
+                    for (int j = 0; j < BPL; ++j) {
+                        const int b = lane + 32 * j;
+                        const int8_t* s8 = reinterpret_cast<const int8_t*>(sf_x) + (size_t)t * D + 32 * b;
+                        const float dxv = sf_x[nt * D / 4 + t * NB + b];
+                        const int4 xa = *reinterpret_cast<const int4*>(s8), xc = *reinterpret_cast<const int4*>(s8 + 16);
+                        int ag = dp4a(wg[j][0].x, xa.x, 0), au = dp4a(wu[j][0].x, xa.x, 0);
+                        ag = dp4a(wg[j][0].y, xa.y, ag); au = dp4a(wu[j][0].y, xa.y, au);
+                        ag = dp4a(wg[j][0].z, xa.z, ag); au = dp4a(wu[j][0].z, xa.z, au);
+                        ag = dp4a(wg[j][0].w, xa.w, ag); au = dp4a(wu[j][0].w, xa.w, au);
+                        ag = dp4a(wg[j][WPB - 1].x, xc.x, ag); au = dp4a(wu[j][WPB - 1].x, xc.x, au);
+                        ag = dp4a(wg[j][WPB - 1].y, xc.y, ag); au = dp4a(wu[j][WPB - 1].y, xc.y, au);
+                        ag = dp4a(wg[j][WPB - 1].z, xc.z, ag); au = dp4a(wu[j][WPB - 1].z, xc.z, au);
+                        ag = dp4a(wg[j][WPB - 1].w, xc.w, ag); au = dp4a(wu[j][WPB - 1].w, xc.w, au);
+                        sg += (float)ag * (dg[j] * dxv);
+                        su += (float)au * (du[j] * dxv);
+                    }
+                    part_g[t] = sg;
+                    part_u[t] = su;
+                }
+            }
+            // the next marked neuron's rows are requested before the reductions
+            if (act) {
+                li = __ffs(act) - 1;
+                load(__shfl_sync(0xffffffffu, ni, li));
+            }
+            float hv = 0.f;  // lane t keeps token t's h
+#pragma unroll
+            for (int t = 0; t < SF_TMAX; ++t) {
+                if (t >= nt || !((m >> t) & 1u)) continue;
+                const float sg = warp_sum(part_g[t]), su = warp_sum(part_u[t]);
+                if (lane == t) hv = swiglu_ref(sg, su);
+            }
+            if (lane < nt) h[(int64_t)lane * n_ff + n] = hv;
+        }
     }
 }
 
-// down, neuron-major, over the pass plan: CTA = (512 output columns, SF_GPC
-// 32-neuron groups); thread owns 2 consecutive columns. The CTA first stages its
-// groups' active neurons, h = SwiGLU(g, u) (quant/mod.rs:1196-1199) of every
-// (token, neuron) and the thread's block scales of each group, while the neurons'
-// weight slices are copied into shared memory (cp.async); then it runs over the
-// neurons from shared memory; y is accumulated with float2 atomics over
-// the group chunks. Q8_0 weights and a token whose list is complete: the reference
-// then takes the dense ffn_swiglu_q, whose down projection re-quantises h to Q8_0
-// blocks (quant/mod.rs:1203), so such a token's h is replaced by its Q8_0 value q * d.
+// down, neuron-major, of the pass: CTA = (512 output columns, 64 neurons), thread =
+// 2 consecutive columns. The CTA loads h of its neurons for every token, keeps the
+// neurons with any nonzero h, copies their weight slices into shared memory
+// (cp.async) while it loads the block scales, then runs over them; y gets float2
+// atomics. Q8_0 weights and a token whose list is complete: the reference then takes
+// the dense ffn_swiglu_q, whose down projection re-quantises h to Q8_0 blocks
+// (quant/mod.rs:1203), so such a token's h is replaced by its Q8_0 value q * d.
+constexpr int SF_DN = 64;  // neurons per down CTA (two 32-neuron scale groups)
 template <int QT, int NTM>
 __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
-                                                 const uint8_t* __restrict__ mask, const int32_t* __restrict__ list,
-                                                 const int32_t* __restrict__ gofs, const float2* __restrict__ gu,
-                                                 const int64_t* __restrict__ ptr, int t0, int nt, int64_t n_embd,
-                                                 int64_t n_ff, float* __restrict__ y) {
-    __shared__ int32_t s_list[SF_GPC * 32];
-    __shared__ float s_h[NTM][SF_GPC * 32];
-    __shared__ float2 s_sc[SF_GPC][256];
+                                                 const float* __restrict__ h, const int64_t* __restrict__ ptr, int t0,
+                                                 int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y) {
+    __shared__ float s_h[NTM][SF_DN];
+    __shared__ int32_t s_list[SF_DN];
+    __shared__ int s_cnt[2];
+    __shared__ float2 s_sc[SF_DN / 32][256];
     constexpr int RB = QT == PI_QT_Q4_0 ? 256 : 512;  // bytes of a neuron's 512 columns
-    __shared__ __align__(16) uint8_t s_w[SF_GPC * 32][RB];
-    const int ng = (int)(n_ff / 32);
-    const int g0 = blockIdx.y * SF_GPC, g1 = min(ng, g0 + SF_GPC);
-    const int i0 = gofs[g0], n = gofs[g1] - i0;
-    if (n == 0) return;
+    __shared__ __align__(16) uint8_t s_w[SF_DN][RB];
+    const int64_t n0 = (int64_t)blockIdx.y * SF_DN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t c = blockIdx.x * 512LL + 2 * tid;
-    if (tid < n) {
-        const int s = list[i0 + tid];
-        s_list[tid] = s;
-        const uint32_t m = mask[s];
+    if (tid < SF_DN) {
 #pragma unroll
-        for (int t = 0; t < NTM; ++t) {
-            float h = 0.f;
-            if (t < nt && ((m >> t) & 1u)) {
-                const float2 v = gu[(int64_t)t * n_ff + s];
-                h = swiglu_ref(v.x, v.y);
-            }
-            s_h[t][tid] = h;
-        }
+        for (int t = 0; t < NTM; ++t) s_h[t][tid] = (t < nt && n0 + tid < n_ff) ? h[(int64_t)t * n_ff + n0 + tid] : 0.f;
     }
     __syncthreads();
-    {  // the active neurons' weight slices, copied in while the scales and h are prepared
+    if (QT == PI_QT_Q8_0 && warp < SF_DN / 32) {
+        for (int t = 0; t < nt && t < NTM; ++t) {
+            if (ptr[t0 + t + 1] - ptr[t0 + t] < n_ff) continue;
+            float sc;
+            const int8_t q = warp_quant_q8(s_h[t][32 * warp + lane], &sc);
+            s_h[t][32 * warp + lane] = fmul((float)q, sc);
+        }
+    }
+    if (warp < SF_DN / 32) {  // the neurons with any nonzero h, ascending
+        bool any = false;
+#pragma unroll
+        for (int t = 0; t < NTM; ++t) any |= s_h[t][32 * warp + lane] != 0.f;
+        const uint32_t bal = __ballot_sync(0xffffffffu, any);
+        if (lane == 0) s_cnt[warp] = __popc(bal);
+        __syncwarp();
+        __shared__ uint32_t s_bal[SF_DN / 32];
+        if (lane == 0) s_bal[warp] = bal;
+        __syncwarp();
+        asm volatile("bar.sync 1, 64;" ::: "memory");
+        const int base = warp ? s_cnt[0] : 0;
+        if (any) s_list[base + __popc(bal & ((1u << lane) - 1u))] = 32 * warp + lane;
+    }
+    __syncthreads();
+    const int n = s_cnt[0] + s_cnt[1];
+    if (n == 0) return;
+    {
         const int64_t rowb = QT == PI_QT_Q4_0 ? n_embd / 2 : n_embd;
         const int64_t cb = blockIdx.x * (int64_t)RB;
         for (int q = tid; q < n * (RB / 16); q += 256) {
             const int i = q / (RB / 16), ch = q % (RB / 16);
             const uint32_t sa = (uint32_t)__cvta_generic_to_shared(&s_w[i][16 * ch]);
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa),
-                         "l"(DQ + (int64_t)s_list[i] * rowb + cb + 16 * ch)
+                         "l"(DQ + (n0 + s_list[i]) * rowb + cb + 16 * ch)
                          : "memory");
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    for (int gi = 0; gi < g1 - g0; ++gi) {
+#pragma unroll
+    for (int gi = 0; gi < SF_DN / 32; ++gi) {
         float2 sc = make_float2(0.f, 0.f);
-        if (gofs[g0 + gi + 1] > gofs[g0 + gi])
-            sc = __half22float2(*reinterpret_cast<const __half2*>(DS + (int64_t)(g0 + gi) * n_embd + c));
+        if (s_cnt[gi] > 0)
+            sc = __half22float2(*reinterpret_cast<const __half2*>(DS + ((n0 >> 5) + gi) * n_embd + c));
         s_sc[gi][tid] = sc;
-    }
-    if (QT == PI_QT_Q8_0) {
-        __syncthreads();
-        for (int t = 0; t < nt && t < NTM; ++t) {
-            if (ptr[t0 + t + 1] - ptr[t0 + t] < n_ff) continue;
-            if (warp < g1 - g0) {  // dense: group warp's 32 neurons are list entries 32 warp .. +31
-                float sc;
-                const int8_t q = warp_quant_q8(s_h[t][32 * warp + lane], &sc);
-                s_h[t][32 * warp + lane] = fmul((float)q, sc);
-            }
-        }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();
@@ -601,8 +567,8 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
     for (int t = 0; t < NTM; ++t) acc[t][0] = acc[t][1] = 0.f;
 #pragma unroll 8
     for (int i = 0; i < n; ++i) {
-        const int s = s_list[i];
-        const float2 sc = s_sc[(s >> 5) - g0][tid];
+        const int sl = s_list[i];
+        const float2 sc = s_sc[sl >> 5][tid];
         float w0, w1;
         if (QT == PI_QT_Q4_0) {
             const uint32_t v = s_w[i][tid];
@@ -615,7 +581,7 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
         }
 #pragma unroll
         for (int t = 0; t < NTM; ++t) {
-            const float hv = s_h[t][i];
+            const float hv = s_h[t][sl];
             acc[t][0] += hv * w0;
             acc[t][1] += hv * w1;
         }
@@ -854,9 +820,9 @@ extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const voi
     if (qtype != PI_QT_Q4_0 && qtype != PI_QT_Q8_0)
         return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: weights must be Q4_0 or Q8_0");
     const int64_t unit = qtype == PI_QT_Q4_0 ? 1024 : 512;
-    if (n_embd % unit || n_embd / unit > 4 || n_embd / unit < 1 || n_ff % 32 || n_embd % 1024 || n_ff > SF_MAX_FF)
+    if (n_embd % unit || n_embd / unit > 4 || n_embd / unit < 1 || n_ff % 64 || n_embd % 1024 || n_ff > SF_MAX_FF)
         return pi_set_error(ctx, PI_ERR_ARG,
-                            "sparse ffn: n_embd must be 1024/2048/4096, n_ff % 32 == 0 and n_ff <= 131072");
+                            "sparse ffn: n_embd must be 1024/2048/4096, n_ff % 64 == 0 and n_ff <= 131072");
     cudaSetDevice(ctx->device);
     pi_sparse_ffn* F = new pi_sparse_ffn();
     F->ctx = ctx;
@@ -880,6 +846,11 @@ extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const voi
         else F->allocs.push_back(F->down_q);
         if (!rc && pi_cuda_check(ctx, cudaMalloc(&F->down_d, (n_ff / 32) * n_embd * 2), "cudaMalloc")) rc = PI_ERR_OOM;
         else if (!rc) F->allocs.push_back(F->down_d);
+    }
+    if (!rc) {
+        if (pi_cuda_check(ctx, cudaMalloc(&F->mask, n_ff), "cudaMalloc")) rc = PI_ERR_OOM;
+        else F->allocs.push_back(F->mask);
+        if (!rc && pi_cuda_check(ctx, cudaMemset(F->mask, 0, n_ff), "memset")) rc = PI_ERR_CUDA;
     }
     if (!rc) {
         const int64_t nthr = (n_embd / 2) * (n_ff / 32);
@@ -907,64 +878,60 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
     if (!ctx || !F) return PI_ERR_ARG;
     if (T < 0 || (T > 0 && (!x || !ptr || !out))) return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: bad argument");
     if (T == 0) return PI_OK;
+    if (((uintptr_t)x | (uintptr_t)out) & 15) return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: x, out 16-byte aligned");
     cudaStream_t st = ST(stream);
-    const int64_t d = F->n_embd, n_ff = F->n_ff, ng = n_ff / 32;
+    const int64_t d = F->n_embd, n_ff = F->n_ff;
     char* scr;
-    const size_t need = (size_t)n_ff * 4 * 2 + (size_t)(ng + 1) * 4 + (size_t)SF_TMAX * n_ff * 8 + (size_t)T * d +
-                        (size_t)T * (d / 32) * 4 + 8192;
+    const size_t need = (size_t)SF_TMAX * n_ff * 4 + (size_t)T * d + (size_t)T * (d / 32) * 4 + 4096;
     if (int rc = pi_scratch(ctx, st, need, &scr)) return rc;
     PiBump b{scr};
-    uint8_t* mask = b.take<uint8_t>(n_ff);
-    int32_t* list = b.take<int32_t>(n_ff);
-    int32_t* gofs = b.take<int32_t>(ng + 1);
-    float2* gu = b.take<float2>((size_t)SF_TMAX * n_ff);
+    float* hb = b.take<float>((size_t)SF_TMAX * n_ff);
     int8_t* xq = nullptr;
     float* xs = nullptr;
-    if (F->qtype == PI_QT_Q8_0) {
+    const bool q4 = F->qtype == PI_QT_Q4_0;
+    if (!q4) {
         xq = b.take<int8_t>(T * d);
         xs = b.take<float>(T * (d / 32));
+        PiProfScope ps(ctx, st, "k_sf_quant");
         k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
     }
-    const int plan_smem = (int)n_ff;
-    pi_smem_attr((const void*)k_sf_plan, SF_MAX_FF);
+    const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
     for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
         {
-            PiProfScope ps(ctx, st, "k_sf_mask");
-            k_sf_plan<<<1, 1024, plan_smem, st>>>(ptr, idx, (int)t0, nt, n_ff, d, mask, list, gofs, out, ctx->dev_err);
+            PiProfScope ps(ctx, st, "k_sf_mark");
+            k_sf_mark<<<(unsigned)std::min<int64_t>(nt * n_ff / 1024 + 1, 512), 256, 0, st>>>(
+                ptr, idx, (int)t0, nt, n_ff, reinterpret_cast<uint32_t*>(F->mask), hb, ctx->dev_err);
         }
-        const int32_t* n_list = gofs + ng;
         {
             PiProfScope ps(ctx, st, "k_sf_gateup");
-            const unsigned gq4 = (unsigned)((n_ff + SF_NPC - 1) / SF_NPC), gq8 = (unsigned)((n_ff + 1) / 2);
-            if (F->qtype == PI_QT_Q4_0) {
-                const uint8_t* G = (const uint8_t*)F->gate.q;
-                const uint8_t* U = (const uint8_t*)F->up.q;
-#define SF_GU4(B) k_sf_gateup_q4<B><<<gq4, SF_NPC * B * 32, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, x, (int)t0, nt, d, n_ff, gu)
-                switch (d / 1024) {
-                    case 1: SF_GU4(1); break;
-                    case 2: SF_GU4(2); break;
-                    case 4: SF_GU4(4); break;
-                }
-#undef SF_GU4
-            } else {
-                const int8_t* G = (const int8_t*)F->gate.q;
-                const int8_t* U = (const int8_t*)F->up.q;
-#define SF_GU8(C) k_sf_gateup_q8<C><<<gq8, 2 * C * 32, 0, st>>>(G, U, F->gate.d, F->up.d, mask, list, n_list, xq, xs, (int)t0, nt, d, n_ff, gu)
-                switch (d / 512) {
-                    case 2: SF_GU8(2); break;
-                    case 4: SF_GU8(4); break;
-                    case 8: SF_GU8(8); break;
-                }
-#undef SF_GU8
+            const size_t smem = q4 ? (size_t)nt * (d / 32) * 36 * 4 : (size_t)nt * d + (size_t)nt * (d / 32) * 4;
+            const uint8_t* G = (const uint8_t*)F->gate.q;
+            const uint8_t* U = (const uint8_t*)F->up.q;
+#define SF_GU(QT, B)                                                                                            \
+    {                                                                                                           \
+        pi_smem_attr((const void*)k_sf_gateup<QT, B>, smem);                                                   \
+        k_sf_gateup<QT, B><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(G, U, F->gate.d, F->up.d, F->mask, x, \
+                                                                          xq, xs, ptr, idx, (int)t0, nt, n_ff, hb, \
+                                                                          out);                                 \
+    }
+            switch ((q4 ? 1 : 16) * (int)(d / 1024)) {
+                case 1: SF_GU(PI_QT_Q4_0, 1) break;
+                case 2: SF_GU(PI_QT_Q4_0, 2) break;
+                case 4: SF_GU(PI_QT_Q4_0, 4) break;
+                case 16: SF_GU(PI_QT_Q8_0, 1) break;
+                case 32: SF_GU(PI_QT_Q8_0, 2) break;
+                case 64: SF_GU(PI_QT_Q8_0, 4) break;
+                default: return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: n_embd must be 1024, 2048 or 4096");
             }
+#undef SF_GU
         }
         {
             PiProfScope ps(ctx, st, "k_sf_down");
-            const dim3 dg((unsigned)(d / 512), (unsigned)((ng + SF_GPC - 1) / SF_GPC));
+            const dim3 dg((unsigned)(d / 512), (unsigned)((n_ff + SF_DN - 1) / SF_DN));
             const uint8_t* DQ = (const uint8_t*)F->down_q;
-#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, mask, list, gofs, gu, ptr, (int)t0, nt, d, n_ff, out)
-            if (F->qtype == PI_QT_Q4_0) {
+#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out)
+            if (q4) {
                 if (nt == 1) SF_DOWN(PI_QT_Q4_0, 1);
                 else SF_DOWN(PI_QT_Q4_0, SF_TMAX);
             } else {
