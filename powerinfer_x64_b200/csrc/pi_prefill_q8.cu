@@ -7,33 +7,38 @@
 // in f32 starting from 0. Here the int8 values of both operands are held as
 // exact f16 and multiplied with tcgen05.mma kind::f16: every product and every
 // partial sum of a block is an integer below 2^20, so the f32 result in TMEM is
-// exactly (float)sumi_b. One MMA pair per 32-element block writes a fresh
-// accumulator; epilogue warps apply each block's scales and add it to f32
-// registers in block order, so each output is the reference's own sequence of
-// roundings. The gate/up kernel applies the reference's SwiGLU and quantises h
-// to Q8_0 per 32 rows, exactly as ffn_swiglu_q does before its down matvec
-// (quant/mod.rs:1184-1249); the down kernel writes y.
+// exactly (float)sumi_b. The scale product d_w,b * d_x,b of every (slot, row) is
+// made on the tensor cores too: both scales are f16 values, so their product
+// (22 significant bits) is exact in f32, and one K = 16 MMA of a slot-scale column
+// by a row-scale row writes all of them. Per block a fresh pair of accumulators
+// (sumi, scale product) lands in TMEM and epilogue warps add sumi * product to
+// f32 registers in block order (one multiply, one add per output and block), so
+// each output is the reference's own sequence of roundings. The gate/up kernel
+// applies the reference's SwiGLU and quantises h to Q8_0 per 32 rows, exactly as
+// ffn_swiglu_q does before its down matvec (quant/mod.rs:1184-1249); the down
+// kernel writes y.
 //
 // Orientation: the token rows of a work item (<= 128 slots) are the MMA's M
-// side and 128 weight rows its N side, so a TMEM lane is one slot and a thread
-// of the epilogue owns one slot: its activation scale is one register per
-// block, the weight scales are broadcast float4 loads, and a 32-row Q8_0 block
-// of h lies in one thread's registers.
+// side and 128 weight rows its N side, so a TMEM lane is one slot, a thread of
+// the epilogue owns one slot, and a 32-row Q8_0 block of h lies in one thread's
+// registers.
 //
 // Operands:
 //   A (slots)   f16 rows [slots][K], slot-major (k_slot_rows writes the gate/up
 //               activations in slot order; the gate/up epilogue writes h so),
 //               loaded by TMA with the 64-byte swizzle the MMA reads;
 //   B (weights) int8 rows of the lane-tiled decode layouts, loaded raw by TMA in
-//               groups of 4 blocks and turned into exact f16 by converter warps.
+//               groups of 4 blocks and turned into exact f16 by converter warps;
+//   scales      per block a [128 x 16] f16 tile of slot scales (column 0) and one
+//               of row scales (column 0), written by the converters (no swizzle).
 //
 // The kernel is persistent: a CTA walks tiles (work item, 128 weight rows) and
 // its pipeline runs on across tile boundaries. Warp roles (QT = 448 threads):
 //   0-7   epilogue: warp w owns slots 32 (w % 4) .. +31 (TMEM lanes) and, for
 //         gate/up, gate columns 32 (w / 4) .. +31 with their up columns (+64),
 //         for down, columns 64 (w / 4) .. +63;
-//   8-11  converters: thread c converts weight row c of each block and
-//         publishes its block scale;
+//   8-11  converters: thread c converts weight row c of each block and writes
+//         the scale tiles' row c (its row's scale, slot c's scale);
 //   12    MMA issuer;  13 TMA producer.
 // Every mbarrier wait is bounded and reports PI_DEVERR_TIMEOUT.
 #include "pi_tc.cuh"
@@ -48,19 +53,31 @@ constexpr int TN = 128;            // weight rows per tile (MMA N)
 constexpr int NEPI = 8, NCONV = 4;
 constexpr int QT = (NEPI + NCONV + 2) * 32;
 constexpr int G4 = 4;              // blocks per raw weight group
-constexpr int RG = 3;              // raw weight groups in flight
-constexpr int PB = 2;              // blocks per stage (one handshake)
+constexpr int RG = 2;              // raw weight groups in flight
+constexpr int PB = 2;              // blocks per operand stage (one handshake)
 constexpr int TS = 4;              // operand stages of PB blocks
-constexpr int DB = 2;              // TMEM buffers of PB x TN columns
-constexpr int SB = 4;              // weight-scale stages
-constexpr int SG = 4;              // activation-scale groups
-constexpr int TILE = 128 * 64;     // 128 rows x 32 f16
-constexpr int STAGE = PB * 2 * TILE;  // {A tile, B tile} per block
+constexpr int DB = 2;              // TMEM buffers of one block: sumi (TN columns) + scale product (TN)
+constexpr int TILE = 128 * 64;     // 128 rows x 32 f16, 64-byte swizzle
+constexpr int STILE = 128 * 32;    // 128 rows x 16 f16, no swizzle (scale tiles)
+constexpr int STAGE = PB * (2 * TILE + 2 * STILE);  // per block {A, B, slot scales, row scales}
 constexpr int RAWW = TN * G4 * 32;    // weight rows of a group (16 KB)
-constexpr int DXG = QN * G4 * 4;      // activation scales of a group (2 KB)
 static_assert(G4 == 2 * PB, "a raw group fills two stages");
 static_assert(QN == 128, "the MMA M side is 128 slots");
-constexpr size_t QSMEM = (size_t)TS * STAGE + (size_t)RG * RAWW + (size_t)SG * DXG + 1024;
+static_assert(DB * 2 * TN == 512, "the TMEM buffers fill the 512 columns");
+constexpr size_t QSMEM = (size_t)TS * STAGE + (size_t)RG * RAWW + 1024;
+
+// UMMA shared-memory descriptor of a K-major tile without swizzle: core matrices of
+// 8 rows x 16 bytes; K-adjacent cores LBO = 128 bytes apart, 8-row groups SBO = 256.
+PI_DEV uint64_t umma_desc_plain(const void* tile) {
+    const uint32_t a = smem_u32(tile);
+    uint64_t d = (uint64_t)((a >> 4) & 0x3FFF);
+    d |= (uint64_t)(128 >> 4) << 16;  // LBO
+    d |= (uint64_t)(256 >> 4) << 32;  // SBO
+    d |= (uint64_t)1 << 46;           // version; layout type 0 = no swizzle
+    return d;
+}
+// byte offset of row r, K elements 0..7 in a plain [128 x 16] scale tile
+PI_DEV int stile_row(int r) { return (r >> 3) * 256 + (r & 7) * 16; }
 
 // 16 int8 (one 16-byte word) -> 16 exact f16, the 16-byte chunks c0 and c0 + 1 of
 // swizzled row r of a SW64 tile: 0x6400 | (b ^ 0x80) is the f16 value 1024 + b + 128,
@@ -113,15 +130,13 @@ struct TileRef {
 template <int MODE, bool FAST>
 __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __grid_constant__ PiPrefillMaps wm,
                                                        const __grid_constant__ CUtensorMap mact,
-                                                       const __grid_constant__ CUtensorMap mscl, uint32_t* err) {
+                                                       const float* __restrict__ xsc, int64_t n_slots, uint32_t* err) {
     extern __shared__ __align__(1024) uint8_t sm_raw[];
     uint8_t* sm = reinterpret_cast<uint8_t*>(((uintptr_t)sm_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t* tiles = sm;                      // TS stages of PB x {A tile, B tile}
-    uint8_t* raws = sm + TS * STAGE;          // RG raw weight groups
-    float* s_dx = reinterpret_cast<float*>(raws + RG * RAWW);  // SG groups of [QN slots][G4 blocks]
-    __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB], scl_full[SB], scl_free[SB];
-    __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG], dx_full[SG], dx_free[SG];
-    __shared__ __align__(16) float s_dw[SB][PB][TN];
+    uint8_t* tiles = sm;              // TS stages of PB x {A tile, B tile, slot-scale tile, row-scale tile}
+    uint8_t* raws = sm + TS * STAGE;  // RG raw weight groups
+    __shared__ __align__(8) uint64_t tile_full[TS], tile_free[TS], d_full[DB], d_free[DB];
+    __shared__ __align__(8) uint64_t raw_full[RG], raw_free[RG];
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = MODE == 0 ? a.d : a.f;
@@ -135,6 +150,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         r.mt = t % MT;
         return r;
     };
+    auto a_tile = [&](int ts, int b) { return tiles + ts * STAGE + b * (2 * TILE + 2 * STILE); };
 
     if (tid == 0) {
         for (int i = 0; i < TS; ++i) {
@@ -145,23 +161,21 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             mbar_init(&d_full[i], 1);
             mbar_init(&d_free[i], NEPI);
         }
-        for (int i = 0; i < SB; ++i) {
-            mbar_init(&scl_full[i], NCONV);
-            mbar_init(&scl_free[i], NEPI);
-        }
         for (int i = 0; i < RG; ++i) {
             mbar_init(&raw_full[i], 1);
             mbar_init(&raw_free[i], NCONV);
         }
-        for (int i = 0; i < SG; ++i) {
-            mbar_init(&dx_full[i], 1);
-            mbar_init(&dx_free[i], NEPI);
-        }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
+    // the scale tiles are zero but for column 0, which the converters rewrite per block
+    for (int ts = 0; ts < TS; ++ts)
+        for (int b = 0; b < PB; ++b)
+            for (int i = tid; i < 2 * STILE / 16; i += QT)
+                reinterpret_cast<uint4*>(a_tile(ts, b) + 2 * TILE)[i] = make_uint4(0, 0, 0, 0);
+    fence_async_smem();
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                     "r"(DB * PB * TN)
+                     "r"(DB * 2 * TN)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -172,7 +186,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     bool ok = true;
 
     if (warp == NEPI + NCONV + 1) {
-        // ---- TMA producer: raw weight groups, activation tiles, activation scales ----
+        // ---- TMA producer: raw weight groups and activation tiles ----
         int g = 0;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
             const TileRef tr = tile_at(t);
@@ -210,28 +224,16 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                         if (s >= TS && !mbar_wait(&tile_free[ts], (s / TS - 1) & 1)) { w_ok = 0; break; }
                         mbar_expect_tx(&tile_full[ts], PB * TILE);
                         for (int b = 0; b < PB; ++b)
-                            tma_load_2d(tiles + ts * STAGE + b * 2 * TILE, &mact, (G4 * q + PB * pi + b) * 32,
-                                        tr.item.y, &tile_full[ts]);
-                    }
-                    if (w_ok) {
-                        const int sg = g % SG;
-                        if (g >= SG && !mbar_wait(&dx_free[sg], (g / SG - 1) & 1)) w_ok = 0;
-                        else {
-                            mbar_expect_tx(&dx_full[sg], DXG);
-                            tma_load_2d(s_dx + sg * (DXG / 4), &mscl, G4 * q, tr.item.y, &dx_full[sg]);
-                        }
+                            tma_load_2d(a_tile(ts, b), &mact, (G4 * q + PB * pi + b) * 32, tr.item.y, &tile_full[ts]);
                     }
                 }
                 if (!__shfl_sync(0xffffffffu, w_ok, 0)) { ok = false; break; }
             }
         }
         // let the last copies land before the CTA can exit (bounded; only matters after a timeout)
-        if (lane == 0 && g > 0) {
-            mbar_wait(&raw_full[(g - 1) % RG], ((g - 1) / RG) & 1);
-            mbar_wait(&dx_full[(g - 1) % SG], ((g - 1) / SG) & 1);
-        }
+        if (lane == 0 && g > 0) mbar_wait(&raw_full[(g - 1) % RG], ((g - 1) / RG) & 1);
     } else if (warp >= NEPI && warp < NEPI + NCONV) {
-        // ---- converters: thread c converts weight row c of every block of a group ----
+        // ---- converters: thread c converts weight row c and writes row c of both scale tiles ----
         const int row = tid - NEPI * 32;
         int g = 0;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
@@ -249,91 +251,112 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                 wr = mrow + tr.mt * TN + row;
             }
             const __half* scp = wd + (size_t)wr * nb;
-            auto load_sc = [&](int q, float (&v)[G4]) {
-                const uint2 h = *reinterpret_cast<const uint2*>(scp + G4 * q);
-                const __half2 h0 = *reinterpret_cast<const __half2*>(&h.x), h1 = *reinterpret_cast<const __half2*>(&h.y);
-                v[0] = __low2float(h0); v[1] = __high2float(h0); v[2] = __low2float(h1); v[3] = __high2float(h1);
+            const int64_t srow = (int64_t)tr.item.y + row;  // this thread's slot (scale row of the A side)
+            const float* xsp = srow < n_slots ? xsc + srow * nb : nullptr;
+            // the row's weight scales and the slot's activation scales of group q, as f16 bits
+            auto load_sc = [&](int q, uint2& w, uint2& x) {
+                w = *reinterpret_cast<const uint2*>(scp + G4 * q);
+                x = make_uint2(0, 0);
+                if (xsp) {  // activation scales are f16 values held in f32: exact conversions
+                    const float4 f = *reinterpret_cast<const float4*>(xsp + G4 * q);
+                    const __half2 lo = __floats2half2_rn(f.x, f.y), hi = __floats2half2_rn(f.z, f.w);
+                    x = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+                }
             };
             // raw position of this row's 16-byte half h of block i
             auto raw_half = [&](const uint8_t* rg, int i, int h) -> const uint8_t* {
                 if (MODE == 0) return rg + (row >> 6) * 2 * 64 * 64 + h * 64 * 64 + (row & 63) * 64 + 16 * i;
                 return rg + (row >> 3) * 1024 + (2 * i + h) * 128 + (row & 7) * 16;  // [r/8][chunk][r%8][16 B]
             };
-            // Chunk j (0..7) of this row's group -> (block i, half h), rotated per row so that
-            // the lanes of a load touch distinct shared-memory banks (gate/up rows are 64 bytes
-            // apart; down rows already interleave 8 rows per 128 bytes)
-            auto chunk_of = [&](int j, int& i, int& h) {
+            // Chunk j (0..3) of this row's stage pi -> (block i, half h); gate/up rows are 64 bytes
+            // apart, so the block is rotated per row pair to spread a load over the banks
+            auto chunk_of = [&](int pi, int j, int& i, int& h) {
                 if (MODE == 0) {
-                    i = (j + (row >> 1)) & 3;
-                    h = j >> 2;
+                    i = PB * pi + ((j + (row >> 1)) & 1);
+                    h = j >> 1;
                 } else {
-                    i = j >> 1;
+                    i = PB * pi + (j >> 1);
                     h = j & 1;
                 }
             };
-            float sc_cur[G4], sc_nxt[G4];
-            load_sc(0, sc_cur);
+            uint2 w_cur, x_cur, w_nxt, x_nxt;
+            load_sc(0, w_cur, x_cur);
             for (int q = 0; q < ng; ++q, ++g) {
                 const int slot = g % RG;
-                if (q + 1 < ng) load_sc(q + 1, sc_nxt);
+                if (q + 1 < ng) load_sc(q + 1, w_nxt, x_nxt);
                 if (!mbar_wait(&raw_full[slot], (g / RG) & 1)) { ok = false; break; }
+                const uint8_t* rg = raws + slot * RAWW;
+                const uint16_t wv[4] = {(uint16_t)(w_cur.x & 0xffff), (uint16_t)(w_cur.x >> 16),
+                                        (uint16_t)(w_cur.y & 0xffff), (uint16_t)(w_cur.y >> 16)};
+                const uint16_t xv[4] = {(uint16_t)(x_cur.x & 0xffff), (uint16_t)(x_cur.x >> 16),
+                                        (uint16_t)(x_cur.y & 0xffff), (uint16_t)(x_cur.y >> 16)};
 #pragma unroll
-                for (int pi = 0; pi < G4 / PB; ++pi) {  // the group's stages: tiles and scale buffers free
+                for (int pi = 0; pi < G4 / PB; ++pi) {  // one stage (PB blocks) at a time
                     const int s = (G4 / PB) * g + pi;
-                    if (s >= TS && !mbar_wait(&tile_free[s % TS], (s / TS - 1) & 1)) ok = false;
-                    if (s >= SB && !mbar_wait(&scl_free[s % SB], (s / SB - 1) & 1)) ok = false;
+                    uint4 rv[2 * PB];
+#pragma unroll
+                    for (int j = 0; j < 2 * PB; ++j) {
+                        int i, h;
+                        chunk_of(pi, j, i, h);
+                        rv[j] = *reinterpret_cast<const uint4*>(raw_half(rg, i, h));
+                    }
+                    if (s >= TS && !mbar_wait(&tile_free[s % TS], (s / TS - 1) & 1)) { ok = false; break; }
+                    uint8_t* st = a_tile(s % TS, 0);
+#pragma unroll
+                    for (int j = 0; j < 2 * PB; ++j) {
+                        int i, h;
+                        chunk_of(pi, j, i, h);
+                        int8x16_to_f16(rv[j], st + (i % PB) * (2 * TILE + 2 * STILE) + TILE, row, 2 * h);
+                    }
+#pragma unroll
+                    for (int b = 0; b < PB; ++b) {  // K element 0 of row `row` in both scale tiles
+                        uint8_t* base = st + b * (2 * TILE + 2 * STILE) + 2 * TILE;
+                        *reinterpret_cast<uint4*>(base + stile_row(row)) = make_uint4(xv[PB * pi + b], 0, 0, 0);
+                        *reinterpret_cast<uint4*>(base + STILE + stile_row(row)) =
+                            make_uint4(wv[PB * pi + b], 0, 0, 0);
+                    }
+                    fence_async_smem();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&tile_full[s % TS]);
                 }
                 if (!ok) break;
-                const uint8_t* rg = raws + slot * RAWW;
-#pragma unroll
-                for (int j = 0; j < 2 * G4; ++j) {
-                    int i, h;
-                    chunk_of(j, i, h);
-                    const int s = (G4 / PB) * g + i / PB;
-                    int8x16_to_f16(*reinterpret_cast<const uint4*>(raw_half(rg, i, h)),
-                                   tiles + (s % TS) * STAGE + (i % PB) * 2 * TILE + TILE, row, 2 * h);
-                }
-#pragma unroll
-                for (int i = 0; i < G4; ++i) s_dw[((G4 / PB) * g + i / PB) % SB][i % PB][row] = sc_cur[i];
-                fence_async_smem();
                 __syncwarp();
-                if (lane == 0) {
-#pragma unroll
-                    for (int pi = 0; pi < G4 / PB; ++pi) {
-                        const int s = (G4 / PB) * g + pi;
-                        mbar_arrive(&tile_full[s % TS]);
-                        mbar_arrive(&scl_full[s % SB]);
-                    }
-                    mbar_arrive(&raw_free[slot]);
-                }
-#pragma unroll
-                for (int i = 0; i < G4; ++i) sc_cur[i] = sc_nxt[i];
+                if (lane == 0) mbar_arrive(&raw_free[slot]);
+                w_cur = w_nxt;
+                x_cur = x_nxt;
             }
         }
     } else if (warp == NEPI + NCONV) {
-        // ---- MMA issuer: per block a fresh accumulator of 128 slots x 128 weight rows ----
-        if (lane == 0) {
-            const uint32_t id = idesc(TN);
-            int s = 0;
-            for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
-                for (int p = 0; p < nb / PB; ++p, ++s) {
-                    const int ts = s % TS, db = s % DB;
-                    if (!mbar_wait(&tile_full[ts], (s / TS) & 1) ||
-                        (s >= DB && !mbar_wait(&d_free[db], (s / DB - 1) & 1))) {
+        // ---- MMA issuer: per block a fresh sumi accumulator (128 slots x 128 weight rows) and
+        // the block's scale products (slot scale x row scale, one K = 16 MMA) next to it.
+        // The whole warp walks the loop and waits; lane 0 issues the MMAs and their commits.
+        const uint32_t id = idesc(TN);
+        int s = 0, blk = 0;
+        for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
+            for (int p = 0; p < nb / PB; ++p, ++s) {
+                const int ts = s % TS;
+                if (!__all_sync(0xffffffffu, mbar_wait(&tile_full[ts], (s / TS) & 1))) { ok = false; break; }
+                for (int b = 0; b < PB; ++b, ++blk) {
+                    const int db = blk % DB;
+                    if (blk >= DB && !__all_sync(0xffffffffu, mbar_wait(&d_free[db], (blk / DB - 1) & 1))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-#pragma unroll
-                    for (int b = 0; b < PB; ++b) {
-                        const uint8_t* at = tiles + ts * STAGE + b * 2 * TILE;
-                        const uint32_t dcol = tmem + (db * PB + b) * TN;
+                    if (lane == 0) {
+                        const uint8_t* at = a_tile(ts, b);
+                        const uint32_t dcol = tmem + db * 2 * TN;
                         mma_f16(dcol, umma_desc(at, 0), umma_desc(at + TILE, 0), id, 0u);
                         mma_f16(dcol, umma_desc(at, 32), umma_desc(at + TILE, 32), id, 1u);
+                        mma_f16(dcol + TN, umma_desc_plain(at + 2 * TILE), umma_desc_plain(at + 2 * TILE + STILE),
+                                id, 0u);
+                        mma_commit(&d_full[db]);
                     }
-                    mma_commit(&tile_free[ts]);
-                    mma_commit(&d_full[db]);
+                    __syncwarp();
                 }
+                if (!ok) break;
+                if (lane == 0) mma_commit(&tile_free[ts]);
+                __syncwarp();
             }
         }
     } else {
@@ -341,57 +364,38 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         const int q4 = warp & 3, m = warp >> 2, srow = 32 * q4 + lane;
         const uint32_t lane_base = (uint32_t)(32 * q4) << 16;
         const int c0 = MODE == 0 ? 32 * m : 64 * m, c1 = MODE == 0 ? 64 + 32 * m : 64 * m + 32;
-        int g = 0, s = 0;
+        int blk = 0;
         for (int t = blockIdx.x; t < n_tiles && ok; t += gridDim.x) {
             const TileRef tr = tile_at(t);
             const bool live = 32 * q4 < tr.item.z;
             float acc[64];
 #pragma unroll
             for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
-            for (int q = 0; q < ng && ok; ++q, ++g) {
-                const int sg = g % SG;
-                if (!mbar_wait(&dx_full[sg], (g / SG) & 1)) { ok = false; break; }
-                const float4 dx4 = *reinterpret_cast<const float4*>(s_dx + sg * (DXG / 4) + srow * G4);
-                for (int pi = 0; pi < G4 / PB; ++pi, ++s) {
-                    const int db = s % DB, sb = s % SB;
-                    const float dxs[PB] = {pi ? dx4.z : dx4.x, pi ? dx4.w : dx4.y};  // blocks 2 pi, 2 pi + 1
-                    if (!mbar_wait(&d_full[db], (s / DB) & 1) || !mbar_wait(&scl_full[sb], (s / SB) & 1)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    if (live) {
+            for (int kb = 0; kb < nb; ++kb, ++blk) {  // blocks in ascending order
+                const int db = blk % DB;
+                if (!mbar_wait(&d_full[db], (blk / DB) & 1)) { ok = false; break; }
+                tc_fence_after();
+                if (live) {
+                    const uint32_t tb = tmem + lane_base + db * 2 * TN;
 #pragma unroll
-                        for (int b = 0; b < PB; ++b) {  // the stage's blocks in ascending order
-                            const float dx = dxs[b];
+                    for (int qq = 0; qq < 4; ++qq) {  // 16 columns at a time: sumi and scale product
+                        const int cb = (qq < 2 ? c0 : c1) + 16 * (qq & 1);
+                        uint32_t v[16], pr[16];
+                        tmem_ld16_nw(tb + cb, v);
+                        tmem_ld16_nw(tb + TN + cb, pr);
+                        tmem_wait_ld();
+                        float* ac = &acc[16 * qq];
 #pragma unroll
-                            for (int hh = 0; hh < 2; ++hh) {
-                                float v[32];
-                                const int cb = hh ? c1 : c0;
-                                tmem_ld32(tmem + lane_base + (db * PB + b) * TN + cb, v);
-#pragma unroll
-                                for (int j4 = 0; j4 < 8; ++j4) {
-                                    const float4 dw = *reinterpret_cast<const float4*>(&s_dw[sb][b][cb + 4 * j4]);
-                                    float* ac = &acc[32 * hh + 4 * j4];
-                                    const float w4[4] = {dw.x, dw.y, dw.z, dw.w};
-#pragma unroll
-                                    for (int e = 0; e < 4; ++e) {
-                                        if (FAST) ac[e] = __fmaf_rn(v[4 * j4 + e], fmul(w4[e], dx), ac[e]);
-                                        else ac[e] = fadd(ac[e], fmul(v[4 * j4 + e], fmul(w4[e], dx)));
-                                    }
-                                }
-                            }
+                        for (int e = 0; e < 16; ++e) {
+                            const float x = __uint_as_float(v[e]), p = __uint_as_float(pr[e]);
+                            if (FAST) ac[e] = __fmaf_rn(x, p, ac[e]);
+                            else ac[e] = fadd(ac[e], fmul(x, p));
                         }
                     }
-                    tc_fence_before();
-                    __syncwarp();
-                    if (lane == 0) {
-                        mbar_arrive(&d_free[db]);
-                        mbar_arrive(&scl_free[sb]);
-                    }
                 }
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0 && ok) mbar_arrive(&dx_free[sg]);
+                if (lane == 0) mbar_arrive(&d_free[db]);
             }
             if (!ok || !live || srow >= tr.item.z) continue;
             const size_t slot = (size_t)tr.item.y + srow;
@@ -427,7 +431,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     tc_fence_before();
     __syncthreads();
     if (warp == 0)
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * PB * TN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * 2 * TN) : "memory");
 }
 
 // Gate/up activations in slot order: slot s < n_routed holds row perm[s], slot
@@ -488,14 +492,6 @@ bool act16_map(CUtensorMap* m, const __half* base, int64_t rows, int64_t cols) {
     const cuuint32_t box[2] = {32, 128};
     return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_64B);
 }
-// slot-major f32 block scales [rows][nb]: 128 rows x 4 blocks per box
-bool scale_map(CUtensorMap* m, const float* base, int64_t rows, int64_t nb) {
-    const cuuint64_t dims[2] = {(cuuint64_t)nb, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)nb * 4};
-    const cuuint32_t box[2] = {4, 128};
-    return encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_NONE);
-}
-
 }  // namespace
 
 bool pi_prefill_q8_shape_ok(int64_t d, int64_t f) {
@@ -526,9 +522,8 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: weight tensor maps unavailable");
     if (!a.xsl || !a.xssl || !a.h16) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: slot buffers missing");
     (void)T;
-    CUtensorMap mx, mxs, mh, mhs;
-    if (!act16_map(&mx, a.xsl, n_slots, a.d) || !scale_map(&mxs, a.xssl, n_slots, a.d / 32) ||
-        !act16_map(&mh, a.h16, n_slots, a.f) || !scale_map(&mhs, a.hs, n_slots, a.f / 32))
+    CUtensorMap mx, mh;
+    if (!act16_map(&mx, a.xsl, n_slots, a.d) || !act16_map(&mh, a.h16, n_slots, a.f))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
     const bool fast = (flags & PI_FWD_FAST_SUM) != 0;
     auto gu = fast ? k_moe_gemm_q8<0, true> : k_moe_gemm_q8<0, false>;
@@ -544,12 +539,12 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
         const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.f / 64), sms);
-        gu<<<g, QT, QSMEM, st>>>(a, L->maps, mx, mxs, ctx->dev_err);
+        gu<<<g, QT, QSMEM, st>>>(a, L->maps, mx, a.xssl, n_slots, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_down");
         const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.d / TN), sms);
-        dn<<<g, QT, QSMEM, st>>>(a, L->maps, mh, mhs, ctx->dev_err);
+        dn<<<g, QT, QSMEM, st>>>(a, L->maps, mh, a.hs, n_slots, ctx->dev_err);
     }
     return pi_cuda_check(ctx, cudaGetLastError(), "prefill Q8_0 GEMM") ? PI_ERR_CUDA : PI_OK;
 }
