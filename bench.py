@@ -471,10 +471,23 @@ def main():
         ops = 2.0 * slots * 2 * cfg.f * cfg.d
         ach = ops / (g_ms / args.steps / 1e3) / 1e12
         ipeak = peaks.get("int8_tops", 4500.0)
+        # The exact method adds sumi * scale product into f32 registers per output and
+        # 32-block (one multiply, one add): the CUDA-core floor of that work at the
+        # sampled clock, 128 f32 lanes per SM
+        sm_count = torch.cuda.get_device_properties(dev).multi_processor_count
+        fp32_floor_ms = 2.0 * slots * 2 * cfg.f * (cfg.d // 32) / (128 * sm_count * 1.965e9) * 1e3
+        c5_traffic = None
+        tf = ROOT / "profiles" / "ncu_traffic.json"
+        if tf.exists() and T == 8192:
+            try:
+                c5_traffic = json.loads(tf.read_text()).get("k_gemm_q8_gateup_c5_T8192_bytes_per_launch")
+            except Exception:
+                c5_traffic = None
         roofline = {"bound": "tensor", "kernel": "k_gemm_q8_gateup", "achieved": ach, "peak": ipeak,
                     "unit": "TOPS (int8)", "frac": ach / ipeak,
                     "peak_source": "measured" if "int8_tops" in peaks else "nominal int8 dense (no measured int8 peak)",
-                    "frac_of_measured_bf16": ach / peaks.get("bf16_tflops", 1590.0), "traffic": None,
+                    "frac_of_measured_bf16": ach / peaks.get("bf16_tflops", 1590.0), "traffic": c5_traffic,
+                    "fp32_epilogue_floor_ms": fp32_floor_ms,
                     "algorithmic_ops_per_step": ops, "avg_launch_us": 1e3 * g_ms / max(g_n, 1),
                     "launches_per_step": g_n / args.steps}
         lops = 2.0 * slots * 3 * cfg.f * cfg.d
