@@ -79,6 +79,8 @@ struct pi_sparse_ffn {
     void* down_q = nullptr;
     __half* down_d = nullptr;
     uint8_t* mask = nullptr;  // [n_ff] token bits of the current pass, zero between passes
+    int32_t* wlist = nullptr;  // [n_ff] neurons marked in the pass, in marking order
+    uint32_t* wctr = nullptr;  // [2] list length, next list entry to claim (zero between passes)
     std::vector<void*> allocs;
 };
 

@@ -290,9 +290,12 @@ PI_DEV uint32_t sf_dense_bits(const int64_t* __restrict__ ptr, int t0, int nt, i
 
 // Marks the pass's (token, neuron) pairs: bit t of mask byte s = neuron s in token
 // t0 + t's list, and zeroes h of the pass. The mask starts zero and the gate/up
-// kernel clears every byte it claims, so it is zero again for the next pass.
+// kernel clears every byte it takes, so it is zero again for the next pass. The
+// first mark of a neuron appends it to the work list (wctr[0] = its length), which
+// the gate/up warps drain; the down kernel resets the counters.
 __global__ __launch_bounds__(256) void k_sf_mark(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
                                                  int t0, int nt, int64_t n_ff, uint32_t* __restrict__ mask32,
+                                                 int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr,
                                                  float* __restrict__ h, uint32_t* __restrict__ err) {
     int64_t bnd[SF_TMAX + 1];
 #pragma unroll
@@ -307,11 +310,34 @@ __global__ __launch_bounds__(256) void k_sf_mark(const int64_t* __restrict__ ptr
             atomicOr(err, PI_DEVERR_INDEX);
             continue;
         }
-        atomicOr(&mask32[sn >> 2], 1u << (8 * (sn & 3) + t));
+        const uint32_t old = atomicOr(&mask32[sn >> 2], 1u << (8 * (sn & 3) + t));
+        if (((old >> (8 * (sn & 3))) & 0xFFu) == 0) wlist[atomicAdd(&wctr[0], 1u)] = (int32_t)sn;
     }
 }
 
 PI_DEV float nibf(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616.0f; }
+// packed f32x2 helpers (sm_100 FADD2 / FFMA2 on register pairs)
+PI_DEV uint64_t f2_pack(float lo, float hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+PI_DEV uint64_t f2_pack_u(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+PI_DEV void f2_unpack(uint64_t v, float& lo, float& hi) { asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v)); }
+PI_DEV uint64_t f2_add(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+PI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 // gate/up of every marked (token, neuron) pair, h = SwiGLU(g, u) (quant/mod.rs:1196-1199)
 // into h[t][n] (0 where the pair is not marked); the pass's output rows are zeroed
 // for the down kernel's atomics. Persistent: one CTA per SM stages the pass's
@@ -322,12 +348,13 @@ PI_DEV float nibf(uint32_t v) { return __int_as_float(0x4B000000u | v) - 8388616
 // whole matrix and sums in f32 (quant/mod.rs:958-969).
 // Q8_0: x quantised to Q8_0 (quant/mod.rs:698-736), int8 block dots, block terms
 // (float)sumi * (d_w * d_x) (quant/mod.rs:819-899).
-template <int QT, int BPL>  // BPL: blocks per lane (n_embd = 32 * 32 * BPL)
+template <int QT, int BPL, int NTM>  // BPL: blocks per lane (n_embd = 32 * 32 * BPL); NTM: tokens (1 or 8)
 __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
     const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
     const __half* __restrict__ UD, uint8_t* __restrict__ mask, const float* __restrict__ x,
     const int8_t* __restrict__ xq, const float* __restrict__ xs, const int64_t* __restrict__ ptr,
-    const int64_t* __restrict__ idx, int t0, int nt, int64_t n_ff, float* __restrict__ h, float* __restrict__ y) {
+    const int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr, int t0, int nt, int64_t n_ff,
+    float* __restrict__ h, float* __restrict__ y) {
     extern __shared__ __align__(16) float sf_x[];
     constexpr int NB = 32 * BPL;  // blocks per row
     constexpr int64_t D = 32 * NB;
@@ -353,103 +380,117 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
     }
     const uint32_t dense = sf_dense_bits(ptr, t0, nt, n_ff);
     __syncthreads();
-    const int64_t W = (int64_t)gridDim.x * SF_GU_WARPS;
     constexpr int WPB = QT == PI_QT_Q4_0 ? 1 : 2;  // 16-byte words per block
-    // Work: without a complete list in the pass, the list entries (e = e0 + i W over
-    // every token's list), each claiming its neuron's mask byte (the first claim of a
-    // neuron gets its token bits and runs it; later ones get 0); with a complete list,
-    // every neuron n = n0 + i W. 32 items at a time: lane i takes item i, then the warp
-    // runs the claimed neurons one after another.
-    const int64_t e0 = ptr[t0], e1 = ptr[t0 + nt];
-    const int64_t n_items = dense ? n_ff : e1 - e0;
-    uint32_t* mask32 = reinterpret_cast<uint32_t*>(mask);
-    for (int64_t i0 = blockIdx.x * (int64_t)SF_GU_WARPS + warp; i0 < n_items; i0 += 32 * W) {
-        const int64_t ii = i0 + lane * W;
-        uint32_t mi = 0;
-        int64_t ni = 0;
-        if (ii < n_items) {
-            if (dense) {
-                ni = ii;
-                mi = (mask[ni] | dense) & ((1u << nt) - 1u);
-                mask[ni] = 0;
-            } else {
-                ni = idx[e0 + ii];
-                if (ni >= 0 && ni < n_ff) {
-                    const int sh = 8 * (int)(ni & 3);
-                    mi = (atomicAnd(&mask32[ni >> 2], ~(0xFFu << sh)) >> sh) & 0xFFu;
-                }
-            }
+    // Work: the neurons the pass marked (the work list), or every neuron when a token's
+    // list is complete. Warps claim one neuron at a time from a counter (a claimed
+    // neuron runs for all of its tokens), so the load follows the work as it comes.
+    // The first item of warp w is item w (no atomic); later ones are W + the counter.
+    const uint32_t n_items = dense ? (uint32_t)n_ff : wctr[0];
+    const uint32_t W = gridDim.x * SF_GU_WARPS;
+    bool first = true;
+    auto claim = [&]() -> int64_t {
+        uint32_t i = n_items;
+        if (first) {
+            i = blockIdx.x * SF_GU_WARPS + warp;
+            first = false;
+        } else if (n_items > W && lane == 0 && W + *reinterpret_cast<volatile uint32_t*>(&wctr[1]) < n_items) {
+            i = W + atomicAdd(&wctr[1], 1u);
         }
-        uint32_t act = __ballot_sync(0xffffffffu, mi != 0);
-        int4 wg[BPL][WPB], wu[BPL][WPB];
-        float dg[BPL], du[BPL];
-        auto load = [&](int64_t n) {
+        i = __shfl_sync(0xffffffffu, i, 0);
+        return i < n_items ? (dense ? (int64_t)i : (int64_t)wlist[i]) : -1;
+    };
+    int4 wg[BPL][WPB], wu[BPL][WPB];
+    float dg[BPL], du[BPL];
+    auto load = [&](int64_t n) {
 #pragma unroll
-            for (int j = 0; j < BPL; ++j) {
-                const int b = lane + 32 * j;
+        for (int j = 0; j < BPL; ++j) {
+            const int b = lane + 32 * j;
 #pragma unroll
-                for (int k = 0; k < WPB; ++k) {
-                    wg[j][k] = ld_stream(G + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
-                    wu[j][k] = ld_stream(U + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
-                }
-                dg[j] = __half2float(GD[n * NB + b]);
-                du[j] = __half2float(UD[n * NB + b]);
+            for (int k = 0; k < WPB; ++k) {
+                wg[j][k] = ld_stream(G + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
+                wu[j][k] = ld_stream(U + n * (D * WPB / 2) + (int64_t)b * 16 * WPB + 16 * k);
             }
-        };
-        if (!act) continue;
-        int li = __ffs(act) - 1;
-        load(__shfl_sync(0xffffffffu, ni, li));
-        while (act) {
-            act &= act - 1;
-            const int64_t n = __shfl_sync(0xffffffffu, ni, li);
-            const uint32_t m = __shfl_sync(0xffffffffu, mi, li);
+            dg[j] = __half2float(GD[n * NB + b]);
+            du[j] = __half2float(UD[n * NB + b]);
+        }
+    };
+    int64_t nxt = claim();
+    if (nxt >= 0) load(nxt);
+    while (nxt >= 0) {
+        const int64_t n = nxt;
+        uint32_t m = 0;
+        if (lane == 0) {
+            m = (mask[n] | dense) & ((1u << nt) - 1u);
+            mask[n] = 0;
+        }
+        m = __shfl_sync(0xffffffffu, m, 0);
+        nxt = claim();
+        {
             // this neuron's rows are in registers: compute every marked token
-            float part_g[SF_TMAX], part_u[SF_TMAX];
+            float part_g[NTM], part_u[NTM];
 #pragma unroll
-            for (int t = 0; t < SF_TMAX; ++t) part_g[t] = part_u[t] = 0.f;
+            for (int t = 0; t < NTM; ++t) part_g[t] = part_u[t] = 0.f;
             if (QT == PI_QT_Q4_0) {
                 // each nibble is decoded once and used by every marked token
 #pragma unroll
                 for (int j = 0; j < BPL; ++j) {
                     const int b = lane + 32 * j;
-                    float bg[SF_TMAX], bu[SF_TMAX];
+                    // packed pair accumulators: (element 2k, element 2k + 1) of each token
+                    uint64_t bg2[NTM], bu2[NTM];
 #pragma unroll
-                    for (int t = 0; t < SF_TMAX; ++t) bg[t] = bu[t] = 0.f;
+                    for (int t = 0; t < NTM; ++t) bg2[t] = bu2[t] = 0ull;
                     uint32_t g0 = wg[j][0].x, g1 = wg[j][0].y, g2 = wg[j][0].z, g3 = wg[j][0].w;
                     uint32_t u0 = wu[j][0].x, u1 = wu[j][0].y, u2 = wu[j][0].z, u3 = wu[j][0].w;
+                    const uint64_t off8 = f2_pack(-8388616.0f, -8388616.0f);
 #pragma unroll 1
                     for (int i = 0; i < 4; ++i) {  // word i = elements 8i .. 8i+7 (byte k: 2k low, 2k+1 high)
-                        float fg[8], fu[8];
+                        // nibbles -> f32 (n - 8): byte k of the low / high nibble planes under the
+                        // exponent of 2^23, minus 2^23 + 8, two at a time
+                        uint64_t fg[4], fu[4];
+                        const uint32_t gl = g0 & 0x0F0F0F0Fu, gh = (g0 >> 4) & 0x0F0F0F0Fu;
+                        const uint32_t ul = u0 & 0x0F0F0F0Fu, uh = (u0 >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            fg[e] = nibf((g0 >> (4 * e)) & 15u);
-                            fu[e] = nibf((u0 >> (4 * e)) & 15u);
+                        for (int k = 0; k < 4; ++k) {
+                            fg[k] = f2_add(f2_pack_u(__byte_perm(gl, 0x4B000000u, 0x7440 + k),
+                                                     __byte_perm(gh, 0x4B000000u, 0x7440 + k)), off8);
+                            fu[k] = f2_add(f2_pack_u(__byte_perm(ul, 0x4B000000u, 0x7440 + k),
+                                                     __byte_perm(uh, 0x4B000000u, 0x7440 + k)), off8);
                         }
 #pragma unroll
-                        for (int t = 0; t < SF_TMAX; ++t) {
+                        for (int t = 0; t < NTM; ++t) {
                             if (t >= nt || !((m >> t) & 1u)) continue;
                             const float* xb = sf_x + (size_t)t * NB * 36 + 36 * b + 8 * i;
                             const float4 xa = *reinterpret_cast<const float4*>(xb);
                             const float4 xc = *reinterpret_cast<const float4*>(xb + 4);
-                            const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xc.x, xc.y, xc.z, xc.w};
+                            const uint64_t xp[4] = {f2_pack(xa.x, xa.y), f2_pack(xa.z, xa.w), f2_pack(xc.x, xc.y),
+                                                    f2_pack(xc.z, xc.w)};
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                bg[t] += fg[e] * xv[e];
-                                bu[t] += fu[e] * xv[e];
+                            for (int k = 0; k < 4; ++k) {
+                                bg2[t] = f2_fma(fg[k], xp[k], bg2[t]);
+                                bu2[t] = f2_fma(fu[k], xp[k], bu2[t]);
                             }
                         }
                         g0 = g1; g1 = g2; g2 = g3;
                         u0 = u1; u1 = u2; u2 = u3;
                     }
+                    float bg[NTM], bu[NTM];
 #pragma unroll
-                    for (int t = 0; t < SF_TMAX; ++t) {
+                    for (int t = 0; t < NTM; ++t) {
+                        float a0, a1, c0, c1;
+                        f2_unpack(bg2[t], a0, a1);
+                        f2_unpack(bu2[t], c0, c1);
+                        bg[t] = a0 + a1;
+                        bu[t] = c0 + c1;
+                    }
+#pragma unroll
+                    for (int t = 0; t < NTM; ++t) {
                         part_g[t] += dg[j] * bg[t];
                         part_u[t] += du[j] * bu[t];
                     }
                 }
             } else {
 #pragma unroll
-                for (int t = 0; t < SF_TMAX; ++t) {
+                for (int t = 0; t < NTM; ++t) {
                     if (t >= nt || !((m >> t) & 1u)) continue;
                     float sg = 0.f, su = 0.f;
 #pragma unroll
@@ -474,13 +515,10 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
                 }
             }
             // the next marked neuron's rows are requested before the reductions
-            if (act) {
-                li = __ffs(act) - 1;
-                load(__shfl_sync(0xffffffffu, ni, li));
-            }
+            if (nxt >= 0) load(nxt);
             float hv = 0.f;  // lane t keeps token t's h
 #pragma unroll
-            for (int t = 0; t < SF_TMAX; ++t) {
+            for (int t = 0; t < NTM; ++t) {
                 if (t >= nt || !((m >> t) & 1u)) continue;
                 const float sg = warp_sum(part_g[t]), su = warp_sum(part_u[t]);
                 if (lane == t) hv = swiglu_ref(sg, su);
@@ -501,7 +539,8 @@ constexpr int SF_DN = 64;  // neurons per down CTA (two 32-neuron scale groups)
 template <int QT, int NTM>
 __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
                                                  const float* __restrict__ h, const int64_t* __restrict__ ptr, int t0,
-                                                 int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y) {
+                                                 int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y,
+                                                 uint32_t* __restrict__ wctr) {
     __shared__ float s_h[NTM][SF_DN];
     __shared__ int32_t s_list[SF_DN];
     __shared__ int s_cnt[2];
@@ -511,6 +550,7 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
     const int64_t n0 = (int64_t)blockIdx.y * SF_DN;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t c = blockIdx.x * 512LL + 2 * tid;
+    if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) wctr[0] = wctr[1] = 0;  // gate/up has drained the list
     if (tid < SF_DN) {
 #pragma unroll
         for (int t = 0; t < NTM; ++t) s_h[t][tid] = (t < nt && n0 + tid < n_ff) ? h[(int64_t)t * n_ff + n0 + tid] : 0.f;
@@ -848,9 +888,13 @@ extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const voi
         else if (!rc) F->allocs.push_back(F->down_d);
     }
     if (!rc) {
-        if (pi_cuda_check(ctx, cudaMalloc(&F->mask, n_ff), "cudaMalloc")) rc = PI_ERR_OOM;
+        // mask [n_ff] bytes, then the work list [n_ff] int32 and its two counters
+        const size_t mb = (size_t)n_ff + (size_t)n_ff * 4 + 64;
+        if (pi_cuda_check(ctx, cudaMalloc(&F->mask, mb), "cudaMalloc")) rc = PI_ERR_OOM;
         else F->allocs.push_back(F->mask);
-        if (!rc && pi_cuda_check(ctx, cudaMemset(F->mask, 0, n_ff), "memset")) rc = PI_ERR_CUDA;
+        if (!rc && pi_cuda_check(ctx, cudaMemset(F->mask, 0, mb), "memset")) rc = PI_ERR_CUDA;
+        F->wlist = reinterpret_cast<int32_t*>(F->mask + n_ff);
+        F->wctr = reinterpret_cast<uint32_t*>(F->wlist + n_ff);
     }
     if (!rc) {
         const int64_t nthr = (n_embd / 2) * (n_ff / 32);
@@ -901,7 +945,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         {
             PiProfScope ps(ctx, st, "k_sf_mark");
             k_sf_mark<<<(unsigned)std::min<int64_t>(nt * n_ff / 1024 + 1, 512), 256, 0, st>>>(
-                ptr, idx, (int)t0, nt, n_ff, reinterpret_cast<uint32_t*>(F->mask), hb, ctx->dev_err);
+                ptr, idx, (int)t0, nt, n_ff, reinterpret_cast<uint32_t*>(F->mask), F->wlist, F->wctr, hb, ctx->dev_err);
         }
         {
             PiProfScope ps(ctx, st, "k_sf_gateup");
@@ -910,10 +954,15 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
             const uint8_t* U = (const uint8_t*)F->up.q;
 #define SF_GU(QT, B)                                                                                            \
     {                                                                                                           \
-        pi_smem_attr((const void*)k_sf_gateup<QT, B>, smem);                                                   \
-        k_sf_gateup<QT, B><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(G, U, F->gate.d, F->up.d, F->mask, x, \
-                                                                          xq, xs, ptr, idx, (int)t0, nt, n_ff, hb, \
-                                                                          out);                                 \
+        if (nt == 1) {                                                                                          \
+            pi_smem_attr((const void*)k_sf_gateup<QT, B, 1>, smem);                                             \
+            k_sf_gateup<QT, B, 1><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(                              \
+                G, U, F->gate.d, F->up.d, F->mask, x, xq, xs, ptr, F->wlist, F->wctr, (int)t0, nt, n_ff, hb, out); \
+        } else {                                                                                                \
+            pi_smem_attr((const void*)k_sf_gateup<QT, B, SF_TMAX>, smem);                                       \
+            k_sf_gateup<QT, B, SF_TMAX><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(                        \
+                G, U, F->gate.d, F->up.d, F->mask, x, xq, xs, ptr, F->wlist, F->wctr, (int)t0, nt, n_ff, hb, out); \
+        }                                                                                                       \
     }
             switch ((q4 ? 1 : 16) * (int)(d / 1024)) {
                 case 1: SF_GU(PI_QT_Q4_0, 1) break;
@@ -930,7 +979,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
             PiProfScope ps(ctx, st, "k_sf_down");
             const dim3 dg((unsigned)(d / 512), (unsigned)((n_ff + SF_DN - 1) / SF_DN));
             const uint8_t* DQ = (const uint8_t*)F->down_q;
-#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out)
+#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out, F->wctr)
             if (q4) {
                 if (nt == 1) SF_DOWN(PI_QT_Q4_0, 1);
                 else SF_DOWN(PI_QT_Q4_0, SF_TMAX);
