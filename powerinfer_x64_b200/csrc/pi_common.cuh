@@ -58,6 +58,14 @@ PI_DEV float warp_sum(float v) {
 }
 
 // Streaming 16-byte load that does not pollute L1 (weights are read once).
+// Programmatic dependent launch (kernels launched with pi_pdl_launch): pdl_wait blocks
+// until the stream's previous kernel has completed and its writes are visible (a no-op
+// for a normal launch); pdl_trigger lets the next kernel start launching once every CTA
+// of this one has run it. Call pdl_wait first, unconditionally, in every CTA, so that a
+// kernel never completes before the one it follows.
+PI_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+PI_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 PI_DEV int4 ld_stream(const void* p) {
     int4 r;
     asm volatile("ld.global.nc.L1::no_allocate.v4.s32 {%0,%1,%2,%3}, [%4];"
@@ -65,3 +73,21 @@ PI_DEV int4 ld_stream(const void* p) {
                  : "l"(p));
     return r;
 }
+
+#ifdef __CUDACC__
+// Launch with programmatic stream serialisation (the kernel must start with pdl_wait()).
+template <typename... KArgs, typename... Args>
+inline void pi_pdl_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+#endif

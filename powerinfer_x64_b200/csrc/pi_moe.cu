@@ -52,6 +52,8 @@ constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one wa
 __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
                                               float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
                                               float* __restrict__ xs) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     extern __shared__ float s_row[];
     __shared__ float s_inv;
     const int t = blockIdx.x, tid = threadIdx.x;
@@ -435,6 +437,8 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
                                                         int32_t* __restrict__ counts,
                                                         const int32_t* __restrict__ list,
                                                         const int32_t* __restrict__ n_list) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     __shared__ float s_p[TK_WARPS][32 * NPL];
     __shared__ int s_sel[TK_WARPS][32];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -448,7 +452,7 @@ __global__ __launch_bounds__(TK_WARPS * 32) void k_topk(const float* __restrict_
 void launch_topk(unsigned grid, cudaStream_t st, const float* logits, int T, int E, int k, int has_shgate,
                  int32_t* idx, float* gates, float* shscale, int32_t* counts, const int32_t* list,
                  const int32_t* n_list) {
-#define TOPK(N) k_topk<N><<<grid, TK_WARPS * 32, 0, st>>>(logits, T, E, k, has_shgate, idx, gates, shscale, counts, list, n_list)
+#define TOPK(N) pi_pdl_launch(k_topk<N>, dim3(grid), dim3(TK_WARPS * 32), 0, st, logits, T, E, k, has_shgate, idx, gates, shscale, counts, list, n_list)
     if (E <= 64) TOPK(2);
     else if (E <= 128) TOPK(4);
     else if (E <= 256) TOPK(8);
@@ -482,6 +486,8 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
                                                        int32_t* __restrict__ idx, float* __restrict__ gates,
                                                        float* __restrict__ shscale, int32_t* __restrict__ counts,
                                                        int32_t* __restrict__ tickets, int fuse, uint32_t* err) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     static_assert(!FUSE || TK * R == TK_WARPS * 32, "one warp per top-k token slot");
     extern __shared__ __align__(16) float rd_sm[];
     __shared__ __align__(8) uint64_t full[RD_NC];
@@ -878,6 +884,8 @@ __global__ __launch_bounds__(256) void k_dispatch(const int32_t* __restrict__ id
                                                   int T, int k, int E, int has_shared, int32_t* __restrict__ offsets,
                                                   int32_t* __restrict__ perm, int32_t* __restrict__ slot_of,
                                                   int4* __restrict__ items, int32_t* __restrict__ n_items, int tg) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     __shared__ int red[8];
     __shared__ int s_wsum[8];
     const int e = blockIdx.x;
@@ -1078,6 +1086,8 @@ constexpr int GU_TB = 8;    // tokens per batch: 4 row-vectors x 8 tokens = 32 c
 constexpr int GU_ROWS = 16; // rows per CTA
 template <int CPL>
 __global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     constexpr int NB = 16 * CPL;   // blocks per row
     constexpr int STRIDE = NB + 4; // padded chain stride (floats): conflict-free 16-byte reads
     extern __shared__ __align__(16) float smem[];
@@ -1179,6 +1189,8 @@ constexpr size_t gateup_q8_smem() {
 // matvec quantises its input): warp per 32-block of hf[slot][.].
 __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __restrict__ hq,
                           float* __restrict__ hs) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= nblk) return;
@@ -1207,6 +1219,8 @@ struct DSL {
 };
 template <int CPQ>
 __global__ __launch_bounds__(DS_THREADS, 1) void k_down_q8s(ExpertArgs a, uint32_t* err) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     using L = DSL<CPQ>;
     constexpr int F = L::F, FB = L::FB, BPQ = L::BPQ, TS = L::TS;
     extern __shared__ __align__(128) uint8_t ds_sm[];
@@ -1528,24 +1542,54 @@ __global__ __launch_bounds__(256) void k_combine(const float* __restrict__ x, co
                                                  const float* __restrict__ shscale, const float* __restrict__ y_sh,
                                                  int T, int k, int d, int has_shared, int residual,
                                                  float* __restrict__ out) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     // thread = 4 consecutive columns (16-byte loads); each column's sum keeps the
     // reference order: routed experts ascending, then the shared expert, then x
     const int t = blockIdx.x;
     const int c = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
     if (c >= d) return;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int j = 0; j < k; ++j) {
-        const int slot = slot_of[(size_t)t * k + j];
-        const float g = gates[(size_t)t * k + j];
-        const float4 v = *reinterpret_cast<const float4*>(y + (size_t)slot * d + c);
-        acc.x = fadd(acc.x, fmul(g, v.x));
-        acc.y = fadd(acc.y, fmul(g, v.y));
-        acc.z = fadd(acc.z, fmul(g, v.z));
-        acc.w = fadd(acc.w, fmul(g, v.w));
+    // the shared row's load goes out first; for k <= 8 every slot index, gate and row is
+    // requested before the sum, so the latencies overlap instead of chaining
+    float4 vsh = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (has_shared)
+        vsh = *reinterpret_cast<const float4*>(y_sh ? y_sh + (size_t)t * d + c : y + ((size_t)T * k + t) * d + c);
+    if (k <= 8) {
+        int sl[8];
+        float gj[8];
+        float4 v[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < k) {
+                sl[j] = slot_of[(size_t)t * k + j];
+                gj[j] = gates[(size_t)t * k + j];
+            }
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < k) v[j] = *reinterpret_cast<const float4*>(y + (size_t)sl[j] * d + c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+            if (j < k) {
+                acc.x = fadd(acc.x, fmul(gj[j], v[j].x));
+                acc.y = fadd(acc.y, fmul(gj[j], v[j].y));
+                acc.z = fadd(acc.z, fmul(gj[j], v[j].z));
+                acc.w = fadd(acc.w, fmul(gj[j], v[j].w));
+            }
+    } else {
+        for (int j = 0; j < k; ++j) {
+            const int slot = slot_of[(size_t)t * k + j];
+            const float g = gates[(size_t)t * k + j];
+            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)slot * d + c);
+            acc.x = fadd(acc.x, fmul(g, v.x));
+            acc.y = fadd(acc.y, fmul(g, v.y));
+            acc.z = fadd(acc.z, fmul(g, v.z));
+            acc.w = fadd(acc.w, fmul(g, v.w));
+        }
     }
     if (has_shared) {
         const float g = shscale[t];
-        const float4 v = *reinterpret_cast<const float4*>(y_sh ? y_sh + (size_t)t * d + c : y + ((size_t)T * k + t) * d + c);
+        const float4 v = vsh;
         acc.x = fadd(acc.x, fmul(g, v.x));
         acc.y = fadd(acc.y, fmul(g, v.y));
         acc.z = fadd(acc.z, fmul(g, v.z));
@@ -1889,7 +1933,7 @@ void launch_dispatch(cudaStream_t st, const int32_t* idx, const int32_t* counts,
         k_dispatch<4><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, T, k, E, has_shared, offsets, perm, slot_of,
                                                          items, n_items, tg);
     else
-        k_dispatch<1><<<(unsigned)(E + 1), 256, 0, st>>>(idx, counts, T, k, E, has_shared, offsets, perm, slot_of,
+        pi_pdl_launch(k_dispatch<1>, dim3((unsigned)(E + 1)), dim3(256), 0, st, idx, counts, T, k, E, has_shared, offsets, perm, slot_of,
                                                          items, n_items, tg);
 }
 
@@ -2003,7 +2047,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
 #define GU_Q8(C)                                                                                              \
     case C: {                                                                                                 \
         pi_smem_attr((const void*)k_gateup_q8<C>, gateup_q8_smem<C>());                                       \
-        k_gateup_q8<C><<<gu, 256, gateup_q8_smem<C>(), st>>>(a);                                             \
+        pi_pdl_launch(k_gateup_q8<C>, dim3(gu), dim3(256), gateup_q8_smem<C>(), st, a);                                             \
         break;                                                                                                \
     }
             GU_Q8(2)
@@ -2015,7 +2059,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
         {
             PiProfScope ps(ctx, st, "k_quant_h");
             const int64_t nblk = n_slots * (L->f / 32);
-            k_quant_h<<<(unsigned)((nblk * 32 + 255) / 256), 256, 0, st>>>(B.hf, nblk, B.hq, B.hs);
+            pi_pdl_launch(k_quant_h, dim3((unsigned)((nblk * 32 + 255) / 256)), dim3(256), 0, st, B.hf, nblk, B.hq, B.hs);
         }
         PiProfScope ps(ctx, st, "k_down");
         const int cpq = L->f % 64 ? 0 : (int)(L->f / 64);  // 16-byte chunks per quarter row
@@ -2025,9 +2069,9 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
             pi_smem_attr((const void*)k_down_q8s<8>, DSL<8>::SMEM);
             const unsigned g = (unsigned)std::min<int64_t>((int64_t)ni * (L->d / DS_ROWS), ctx->sm_count);
             switch (cpq) {
-                case 2: k_down_q8s<2><<<g, DS_THREADS, DSL<2>::SMEM, st>>>(a, ctx->dev_err); break;
-                case 4: k_down_q8s<4><<<g, DS_THREADS, DSL<4>::SMEM, st>>>(a, ctx->dev_err); break;
-                case 8: k_down_q8s<8><<<g, DS_THREADS, DSL<8>::SMEM, st>>>(a, ctx->dev_err); break;
+                case 2: pi_pdl_launch(k_down_q8s<2>, dim3(g), dim3(DS_THREADS), DSL<2>::SMEM, st, a, ctx->dev_err); break;
+                case 4: pi_pdl_launch(k_down_q8s<4>, dim3(g), dim3(DS_THREADS), DSL<4>::SMEM, st, a, ctx->dev_err); break;
+                case 8: pi_pdl_launch(k_down_q8s<8>, dim3(g), dim3(DS_THREADS), DSL<8>::SMEM, st, a, ctx->dev_err); break;
             }
             return pi_cuda_check(ctx, cudaGetLastError(), "experts") ? PI_ERR_CUDA : PI_OK;
         }
@@ -2127,7 +2171,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const bool quant = q8 && (!route_only || (flags & PI_FWD_KEEP_Q8));
     if (do_norm || quant) {
         PiProfScope ps(ctx, st, "k_prep");
-        k_prep<<<(unsigned)T, 256, sizeof(float) * d, st>>>(x, d, do_norm, 1e-6f, B.normed, quant ? 1 : 0, B.xq,
+        pi_pdl_launch(k_prep, dim3((unsigned)T), dim3(256), sizeof(float) * d, st, x, d, do_norm, 1e-6f, B.normed, quant ? 1 : 0, B.xq,
                                                              B.xs);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
@@ -2181,7 +2225,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
 #define RD16(N)                                                                                               \
     {                                                                                                         \
         pi_smem_attr((const void*)k_router_dec<16, 8, N, true>, rd_smem<16, 8>(2048));                        \
-        k_router_dec<16, 8, N, true><<<rg, 128, rd_smem<16, 8>(d), st>>>(xin, L->router, L->bias, (int)T, d, \
+        pi_pdl_launch(k_router_dec<16, 8, N, true>, dim3(rg), dim3(128), rd_smem<16, 8>(d), st, xin, L->router, L->bias, (int)T, d, \
                                                                          E, B.logits, k, hs, idx, gates,      \
                                                                          B.shscale, counts, tickets, fuse,    \
                                                                          ctx->dev_err);                       \
@@ -2194,7 +2238,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             } else {
                 pi_smem_attr((const void*)k_router_dec<8, 4, 16, false>, rd_smem<8, 4>(4096));
                 dim3 rg((unsigned)((E + 1 + 7) / 8), (unsigned)((T + 3) / 4));
-                k_router_dec<8, 4, 16, false><<<rg, 32, rd_smem<8, 4>(d), st>>>(
+                pi_pdl_launch(k_router_dec<8, 4, 16, false>, dim3(rg), dim3(32), rd_smem<8, 4>(d), st, 
                     xin, L->router, L->bias, (int)T, d, E, B.logits, k, hs, idx, gates, B.shscale, counts, tickets, 0,
                     ctx->dev_err);
                 launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
@@ -2223,7 +2267,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     }
     if (int rc = run_experts(ctx, L, a, T, n_slots, ni, gemm, B, st, flags)) return rc;
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<dim3((unsigned)T, (unsigned)((d + 1023) / 1024)), 256, 0, st>>>(x, B.y, gates, B.slot_of, B.shscale,
+    pi_pdl_launch(k_combine, dim3(dim3((unsigned)T, (unsigned)((d + 1023) / 1024))), dim3(256), 0, st, x, B.y, gates, B.slot_of, B.shscale,
                                                                            nullptr, (int)T, k, d,
                                                                            L->has_shared ? 1 : 0,
                                                                            (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
@@ -2321,7 +2365,7 @@ int pi_moe_ep_combine_run(pi_ctx* ctx, const pi_moe_layer* L, const float* x, in
                           float* out, cudaStream_t st) {
     const int d = (int)L->d;
     PiProfScope ps(ctx, st, "k_combine");
-    k_combine<<<dim3((unsigned)T, (unsigned)((d + 1023) / 1024)), 256, 0, st>>>(
+    pi_pdl_launch(k_combine, dim3(dim3((unsigned)T, (unsigned)((d + 1023) / 1024))), dim3(256), 0, st, 
         x, y_back, gates, slot_row, shscale, y_shared, (int)T, L->k, d, (L->has_shared && y_shared) ? 1 : 0,
         (flags & PI_FWD_RESIDUAL) ? 1 : 0, out);
     return pi_cuda_check(ctx, cudaGetLastError(), "ep combine") ? PI_ERR_CUDA : PI_OK;
