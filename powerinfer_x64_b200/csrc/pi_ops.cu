@@ -297,6 +297,8 @@ __global__ __launch_bounds__(256) void k_sf_mark(const int64_t* __restrict__ ptr
                                                  int t0, int nt, int64_t n_ff, uint32_t* __restrict__ mask32,
                                                  int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr,
                                                  float* __restrict__ h, uint32_t* __restrict__ err) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     int64_t bnd[SF_TMAX + 1];
 #pragma unroll
     for (int t = 0; t <= SF_TMAX; ++t) bnd[t] = t <= nt ? ptr[t0 + t] : 0;
@@ -355,6 +357,8 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
     const int8_t* __restrict__ xq, const float* __restrict__ xs, const int64_t* __restrict__ ptr,
     const int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr, int t0, int nt, int64_t n_ff,
     float* __restrict__ h, float* __restrict__ y) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     extern __shared__ __align__(16) float sf_x[];
     constexpr int NB = 32 * BPL;  // blocks per row
     constexpr int64_t D = 32 * NB;
@@ -541,6 +545,8 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
                                                  const float* __restrict__ h, const int64_t* __restrict__ ptr, int t0,
                                                  int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y,
                                                  uint32_t* __restrict__ wctr) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
     __shared__ float s_h[NTM][SF_DN];
     __shared__ int32_t s_list[SF_DN];
     __shared__ int s_cnt[2];
@@ -944,7 +950,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
         {
             PiProfScope ps(ctx, st, "k_sf_mark");
-            k_sf_mark<<<(unsigned)std::min<int64_t>(nt * n_ff / 1024 + 1, 512), 256, 0, st>>>(
+            pi_pdl_launch(k_sf_mark, dim3((unsigned)std::min<int64_t>(nt * n_ff / 1024 + 1, 512)), dim3(256), 0, st,
                 ptr, idx, (int)t0, nt, n_ff, reinterpret_cast<uint32_t*>(F->mask), F->wlist, F->wctr, hb, ctx->dev_err);
         }
         {
@@ -956,11 +962,11 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
     {                                                                                                           \
         if (nt == 1) {                                                                                          \
             pi_smem_attr((const void*)k_sf_gateup<QT, B, 1>, smem);                                             \
-            k_sf_gateup<QT, B, 1><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(                              \
+            pi_pdl_launch(k_sf_gateup<QT, B, 1>, dim3((unsigned)sms), dim3(SF_GU_WARPS * 32), smem, st,        \
                 G, U, F->gate.d, F->up.d, F->mask, x, xq, xs, ptr, F->wlist, F->wctr, (int)t0, nt, n_ff, hb, out); \
         } else {                                                                                                \
             pi_smem_attr((const void*)k_sf_gateup<QT, B, SF_TMAX>, smem);                                       \
-            k_sf_gateup<QT, B, SF_TMAX><<<(unsigned)sms, SF_GU_WARPS * 32, smem, st>>>(                        \
+            pi_pdl_launch(k_sf_gateup<QT, B, SF_TMAX>, dim3((unsigned)sms), dim3(SF_GU_WARPS * 32), smem, st,  \
                 G, U, F->gate.d, F->up.d, F->mask, x, xq, xs, ptr, F->wlist, F->wctr, (int)t0, nt, n_ff, hb, out); \
         }                                                                                                       \
     }
@@ -979,7 +985,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
             PiProfScope ps(ctx, st, "k_sf_down");
             const dim3 dg((unsigned)(d / 512), (unsigned)((n_ff + SF_DN - 1) / SF_DN));
             const uint8_t* DQ = (const uint8_t*)F->down_q;
-#define SF_DOWN(QT, NTM) k_sf_down<QT, NTM><<<dg, 256, 0, st>>>(DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out, F->wctr)
+#define SF_DOWN(QT, NTM) pi_pdl_launch(k_sf_down<QT, NTM>, dg, dim3(256), 0, st, DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out, F->wctr)
             if (q4) {
                 if (nt == 1) SF_DOWN(PI_QT_Q4_0, 1);
                 else SF_DOWN(PI_QT_Q4_0, SF_TMAX);
