@@ -238,13 +238,16 @@ def expert_forward(x, gate_w, up_w, down_w, n_embd: int, expert_ffn_dim: int):
 
 
 def moe_forward(x, router: MoeRouter, expert_provider, n_embd: int, expert_ffn_dim: int):
-    """moe/mod.rs:193-219: route, run the k experts, weighted sum in routing order."""
-    torch = _torch()
+    """moe/mod.rs:193-219: route, run the k experts, weighted sum in routing order.
+
+    The routing and every expert's SwiGLU run on the GPU (``pi_router_topk_softmax``,
+    ``pi_ffn_swiglu_q``); like the reference, the caller's vector lives on the host, so
+    the k-term weighted sum is done there in f32, multiply then add per term, in the
+    routing order (moe/mod.rs:211-216)."""
     routing = router.route(x)
-    out = torch.zeros(n_embd, dtype=torch.float32, device="cuda")
+    out = np.zeros(n_embd, np.float32)
     for i, e in enumerate(routing.expert_indices):
         g, u, d = expert_provider.get_expert_f32(e)
-        eo = torch.from_numpy(expert_forward(x, g, u, d, n_embd, expert_ffn_dim)).cuda()
-        w = torch.tensor(routing.expert_weights[i], dtype=torch.float32, device="cuda")
-        out += w * eo  # f32 multiply then add (separate kernels: no FMA)
-    return out.cpu().numpy()
+        eo = expert_forward(x, g, u, d, n_embd, expert_ffn_dim)
+        out = out + np.float32(routing.expert_weights[i]) * eo
+    return out
