@@ -42,6 +42,50 @@ namespace {
 
 constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one warp per token)
 
+// One token row xr (global or shared memory) by a 256-thread CTA; __syncthreads inside.
+PI_DEV void split_row(const float* xr, int t, int d, __half* __restrict__ xh, __half* __restrict__ xl,
+                      float* __restrict__ xnorm) {
+    __shared__ double red[8];
+    __shared__ int s_bad;
+    const int tid = threadIdx.x;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+    double ss = 0.0;
+    bool bad = false;
+    for (int c = tid * 8; c < d; c += 256 * 8) {
+        const float4 v0 = *reinterpret_cast<const float4*>(xr + c);
+        const float4 v1 = *reinterpret_cast<const float4*>(xr + c + 4);
+        const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+        uint32_t hi[4], lo[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const __half2 hv = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
+            const float2 hf = __half22float2(hv);
+            const __half2 lv = __floats2half2_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
+            hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
+            lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            ss += (double)f[j] * (double)f[j];
+            bad |= !(fabsf(f[j]) < 32768.0f);
+        }
+        *reinterpret_cast<uint4*>(xh + (size_t)t * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<uint4*>(xl + (size_t)t * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    if (bad) s_bad = 1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    if (tid == 0) {
+        double tot = 0.0;
+        for (int w = 0; w < 8; ++w) tot += red[w];
+        // the f64 sum is within ~2^-40 relative; 1 + 2^-20 covers it and the f32 rounding
+        xnorm[t] = s_bad ? INFINITY : __double2float_ru(__dsqrt_ru(tot) * (1.0 + 0x1p-20));
+    }
+}
+
 // ---------------------------------------------------------------------------
 // k_prep: optional RMSNorm, then Q8_0 quantisation of the (normed) tokens.
 // grid T, block 256, dynamic shared memory d floats: the CTA stages its token
@@ -51,7 +95,8 @@ constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one wa
 // ---------------------------------------------------------------------------
 __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
                                               float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
-                                              float* __restrict__ xs) {
+                                              float* __restrict__ xs, __half* __restrict__ xh,
+                                              __half* __restrict__ xl, float* __restrict__ xnorm) {
     pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
     pdl_trigger();
     extern __shared__ float s_row[];
@@ -90,6 +135,7 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
         if (do_norm) {
             v = fmul(v, inv);  // * weight (1.0) is exact
             normed[(size_t)t * d + i] = v;
+            s_row[i] = v;
         }
         if (do_quant) {
             float sc;
@@ -98,6 +144,8 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
             if ((tid & 31) == 0) xs[(size_t)t * (d / 32) + i / 32] = sc;
         }
     }
+    // the certified tensor-core router's f16 hi/lo split and norm bound of the (normed) row
+    if (xh) split_row(s_row, t, d, xh, xl, xnorm);
 }
 
 // ---------------------------------------------------------------------------
@@ -561,48 +609,10 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
 // grid T, block 256.
 // ---------------------------------------------------------------------------
 constexpr int KC_ROUTER = 32, TC_PER_LANE = 8, TC_WARPS = 4, RCH = 64, RPF = 8;
+
 __global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ x, int d, __half* __restrict__ xh,
                                                       __half* __restrict__ xl, float* __restrict__ xnorm) {
-    __shared__ double red[8];
-    __shared__ int s_bad;
-    const int t = blockIdx.x, tid = threadIdx.x;
-    if (tid == 0) s_bad = 0;
-    __syncthreads();
-    const float* xr = x + (size_t)t * d;
-    double ss = 0.0;
-    bool bad = false;
-    for (int c = tid * 8; c < d; c += 256 * 8) {
-        const float4 v0 = *reinterpret_cast<const float4*>(xr + c);
-        const float4 v1 = *reinterpret_cast<const float4*>(xr + c + 4);
-        const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-        uint32_t hi[4], lo[4];
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const __half2 hv = __floats2half2_rn(f[2 * q], f[2 * q + 1]);
-            const float2 hf = __half22float2(hv);
-            const __half2 lv = __floats2half2_rn(f[2 * q] - hf.x, f[2 * q + 1] - hf.y);
-            hi[q] = *reinterpret_cast<const uint32_t*>(&hv);
-            lo[q] = *reinterpret_cast<const uint32_t*>(&lv);
-        }
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            ss += (double)f[j] * (double)f[j];
-            bad |= !(fabsf(f[j]) < 32768.0f);
-        }
-        *reinterpret_cast<uint4*>(xh + (size_t)t * d + c) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(xl + (size_t)t * d + c) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-    }
-    if (bad) s_bad = 1;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if ((tid & 31) == 0) red[tid >> 5] = ss;
-    __syncthreads();
-    if (tid == 0) {
-        double tot = 0.0;
-        for (int w = 0; w < 8; ++w) tot += red[w];
-        // the f64 sum is within ~2^-40 relative; 1 + 2^-20 covers it and the f32 rounding
-        xnorm[t] = s_bad ? INFINITY : __double2float_ru(__dsqrt_ru(tot) * (1.0 + 0x1p-20));
-    }
+    split_row(x + (size_t)blockIdx.x * d, blockIdx.x, d, xh, xl, xnorm);
 }
 
 // ---------------------------------------------------------------------------
@@ -2171,8 +2181,10 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     const bool quant = q8 && (!route_only || (flags & PI_FWD_KEEP_Q8));
     if (do_norm || quant) {
         PiProfScope ps(ctx, st, "k_prep");
-        pi_pdl_launch(k_prep, dim3((unsigned)T), dim3(256), sizeof(float) * d, st, x, d, do_norm, 1e-6f, B.normed, quant ? 1 : 0, B.xq,
-                                                             B.xs);
+        const bool split = use_router_tc(L, T);  // the router's hi/lo split comes from this pass
+        pi_pdl_launch(k_prep, dim3((unsigned)T), dim3(256), sizeof(float) * d, st, x, d, do_norm, 1e-6f, B.normed,
+                      quant ? 1 : 0, B.xq, B.xs, split ? B.xth : nullptr, split ? B.xtl : nullptr,
+                      split ? B.xnorm : nullptr);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
@@ -2181,7 +2193,7 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     if (use_router_tc(L, T)) {
         // prefill-sized batch: fast logits on tensor cores, exact chains for the
         // candidates of each token, the exact path for tokens that stay uncertain
-        {
+        if (!(do_norm || quant)) {  // else k_prep made the split
             PiProfScope ps(ctx, st, "k_split_tokens");
             k_split_tokens<<<(unsigned)T, 256, 0, st>>>(xin, d, B.xth, B.xtl, B.xnorm);
         }
