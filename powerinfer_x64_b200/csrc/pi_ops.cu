@@ -289,10 +289,10 @@ PI_DEV uint32_t sf_dense_bits(const int64_t* __restrict__ ptr, int t0, int nt, i
 }
 
 // Marks the pass's (token, neuron) pairs: bit t of mask byte s = neuron s in token
-// t0 + t's list, and zeroes h of the pass. The mask starts zero and the gate/up
-// kernel clears every byte it takes, so it is zero again for the next pass. The
-// first mark of a neuron appends it to the work list (wctr[0] = its length), which
-// the gate/up warps drain; the down kernel resets the counters.
+// t0 + t's list, and zeroes h of the pass. The mask starts zero; the down kernel
+// clears it (with coalesced stores, after gate/up has read it) and resets the
+// counters, so both are zero again for the next pass. The first mark of a neuron
+// appends it to the work list (wctr[0] = its length), which the gate/up warps drain.
 __global__ __launch_bounds__(256) void k_sf_mark(const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
                                                  int t0, int nt, int64_t n_ff, uint32_t* __restrict__ mask32,
                                                  int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr,
@@ -422,12 +422,11 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
     if (nxt >= 0) load(nxt);
     while (nxt >= 0) {
         const int64_t n = nxt;
-        uint32_t m = 0;
-        if (lane == 0) {
-            m = (mask[n] | dense) & ((1u << nt) - 1u);
-            mask[n] = 0;
+        uint32_t m = 1;  // one token: every listed neuron is its own (no mask read to wait for)
+        if (NTM != 1) {
+            if (lane == 0) m = (mask[n] | dense) & ((1u << nt) - 1u);
+            m = __shfl_sync(0xffffffffu, m, 0);
         }
-        m = __shfl_sync(0xffffffffu, m, 0);
         nxt = claim();
         {
             // this neuron's rows are in registers: compute every marked token
@@ -544,7 +543,7 @@ template <int QT, int NTM>
 __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ, const __half* __restrict__ DS,
                                                  const float* __restrict__ h, const int64_t* __restrict__ ptr, int t0,
                                                  int nt, int64_t n_embd, int64_t n_ff, float* __restrict__ y,
-                                                 uint32_t* __restrict__ wctr) {
+                                                 uint32_t* __restrict__ wctr, uint8_t* __restrict__ mask) {
     pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
     pdl_trigger();
     __shared__ float s_h[NTM][SF_DN];
@@ -557,6 +556,9 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t c = blockIdx.x * 512LL + 2 * tid;
     if (blockIdx.x == 0 && blockIdx.y == 0 && tid == 0) wctr[0] = wctr[1] = 0;  // gate/up has drained the list
+    // the pass's marks are read: clear this neuron group's mask bytes for the next pass
+    if (blockIdx.x == 0 && tid < SF_DN / 16 && n0 + 16 * (tid + 1) <= n_ff)
+        reinterpret_cast<uint4*>(mask + n0)[tid] = make_uint4(0, 0, 0, 0);
     if (tid < SF_DN) {
 #pragma unroll
         for (int t = 0; t < NTM; ++t) s_h[t][tid] = (t < nt && n0 + tid < n_ff) ? h[(int64_t)t * n_ff + n0 + tid] : 0.f;
@@ -985,7 +987,7 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
             PiProfScope ps(ctx, st, "k_sf_down");
             const dim3 dg((unsigned)(d / 512), (unsigned)((n_ff + SF_DN - 1) / SF_DN));
             const uint8_t* DQ = (const uint8_t*)F->down_q;
-#define SF_DOWN(QT, NTM) pi_pdl_launch(k_sf_down<QT, NTM>, dg, dim3(256), 0, st, DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out, F->wctr)
+#define SF_DOWN(QT, NTM) pi_pdl_launch(k_sf_down<QT, NTM>, dg, dim3(256), 0, st, DQ, F->down_d, hb, ptr, (int)t0, nt, d, n_ff, out, F->wctr, F->mask)
             if (q4) {
                 if (nt == 1) SF_DOWN(PI_QT_Q4_0, 1);
                 else SF_DOWN(PI_QT_Q4_0, SF_TMAX);
