@@ -24,8 +24,10 @@ int pi_cuda_check(pi_ctx* ctx, cudaError_t e, const char* what) {
 // The dynamic shared-memory limit is an attribute of a kernel on one device, so
 // it is raised once per (kernel, current device) and again whenever a launch
 // needs more than was set; the record is shared by every thread of the process.
+// The default limit covers static plus dynamic bytes up to 48 KB, so a request
+// within 40 KB leaves any kernel here room for its static shared memory.
 void pi_smem_attr(const void* fn, size_t bytes) {
-    if (bytes <= 48 * 1024) return;
+    if (bytes <= 40 * 1024) return;
     static std::mutex mu;
     static std::map<std::pair<const void*, int>, size_t> done;
     int dev = 0;

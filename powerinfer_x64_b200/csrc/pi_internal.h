@@ -81,6 +81,9 @@ struct pi_sparse_ffn {
     uint8_t* mask = nullptr;  // [n_ff] token bits of the current pass, zero between passes
     int32_t* wlist = nullptr;  // [n_ff] neurons marked in the pass, in marking order
     uint32_t* wctr = nullptr;  // [2] list length, next list entry to claim (zero between passes)
+    uint32_t* fbar = nullptr;  // fused pass: grid barrier {count, generation}
+    uint32_t* tick = nullptr;  // fused pass: [n_ff / 32] per-range tickets (zero between passes)
+    bool fused = true;         // one fused launch per pass (PI_SF_SPLIT=1 at create: three launches)
     std::vector<void*> allocs;
 };
 

@@ -350,20 +350,24 @@ PI_DEV uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
 // whole matrix and sums in f32 (quant/mod.rs:958-969).
 // Q8_0: x quantised to Q8_0 (quant/mod.rs:698-736), int8 block dots, block terms
 // (float)sumi * (d_w * d_x) (quant/mod.rs:819-899).
-template <int QT, int BPL, int NTM>  // BPL: blocks per lane (n_embd = 32 * 32 * BPL); NTM: tokens (1 or 8)
-__global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
-    const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
-    const __half* __restrict__ UD, uint8_t* __restrict__ mask, const float* __restrict__ x,
-    const int8_t* __restrict__ xq, const float* __restrict__ xs, const int64_t* __restrict__ ptr,
-    const int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr, int t0, int nt, int64_t n_ff,
-    float* __restrict__ h, float* __restrict__ y) {
-    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
-    pdl_trigger();
-    extern __shared__ __align__(16) float sf_x[];
+// DIRECT (one token, the fused pass): the work items are the token's own list
+// entries, read straight from idx; a neuron listed twice is computed once (the
+// first claim sets its mask bit, a later claim that finds the bit set skips it),
+// and out-of-range entries set PI_DEVERR_INDEX and are skipped.
+template <int QT, int BPL, int NTM, bool DIRECT>
+PI_DEV void sf_gateup_body(const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
+                           const __half* __restrict__ UD, uint8_t* __restrict__ mask, const float* __restrict__ x,
+                           const int8_t* __restrict__ xq, const float* __restrict__ xs,
+                           const int64_t* __restrict__ ptr, const int64_t* __restrict__ idx,
+                           const int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr, int t0, int nt,
+                           int64_t n_ff, float* __restrict__ h, float* __restrict__ y, uint32_t* __restrict__ err,
+                           float* __restrict__ sf_x) {
+    static_assert(!DIRECT || NTM == 1, "list entries as work items: one token per pass");
     constexpr int NB = 32 * BPL;  // blocks per row
     constexpr int64_t D = 32 * NB;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    // stage the pass's activations; zero its output rows
+    // stage the pass's activations; zero its output rows (run after the first rows are requested)
+    auto stage_x = [&]() {
     if (QT == PI_QT_Q4_0) {
         for (int k = tid; k < nt * (int)D / 4; k += blockDim.x) {
             const int t = k / ((int)D / 4), r = k % ((int)D / 4);
@@ -382,26 +386,43 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
         for (int64_t k = blockIdx.x * (int64_t)blockDim.x + tid; k < nt * D / 4; k += (int64_t)gridDim.x * blockDim.x)
             o4[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    };
     const uint32_t dense = sf_dense_bits(ptr, t0, nt, n_ff);
-    __syncthreads();
     constexpr int WPB = QT == PI_QT_Q4_0 ? 1 : 2;  // 16-byte words per block
     // Work: the neurons the pass marked (the work list), or every neuron when a token's
     // list is complete. Warps claim one neuron at a time from a counter (a claimed
     // neuron runs for all of its tokens), so the load follows the work as it comes.
     // The first item of warp w is item w (no atomic); later ones are W + the counter.
-    const uint32_t n_items = dense ? (uint32_t)n_ff : wctr[0];
+    // (the list length is read through L2: in the fused pass other CTAs wrote it)
+    const int64_t p0 = DIRECT ? ptr[t0] : 0;
+    const uint32_t n_items = dense ? (uint32_t)n_ff
+                                   : (DIRECT ? (uint32_t)(ptr[t0 + 1] - p0) : __ldcg(&wctr[0]));
     const uint32_t W = gridDim.x * SF_GU_WARPS;
     bool first = true;
     auto claim = [&]() -> int64_t {
-        uint32_t i = n_items;
-        if (first) {
-            i = blockIdx.x * SF_GU_WARPS + warp;
-            first = false;
-        } else if (n_items > W && lane == 0 && W + *reinterpret_cast<volatile uint32_t*>(&wctr[1]) < n_items) {
-            i = W + atomicAdd(&wctr[1], 1u);
+        for (;;) {
+            uint32_t i = n_items;
+            if (first) {
+                i = blockIdx.x * SF_GU_WARPS + warp;
+                first = false;
+            } else if (n_items > W && lane == 0 && W + *reinterpret_cast<volatile uint32_t*>(&wctr[1]) < n_items) {
+                i = W + atomicAdd(&wctr[1], 1u);
+            }
+            i = __shfl_sync(0xffffffffu, i, 0);
+            if (i >= n_items) return -1;
+            if (dense) return (int64_t)i;
+            if (!DIRECT) return (int64_t)__ldcg(&wlist[i]);
+            const int64_t sn = idx[p0 + i];
+            if (sn >= 0 && sn < n_ff) return sn;
+            if (lane == 0) atomicOr(err, PI_DEVERR_INDEX);
         }
-        i = __shfl_sync(0xffffffffu, i, 0);
-        return i < n_items ? (dense ? (int64_t)i : (int64_t)wlist[i]) : -1;
+    };
+    // DIRECT: the claim that sets neuron n's mask bit computes it; a repeated entry skips
+    auto repeated = [&](int64_t n) -> bool {
+        if (!DIRECT || dense) return false;
+        uint32_t old = 0;
+        if (lane == 0) old = atomicOr(reinterpret_cast<uint32_t*>(mask) + (n >> 2), 1u << (8 * (n & 3)));
+        return (__shfl_sync(0xffffffffu, old, 0) >> (8 * (n & 3))) & 1u;
     };
     int4 wg[BPL][WPB], wu[BPL][WPB];
     float dg[BPL], du[BPL];
@@ -419,14 +440,22 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
         }
     };
     int64_t nxt = claim();
-    if (nxt >= 0) load(nxt);
+    bool nxt_rep = false;
+    if (nxt >= 0) {
+        load(nxt);
+        nxt_rep = repeated(nxt);
+    }
+    stage_x();  // while the first rows are in flight
+    __syncthreads();
     while (nxt >= 0) {
         const int64_t n = nxt;
+        const bool rep = nxt_rep;
         uint32_t m = 1;  // one token: every listed neuron is its own (no mask read to wait for)
         if (NTM != 1) {
-            if (lane == 0) m = (mask[n] | dense) & ((1u << nt) - 1u);
+            if (lane == 0) m = (__ldcg(&mask[n]) | dense) & ((1u << nt) - 1u);
             m = __shfl_sync(0xffffffffu, m, 0);
         }
+        if (rep) m = 0;
         nxt = claim();
         {
             // this neuron's rows are in registers: compute every marked token
@@ -518,7 +547,10 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
                 }
             }
             // the next marked neuron's rows are requested before the reductions
-            if (nxt >= 0) load(nxt);
+            if (nxt >= 0) {
+                load(nxt);
+                nxt_rep = repeated(nxt);
+            }
             float hv = 0.f;  // lane t keeps token t's h
 #pragma unroll
             for (int t = 0; t < NTM; ++t) {
@@ -526,9 +558,23 @@ __global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
                 const float sg = warp_sum(part_g[t]), su = warp_sum(part_u[t]);
                 if (lane == t) hv = swiglu_ref(sg, su);
             }
-            if (lane < nt) h[(int64_t)lane * n_ff + n] = hv;
+            if (lane < nt && !rep) h[(int64_t)lane * n_ff + n] = hv;
         }
     }
+}
+
+template <int QT, int BPL, int NTM>  // BPL: blocks per lane (n_embd = 32 * 32 * BPL); NTM: tokens (1 or 8)
+__global__ __launch_bounds__(SF_GU_WARPS * 32, 1) void k_sf_gateup(
+    const uint8_t* __restrict__ G, const uint8_t* __restrict__ U, const __half* __restrict__ GD,
+    const __half* __restrict__ UD, uint8_t* __restrict__ mask, const float* __restrict__ x,
+    const int8_t* __restrict__ xq, const float* __restrict__ xs, const int64_t* __restrict__ ptr,
+    const int32_t* __restrict__ wlist, uint32_t* __restrict__ wctr, int t0, int nt, int64_t n_ff,
+    float* __restrict__ h, float* __restrict__ y) {
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
+    extern __shared__ __align__(16) float sf_x[];
+    sf_gateup_body<QT, BPL, NTM, false>(G, U, GD, UD, mask, x, xq, xs, ptr, nullptr, wlist, wctr, t0, nt, n_ff, h, y,
+                                        nullptr, sf_x);
 }
 
 // down, neuron-major, of the pass: CTA = (512 output columns, 64 neurons), thread =
@@ -638,6 +684,279 @@ __global__ __launch_bounds__(256) void k_sf_down(const uint8_t* __restrict__ DQ,
     for (int t = 0; t < NTM; ++t)
         if (t < nt && (acc[t][0] != 0.f || acc[t][1] != 0.f))
             atomicAdd(reinterpret_cast<float2*>(y + (int64_t)(t0 + t) * n_embd + c), make_float2(acc[t][0], acc[t][1]));
+}
+
+// ---------------------------------------------------------------------------
+// A one-token sparse-FFN pass in one persistent kernel (one CTA of 512 threads per
+// SM, every CTA resident): gate/up -> grid barrier -> down. It computes what
+// k_sf_mark, k_sf_gateup and k_sf_down compute for one token, without their launch
+// gaps: gate/up warps take the token's list entries straight from idx (a repeated
+// entry is computed once: the first claim sets the neuron's mask bit), and each
+// CTA prefetches the down block scales of its first unit while gate/up runs.
+// (Passes of several tokens keep the three launches: measured, a mark phase and a
+// second barrier inside one kernel cost more than the launches they replace.)
+//
+// Down work unit = (512 output columns, a range of RN consecutive neurons, RN a
+// multiple of 32 so the range holds whole 32-neuron scale groups). The unit finds
+// its active neurons from the mask (every neuron when the token's list is
+// complete), stages their weight slices by cp.async in
+// double-buffered chunks (as many neurons as the shared memory left by gate/up
+// holds, at least 128), sums them in two halves of 256 threads (2 columns a
+// thread, packed f32x2 fused multiply-adds) and adds the result to y with float2
+// atomics. The last of the
+// n_embd / 512 units of a range to read the range's mask clears it (a ticket per
+// range), so the mask is zero again for the next pass; CTA 0 resets the work-list
+// counters after the second barrier.
+// ---------------------------------------------------------------------------
+struct SfGridBar {
+    uint32_t count, gen;
+};
+
+// Grid-wide barrier for a kernel whose CTAs are all resident: the last CTA to
+// arrive resets the count and advances the generation the others wait on. The
+// wait is bounded (2^24 polls, the later ones 32 ns apart: about half a second);
+// when it runs out, the kernel
+// records PI_DEVERR_TIMEOUT and every CTA returns.
+PI_DEV bool sf_grid_sync(SfGridBar* g, uint32_t* err, int* s_ok) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int ok = 1;
+        volatile uint32_t* gen = &g->gen;
+        const uint32_t g0 = *gen;
+        __threadfence();
+        if (atomicAdd(&g->count, 1u) == gridDim.x - 1) {
+            atomicExch(&g->count, 0u);
+            __threadfence();
+            atomicAdd(&g->gen, 1u);
+        } else {
+            uint32_t it = 0;
+            while (*gen == g0) {
+                if (++it > (1u << 24)) {
+                    ok = 0;
+                    atomicOr(err, PI_DEVERR_TIMEOUT);
+                    break;
+                }
+                if (it > 4096) __nanosleep(32);
+            }
+        }
+        __threadfence();
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+struct SfFusedArgs {
+    const uint8_t *G, *U;
+    const __half *GD, *UD;
+    const uint8_t* DQ;
+    const __half* DS;
+    uint8_t* mask;
+    int32_t* wlist;
+    uint32_t* wctr;
+    uint32_t* tick;  // [n_ff / 32] per-range tickets, zero between passes
+    SfGridBar* bar;
+    const float* x;
+    const int8_t* xq;
+    const float* xs;
+    const int64_t *ptr, *idx;
+    int t0, nt, rn, fch;  // rn: neurons per down range; fch: neurons per down chunk (multiple of 32)
+    int64_t n_embd, n_ff;
+    float *h, *y;
+    uint32_t* err;
+    uint32_t stage_bytes;  // bytes of the staging region (x for gate/up, then the down chunks)
+};
+
+constexpr int SF_FT = 512;   // threads of a fused CTA
+constexpr int SF_FMAXG = 32;  // scale groups per range (bounds the prefetched scales)
+
+template <int QT, int BPL>
+__global__ __launch_bounds__(SF_FT, 1) void k_sf_fused(const __grid_constant__ SfFusedArgs a) {
+    constexpr int NTM = 1;
+    static_assert(SF_GU_WARPS * 32 == SF_FT, "gate/up body runs on the fused CTA");
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    extern __shared__ __align__(16) uint8_t sf_sm[];
+    constexpr int RB = QT == PI_QT_Q4_0 ? 256 : 512;  // bytes of one neuron's 512 columns
+    __shared__ int s_ok, s_cnt[SF_FT / 32], s_flag;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nt = a.nt;
+    const int64_t n_ff = a.n_ff, d = a.n_embd;
+    const int n_cc = (int)(d / 512), rn = a.rn;
+    const int n_rng = (int)((n_ff + rn - 1) / rn), n_units = n_cc * n_rng;
+    // dynamic shared memory: [staging | down chunk] [scales of a range] [active list]
+    uint8_t* stage = sf_sm;
+    __half2* s_sc = reinterpret_cast<__half2*>(sf_sm + a.stage_bytes);  // [group][256] column pairs
+    uint32_t* s_act = reinterpret_cast<uint32_t*>(sf_sm + a.stage_bytes + SF_FMAXG * 1024);
+    auto load_scales = [&](int u) {
+        const int cc = u % n_cc;
+        const int64_t s0 = (int64_t)(u / n_cc) * rn;
+        const int ng = (int)(min((int64_t)rn, n_ff - s0) / 32);
+        for (int q = tid; q < ng * 64; q += SF_FT) {  // 64 pieces of 16 bytes per group
+            const int g = q >> 6, pc = q & 63;
+            const uint32_t sa = (uint32_t)__cvta_generic_to_shared(reinterpret_cast<uint8_t*>(s_sc) + g * 1024 + 16 * pc);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa),
+                         "l"(a.DS + (s0 / 32 + g) * d + cc * 512 + 8 * pc)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    if (blockIdx.x < n_units) load_scales(blockIdx.x);  // lands while gate/up runs
+
+    const uint32_t tmask = 1u;
+    // ---- gate/up (h of the listed neurons; the token's row of y zeroed)
+    sf_gateup_body<QT, BPL, 1, true>(a.G, a.U, a.GD, a.UD, a.mask, a.x, a.xq, a.xs, a.ptr, a.idx, a.wlist, a.wctr,
+                                     a.t0, nt, n_ff, a.h, a.y, a.err, reinterpret_cast<float*>(stage));
+    if (!sf_grid_sync(a.bar, a.err, &s_ok)) return;
+    pdl_trigger();  // every CTA is resident and past its last wait on the others
+    if (blockIdx.x == 0 && tid == 0) a.wctr[0] = a.wctr[1] = 0;  // the list is drained
+    const uint32_t dense = sf_dense_bits(a.ptr, a.t0, nt, n_ff);
+
+    // ---- down
+    const int fch = a.fch;                                                      // neurons per down chunk
+    uint8_t* s_w = stage;                                                       // [2][fch][RB]
+    float* s_h = reinterpret_cast<float*>(stage + 2 * fch * RB);               // [2][NTM][fch]
+    float2* s_red = reinterpret_cast<float2*>(stage + 2 * fch * RB + 2 * NTM * fch * 4);  // [NTM][256]
+    const int hf = tid >> 8, j = tid & 255;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const int cc = u % n_cc, r = u / n_cc;
+        const int64_t s0 = (int64_t)r * rn;
+        const int ns = (int)min((int64_t)rn, n_ff - s0);
+        if (u != (int)blockIdx.x) {
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            __syncthreads();  // the previous unit is done with the scales
+            load_scales(u);
+        }
+        // active neurons of the range, ascending: entry = token bits << 16 | neuron offset
+        int cnt = 0;
+        uint32_t mine[2] = {0, 0};
+        bool have[2] = {false, false};
+        for (int k = 0; k < 2; ++k) {
+            const int i = warp * 64 + 32 * k + lane;
+            uint32_t bits = 0;
+            if (i < ns) bits = ((uint32_t)__ldcg(&a.mask[s0 + i]) | dense) & tmask;
+            have[k] = bits != 0;
+            mine[k] = (bits << 16) | (uint32_t)i;
+            cnt += __popc(__ballot_sync(0xffffffffu, have[k]));
+        }
+        if (lane == 0) s_cnt[warp] = cnt;
+        __syncthreads();
+        int base = 0, nact = 0;
+        for (int w = 0; w < SF_FT / 32; ++w) {
+            base += w < warp ? s_cnt[w] : 0;
+            nact += s_cnt[w];
+        }
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t bal = __ballot_sync(0xffffffffu, have[k]);
+            if (have[k]) s_act[base + __popc(bal & ((1u << lane) - 1u))] = mine[k];
+            base += __popc(bal);
+        }
+        if (tid == 0) s_flag = atomicAdd(&a.tick[r], 1u) == (uint32_t)(n_cc - 1);
+        __syncthreads();
+        if (s_flag) {  // every unit of this range has read its mask: clear it for the next pass
+            for (int i = tid; i < ns / 16; i += SF_FT)
+                reinterpret_cast<uint4*>(a.mask + s0)[i] = make_uint4(0, 0, 0, 0);
+            if (tid == 0) atomicExch(&a.tick[r], 0u);
+        }
+        const int64_t c = cc * 512LL + 2 * j;
+        const int64_t rowb = QT == PI_QT_Q4_0 ? d / 2 : d;
+        uint64_t acc[NTM];  // packed (column c, c + 1) sums per token
+#pragma unroll
+        for (int t = 0; t < NTM; ++t) acc[t] = 0ull;
+        // chunks of fch active neurons, double-buffered: chunk k + 1's weight slices are
+        // in flight while chunk k is summed
+        auto issue = [&](int c0, int bf) {
+            const int nc = min(fch, nact - c0);
+            uint8_t* w = s_w + bf * (fch * RB);
+            for (int q = tid; q < nc * (RB / 16); q += SF_FT) {
+                const int i = q / (RB / 16), ch = q % (RB / 16);
+                const int64_t sn = s0 + (s_act[c0 + i] & 0xffffu);
+                const uint32_t sa = (uint32_t)__cvta_generic_to_shared(w + i * RB + 16 * ch);
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(sa),
+                             "l"(a.DQ + sn * rowb + cc * (int64_t)RB + 16 * ch)
+                             : "memory");
+            }
+            asm volatile("cp.async.commit_group;" ::: "memory");
+            for (int q = tid; q < NTM * fch; q += SF_FT) {
+                const int t = q / fch, i = q % fch;
+                float v = 0.f;
+                if (t < nt && i < nc) {
+                    const uint32_t e = s_act[c0 + i];
+                    if ((e >> (16 + t)) & 1u) v = __ldcg(&a.h[(int64_t)t * n_ff + s0 + (e & 0xffffu)]);
+                }
+                s_h[(bf * NTM + t) * fch + i] = v;
+            }
+        };
+        if (nact > 0) issue(0, 0);
+        for (int c0 = 0, bf = 0; c0 < nact; c0 += fch, bf ^= 1) {
+            const int nc = min(fch, nact - c0);
+            if (c0 + fch < nact) {
+                issue(c0 + fch, bf ^ 1);
+                asm volatile("cp.async.wait_group 1;" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;" ::: "memory");
+            }
+            float* sh = s_h + bf * NTM * fch;
+            const uint8_t* w = s_w + bf * (fch * RB);
+            if (QT == PI_QT_Q8_0 && dense) {
+                // a complete list takes the dense ffn_swiglu_q, which re-quantises h to Q8_0
+                // (quant/mod.rs:1203); with a complete list every neuron is active, so the
+                // chunk holds whole 32-neuron groups in order
+                __syncthreads();
+                for (int g = warp; 32 * g < nc; g += SF_FT / 32) {
+                    for (int t = 0; t < nt && t < NTM; ++t) {
+                        if (!((dense >> t) & 1u)) continue;
+                        float sc;
+                        const int8_t qv = warp_quant_q8(sh[t * fch + 32 * g + lane], &sc);
+                        sh[t * fch + 32 * g + lane] = fmul((float)qv, sc);
+                    }
+                }
+            }
+            __syncthreads();
+            for (int i = hf; i < nc; i += 2) {
+                const int sl = (int)(s_act[c0 + i] & 0xffffu);
+                const float2 sc = __half22float2(s_sc[(sl >> 5) * 256 + j]);
+                float w0, w1;
+                if (QT == PI_QT_Q4_0) {
+                    const uint32_t v = w[i * RB + j];
+                    w0 = nibf(v & 15u) * sc.x;
+                    w1 = nibf(v >> 4) * sc.y;
+                } else {
+                    const uint32_t v = *reinterpret_cast<const uint16_t*>(&w[i * RB + 2 * j]);
+                    w0 = (float)(int8_t)(v & 0xffu) * sc.x;
+                    w1 = (float)(int8_t)(v >> 8) * sc.y;
+                }
+                const uint64_t w2 = f2_pack(w0, w1);
+#pragma unroll
+                for (int t = 0; t < NTM; ++t) {
+                    const float hv = sh[t * fch + i];
+                    acc[t] = f2_fma(w2, f2_pack(hv, hv), acc[t]);
+                }
+            }
+            __syncthreads();  // the chunk's buffers are free
+        }
+        if (hf == 1) {
+#pragma unroll
+            for (int t = 0; t < NTM; ++t) {
+                float v0, v1;
+                f2_unpack(acc[t], v0, v1);
+                s_red[t * 256 + j] = make_float2(v0, v1);
+            }
+        }
+        __syncthreads();
+        if (hf == 0) {
+#pragma unroll
+            for (int t = 0; t < NTM; ++t) {
+                const float2 o = s_red[t * 256 + j];
+                float v0, v1;
+                f2_unpack(acc[t], v0, v1);
+                v0 += o.x;
+                v1 += o.y;
+                if (t < nt && (v0 != 0.f || v1 != 0.f))
+                    atomicAdd(reinterpret_cast<float2*>(a.y + (int64_t)(a.t0 + t) * d + c), make_float2(v0, v1));
+            }
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");  // a CTA without a unit may still own none
 }
 
 // Repack GGUF down [ne0=n_ff, ne1=n_embd] to neuron-major. Thread per
@@ -896,13 +1215,18 @@ extern "C" int pi_sparse_ffn_create(pi_ctx* ctx, const void* gate_raw, const voi
         else if (!rc) F->allocs.push_back(F->down_d);
     }
     if (!rc) {
-        // mask [n_ff] bytes, then the work list [n_ff] int32 and its two counters
-        const size_t mb = (size_t)n_ff + (size_t)n_ff * 4 + 64;
+        // mask [n_ff] bytes, then the work list [n_ff] int32 and its two counters, the fused
+        // pass's grid barrier and its per-range tickets [n_ff / 32]
+        const size_t mb = (size_t)n_ff + (size_t)n_ff * 4 + 64 + 64 + (size_t)(n_ff / 32) * 4;
         if (pi_cuda_check(ctx, cudaMalloc(&F->mask, mb), "cudaMalloc")) rc = PI_ERR_OOM;
         else F->allocs.push_back(F->mask);
         if (!rc && pi_cuda_check(ctx, cudaMemset(F->mask, 0, mb), "memset")) rc = PI_ERR_CUDA;
         F->wlist = reinterpret_cast<int32_t*>(F->mask + n_ff);
         F->wctr = reinterpret_cast<uint32_t*>(F->wlist + n_ff);
+        F->fbar = reinterpret_cast<uint32_t*>(F->mask + n_ff + n_ff * 4 + 64);
+        F->tick = reinterpret_cast<uint32_t*>(F->mask + n_ff + n_ff * 4 + 128);
+        const char* split = getenv("PI_SF_SPLIT");
+        F->fused = !(split && split[0] == '1');
     }
     if (!rc) {
         const int64_t nthr = (n_embd / 2) * (n_ff / 32);
@@ -923,6 +1247,77 @@ extern "C" void pi_sparse_ffn_destroy(pi_sparse_ffn* F) {
     if (!F) return;
     for (void* p : F->allocs) cudaFree(p);
     delete F;
+}
+
+// One fused launch for a one-token pass (k_sf_fused): grid = one CTA per SM, all
+// resident (its grid barrier needs that).
+static int sf_forward_fused(pi_ctx* ctx, pi_sparse_ffn* F, const float* x, int64_t T, const int64_t* ptr,
+                            const int64_t* idx, float* out, cudaStream_t st, float* hb, const int8_t* xq,
+                            const float* xs, int sms) {
+    const int64_t d = F->n_embd, n_ff = F->n_ff;
+    const bool q4 = F->qtype == PI_QT_Q4_0;
+    const int n_cc = (int)(d / 512);
+    const int64_t groups = n_ff / 32, per = std::max(1, sms / n_cc);
+    const int gpr = (int)std::min<int64_t>(SF_FMAXG, (groups + per - 1) / per);
+    {
+        const int64_t t0 = 0;
+        const int nt = 1, ntm = 1;
+        const size_t xst = q4 ? (size_t)nt * (d / 32) * 36 * 4 : (size_t)nt * d + (size_t)nt * (d / 32) * 4;
+        // down chunks: at least 128 neurons, more where the gate/up staging leaves room
+        const size_t perb = 2 * (size_t)(q4 ? 256 : 512) + 2 * (size_t)ntm * 4, red = (size_t)ntm * 256 * 8;
+        const size_t stage = (std::max(xst, 128 * perb + red) + 15) & ~(size_t)15;
+        const int fch = (int)std::min<size_t>(1024, (stage - red) / perb / 32 * 32);
+        const size_t smem = stage + SF_FMAXG * 1024 + 1024 * 4;
+        SfFusedArgs a;
+        a.G = (const uint8_t*)F->gate.q;
+        a.U = (const uint8_t*)F->up.q;
+        a.GD = F->gate.d;
+        a.UD = F->up.d;
+        a.DQ = (const uint8_t*)F->down_q;
+        a.DS = F->down_d;
+        a.mask = F->mask;
+        a.wlist = F->wlist;
+        a.wctr = F->wctr;
+        a.tick = F->tick;
+        a.bar = reinterpret_cast<SfGridBar*>(F->fbar);
+        a.x = x;
+        a.xq = xq;
+        a.xs = xs;
+        a.ptr = ptr;
+        a.idx = idx;
+        a.t0 = (int)t0;
+        a.nt = nt;
+        a.rn = 32 * gpr;
+        a.fch = fch;
+        a.n_embd = d;
+        a.n_ff = n_ff;
+        a.h = hb;
+        a.y = out;
+        a.err = ctx->dev_err;
+        a.stage_bytes = (uint32_t)stage;
+        PiProfScope ps(ctx, st, "k_sf_fused");
+#define SF_FU(QT, B)                                                                         \
+    {                                                                                        \
+        auto kf = k_sf_fused<QT, B>;                                                         \
+        pi_smem_attr((const void*)kf, smem);                                                 \
+        int occ = 0;                                                                         \
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kf, SF_FT, smem);                \
+        if (occ < 1) return pi_set_error(ctx, PI_ERR_CUDA, "sparse ffn: fused pass does not fit an SM"); \
+        pi_pdl_launch(kf, dim3((unsigned)sms), dim3(SF_FT), smem, st, a);                    \
+    }
+        switch ((q4 ? 1 : 16) * (int)(d / 1024)) {
+            case 1: SF_FU(PI_QT_Q4_0, 1) break;
+            case 2: SF_FU(PI_QT_Q4_0, 2) break;
+            case 4: SF_FU(PI_QT_Q4_0, 4) break;
+            case 16: SF_FU(PI_QT_Q8_0, 1) break;
+            case 32: SF_FU(PI_QT_Q8_0, 2) break;
+            case 64: SF_FU(PI_QT_Q8_0, 4) break;
+            default: return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: n_embd must be 1024, 2048 or 4096");
+        }
+#undef SF_FU
+        LAUNCH_CHECK("sparse ffn (fused)");
+    }
+    return PI_OK;
 }
 
 extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float* x, int64_t T, const int64_t* ptr,
@@ -948,6 +1343,8 @@ extern "C" int pi_sparse_ffn_forward(pi_ctx* ctx, pi_sparse_ffn* F, const float*
         k_quant_act<<<nblocks(T * d, 256), 256, 0, st>>>(x, T * d, xq, xs);
     }
     const int sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
+    if (d != 1024 && d != 2048 && d != 4096) return pi_set_error(ctx, PI_ERR_ARG, "sparse ffn: n_embd must be 1024, 2048 or 4096");
+    if (F->fused && T == 1) return sf_forward_fused(ctx, F, x, T, ptr, idx, out, st, hb, xq, xs, sms);
     for (int64_t t0 = 0; t0 < T; t0 += SF_TMAX) {
         const int nt = (int)std::min<int64_t>(SF_TMAX, T - t0);
         {

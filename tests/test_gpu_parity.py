@@ -415,6 +415,49 @@ def test_sparse_ffn_small(pkg, orc, torch, qt):
         F.forward(torch.from_numpy(x[:1]).cuda(), [np.array([n_ff], np.int64)])
 
 
+@pytest.mark.parametrize("qt", [2, 8])
+def test_sparse_ffn_one_token_fused(pkg, orc, torch, qt, monkeypatch):
+    """A one-token pass runs as one fused launch (gate/up straight from the
+    token's list, grid barrier, down). Against the oracle: empty, short, long,
+    unsorted and complete (dense) lists; a list with repeated entries gives the
+    same output as the three-launch path (PI_SF_SPLIT=1), which marks each
+    neuron once; an out-of-range entry is refused."""
+    from powerinfer_x64_b200 import PiError, predictor
+
+    rng = np.random.default_rng(21)
+    n_embd, n_ff = 2048, 4096
+    q = orc.quantize_q8_0 if qt == 8 else orc.quantize_q4_0
+    g, u, d = (q((rng.standard_normal(n_embd * n_ff) * 0.02).astype(np.float32)) for _ in range(3))
+    F = predictor.SparseFFN(g, u, d, qt, n_embd, n_ff)
+    monkeypatch.setenv("PI_SF_SPLIT", "1")
+    Fs = predictor.SparseFFN(g, u, d, qt, n_embd, n_ff)
+    monkeypatch.delenv("PI_SF_SPLIT")
+    x = rng.standard_normal((1, n_embd)).astype(np.float32)
+    xd = torch.from_numpy(x).cuda()
+    for lst in (np.zeros(0, np.int64), np.array([7], np.int64), rng.permutation(n_ff)[:600],
+                np.sort(rng.choice(n_ff, 3000, replace=False)), np.arange(n_ff)):
+        lst = np.asarray(lst, np.int64)
+        got = F.forward(xd, [lst]).cpu().numpy()
+        if lst.size == 0:
+            assert np.all(got == 0)
+            continue
+        close(got[0], orc.sparse_ffn(x, g, u, d, qt, n_embd, n_ff, [np.sort(lst)])[0])
+    rep = np.concatenate([rng.choice(n_ff, 500, replace=False)] * 2)
+    a = F.forward(xd, [rep]).cpu().numpy()
+    b = Fs.forward(xd, [rep]).cpu().numpy()
+    close(a[0], b[0], rel_l2=1e-5, max_abs=1e-5)
+    close(a[0], orc.sparse_ffn(x, g, u, d, qt, n_embd, n_ff, [np.unique(rep)])[0])
+    # an out-of-range entry reaches the device (the host check is for Python lists only)
+    bad = (torch.tensor([0, 2], dtype=torch.int64, device="cuda"),
+           torch.tensor([3, n_ff + 5], dtype=torch.int64, device="cuda"))
+    F.forward(xd, csr=bad)
+    with pytest.raises(PiError):
+        F.ctx.sync_check()
+    # the context is usable afterwards
+    close(F.forward(xd, [np.array([7], np.int64)]).cpu().numpy()[0],
+          orc.sparse_ffn(x, g, u, d, qt, n_embd, n_ff, [np.array([7], np.int64)])[0])
+
+
 @pytest.mark.parametrize("T", [1, 8])
 def test_c4_sparse_parity(pkg, orc, torch, T):
     from powerinfer_x64_b200 import predictor, synth
