@@ -42,17 +42,18 @@ namespace {
 
 constexpr int TG = 16;  // tokens per work item (gate/up quantises h with one warp per token)
 
-// One token row xr (global or shared memory) by a 256-thread CTA; __syncthreads inside.
+// One token row xr (global or shared memory) by an NT-thread CTA; __syncthreads inside.
+template <int NT = 256>
 PI_DEV void split_row(const float* xr, int t, int d, __half* __restrict__ xh, __half* __restrict__ xl,
                       float* __restrict__ xnorm) {
-    __shared__ double red[8];
+    __shared__ double red[NT / 32];
     __shared__ int s_bad;
     const int tid = threadIdx.x;
     if (tid == 0) s_bad = 0;
     __syncthreads();
     double ss = 0.0;
     bool bad = false;
-    for (int c = tid * 8; c < d; c += 256 * 8) {
+    for (int c = tid * 8; c < d; c += NT * 8) {
         const float4 v0 = *reinterpret_cast<const float4*>(xr + c);
         const float4 v1 = *reinterpret_cast<const float4*>(xr + c + 4);
         const float f[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
@@ -80,7 +81,7 @@ PI_DEV void split_row(const float* xr, int t, int d, __half* __restrict__ xh, __
     __syncthreads();
     if (tid == 0) {
         double tot = 0.0;
-        for (int w = 0; w < 8; ++w) tot += red[w];
+        for (int w = 0; w < NT / 32; ++w) tot += red[w];
         // the f64 sum is within ~2^-40 relative; 1 + 2^-20 covers it and the f32 rounding
         xnorm[t] = s_bad ? INFINITY : __double2float_ru(__dsqrt_ru(tot) * (1.0 + 0x1p-20));
     }
@@ -93,7 +94,10 @@ PI_DEV void split_row(const float* xr, int t, int d, __half* __restrict__ xh, __
 // every warp normalises and quantises 32-element blocks (one block per warp
 // per pass).
 // ---------------------------------------------------------------------------
-__global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
+// NT threads per token: 256 for a few tokens, 128 for large batches (more tokens per SM
+// in flight while four lanes of each run the sequential sum of squares).
+template <int NT>
+__global__ __launch_bounds__(NT) void k_prep(const float* __restrict__ x, int d, int do_norm, float eps,
                                               float* __restrict__ normed, int do_quant, int8_t* __restrict__ xq,
                                               float* __restrict__ xs, __half* __restrict__ xh,
                                               __half* __restrict__ xl, float* __restrict__ xnorm) {
@@ -103,7 +107,7 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
     __shared__ float s_inv;
     const int t = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + (size_t)t * d;
-    for (int c = tid; c < d / 4; c += 256)
+    for (int c = tid; c < d / 4; c += NT)
         *reinterpret_cast<float4*>(&s_row[4 * c]) = *reinterpret_cast<const float4*>(xr + 4 * c);
     __syncthreads();
     float inv = 1.0f;
@@ -130,7 +134,7 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
         __syncthreads();
         inv = s_inv;
     }
-    for (int i = tid; i < d; i += 256) {  // d % 32 == 0: a warp covers one quant block per pass
+    for (int i = tid; i < d; i += NT) {  // d % 32 == 0: a warp covers one quant block per pass
         float v = s_row[i];
         if (do_norm) {
             v = fmul(v, inv);  // * weight (1.0) is exact
@@ -145,7 +149,7 @@ __global__ __launch_bounds__(256) void k_prep(const float* __restrict__ x, int d
         }
     }
     // the certified tensor-core router's f16 hi/lo split and norm bound of the (normed) row
-    if (xh) split_row(s_row, t, d, xh, xl, xnorm);
+    if (xh) split_row<NT>(s_row, t, d, xh, xl, xnorm);
 }
 
 // ---------------------------------------------------------------------------
@@ -608,7 +612,7 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
 // a value is not finite or |x| >= 2^15, which sends the token to the exact path).
 // grid T, block 256.
 // ---------------------------------------------------------------------------
-constexpr int KC_ROUTER = 32, TC_PER_LANE = 8, TC_WARPS = 4, RCH = 64, RPF = 8;
+constexpr int KC_ROUTER = 32, TC_PER_LANE = 8, TC_WARPS = 4;
 
 __global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ x, int d, __half* __restrict__ xh,
                                                       __half* __restrict__ xl, float* __restrict__ xnorm) {
@@ -616,7 +620,7 @@ __global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ 
 }
 
 // ---------------------------------------------------------------------------
-// k_router_cand: one warp per token. From the fast logits l_e (tensor cores) it
+// k_router_cand: a warp walks RC_TPW tokens. From the fast logits l_e (tensor cores) it
 // builds intervals [l_e - eps_e, l_e + eps_e] that contain the reference's
 // logit (sequential f32 sum, quant/mod.rs:921-935, then + bias), with
 //   eps_e = 2 ((4d + 64) u ||x|| ||w_e|| + 2^-23 sqrt(d) (||w_e|| + 2^-rs ||x||))
@@ -626,192 +630,280 @@ __global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ 
 // the hi/lo representation (12 u |x_i w_i|, and 2^-25 where a part is
 // subnormal), and the final f32 operations; sum |x_i w_i| <= ||x|| ||w_e||.
 // Every expert whose upper end reaches the k-th largest lower end is a
-// candidate (the true top-k are among them, at most 31 kept); each lane then
-// runs the reference's exact chain for one candidate (one more lane for the
-// shared-expert gate row), and the top-k is taken on the exact logits. The
+// candidate (the true top-k are among them, at most 31 kept). The candidates'
+// rows (and the shared-expert gate row) of consecutive tokens join a batch of
+// up to 32 rows; each lane of the warp then runs the reference's exact chain for
+// one row of the batch, against its own token's x, and each token's top-k is
+// taken on its exact logits. The
 // token is certified when the k-th exact logit clears both the next candidate
 // and every non-candidate's upper end by 2^-16 (1 + |l_k - max|), so that the
 // reference's choice by rounded probability (ties to the lowest index) is the
 // same. Certified tokens get idx (ascending), gates from the exact logits and
 // the shared gate; the others are appended to flag_list for the exact path.
 // ---------------------------------------------------------------------------
-__global__ __launch_bounds__(TC_WARPS * 32) void k_router_cand(
+constexpr int RC_TT = 64;      // tokens per CTA at most
+constexpr int RC_THR = 512;    // threads per CTA
+constexpr int RC_JPT = 4;      // exact chains per thread at most (64 tokens x 32 rows)
+constexpr int RC_CH = 32;      // floats of each staged row per piece
+constexpr int RC_NS = 3;       // pieces in flight
+constexpr int RC_PITCH = RC_CH + 4;  // +4: 16-byte loads of rows 1 .. 7 apart hit distinct banks
+constexpr int RC_MAXR = 257;   // staged router rows: E <= 256 experts + the shared-expert gate row
+size_t router_cand_smem() { return (size_t)RC_NS * (RC_TT + RC_MAXR) * RC_PITCH * 4; }
+
+__global__ __launch_bounds__(RC_THR, 1) void k_router_cand(
     const float* __restrict__ logits, const float* __restrict__ xnorm, const float* __restrict__ wnrm, int rs,
-    const float* __restrict__ xin, const float* __restrict__ W, const float* __restrict__ bias, int T, int d, int E,
-    int k, int has_shgate, int32_t* __restrict__ idx, float* __restrict__ gates, float* __restrict__ shscale,
+    const float* __restrict__ xin, const float* __restrict__ W, const float* __restrict__ bias, int T, int tt, int d,
+    int E, int k, int has_shgate, int32_t* __restrict__ idx, float* __restrict__ gates, float* __restrict__ shscale,
     int32_t* __restrict__ counts, int32_t* __restrict__ flag_list, int32_t* __restrict__ n_flag) {
-    __shared__ int s_c[TC_WARPS][32];
-    __shared__ __align__(16) float s_w[TC_WARPS][32][RCH + 4];  // +4: a warp's 16-byte loads of 32 rows hit distinct banks
-    __shared__ __align__(16) float s_x[TC_WARPS][RCH];
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int t = blockIdx.x * TC_WARPS + warp;
-    if (t >= T) return;
-    const float nx = xnorm[t];
-    const float* lr = logits + (size_t)t * (E + 1);
+    extern __shared__ __align__(16) float rc_sm[];  // RC_NS pieces of {tt x rows, the used router rows}
+    __shared__ uint8_t s_cand[RC_TT][32];           // candidates of each token (expert ids < 256)
+    __shared__ int s_nc[RC_TT], s_joff[RC_TT + 1];  // candidates (-1: flagged), first chain of each token
+    __shared__ float s_max[RC_TT];                  // largest upper end among a token's non-candidates
+    __shared__ uint32_t s_used[9];                  // router rows some token of the tile needs (bit E: gate row)
+    __shared__ int16_t s_rslot[RC_MAXR];            // router row -> staged slot
+    __shared__ int16_t s_rows[RC_MAXR];             // staged slot -> router row
+    __shared__ float s_ex[RC_TT * 32];              // exact logits, by chain
+    __shared__ int s_nrows;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarp = RC_THR / 32;
+    const int t0 = blockIdx.x * tt, ntok = min(tt, T - t0);
+    if (ntok <= 0) return;
     const float c1 = 2.0f * (4.0f * d + 64.0f) * 0x1p-24f;
     const float cab = 2.0f * sqrtf((float)d) * 0x1p-23f;
-    const float sx = ldexpf(nx, -rs);
-    float lo_[TC_PER_LANE], up_[TC_PER_LANE];
-    bool bad = !(nx < INFINITY);
-#pragma unroll
-    for (int j = 0; j < TC_PER_LANE; ++j) {
-        const int e = lane + 32 * j;
-        lo_[j] = up_[j] = -INFINITY;
-        if (e < E) {
-            const float l = lr[e], b = bias ? fabsf(bias[e]) : 0.0f, wn = wnrm[e];
-            const float eps = c1 * nx * wn + cab * (wn + sx) + 0x1p-21f * (fabsf(l) + b);
-            lo_[j] = l - eps;
-            up_[j] = l + eps;
-            bad |= !(fabsf(l) < INFINITY) || !(eps < INFINITY);
-        }
-    }
-    // tau = k-th largest lower end
-    uint32_t taken = 0;
-    float tau = -INFINITY;
-    for (int r = 0; r < k; ++r) {
-        float bl = -INFINITY;
-        int bi = 0x7fffffff;
+    if (tid < 9) s_used[tid] = 0;
+    __syncthreads();
+    // ---- candidates, one warp per token
+    for (int sl = warp; sl < ntok; sl += nwarp) {
+        const int t = t0 + sl;
+        const float nx = xnorm[t];
+        const float* lr = logits + (size_t)t * (E + 1);
+        const float sx = ldexpf(nx, -rs);
+        float lo_[TC_PER_LANE], up_[TC_PER_LANE];
+        bool bad = !(nx < INFINITY);
 #pragma unroll
         for (int j = 0; j < TC_PER_LANE; ++j) {
             const int e = lane + 32 * j;
-            if (e < E && !((taken >> j) & 1u) && (lo_[j] > bl || (lo_[j] == bl && e < bi))) { bl = lo_[j]; bi = e; }
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ol > bl || (ol == bl && oi < bi)) { bl = ol; bi = oi; }
-        }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-        tau = bl;
-    }
-    // candidates: upper end >= tau
-    int nc = 0;
-    float maxout = -INFINITY;
-#pragma unroll
-    for (int j = 0; j < TC_PER_LANE; ++j) {
-        const int e = lane + 32 * j;
-        const bool cand = e < E && up_[j] >= tau;
-        const unsigned bal = __ballot_sync(0xffffffffu, cand);
-        const int pos = nc + __popc(bal & ((1u << lane) - 1u));
-        if (cand && pos < 31) s_c[warp][pos] = e;
-        nc += __popc(bal);
-        if (e < E && !cand) maxout = fmaxf(maxout, up_[j]);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) maxout = fmaxf(maxout, __shfl_xor_sync(0xffffffffu, maxout, o));
-    bad |= nc > 31;
-    if (__any_sync(0xffffffffu, bad)) {
-        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
-        return;
-    }
-    __syncwarp();
-    // exact chains (reference order, no FMA): lane j < nc -> candidate j, lane nc -> gate row.
-    // The warp stages RCH-wide pieces of its rows (coalesced loads) and of x in shared memory.
-    const int nrows = nc + (has_shgate ? 1 : 0);
-    const int row = lane < nc ? s_c[warp][lane] : ((lane == nc && has_shgate) ? E : -1);
-    const float* xr = xin + (size_t)t * d;
-    float acc = 0.0f;
-    // lane's share of a piece: float4 q = lane + 32 m (m < RPF) of the nrows x RCH/4 grid,
-    // loaded one piece ahead; source pointers and shared offsets are fixed per lane
-    // (nrows <= 32: rows beyond the first 32 RPF / (RCH / 4) are staged without prefetch)
-    const float* src[RPF];
-    float* dst[RPF];
-    int nmine = 0;
-#pragma unroll
-    for (int m = 0; m < RPF; ++m) {
-        const int q = lane + 32 * m;
-        const int r = q / (RCH / 4), c4 = q % (RCH / 4);
-        const bool v = q < nrows * (RCH / 4);
-        const int rid = v ? (r < nc ? s_c[warp][r] : E) : 0;
-        src[m] = W + (size_t)rid * d + 4 * c4;
-        dst[m] = &s_w[warp][v ? r : 0][4 * c4];
-        nmine += v;
-    }
-    float4 pw[RPF], px;
-    auto fetch = [&](int i0) {
-#pragma unroll
-        for (int m = 0; m < RPF; ++m)
-            if (m < nmine) pw[m] = __ldg(reinterpret_cast<const float4*>(src[m] + i0));
-        if (lane < RCH / 4) px = *reinterpret_cast<const float4*>(xr + i0 + 4 * lane);
-    };
-    fetch(0);
-    for (int i0 = 0; i0 < d; i0 += RCH) {
-        __syncwarp();
-#pragma unroll
-        for (int m = 0; m < RPF; ++m)
-            if (m < nmine) *reinterpret_cast<float4*>(dst[m]) = pw[m];
-        for (int q = lane + 32 * RPF; q < nrows * (RCH / 4); q += 32) {  // rows beyond the prefetched share
-            const int r = q / (RCH / 4), c4 = q % (RCH / 4);
-            const int rid = r < nc ? s_c[warp][r] : E;
-            *reinterpret_cast<float4*>(&s_w[warp][r][4 * c4]) =
-                __ldg(reinterpret_cast<const float4*>(W + (size_t)rid * d + i0 + 4 * c4));
-        }
-        if (lane < RCH / 4) *reinterpret_cast<float4*>(&s_x[warp][4 * lane]) = px;
-        __syncwarp();
-        if (i0 + RCH < d) fetch(i0 + RCH);
-        if (row >= 0) {
-            const float* wr = s_w[warp][lane];
-#pragma unroll 4
-            for (int i = 0; i < RCH; i += 4) {
-                const float4 wv = *reinterpret_cast<const float4*>(wr + i);
-                const float4 xv = *reinterpret_cast<const float4*>(&s_x[warp][i]);
-                acc = fadd(acc, fmul(wv.x, xv.x));
-                acc = fadd(acc, fmul(wv.y, xv.y));
-                acc = fadd(acc, fmul(wv.z, xv.z));
-                acc = fadd(acc, fmul(wv.w, xv.w));
+            lo_[j] = up_[j] = -INFINITY;
+            if (e < E) {
+                const float l = lr[e], b = bias ? fabsf(bias[e]) : 0.0f, wn = wnrm[e];
+                const float eps = c1 * nx * wn + cab * (wn + sx) + 0x1p-21f * (fabsf(l) + b);
+                lo_[j] = l - eps;
+                up_[j] = l + eps;
+                bad |= !(fabsf(l) < INFINITY) || !(eps < INFINITY);
             }
         }
-    }
-    if (row >= 0 && row < E && bias) acc = fadd(acc, bias[row]);
-    const float gl = __shfl_sync(0xffffffffu, acc, nc < 32 ? nc : 0);  // gate row's logit
-    // top-k on the exact logits (ties to the lowest index)
-    const float myv = lane < nc ? acc : -INFINITY;
-    const int myi = lane < nc ? row : 0x7fffffff;
-    float m = myv;
+        // tau = k-th largest lower end
+        uint32_t taken = 0;
+        float tau = -INFINITY;
+        for (int r = 0; r < k; ++r) {
+            float bl = -INFINITY;
+            int bi = 0x7fffffff;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-    bool sel = false;
-    float lk = -INFINITY;
-    for (int r = 0; r < k; ++r) {
-        float bv = sel ? -INFINITY : myv;
-        int bi = sel ? 0x7fffffff : myi;
+            for (int j = 0; j < TC_PER_LANE; ++j) {
+                const int e = lane + 32 * j;
+                if (e < E && !((taken >> j) & 1u) && (lo_[j] > bl || (lo_[j] == bl && e < bi))) { bl = lo_[j]; bi = e; }
+            }
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ol = __shfl_xor_sync(0xffffffffu, bl, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ol > bl || (ol == bl && oi < bi)) { bl = ol; bi = oi; }
+            }
+            if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+            tau = bl;
         }
-        if (lane < nc && myi == bi) sel = true;
-        lk = bv;
-    }
-    float nxt = (lane < nc && !sel) ? myv : -INFINITY;
+        // candidates: upper end >= tau (at most 31 kept)
+        int nc = 0;
+        float maxout = -INFINITY;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) nxt = fmaxf(nxt, __shfl_xor_sync(0xffffffffu, nxt, o));
-    const float delta = 0x1p-16f * (1.0f + fabsf(lk - m));
-    if (!(lk - nxt > delta && lk - maxout > delta)) {
-        if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
-        return;
+        for (int j = 0; j < TC_PER_LANE; ++j) {
+            const int e = lane + 32 * j;
+            const bool cand = e < E && up_[j] >= tau;
+            const unsigned bal = __ballot_sync(0xffffffffu, cand);
+            const int pos = nc + __popc(bal & ((1u << lane) - 1u));
+            if (cand && pos < 31) s_cand[sl][pos] = (uint8_t)e;
+            nc += __popc(bal);
+            if (e < E && !cand) maxout = fmaxf(maxout, up_[j]);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) maxout = fmaxf(maxout, __shfl_xor_sync(0xffffffffu, maxout, o));
+        bad |= nc > 31;
+        if (__any_sync(0xffffffffu, bad)) {
+            if (lane == 0) {
+                flag_list[atomicAdd(n_flag, 1)] = t;
+                s_nc[sl] = -1;
+            }
+            continue;
+        }
+        __syncwarp();
+        if (lane < nc) atomicOr(&s_used[s_cand[sl][lane] >> 5], 1u << (s_cand[sl][lane] & 31));
+        if (lane == 0) {
+            s_nc[sl] = nc;
+            s_max[sl] = maxout;
+            if (has_shgate) atomicOr(&s_used[E >> 5], 1u << (E & 31));
+        }
     }
-    // ascending order of the selected experts (model/mod.rs:1303), gates from the exact logits
-    const unsigned selm = __ballot_sync(0xffffffffu, sel);
-    int rank = 0;
-    for (unsigned b = selm; b; b &= b - 1) {
-        const int ln = __ffs(b) - 1;
-        rank += __shfl_sync(0xffffffffu, myi, ln) < myi;
+    __syncthreads();
+    // ---- the tile's router rows (ascending) and its chains: token sl's chains are
+    // s_joff[sl] .. s_joff[sl + 1] - 1, its candidates in order, then its gate row
+    if (warp == 0) {
+        uint32_t wv = lane < 9 ? s_used[lane] : 0u;
+        int pre = __popc(wv);
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, pre, o);
+            if (lane >= o) pre += v;
+        }
+        int base = pre - __popc(wv);
+        for (; wv; wv &= wv - 1) {
+            const int e = 32 * lane + __ffs(wv) - 1;
+            s_rslot[e] = (int16_t)base;
+            s_rows[base++] = (int16_t)e;
+        }
+        if (lane == 31) s_nrows = pre;
+    } else if (warp == 1) {
+        int run = 0;
+        for (int s0 = 0; s0 < ntok; s0 += 32) {
+            const int sl = s0 + lane;
+            const int n = sl < ntok && s_nc[sl] >= 0 ? s_nc[sl] + (has_shgate ? 1 : 0) : 0;
+            int pre = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(0xffffffffu, pre, o);
+                if (lane >= o) pre += v;
+            }
+            if (sl < ntok) s_joff[sl] = run + pre - n;
+            run += __shfl_sync(0xffffffffu, pre, 31);
+        }
+        if (lane == 0) s_joff[ntok] = run;
     }
-    const float p = sel ? exp_cr(fsub(myv, m)) : 0.0f;
-    float ssum = 0.0f;
-    for (int r = 0; r < k; ++r) {  // sequential, ascending expert order
-        const unsigned b = __ballot_sync(0xffffffffu, sel && rank == r);
-        ssum = fadd(ssum, __shfl_sync(0xffffffffu, p, __ffs(b) - 1));
+    __syncthreads();
+    const int nrows = s_nrows, njobs = s_joff[ntok];
+    // ---- exact chains (reference order, no FMA): thread takes chains tid + RC_THR m
+    int xo[RC_JPT], wo[RC_JPT];
+    float acc[RC_JPT];
+#pragma unroll
+    for (int m = 0; m < RC_JPT; ++m) {
+        acc[m] = 0.0f;
+        xo[m] = wo[m] = 0;
+        const int jb = tid + RC_THR * m;
+        if (jb < njobs) {
+            int sl = 0;  // the chain's token: last sl with s_joff[sl] <= jb
+            for (int b = 32; b > 0; b >>= 1)
+                if (sl + b < ntok && s_joff[sl + b] <= jb) sl += b;
+            const int j = jb - s_joff[sl];
+            const int row = j < s_nc[sl] ? s_cand[sl][j] : E;
+            xo[m] = sl * RC_PITCH;
+            wo[m] = (tt + s_rslot[row]) * RC_PITCH;
+        }
     }
-    if (sel) {
-        idx[(size_t)t * k + rank] = myi;
-        gates[(size_t)t * k + rank] = ssum > 0.0f ? fdiv(p, ssum) : p;
-        atomicAdd(&counts[myi], 1);
+    const int piece = (tt + nrows) * RC_PITCH;  // floats of one staged piece
+    // piece p of every staged row, 16 bytes per cp.async
+    auto stage = [&](int p) {
+        float* dst = rc_sm + (p % RC_NS) * piece;
+        for (int q = tid; q < (ntok + nrows) * (RC_CH / 4); q += RC_THR) {
+            const int r = q / (RC_CH / 4), c4 = q % (RC_CH / 4);
+            const float* src = r < ntok ? xin + (size_t)(t0 + r) * d : W + (size_t)s_rows[r - ntok] * d;
+            const int so = (r < ntok ? r : tt + r - ntok) * RC_PITCH + 4 * c4;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst + so)),
+                         "l"(src + p * RC_CH + 4 * c4)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    const int np = d / RC_CH;
+    for (int p = 0; p < RC_NS - 1; ++p) {
+        if (p < np) stage(p);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(gl) : 1.0f;
+    for (int p = 0; p < np; ++p) {
+        asm volatile("cp.async.wait_group %0;" ::"n"(RC_NS - 2) : "memory");
+        __syncthreads();  // piece p landed for every thread; piece p - 1's buffer is free
+        if (p + RC_NS - 1 < np) stage(p + RC_NS - 1);
+        else asm volatile("cp.async.commit_group;" ::: "memory");
+        const float* base = rc_sm + (p % RC_NS) * piece;
+#pragma unroll
+        for (int m = 0; m < RC_JPT; ++m) {
+            if (tid + RC_THR * m >= njobs) break;
+            const float* xr = base + xo[m];
+            const float* wr = base + wo[m];
+            float a = acc[m];
+#pragma unroll
+            for (int i = 0; i < RC_CH; i += 4) {
+                const float4 wv = *reinterpret_cast<const float4*>(wr + i);
+                const float4 xv = *reinterpret_cast<const float4*>(xr + i);
+                a = fadd(a, fmul(wv.x, xv.x));
+                a = fadd(a, fmul(wv.y, xv.y));
+                a = fadd(a, fmul(wv.z, xv.z));
+                a = fadd(a, fmul(wv.w, xv.w));
+            }
+            acc[m] = a;
+        }
+    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+#pragma unroll
+    for (int m = 0; m < RC_JPT; ++m) {
+        const int jb = tid + RC_THR * m;
+        if (jb < njobs) {
+            const int row = s_rows[wo[m] / RC_PITCH - tt];
+            s_ex[jb] = (row < E && bias) ? fadd(acc[m], bias[row]) : acc[m];
+        }
+    }
+    __syncthreads();
+    // ---- per token: top-k on the exact logits, certification, gates
+    for (int sl = warp; sl < ntok; sl += nwarp) {
+        const int nc = s_nc[sl];
+        if (nc < 0) continue;
+        const int t = t0 + sl, off = s_joff[sl];
+        const float maxout = s_max[sl];
+        const float gl = has_shgate ? s_ex[off + nc] : 0.0f;  // gate row's logit
+        // top-k on the exact logits (ties to the lowest index)
+        const float myv = lane < nc ? s_ex[off + lane] : -INFINITY;
+        const int myi = lane < nc ? (int)s_cand[sl][lane] : 0x7fffffff;
+        float m = myv;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bool sel = false;
+        float lk = -INFINITY;
+        for (int r = 0; r < k; ++r) {
+            float bv = sel ? -INFINITY : myv;
+            int bi = sel ? 0x7fffffff : myi;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if (lane < nc && myi == bi) sel = true;
+            lk = bv;
+        }
+        float nxt = (lane < nc && !sel) ? myv : -INFINITY;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) nxt = fmaxf(nxt, __shfl_xor_sync(0xffffffffu, nxt, o));
+        const float delta = 0x1p-16f * (1.0f + fabsf(lk - m));
+        if (!(lk - nxt > delta && lk - maxout > delta)) {
+            if (lane == 0) flag_list[atomicAdd(n_flag, 1)] = t;
+            continue;
+        }
+        // ascending order of the selected experts (model/mod.rs:1303), gates from the exact logits
+        const unsigned selm = __ballot_sync(0xffffffffu, sel);
+        int rank = 0;
+        for (unsigned b = selm; b; b &= b - 1) {
+            const int ln = __ffs(b) - 1;
+            rank += __shfl_sync(0xffffffffu, myi, ln) < myi;
+        }
+        const float p = sel ? exp_cr(fsub(myv, m)) : 0.0f;
+        float ssum = 0.0f;
+        for (int r = 0; r < k; ++r) {  // sequential, ascending expert order
+            const unsigned b = __ballot_sync(0xffffffffu, sel && rank == r);
+            ssum = fadd(ssum, __shfl_sync(0xffffffffu, p, __ffs(b) - 1));
+        }
+        if (sel) {
+            idx[(size_t)t * k + rank] = myi;
+            gates[(size_t)t * k + rank] = ssum > 0.0f ? fdiv(p, ssum) : p;
+            atomicAdd(&counts[myi], 1);
+        }
+        if (lane == 0 && shscale) shscale[t] = has_shgate ? sigmoid_ref(gl) : 1.0f;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -2182,9 +2274,14 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
     if (do_norm || quant) {
         PiProfScope ps(ctx, st, "k_prep");
         const bool split = use_router_tc(L, T);  // the router's hi/lo split comes from this pass
-        pi_pdl_launch(k_prep, dim3((unsigned)T), dim3(256), sizeof(float) * d, st, x, d, do_norm, 1e-6f, B.normed,
-                      quant ? 1 : 0, B.xq, B.xs, split ? B.xth : nullptr, split ? B.xtl : nullptr,
-                      split ? B.xnorm : nullptr);
+        if (T >= 1024)
+            pi_pdl_launch(k_prep<128>, dim3((unsigned)T), dim3(128), sizeof(float) * d, st, x, d, do_norm, 1e-6f,
+                          B.normed, quant ? 1 : 0, B.xq, B.xs, split ? B.xth : nullptr, split ? B.xtl : nullptr,
+                          split ? B.xnorm : nullptr);
+        else
+            pi_pdl_launch(k_prep<256>, dim3((unsigned)T), dim3(256), sizeof(float) * d, st, x, d, do_norm, 1e-6f,
+                          B.normed, quant ? 1 : 0, B.xq, B.xs, split ? B.xth : nullptr, split ? B.xtl : nullptr,
+                          split ? B.xnorm : nullptr);
     }
     // routing: certified fast logits, then exact logits for the tokens that could not be certified
     if (pi_cuda_check(ctx, cudaMemsetAsync(counts, 0, sizeof(int32_t) * E, st), "memset counts")) return PI_ERR_CUDA;
@@ -2200,8 +2297,12 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
         if (int rc = pi_router_logits_tc(ctx, L, B.xth, B.xtl, T, B.logits, st)) return rc;
         {
             PiProfScope ps(ctx, st, "k_router_cand");
-            k_router_cand<<<(unsigned)((T + TC_WARPS - 1) / TC_WARPS), TC_WARPS * 32, 0, st>>>(
-                B.logits, B.xnorm, L->router_nrm, L->router_rs, xin, L->router, L->bias, (int)T, d, E, k,
+            // tiles of tokens: one CTA per SM where T allows, at most RC_TT tokens each
+            const int64_t sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
+            const int tt = (int)std::min<int64_t>(RC_TT, std::max<int64_t>(16, (T + sms - 1) / sms));
+            pi_smem_attr((const void*)k_router_cand, router_cand_smem());
+            k_router_cand<<<(unsigned)((T + tt - 1) / tt), RC_THR, router_cand_smem(), st>>>(
+                B.logits, B.xnorm, L->router_nrm, L->router_rs, xin, L->router, L->bias, (int)T, tt, d, E, k,
                 L->has_shared_gate ? 1 : 0, idx, gates, B.shscale, counts, B.flag_list, B.n_flag);
         }
         {
