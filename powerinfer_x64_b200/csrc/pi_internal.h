@@ -173,10 +173,8 @@ struct ExpertArgs {
     float* hs;   // Q8_0: [slots][f/32]
     float* hf;   // Q4_0: [slots][f]
     float* y;    // [slots][d]
-    // Q8_0 prefill GEMM: activations in slot order as exact f16 [slots][d] with their
-    // block scales [slots][d/32], and h as exact f16 [slots][f] (scales in hs)
-    __half* xsl;
-    float* xssl;
+    // Q8_0 prefill GEMM: h as exact f16 [slots][f] (scales in hs); the gate/up GEMM
+    // gathers its slots' activation rows from xq / xs itself
     __half* h16;
     // slot -> activation row: routed slot s < n_routed reads row perm[s]; shared slot
     // n_routed + t reads row sh_row0 + t. With n_routed_dev set, n_routed is *n_routed_dev

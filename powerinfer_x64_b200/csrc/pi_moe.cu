@@ -1976,8 +1976,7 @@ struct FwdBufs {
     __half *xh, *xl, *hh, *hl;
     __half *xth, *xtl;  // tensor-core router: tokens split into f16 hi/lo
     float* xnorm;
-    __half *xsl, *h16;  // Q8_0 prefill GEMM: slot-major f16 activations and h
-    float* xssl;
+    __half* h16;  // Q8_0 prefill GEMM: h in slot order as exact f16
     int32_t* disp_cc;   // large-batch dispatch: per-chunk expert counts
     size_t bytes;
 };
@@ -2065,12 +2064,9 @@ FwdBufs carve(const pi_moe_layer* L, int64_t T, int flags, char* base) {
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     if (use_gemm(L, T, flags) && L->qtype == PI_QT_Q8_0) {
-        f.xsl = b.take<__half>(slots * d);
-        f.xssl = b.take<float>(slots * (d / 32));
         f.h16 = b.take<__half>(slots * F);
     } else {
-        f.xsl = f.h16 = nullptr;
-        f.xssl = nullptr;
+        f.h16 = nullptr;
     }
     if (use_gemm(L, T, flags) && L->qtype == PI_QT_Q4_0) {
         f.xh = f.xl = nullptr;
@@ -2123,8 +2119,6 @@ ExpertArgs expert_args(const pi_moe_layer* L, int E_items, const FwdBufs& B, con
     a.hs = B.hs;
     a.hf = B.hf;
     a.y = B.y;
-    a.xsl = B.xsl;
-    a.xssl = B.xssl;
     a.h16 = B.h16;
     a.n_routed_dev = nullptr;
     a.sh_row0 = 0;
@@ -2439,8 +2433,6 @@ FwdBufs carve_rows(const pi_moe_layer* L, int64_t n, char* base) {
     f.hf = b.take<float>(slots * F);
     f.y = b.take<float>(slots * d);
     if (rows_gemm(L, n)) {
-        f.xsl = b.take<__half>(slots * d);
-        f.xssl = b.take<float>(slots * (d / 32));
         f.h16 = b.take<__half>(slots * F);
     }
     f.bytes = b.off + 256;
@@ -2521,8 +2513,6 @@ FwdBufs carve_multi(const pi_moe_layer* L, int64_t n_rows, int k, int64_t n_home
     f.disp_cc = b.take<int32_t>(((n_rows + DC - 1) / DC + 1) * En);
     f.hs = b.take<float>(slots * (F / 32));
     f.y = b.take<float>(slots * d);
-    f.xsl = b.take<__half>(slots * d);
-    f.xssl = b.take<float>(slots * (d / 32));
     f.h16 = b.take<__half>(slots * F);
     f.bytes = b.off + 256;
     return f;

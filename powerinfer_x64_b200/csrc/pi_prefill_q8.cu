@@ -24,9 +24,12 @@
 // registers.
 //
 // Operands:
-//   A (slots)   f16 rows [slots][K], slot-major (k_slot_rows writes the gate/up
-//               activations in slot order; the gate/up epilogue writes h so),
-//               loaded by TMA with the 64-byte swizzle the MMA reads;
+//   A (slots)   gate/up: each converter thread gathers its slot's token row of the
+//               quantised activations (int8, through the dispatch permutation; the
+//               next stage's words are requested while this one is converted) and
+//               writes exact f16 into the 64-byte-swizzled tile the MMA reads;
+//               down: h as f16 rows [slots][f] in slot order (the gate/up epilogue
+//               writes them so), loaded by TMA with the same swizzle;
 //   B (weights) int8 rows of the lane-tiled decode layouts, loaded raw by TMA in
 //               groups of 4 blocks and turned into exact f16 by converter warps;
 //   scales      per block a [128 x 16] f16 tile of slot scales (column 0) and one
@@ -37,8 +40,9 @@
 //   0-7   epilogue: warp w owns slots 32 (w % 4) .. +31 (TMEM lanes) and, for
 //         gate/up, gate columns 32 (w / 4) .. +31 with their up columns (+64),
 //         for down, columns 64 (w / 4) .. +63;
-//   8-11  converters: thread c converts weight row c of each block and writes
-//         the scale tiles' row c (its row's scale, slot c's scale);
+//   8-11  converters: thread c converts weight row c of each block, for gate/up
+//         also slot c's activation row, and writes the scale tiles' row c (its
+//         row's scale, slot c's scale);
 //   12    MMA issuer;  13 TMA producer.
 // Every mbarrier wait is bounded and reports PI_DEVERR_TIMEOUT.
 #include "pi_tc.cuh"
@@ -140,6 +144,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
     __shared__ uint32_t s_tmem;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int K = MODE == 0 ? a.d : a.f;
+    const int n_routed = a.n_routed_dev ? *a.n_routed_dev : a.n_routed;  // routed slots (gate/up gathers)
     const int nb = K / 32, ng = nb / G4;
     const int MT = MODE == 0 ? a.f / 64 : a.d / TN;  // weight-row tiles per item
     const int n_tiles = *a.n_items * MT;
@@ -154,7 +159,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
 
     if (tid == 0) {
         for (int i = 0; i < TS; ++i) {
-            mbar_init(&tile_full[i], NCONV + 1);
+            mbar_init(&tile_full[i], MODE == 0 ? NCONV : NCONV + 1);  // gate/up: the converters write A too
             mbar_init(&tile_free[i], 1);
         }
         for (int i = 0; i < DB; ++i) {
@@ -219,7 +224,7 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                             tma_load_4d(rw, md, q * 16, 0, 0, (mrow + tr.mt * TN) >> 3, &raw_full[slot]);
                         }
                     }
-                    for (int pi = 0; pi < G4 / PB && w_ok; ++pi) {
+                    for (int pi = 0; pi < G4 / PB && w_ok && MODE == 1; ++pi) {
                         const int s = (G4 / PB) * g + pi, ts = s % TS;
                         if (s >= TS && !mbar_wait(&tile_free[ts], (s / TS - 1) & 1)) { w_ok = 0; break; }
                         mbar_expect_tx(&tile_full[ts], PB * TILE);
@@ -253,6 +258,18 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             const __half* scp = wd + (size_t)wr * nb;
             const int64_t srow = (int64_t)tr.item.y + row;  // this thread's slot (scale row of the A side)
             const float* xsp = srow < n_slots ? xsc + srow * nb : nullptr;
+            // gate/up: the slot's token row (int8) and scales, gathered here (routed slot s
+            // reads token perm[s], shared slot n_routed + t reads row sh_row0 + t)
+            const int8_t* xrow = nullptr;
+            if (MODE == 0) {
+                xsp = nullptr;
+                if (row < tr.item.z) {
+                    const bool shs = srow >= n_routed;
+                    const int64_t tok = shs ? a.sh_row0 + (srow - n_routed) : a.perm[srow];
+                    xrow = (shs && a.xq_sh ? a.xq_sh : a.xq) + tok * K;
+                    xsp = (shs && a.xs_sh ? a.xs_sh : a.xs) + tok * nb;
+                }
+            }
             // the row's weight scales and the slot's activation scales of group q, as f16 bits
             auto load_sc = [&](int q, uint2& w, uint2& x) {
                 w = *reinterpret_cast<const uint2*>(scp + G4 * q);
@@ -281,6 +298,10 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
             };
             uint2 w_cur, x_cur, w_nxt, x_nxt;
             load_sc(0, w_cur, x_cur);
+            uint4 an[2 * PB];  // gate/up: the next stage's activation words (int8 zeros past the slot count)
+#pragma unroll
+            for (int j = 0; j < 2 * PB; ++j)
+                an[j] = MODE == 0 && xrow ? *reinterpret_cast<const uint4*>(xrow + 16 * j) : make_uint4(0u, 0u, 0u, 0u);
             for (int q = 0; q < ng; ++q, ++g) {
                 const int slot = g % RG;
                 if (q + 1 < ng) load_sc(q + 1, w_nxt, x_nxt);
@@ -293,6 +314,24 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
 #pragma unroll
                 for (int pi = 0; pi < G4 / PB; ++pi) {  // one stage (PB blocks) at a time
                     const int s = (G4 / PB) * g + pi;
+                    // gate/up: this stage's activations are in av; request the next stage's
+                    uint4 av[2 * PB];
+                    if (MODE == 0) {
+#pragma unroll
+                        for (int j = 0; j < 2 * PB; ++j) av[j] = an[j];
+                        const int nblk = G4 * q + PB * (pi + 1);  // first block of the next stage
+#pragma unroll
+                        for (int j = 0; j < 2 * PB; ++j)
+                            an[j] = xrow && nblk < nb ? *reinterpret_cast<const uint4*>(xrow + nblk * 32 + 16 * j)
+                                                      : make_uint4(0u, 0u, 0u, 0u);  // int8 zeros
+                    }
+                    if (s >= TS && !mbar_wait(&tile_free[s % TS], (s / TS - 1) & 1)) { ok = false; break; }
+                    uint8_t* st = a_tile(s % TS, 0);
+                    if (MODE == 0) {  // A: block b's 32 values -> chunks 0..3 of row `row`
+#pragma unroll
+                        for (int j = 0; j < 2 * PB; ++j)
+                            int8x16_to_f16(av[j], st + (j >> 1) * (2 * TILE + 2 * STILE), row, 2 * (j & 1));
+                    }
                     uint4 rv[2 * PB];
 #pragma unroll
                     for (int j = 0; j < 2 * PB; ++j) {
@@ -300,8 +339,6 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
                         chunk_of(pi, j, i, h);
                         rv[j] = *reinterpret_cast<const uint4*>(raw_half(rg, i, h));
                     }
-                    if (s >= TS && !mbar_wait(&tile_free[s % TS], (s / TS - 1) & 1)) { ok = false; break; }
-                    uint8_t* st = a_tile(s % TS, 0);
 #pragma unroll
                     for (int j = 0; j < 2 * PB; ++j) {
                         int i, h;
@@ -434,41 +471,6 @@ __global__ __launch_bounds__(QT, 1) void k_moe_gemm_q8(ExpertArgs a, const __gri
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(DB * 2 * TN) : "memory");
 }
 
-// Gate/up activations in slot order: slot s < n_routed holds row perm[s], slot
-// n_routed + t (t < n_sh) the shared expert's row sh_row0 + t; CTAs past the
-// realised slots exit. Q8_0 values become exact f16; the block scales are copied
-// alongside. One CTA per slot, 16 values per thread.
-__global__ __launch_bounds__(128) void k_slot_rows(const int8_t* __restrict__ xq, const float* __restrict__ xs,
-                                                   const int8_t* __restrict__ xq_sh, const float* __restrict__ xs_sh,
-                                                   const int32_t* __restrict__ perm, int n_routed,
-                                                   const int32_t* __restrict__ n_routed_dev, int sh_row0, int n_sh,
-                                                   int d, __half* __restrict__ xsl, float* __restrict__ xssl) {
-    const int s = blockIdx.x;
-    if (n_routed_dev) n_routed = *n_routed_dev;
-    if (s >= n_routed + n_sh) return;
-    const bool sh = s >= n_routed;
-    const int tok = sh ? sh_row0 + s - n_routed : perm[s];
-    if (sh && xq_sh) {  // the shared expert's rows live in their own array
-        xq = xq_sh;
-        xs = xs_sh;
-    }
-    const int8_t* src = xq + (size_t)tok * d;
-    __half* dst = xsl + (size_t)s * d;
-    for (int c = threadIdx.x; c < d / 16; c += blockDim.x) {
-        const int4 v = *reinterpret_cast<const int4*>(src + 16 * c);
-        const int8_t* b = reinterpret_cast<const int8_t*>(&v);
-        uint32_t w[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            const __half2 p = __halves2half2(__int2half_rn(b[2 * e]), __int2half_rn(b[2 * e + 1]));
-            w[e] = *reinterpret_cast<const uint32_t*>(&p);
-        }
-        reinterpret_cast<uint4*>(dst + 16 * c)[0] = make_uint4(w[0], w[1], w[2], w[3]);
-        reinterpret_cast<uint4*>(dst + 16 * c)[1] = make_uint4(w[4], w[5], w[6], w[7]);
-    }
-    for (int c = threadIdx.x; c < d / 32; c += blockDim.x) xssl[(size_t)s * (d / 32) + c] = xs[(size_t)tok * (d / 32) + c];
-}
-
 // Q8_0 weight rows for the TMA producer: gate/up [rows][d] bytes (box 64 B x 64 rows),
 // lane-tiled down rows as {64 B, 8, cpq, rows/8} (box {16, 8, cpq, 16}).
 bool q8_gateup_map(CUtensorMap* m, const PiMats& w) {
@@ -520,26 +522,21 @@ int pi_prefill_experts_q8(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& 
         return pi_set_error(ctx, PI_ERR_ARG,
                             "prefill Q8_0 GEMM: n_embd must be a multiple of 1024 and the expert widths 512");
     if (!L->maps_ok) return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: weight tensor maps unavailable");
-    if (!a.xsl || !a.xssl || !a.h16) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: slot buffers missing");
+    if (!a.h16) return pi_set_error(ctx, PI_ERR_ARG, "prefill Q8_0 GEMM: slot buffers missing");
     (void)T;
-    CUtensorMap mx, mh;
-    if (!act16_map(&mx, a.xsl, n_slots, a.d) || !act16_map(&mh, a.h16, n_slots, a.f))
+    CUtensorMap mh;  // down reads h by TMA; gate/up gathers its slots' token rows in the converters
+    if (!act16_map(&mh, a.h16, n_slots, a.f))
         return pi_set_error(ctx, PI_ERR_CUDA, "prefill Q8_0 GEMM: cuTensorMapEncodeTiled failed");
     const bool fast = (flags & PI_FWD_FAST_SUM) != 0;
     auto gu = fast ? k_moe_gemm_q8<0, true> : k_moe_gemm_q8<0, false>;
     auto dn = fast ? k_moe_gemm_q8<1, true> : k_moe_gemm_q8<1, false>;
     pi_smem_attr((const void*)gu, QSMEM);
     pi_smem_attr((const void*)dn, QSMEM);
-    {
-        PiProfScope ps(ctx, st, "k_slot_rows");
-        k_slot_rows<<<(unsigned)n_slots, 128, 0, st>>>(a.xq, a.xs, a.xq_sh, a.xs_sh, a.perm, a.n_routed,
-                                                       a.n_routed_dev, a.sh_row0, a.n_sh, a.d, a.xsl, a.xssl);
-    }
     const int64_t sms = ctx->sm_count > 0 ? ctx->sm_count : 148;
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_gateup");
         const unsigned g = (unsigned)std::min<int64_t>(max_items * (a.f / 64), sms);
-        gu<<<g, QT, QSMEM, st>>>(a, L->maps, mx, a.xssl, n_slots, ctx->dev_err);
+        gu<<<g, QT, QSMEM, st>>>(a, L->maps, mh, nullptr, n_slots, ctx->dev_err);
     }
     {
         PiProfScope ps(ctx, st, "k_gemm_q8_down");
