@@ -531,8 +531,8 @@ void launch_topk(unsigned grid, cudaStream_t st, const float* logits, int T, int
 constexpr int RD_NC = 4;  // chunks of the inputs, one mbarrier each
 template <int R, int TK>
 constexpr size_t rd_smem(int d) { return sizeof(float) * (size_t)(R + TK) * (d + 4); }
-template <int R, int TK, int NPL, bool FUSE>
-__global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__ xin, const float* __restrict__ W,
+template <int R, int TK, int NPL, bool FUSE, int NTH>
+__global__ __launch_bounds__(NTH) void k_router_dec(const float* __restrict__ xin, const float* __restrict__ W,
                                                        const float* __restrict__ bias, int T, int d, int E,
                                                        float* __restrict__ logits, int k, int has_shgate,
                                                        int32_t* __restrict__ idx, float* __restrict__ gates,
@@ -540,7 +540,8 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
                                                        int32_t* __restrict__ tickets, int fuse, uint32_t* err) {
     pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
     pdl_trigger();
-    static_assert(!FUSE || TK * R == TK_WARPS * 32, "one warp per top-k token slot");
+    static_assert(!FUSE || NTH == TK_WARPS * 32, "one warp per top-k token slot");
+    static_assert(R * TK <= NTH, "a lane per (row, token)");
     extern __shared__ __align__(16) float rd_sm[];
     __shared__ __align__(8) uint64_t full[RD_NC];
     const int tid = threadIdx.x;
@@ -554,7 +555,7 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
     }
     __syncthreads();
     // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens
-    for (int q = tid; q < (R + TK) * RD_NC; q += TK * R) {
+    for (int q = tid; q < (R + TK) * RD_NC; q += NTH) {
         const int row = q % (R + TK), c = q / (R + TK);
         const float* src = nullptr;
         if (row < nrow) src = W + (int64_t)(e0 + row) * d;
@@ -562,7 +563,7 @@ __global__ __launch_bounds__(TK * R) void k_router_dec(const float* __restrict__
         if (src) pitc::bulk_load(rd_sm + row * pitch + c * dc, src + c * dc, (uint32_t)dc * 4, &full[c]);
     }
     const int r = tid % R, tk = tid / R;
-    const bool live = r < nrow && tk < nt;
+    const bool live = r < nrow && tk < nt;  // lanes tid >= R * TK have tk >= TK >= nt
     const float* wr = rd_sm + r * pitch;
     const float* xv = rd_sm + (R + tk) * pitch;
     float acc = 0.0f;
@@ -2328,24 +2329,32 @@ int pi_moe_run(pi_ctx* ctx, pi_moe_layer* L, const float* x, int64_t T, float* o
             // routes it); larger ones route in a separate launch with a warp per token
             const int fuse = T <= 8 ? 1 : 0;
             if (d <= 2048) {
-                dim3 rg((unsigned)((E + 1 + 15) / 16), (unsigned)((T + 7) / 8));
-#define RD16(N)                                                                                               \
+                // rows per CTA shrink with the batch, so that the CTAs (and the SMs staging
+                // router rows) stay many: R rows x TK tokens per 128-thread CTA
+#define RDL(R, TK, N)                                                                                         \
     {                                                                                                         \
-        pi_smem_attr((const void*)k_router_dec<16, 8, N, true>, rd_smem<16, 8>(2048));                        \
-        pi_pdl_launch(k_router_dec<16, 8, N, true>, dim3(rg), dim3(128), rd_smem<16, 8>(d), st, xin, L->router, L->bias, (int)T, d, \
-                                                                         E, B.logits, k, hs, idx, gates,      \
-                                                                         B.shscale, counts, tickets, fuse,    \
-                                                                         ctx->dev_err);                       \
+        dim3 rg((unsigned)((E + 1 + R - 1) / R), (unsigned)((T + TK - 1) / TK));                              \
+        pi_smem_attr((const void*)k_router_dec<R, TK, N, true, 128>, rd_smem<R, TK>(2048));                   \
+        pi_pdl_launch(k_router_dec<R, TK, N, true, 128>, rg, dim3(128), rd_smem<R, TK>(d), st, xin, L->router, \
+                      L->bias, (int)T, d, E, B.logits, k, hs, idx, gates, B.shscale, counts, tickets, fuse,  \
+                      ctx->dev_err);                                                                          \
+    }
+#define RD16(N)                                   \
+    {                                             \
+        if (T <= 2) RDL(2, 2, N)                  \
+        else if (T <= 8) RDL(4, 8, N)             \
+        else RDL(16, 8, N)                        \
     }
                 if (E <= 64) RD16(2) else if (E <= 128) RD16(4) else if (E <= 256) RD16(8) else RD16(16)
 #undef RD16
+#undef RDL
                 if (!fuse)
                     launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
                                 B.logits, (int)T, E, k, hs, idx, gates, B.shscale, counts, nullptr, nullptr);
             } else {
-                pi_smem_attr((const void*)k_router_dec<8, 4, 16, false>, rd_smem<8, 4>(4096));
+                pi_smem_attr((const void*)k_router_dec<8, 4, 16, false, 32>, rd_smem<8, 4>(4096));
                 dim3 rg((unsigned)((E + 1 + 7) / 8), (unsigned)((T + 3) / 4));
-                pi_pdl_launch(k_router_dec<8, 4, 16, false>, dim3(rg), dim3(32), rd_smem<8, 4>(d), st, 
+                pi_pdl_launch(k_router_dec<8, 4, 16, false, 32>, dim3(rg), dim3(32), rd_smem<8, 4>(d), st, 
                     xin, L->router, L->bias, (int)T, d, E, B.logits, k, hs, idx, gates, B.shscale, counts, tickets, 0,
                     ctx->dev_err);
                 launch_topk((unsigned)std::min<int64_t>((T + TK_WARPS - 1) / TK_WARPS, 8 * ctx->sm_count), st,
