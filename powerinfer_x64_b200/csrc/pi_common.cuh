@@ -61,8 +61,9 @@ PI_DEV float warp_sum(float v) {
 // Programmatic dependent launch (kernels launched with pi_pdl_launch): pdl_wait blocks
 // until the stream's previous kernel has completed and its writes are visible (a no-op
 // for a normal launch); pdl_trigger lets the next kernel start launching once every CTA
-// of this one has run it. Call pdl_wait first, unconditionally, in every CTA, so that a
-// kernel never completes before the one it follows.
+// of this one has run it. Every CTA calls pdl_wait unconditionally, before it can return
+// and before it touches anything the previous kernel writes (reads of constant weights may
+// come first), so that a kernel never completes before the one it follows.
 PI_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 PI_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 

@@ -538,8 +538,6 @@ __global__ __launch_bounds__(NTH) void k_router_dec(const float* __restrict__ xi
                                                        int32_t* __restrict__ idx, float* __restrict__ gates,
                                                        float* __restrict__ shscale, int32_t* __restrict__ counts,
                                                        int32_t* __restrict__ tickets, int fuse, uint32_t* err) {
-    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
-    pdl_trigger();
     static_assert(!FUSE || NTH == TK_WARPS * 32, "one warp per top-k token slot");
     static_assert(R * TK <= NTH, "a lane per (row, token)");
     extern __shared__ __align__(16) float rd_sm[];
@@ -554,13 +552,22 @@ __global__ __launch_bounds__(NTH) void k_router_dec(const float* __restrict__ xi
         for (int c = 0; c < RD_NC; ++c) pitc::mbar_expect_tx(&full[c], (uint32_t)((nrow + nt) * dc * 4));
     }
     __syncthreads();
-    // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens
-    for (int q = tid; q < (R + TK) * RD_NC; q += NTH) {
-        const int row = q % (R + TK), c = q / (R + TK);
-        const float* src = nullptr;
-        if (row < nrow) src = W + (int64_t)(e0 + row) * d;
-        else if (row >= R && row - R < nt) src = xin + (int64_t)(t0 + row - R) * d;
-        if (src) pitc::bulk_load(rd_sm + row * pitch + c * dc, src + c * dc, (uint32_t)dc * 4, &full[c]);
+    // copy (row q, chunk c) by thread q + (R + TK) c: rows 0..R-1 router, R.. tokens.
+    // The router rows are constant, so their copies start before the programmatic-launch
+    // wait and overlap the tail of the kernel that writes the token rows.
+    for (int q = tid; q < R * RD_NC; q += NTH) {
+        const int row = q % R, c = q / R;
+        if (row < nrow)
+            pitc::bulk_load(rd_sm + row * pitch + c * dc, W + (int64_t)(e0 + row) * d + c * dc, (uint32_t)dc * 4,
+                            &full[c]);
+    }
+    pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
+    pdl_trigger();
+    for (int q = tid; q < TK * RD_NC; q += NTH) {
+        const int row = q % TK, c = q / TK;
+        if (row < nt)
+            pitc::bulk_load(rd_sm + (R + row) * pitch + c * dc, xin + (int64_t)(t0 + row) * d + c * dc,
+                            (uint32_t)dc * 4, &full[c]);
     }
     const int r = tid % R, tk = tid / R;
     const bool live = r < nrow && tk < nt;  // lanes tid >= R * TK have tk >= TK >= nt
