@@ -1179,11 +1179,13 @@ __global__ __launch_bounds__(DC) void k_disp_scatter(const int32_t* __restrict__
 // ---------------------------------------------------------------------------
 PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot - a.n_routed : a.perm[slot]; }
 
-// Q8_0 gate+up: CTA = 16 rows of one expert (8 warps x 2 rows, gate and
-// up = 4 row-vectors per warp), CPL = d/512 16-byte chunks per lane per row
+// Q8_0 gate+up: CTA = 2 * GU_WARPS rows of one expert (2 rows per warp, gate
+// and up = 4 row-vectors per warp), CPL = d/512 16-byte chunks per lane per row
 // (lane l holds chunks l + 32c; chunks 2m, 2m+1 form 32-element block m).
-// 256 threads and ~70 KB of shared memory let two CTAs share an SM, so one
-// CTA's weight loads overlap another's arithmetic.
+// Small CTAs (64 threads, ~17 KB of shared memory, eight per SM) retire and are
+// replaced one by one, so an SM's weight loads overlap other CTAs' arithmetic
+// without waiting for a large CTA's slowest warp (C2 T=64: 106 us with 256-thread
+// CTAs, 100.5 with 128, 99.9 with 64).
 //
 // The sums keep the reference's order exactly (matvec_q8_0_sse_range,
 // quant/mod.rs:835-871): per block an exact int32 dot, the term
@@ -1193,16 +1195,17 @@ PI_DEV int slot_token(const ExpertArgs& a, bool sh, int slot) { return sh ? slot
 // reference's h bit for bit (up to its expf rounding), so the Q8_0
 // re-quantisation of h in k_down_q8 makes the same integer choices.
 constexpr int GU_TB = 8;    // tokens per batch: 4 row-vectors x 8 tokens = 32 chains per warp
-constexpr int GU_ROWS = 16; // rows per CTA
+constexpr int GU_WARPS = 2;            // warps per CTA (2 rows each)
+constexpr int GU_ROWS = 2 * GU_WARPS;  // rows per CTA
 template <int CPL>
-__global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
+__global__ __launch_bounds__(GU_WARPS * 32, 16 / GU_WARPS) void k_gateup_q8(ExpertArgs a) {
     pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
     pdl_trigger();
     constexpr int NB = 16 * CPL;   // blocks per row
     constexpr int STRIDE = NB + 4; // padded chain stride (floats): conflict-free 16-byte reads
     extern __shared__ __align__(16) float smem[];
     float* terms = smem + (threadIdx.x >> 5) * (4 * GU_TB * STRIDE);
-    __shared__ float res[8][4][GU_TB];
+    __shared__ float res[GU_WARPS][4][GU_TB];
     const int it = blockIdx.y;
     if (it >= *a.n_items) return;
     const int4 item = a.items[it];
@@ -1292,7 +1295,7 @@ __global__ __launch_bounds__(256, 2) void k_gateup_q8(ExpertArgs a) {
 
 template <int CPL>
 constexpr size_t gateup_q8_smem() {
-    return (size_t)8 * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
+    return (size_t)GU_WARPS * 4 * GU_TB * (16 * CPL + 4) * sizeof(float);
 }
 
 // Q8_0 h re-quantisation (quant/mod.rs:698-736, as the reference's down
@@ -2151,7 +2154,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
 #define GU_Q8(C)                                                                                              \
     case C: {                                                                                                 \
         pi_smem_attr((const void*)k_gateup_q8<C>, gateup_q8_smem<C>());                                       \
-        pi_pdl_launch(k_gateup_q8<C>, dim3(gu), dim3(256), gateup_q8_smem<C>(), st, a);                                             \
+        pi_pdl_launch(k_gateup_q8<C>, dim3(gu), dim3(GU_WARPS * 32), gateup_q8_smem<C>(), st, a);                                             \
         break;                                                                                                \
     }
             GU_Q8(2)
