@@ -134,18 +134,37 @@ __global__ __launch_bounds__(NT) void k_prep(const float* __restrict__ x, int d,
         __syncthreads();
         inv = s_inv;
     }
-    for (int i = tid; i < d; i += NT) {  // d % 32 == 0: a warp covers one quant block per pass
-        float v = s_row[i];
+    // four consecutive elements per thread (d % 32 == 0): eight lanes hold one Q8_0 block, so
+    // its absmax takes three shuffles and its two divisions are paid once per four elements;
+    // the arithmetic of each value is warp_quant_q8's (quant/mod.rs:698-736)
+    for (int c = tid; c < d / 4; c += NT) {
+        float4 v = *reinterpret_cast<const float4*>(&s_row[4 * c]);
         if (do_norm) {
-            v = fmul(v, inv);  // * weight (1.0) is exact
-            normed[(size_t)t * d + i] = v;
-            s_row[i] = v;
+            v = make_float4(fmul(v.x, inv), fmul(v.y, inv), fmul(v.z, inv), fmul(v.w, inv));  // * weight (1.0)
+            *reinterpret_cast<float4*>(normed + (size_t)t * d + 4 * c) = v;
+            *reinterpret_cast<float4*>(&s_row[4 * c]) = v;
         }
         if (do_quant) {
-            float sc;
-            const int8_t q = warp_quant_q8(v, &sc);
-            xq[(size_t)t * d + i] = q;
-            if ((tid & 31) == 0) xs[(size_t)t * (d / 32) + i / 32] = sc;
+            const float e[4] = {v.x, v.y, v.z, v.w};
+            float amax = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float a = fabsf(e[j]);
+                amax = fmaxf(amax, (a == a) ? a : 0.0f);  // NaN never wins `abs > amax`
+            }
+#pragma unroll
+            for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float dq = fdiv(amax, 127.0f);
+            const float id = (dq != 0.0f) ? fdiv(1.0f, dq) : 0.0f;
+            uint32_t packed = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float r = roundf(fmul(e[j], id));  // half away from zero, like Rust f32::round
+                const int q = (r != r) ? 0 : (int)fminf(127.0f, fmaxf(-127.0f, r));
+                packed |= (uint32_t)(q & 0xff) << (8 * j);
+            }
+            *reinterpret_cast<uint32_t*>(xq + (size_t)t * d + 4 * c) = packed;
+            if ((c & 7) == 0) xs[(size_t)t * (d / 32) + c / 8] = __half2float(__float2half_rn(dq));
         }
     }
     // the certified tensor-core router's f16 hi/lo split and norm bound of the (normed) row
