@@ -49,6 +49,31 @@ PI_DEV int8_t warp_quant_q8(float x, float* scale_out) {
     return (int8_t)q;
 }
 
+// Q8_0 quantisation of four consecutive values of a 32-block whose eight quarters sit in
+// eight aligned consecutive lanes (all 32 lanes of the warp call it): returns the four
+// int8 values packed little-endian, with warp_quant_q8's arithmetic per value.
+PI_DEV uint32_t quad_quant_q8(const float e[4], float* scale_out) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float a = fabsf(e[j]);
+        amax = fmaxf(amax, (a == a) ? a : 0.0f);  // NaN never wins `abs > amax`
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float d = fdiv(amax, 127.0f);
+    const float id = (d != 0.0f) ? fdiv(1.0f, d) : 0.0f;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float r = roundf(fmul(e[j], id));  // half away from zero, like Rust f32::round
+        const int q = (r != r) ? 0 : (int)fminf(127.0f, fmaxf(-127.0f, r));
+        packed |= (uint32_t)(q & 0xff) << (8 * j);
+    }
+    *scale_out = __half2float(__float2half_rn(d));
+    return packed;
+}
+
 PI_DEV int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 PI_DEV float warp_sum(float v) {

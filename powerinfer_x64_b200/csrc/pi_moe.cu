@@ -134,9 +134,9 @@ __global__ __launch_bounds__(NT) void k_prep(const float* __restrict__ x, int d,
         __syncthreads();
         inv = s_inv;
     }
-    // four consecutive elements per thread (d % 32 == 0): eight lanes hold one Q8_0 block, so
-    // its absmax takes three shuffles and its two divisions are paid once per four elements;
-    // the arithmetic of each value is warp_quant_q8's (quant/mod.rs:698-736)
+    // four consecutive elements per thread (d % 128 == 0, so every warp pass is full): eight
+    // lanes hold one Q8_0 block, so its absmax takes three shuffles and its two divisions are
+    // paid once per four elements (quad_quant_q8; quant/mod.rs:698-736)
     for (int c = tid; c < d / 4; c += NT) {
         float4 v = *reinterpret_cast<const float4*>(&s_row[4 * c]);
         if (do_norm) {
@@ -146,25 +146,9 @@ __global__ __launch_bounds__(NT) void k_prep(const float* __restrict__ x, int d,
         }
         if (do_quant) {
             const float e[4] = {v.x, v.y, v.z, v.w};
-            float amax = 0.0f;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float a = fabsf(e[j]);
-                amax = fmaxf(amax, (a == a) ? a : 0.0f);  // NaN never wins `abs > amax`
-            }
-#pragma unroll
-            for (int o = 1; o < 8; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float dq = fdiv(amax, 127.0f);
-            const float id = (dq != 0.0f) ? fdiv(1.0f, dq) : 0.0f;
-            uint32_t packed = 0;
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float r = roundf(fmul(e[j], id));  // half away from zero, like Rust f32::round
-                const int q = (r != r) ? 0 : (int)fminf(127.0f, fmaxf(-127.0f, r));
-                packed |= (uint32_t)(q & 0xff) << (8 * j);
-            }
-            *reinterpret_cast<uint32_t*>(xq + (size_t)t * d + 4 * c) = packed;
-            if ((c & 7) == 0) xs[(size_t)t * (d / 32) + c / 8] = __half2float(__float2half_rn(dq));
+            float sc;
+            *reinterpret_cast<uint32_t*>(xq + (size_t)t * d + 4 * c) = quad_quant_q8(e, &sc);
+            if ((c & 7) == 0) xs[(size_t)t * (d / 32) + c / 8] = sc;
         }
     }
     // the certified tensor-core router's f16 hi/lo split and norm bound of the (normed) row
@@ -1323,12 +1307,18 @@ __global__ void k_quant_h(const float* __restrict__ hf, int64_t nblk, int8_t* __
                           float* __restrict__ hs) {
     pdl_wait();  // programmatic launch: the previous kernel of the stream is complete
     pdl_trigger();
-    const int64_t b = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (b >= nblk) return;
+    // thread = four consecutive values, eight lanes per 32-block (quad_quant_q8); threads
+    // past the end still take part in the shuffles of their warp
+    const int64_t g = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+    const bool live = g < nblk * 8;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) v = *reinterpret_cast<const float4*>(hf + 4 * g);
+    const float e[4] = {v.x, v.y, v.z, v.w};
     float sc;
-    hq[b * 32 + lane] = warp_quant_q8(hf[b * 32 + lane], &sc);
-    if (lane == 0) hs[b] = sc;
+    const uint32_t q = quad_quant_q8(e, &sc);
+    if (!live) return;
+    *reinterpret_cast<uint32_t*>(hq + 4 * g) = q;
+    if ((g & 7) == 0) hs[g >> 3] = sc;
 }
 
 // Q8_0 down, streamed: a persistent CTA per SM walks work units u = (item, block of
@@ -2185,7 +2175,7 @@ int run_experts(pi_ctx* ctx, const pi_moe_layer* L, const ExpertArgs& a, int64_t
         {
             PiProfScope ps(ctx, st, "k_quant_h");
             const int64_t nblk = n_slots * (L->f / 32);
-            pi_pdl_launch(k_quant_h, dim3((unsigned)((nblk * 32 + 255) / 256)), dim3(256), 0, st, B.hf, nblk, B.hq, B.hs);
+            pi_pdl_launch(k_quant_h, dim3((unsigned)((nblk * 8 + 255) / 256)), dim3(256), 0, st, B.hf, nblk, B.hq, B.hs);
         }
         PiProfScope ps(ctx, st, "k_down");
         const int cpq = L->f % 64 ? 0 : (int)(L->f / 64);  // 16-byte chunks per quarter row
