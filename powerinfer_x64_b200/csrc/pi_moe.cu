@@ -655,8 +655,8 @@ __global__ __launch_bounds__(256) void k_split_tokens(const float* __restrict__ 
 constexpr int RC_TT = 64;      // tokens per CTA at most
 constexpr int RC_THR = 512;    // threads per CTA
 constexpr int RC_JPT = 4;      // exact chains per thread at most (64 tokens x 32 rows)
-constexpr int RC_CH = 32;      // floats of each staged row per piece
-constexpr int RC_NS = 3;       // pieces in flight
+constexpr int RC_CH = 64;      // floats of each staged row per piece
+constexpr int RC_NS = 2;       // pieces in flight
 constexpr int RC_PITCH = RC_CH + 4;  // +4: 16-byte loads of rows 1 .. 7 apart hit distinct banks
 constexpr int RC_MAXR = 257;   // staged router rows: E <= 256 experts + the shared-expert gate row
 size_t router_cand_smem() { return (size_t)RC_NS * (RC_TT + RC_MAXR) * RC_PITCH * 4; }
