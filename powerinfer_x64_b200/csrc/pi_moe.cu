@@ -1109,10 +1109,16 @@ __global__ __launch_bounds__(512) void k_disp_scan(int32_t* __restrict__ cc, int
     const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
     int cnt = 0;
     if (e < E)
-        for (int c = 0; c < nchunk; ++c) {
-            const int v = cc[(size_t)c * E + e];
-            cc[(size_t)c * E + e] = cnt;
-            cnt += v;
+        for (int c0 = 0; c0 < nchunk; c0 += 16) {  // 16 chunks' counts in flight per round trip
+            int v[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = c0 + j < nchunk ? cc[(size_t)(c0 + j) * E + e] : 0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j)
+                if (c0 + j < nchunk) {
+                    cc[(size_t)(c0 + j) * E + e] = cnt;
+                    cnt += v[j];
+                }
         }
     const int ni = (cnt + tg - 1) / tg;
     int a = cnt, b = ni;  // inclusive block scans of counts and item counts
